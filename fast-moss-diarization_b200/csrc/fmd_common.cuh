@@ -1,0 +1,110 @@
+// Shared device helpers for the sm_100a decoder kernels.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#define FMD_DEV __device__ __forceinline__
+
+namespace fmd {
+
+constexpr int kHeadDim = 128;     // only head_dim 128 is supported
+constexpr int kPageTokens = 64;   // KV page: 64 positions of one (layer, k|v, kv head)
+constexpr int kQ8Block = 32;      // GGML Q8_0 block length along the input axis
+
+// ---- activation dtype traits ------------------------------------------------
+template <typename T> struct Act;
+template <> struct Act<__nv_bfloat16> {
+  static FMD_DEV float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
+  static FMD_DEV __nv_bfloat16 from_f(float x) { return __float2bfloat16_rn(x); }
+  static FMD_DEV uint32_t pack2(float lo, float hi) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+  static FMD_DEV float2 unpack2(uint32_t u) {
+    // bf16 -> f32 is a 16-bit shift: exact.
+    return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
+  }
+};
+template <> struct Act<__half> {
+  static FMD_DEV float to_f(__half x) { return __half2float(x); }
+  static FMD_DEV __half from_f(float x) { return __float2half_rn(x); }
+  static FMD_DEV uint32_t pack2(float lo, float hi) {
+    __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+  static FMD_DEV float2 unpack2(uint32_t u) {
+    __half2 v = *reinterpret_cast<__half2*>(&u);
+    return __half22float2(v);
+  }
+};
+
+// Round an f32 through the activation dtype (the reference stores every op
+// result in the activation dtype).
+template <typename T> FMD_DEV float rnd(float x) { return Act<T>::to_f(Act<T>::from_f(x)); }
+
+// ---- warp reductions ---------------------------------------------------------
+FMD_DEV float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+FMD_DEV float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// ---- tensor-core MMA (m16n8k16, f32 accumulate) -------------------------------
+template <typename T> FMD_DEV void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1);
+template <> FMD_DEV void mma16816<__nv_bfloat16>(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+template <> FMD_DEV void mma16816<__half>(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// ---- shared-memory / async-copy helpers ------------------------------------------
+FMD_DEV uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+
+// 16-byte async copy global->shared; `bytes` < 16 zero-fills the rest (0 = all zero).
+FMD_DEV void cp_async16(void* smem, const void* gmem, int bytes = 16) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(smem_u32(smem)), "l"(gmem), "r"(bytes));
+}
+FMD_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N> FMD_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
+
+FMD_DEV void ldmatrix_x4(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+FMD_DEV void ldmatrix_x4_trans(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+// 16-byte streaming load that bypasses L1 allocation (weights are read once).
+FMD_DEV int4 ld_stream16(const void* p) {
+  int4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.s32 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+// f16 bits -> f32 (exact).
+FMD_DEV float h2f_bits(uint16_t b) { return __half2float(__ushort_as_half(b)); }
+
+}  // namespace fmd

@@ -1,0 +1,886 @@
+// sm_100a kernels of the batched Qwen3 decoder step.
+//
+// Every kernel reads its row counts from the device plan (`PlanCounts`), so
+// grids are fixed per handle and a whole step can be captured once in a CUDA
+// graph and replayed while the device scheduler changes the batch.
+//
+// Arithmetic contract (mirrors the reference's rounding points,
+// crates/fmd-core/src/model/qwen3.rs and linear.rs): every op result that the
+// reference stores in the activation dtype is rounded to it here too; matmuls
+// and reductions accumulate in f32.
+#include <float.h>
+#include <math.h>
+
+#include "fmd_kernels.cuh"
+
+namespace fmd {
+
+namespace {
+
+template <int NT>
+FMD_DEV float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < NT / 32; ++i) s += red[i];
+  __syncthreads();
+  return s;
+}
+
+// ---------------------------------------------------------------------------
+// Embedding gather (qwen3.rs:405-412) fused with layer 0's input RMSNorm
+// (linear.rs:293-302). Rows come from the token table or, for prompt rows,
+// from the prompt-embedding arena (the spliced audio/text embeddings).
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(128) k_embed_norm(Plan p, const T* __restrict__ table, const T* __restrict__ arena,
+                                                    T* __restrict__ x, const T* __restrict__ w, T* __restrict__ xn,
+                                                    int H, float eps) {
+  __shared__ float red[4];
+  const int n_rows = p.counts->n_rows;
+  for (int r = blockIdx.x; r < n_rows; r += gridDim.x) {
+  const int tok = p.row_tok[r];
+  const T* src = tok >= 0 ? table + (size_t)tok * H : arena + (size_t)p.row_emb[r] * H;
+  T* xr = x + (size_t)r * H;
+  float ss = 0.f;
+  for (int i = threadIdx.x * 8; i < H; i += 128 * 8) {
+    const int4 v = *reinterpret_cast<const int4*>(src + i);
+    *reinterpret_cast<int4*>(xr + i) = v;
+    const uint32_t* u = reinterpret_cast<const uint32_t*>(&v);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = Act<T>::unpack2(u[j]);
+      ss += f.x * f.x + f.y * f.y;
+    }
+  }
+  const float inv = rsqrtf(block_sum<128>(ss, red) / H + eps);
+  for (int i = threadIdx.x * 8; i < H; i += 128 * 8) {
+    const int4 v = *reinterpret_cast<const int4*>(src + i);
+    const int4 wv = *reinterpret_cast<const int4*>(w + i);
+    const uint32_t* u = reinterpret_cast<const uint32_t*>(&v);
+    const uint32_t* uw = reinterpret_cast<const uint32_t*>(&wv);
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = Act<T>::unpack2(u[j]);
+      const float2 g = Act<T>::unpack2(uw[j]);
+      o[j] = Act<T>::pack2(f.x * inv * g.x, f.y * inv * g.y);
+    }
+    *reinterpret_cast<int4*>(xn + (size_t)r * H + i) = *reinterpret_cast<int4*>(o);
+  }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Residual add + RMSNorm: x <- rnd(x + rnd(sum_s part[s])); xn <- rmsnorm(x).
+// The O-projection and down-projection epilogues (qwen3.rs:333-338) fused with
+// the next norm (post-attention, next layer's input, or the final norm).
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(128) k_residual_norm(const int* __restrict__ n_rows_ptr, T* __restrict__ x,
+                                                       const float* __restrict__ part, int split,
+                                                       size_t split_stride, const T* __restrict__ w,
+                                                       T* __restrict__ xn, int H, float eps) {
+  __shared__ float red[4];
+  const int n_rows = *n_rows_ptr;
+  const int S = effective_split(split, n_rows);
+  for (int r = blockIdx.x; r < n_rows; r += gridDim.x) {
+  T* xr = x + (size_t)r * H;
+  float ss = 0.f;
+  for (int i = threadIdx.x * 8; i < H; i += 128 * 8) {
+    int4 v = *reinterpret_cast<const int4*>(xr + i);
+    uint32_t* u = reinterpret_cast<uint32_t*>(&v);
+    if (part != nullptr) {
+      float acc[8];
+      const float* p0 = part + (size_t)r * H + i;
+      float4 a = *reinterpret_cast<const float4*>(p0), b = *reinterpret_cast<const float4*>(p0 + 4);
+      acc[0] = a.x; acc[1] = a.y; acc[2] = a.z; acc[3] = a.w; acc[4] = b.x; acc[5] = b.y; acc[6] = b.z; acc[7] = b.w;
+      for (int s = 1; s < S; ++s) {
+        const float* ps = p0 + (size_t)s * split_stride;
+        a = *reinterpret_cast<const float4*>(ps);
+        b = *reinterpret_cast<const float4*>(ps + 4);
+        acc[0] += a.x; acc[1] += a.y; acc[2] += a.z; acc[3] += a.w;
+        acc[4] += b.x; acc[5] += b.y; acc[6] += b.z; acc[7] += b.w;
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = Act<T>::unpack2(u[j]);
+        u[j] = Act<T>::pack2(f.x + rnd<T>(acc[2 * j]), f.y + rnd<T>(acc[2 * j + 1]));
+      }
+      *reinterpret_cast<int4*>(xr + i) = v;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = Act<T>::unpack2(u[j]);
+      ss += f.x * f.x + f.y * f.y;
+    }
+  }
+  const float inv = rsqrtf(block_sum<128>(ss, red) / H + eps);
+  for (int i = threadIdx.x * 8; i < H; i += 128 * 8) {
+    const int4 v = *reinterpret_cast<const int4*>(xr + i);
+    const int4 wv = *reinterpret_cast<const int4*>(w + i);
+    const uint32_t* u = reinterpret_cast<const uint32_t*>(&v);
+    const uint32_t* uw = reinterpret_cast<const uint32_t*>(&wv);
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = Act<T>::unpack2(u[j]);
+      const float2 g = Act<T>::unpack2(uw[j]);
+      o[j] = Act<T>::pack2(f.x * inv * g.x, f.y * inv * g.y);
+    }
+    *reinterpret_cast<int4*>(xn + (size_t)r * H + i) = *reinterpret_cast<int4*>(o);
+  }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Skinny GEMM y = x W^T on the tensor cores (mma.sync m16n8k16, f32 acc),
+// weights fed straight from HBM into A-fragments (Q8_0 dequantised in
+// registers), activations staged in shared memory.
+//
+// Swap-AB: A = 16 output features x 16 k, B = 16 k x 8 token rows. The k order
+// inside one 64-wide k-block is permuted identically for A and B so that each
+// thread reads 16 CONSECUTIVE weights of a row (one 16-byte Q8_0 load, within
+// a single 32-value block, so one scale) and 16 consecutive activations:
+// fragment k-column {2t,2t+1 | 2t+8,2t+9} of MMA j <-> k = 16t + 4j + {0,1 | 2,3}.
+//
+// CTA = 4 warps = 64 output features; grid.y splits K when the pass has
+// <= 64 rows (decode), writing f32 partials that the consumer kernel sums;
+// grid.z strides over 64-row tiles.
+// ---------------------------------------------------------------------------
+struct WRaw {
+  int4 a, b, c, d;
+  float da, db;
+};
+
+template <typename T, bool Q8>
+__global__ void __launch_bounds__(128) k_linear(const T* __restrict__ x, int ldx, const int* __restrict__ row_map,
+                                                const int* __restrict__ n_rows_ptr, LinW W, float* __restrict__ out,
+                                                size_t split_stride) {
+  __shared__ __align__(16) T xs[2][64][72];
+  const int n_rows = *n_rows_ptr;
+  const int S = effective_split(W.split, n_rows);
+  if ((int)blockIdx.y >= S) return;
+  const int K = W.K, N = W.N;
+  const int klen = K / S;
+  const int kbeg = blockIdx.y * klen;
+  const int nkb = klen >> 6;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int f0 = blockIdx.x * 64 + warp * 16 + g;
+  const int KB = K / kQ8Block;
+
+  for (int row0 = blockIdx.z * 64; row0 < n_rows; row0 += gridDim.z * 64) {
+    const int rows = min(64, n_rows - row0);
+    const int n_tiles = (rows + 7) >> 3;
+
+    // per-thread source rows of the activation tile (4 x 16-byte chunks)
+    const T* xsrc[4];
+    int xbytes[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int r = (threadIdx.x >> 3) + 16 * i;
+      const int ch = threadIdx.x & 7;
+      if (r < rows) {
+        const int gr = row_map ? row_map[row0 + r] : row0 + r;
+        xsrc[i] = x + (size_t)gr * ldx + kbeg + ch * 8;
+        xbytes[i] = 16;
+      } else {
+        xsrc[i] = x;
+        xbytes[i] = 0;
+      }
+    }
+    auto load_x = [&](int stage, int kb) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int r = (threadIdx.x >> 3) + 16 * i;
+        const int ch = threadIdx.x & 7;
+        cp_async16(&xs[stage][r][ch * 8], xbytes[i] ? xsrc[i] + kb * 64 : xsrc[i], xbytes[i]);
+      }
+      cp_async_commit();
+    };
+    auto load_w = [&](int kb, WRaw& w) {
+      const int k = kbeg + kb * 64 + 16 * t;
+      if constexpr (Q8) {
+        w.a = ld_stream16(W.qs + (size_t)f0 * K + k);
+        w.b = ld_stream16(W.qs + (size_t)(f0 + 8) * K + k);
+        w.da = h2f_bits(W.d[(size_t)f0 * KB + (k >> 5)]);
+        w.db = h2f_bits(W.d[(size_t)(f0 + 8) * KB + (k >> 5)]);
+      } else {
+        const T* wp = reinterpret_cast<const T*>(W.w);
+        w.a = ld_stream16(wp + (size_t)f0 * K + k);
+        w.b = ld_stream16(wp + (size_t)f0 * K + k + 8);
+        w.c = ld_stream16(wp + (size_t)(f0 + 8) * K + k);
+        w.d = ld_stream16(wp + (size_t)(f0 + 8) * K + k + 8);
+      }
+    };
+
+    float acc[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+
+    WRaw wc, wn;
+    load_x(0, 0);
+    load_w(0, wc);
+    for (int kb = 0; kb < nkb; ++kb) {
+      if (kb + 1 < nkb) {
+        load_x((kb + 1) & 1, kb + 1);
+        load_w(kb + 1, wn);
+        cp_async_wait<1>();
+      } else {
+        cp_async_wait<0>();
+      }
+      __syncthreads();
+
+      // A fragments for the 4 MMAs of this k-block
+      uint32_t af[4][4];
+      if constexpr (Q8) {
+        const uint32_t* ua = reinterpret_cast<const uint32_t*>(&wc.a);
+        const uint32_t* ub = reinterpret_cast<const uint32_t*>(&wc.b);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float e[4], f[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            // exact int8 -> f32 via the 2^23 magic (byte placed in the mantissa)
+            e[i] = (__int_as_float(__byte_perm(ua[j] ^ 0x80808080u, 0x4B000000u, 0x7440u | i)) - 8388736.f) * wc.da;
+            f[i] = (__int_as_float(__byte_perm(ub[j] ^ 0x80808080u, 0x4B000000u, 0x7440u | i)) - 8388736.f) * wc.db;
+          }
+          af[j][0] = Act<T>::pack2(e[0], e[1]);
+          af[j][1] = Act<T>::pack2(f[0], f[1]);
+          af[j][2] = Act<T>::pack2(e[2], e[3]);
+          af[j][3] = Act<T>::pack2(f[2], f[3]);
+        }
+      } else {
+        const uint32_t* ua = reinterpret_cast<const uint32_t*>(&wc.a);
+        const uint32_t* ub = reinterpret_cast<const uint32_t*>(&wc.b);
+        const uint32_t* uc = reinterpret_cast<const uint32_t*>(&wc.c);
+        const uint32_t* ud = reinterpret_cast<const uint32_t*>(&wc.d);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t* r0 = j < 2 ? ua : ub;
+          const uint32_t* r1 = j < 2 ? uc : ud;
+          af[j][0] = r0[(2 * j) & 3];
+          af[j][2] = r0[(2 * j + 1) & 3];
+          af[j][1] = r1[(2 * j) & 3];
+          af[j][3] = r1[(2 * j + 1) & 3];
+        }
+      }
+      const int st = kb & 1;
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        if (nt < n_tiles) {
+          const int4 x0 = *reinterpret_cast<const int4*>(&xs[st][nt * 8 + g][16 * t]);
+          const int4 x1 = *reinterpret_cast<const int4*>(&xs[st][nt * 8 + g][16 * t + 8]);
+          const uint32_t xw[8] = {(uint32_t)x0.x, (uint32_t)x0.y, (uint32_t)x0.z, (uint32_t)x0.w,
+                                  (uint32_t)x1.x, (uint32_t)x1.y, (uint32_t)x1.z, (uint32_t)x1.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) mma16816<T>(acc[nt], af[j], xw[2 * j], xw[2 * j + 1]);
+        }
+      }
+      __syncthreads();
+      wc = wn;
+    }
+
+    float* o = out + (size_t)blockIdx.y * split_stride;
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+      if (nt < n_tiles) {
+        const int lr = nt * 8 + 2 * t;
+        if (lr < rows) {
+          o[(size_t)(row0 + lr) * N + f0] = acc[nt][0];
+          o[(size_t)(row0 + lr) * N + f0 + 8] = acc[nt][2];
+        }
+        if (lr + 1 < rows) {
+          o[(size_t)(row0 + lr + 1) * N + f0] = acc[nt][1];
+          o[(size_t)(row0 + lr + 1) * N + f0 + 8] = acc[nt][3];
+        }
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// QKV epilogue (qwen3.rs:213-227): sum K-split partials, round, per-head
+// RMSNorm of q and k (q_norm / k_norm), RoPE with the activation-dtype tables
+// at the row's own position, then q -> q buffer and k, v -> the paged cache.
+// One warp per head, 4 dims per lane; the RoPE partner dim (d +- 64) lives 16
+// lanes away.
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(256) k_qkv_epilogue(Plan p, const float* __restrict__ part, int split,
+                                                      size_t split_stride, int Hq, int Hkv,
+                                                      const T* __restrict__ qn_w, const T* __restrict__ kn_w,
+                                                      const T* __restrict__ cos_t, const T* __restrict__ sin_t,
+                                                      T* __restrict__ q_out, KvView kv, int layer, float eps) {
+  const int n_rows = p.counts->n_rows;
+  const int S = effective_split(split, n_rows);
+  const int N = (Hq + 2 * Hkv) * kHeadDim;
+  for (int r = blockIdx.x; r < n_rows; r += gridDim.x) {
+  const int pos = p.row_pos[r], slot = p.row_slot[r];
+  const int page = kv.page_table[(size_t)slot * kv.max_pages_per_slot + (pos / kPageTokens)];
+  const int off = pos % kPageTokens;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  T* kvb = reinterpret_cast<T*>(kv.base);
+  for (int hh = warp; hh < Hq + 2 * Hkv; hh += 8) {
+    const int c = hh * kHeadDim + lane * 4;
+    float v[4];
+    {
+      const float* p0 = part + (size_t)r * N + c;
+      float4 a = *reinterpret_cast<const float4*>(p0);
+      for (int s = 1; s < S; ++s) {
+        const float4 b = *reinterpret_cast<const float4*>(p0 + (size_t)s * split_stride);
+        a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
+      }
+      v[0] = rnd<T>(a.x); v[1] = rnd<T>(a.y); v[2] = rnd<T>(a.z); v[3] = rnd<T>(a.w);
+    }
+    T* dst;
+    if (hh < Hq + Hkv) {
+      const T* nw = hh < Hq ? qn_w : kn_w;
+      const float ss = warp_sum(v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3]);
+      const float inv = rsqrtf(ss / kHeadDim + eps);
+      float y[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) y[i] = rnd<T>(v[i] * inv * Act<T>::to_f(nw[lane * 4 + i]));
+      const int dd = (lane & 15) * 4;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float pr = __shfl_xor_sync(0xffffffffu, y[i], 16);
+        const float cs = Act<T>::to_f(cos_t[(size_t)pos * (kHeadDim / 2) + dd + i]);
+        const float sn = Act<T>::to_f(sin_t[(size_t)pos * (kHeadDim / 2) + dd + i]);
+        v[i] = lane < 16 ? y[i] * cs - pr * sn : pr * sn + y[i] * cs;
+      }
+      dst = hh < Hq ? q_out + (size_t)r * Hq * kHeadDim + hh * kHeadDim
+                    : kvb + kv.elem_offset(layer, page, 0, hh - Hq) + (size_t)off * kHeadDim;
+    } else {
+      dst = kvb + kv.elem_offset(layer, page, 1, hh - Hq - Hkv) + (size_t)off * kHeadDim;
+    }
+    uint2 o;
+    o.x = Act<T>::pack2(v[0], v[1]);
+    o.y = Act<T>::pack2(v[2], v[3]);
+    *reinterpret_cast<uint2*>(dst + lane * 4) = o;
+  }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Split-KV GQA decode attention (qwen3.rs:229-257 for t = 1): one CTA per
+// (split item, kv head) computes both query heads of the group from one read
+// of each K/V row. 8 groups of 16 lanes each take 4 keys at a time (16-byte
+// loads, 8 dims per lane); online softmax in the exp2 domain; partial
+// (m, l, acc) per item, merged by k_attn_combine.
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(128) k_attn_decode(Plan p, int Hq, const T* __restrict__ q, KvView kv, int layer,
+                                                     float scale_log2, float* __restrict__ part_acc,
+                                                     float* __restrict__ part_ml) {
+  __shared__ float s_m[8][2], s_l[8][2];
+  __shared__ float s_acc[8][2][kHeadDim];
+  const int n_items = p.counts->n_ditems;
+  const int h = blockIdx.y;
+  const int grp = threadIdx.x >> 4, l16 = threadIdx.x & 15;
+  const T* kvb = reinterpret_cast<const T*>(kv.base);
+  const size_t v_off = (size_t)kv.kv_heads * kPageTokens * kHeadDim;
+  for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
+    const int r = p.di_row[it], k0 = p.di_start[it], k1 = p.di_end[it];
+    const int slot = p.row_slot[r];
+    const int* ptab = kv.page_table + (size_t)slot * kv.max_pages_per_slot;
+    float qa[8], qb[8];
+    {
+      const T* qr = q + (size_t)r * Hq * kHeadDim + (2 * h) * kHeadDim + l16 * 8;
+      const int4 va = *reinterpret_cast<const int4*>(qr);
+      const int4 vb = *reinterpret_cast<const int4*>(qr + kHeadDim);
+      const uint32_t* ua = reinterpret_cast<const uint32_t*>(&va);
+      const uint32_t* ub = reinterpret_cast<const uint32_t*>(&vb);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 fa = Act<T>::unpack2(ua[j]), fb = Act<T>::unpack2(ub[j]);
+        qa[2 * j] = fa.x * scale_log2; qa[2 * j + 1] = fa.y * scale_log2;
+        qb[2 * j] = fb.x * scale_log2; qb[2 * j + 1] = fb.y * scale_log2;
+      }
+    }
+    float m0 = -FLT_MAX, m1 = -FLT_MAX, l0 = 0.f, l1 = 0.f;
+    float acc0[8], acc1[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc0[i] = acc1[i] = 0.f;
+
+    // The trip count is uniform across the warp (both 16-lane halves iterate
+    // together) because the key reduction below shuffles over the full warp.
+    const int warp_first = k0 + (grp >> 1) * 8;
+    for (int wb = warp_first; wb < k1; wb += 32) {
+      const int tk = wb + (grp & 1) * 4;
+      int4 kk[4], vv[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int tok = tk + j;
+        if (tok < k1) {
+          const int page = ptab[tok >> 6];
+          const T* kp = kvb + kv.elem_offset(layer, page, 0, h) + (size_t)(tok & 63) * kHeadDim + l16 * 8;
+          kk[j] = *reinterpret_cast<const int4*>(kp);
+          vv[j] = *reinterpret_cast<const int4*>(kp + v_off);
+        } else {
+          kk[j] = make_int4(0, 0, 0, 0);
+          vv[j] = make_int4(0, 0, 0, 0);
+        }
+      }
+      float s0[4], s1[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t* u = reinterpret_cast<const uint32_t*>(&kk[j]);
+        float a = 0.f, b = 0.f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = Act<T>::unpack2(u[i]);
+          a = fmaf(qa[2 * i], f.x, a); a = fmaf(qa[2 * i + 1], f.y, a);
+          b = fmaf(qb[2 * i], f.x, b); b = fmaf(qb[2 * i + 1], f.y, b);
+        }
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) {
+          a += __shfl_xor_sync(0xffffffffu, a, o);
+          b += __shfl_xor_sync(0xffffffffu, b, o);
+        }
+        const bool valid = tk + j < k1;
+        s0[j] = valid ? a : -FLT_MAX;
+        s1[j] = valid ? b : -FLT_MAX;
+      }
+      const float mx0 = fmaxf(fmaxf(s0[0], s0[1]), fmaxf(s0[2], s0[3]));
+      const float mx1 = fmaxf(fmaxf(s1[0], s1[1]), fmaxf(s1[2], s1[3]));
+      const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+      const float c0 = exp2f(m0 - mn0), c1 = exp2f(m1 - mn1);
+      float p0[4], p1[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const bool valid = tk + j < k1;  // a half may hold no valid key at all
+        p0[j] = valid ? exp2f(s0[j] - mn0) : 0.f;
+        p1[j] = valid ? exp2f(s1[j] - mn1) : 0.f;
+      }
+      l0 = l0 * c0 + (p0[0] + p0[1]) + (p0[2] + p0[3]);
+      l1 = l1 * c1 + (p1[0] + p1[1]) + (p1[2] + p1[3]);
+      m0 = mn0;
+      m1 = mn1;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        acc0[i] *= c0;
+        acc1[i] *= c1;
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t* u = reinterpret_cast<const uint32_t*>(&vv[j]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 f = Act<T>::unpack2(u[i]);
+          acc0[2 * i] = fmaf(p0[j], f.x, acc0[2 * i]);
+          acc0[2 * i + 1] = fmaf(p0[j], f.y, acc0[2 * i + 1]);
+          acc1[2 * i] = fmaf(p1[j], f.x, acc1[2 * i]);
+          acc1[2 * i + 1] = fmaf(p1[j], f.y, acc1[2 * i + 1]);
+        }
+      }
+    }
+    // merge the 8 groups
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      s_acc[grp][0][l16 * 8 + i] = acc0[i];
+      s_acc[grp][1][l16 * 8 + i] = acc1[i];
+    }
+    if (l16 == 0) {
+      s_m[grp][0] = m0; s_m[grp][1] = m1;
+      s_l[grp][0] = l0; s_l[grp][1] = l1;
+    }
+    __syncthreads();
+    {
+      const int d = threadIdx.x;  // 128 threads = 128 dims
+#pragma unroll
+      for (int hd = 0; hd < 2; ++hd) {
+        float M = -FLT_MAX;
+#pragma unroll
+        for (int gi = 0; gi < 8; ++gi) M = fmaxf(M, s_m[gi][hd]);
+        float A = 0.f, L = 0.f;
+#pragma unroll
+        for (int gi = 0; gi < 8; ++gi) {
+          const float wgt = exp2f(s_m[gi][hd] - M);
+          A = fmaf(s_acc[gi][hd][d], wgt, A);
+          L = fmaf(s_l[gi][hd], wgt, L);
+        }
+        const size_t e = (size_t)it * Hq + 2 * h + hd;
+        part_acc[e * kHeadDim + d] = A;
+        if (d == 0) {
+          part_ml[e * 2] = M;
+          part_ml[e * 2 + 1] = L;
+        }
+      }
+    }
+    __syncthreads();
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) k_attn_combine(Plan p, int Hq, const float* __restrict__ part_acc,
+                                                      const float* __restrict__ part_ml, T* __restrict__ ctx) {
+  const int n_dec = p.counts->n_decode;
+  for (int r = blockIdx.x; r < n_dec; r += gridDim.x) {
+  const int i0 = p.drow_item0[r], n = p.drow_nitems[r];
+  for (int e = threadIdx.x; e < Hq * kHeadDim; e += blockDim.x) {
+    const int hq = e / kHeadDim, d = e % kHeadDim;
+    float M = -FLT_MAX;
+    for (int i = 0; i < n; ++i) M = fmaxf(M, part_ml[((size_t)(i0 + i) * Hq + hq) * 2]);
+    float A = 0.f, L = 0.f;
+    for (int i = 0; i < n; ++i) {
+      const size_t b = (size_t)(i0 + i) * Hq + hq;
+      const float wgt = exp2f(part_ml[b * 2] - M);
+      L = fmaf(part_ml[b * 2 + 1], wgt, L);
+      A = fmaf(part_acc[b * kHeadDim + d], wgt, A);
+    }
+    ctx[(size_t)r * Hq * kHeadDim + e] = Act<T>::from_f(A / L);
+  }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Chunked-prefill flash attention (qwen3.rs:229-257 with the causal mask of
+// :523-562): one CTA per (block of <= 32 query rows of one sequence, kv head)
+// covers both query heads of the group (4 warps = 2 heads x 2 x 16 rows) so
+// each K/V tile is loaded once. K/V tiles = one 64-position page, cp.async
+// double-buffered into XOR-swizzled shared memory; QK^T and PV on mma.sync.
+// Positions at or beyond the cached length are zero-filled, so masked columns
+// never multiply a stale value.
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(128) k_attn_prefill(Plan p, int Hq, const T* __restrict__ q, KvView kv, int layer,
+                                                      float scale_log2, T* __restrict__ ctx) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int n_blocks = p.counts->n_pblocks;
+  for (int b = blockIdx.x; b < n_blocks; b += gridDim.x) {
+  const int h = blockIdx.y;
+  const int r0 = p.pb_row0[b], n = p.pb_n[b];
+  const int slot = p.row_slot[r0], pos0 = p.row_pos[r0];
+  const int kv_len = pos0 + n;
+  const int n_tiles = (kv_len + 63) >> 6;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int qh = 2 * h + (warp >> 1);
+  const int tq0 = (warp & 1) * 16;
+  const int ra = tq0 + g, rb = ra + 8;
+  const int qpa = pos0 + ra, qpb = pos0 + rb;
+  const int* ptab = kv.page_table + (size_t)slot * kv.max_pages_per_slot;
+  const T* kvb = reinterpret_cast<const T*>(kv.base);
+  const size_t v_off = (size_t)kv.kv_heads * kPageTokens * kHeadDim;
+
+  uint32_t qf[8][4];
+  {
+    const uint32_t* qa = reinterpret_cast<const uint32_t*>(q + (size_t)(r0 + ra) * Hq * kHeadDim + qh * kHeadDim);
+    const uint32_t* qb = reinterpret_cast<const uint32_t*>(q + (size_t)(r0 + rb) * Hq * kHeadDim + qh * kHeadDim);
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      qf[ks][0] = ra < n ? qa[ks * 8 + t] : 0u;
+      qf[ks][1] = rb < n ? qb[ks * 8 + t] : 0u;
+      qf[ks][2] = ra < n ? qa[ks * 8 + 4 + t] : 0u;
+      qf[ks][3] = rb < n ? qb[ks * 8 + 4 + t] : 0u;
+    }
+  }
+  float o[16][4];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m_a = -FLT_MAX, m_b = -FLT_MAX, l_a = 0.f, l_b = 0.f;
+
+  auto load_tile = [&](int stage, int kt) {
+    const int page = ptab[kt];
+    const T* ksrc = kvb + kv.elem_offset(layer, page, 0, h);
+    const T* vsrc = ksrc + v_off;
+    const int valid = min(64, kv_len - kt * 64);
+    uint8_t* ks = smem + stage * 32768;
+    uint8_t* vs = ks + 16384;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int c = threadIdx.x + i * 128;
+      const int row = c >> 4, ch = c & 15;
+      const int soff = row * 256 + ((ch ^ (row & 7)) << 4);
+      const int bytes = row < valid ? 16 : 0;
+      cp_async16(ks + soff, ksrc + row * kHeadDim + ch * 8, bytes);
+      cp_async16(vs + soff, vsrc + row * kHeadDim + ch * 8, bytes);
+    }
+    cp_async_commit();
+  };
+
+  load_tile(0, 0);
+  for (int kt = 0; kt < n_tiles; ++kt) {
+    if (kt + 1 < n_tiles) {
+      load_tile((kt + 1) & 1, kt + 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const uint32_t ks_base = smem_u32(smem + (kt & 1) * 32768);
+    const uint32_t vs_base = ks_base + 16384;
+
+    float s[8][4];
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+      s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+      const int key = nt * 8 + (lane & 7);
+#pragma unroll
+      for (int kp = 0; kp < 4; ++kp) {
+        const int ch = 4 * kp + (lane >> 3);
+        uint32_t rr[4];
+        ldmatrix_x4(rr, ks_base + key * 256 + ((ch ^ (key & 7)) << 4));
+        mma16816<T>(s[nt], qf[2 * kp], rr[0], rr[1]);
+        mma16816<T>(s[nt], qf[2 * kp + 1], rr[2], rr[3]);
+      }
+    }
+    float mx_a = -FLT_MAX, mx_b = -FLT_MAX;
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+      const int key = kt * 64 + nt * 8 + 2 * t;
+      s[nt][0] = key <= qpa ? s[nt][0] * scale_log2 : -FLT_MAX;
+      s[nt][1] = key + 1 <= qpa ? s[nt][1] * scale_log2 : -FLT_MAX;
+      s[nt][2] = key <= qpb ? s[nt][2] * scale_log2 : -FLT_MAX;
+      s[nt][3] = key + 1 <= qpb ? s[nt][3] * scale_log2 : -FLT_MAX;
+      mx_a = fmaxf(mx_a, fmaxf(s[nt][0], s[nt][1]));
+      mx_b = fmaxf(mx_b, fmaxf(s[nt][2], s[nt][3]));
+    }
+    mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 1));
+    mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 2));
+    mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 1));
+    mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 2));
+    const float mn_a = fmaxf(m_a, mx_a), mn_b = fmaxf(m_b, mx_b);
+    const float ca = exp2f(m_a - mn_a), cb = exp2f(m_b - mn_b);
+    float sum_a = 0.f, sum_b = 0.f;
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+      s[nt][0] = exp2f(s[nt][0] - mn_a);
+      s[nt][1] = exp2f(s[nt][1] - mn_a);
+      s[nt][2] = exp2f(s[nt][2] - mn_b);
+      s[nt][3] = exp2f(s[nt][3] - mn_b);
+      sum_a += s[nt][0] + s[nt][1];
+      sum_b += s[nt][2] + s[nt][3];
+    }
+    l_a = l_a * ca + sum_a;
+    l_b = l_b * cb + sum_b;
+    m_a = mn_a;
+    m_b = mn_b;
+#pragma unroll
+    for (int dn = 0; dn < 16; ++dn) {
+      o[dn][0] *= ca; o[dn][1] *= ca;
+      o[dn][2] *= cb; o[dn][3] *= cb;
+    }
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      uint32_t pa[4];
+      pa[0] = Act<T>::pack2(s[2 * kk][0], s[2 * kk][1]);
+      pa[1] = Act<T>::pack2(s[2 * kk][2], s[2 * kk][3]);
+      pa[2] = Act<T>::pack2(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+      pa[3] = Act<T>::pack2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+      const int key = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+#pragma unroll
+      for (int dp = 0; dp < 8; ++dp) {
+        const int ch = 2 * dp + (lane >> 4);
+        uint32_t rr[4];
+        ldmatrix_x4_trans(rr, vs_base + key * 256 + ((ch ^ (key & 7)) << 4));
+        mma16816<T>(o[2 * dp], pa, rr[0], rr[1]);
+        mma16816<T>(o[2 * dp + 1], pa, rr[2], rr[3]);
+      }
+    }
+    __syncthreads();
+  }
+  l_a += __shfl_xor_sync(0xffffffffu, l_a, 1);
+  l_a += __shfl_xor_sync(0xffffffffu, l_a, 2);
+  l_b += __shfl_xor_sync(0xffffffffu, l_b, 1);
+  l_b += __shfl_xor_sync(0xffffffffu, l_b, 2);
+  const float ia = 1.f / l_a, ib = 1.f / l_b;
+  T* ca_ = ctx + (size_t)(r0 + ra) * Hq * kHeadDim + qh * kHeadDim;
+  T* cb_ = ctx + (size_t)(r0 + rb) * Hq * kHeadDim + qh * kHeadDim;
+#pragma unroll
+  for (int dn = 0; dn < 16; ++dn) {
+    if (ra < n) *reinterpret_cast<uint32_t*>(ca_ + dn * 8 + 2 * t) = Act<T>::pack2(o[dn][0] * ia, o[dn][1] * ia);
+    if (rb < n) *reinterpret_cast<uint32_t*>(cb_ + dn * 8 + 2 * t) = Act<T>::pack2(o[dn][2] * ib, o[dn][3] * ib);
+  }
+  __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// SwiGLU (qwen3.rs:288-292): h = rnd(rnd(silu(rnd(gate))) * rnd(up)).
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(256) k_silu_mul(const int* __restrict__ n_rows_ptr, const float* __restrict__ part,
+                                                  int split, size_t split_stride, int I, T* __restrict__ h) {
+  const int n_rows = *n_rows_ptr;
+  const int S = effective_split(split, n_rows);
+  for (int r = blockIdx.x; r < n_rows; r += gridDim.x) {
+  const float* p0 = part + (size_t)r * 2 * I;
+  for (int c = threadIdx.x * 4; c < I; c += blockDim.x * 4) {
+    float4 gs = *reinterpret_cast<const float4*>(p0 + c);
+    float4 us = *reinterpret_cast<const float4*>(p0 + I + c);
+    for (int s = 1; s < S; ++s) {
+      const float4 a = *reinterpret_cast<const float4*>(p0 + (size_t)s * split_stride + c);
+      const float4 b = *reinterpret_cast<const float4*>(p0 + (size_t)s * split_stride + I + c);
+      gs.x += a.x; gs.y += a.y; gs.z += a.z; gs.w += a.w;
+      us.x += b.x; us.y += b.y; us.z += b.z; us.w += b.w;
+    }
+    const float gv[4] = {gs.x, gs.y, gs.z, gs.w}, uv[4] = {us.x, us.y, us.z, us.w};
+    float o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float gr = rnd<T>(gv[i]);
+      const float sg = rnd<T>(gr / (1.f + expf(-gr)));
+      o[i] = sg * rnd<T>(uv[i]);
+    }
+    uint2 w;
+    w.x = Act<T>::pack2(o[0], o[1]);
+    w.y = Act<T>::pack2(o[2], o[3]);
+    *reinterpret_cast<uint2*>(h + (size_t)r * I + c) = w;
+  }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Logits + greedy pick (qwen3.rs:459-463, engine.rs:550-559): logits are the
+// lm_head result rounded to the activation dtype, then widened to f32; the
+// argmax takes the lowest index among equal maxima.
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(1024) k_logits_argmax(const int* __restrict__ n_sample_ptr,
+                                                        const float* __restrict__ part, int V,
+                                                        float* __restrict__ logits, int* __restrict__ next_ids) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  const int r = blockIdx.x;
+  if (r >= *n_sample_ptr) return;
+  const float* pr = part + (size_t)r * V;
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int v = threadIdx.x * 4; v < V; v += 1024 * 4) {
+    float4 a = *reinterpret_cast<const float4*>(pr + v);
+    a.x = rnd<T>(a.x); a.y = rnd<T>(a.y); a.z = rnd<T>(a.z); a.w = rnd<T>(a.w);
+    if (logits) *reinterpret_cast<float4*>(logits + (size_t)r * V + v) = a;
+    if (a.x > best) { best = a.x; bi = v; }
+    if (a.y > best) { best = a.y; bi = v + 1; }
+    if (a.z > best) { best = a.z; bi = v + 2; }
+    if (a.w > best) { best = a.w; bi = v + 3; }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) { sv[warp] = best; si[warp] = bi; }
+  __syncthreads();
+  if (warp == 0) {
+    best = sv[lane];
+    bi = si[lane];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+    }
+    if (lane == 0) next_ids[r] = bi;
+  }
+}
+
+// Dequantise / widen one stored projection to f32 (inspection only).
+template <typename T>
+__global__ void k_dequant(LinW W, float* __restrict__ out) {
+  const size_t total = (size_t)W.N * W.K;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    if (W.q8) {
+      const size_t n = i / W.K, k = i % W.K;
+      out[i] = (float)W.qs[i] * h2f_bits(W.d[n * (W.K / kQ8Block) + k / kQ8Block]);
+    } else {
+      out[i] = Act<T>::to_f(reinterpret_cast<const T*>(W.w)[i]);
+    }
+  }
+}
+
+}  // namespace
+
+// ---- launchers ----------------------------------------------------------------------
+
+#define FMD_DISPATCH(at, ...)                  \
+  do {                                         \
+    if ((at) == kBF16) {                       \
+      using T = __nv_bfloat16;                 \
+      __VA_ARGS__;                             \
+    } else {                                   \
+      using T = __half;                        \
+      __VA_ARGS__;                             \
+    }                                          \
+  } while (0)
+
+void launch_embed_norm(ActType at, const Plan& p, int R, const void* table, const void* arena, void* x, const void* w,
+                       void* xn, int H, float eps, cudaStream_t s) {
+  FMD_DISPATCH(at, k_embed_norm<T><<<R, 128, 0, s>>>(p, (const T*)table, (const T*)arena, (T*)x, (const T*)w,
+                                                      (T*)xn, H, eps));
+}
+
+void launch_linear(ActType at, const LinW& W, const void* x, int ldx, const int* row_map, const int* n_rows_ptr,
+                   int max_rows, float* out, size_t split_stride, cudaStream_t s) {
+  const int row_tiles = (max_rows + 63) / 64;
+  dim3 grid(W.N / 64, W.split, row_tiles < 8 ? row_tiles : 8);
+  FMD_DISPATCH(at, {
+    if (W.q8)
+      k_linear<T, true><<<grid, 128, 0, s>>>((const T*)x, ldx, row_map, n_rows_ptr, W, out, split_stride);
+    else
+      k_linear<T, false><<<grid, 128, 0, s>>>((const T*)x, ldx, row_map, n_rows_ptr, W, out, split_stride);
+  });
+}
+
+void launch_qkv_epilogue(ActType at, const Plan& p, int R, const float* part, int split, size_t split_stride,
+                         int Hq, int Hkv, const void* qn_w, const void* kn_w, const void* cos, const void* sin,
+                         void* q_out, const KvView& kv, int layer, float eps, cudaStream_t s) {
+  FMD_DISPATCH(at, k_qkv_epilogue<T><<<R, 256, 0, s>>>(p, part, split, split_stride, Hq, Hkv, (const T*)qn_w,
+                                                        (const T*)kn_w, (const T*)cos, (const T*)sin, (T*)q_out, kv,
+                                                        layer, eps));
+}
+
+void launch_attn_decode(ActType at, const Plan& p, int grid_items, int Hq, int Hkv, const void* q, const KvView& kv,
+                        int layer, float scale, float* part_acc, float* part_ml, cudaStream_t s) {
+  const float scale_log2 = scale * 1.4426950408889634f;
+  dim3 grid(grid_items, Hkv);
+  FMD_DISPATCH(at, k_attn_decode<T><<<grid, 128, 0, s>>>(p, Hq, (const T*)q, kv, layer, scale_log2, part_acc,
+                                                          part_ml));
+}
+
+void launch_attn_combine(ActType at, const Plan& p, int R, int Hq, const float* part_acc, const float* part_ml,
+                         void* ctx, cudaStream_t s) {
+  FMD_DISPATCH(at, k_attn_combine<T><<<R, 256, 0, s>>>(p, Hq, part_acc, part_ml, (T*)ctx));
+}
+
+void launch_attn_prefill(ActType at, const Plan& p, int PB, int Hq, int Hkv, const void* q, const KvView& kv,
+                         int layer, float scale, void* ctx, cudaStream_t s) {
+  const float scale_log2 = scale * 1.4426950408889634f;
+  dim3 grid(PB, Hkv);
+  const int smem = 65536;
+  FMD_DISPATCH(at, k_attn_prefill<T><<<grid, 128, smem, s>>>(p, Hq, (const T*)q, kv, layer, scale_log2, (T*)ctx));
+}
+
+void launch_residual_norm(ActType at, const int* n_rows_ptr, int R, void* x, const float* part, int split,
+                          size_t split_stride, const void* w, void* xn, int H, float eps, cudaStream_t s) {
+  FMD_DISPATCH(at, k_residual_norm<T><<<R, 128, 0, s>>>(n_rows_ptr, (T*)x, part, split, split_stride, (const T*)w,
+                                                         (T*)xn, H, eps));
+}
+
+void launch_silu_mul(ActType at, const int* n_rows_ptr, int R, const float* part, int split, size_t split_stride,
+                     int I, void* h, cudaStream_t s) {
+  FMD_DISPATCH(at, k_silu_mul<T><<<R, 256, 0, s>>>(n_rows_ptr, part, split, split_stride, I, (T*)h));
+}
+
+void launch_logits_argmax(ActType at, const int* n_sample_ptr, int B, const float* part, int V, float* logits,
+                          int* next_ids, cudaStream_t s) {
+  FMD_DISPATCH(at, k_logits_argmax<T><<<B, 1024, 0, s>>>(n_sample_ptr, part, V, logits, next_ids));
+}
+
+cudaError_t init_kernels() {
+  cudaError_t e = cudaFuncSetAttribute(k_attn_prefill<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 65536);
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(k_attn_prefill<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, 65536);
+}
+
+void launch_dequant(ActType at, const LinW& W, float* out, cudaStream_t s) {
+  FMD_DISPATCH(at, k_dequant<T><<<1024, 256, 0, s>>>(W, out));
+}
+
+}  // namespace fmd

@@ -1,0 +1,136 @@
+// Device-side data structures shared by the kernels, the scheduler and the
+// host runtime, plus the launchers the runtime calls.
+#pragma once
+
+#include "fmd_common.cuh"
+
+namespace fmd {
+
+// Counts of one forward pass ("step"). Written by the host (operator entry
+// points) or by the device scheduler (continuous-batching engine).
+struct PlanCounts {
+  int n_rows;     // token rows in this pass
+  int n_decode;   // rows [0, n_decode) are one-token decode rows
+  int n_sample;   // rows whose logits / greedy id are wanted
+  int n_pblocks;  // prefill attention blocks (<= 32 consecutive rows of one slot)
+  int n_ditems;   // decode attention split items
+  int finished;   // engine: every request is done
+  int pad0, pad1;
+};
+
+// Per-pass token plan. All arrays live in one device buffer (`PlanLayout`).
+struct Plan {
+  PlanCounts* counts;
+  int* row_slot;     // [R] sequence slot of each row
+  int* row_pos;      // [R] absolute position (= KV index the row writes)
+  int* row_tok;      // [R] token id, or -1: take the row from the embedding arena
+  int* row_emb;      // [R] arena row when row_tok < 0
+  int* sample_row;   // [B] rows that produce logits, in output order
+  int* sample_slot;  // [B] their slots (engine bookkeeping)
+  int* pb_row0;      // [PB] first row of a prefill attention block
+  int* pb_n;         // [PB] rows in the block (1..32)
+  int* di_row;       // [DI] decode row of a split item
+  int* di_start;     // [DI] first key position of the item
+  int* di_end;       // [DI] one past the last key position
+  int* drow_item0;   // [R]  first split item of a decode row
+  int* drow_nitems;  // [R]  split items of a decode row
+};
+
+// Sizes of the plan arrays and their offsets (in ints) inside one buffer.
+struct PlanLayout {
+  int R, B, PB, DI;
+  size_t off_counts, off_row_slot, off_row_pos, off_row_tok, off_row_emb, off_sample_row, off_sample_slot,
+      off_pb_row0, off_pb_n, off_di_row, off_di_start, off_di_end, off_drow_item0, off_drow_nitems, total;
+  void init(int r, int b, int pb, int di) {
+    R = r; B = b; PB = pb; DI = di;
+    size_t o = 0;
+    off_counts = o; o += sizeof(PlanCounts) / sizeof(int);
+    off_row_slot = o; o += R;
+    off_row_pos = o; o += R;
+    off_row_tok = o; o += R;
+    off_row_emb = o; o += R;
+    off_sample_row = o; o += B;
+    off_sample_slot = o; o += B;
+    off_pb_row0 = o; o += PB;
+    off_pb_n = o; o += PB;
+    off_di_row = o; o += DI;
+    off_di_start = o; o += DI;
+    off_di_end = o; o += DI;
+    off_drow_item0 = o; o += R;
+    off_drow_nitems = o; o += R;
+    total = o;
+  }
+  Plan bind(int* base) const {
+    Plan p;
+    p.counts = reinterpret_cast<PlanCounts*>(base + off_counts);
+    p.row_slot = base + off_row_slot;
+    p.row_pos = base + off_row_pos;
+    p.row_tok = base + off_row_tok;
+    p.row_emb = base + off_row_emb;
+    p.sample_row = base + off_sample_row;
+    p.sample_slot = base + off_sample_slot;
+    p.pb_row0 = base + off_pb_row0;
+    p.pb_n = base + off_pb_n;
+    p.di_row = base + off_di_row;
+    p.di_start = base + off_di_start;
+    p.di_end = base + off_di_end;
+    p.drow_item0 = base + off_drow_item0;
+    p.drow_nitems = base + off_drow_nitems;
+    return p;
+  }
+};
+
+constexpr int kRowsPerPBlock = 32;   // query rows per prefill attention block
+constexpr int kDecodeItemTokens = 256;  // keys per decode attention split item
+
+// Paged KV pool: [layer][page][k|v][kv_head][kPageTokens][kHeadDim], act dtype.
+struct KvView {
+  void* base;
+  const int* page_table;  // [max_slots][max_pages_per_slot]
+  int n_pages;
+  int max_pages_per_slot;
+  int kv_heads;
+  __host__ __device__ size_t elem_offset(int layer, int page, int kv, int head) const {
+    return ((((size_t)layer * n_pages + page) * 2 + kv) * kv_heads + head) * (size_t)(kPageTokens * kHeadDim);
+  }
+};
+
+// A projection stored on the device: Q8_0 as int8 [N][K] + f16 scales
+// [N][K/32], or dense activation-dtype [N][K].
+struct LinW {
+  int N = 0, K = 0;
+  bool q8 = false;
+  const int8_t* qs = nullptr;
+  const uint16_t* d = nullptr;
+  const void* w = nullptr;
+  int split = 1;  // K splits used when a pass has <= 64 rows
+};
+
+// Device-side K split actually used for a pass with `n_rows` rows.
+__host__ __device__ inline int effective_split(int split, int n_rows) { return n_rows <= 64 ? split : 1; }
+
+enum ActType { kBF16 = 0, kF16 = 1 };
+
+// ---- launchers (fmd_kernels.cu) -------------------------------------------------
+void launch_embed_norm(ActType at, const Plan& p, int R, const void* table, const void* arena, void* x, const void* w,
+                       void* xn, int H, float eps, cudaStream_t s);
+void launch_linear(ActType at, const LinW& W, const void* x, int ldx, const int* row_map, const int* n_rows_ptr,
+                   int max_rows, float* out, size_t split_stride, cudaStream_t s);
+void launch_qkv_epilogue(ActType at, const Plan& p, int R, const float* part, int split, size_t split_stride,
+                         int Hq, int Hkv, const void* qn_w, const void* kn_w, const void* cos, const void* sin,
+                         void* q_out, const KvView& kv, int layer, float eps, cudaStream_t s);
+void launch_attn_decode(ActType at, const Plan& p, int grid_items, int Hq, int Hkv, const void* q, const KvView& kv,
+                        int layer, float scale, float* part_acc, float* part_ml, cudaStream_t s);
+void launch_attn_combine(ActType at, const Plan& p, int R, int Hq, const float* part_acc, const float* part_ml,
+                         void* ctx, cudaStream_t s);
+void launch_attn_prefill(ActType at, const Plan& p, int PB, int Hq, int Hkv, const void* q, const KvView& kv,
+                         int layer, float scale, void* ctx, cudaStream_t s);
+void launch_residual_norm(ActType at, const int* n_rows_ptr, int R, void* x, const float* part, int split,
+                          size_t split_stride, const void* w, void* xn, int H, float eps, cudaStream_t s);
+void launch_silu_mul(ActType at, const int* n_rows_ptr, int R, const float* part, int split, size_t split_stride,
+                     int I, void* h, cudaStream_t s);
+void launch_logits_argmax(ActType at, const int* n_sample_ptr, int B, const float* part, int V, float* logits,
+                          int* next_ids, cudaStream_t s);
+void launch_dequant(ActType at, const LinW& W, float* out, cudaStream_t s);
+
+}  // namespace fmd

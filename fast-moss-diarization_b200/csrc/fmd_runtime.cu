@@ -1,0 +1,1129 @@
+// Host runtime of the B200 decoder: handle, weight upload (with the Q8_0
+// quantiser of linear.rs:194-202), paged KV pool, per-pass plans, the forward
+// pass, the continuous-batching engine loop with CUDA-graph replay, and the
+// extern "C" entry points declared in include/fmd_decoder.h.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "../../include/fmd_decoder.h"
+#include "fmd_kernels.cuh"
+#include "fmd_scheduler.cuh"
+
+namespace fmd {
+cudaError_t init_kernels();
+}
+
+using namespace fmd;
+
+namespace {
+
+constexpr int kVersion = 1;
+constexpr int kMaxSlotsLimit = 256;
+constexpr int kEngineCheckEvery = 16;
+
+struct Status {
+  int code;
+  std::string msg;
+};
+
+struct DevBuf {
+  void* p = nullptr;
+  size_t bytes = 0;
+};
+
+struct LayerDev {
+  void* in_norm = nullptr;
+  void* post_norm = nullptr;
+  void* q_norm = nullptr;
+  void* k_norm = nullptr;
+  LinW qkv, o, gate_up, down;
+};
+
+uint16_t f32_to_bf16_bits(float f) {
+  __nv_bfloat16 b = __float2bfloat16_rn(f);
+  return *reinterpret_cast<uint16_t*>(&b);
+}
+uint16_t f32_to_f16_bits(float f) {
+  __half h = __float2half_rn(f);
+  return *reinterpret_cast<uint16_t*>(&h);
+}
+float bf16_bits_to_f32(uint16_t b) {
+  uint32_t u = (uint32_t)b << 16;
+  float f;
+  std::memcpy(&f, &u, 4);
+  return f;
+}
+float f16_bits_to_f32(uint16_t b) {
+  __half h = *reinterpret_cast<__half*>(&b);
+  return __half2float(h);
+}
+
+// GGML Q8_0 quantisation of one row-major (rows, cols) f32 matrix into the
+// structure-of-arrays device layout (int8 [rows][cols] + f16 [rows][cols/32]).
+// d = amax/127; id = 1/d (0 if d == 0); q = roundf(x * id) (half away from 0).
+void quantize_rows(const float* src, int64_t rows, int64_t cols, int8_t* qs, uint16_t* d) {
+  auto work = [&](int64_t r0, int64_t r1) {
+    for (int64_t r = r0; r < r1; ++r) {
+      for (int64_t b = 0; b < cols / 32; ++b) {
+        const float* x = src + r * cols + b * 32;
+        float amax = 0.f;
+        for (int j = 0; j < 32; ++j) amax = std::max(amax, std::fabs(x[j]));
+        const float dd = amax / 127.f;
+        const float id = dd != 0.f ? 1.f / dd : 0.f;
+        d[r * (cols / 32) + b] = f32_to_f16_bits(dd);
+        for (int j = 0; j < 32; ++j) qs[r * cols + b * 32 + j] = (int8_t)std::roundf(x[j] * id);
+      }
+    }
+  };
+  const int64_t nt = std::max<int64_t>(1, std::min<int64_t>(std::thread::hardware_concurrency(), rows / 256));
+  std::vector<std::thread> th;
+  for (int64_t i = 0; i < nt; ++i) th.emplace_back(work, rows * i / nt, rows * (i + 1) / nt);
+  for (auto& t : th) t.join();
+}
+
+}  // namespace
+
+struct fmd_handle {
+  fmd_config cfg{};
+  int precision = 0;
+  bool q8 = false;
+  ActType at = kBF16;
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  std::string err;
+  std::vector<DevBuf> allocs;
+  int64_t weight_bytes = 0, kv_bytes = 0, work_bytes = 0;
+
+  // model
+  bool loaded = false;
+  void* embed = nullptr;
+  void* final_norm = nullptr;
+  LinW lm_head;
+  std::vector<LayerDev> layers;
+  void* rope_cos = nullptr;
+  void* rope_sin = nullptr;
+  int rope_len = 0;
+  float attn_scale = 0.f;
+
+  // kv pool + work buffers
+  bool reserved = false;
+  int max_slots = 0, max_rows = 0, n_pages = 0, max_pages_per_slot = 0;
+  int pb_max = 0, di_max = 0, di_grid = 0, pb_grid = 0;
+  KvView kv{};
+  int* d_page_table = nullptr;
+  std::vector<int> h_page_table;
+  std::vector<int> free_pages;           // host allocator (operator mode)
+  std::vector<int> slot_cap, slot_len, slot_npages;
+  void *x = nullptr, *xn = nullptr, *qbuf = nullptr, *ctx = nullptr, *hbuf = nullptr, *arena = nullptr;
+  float *part = nullptr, *pacc = nullptr, *pml = nullptr, *logits = nullptr;
+  size_t split_stride = 0;
+  int* next_ids = nullptr;
+  PlanLayout layout{};
+  int* d_plan = nullptr;
+  int* h_plan = nullptr;  // pinned mirror
+  Plan plan{};
+  int64_t arena_rows = 0;
+
+  // engine
+  DevBuf eng_reqs, eng_arena, eng_tokens, eng_results;
+  int eng_n_reqs = 0, eng_tok_stride = 0;
+  int* eng_slot = nullptr;  // 7 arrays of max_slots
+  int* eng_free = nullptr;
+  EngineCounters* eng_ctr = nullptr;
+  EngineCounters* h_ctr = nullptr;
+  cudaGraphExec_t graph_exec = nullptr;
+  int graph_batch = -1, graph_chunk = -1;
+
+  int elem() const { return 2; }
+  int H() const { return cfg.hidden_size; }
+  int Hq() const { return cfg.num_attention_heads; }
+  int Hkv() const { return cfg.num_key_value_heads; }
+  int qkvN() const { return (Hq() + 2 * Hkv()) * kHeadDim; }
+};
+
+namespace {
+
+int fail(fmd_handle* h, int code, const std::string& msg) {
+  if (h) h->err = msg;
+  return code;
+}
+
+#define CK(call)                                                                                         \
+  do {                                                                                                   \
+    cudaError_t e_ = (call);                                                                             \
+    if (e_ != cudaSuccess)                                                                               \
+      return fail(h, e_ == cudaErrorMemoryAllocation ? FMD_ENOMEM : FMD_EIO,                              \
+                  std::string(#call) + ": " + cudaGetErrorString(e_));                                    \
+  } while (0)
+
+int dev_alloc(fmd_handle* h, size_t bytes, void** out, int64_t* counter) {
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes ? bytes : 16);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(h, FMD_ENOMEM, "cudaMalloc of " + std::to_string(bytes) + " bytes failed: " + cudaGetErrorString(e));
+  }
+  h->allocs.push_back({p, bytes});
+  if (counter) *counter += (int64_t)bytes;
+  *out = p;
+  return FMD_OK;
+}
+
+int upload(fmd_handle* h, void* dst, const void* src, size_t bytes) {
+  CK(cudaMemcpy(dst, src, bytes, cudaMemcpyHostToDevice));
+  return FMD_OK;
+}
+
+// Host tensor -> f32 vector
+bool to_f32(const fmd_tensor& t, size_t n, std::vector<float>& out) {
+  out.resize(n);
+  if (t.data == nullptr) return false;
+  switch (t.dtype) {
+    case FMD_DT_F32: std::memcpy(out.data(), t.data, n * 4); return true;
+    case FMD_DT_BF16: {
+      const uint16_t* s = (const uint16_t*)t.data;
+      for (size_t i = 0; i < n; ++i) out[i] = bf16_bits_to_f32(s[i]);
+      return true;
+    }
+    case FMD_DT_F16: {
+      const uint16_t* s = (const uint16_t*)t.data;
+      for (size_t i = 0; i < n; ++i) out[i] = f16_bits_to_f32(s[i]);
+      return true;
+    }
+    default: return false;
+  }
+}
+
+// Dense host tensor -> activation dtype on the device.
+int upload_dense(fmd_handle* h, const fmd_tensor& t, size_t n, void** out, const char* what) {
+  if (t.data == nullptr) return fail(h, FMD_EINVAL, std::string("missing tensor ") + what);
+  if (t.dtype == FMD_DT_Q8_0) return fail(h, FMD_EINVAL, std::string(what) + " must be dense");
+  std::vector<uint16_t> bits(n);
+  const bool bf = h->at == kBF16;
+  if ((bf && t.dtype == FMD_DT_BF16) || (!bf && t.dtype == FMD_DT_F16)) {
+    std::memcpy(bits.data(), t.data, n * 2);
+  } else {
+    std::vector<float> f;
+    if (!to_f32(t, n, f)) return fail(h, FMD_EINVAL, std::string("bad dtype for ") + what);
+    for (size_t i = 0; i < n; ++i) bits[i] = bf ? f32_to_bf16_bits(f[i]) : f32_to_f16_bits(f[i]);
+  }
+  int rc = dev_alloc(h, n * 2, out, &h->weight_bytes);
+  if (rc) return rc;
+  return upload(h, *out, bits.data(), n * 2);
+}
+
+// Projection parts stacked along the output axis (linear.rs:220-265).
+int upload_linear(fmd_handle* h, const std::vector<std::pair<const fmd_tensor*, int>>& parts, int K, LinW& W,
+                  const char* what) {
+  int N = 0;
+  for (auto& p : parts) N += p.second;
+  if (N % 64 || K % 64) return fail(h, FMD_ENOTSUP, std::string(what) + ": dims must be multiples of 64");
+  W.N = N;
+  W.K = K;
+  W.q8 = h->q8;
+  if (!h->q8) {
+    std::vector<uint16_t> bits((size_t)N * K);
+    size_t off = 0;
+    for (auto& p : parts) {
+      const size_t n = (size_t)p.second * K;
+      const fmd_tensor& t = *p.first;
+      if (t.data == nullptr) return fail(h, FMD_EINVAL, std::string("missing tensor ") + what);
+      const bool bf = h->at == kBF16;
+      if ((bf && t.dtype == FMD_DT_BF16) || (!bf && t.dtype == FMD_DT_F16)) {
+        std::memcpy(bits.data() + off, t.data, n * 2);
+      } else {
+        std::vector<float> f;
+        if (!to_f32(t, n, f)) return fail(h, FMD_EINVAL, std::string("bad dtype for ") + what);
+        for (size_t i = 0; i < n; ++i) bits[off + i] = bf ? f32_to_bf16_bits(f[i]) : f32_to_f16_bits(f[i]);
+      }
+      off += n;
+    }
+    void* d;
+    int rc = dev_alloc(h, bits.size() * 2, &d, &h->weight_bytes);
+    if (rc) return rc;
+    if ((rc = upload(h, d, bits.data(), bits.size() * 2))) return rc;
+    W.w = d;
+  } else {
+    std::vector<int8_t> qs((size_t)N * K);
+    std::vector<uint16_t> sc((size_t)N * (K / 32));
+    size_t row = 0;
+    for (auto& p : parts) {
+      const fmd_tensor& t = *p.first;
+      const size_t rows = p.second;
+      if (t.data == nullptr) return fail(h, FMD_EINVAL, std::string("missing tensor ") + what);
+      if (t.dtype == FMD_DT_Q8_0) {
+        const uint8_t* b = (const uint8_t*)t.data;
+        for (size_t r = 0; r < rows; ++r)
+          for (int kb = 0; kb < K / 32; ++kb) {
+            const uint8_t* blk = b + (r * (K / 32) + kb) * 34;
+            std::memcpy(&sc[(row + r) * (K / 32) + kb], blk, 2);
+            std::memcpy(&qs[(row + r) * K + kb * 32], blk + 2, 32);
+          }
+      } else {
+        std::vector<float> f;
+        if (!to_f32(t, rows * K, f)) return fail(h, FMD_EINVAL, std::string("bad dtype for ") + what);
+        quantize_rows(f.data(), rows, K, qs.data() + row * K, sc.data() + row * (K / 32));
+      }
+      row += rows;
+    }
+    void *dq, *dd;
+    int rc = dev_alloc(h, qs.size(), &dq, &h->weight_bytes);
+    if (rc) return rc;
+    if ((rc = dev_alloc(h, sc.size() * 2, &dd, &h->weight_bytes))) return rc;
+    if ((rc = upload(h, dq, qs.data(), qs.size()))) return rc;
+    if ((rc = upload(h, dd, sc.data(), sc.size() * 2))) return rc;
+    W.qs = (const int8_t*)dq;
+    W.d = (const uint16_t*)dd;
+  }
+  // K split for passes with <= 64 rows: aim for >= ~2 CTAs per SM.
+  int split = 1;
+  const int ctas = N / 64;
+  while (split < 16 && ctas * split < 296 && K % (64 * split * 2) == 0 && K / (split * 2) >= 128) split *= 2;
+  W.split = split;
+  return FMD_OK;
+}
+
+void release_graph(fmd_handle* h) {
+  if (h->graph_exec) {
+    cudaGraphExecDestroy(h->graph_exec);
+    h->graph_exec = nullptr;
+  }
+  h->graph_batch = h->graph_chunk = -1;
+}
+
+// Opt-in launch tracing (FMD_TRACE=1): synchronise after every launch and log
+// it, so a kernel that stalls or faults is identified by name.
+bool trace_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("FMD_TRACE");
+    return v != nullptr && v[0] == '1';
+  }();
+  return on;
+}
+void trace(fmd_handle* h, const char* what, int layer) {
+  if (!trace_enabled()) return;
+  const auto t0 = std::chrono::steady_clock::now();
+  cudaError_t e = cudaStreamSynchronize(h->stream);
+  const double ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+  std::fprintf(stderr, "[fmd] %-16s layer %3d  %8.3f ms  %s\n", what, layer, ms, cudaGetErrorString(e));
+}
+
+// ---- forward pass ------------------------------------------------------------------
+void run_forward(fmd_handle* h, float* logits_dev, const void* arena) {
+  cudaStream_t s = h->stream;
+  const fmd_config& c = h->cfg;
+  const int R = h->max_rows, H = c.hidden_size, I = c.intermediate_size;
+  const int row_grid = std::min(R, 296);
+  const int* nrows = &h->plan.counts->n_rows;
+  const int* nsamp = &h->plan.counts->n_sample;
+  const float eps = c.rms_norm_eps;
+  const size_t ss = h->split_stride;
+  launch_embed_norm(h->at, h->plan, row_grid, h->embed, arena, h->x, h->layers[0].in_norm, h->xn, H, eps, s);
+  trace(h, "embed_norm", -1);
+  for (int l = 0; l < c.num_hidden_layers; ++l) {
+    const LayerDev& L = h->layers[l];
+    launch_linear(h->at, L.qkv, h->xn, H, nullptr, nrows, R, h->part, ss, s);
+    trace(h, "qkv", l);
+    launch_qkv_epilogue(h->at, h->plan, row_grid, h->part, L.qkv.split, ss, h->Hq(), h->Hkv(), L.q_norm, L.k_norm,
+                        h->rope_cos, h->rope_sin, h->qbuf, h->kv, l, eps, s);
+    trace(h, "qkv_epi", l);
+    launch_attn_decode(h->at, h->plan, h->di_grid, h->Hq(), h->Hkv(), h->qbuf, h->kv, l, h->attn_scale, h->pacc,
+                       h->pml, s);
+    trace(h, "attn_decode", l);
+    launch_attn_combine(h->at, h->plan, std::min(h->max_slots, 296), h->Hq(), h->pacc, h->pml, h->ctx, s);
+    trace(h, "attn_combine", l);
+    launch_attn_prefill(h->at, h->plan, h->pb_grid, h->Hq(), h->Hkv(), h->qbuf, h->kv, l, h->attn_scale, h->ctx, s);
+    trace(h, "attn_prefill", l);
+    launch_linear(h->at, L.o, h->ctx, h->Hq() * kHeadDim, nullptr, nrows, R, h->part, ss, s);
+    trace(h, "o_proj", l);
+    launch_residual_norm(h->at, nrows, row_grid, h->x, h->part, L.o.split, ss, L.post_norm, h->xn, H, eps, s);
+    trace(h, "res_norm1", l);
+    launch_linear(h->at, L.gate_up, h->xn, H, nullptr, nrows, R, h->part, ss, s);
+    trace(h, "gate_up", l);
+    launch_silu_mul(h->at, nrows, row_grid, h->part, L.gate_up.split, ss, I, h->hbuf, s);
+    trace(h, "silu", l);
+    launch_linear(h->at, L.down, h->hbuf, I, nullptr, nrows, R, h->part, ss, s);
+    trace(h, "down", l);
+    const void* next_norm = l + 1 < c.num_hidden_layers ? h->layers[l + 1].in_norm : h->final_norm;
+    launch_residual_norm(h->at, nrows, row_grid, h->x, h->part, L.down.split, ss, next_norm, h->xn, H, eps, s);
+    trace(h, "res_norm2", l);
+  }
+  launch_linear(h->at, h->lm_head, h->xn, H, h->plan.sample_row, nsamp, h->max_slots, h->part, ss, s);
+  trace(h, "lm_head", -1);
+  launch_logits_argmax(h->at, nsamp, h->max_slots, h->part, c.vocab_size, logits_dev, h->next_ids, s);
+  trace(h, "argmax", -1);
+}
+
+// ---- host plan helpers -------------------------------------------------------------
+struct HostPlan {
+  fmd_handle* h;
+  Plan p;  // bound to the pinned mirror
+  int rows = 0, n_decode = 0, samples = 0, pblocks = 0, items = 0;
+  explicit HostPlan(fmd_handle* hh) : h(hh) { p = hh->layout.bind(hh->h_plan); }
+  void add_decode(int slot, int pos, int tok) {
+    const int r = rows++;
+    p.row_slot[r] = slot;
+    p.row_pos[r] = pos;
+    p.row_tok[r] = tok;
+    p.row_emb[r] = 0;
+    const int kv_len = pos + 1;
+    const int nit = (kv_len + kDecodeItemTokens - 1) / kDecodeItemTokens;
+    p.drow_item0[r] = items;
+    p.drow_nitems[r] = nit;
+    for (int j = 0; j < nit; ++j) {
+      p.di_row[items + j] = r;
+      p.di_start[items + j] = j * kDecodeItemTokens;
+      p.di_end[items + j] = std::min(kv_len, (j + 1) * kDecodeItemTokens);
+    }
+    items += nit;
+    p.sample_row[samples] = r;
+    p.sample_slot[samples] = slot;
+    ++samples;
+    n_decode = rows;
+  }
+  // `n` prompt rows of `slot` at positions pos0.., arena rows emb0..; sample the last one if `sample`.
+  void add_prefill(int slot, int pos0, int n, int emb0, bool sample) {
+    const int r0 = rows;
+    for (int i = 0; i < n; ++i) {
+      p.row_slot[r0 + i] = slot;
+      p.row_pos[r0 + i] = pos0 + i;
+      p.row_tok[r0 + i] = -1;
+      p.row_emb[r0 + i] = emb0 + i;
+    }
+    for (int j = 0; j < n; j += kRowsPerPBlock) {
+      p.pb_row0[pblocks] = r0 + j;
+      p.pb_n[pblocks] = std::min(kRowsPerPBlock, n - j);
+      ++pblocks;
+    }
+    rows += n;
+    if (sample) {
+      p.sample_row[samples] = r0 + n - 1;
+      p.sample_slot[samples] = slot;
+      ++samples;
+    }
+  }
+  int commit() {
+    PlanCounts* c = p.counts;
+    c->n_rows = rows;
+    c->n_decode = n_decode;
+    c->n_sample = samples;
+    c->n_pblocks = pblocks;
+    c->n_ditems = items;
+    c->finished = 0;
+    fmd_handle* hh = h;
+    cudaError_t e = cudaMemcpyAsync(hh->d_plan, hh->h_plan, hh->layout.total * sizeof(int), cudaMemcpyHostToDevice,
+                                    hh->stream);
+    if (e != cudaSuccess) return fail(hh, FMD_EIO, std::string("plan upload: ") + cudaGetErrorString(e));
+    return FMD_OK;
+  }
+};
+
+int check_ready(fmd_handle* h) {
+  if (!h) return FMD_EINVAL;
+  if (!h->loaded) return fail(h, FMD_EBUSY, "no weights loaded (fmd_load_weights)");
+  if (!h->reserved) return fail(h, FMD_EBUSY, "no KV pool reserved (fmd_kv_reserve)");
+  return FMD_OK;
+}
+
+int sync_check(fmd_handle* h) {
+  cudaError_t e = cudaStreamSynchronize(h->stream);
+  if (e != cudaSuccess) return fail(h, FMD_EIO, std::string("device error: ") + cudaGetErrorString(e));
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(h, FMD_EIO, std::string("launch error: ") + cudaGetErrorString(e));
+  return FMD_OK;
+}
+
+int convert_rows_to_act(fmd_handle* h, const void* src, int32_t dtype, size_t rows, std::vector<uint16_t>& out) {
+  const size_t n = rows * h->H();
+  out.resize(n);
+  const bool bf = h->at == kBF16;
+  if ((bf && dtype == FMD_DT_BF16) || (!bf && dtype == FMD_DT_F16)) {
+    std::memcpy(out.data(), src, n * 2);
+  } else if (dtype == FMD_DT_F32) {
+    const float* f = (const float*)src;
+    for (size_t i = 0; i < n; ++i) out[i] = bf ? f32_to_bf16_bits(f[i]) : f32_to_f16_bits(f[i]);
+  } else {
+    return fail(h, FMD_EINVAL, "embeds dtype must be f32 or the activation dtype");
+  }
+  return FMD_OK;
+}
+
+int copy_outputs(fmd_handle* h, int n_sample, const std::vector<int>& order, float* logits, int32_t* ids) {
+  // order[i] = caller index of sample row i
+  const int V = h->cfg.vocab_size;
+  std::vector<int> tmp(n_sample);
+  if (ids) {
+    CK(cudaMemcpyAsync(tmp.data(), h->next_ids, n_sample * sizeof(int), cudaMemcpyDeviceToHost, h->stream));
+  }
+  if (logits) {
+    for (int i = 0; i < n_sample; ++i)
+      CK(cudaMemcpyAsync(logits + (size_t)order[i] * V, h->logits + (size_t)i * V, (size_t)V * 4,
+                         cudaMemcpyDeviceToHost, h->stream));
+  }
+  int rc = sync_check(h);
+  if (rc) return rc;
+  if (ids)
+    for (int i = 0; i < n_sample; ++i) ids[order[i]] = tmp[i];
+  return FMD_OK;
+}
+
+int ensure_pages(fmd_handle* h, int slot, int upto_len) {
+  const int need = (upto_len + kPageTokens - 1) / kPageTokens;
+  if (need > h->max_pages_per_slot) return fail(h, FMD_EOVERFLOW, "sequence longer than the RoPE table / slot limit");
+  bool changed = false;
+  while (h->slot_npages[slot] < need) {
+    if (h->free_pages.empty()) return fail(h, FMD_ENOMEM, "KV pool exhausted");
+    h->h_page_table[(size_t)slot * h->max_pages_per_slot + h->slot_npages[slot]] = h->free_pages.back();
+    h->free_pages.pop_back();
+    h->slot_npages[slot] += 1;
+    changed = true;
+  }
+  if (changed) {
+    const size_t off = (size_t)slot * h->max_pages_per_slot;
+    CK(cudaMemcpyAsync(h->d_page_table + off, h->h_page_table.data() + off, need * sizeof(int),
+                       cudaMemcpyHostToDevice, h->stream));
+  }
+  return FMD_OK;
+}
+
+}  // namespace
+
+// =====================================================================================
+extern "C" {
+
+int fmd_version(void) { return kVersion; }
+
+const char* fmd_status_string(int32_t status) {
+  switch (status) {
+    case FMD_OK: return "ok";
+    case FMD_EINVAL: return "invalid argument";
+    case FMD_ENOMEM: return "out of device memory / KV pool exhausted";
+    case FMD_EIO: return "CUDA error";
+    case FMD_EBUSY: return "handle not ready";
+    case FMD_EOVERFLOW: return "KV cache capacity exceeded";
+    case FMD_ENOTSUP: return "not supported";
+    case FMD_ETIMEDOUT: return "device-side wait timed out";
+    default: return "unknown status";
+  }
+}
+
+const char* fmd_last_error(const fmd_handle* h) { return h ? h->err.c_str() : "null handle"; }
+
+int fmd_create(const fmd_config* cfg, int32_t precision, int32_t device, fmd_handle** out) {
+  if (!cfg || !out) return FMD_EINVAL;
+  *out = nullptr;
+  if (precision == FMD_PREC_F32) return FMD_ENOTSUP;
+  if (precision < FMD_PREC_F16 || precision > FMD_PREC_INT8_BF16) return FMD_EINVAL;
+  if (cfg->head_dim != kHeadDim) return FMD_ENOTSUP;
+  if (cfg->num_attention_heads != 2 * cfg->num_key_value_heads) return FMD_ENOTSUP;
+  if (cfg->hidden_size % 64 || cfg->intermediate_size % 64 || cfg->vocab_size % 64) return FMD_ENOTSUP;
+  if (cfg->num_hidden_layers < 1 || cfg->hidden_size <= 0) return FMD_EINVAL;
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev) {
+    cudaGetLastError();
+    return FMD_EIO;
+  }
+  fmd_handle* h = new fmd_handle();
+  h->cfg = *cfg;
+  h->precision = precision;
+  h->q8 = precision == FMD_PREC_INT8 || precision == FMD_PREC_INT8_BF16;
+  h->at = (precision == FMD_PREC_BF16 || precision == FMD_PREC_INT8_BF16) ? kBF16 : kF16;
+  h->device = device;
+  h->attn_scale = (float)(1.0 / std::sqrt((double)cfg->head_dim));
+  if (cudaSetDevice(device) != cudaSuccess || cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking) != cudaSuccess ||
+      init_kernels() != cudaSuccess) {
+    cudaGetLastError();
+    delete h;
+    return FMD_EIO;
+  }
+  *out = h;
+  return FMD_OK;
+}
+
+int fmd_destroy(fmd_handle* h) {
+  if (!h) return FMD_OK;
+  cudaSetDevice(h->device);
+  cudaStreamSynchronize(h->stream);
+  release_graph(h);
+  for (auto& a : h->allocs) cudaFree(a.p);
+  for (DevBuf* b : {&h->eng_reqs, &h->eng_arena, &h->eng_tokens, &h->eng_results})
+    if (b->p) cudaFree(b->p);
+  if (h->h_plan) cudaFreeHost(h->h_plan);
+  if (h->h_ctr) cudaFreeHost(h->h_ctr);
+  if (h->stream) cudaStreamDestroy(h->stream);
+  delete h;
+  return FMD_OK;
+}
+
+int fmd_load_weights(fmd_handle* h, const fmd_weights* w) {
+  if (!h || !w || !w->layers) return fail(h, FMD_EINVAL, "null weights");
+  if (h->loaded) return fail(h, FMD_EBUSY, "weights already loaded");
+  CK(cudaSetDevice(h->device));
+  const fmd_config& c = h->cfg;
+  const int H = c.hidden_size, I = c.intermediate_size, qd = c.num_attention_heads * kHeadDim,
+            kvd = c.num_key_value_heads * kHeadDim;
+  int rc;
+  if ((rc = upload_dense(h, w->embed_tokens, (size_t)c.vocab_size * H, &h->embed, "embed_tokens"))) return rc;
+  if ((rc = upload_dense(h, w->norm, H, &h->final_norm, "norm"))) return rc;
+  h->layers.resize(c.num_hidden_layers);
+  for (int l = 0; l < c.num_hidden_layers; ++l) {
+    const fmd_layer_weights& s = w->layers[l];
+    LayerDev& L = h->layers[l];
+    if ((rc = upload_dense(h, s.input_layernorm, H, &L.in_norm, "input_layernorm"))) return rc;
+    if ((rc = upload_dense(h, s.post_attention_layernorm, H, &L.post_norm, "post_attention_layernorm"))) return rc;
+    if ((rc = upload_dense(h, s.q_norm, kHeadDim, &L.q_norm, "q_norm"))) return rc;
+    if ((rc = upload_dense(h, s.k_norm, kHeadDim, &L.k_norm, "k_norm"))) return rc;
+    if ((rc = upload_linear(h, {{&s.q_proj, qd}, {&s.k_proj, kvd}, {&s.v_proj, kvd}}, H, L.qkv, "qkv"))) return rc;
+    if ((rc = upload_linear(h, {{&s.o_proj, H}}, qd, L.o, "o_proj"))) return rc;
+    if ((rc = upload_linear(h, {{&s.gate_proj, I}, {&s.up_proj, I}}, H, L.gate_up, "gate_up"))) return rc;
+    if ((rc = upload_linear(h, {{&s.down_proj, H}}, I, L.down, "down_proj"))) return rc;
+  }
+  // lm_head: tied to the embedding unless given (qwen3.rs:366-372); in int8 it
+  // is quantised from the source values (qwen3.rs:566-578).
+  const fmd_tensor& head = w->lm_head.data ? w->lm_head : w->embed_tokens;
+  if (!h->q8 && !w->lm_head.data) {
+    h->lm_head.N = c.vocab_size;
+    h->lm_head.K = H;
+    h->lm_head.q8 = false;
+    h->lm_head.w = h->embed;
+    h->lm_head.split = 1;
+  } else {
+    if ((rc = upload_linear(h, {{&head, c.vocab_size}}, H, h->lm_head, "lm_head"))) return rc;
+  }
+  h->lm_head.split = 1;
+  // RoPE tables (qwen3.rs:116-136): inv_freq in f64 -> f32, pos*inv_freq in
+  // f32, cos/sin in f32, stored in the activation dtype.
+  h->rope_len = std::min(c.max_position_embeddings, 65536);
+  const int half = kHeadDim / 2;
+  std::vector<float> inv(half);
+  for (int i = 0; i < half; ++i) inv[i] = (float)(1.0 / std::pow(c.rope_theta, 2.0 * i / kHeadDim));
+  std::vector<uint16_t> cs((size_t)h->rope_len * half), sn((size_t)h->rope_len * half);
+  const bool bf = h->at == kBF16;
+  for (int p = 0; p < h->rope_len; ++p)
+    for (int i = 0; i < half; ++i) {
+      const float f = (float)p * inv[i];
+      const float cv = std::cos(f), sv = std::sin(f);
+      cs[(size_t)p * half + i] = bf ? f32_to_bf16_bits(cv) : f32_to_f16_bits(cv);
+      sn[(size_t)p * half + i] = bf ? f32_to_bf16_bits(sv) : f32_to_f16_bits(sv);
+    }
+  if ((rc = dev_alloc(h, cs.size() * 2, &h->rope_cos, &h->weight_bytes))) return rc;
+  if ((rc = dev_alloc(h, sn.size() * 2, &h->rope_sin, &h->weight_bytes))) return rc;
+  if ((rc = upload(h, h->rope_cos, cs.data(), cs.size() * 2))) return rc;
+  if ((rc = upload(h, h->rope_sin, sn.data(), sn.size() * 2))) return rc;
+  h->loaded = true;
+  return FMD_OK;
+}
+
+int64_t fmd_cache_bytes(const fmd_config* cfg, int32_t precision, int64_t batch, int64_t capacity) {
+  if (!cfg) return FMD_EINVAL;
+  const int64_t elem = precision == FMD_PREC_F32 ? 4 : 2;
+  return (int64_t)cfg->num_hidden_layers * 2 * batch * cfg->num_key_value_heads * capacity * cfg->head_dim * elem;
+}
+
+int fmd_memory_bytes(const fmd_handle* h, int64_t* weights, int64_t* kv_pool, int64_t* workspace) {
+  if (!h) return FMD_EINVAL;
+  if (weights) *weights = h->weight_bytes;
+  if (kv_pool) *kv_pool = h->kv_bytes;
+  if (workspace) *workspace = h->work_bytes;
+  return FMD_OK;
+}
+
+int fmd_kv_reserve(fmd_handle* h, int32_t max_slots, int64_t max_tokens_total, int32_t max_rows_per_step) {
+  if (!h) return FMD_EINVAL;
+  if (!h->loaded) return fail(h, FMD_EBUSY, "load weights before reserving the KV pool");
+  if (h->reserved) return fail(h, FMD_EBUSY, "KV pool already reserved");
+  if (max_slots < 1 || max_slots > kMaxSlotsLimit || max_tokens_total < 1 || max_rows_per_step < max_slots)
+    return fail(h, FMD_EINVAL, "bad KV reservation sizes (need 1 <= max_slots <= 256, rows >= slots)");
+  CK(cudaSetDevice(h->device));
+  const fmd_config& c = h->cfg;
+  const int H = c.hidden_size, I = c.intermediate_size, V = c.vocab_size;
+  h->max_slots = max_slots;
+  h->max_rows = max_rows_per_step;
+  h->max_pages_per_slot = h->rope_len / kPageTokens;  // every position stays inside the RoPE table
+  if (h->max_pages_per_slot < 1) return fail(h, FMD_ENOTSUP, "max_position_embeddings must be >= 64");
+  const int64_t pages = (max_tokens_total + kPageTokens - 1) / kPageTokens + max_slots;
+  if (pages > (1LL << 30)) return fail(h, FMD_ENOMEM, "KV pool too large");
+  h->n_pages = (int)pages;
+  int rc;
+  // KV pool
+  const size_t kv_elems = (size_t)c.num_hidden_layers * h->n_pages * 2 * c.num_key_value_heads * kPageTokens * kHeadDim;
+  void* kvp;
+  if ((rc = dev_alloc(h, kv_elems * 2, &kvp, &h->kv_bytes))) return rc;
+  CK(cudaMemset(kvp, 0, kv_elems * 2));
+  h->kv.base = kvp;
+  h->kv.n_pages = h->n_pages;
+  h->kv.max_pages_per_slot = h->max_pages_per_slot;
+  h->kv.kv_heads = c.num_key_value_heads;
+  void* pt;
+  if ((rc = dev_alloc(h, (size_t)max_slots * h->max_pages_per_slot * 4, &pt, &h->work_bytes))) return rc;
+  CK(cudaMemset(pt, 0, (size_t)max_slots * h->max_pages_per_slot * 4));
+  h->d_page_table = (int*)pt;
+  h->kv.page_table = h->d_page_table;
+  h->h_page_table.assign((size_t)max_slots * h->max_pages_per_slot, 0);
+  h->free_pages.clear();
+  for (int i = h->n_pages - 1; i >= 0; --i) h->free_pages.push_back(i);
+  h->slot_cap.assign(max_slots, -1);
+  h->slot_len.assign(max_slots, 0);
+  h->slot_npages.assign(max_slots, 0);
+  // work buffers
+  const int R = h->max_rows;
+  int max_split = 1;
+  for (auto& L : h->layers)
+    for (const LinW* W : {&L.qkv, &L.o, &L.gate_up, &L.down}) max_split = std::max(max_split, W->split);
+  const int Nmax = std::max({h->qkvN(), 2 * I, H});
+  h->split_stride = (size_t)std::max(R, 64) * Nmax;
+  const size_t part_elems = std::max({h->split_stride * max_split, (size_t)max_slots * V});
+  h->pb_max = R / kRowsPerPBlock + max_slots;
+  h->di_max = (int)std::min<int64_t>((int64_t)max_slots * h->max_pages_per_slot,
+                                     (int64_t)h->n_pages * kPageTokens / kDecodeItemTokens + 2 * max_slots + 1);
+  h->di_grid = 296;
+  h->pb_grid = std::min(h->pb_max, 148);
+  const int HqD = h->Hq() * kHeadDim;
+  void* p;
+  auto A = [&](size_t bytes, void** dst) { return dev_alloc(h, bytes, dst, &h->work_bytes); };
+  if ((rc = A((size_t)R * H * 2, &h->x))) return rc;
+  if ((rc = A((size_t)R * H * 2, &h->xn))) return rc;
+  if ((rc = A((size_t)R * HqD * 2, &h->qbuf))) return rc;
+  if ((rc = A((size_t)R * HqD * 2, &h->ctx))) return rc;
+  if ((rc = A((size_t)R * I * 2, &h->hbuf))) return rc;
+  if ((rc = A((size_t)R * H * 2, &h->arena))) return rc;
+  h->arena_rows = R;
+  if ((rc = A(part_elems * 4, &p))) return rc;
+  h->part = (float*)p;
+  if ((rc = A((size_t)h->di_max * HqD * 4, &p))) return rc;
+  h->pacc = (float*)p;
+  if ((rc = A((size_t)h->di_max * h->Hq() * 2 * 4, &p))) return rc;
+  h->pml = (float*)p;
+  if ((rc = A((size_t)max_slots * V * 4, &p))) return rc;
+  h->logits = (float*)p;
+  if ((rc = A((size_t)max_slots * 4, &p))) return rc;
+  h->next_ids = (int*)p;
+  h->layout.init(R, max_slots, h->pb_max, h->di_max);
+  if ((rc = A(h->layout.total * 4, &p))) return rc;
+  CK(cudaMemset(p, 0, h->layout.total * 4));
+  h->d_plan = (int*)p;
+  h->plan = h->layout.bind(h->d_plan);
+  CK(cudaMallocHost((void**)&h->h_plan, h->layout.total * 4));
+  std::memset(h->h_plan, 0, h->layout.total * 4);
+  // engine slot arrays
+  if ((rc = A((size_t)max_slots * 7 * 4, &p))) return rc;
+  CK(cudaMemset(p, 0, (size_t)max_slots * 7 * 4));
+  h->eng_slot = (int*)p;
+  if ((rc = A((size_t)h->n_pages * 4, &p))) return rc;
+  h->eng_free = (int*)p;
+  if ((rc = A(sizeof(EngineCounters), &p))) return rc;
+  h->eng_ctr = (EngineCounters*)p;
+  CK(cudaMallocHost((void**)&h->h_ctr, sizeof(EngineCounters)));
+  h->reserved = true;
+  return FMD_OK;
+}
+
+int fmd_embed(fmd_handle* h, const int32_t* ids, int64_t n, void* out) {
+  int rc = check_ready(h);
+  if (rc) return rc;
+  if (!ids || !out || n < 0) return fail(h, FMD_EINVAL, "bad embed arguments");
+  CK(cudaSetDevice(h->device));
+  const int H = h->H();
+  for (int64_t i = 0; i < n; ++i) {
+    if (ids[i] < 0 || ids[i] >= h->cfg.vocab_size) return fail(h, FMD_EINVAL, "token id out of range");
+    CK(cudaMemcpyAsync((char*)out + i * H * 2, (const char*)h->embed + (size_t)ids[i] * H * 2, H * 2,
+                       cudaMemcpyDeviceToHost, h->stream));
+  }
+  return sync_check(h);
+}
+
+int fmd_slot_open(fmd_handle* h, int32_t slot, int32_t capacity) {
+  int rc = check_ready(h);
+  if (rc) return rc;
+  if (slot < 0 || slot >= h->max_slots || capacity < 1) return fail(h, FMD_EINVAL, "bad slot or capacity");
+  if (h->slot_cap[slot] >= 0) return fail(h, FMD_EBUSY, "slot already open");
+  if (capacity > h->max_pages_per_slot * kPageTokens)
+    return fail(h, FMD_EOVERFLOW, "capacity exceeds the RoPE table length");
+  const int need = (capacity + kPageTokens - 1) / kPageTokens;
+  if ((int)h->free_pages.size() < need) return fail(h, FMD_ENOMEM, "KV pool has too few free pages");
+  h->slot_cap[slot] = capacity;
+  h->slot_len[slot] = 0;
+  CK(cudaSetDevice(h->device));
+  if ((rc = ensure_pages(h, slot, capacity))) return rc;
+  return sync_check(h);
+}
+
+int fmd_slot_release(fmd_handle* h, int32_t slot) {
+  if (!h) return FMD_EINVAL;
+  if (!h->reserved || slot < 0 || slot >= h->max_slots) return fail(h, FMD_EINVAL, "bad slot");
+  for (int k = 0; k < h->slot_npages[slot]; ++k)
+    h->free_pages.push_back(h->h_page_table[(size_t)slot * h->max_pages_per_slot + k]);
+  h->slot_npages[slot] = 0;
+  h->slot_cap[slot] = -1;
+  h->slot_len[slot] = 0;
+  return FMD_OK;
+}
+
+int fmd_slot_len(fmd_handle* h, int32_t slot, int32_t* len) {
+  if (!h || !len) return FMD_EINVAL;
+  if (!h->reserved || slot < 0 || slot >= h->max_slots || h->slot_cap[slot] < 0)
+    return fail(h, FMD_EINVAL, "slot not open");
+  *len = h->slot_len[slot];
+  return FMD_OK;
+}
+
+int fmd_prefill(fmd_handle* h, int32_t n, const int32_t* slots, const int32_t* lens, const void* embeds,
+                int32_t embeds_dtype, float* logits, int32_t* next_ids) {
+  int rc = check_ready(h);
+  if (rc) return rc;
+  if (n < 1 || n > h->max_slots || !slots || !lens || !embeds) return fail(h, FMD_EINVAL, "bad prefill arguments");
+  CK(cudaSetDevice(h->device));
+  int64_t total = 0;
+  std::vector<char> seen(h->max_slots, 0);
+  for (int i = 0; i < n; ++i) {
+    const int s = slots[i];
+    if (s < 0 || s >= h->max_slots || h->slot_cap[s] < 0) return fail(h, FMD_EINVAL, "prefill on a closed slot");
+    if (seen[s]) return fail(h, FMD_EINVAL, "slot listed twice");
+    seen[s] = 1;
+    if (lens[i] < 1) return fail(h, FMD_EINVAL, "empty prompt");
+    if (h->slot_len[s] + lens[i] > h->slot_cap[s])
+      return fail(h, FMD_EOVERFLOW, "kv cache overflow: " + std::to_string(h->slot_len[s]) + " + " +
+                                        std::to_string(lens[i]) + " exceeds capacity " +
+                                        std::to_string(h->slot_cap[s]));
+    total += lens[i];
+  }
+  const size_t rowb = (size_t)h->H() * (embeds_dtype == FMD_DT_F32 ? 4 : 2);
+  // Passes of up to max_rows rows; a sequence may span passes (chunked prefill).
+  std::vector<int> done(n, 0);
+  std::vector<int64_t> src_off(n, 0);
+  for (int i = 1; i < n; ++i) src_off[i] = src_off[i - 1] + lens[i - 1];
+  int remaining = n;
+  std::vector<int> order;
+  std::vector<uint16_t> act;
+  release_graph(h);
+  while (remaining > 0) {
+    HostPlan hp(h);
+    order.clear();
+    std::vector<std::pair<int, int>> segs;  // (seq, rows)
+    int rows = 0;
+    for (int i = 0; i < n && rows < h->max_rows; ++i) {
+      const int left = lens[i] - done[i];
+      if (left == 0) continue;
+      const int take = std::min(left, h->max_rows - rows);
+      segs.push_back({i, take});
+      rows += take;
+    }
+    // stage the embeddings of this pass into the arena, back to back
+    int arow = 0;
+    for (auto& sg : segs) {
+      const int i = sg.first, take = sg.second;
+      const char* src = (const char*)embeds + (size_t)(src_off[i] + done[i]) * rowb;
+      if ((rc = convert_rows_to_act(h, src, embeds_dtype, take, act))) return rc;
+      CK(cudaMemcpyAsync((char*)h->arena + (size_t)arow * h->H() * 2, act.data(), act.size() * 2,
+                         cudaMemcpyHostToDevice, h->stream));
+      const int s = slots[i];
+      const bool last = done[i] + take == lens[i];
+      hp.add_prefill(s, h->slot_len[s], take, arow, last);
+      if (last) order.push_back(i);
+      arow += take;
+      CK(cudaStreamSynchronize(h->stream));  // `act` is reused
+    }
+    if ((rc = hp.commit())) return rc;
+    run_forward(h, logits ? h->logits : nullptr, h->arena);
+    for (auto& sg : segs) {
+      const int i = sg.first;
+      h->slot_len[slots[i]] += sg.second;
+      done[i] += sg.second;
+      if (done[i] == lens[i]) --remaining;
+    }
+    if ((rc = copy_outputs(h, (int)order.size(), order, logits, next_ids))) return rc;
+  }
+  return FMD_OK;
+}
+
+int fmd_decode_step(fmd_handle* h, int32_t n, const int32_t* slots, const int32_t* ids, float* logits,
+                    int32_t* next_ids) {
+  int rc = check_ready(h);
+  if (rc) return rc;
+  if (n < 1 || n > h->max_slots || !slots || !ids) return fail(h, FMD_EINVAL, "bad decode arguments");
+  CK(cudaSetDevice(h->device));
+  std::vector<char> seen(h->max_slots, 0);
+  for (int i = 0; i < n; ++i) {
+    const int s = slots[i];
+    if (s < 0 || s >= h->max_slots || h->slot_cap[s] < 0) return fail(h, FMD_EINVAL, "decode on a closed slot");
+    if (seen[s]) return fail(h, FMD_EINVAL, "slot listed twice");
+    seen[s] = 1;
+    if (ids[i] < 0 || ids[i] >= h->cfg.vocab_size) return fail(h, FMD_EINVAL, "token id out of range");
+    if (h->slot_len[s] + 1 > h->slot_cap[s])
+      return fail(h, FMD_EOVERFLOW, "kv cache overflow: " + std::to_string(h->slot_len[s]) +
+                                        " + 1 exceeds capacity " + std::to_string(h->slot_cap[s]));
+  }
+  release_graph(h);
+  HostPlan hp(h);
+  std::vector<int> order(n);
+  for (int i = 0; i < n; ++i) {
+    hp.add_decode(slots[i], h->slot_len[slots[i]], ids[i]);
+    order[i] = i;
+  }
+  if ((rc = hp.commit())) return rc;
+  run_forward(h, logits ? h->logits : nullptr, h->arena);
+  for (int i = 0; i < n; ++i) h->slot_len[slots[i]] += 1;
+  return copy_outputs(h, n, order, logits, next_ids);
+}
+
+// ---- continuous-batching engine ------------------------------------------------------
+int fmd_engine_load(fmd_handle* h, const fmd_request* reqs, int32_t n_reqs, const void* embeds, int64_t embed_rows,
+                    int32_t embeds_dtype) {
+  int rc = check_ready(h);
+  if (rc) return rc;
+  if (n_reqs < 1 || !reqs || !embeds || embed_rows < 1 || embed_rows >= (1LL << 31))
+    return fail(h, FMD_EINVAL, "bad engine queue");
+  CK(cudaSetDevice(h->device));
+  int max_new = 1;
+  for (int i = 0; i < n_reqs; ++i) {
+    if (reqs[i].prompt_len < 1 || reqs[i].embed_row < 0 || reqs[i].embed_row + reqs[i].prompt_len > embed_rows)
+      return fail(h, FMD_EINVAL, "request " + std::to_string(i) + " reads outside the embedding arena");
+    max_new = std::max(max_new, reqs[i].max_new_tokens);
+  }
+  for (int s = 0; s < h->max_slots; ++s)
+    if (h->slot_cap[s] >= 0) return fail(h, FMD_EBUSY, "close operator-mode slots before running the engine");
+  release_graph(h);
+  for (DevBuf* b : {&h->eng_reqs, &h->eng_arena, &h->eng_tokens, &h->eng_results}) {
+    if (b->p) cudaFree(b->p);
+    b->p = nullptr;
+    b->bytes = 0;
+  }
+  auto alloc = [&](DevBuf& b, size_t bytes) -> int {
+    cudaError_t e = cudaMalloc(&b.p, bytes);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      b.p = nullptr;
+      return fail(h, FMD_ENOMEM, "engine buffer allocation failed");
+    }
+    b.bytes = bytes;
+    return FMD_OK;
+  };
+  static_assert(sizeof(fmd_request) == sizeof(DevRequest), "request layout");
+  if ((rc = alloc(h->eng_reqs, sizeof(DevRequest) * n_reqs))) return rc;
+  CK(cudaMemcpy(h->eng_reqs.p, reqs, sizeof(DevRequest) * n_reqs, cudaMemcpyHostToDevice));
+  const size_t arena_bytes = (size_t)embed_rows * h->H() * 2;
+  if ((rc = alloc(h->eng_arena, arena_bytes))) return rc;
+  // convert in slices to bound host memory
+  const size_t rowb = (size_t)h->H() * (embeds_dtype == FMD_DT_F32 ? 4 : 2);
+  std::vector<uint16_t> act;
+  for (int64_t r = 0; r < embed_rows; r += 65536) {
+    const int64_t nr = std::min<int64_t>(65536, embed_rows - r);
+    if ((rc = convert_rows_to_act(h, (const char*)embeds + r * rowb, embeds_dtype, nr, act))) return rc;
+    CK(cudaMemcpy((char*)h->eng_arena.p + (size_t)r * h->H() * 2, act.data(), act.size() * 2,
+                  cudaMemcpyHostToDevice));
+  }
+  h->eng_n_reqs = n_reqs;
+  h->eng_tok_stride = max_new;
+  if ((rc = alloc(h->eng_tokens, (size_t)n_reqs * max_new * 4))) return rc;
+  if ((rc = alloc(h->eng_results, sizeof(DevResult) * n_reqs))) return rc;
+  CK(cudaMemset(h->eng_results.p, 0, sizeof(DevResult) * n_reqs));
+  return FMD_OK;
+}
+
+namespace {
+EngineDev make_engine_dev(fmd_handle* h, int max_batch, int chunk) {
+  EngineDev e{};
+  e.n_reqs = h->eng_n_reqs;
+  e.n_pages = h->n_pages;
+  e.consume_only = 0;
+  e.max_batch = max_batch;
+  e.prefill_chunk = chunk;
+  e.max_rows = h->max_rows;
+  e.max_pages_per_slot = h->max_pages_per_slot;
+  e.eos = h->cfg.eos_token_id;
+  e.page_tokens = kPageTokens;
+  e.tok_stride = h->eng_tok_stride;
+  e.reqs = (const DevRequest*)h->eng_reqs.p;
+  const int S = h->max_slots;
+  e.slot_state = h->eng_slot;
+  e.slot_req = h->eng_slot + S;
+  e.slot_len = h->eng_slot + 2 * S;
+  e.slot_pdone = h->eng_slot + 3 * S;
+  e.slot_ngen = h->eng_slot + 4 * S;
+  e.slot_last = h->eng_slot + 5 * S;
+  e.slot_npages = h->eng_slot + 6 * S;
+  e.free_stack = h->eng_free;
+  e.page_table = h->d_page_table;
+  e.out_tokens = (int*)h->eng_tokens.p;
+  e.results = (DevResult*)h->eng_results.p;
+  e.ctr = h->eng_ctr;
+  e.next_ids = h->next_ids;
+  e.plan = h->plan;
+  return e;
+}
+}  // namespace
+
+int fmd_engine_run(fmd_handle* h, int32_t max_batch, int32_t prefill_chunk, int64_t max_steps, fmd_stats* stats) {
+  int rc = check_ready(h);
+  if (rc) return rc;
+  if (!h->eng_reqs.p) return fail(h, FMD_EBUSY, "no queue loaded (fmd_engine_load)");
+  if (max_batch < 1 || max_batch > h->max_slots) return fail(h, FMD_EINVAL, "max_batch exceeds reserved slots");
+  if (prefill_chunk < 1 || max_batch + prefill_chunk > h->max_rows)
+    return fail(h, FMD_EINVAL, "max_batch + prefill_chunk exceeds max_rows_per_step");
+  for (int s = 0; s < h->max_slots; ++s)
+    if (h->slot_cap[s] >= 0) return fail(h, FMD_EBUSY, "close operator-mode slots before running the engine");
+  CK(cudaSetDevice(h->device));
+  const auto t0 = std::chrono::steady_clock::now();
+  // reset engine state: all slots free, all pages on the free stack, empty plan
+  CK(cudaMemsetAsync(h->eng_slot, 0, (size_t)h->max_slots * 7 * 4, h->stream));
+  {
+    std::vector<int> fs(h->n_pages);
+    for (int i = 0; i < h->n_pages; ++i) fs[i] = h->n_pages - 1 - i;
+    CK(cudaMemcpyAsync(h->eng_free, fs.data(), fs.size() * 4, cudaMemcpyHostToDevice, h->stream));
+    EngineCounters c{};
+    c.free_top = h->n_pages;
+    *h->h_ctr = c;
+    CK(cudaMemcpyAsync(h->eng_ctr, h->h_ctr, sizeof(c), cudaMemcpyHostToDevice, h->stream));
+    CK(cudaMemsetAsync(h->d_plan, 0, h->layout.total * 4, h->stream));
+    CK(cudaMemsetAsync(h->eng_results.p, 0, sizeof(DevResult) * h->eng_n_reqs, h->stream));
+    CK(cudaStreamSynchronize(h->stream));
+  }
+  if (!h->graph_exec || h->graph_batch != max_batch || h->graph_chunk != prefill_chunk) {
+    release_graph(h);
+    const EngineDev e = make_engine_dev(h, max_batch, prefill_chunk);
+    cudaGraph_t g;
+    CK(cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal));
+    launch_schedule(e, h->stream);
+    run_forward(h, nullptr, h->eng_arena.p);
+    CK(cudaStreamEndCapture(h->stream, &g));
+    cudaError_t ie = cudaGraphInstantiate(&h->graph_exec, g, 0);
+    cudaGraphDestroy(g);
+    if (ie != cudaSuccess) return fail(h, FMD_EIO, std::string("graph instantiate: ") + cudaGetErrorString(ie));
+    h->graph_batch = max_batch;
+    h->graph_chunk = prefill_chunk;
+  }
+  int64_t launched = 0;
+  bool finished = false;
+  long long last_progress = -1;
+  int idle_checks = 0;
+  while (!finished && launched < max_steps) {
+    const int64_t k = std::min<int64_t>(kEngineCheckEvery, max_steps - launched);
+    for (int64_t i = 0; i < k; ++i) CK(cudaGraphLaunch(h->graph_exec, h->stream));
+    launched += k;
+    CK(cudaMemcpyAsync(h->h_ctr, h->eng_ctr, sizeof(EngineCounters), cudaMemcpyDeviceToHost, h->stream));
+    if ((rc = sync_check(h))) return rc;
+    finished = h->h_ctr->done >= h->eng_n_reqs;
+    // every live step emits a token or consumes prompt rows; a run of checks
+    // without either means the queue cannot make progress
+    const long long progress = h->h_ctr->gen_tokens + h->h_ctr->prefill_tokens + h->h_ctr->done;
+    idle_checks = progress == last_progress ? idle_checks + 1 : 0;
+    last_progress = progress;
+    if (!finished && idle_checks >= 4)
+      return fail(h, FMD_ETIMEDOUT, "engine made no progress for " + std::to_string(4 * kEngineCheckEvery) +
+                                        " steps (requests done " + std::to_string(h->h_ctr->done) + ")");
+  }
+  // a consume-only scheduler pass books the samples of the last step run
+  if (!finished) {
+    EngineDev e = make_engine_dev(h, max_batch, prefill_chunk);
+    e.consume_only = 1;
+    launch_schedule(e, h->stream);
+    CK(cudaMemcpyAsync(h->h_ctr, h->eng_ctr, sizeof(EngineCounters), cudaMemcpyDeviceToHost, h->stream));
+    if ((rc = sync_check(h))) return rc;
+  }
+  const auto t1 = std::chrono::steady_clock::now();
+  if (stats) {
+    std::memset(stats, 0, sizeof(*stats));
+    stats->steps = h->h_ctr->steps;
+    stats->generated_tokens = h->h_ctr->gen_tokens;
+    stats->prefill_tokens = h->h_ctr->prefill_tokens;
+    stats->requests_done = h->h_ctr->done;
+    stats->generate_seconds = std::chrono::duration<double>(t1 - t0).count();
+    stats->device_status = h->h_ctr->status;
+  }
+  return FMD_OK;
+}
+
+int fmd_engine_fetch(fmd_handle* h, int32_t* tokens, int32_t token_stride, fmd_result* results) {
+  if (!h) return FMD_EINVAL;
+  if (!h->eng_reqs.p) return fail(h, FMD_EBUSY, "no queue loaded");
+  CK(cudaSetDevice(h->device));
+  if (tokens) {
+    if (token_stride < h->eng_tok_stride) return fail(h, FMD_EINVAL, "token_stride smaller than the max budget");
+    CK(cudaMemcpy2D(tokens, (size_t)token_stride * 4, h->eng_tokens.p, (size_t)h->eng_tok_stride * 4,
+                    (size_t)h->eng_tok_stride * 4, h->eng_n_reqs, cudaMemcpyDeviceToHost));
+  }
+  if (results) CK(cudaMemcpy(results, h->eng_results.p, sizeof(DevResult) * h->eng_n_reqs, cudaMemcpyDeviceToHost));
+  return FMD_OK;
+}
+
+int fmd_generate(fmd_handle* h, const fmd_request* reqs, int32_t n_reqs, const void* embeds, int64_t embed_rows,
+                 int32_t embeds_dtype, int32_t max_batch, int32_t prefill_chunk, int32_t* tokens, int32_t token_stride,
+                 fmd_result* results, fmd_stats* stats) {
+  int rc = fmd_engine_load(h, reqs, n_reqs, embeds, embed_rows, embeds_dtype);
+  if (rc) return rc;
+  if ((rc = fmd_engine_run(h, max_batch, prefill_chunk, INT64_MAX / 2, stats))) return rc;
+  return fmd_engine_fetch(h, tokens, token_stride, results);
+}
+
+// ---- inspection ------------------------------------------------------------------------
+int fmd_debug_weight(fmd_handle* h, int32_t layer, int32_t which, float* out, int64_t out_elems) {
+  if (!h || !out) return FMD_EINVAL;
+  if (!h->loaded) return fail(h, FMD_EBUSY, "no weights");
+  const LinW* W = nullptr;
+  if (which == 4) {
+    W = &h->lm_head;
+  } else {
+    if (layer < 0 || layer >= (int)h->layers.size()) return fail(h, FMD_EINVAL, "bad layer");
+    const LayerDev& L = h->layers[layer];
+    W = which == 0 ? &L.qkv : which == 1 ? &L.o : which == 2 ? &L.gate_up : which == 3 ? &L.down : nullptr;
+  }
+  if (!W) return fail(h, FMD_EINVAL, "bad weight selector");
+  const size_t n = (size_t)W->N * W->K;
+  if (out_elems < (int64_t)n) return fail(h, FMD_EINVAL, "output too small");
+  CK(cudaSetDevice(h->device));
+  float* d;
+  CK(cudaMalloc(&d, n * 4));
+  launch_dequant(h->at, *W, d, h->stream);
+  cudaError_t e = cudaMemcpyAsync(out, d, n * 4, cudaMemcpyDeviceToHost, h->stream);
+  cudaError_t e2 = cudaStreamSynchronize(h->stream);
+  cudaFree(d);
+  if (e != cudaSuccess || e2 != cudaSuccess) return fail(h, FMD_EIO, "dequant copy failed");
+  return FMD_OK;
+}
+
+int fmd_debug_kv(fmd_handle* h, int32_t slot, int32_t layer, int32_t pos, int32_t n, void* k_out, void* v_out) {
+  if (!h || !k_out || !v_out) return FMD_EINVAL;
+  if (!h->reserved || slot < 0 || slot >= h->max_slots || layer < 0 || layer >= h->cfg.num_hidden_layers || pos < 0 ||
+      n < 0 || (int64_t)(pos + n) > (int64_t)h->slot_npages[slot] * kPageTokens)
+    return fail(h, FMD_EINVAL, "bad kv range");
+  CK(cudaSetDevice(h->device));
+  const int Hkv = h->Hkv();
+  const size_t rowb = kHeadDim * 2;
+  for (int i = 0; i < n; ++i) {
+    const int p = pos + i;
+    const int page = h->h_page_table[(size_t)slot * h->max_pages_per_slot + p / kPageTokens];
+    for (int kvi = 0; kvi < 2; ++kvi)
+      for (int hh = 0; hh < Hkv; ++hh) {
+        const char* src = (const char*)h->kv.base + (h->kv.elem_offset(layer, page, kvi, hh) + (size_t)(p % kPageTokens) * kHeadDim) * 2;
+        char* dst = (char*)(kvi ? v_out : k_out) + ((size_t)i * Hkv + hh) * rowb;
+        CK(cudaMemcpyAsync(dst, src, rowb, cudaMemcpyDeviceToHost, h->stream));
+      }
+  }
+  return sync_check(h);
+}
+
+int fmd_q8_0_quantize(const float* src, int64_t rows, int64_t cols, void* blocks) {
+  if (!src || !blocks || rows < 0 || cols % 32) return FMD_EINVAL;
+  std::vector<int8_t> qs((size_t)rows * cols);
+  std::vector<uint16_t> d((size_t)rows * (cols / 32));
+  quantize_rows(src, rows, cols, qs.data(), d.data());
+  uint8_t* b = (uint8_t*)blocks;
+  for (int64_t r = 0; r < rows; ++r)
+    for (int64_t k = 0; k < cols / 32; ++k) {
+      uint8_t* blk = b + (r * (cols / 32) + k) * 34;
+      std::memcpy(blk, &d[r * (cols / 32) + k], 2);
+      std::memcpy(blk + 2, &qs[r * cols + k * 32], 32);
+    }
+  return FMD_OK;
+}
+
+}  // extern "C"
