@@ -1,0 +1,375 @@
+"""Benchmark: decoded tokens/s of the batched Qwen3 decoder step on B200.
+
+Workload: Q8_0 weights (int8 uniform in [-127, 127], f16
+scales |N(0, 0.002)|) with bf16 activations, the full Qwen3 backbone shape
+(28 layers, hidden 1024, 16/8 heads, FFN 3072, vocab 151936), a queue of 256
+requests with prompt lengths log-uniform over 300-8000 and geometric stop steps
+(mean 600, cap 4096), decoded 32 at a time by the on-GPU continuous-batching
+engine (finished slots refilled on the device, prompts prefilled in 2048-row
+chunks inside decode steps).
+
+One bench "step" = one window of `--window` device steps of that engine with
+the queue and weights resident in HBM; `value` = tokens emitted in the K timed
+windows / their CUDA-event time (max over ranks), summed over ranks. `e2e` =
+the same queue through the public host-buffer entry point (`fmd_generate`:
+pinned host arena -> device, run to completion, tokens -> host), wall clock.
+The working set (0.63 GB weights + ~10 GB KV) is far larger than L2, so no L2
+flush is needed between steps.
+
+`--impl reference` times the CPU restatement of the reference decoder
+(oracle/, a PyTorch fp32 port of qwen3.rs; the Rust/candle original cannot be
+built here) on a bounded decode sample of the same workload.
+
+Multi-GPU (torchrun): one process per GPU, each with its own seeded config-3
+queue (request-level data parallelism, no collective on the hot path);
+`scaling` is "weak".
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import __graft_entry__  # noqa: E402
+
+METRIC = "decoded tokens/s per GPU (Q8_0, bf16) and % of HBM roofline; audio s/s"
+UNIT = "tokens/s"
+PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
+TRAFFIC_FILE = ROOT / "profiles" / "attn_decode_config3.md"
+KERNELS_PER_STEP = lambda layers: 1 + 1 + 11 * layers + 2  # noqa: E731  scheduler, embed, per layer, head
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=8)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--window", type=int, default=128, help="device steps per bench step")
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--requests", type=int, default=256)
+    ap.add_argument("--batch", type=int, default=32)
+    ap.add_argument("--chunk", type=int, default=2048)
+    ap.add_argument("--layers", type=int, default=28)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--seed", type=int, default=0)
+    return ap.parse_args()
+
+
+# ---- distributed plumbing ----------------------------------------------------------
+class Dist:
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = None
+        if self.world > 1:
+            import datetime
+
+            import torch
+            import torch.distributed as dist
+
+            torch.cuda.set_device(self.local)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                    device_id=torch.device("cuda", self.local))
+            self.pg = dist
+
+    def barrier(self):
+        if self.pg:
+            self.pg.barrier()
+
+    def reduce(self, value: float, op: str) -> float:
+        if not self.pg:
+            return value
+        import torch
+
+        t = torch.tensor([value], dtype=torch.float64, device=f"cuda:{self.local}")
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX if op == "max" else self.pg.ReduceOp.SUM)
+        return float(t.item())
+
+    def close(self):
+        if self.pg:
+            self.pg.barrier()
+            self.pg.destroy_process_group()
+
+
+# ---- clocks -----------------------------------------------------------------------------
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, power, reasons = [], [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+                power.append(float(parts[3]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "power_w_max": max(power) if power else None, "samples": len(sm), "reasons": sorted(reasons)}
+
+
+def load_peaks() -> tuple[float, str]:
+    try:
+        return float(json.loads(PEAKS_FILE.read_text())["hbm_gbs"]), "measured"
+    except (OSError, ValueError, KeyError):
+        return 6650.0, "fallback"
+
+
+def traffic_per_kv_token() -> float | None:
+    """DRAM bytes per key position of one decode-attention launch, from the
+    committed ncu summary (line `traffic_bytes_per_kv_token: X`)."""
+    try:
+        for ln in TRAFFIC_FILE.read_text().splitlines():
+            if ln.strip().startswith("traffic_bytes_per_kv_token:"):
+                return float(ln.split(":", 1)[1])
+    except OSError:
+        pass
+    return None
+
+
+# ---- model + workload ---------------------------------------------------------------------
+def build_model_and_queue(args, rank: int):
+    pkg = __graft_entry__.load_package()
+    import importlib
+
+    syn = importlib.import_module("fmd_b200.synthetic")
+    cfg = pkg.TextConfig(num_hidden_layers=args.layers)
+    w = syn.make_weights(cfg, seed=args.seed, prequantized=True)
+    wl = syn.workload(3, cfg, w["embed"], seed=args.seed + 1000 * rank, n_requests=args.requests)
+    return pkg, cfg, w, wl
+
+
+def cpu_sample(cfg, w, wl, seconds: float = 12.0, n_seq: int = 4, steps: int | None = None, warmup: int = 0):
+    """Decode-only sample of the workload on the host cores with the CPU
+    restatement (oracle/): `n_seq` sequences at the workload's prompt lengths,
+    KV caches filled with seeded N(0,1) values (prefill not timed)."""
+    import torch
+
+    from oracle import qwen3_ref as ref
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    model = ref.Qwen3Ref(ref.TextConfig(**cfg.oracle_kwargs()), w, "int8_bf16", max_len=8192 + 64)
+    rng = torch.Generator().manual_seed(7)
+    lens = [int(x) for x in wl.prompt_lens[:n_seq]]
+    caches = []
+    for L in lens:
+        cs = model.new_caches(1, L + 64)
+        for c in cs:
+            c.k[:, :, :L] = model.act.r(torch.randn(c.k[:, :, :L].shape, generator=rng))
+            c.v[:, :, :L] = model.act.r(torch.randn(c.v[:, :, :L].shape, generator=rng))
+            c.len = L
+        caches.append(cs)
+    tok = [int(t) for t in np.random.default_rng(3).integers(0, cfg.vocab_size, n_seq)]
+
+    def one_step():
+        for i in range(n_seq):
+            lg = model.decode_step(tok[i], caches[i])
+            tok[i] = int(torch.argmax(lg))
+
+    for _ in range(warmup):
+        one_step()
+    t0 = time.perf_counter()
+    done = 0
+    while True:
+        one_step()
+        done += 1
+        el = time.perf_counter() - t0
+        if (steps is not None and done >= steps) or (steps is None and (el >= seconds or done >= 64)):
+            break
+    el = time.perf_counter() - t0
+    return {"value": n_seq * done / el, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{done} greedy decode steps x {n_seq} sequences (prompt lengths {lens}) of the config-3 "
+                      f"workload, KV caches pre-filled with seeded values (prefill not timed), 28-layer Q8_0 model, "
+                      f"torch fp32 CPU restatement of qwen3.rs with bf16 rounding, {threads} threads",
+            "seconds": el}
+
+
+def run_reference(args, dist: Dist):
+    """`--impl reference`: the reference's CPU path (restated) on a bounded
+    sample of the same workload; rank 0 only."""
+    if dist.rank != 0:
+        return
+    pkg, cfg, w, wl = build_model_and_queue(args, 0)
+    res = cpu_sample(cfg, w, wl, steps=max(args.steps, 1), warmup=max(args.warmup, 0), n_seq=4)
+    line = {"metric": METRIC, "value": res["value"], "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1000.0 * res["seconds"] / max(args.steps, 1),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": "config3: Q8_0 decoder, batch-32 continuous batching, 256-request queue",
+                       "sample": "decode-only", "model": "qwen3-0.6B shape, random init"},
+            "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": res["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    dist = Dist()
+    if args.impl == "reference":
+        try:
+            run_reference(args, dist)
+        finally:
+            dist.close()
+        return
+
+    pkg, cfg, w, wl = build_model_and_queue(args, dist.rank)
+    dec = pkg.Qwen3Decoder(cfg, wl.precision, device=dist.local)
+    dec.load_weights(w)
+    top = np.sort(wl.prompt_lens)[-args.batch:]
+    pool_tokens = int(np.sum(top + 4096 + 64))
+    dec.reserve(max_slots=args.batch, max_tokens=pool_tokens, max_rows=args.batch + args.chunk)
+    eng = pkg.Engine(dec)
+    forced = wl.forced_stop
+    eng.load(wl.prompt_lens, wl.max_new, forced, wl.arena)
+    eng.start(args.batch, args.chunk)
+
+    # warm-up windows (untimed), then K timed windows
+    for _ in range(args.warmup):
+        eng.step(args.window)
+    dist.barrier()
+    clocks = ClockSampler(dist.local)
+    clocks.start()
+    wins = []
+    for _ in range(args.steps):
+        st = eng.step(args.window)
+        wins.append(st)
+        if st.window_steps == 0:
+            break
+    clk = clocks.stop()
+    dist.barrier()
+    tokens = sum(s.window_tokens for s in wins)
+    dev_ms = sum(s.window_device_ms for s in wins)
+    steps_run = sum(s.window_steps for s in wins)
+    tot_tokens = dist.reduce(float(tokens), "sum")
+    max_ms = dist.reduce(dev_ms, "max")
+    value = tot_tokens / (max_ms / 1000.0) if max_ms > 0 else 0.0
+
+    # dominant kernel: decode attention (CUDA events around each launch of
+    # the last step of every timed window)
+    peak, peak_kind = load_peaks()
+    samples = [(s.attn_kv_tokens, s.attn_decode_ms, s.attn_rows) for s in wins if s.attn_decode_ms > 0]
+    kv_per_launch = statistics.mean(x[0] for x in samples) if samples else 0.0
+    ms_per_launch = statistics.mean(x[1] for x in samples) if samples else 0.0
+    rows = statistics.mean(x[2] for x in samples) if samples else 0.0
+    kvh, hd, hq = cfg.num_key_value_heads, cfg.head_dim, cfg.num_attention_heads
+    alg_bytes = kv_per_launch * kvh * hd * 2 * 2 + rows * hq * hd * 2 * 2
+    achieved = alg_bytes / (ms_per_launch / 1000.0) / 1e9 if ms_per_launch > 0 else 0.0
+    tpk = traffic_per_kv_token()
+
+    # whole-step HBM roofline at the measured mean context
+    w_bytes = cfg.n_params() * 34 / 32
+    mean_kv = kv_per_launch
+    step_bytes = w_bytes + mean_kv * cfg.kv_bytes_per_token() + rows * cfg.kv_bytes_per_token()
+    step_ms = dev_ms / max(steps_run, 1)
+
+    e2e = None
+    if not args.no_e2e:
+        import torch
+
+        arena_pinned = torch.from_numpy(wl.arena).pin_memory()
+        arena_np = arena_pinned.numpy()
+        eng2 = pkg.Engine(dec)
+        dist.barrier()
+        t0 = time.perf_counter()
+        out, st2 = eng2.generate(wl.prompt_lens, wl.max_new, forced, arena_np, max_batch=args.batch,
+                                 prefill_chunk=args.chunk)
+        el = time.perf_counter() - t0
+        gen = sum(len(o.tokens) for o in out)
+        tot = dist.reduce(float(gen), "sum")
+        el_max = dist.reduce(el, "max")
+        h2d = wl.arena.nbytes + 24 * len(wl.prompt_lens)
+        d2h = 4 * len(wl.prompt_lens) * int(np.max(wl.max_new)) + 8 * len(wl.prompt_lens)
+        e2e = {"value": tot / el_max, "unit": UNIT, "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+               "step": "whole queue through fmd_generate (pinned host arena in, tokens out)",
+               "seconds": el_max, "tokens": int(tot)}
+
+    cpu = None
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu:
+        cpu = cpu_sample(cfg, w, wl)
+        cpu.pop("seconds", None)
+
+    if dist.rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": dist.world, "steps": len(wins),
+            "warmup": args.warmup, "ms_per_step": max_ms / max(len(wins), 1), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16 activations, Q8_0 weights", "data": "synthetic",
+            "config": {"workload": "BASELINE config 3: Q8_0 decoder + lm_head, bf16 activations, batch 32 "
+                                   "continuous batching over a 256-request queue (prompts log-uniform 300-8000, "
+                                   "geometric stops mean 600 cap 4096), on-GPU refill, 2048-row prefill chunks",
+                       "requests_per_gpu": len(wl.prompt_lens), "batch": args.batch, "prefill_chunk": args.chunk,
+                       "layers": cfg.num_hidden_layers, "step": f"{args.window} device steps",
+                       "device_steps_timed": int(steps_run), "l2": "working set >> L2 (no flush needed)",
+                       "parallelism": f"dp{dist.world} (request-sharded, no collective)"},
+            "roofline": {"bound": "hbm", "kernel": "k_attn_decode (split-KV GQA decode attention)",
+                         "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "traffic": (tpk * kv_per_launch) if tpk else None, "peak_kind": peak_kind,
+                         "alg_bytes_per_launch": alg_bytes, "ms_per_launch": ms_per_launch},
+            "step_roofline": {"bytes_per_step": step_bytes, "ms_per_step": step_ms,
+                              "achieved_gbs": step_bytes / (step_ms / 1000.0) / 1e9 if step_ms > 0 else 0.0,
+                              "frac": (step_bytes / (step_ms / 1000.0) / 1e9) / peak if step_ms > 0 else 0.0,
+                              "mean_decode_rows": rows, "mean_kv_positions": mean_kv},
+            "clocks": clk,
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+            "gpu_launches": int(steps_run * KERNELS_PER_STEP(cfg.num_hidden_layers) + len(wins)),
+            "tokens_timed": int(tot_tokens),
+        }
+        print(json.dumps(line), flush=True)
+    dec.close()
+    dist.close()
+
+
+if __name__ == "__main__":
+    main()

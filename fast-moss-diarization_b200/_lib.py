@@ -37,7 +37,8 @@ FINISH_STOP, FINISH_LENGTH, FINISH_ERROR = 0, 1, 2
 EXPORTS = [
     "fmd_create", "fmd_destroy", "fmd_last_error", "fmd_status_string", "fmd_version", "fmd_load_weights",
     "fmd_kv_reserve", "fmd_cache_bytes", "fmd_memory_bytes", "fmd_embed", "fmd_slot_open", "fmd_slot_release",
-    "fmd_slot_len", "fmd_prefill", "fmd_decode_step", "fmd_engine_load", "fmd_engine_run", "fmd_engine_fetch",
+    "fmd_slot_len", "fmd_prefill", "fmd_decode_step", "fmd_engine_load", "fmd_engine_start", "fmd_engine_step",
+    "fmd_engine_run", "fmd_engine_fetch",
     "fmd_generate", "fmd_debug_weight", "fmd_debug_kv", "fmd_q8_0_quantize",
 ]
 
@@ -86,7 +87,9 @@ class Result(C.Structure):
 class Stats(C.Structure):
     _fields_ = [("steps", C.c_int64), ("generated_tokens", C.c_int64), ("prefill_tokens", C.c_int64),
                 ("requests_done", C.c_int64), ("generate_seconds", C.c_double), ("device_status", C.c_int32),
-                ("reserved", C.c_int32)]
+                ("reserved", C.c_int32), ("window_steps", C.c_int64), ("window_tokens", C.c_int64),
+                ("window_device_ms", C.c_double), ("attn_decode_ms", C.c_double), ("attn_kv_tokens", C.c_int64),
+                ("attn_rows", C.c_int64)]
 
 
 _lib = None
@@ -119,6 +122,8 @@ def load() -> C.CDLL:
         "fmd_prefill": (C.c_int, [P, I32, IP, IP, P, I32, C.POINTER(C.c_float), IP]),
         "fmd_decode_step": (C.c_int, [P, I32, IP, IP, C.POINTER(C.c_float), IP]),
         "fmd_engine_load": (C.c_int, [P, C.POINTER(Request), I32, P, I64, I32]),
+        "fmd_engine_start": (C.c_int, [P, I32, I32]),
+        "fmd_engine_step": (C.c_int, [P, I64, C.POINTER(Stats)]),
         "fmd_engine_run": (C.c_int, [P, I32, I32, I64, C.POINTER(Stats)]),
         "fmd_engine_fetch": (C.c_int, [P, IP, I32, C.POINTER(Result)]),
         "fmd_generate": (C.c_int, [P, C.POINTER(Request), I32, P, I64, I32, I32, I32, IP, I32,

@@ -142,6 +142,10 @@ struct fmd_handle {
   EngineCounters* h_ctr = nullptr;
   cudaGraphExec_t graph_exec = nullptr;
   int graph_batch = -1, graph_chunk = -1;
+  bool engine_started = false;
+  bool record_attn_events = false;             // set while capturing the step graph
+  std::vector<cudaEvent_t> attn_events;        // [2 * layers] around each decode-attention launch
+  cudaEvent_t win_begin = nullptr, win_end = nullptr;
 
   int elem() const { return 2; }
   int H() const { return cfg.hidden_size; }
@@ -336,8 +340,10 @@ void run_forward(fmd_handle* h, float* logits_dev, const void* arena) {
     launch_qkv_epilogue(h->at, h->plan, row_grid, h->part, L.qkv.split, ss, h->Hq(), h->Hkv(), L.q_norm, L.k_norm,
                         h->rope_cos, h->rope_sin, h->qbuf, h->kv, l, eps, s);
     trace(h, "qkv_epi", l);
+    if (h->record_attn_events) cudaEventRecordWithFlags(h->attn_events[2 * l], s, cudaEventRecordExternal);
     launch_attn_decode(h->at, h->plan, h->di_grid, h->Hq(), h->Hkv(), h->qbuf, h->kv, l, h->attn_scale, h->pacc,
                        h->pml, s);
+    if (h->record_attn_events) cudaEventRecordWithFlags(h->attn_events[2 * l + 1], s, cudaEventRecordExternal);
     trace(h, "attn_decode", l);
     launch_attn_combine(h->at, h->plan, std::min(h->max_slots, 296), h->Hq(), h->pacc, h->pml, h->ctx, s);
     trace(h, "attn_combine", l);
@@ -554,6 +560,9 @@ int fmd_destroy(fmd_handle* h) {
   cudaSetDevice(h->device);
   cudaStreamSynchronize(h->stream);
   release_graph(h);
+  for (cudaEvent_t e : h->attn_events) cudaEventDestroy(e);
+  if (h->win_begin) cudaEventDestroy(h->win_begin);
+  if (h->win_end) cudaEventDestroy(h->win_end);
   for (auto& a : h->allocs) cudaFree(a.p);
   for (DevBuf* b : {&h->eng_reqs, &h->eng_arena, &h->eng_tokens, &h->eng_results})
     if (b->p) cudaFree(b->p);
@@ -912,10 +921,14 @@ int fmd_engine_load(fmd_handle* h, const fmd_request* reqs, int32_t n_reqs, cons
   CK(cudaMemcpy(h->eng_reqs.p, reqs, sizeof(DevRequest) * n_reqs, cudaMemcpyHostToDevice));
   const size_t arena_bytes = (size_t)embed_rows * h->H() * 2;
   if ((rc = alloc(h->eng_arena, arena_bytes))) return rc;
-  // convert in slices to bound host memory
+  // convert in slices to bound host memory; an arena already in the
+  // activation dtype is copied straight from the caller's (possibly pinned)
+  // buffer
   const size_t rowb = (size_t)h->H() * (embeds_dtype == FMD_DT_F32 ? 4 : 2);
+  const bool same = (h->at == kBF16 && embeds_dtype == FMD_DT_BF16) || (h->at == kF16 && embeds_dtype == FMD_DT_F16);
+  if (same) CK(cudaMemcpy(h->eng_arena.p, embeds, arena_bytes, cudaMemcpyHostToDevice));
   std::vector<uint16_t> act;
-  for (int64_t r = 0; r < embed_rows; r += 65536) {
+  for (int64_t r = 0; !same && r < embed_rows; r += 65536) {
     const int64_t nr = std::min<int64_t>(65536, embed_rows - r);
     if ((rc = convert_rows_to_act(h, (const char*)embeds + r * rowb, embeds_dtype, nr, act))) return rc;
     CK(cudaMemcpy((char*)h->eng_arena.p + (size_t)r * h->H() * 2, act.data(), act.size() * 2,
@@ -962,7 +975,7 @@ EngineDev make_engine_dev(fmd_handle* h, int max_batch, int chunk) {
 }
 }  // namespace
 
-int fmd_engine_run(fmd_handle* h, int32_t max_batch, int32_t prefill_chunk, int64_t max_steps, fmd_stats* stats) {
+int fmd_engine_start(fmd_handle* h, int32_t max_batch, int32_t prefill_chunk) {
   int rc = check_ready(h);
   if (rc) return rc;
   if (!h->eng_reqs.p) return fail(h, FMD_EBUSY, "no queue loaded (fmd_engine_load)");
@@ -972,28 +985,34 @@ int fmd_engine_run(fmd_handle* h, int32_t max_batch, int32_t prefill_chunk, int6
   for (int s = 0; s < h->max_slots; ++s)
     if (h->slot_cap[s] >= 0) return fail(h, FMD_EBUSY, "close operator-mode slots before running the engine");
   CK(cudaSetDevice(h->device));
-  const auto t0 = std::chrono::steady_clock::now();
+  h->engine_started = false;
   // reset engine state: all slots free, all pages on the free stack, empty plan
   CK(cudaMemsetAsync(h->eng_slot, 0, (size_t)h->max_slots * 7 * 4, h->stream));
-  {
-    std::vector<int> fs(h->n_pages);
-    for (int i = 0; i < h->n_pages; ++i) fs[i] = h->n_pages - 1 - i;
-    CK(cudaMemcpyAsync(h->eng_free, fs.data(), fs.size() * 4, cudaMemcpyHostToDevice, h->stream));
-    EngineCounters c{};
-    c.free_top = h->n_pages;
-    *h->h_ctr = c;
-    CK(cudaMemcpyAsync(h->eng_ctr, h->h_ctr, sizeof(c), cudaMemcpyHostToDevice, h->stream));
-    CK(cudaMemsetAsync(h->d_plan, 0, h->layout.total * 4, h->stream));
-    CK(cudaMemsetAsync(h->eng_results.p, 0, sizeof(DevResult) * h->eng_n_reqs, h->stream));
-    CK(cudaStreamSynchronize(h->stream));
+  std::vector<int> fs(h->n_pages);
+  for (int i = 0; i < h->n_pages; ++i) fs[i] = h->n_pages - 1 - i;
+  CK(cudaMemcpyAsync(h->eng_free, fs.data(), fs.size() * 4, cudaMemcpyHostToDevice, h->stream));
+  EngineCounters c{};
+  c.free_top = h->n_pages;
+  *h->h_ctr = c;
+  CK(cudaMemcpyAsync(h->eng_ctr, h->h_ctr, sizeof(c), cudaMemcpyHostToDevice, h->stream));
+  CK(cudaMemsetAsync(h->d_plan, 0, h->layout.total * 4, h->stream));
+  CK(cudaMemsetAsync(h->eng_results.p, 0, sizeof(DevResult) * h->eng_n_reqs, h->stream));
+  CK(cudaStreamSynchronize(h->stream));
+  if (h->attn_events.empty()) {
+    h->attn_events.resize(2 * h->cfg.num_hidden_layers);
+    for (auto& e : h->attn_events) CK(cudaEventCreate(&e));
+    CK(cudaEventCreate(&h->win_begin));
+    CK(cudaEventCreate(&h->win_end));
   }
   if (!h->graph_exec || h->graph_batch != max_batch || h->graph_chunk != prefill_chunk) {
     release_graph(h);
     const EngineDev e = make_engine_dev(h, max_batch, prefill_chunk);
     cudaGraph_t g;
     CK(cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal));
+    h->record_attn_events = true;
     launch_schedule(e, h->stream);
     run_forward(h, nullptr, h->eng_arena.p);
+    h->record_attn_events = false;
     CK(cudaStreamEndCapture(h->stream, &g));
     cudaError_t ie = cudaGraphInstantiate(&h->graph_exec, g, 0);
     cudaGraphDestroy(g);
@@ -1001,10 +1020,25 @@ int fmd_engine_run(fmd_handle* h, int32_t max_batch, int32_t prefill_chunk, int6
     h->graph_batch = max_batch;
     h->graph_chunk = prefill_chunk;
   }
+  h->engine_started = true;
+  return FMD_OK;
+}
+
+int fmd_engine_step(fmd_handle* h, int64_t max_steps, fmd_stats* stats) {
+  int rc = check_ready(h);
+  if (rc) return rc;
+  if (!h->engine_started || !h->graph_exec) return fail(h, FMD_EBUSY, "engine not started (fmd_engine_start)");
+  if (max_steps < 0) return fail(h, FMD_EINVAL, "negative step count");
+  CK(cudaSetDevice(h->device));
+  const auto t0 = std::chrono::steady_clock::now();
+  CK(cudaMemcpyAsync(h->h_ctr, h->eng_ctr, sizeof(EngineCounters), cudaMemcpyDeviceToHost, h->stream));
+  if ((rc = sync_check(h))) return rc;
+  const long long tokens0 = h->h_ctr->gen_tokens;
+  bool finished = h->h_ctr->done >= h->eng_n_reqs;
   int64_t launched = 0;
-  bool finished = false;
   long long last_progress = -1;
   int idle_checks = 0;
+  CK(cudaEventRecord(h->win_begin, h->stream));
   while (!finished && launched < max_steps) {
     const int64_t k = std::min<int64_t>(kEngineCheckEvery, max_steps - launched);
     for (int64_t i = 0; i < k; ++i) CK(cudaGraphLaunch(h->graph_exec, h->stream));
@@ -1022,12 +1056,25 @@ int fmd_engine_run(fmd_handle* h, int32_t max_batch, int32_t prefill_chunk, int6
                                         " steps (requests done " + std::to_string(h->h_ctr->done) + ")");
   }
   // a consume-only scheduler pass books the samples of the last step run
-  if (!finished) {
-    EngineDev e = make_engine_dev(h, max_batch, prefill_chunk);
-    e.consume_only = 1;
-    launch_schedule(e, h->stream);
-    CK(cudaMemcpyAsync(h->h_ctr, h->eng_ctr, sizeof(EngineCounters), cudaMemcpyDeviceToHost, h->stream));
-    if ((rc = sync_check(h))) return rc;
+  EngineDev e = make_engine_dev(h, h->graph_batch, h->graph_chunk);
+  e.consume_only = 1;
+  CK(cudaEventRecord(h->win_end, h->stream));
+  const long long kv_last = h->h_ctr->last_kv_tokens, rows_last = h->h_ctr->last_decode_rows;
+  launch_schedule(e, h->stream);
+  CK(cudaMemcpyAsync(h->h_ctr, h->eng_ctr, sizeof(EngineCounters), cudaMemcpyDeviceToHost, h->stream));
+  if ((rc = sync_check(h))) return rc;
+  // the consume-only pass leaves an empty plan; the next graph step re-plans
+  // from the slot state, so the window boundary changes no result.
+  float win_ms = 0.f;
+  if (launched > 0) CK(cudaEventElapsedTime(&win_ms, h->win_begin, h->win_end));
+  double attn_ms = 0.0;
+  if (launched > 0) {
+    for (int l = 0; l < h->cfg.num_hidden_layers; ++l) {
+      float ms = 0.f;
+      CK(cudaEventElapsedTime(&ms, h->attn_events[2 * l], h->attn_events[2 * l + 1]));
+      attn_ms += ms;
+    }
+    attn_ms /= h->cfg.num_hidden_layers;
   }
   const auto t1 = std::chrono::steady_clock::now();
   if (stats) {
@@ -1038,8 +1085,20 @@ int fmd_engine_run(fmd_handle* h, int32_t max_batch, int32_t prefill_chunk, int6
     stats->requests_done = h->h_ctr->done;
     stats->generate_seconds = std::chrono::duration<double>(t1 - t0).count();
     stats->device_status = h->h_ctr->status;
+    stats->window_steps = launched;
+    stats->window_tokens = h->h_ctr->gen_tokens - tokens0;
+    stats->window_device_ms = win_ms;
+    stats->attn_decode_ms = attn_ms;
+    stats->attn_kv_tokens = kv_last;
+    stats->attn_rows = rows_last;
   }
   return FMD_OK;
+}
+
+int fmd_engine_run(fmd_handle* h, int32_t max_batch, int32_t prefill_chunk, int64_t max_steps, fmd_stats* stats) {
+  int rc = fmd_engine_start(h, max_batch, prefill_chunk);
+  if (rc) return rc;
+  return fmd_engine_step(h, max_steps, stats);
 }
 
 int fmd_engine_fetch(fmd_handle* h, int32_t* tokens, int32_t token_stride, fmd_result* results) {

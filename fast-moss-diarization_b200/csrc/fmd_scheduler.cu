@@ -106,9 +106,11 @@ __global__ void __launch_bounds__(256) k_schedule(EngineDev e) {
 
     // ---- 3. lay out the next plan (segment descriptors) ----
     int rows = 0, items = 0, samples = 0, pblocks = 0;
+    long long kv_tokens = 0;
     for (int s = 0; s < e.max_batch; ++s) {
       s_seg_n[s] = 0;
       if (e.slot_state[s] == kSlotDecode && rows < e.max_rows) {
+        kv_tokens += e.slot_len[s] + 1;
         s_seg_row0[s] = rows;
         s_seg_n[s] = 1;
         s_seg_pos0[s] = e.slot_len[s];
@@ -121,6 +123,8 @@ __global__ void __launch_bounds__(256) k_schedule(EngineDev e) {
       }
     }
     const int n_decode = rows;
+    c->last_kv_tokens = kv_tokens;
+    c->last_decode_rows = n_decode;
     int budget_rows = e.prefill_chunk;
     for (int s = 0; s < e.max_batch; ++s) {
       if (e.slot_state[s] != kSlotPrefill) continue;

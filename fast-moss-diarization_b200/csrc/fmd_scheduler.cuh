@@ -29,6 +29,8 @@ struct EngineCounters {
   long long steps;
   long long gen_tokens;
   long long prefill_tokens;
+  long long last_kv_tokens;    // sum of (pos + 1) over the decode rows of the latest plan
+  long long last_decode_rows;
 };
 
 struct EngineDev {

@@ -29,7 +29,8 @@ class Generated:
 
 @dataclass
 class BatchStats:
-    """The decode-side fields of `BatchStats` (engine.rs:151-174)."""
+    """The decode-side fields of `BatchStats` (engine.rs:151-174), plus the
+    device-timed window of the last `run`/`step` call."""
 
     requests: int = 0
     generate_seconds: float = 0.0
@@ -37,6 +38,21 @@ class BatchStats:
     prefill_tokens: int = 0
     steps: int = 0
     device_status: int = 0
+    window_steps: int = 0
+    window_tokens: int = 0
+    window_device_ms: float = 0.0
+    attn_decode_ms: float = 0.0
+    attn_kv_tokens: int = 0
+    attn_rows: int = 0
+
+    @classmethod
+    def from_c(cls, st) -> "BatchStats":
+        return cls(requests=int(st.requests_done), generate_seconds=st.generate_seconds,
+                   generated_tokens=int(st.generated_tokens), prefill_tokens=int(st.prefill_tokens),
+                   steps=int(st.steps), device_status=int(st.device_status), window_steps=int(st.window_steps),
+                   window_tokens=int(st.window_tokens), window_device_ms=float(st.window_device_ms),
+                   attn_decode_ms=float(st.attn_decode_ms), attn_kv_tokens=int(st.attn_kv_tokens),
+                   attn_rows=int(st.attn_rows))
 
     @property
     def decode_tokens_per_second(self) -> float:
@@ -89,9 +105,23 @@ class Engine:
     def run(self, max_batch: int, prefill_chunk: int = 2048, max_steps: int = 1 << 40) -> BatchStats:
         st = _lib.Stats()
         self.lib_check(self.lib.fmd_engine_run(self.dec.handle, max_batch, prefill_chunk, max_steps, C.byref(st)))
-        return BatchStats(requests=int(st.requests_done), generate_seconds=st.generate_seconds,
-                          generated_tokens=int(st.generated_tokens), prefill_tokens=int(st.prefill_tokens),
-                          steps=int(st.steps), device_status=int(st.device_status))
+        return BatchStats.from_c(st)
+
+    def start(self, max_batch: int, prefill_chunk: int = 2048) -> None:
+        """Reset onto the loaded queue and build the step graph."""
+        self.lib_check(self.lib.fmd_engine_start(self.dec.handle, max_batch, prefill_chunk))
+
+    def step(self, max_steps: int) -> BatchStats:
+        """Advance the started engine by up to `max_steps` device steps."""
+        st = _lib.Stats()
+        self.lib_check(self.lib.fmd_engine_step(self.dec.handle, max_steps, C.byref(st)))
+        return BatchStats.from_c(st)
+
+    @property
+    def done(self) -> bool:
+        st = _lib.Stats()
+        self.lib_check(self.lib.fmd_engine_step(self.dec.handle, 0, C.byref(st)))
+        return st.requests_done >= self.n
 
     def fetch(self) -> list[Generated]:
         stride = max(self.max_new, 1)

@@ -123,13 +123,22 @@ typedef struct fmd_result {
 } fmd_result;
 
 typedef struct fmd_stats {
-  int64_t steps;            /* device steps run                                  */
+  int64_t steps;            /* device steps run since fmd_engine_start           */
   int64_t generated_tokens; /* engine.rs:395 BatchStats::generated_tokens        */
   int64_t prefill_tokens;
   int64_t requests_done;
-  double generate_seconds;  /* wall time of the run (engine.rs:424)              */
+  double generate_seconds;  /* wall time of the call (engine.rs:424)             */
   int32_t device_status;    /* 0, or a FMD_E* code raised on the device          */
   int32_t reserved;
+  /* the window advanced by this call (fmd_engine_step / fmd_engine_run) */
+  int64_t window_steps;     /* device steps launched                             */
+  int64_t window_tokens;    /* tokens emitted                                    */
+  double window_device_ms;  /* CUDA-event time on the engine stream              */
+  /* decode attention of the window's last step (CUDA events around each of
+   * its per-layer launches inside the step graph) */
+  double attn_decode_ms;    /* mean duration of one launch                       */
+  int64_t attn_kv_tokens;   /* sum of key positions read by one launch           */
+  int64_t attn_rows;        /* decode rows in that step                          */
 } fmd_stats;
 
 /* ---- handle ------------------------------------------------------------- */
@@ -198,10 +207,20 @@ int fmd_decode_step(fmd_handle* h, int32_t n, const int32_t* slots, const int32_
 int fmd_engine_load(fmd_handle* h, const fmd_request* reqs, int32_t n_reqs,
                     const void* embeds, int64_t embed_rows, int32_t embeds_dtype);
 
-/* Run the loaded queue on the device: up to `max_batch` sequences decode
- * together; finished slots are refilled from the queue on the GPU; prompts
- * are prefilled in chunks of up to `prefill_chunk` rows mixed into decode
- * steps. Returns when every request is done or `max_steps` steps ran. */
+/* Reset the engine onto the loaded queue (all slots free, all KV pages free)
+ * and build the CUDA graph of one step for (`max_batch`, `prefill_chunk`). */
+int fmd_engine_start(fmd_handle* h, int32_t max_batch, int32_t prefill_chunk);
+
+/* Advance the started engine by up to `max_steps` device steps (fewer if the
+ * queue drains). `stats` is cumulative since fmd_engine_start, plus the window
+ * fields for this call. */
+int fmd_engine_step(fmd_handle* h, int64_t max_steps, fmd_stats* stats);
+
+/* fmd_engine_start + fmd_engine_step until the queue drains: up to
+ * `max_batch` sequences decode together; finished slots are refilled from the
+ * queue on the GPU; prompts are prefilled in chunks of up to `prefill_chunk`
+ * rows mixed into decode steps. Returns when every request is done or
+ * `max_steps` steps ran. */
 int fmd_engine_run(fmd_handle* h, int32_t max_batch, int32_t prefill_chunk, int64_t max_steps,
                    fmd_stats* stats);
 
