@@ -66,6 +66,8 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--max-new", type=int, default=4096,
+                    help="cap on max_new_tokens per request (bounds the KV pool for profiling runs)")
     return ap.parse_args()
 
 
@@ -187,6 +189,7 @@ def build_model_and_queue(args, rank: int):
     cfg = pkg.TextConfig(num_hidden_layers=args.layers)
     w = syn.make_weights(cfg, seed=args.seed, prequantized=True)
     wl = syn.workload(3, cfg, w["embed"], seed=args.seed + 1000 * rank, n_requests=args.requests)
+    wl.max_new = np.minimum(wl.max_new, args.max_new)
     return pkg, cfg, w, wl
 
 
@@ -268,7 +271,7 @@ def main():
     dec = pkg.Qwen3Decoder(cfg, wl.precision, device=dist.local)
     dec.load_weights(w)
     top = np.sort(wl.prompt_lens)[-args.batch:]
-    pool_tokens = int(np.sum(top + 4096 + 64))
+    pool_tokens = int(np.sum(top + int(np.max(wl.max_new)) + 64))
     dec.reserve(max_slots=args.batch, max_tokens=pool_tokens, max_rows=args.batch + args.chunk)
     eng = pkg.Engine(dec)
     forced = wl.forced_stop

@@ -366,178 +366,6 @@ __global__ void __launch_bounds__(256) k_qkv_epilogue(Plan p, const float* __res
 }
 
 // ---------------------------------------------------------------------------
-// Split-KV GQA decode attention (qwen3.rs:229-257 for t = 1): one CTA per
-// (split item, kv head) computes both query heads of the group from one read
-// of each K/V row. 8 groups of 16 lanes each take 4 keys at a time (16-byte
-// loads, 8 dims per lane); online softmax in the exp2 domain; partial
-// (m, l, acc) per item, merged by k_attn_combine.
-// ---------------------------------------------------------------------------
-template <typename T>
-__global__ void __launch_bounds__(128) k_attn_decode(Plan p, int Hq, const T* __restrict__ q, KvView kv, int layer,
-                                                     float scale_log2, float* __restrict__ part_acc,
-                                                     float* __restrict__ part_ml) {
-  __shared__ float s_m[8][2], s_l[8][2];
-  __shared__ float s_acc[8][2][kHeadDim];
-  const int n_items = p.counts->n_ditems;
-  const int h = blockIdx.y;
-  const int grp = threadIdx.x >> 4, l16 = threadIdx.x & 15;
-  const T* kvb = reinterpret_cast<const T*>(kv.base);
-  const size_t v_off = (size_t)kv.kv_heads * kPageTokens * kHeadDim;
-  for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
-    const int r = p.di_row[it], k0 = p.di_start[it], k1 = p.di_end[it];
-    const int slot = p.row_slot[r];
-    const int* ptab = kv.page_table + (size_t)slot * kv.max_pages_per_slot;
-    float qa[8], qb[8];
-    {
-      const T* qr = q + (size_t)r * Hq * kHeadDim + (2 * h) * kHeadDim + l16 * 8;
-      const int4 va = *reinterpret_cast<const int4*>(qr);
-      const int4 vb = *reinterpret_cast<const int4*>(qr + kHeadDim);
-      const uint32_t* ua = reinterpret_cast<const uint32_t*>(&va);
-      const uint32_t* ub = reinterpret_cast<const uint32_t*>(&vb);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float2 fa = Act<T>::unpack2(ua[j]), fb = Act<T>::unpack2(ub[j]);
-        qa[2 * j] = fa.x * scale_log2; qa[2 * j + 1] = fa.y * scale_log2;
-        qb[2 * j] = fb.x * scale_log2; qb[2 * j + 1] = fb.y * scale_log2;
-      }
-    }
-    float m0 = -FLT_MAX, m1 = -FLT_MAX, l0 = 0.f, l1 = 0.f;
-    float acc0[8], acc1[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) acc0[i] = acc1[i] = 0.f;
-
-    // The trip count is uniform across the warp (both 16-lane halves iterate
-    // together) because the key reduction below shuffles over the full warp.
-    const int warp_first = k0 + (grp >> 1) * 8;
-    for (int wb = warp_first; wb < k1; wb += 32) {
-      const int tk = wb + (grp & 1) * 4;
-      int4 kk[4], vv[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int tok = tk + j;
-        if (tok < k1) {
-          const int page = ptab[tok >> 6];
-          const T* kp = kvb + kv.elem_offset(layer, page, 0, h) + (size_t)(tok & 63) * kHeadDim + l16 * 8;
-          kk[j] = *reinterpret_cast<const int4*>(kp);
-          vv[j] = *reinterpret_cast<const int4*>(kp + v_off);
-        } else {
-          kk[j] = make_int4(0, 0, 0, 0);
-          vv[j] = make_int4(0, 0, 0, 0);
-        }
-      }
-      float s0[4], s1[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const uint32_t* u = reinterpret_cast<const uint32_t*>(&kk[j]);
-        float a = 0.f, b = 0.f;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float2 f = Act<T>::unpack2(u[i]);
-          a = fmaf(qa[2 * i], f.x, a); a = fmaf(qa[2 * i + 1], f.y, a);
-          b = fmaf(qb[2 * i], f.x, b); b = fmaf(qb[2 * i + 1], f.y, b);
-        }
-#pragma unroll
-        for (int o = 8; o > 0; o >>= 1) {
-          a += __shfl_xor_sync(0xffffffffu, a, o);
-          b += __shfl_xor_sync(0xffffffffu, b, o);
-        }
-        const bool valid = tk + j < k1;
-        s0[j] = valid ? a : -FLT_MAX;
-        s1[j] = valid ? b : -FLT_MAX;
-      }
-      const float mx0 = fmaxf(fmaxf(s0[0], s0[1]), fmaxf(s0[2], s0[3]));
-      const float mx1 = fmaxf(fmaxf(s1[0], s1[1]), fmaxf(s1[2], s1[3]));
-      const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-      const float c0 = exp2f(m0 - mn0), c1 = exp2f(m1 - mn1);
-      float p0[4], p1[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const bool valid = tk + j < k1;  // a half may hold no valid key at all
-        p0[j] = valid ? exp2f(s0[j] - mn0) : 0.f;
-        p1[j] = valid ? exp2f(s1[j] - mn1) : 0.f;
-      }
-      l0 = l0 * c0 + (p0[0] + p0[1]) + (p0[2] + p0[3]);
-      l1 = l1 * c1 + (p1[0] + p1[1]) + (p1[2] + p1[3]);
-      m0 = mn0;
-      m1 = mn1;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        acc0[i] *= c0;
-        acc1[i] *= c1;
-      }
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const uint32_t* u = reinterpret_cast<const uint32_t*>(&vv[j]);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float2 f = Act<T>::unpack2(u[i]);
-          acc0[2 * i] = fmaf(p0[j], f.x, acc0[2 * i]);
-          acc0[2 * i + 1] = fmaf(p0[j], f.y, acc0[2 * i + 1]);
-          acc1[2 * i] = fmaf(p1[j], f.x, acc1[2 * i]);
-          acc1[2 * i + 1] = fmaf(p1[j], f.y, acc1[2 * i + 1]);
-        }
-      }
-    }
-    // merge the 8 groups
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      s_acc[grp][0][l16 * 8 + i] = acc0[i];
-      s_acc[grp][1][l16 * 8 + i] = acc1[i];
-    }
-    if (l16 == 0) {
-      s_m[grp][0] = m0; s_m[grp][1] = m1;
-      s_l[grp][0] = l0; s_l[grp][1] = l1;
-    }
-    __syncthreads();
-    {
-      const int d = threadIdx.x;  // 128 threads = 128 dims
-#pragma unroll
-      for (int hd = 0; hd < 2; ++hd) {
-        float M = -FLT_MAX;
-#pragma unroll
-        for (int gi = 0; gi < 8; ++gi) M = fmaxf(M, s_m[gi][hd]);
-        float A = 0.f, L = 0.f;
-#pragma unroll
-        for (int gi = 0; gi < 8; ++gi) {
-          const float wgt = exp2f(s_m[gi][hd] - M);
-          A = fmaf(s_acc[gi][hd][d], wgt, A);
-          L = fmaf(s_l[gi][hd], wgt, L);
-        }
-        const size_t e = (size_t)it * Hq + 2 * h + hd;
-        part_acc[e * kHeadDim + d] = A;
-        if (d == 0) {
-          part_ml[e * 2] = M;
-          part_ml[e * 2 + 1] = L;
-        }
-      }
-    }
-    __syncthreads();
-  }
-}
-
-template <typename T>
-__global__ void __launch_bounds__(256) k_attn_combine(Plan p, int Hq, const float* __restrict__ part_acc,
-                                                      const float* __restrict__ part_ml, T* __restrict__ ctx) {
-  const int n_dec = p.counts->n_decode;
-  for (int r = blockIdx.x; r < n_dec; r += gridDim.x) {
-  const int i0 = p.drow_item0[r], n = p.drow_nitems[r];
-  for (int e = threadIdx.x; e < Hq * kHeadDim; e += blockDim.x) {
-    const int hq = e / kHeadDim, d = e % kHeadDim;
-    float M = -FLT_MAX;
-    for (int i = 0; i < n; ++i) M = fmaxf(M, part_ml[((size_t)(i0 + i) * Hq + hq) * 2]);
-    float A = 0.f, L = 0.f;
-    for (int i = 0; i < n; ++i) {
-      const size_t b = (size_t)(i0 + i) * Hq + hq;
-      const float wgt = exp2f(part_ml[b * 2] - M);
-      L = fmaf(part_ml[b * 2 + 1], wgt, L);
-      A = fmaf(part_acc[b * kHeadDim + d], wgt, A);
-    }
-    ctx[(size_t)r * Hq * kHeadDim + e] = Act<T>::from_f(A / L);
-  }
-  }
-}
-
-// ---------------------------------------------------------------------------
 // Chunked-prefill flash attention (qwen3.rs:229-257 with the causal mask of
 // :523-562): one CTA per (block of <= 32 query rows of one sequence, kv head)
 // covers both query heads of the group (4 warps = 2 heads x 2 x 16 rows) so
@@ -834,19 +662,6 @@ void launch_qkv_epilogue(ActType at, const Plan& p, int R, const float* part, in
   FMD_DISPATCH(at, k_qkv_epilogue<T><<<R, 256, 0, s>>>(p, part, split, split_stride, Hq, Hkv, (const T*)qn_w,
                                                         (const T*)kn_w, (const T*)cos, (const T*)sin, (T*)q_out, kv,
                                                         layer, eps));
-}
-
-void launch_attn_decode(ActType at, const Plan& p, int grid_items, int Hq, int Hkv, const void* q, const KvView& kv,
-                        int layer, float scale, float* part_acc, float* part_ml, cudaStream_t s) {
-  const float scale_log2 = scale * 1.4426950408889634f;
-  dim3 grid(grid_items, Hkv);
-  FMD_DISPATCH(at, k_attn_decode<T><<<grid, 128, 0, s>>>(p, Hq, (const T*)q, kv, layer, scale_log2, part_acc,
-                                                          part_ml));
-}
-
-void launch_attn_combine(ActType at, const Plan& p, int R, int Hq, const float* part_acc, const float* part_ml,
-                         void* ctx, cudaStream_t s) {
-  FMD_DISPATCH(at, k_attn_combine<T><<<R, 256, 0, s>>>(p, Hq, part_acc, part_ml, (T*)ctx));
 }
 
 void launch_attn_prefill(ActType at, const Plan& p, int PB, int Hq, int Hkv, const void* q, const KvView& kv,

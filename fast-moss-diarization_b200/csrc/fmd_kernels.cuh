@@ -119,10 +119,6 @@ void launch_linear(ActType at, const LinW& W, const void* x, int ldx, const int*
 void launch_qkv_epilogue(ActType at, const Plan& p, int R, const float* part, int split, size_t split_stride,
                          int Hq, int Hkv, const void* qn_w, const void* kn_w, const void* cos, const void* sin,
                          void* q_out, const KvView& kv, int layer, float eps, cudaStream_t s);
-void launch_attn_decode(ActType at, const Plan& p, int grid_items, int Hq, int Hkv, const void* q, const KvView& kv,
-                        int layer, float scale, float* part_acc, float* part_ml, cudaStream_t s);
-void launch_attn_combine(ActType at, const Plan& p, int R, int Hq, const float* part_acc, const float* part_ml,
-                         void* ctx, cudaStream_t s);
 void launch_attn_prefill(ActType at, const Plan& p, int PB, int Hq, int Hkv, const void* q, const KvView& kv,
                          int layer, float scale, void* ctx, cudaStream_t s);
 void launch_residual_norm(ActType at, const int* n_rows_ptr, int R, void* x, const float* part, int split,
@@ -132,5 +128,14 @@ void launch_silu_mul(ActType at, const int* n_rows_ptr, int R, const float* part
 void launch_logits_argmax(ActType at, const int* n_sample_ptr, int B, const float* part, int V, float* logits,
                           int* next_ids, cudaStream_t s);
 void launch_dequant(ActType at, const LinW& W, float* out, cudaStream_t s);
+
+// fmd_attn_decode.cu: TMA-fed decode attention with the split-KV merge fused in.
+// `tmap` points at a CUtensorMap over the KV pool viewed as 2D
+// [layers*pages*2*kv_heads*64 rows][128 dims], box 64x64, 128B swizzle.
+size_t attn_decode_smem_bytes();
+cudaError_t init_attn_decode();
+void launch_attn_decode_tma(ActType at, const void* tmap, const Plan& p, int grid, int Hq, int Hkv, const void* q,
+                            const KvView& kv, int layer, float scale, float* part_acc, float* part_ml, int* counters,
+                            void* ctx, int* status, cudaStream_t s);
 
 }  // namespace fmd

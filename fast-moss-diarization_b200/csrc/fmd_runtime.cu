@@ -2,6 +2,8 @@
 // quantiser of linear.rs:194-202), paged KV pool, per-pass plans, the forward
 // pass, the continuous-batching engine loop with CUDA-graph replay, and the
 // extern "C" entry points declared in include/fmd_decoder.h.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -119,6 +121,9 @@ struct fmd_handle {
   int max_slots = 0, max_rows = 0, n_pages = 0, max_pages_per_slot = 0;
   int pb_max = 0, di_max = 0, di_grid = 0, pb_grid = 0;
   KvView kv{};
+  alignas(64) CUtensorMap kv_tmap;  // the KV pool as [rows][128] for TMA tile loads
+  int* attn_counters = nullptr;     // [max_slots][kv_heads] split-KV merge counters
+  int* d_status = nullptr;          // device-side error status (bounded waits)
   int* d_page_table = nullptr;
   std::vector<int> h_page_table;
   std::vector<int> free_pages;           // host allocator (operator mode)
@@ -341,12 +346,10 @@ void run_forward(fmd_handle* h, float* logits_dev, const void* arena) {
                         h->rope_cos, h->rope_sin, h->qbuf, h->kv, l, eps, s);
     trace(h, "qkv_epi", l);
     if (h->record_attn_events) cudaEventRecordWithFlags(h->attn_events[2 * l], s, cudaEventRecordExternal);
-    launch_attn_decode(h->at, h->plan, h->di_grid, h->Hq(), h->Hkv(), h->qbuf, h->kv, l, h->attn_scale, h->pacc,
-                       h->pml, s);
+    launch_attn_decode_tma(h->at, &h->kv_tmap, h->plan, h->di_grid, h->Hq(), h->Hkv(), h->qbuf, h->kv, l,
+                           h->attn_scale, h->pacc, h->pml, h->attn_counters, h->ctx, h->d_status, s);
     if (h->record_attn_events) cudaEventRecordWithFlags(h->attn_events[2 * l + 1], s, cudaEventRecordExternal);
     trace(h, "attn_decode", l);
-    launch_attn_combine(h->at, h->plan, std::min(h->max_slots, 296), h->Hq(), h->pacc, h->pml, h->ctx, s);
-    trace(h, "attn_combine", l);
     launch_attn_prefill(h->at, h->plan, h->pb_grid, h->Hq(), h->Hkv(), h->qbuf, h->kv, l, h->attn_scale, h->ctx, s);
     trace(h, "attn_prefill", l);
     launch_linear(h->at, L.o, h->ctx, h->Hq() * kHeadDim, nullptr, nrows, R, h->part, ss, s);
@@ -445,6 +448,15 @@ int sync_check(fmd_handle* h) {
   if (e != cudaSuccess) return fail(h, FMD_EIO, std::string("device error: ") + cudaGetErrorString(e));
   e = cudaGetLastError();
   if (e != cudaSuccess) return fail(h, FMD_EIO, std::string("launch error: ") + cudaGetErrorString(e));
+  if (h->d_status) {
+    int st = 0;
+    e = cudaMemcpy(&st, h->d_status, sizeof(int), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return fail(h, FMD_EIO, std::string("status read: ") + cudaGetErrorString(e));
+    if (st != 0) {
+      cudaMemset(h->d_status, 0, sizeof(int));
+      return fail(h, st, "a bounded device-side wait gave up (status " + std::to_string(st) + ")");
+    }
+  }
   return FMD_OK;
 }
 
@@ -546,7 +558,7 @@ int fmd_create(const fmd_config* cfg, int32_t precision, int32_t device, fmd_han
   h->device = device;
   h->attn_scale = (float)(1.0 / std::sqrt((double)cfg->head_dim));
   if (cudaSetDevice(device) != cudaSuccess || cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking) != cudaSuccess ||
-      init_kernels() != cudaSuccess) {
+      init_kernels() != cudaSuccess || init_attn_decode() != cudaSuccess) {
     cudaGetLastError();
     delete h;
     return FMD_EIO;
@@ -672,6 +684,24 @@ int fmd_kv_reserve(fmd_handle* h, int32_t max_slots, int64_t max_tokens_total, i
   h->kv.n_pages = h->n_pages;
   h->kv.max_pages_per_slot = h->max_pages_per_slot;
   h->kv.kv_heads = c.num_key_value_heads;
+  {
+    const uint64_t rows = (uint64_t)c.num_hidden_layers * h->n_pages * 2 * c.num_key_value_heads * kPageTokens;
+    if (rows > (uint64_t)INT32_MAX) return fail(h, FMD_ENOTSUP, "KV pool too large for 32-bit TMA row coordinates");
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult qr;
+    CK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &qr));
+    if (fn == nullptr || qr != cudaDriverEntryPointSuccess)
+      return fail(h, FMD_EIO, "cuTensorMapEncodeTiled is unavailable in this driver");
+    auto encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    const cuuint64_t dims[2] = {(cuuint64_t)kHeadDim, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)kHeadDim * 2};
+    const cuuint32_t box[2] = {64, (cuuint32_t)kPageTokens};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult cr = encode(&h->kv_tmap, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, kvp, dims, strides, box, estr,
+                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (cr != CUDA_SUCCESS) return fail(h, FMD_EIO, "cuTensorMapEncodeTiled failed: " + std::to_string((int)cr));
+  }
   void* pt;
   if ((rc = dev_alloc(h, (size_t)max_slots * h->max_pages_per_slot * 4, &pt, &h->work_bytes))) return rc;
   CK(cudaMemset(pt, 0, (size_t)max_slots * h->max_pages_per_slot * 4));
@@ -716,6 +746,12 @@ int fmd_kv_reserve(fmd_handle* h, int32_t max_slots, int64_t max_tokens_total, i
   h->logits = (float*)p;
   if ((rc = A((size_t)max_slots * 4, &p))) return rc;
   h->next_ids = (int*)p;
+  if ((rc = A((size_t)max_slots * c.num_key_value_heads * 4, &p))) return rc;
+  CK(cudaMemset(p, 0, (size_t)max_slots * c.num_key_value_heads * 4));
+  h->attn_counters = (int*)p;
+  if ((rc = A(sizeof(int), &p))) return rc;
+  CK(cudaMemset(p, 0, sizeof(int)));
+  h->d_status = (int*)p;
   h->layout.init(R, max_slots, h->pb_max, h->di_max);
   if ((rc = A(h->layout.total * 4, &p))) return rc;
   CK(cudaMemset(p, 0, h->layout.total * 4));
