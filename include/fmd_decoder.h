@@ -246,6 +246,30 @@ int fmd_debug_weight(fmd_handle* h, int32_t layer, int32_t which, float* out, in
 int fmd_debug_kv(fmd_handle* h, int32_t slot, int32_t layer, int32_t pos, int32_t n, void* k_out,
                  void* v_out);
 
+/* ---- greedy pick without allocation -------------------------------------- */
+
+/* No counterpart in the reference. Greedy ids (per-row argmax, lowest index
+ * among equal maxima) of `n_rows` x `vocab` f32 logits that the caller already
+ * holds on the current device, written to the caller's device buffer
+ * `next_ids` on `stream` (a cudaStream_t; NULL = legacy default stream). No
+ * handle, no synchronisation.
+ *
+ * Who it is for: callers that can't let a library call cudaMalloc or cudaFree,
+ * such as a host engine that sizes and owns every device byte itself, or code
+ * that must not stall behind the device synchronisation those calls can imply.
+ * This entry point allocates nothing. Its scratch is a fixed 128 KiB array
+ * compiled into the library, which every GPU that loads the library holds
+ * until the process exits.
+ *
+ * Limits: 1 <= n_rows <= 64 and 1 <= vocab <= 1048576; larger sizes return
+ * FMD_EINVAL without launching anything. The first call on each device looks
+ * up the scratch's device address with that device current, so make that
+ * first call before any stream capture on that device. All calls share the
+ * one scratch array, which keeps the last call's contents. Each call writes
+ * every entry it reads, so nothing needs clearing, but calls whose kernels
+ * overlap on the GPU (different streams or host threads) race. */
+int fmd_greedy_pick_noalloc(const float* logits, int32_t n_rows, int32_t vocab, int32_t* next_ids, void* stream);
+
 /* Host-side GGML Q8_0 quantiser (the `QTensor::quantize` step of
  * linear.rs:197): rows x cols f32 -> rows x cols/32 34-byte blocks. */
 int fmd_q8_0_quantize(const float* src, int64_t rows, int64_t cols, void* blocks);
