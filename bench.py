@@ -49,7 +49,10 @@ METRIC = "decoded tokens/s per GPU (Q8_0, bf16) and % of HBM roofline; audio s/s
 UNIT = "tokens/s"
 PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
 TRAFFIC_FILE = ROOT / "profiles" / "attn_decode_config3.md"
-KERNELS_PER_STEP = lambda layers: 1 + 1 + 11 * layers + 2  # noqa: E731  scheduler, embed, per layer, head
+# kernels per engine step: scheduler + embed + per layer + lm_head/greedy; a step
+# that may carry prefill rows runs 11 kernels per layer, a decode-only step 7
+KERNELS_MIXED = lambda layers: 1 + 1 + 11 * layers + 2  # noqa: E731
+KERNELS_DECODE = lambda layers: 1 + 1 + 7 * layers + 2  # noqa: E731
 
 
 def parse_args():
@@ -295,6 +298,7 @@ def main():
     tokens = sum(s.window_tokens for s in wins)
     dev_ms = sum(s.window_device_ms for s in wins)
     steps_run = sum(s.window_steps for s in wins)
+    mixed_run = sum(s.window_mixed_steps for s in wins)
     tot_tokens = dist.reduce(float(tokens), "sum")
     max_ms = dist.reduce(dev_ms, "max")
     value = tot_tokens / (max_ms / 1000.0) if max_ms > 0 else 0.0
@@ -366,7 +370,9 @@ def main():
             "clocks": clk,
             "e2e": e2e,
             "cpu_baseline": cpu,
-            "gpu_launches": int(steps_run * KERNELS_PER_STEP(cfg.num_hidden_layers) + len(wins)),
+            "gpu_launches": int(mixed_run * KERNELS_MIXED(cfg.num_hidden_layers)
+                                + (steps_run - mixed_run) * KERNELS_DECODE(cfg.num_hidden_layers) + len(wins)),
+            "mixed_steps_timed": int(mixed_run),
             "tokens_timed": int(tot_tokens),
         }
         print(json.dumps(line), flush=True)

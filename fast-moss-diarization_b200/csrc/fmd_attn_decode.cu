@@ -63,6 +63,8 @@ __global__ void __launch_bounds__(160, 2)
   uint64_t* empty = full + kStages;
   __shared__ int s_last;
 
+  griddep_launch();
+  griddep_wait();
   const int n_work = p.counts->n_ditems * Hkv;
   if ((int)blockIdx.x >= n_work) return;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
@@ -293,11 +295,11 @@ void launch_attn_decode_tma(ActType at, const void* tmap, const Plan& p, int gri
   const CUtensorMap& m = *reinterpret_cast<const CUtensorMap*>(tmap);
   const size_t smem = attn_decode_smem_bytes();
   if (at == kBF16)
-    k_attn_decode_tma<__nv_bfloat16><<<grid, 160, smem, s>>>(m, p, Hq, Hkv, (const __nv_bfloat16*)q, kv, layer,
+    launch_pdl(k_attn_decode_tma<__nv_bfloat16>, dim3(grid), dim3(160), smem, s, m, p, Hq, Hkv, (const __nv_bfloat16*)q, kv, layer,
                                                              scale_log2, part_acc, part_ml, counters,
                                                              (__nv_bfloat16*)ctx, status);
   else
-    k_attn_decode_tma<__half><<<grid, 160, smem, s>>>(m, p, Hq, Hkv, (const __half*)q, kv, layer, scale_log2,
+    launch_pdl(k_attn_decode_tma<__half>, dim3(grid), dim3(160), smem, s, m, p, Hq, Hkv, (const __half*)q, kv, layer, scale_log2,
                                                       part_acc, part_ml, counters, (__half*)ctx, status);
 }
 

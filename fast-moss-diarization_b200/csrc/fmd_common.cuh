@@ -107,6 +107,15 @@ FMD_DEV int4 ld_stream16(const void* p) {
 // f16 bits -> f32 (exact).
 FMD_DEV float h2f_bits(uint16_t b) { return __half2float(__ushort_as_half(b)); }
 
+// Programmatic dependent launch: every kernel of a step lets the next one be
+// scheduled as soon as it starts (griddep_launch), and touches data written
+// by earlier kernels only after griddep_wait, which returns once the
+// preceding grid has completed and its writes are visible. Work that reads
+// nothing from earlier kernels (weight prefetch, barrier set-up) goes before
+// the wait. Both are no-ops for a kernel launched without the attribute.
+FMD_DEV void griddep_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+FMD_DEV void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
+
 }  // namespace fmd
 
 // ---- mbarrier + TMA (sm_90+/sm_100a) ------------------------------------------------

@@ -1,0 +1,868 @@
+// Decode-step projections: split-K GEMV with the K split reduced inside a
+// thread-block cluster, and every epilogue and norm fused.
+//
+// A decode step multiplies ~32 token rows by each projection of a layer
+// (crates/fmd-core/src/model/linear.rs:29-65; FusedLinear :85-95). The weights
+// are read once per step, so the kernels are weight-streaming GEMVs whose
+// cost is latency: this file removes the extra kernels a split-K needs.
+//
+//  * grid (N/FT feature tiles, S k-splits, row tiles); the S CTAs of one
+//    feature tile form a cluster (S <= 8). Each computes a partial
+//    FT x rows tile for its 1/S of K on mma.sync (weights Q8_0 dequantised in
+//    registers, or dense), keeps it in its shared memory, and after
+//    cluster.sync() CTA rank r sums the S partials of rows r, r+S, ... over
+//    distributed shared memory and applies the epilogue to them. No global
+//    partials, no atomics, a fixed summation order.
+//  * each CTA's whole weight slice (FT rows x K/S, 8-74 KB) is requested at
+//    kernel start with one TMA bulk copy per row into padded shared-memory
+//    rows, before griddepcontrol.wait, so the weight stream overlaps the
+//    previous kernel (programmatic dependent launch) and every byte a CTA
+//    needs is in flight at once; the Q8_0 scales go to registers meanwhile.
+//  * RMSNorm (linear.rs:293-302) is folded into the consumer: the epilogue
+//    that updates the residual stream also writes, per row, the sum of squares
+//    of its FT features (ssq[row][tile]); the next projection turns the row's
+//    partial sums into rsqrt(mean + eps) and normalises its activation tile as
+//    it lands in shared memory (xn = rnd(x * rs * w), as the reference does).
+//
+// Epilogues (the reference's rounding points):
+//  * kGemvQkv    FT = 128 = one head: RMSNorm of q/k per head, RoPE at the
+//                row's position, q -> q buffer, k/v -> paged KV cache
+//                (qwen3.rs:213-227);
+//  * kGemvResid  x <- rnd(x + rnd(y)) and ssq of the new x (qwen3.rs:333-338);
+//  * kGemvSwiglu gate/up rows interleaved in 32-row groups at load, so a
+//                64-row tile holds 32 matching gate and up features:
+//                h = rnd(rnd(silu(rnd(g))) * rnd(u)) (qwen3.rs:288-292);
+//  * kGemvLogits FT = 128, S = 2: rounded logits (qwen3.rs:459-463),
+//                optionally stored as f32, and the tile's (max, lowest index)
+//                per row.
+#include <cooperative_groups.h>
+#include <cstring>
+#include <float.h>
+#include <math.h>
+
+#include "fmd_kernels.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace fmd {
+
+namespace {
+
+constexpr int kRows = 64;   // rows per row tile (decode steps carry one row per sequence)
+constexpr int kMaxKb = 16;  // 64-wide k-blocks per CTA (K / S <= 1024)
+constexpr uint32_t kWaitLimit = 1u << 22;
+constexpr int kStatusTimeout = -110;
+
+// Decode-packed weights. Each CTA's slice (FT features x K/S) is one
+// contiguous tile in HBM, ordered [k-block][warp][fragment] so that a k-block
+// is one TMA bulk copy and a warp's fragment reads are 512 consecutive bytes
+// (conflict-free, no padding). One (k-block, warp) unit covers 16 features x
+// 64 k; lane (g, t) owns k [16t, 16t + 16) of features g and g + 8:
+//  * Q8_0: [0, 512) lane-major 16 bytes of feature g, [512, 1024) feature
+//    g + 8, [1024, 1088) the f16 scales of the unit's 16 features x 2 blocks
+//    (feature-major), so the scales travel with the quants;
+//  * 16-bit: four 512-byte planes: feature g k 0-7 | 8-15, g + 8 k 0-7 | 8-15.
+constexpr int kUnitQ8 = 1088;
+constexpr int kUnitDense = 2048;
+
+struct WRegs {
+  int4 a, b, c, d;
+  float da, db;
+};
+
+// A fragments of the 4 MMAs of one 64-wide k-block (see the k permutation in
+// the header of fmd_kernels.cu's k_linear): thread (g, t) holds weights
+// [16t, 16t+16) of rows f0 and f0+8.
+template <typename T, bool Q8>
+FMD_DEV void gemv_afrag(const WRegs& w, uint32_t (&af)[4][4]) {
+  if constexpr (Q8) {
+    const uint32_t* ua = reinterpret_cast<const uint32_t*>(&w.a);
+    const uint32_t* ub = reinterpret_cast<const uint32_t*>(&w.b);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float e[4], f[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        e[i] = (__int_as_float(__byte_perm(ua[j] ^ 0x80808080u, 0x4B000000u, 0x7440u | i)) - 8388736.f) * w.da;
+        f[i] = (__int_as_float(__byte_perm(ub[j] ^ 0x80808080u, 0x4B000000u, 0x7440u | i)) - 8388736.f) * w.db;
+      }
+      af[j][0] = Act<T>::pack2(e[0], e[1]);
+      af[j][1] = Act<T>::pack2(f[0], f[1]);
+      af[j][2] = Act<T>::pack2(e[2], e[3]);
+      af[j][3] = Act<T>::pack2(f[2], f[3]);
+    }
+  } else {
+    const uint32_t* ua = reinterpret_cast<const uint32_t*>(&w.a);
+    const uint32_t* ub = reinterpret_cast<const uint32_t*>(&w.b);
+    const uint32_t* uc = reinterpret_cast<const uint32_t*>(&w.c);
+    const uint32_t* ud = reinterpret_cast<const uint32_t*>(&w.d);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t* r0 = j < 2 ? ua : ub;
+      const uint32_t* r1 = j < 2 ? uc : ud;
+      af[j][0] = r0[(2 * j) & 3];
+      af[j][2] = r0[(2 * j + 1) & 3];
+      af[j][1] = r1[(2 * j) & 3];
+      af[j][3] = r1[(2 * j + 1) & 3];
+    }
+  }
+}
+
+template <typename T, bool Q8, int FW, int EPI, bool NORM>
+__global__ void __launch_bounds__(FW * 32) k_gemv(const T* __restrict__ x, int ldx, const int* __restrict__ row_map,
+                                                 const int* __restrict__ n_rows_ptr, LinW W, GemvEpi ep, int xrows,
+                                                 int* __restrict__ status) {
+  constexpr int NT = FW * 32;
+  constexpr int FT = FW * 16;
+  constexpr int UNIT = Q8 ? kUnitQ8 : kUnitDense;
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ __align__(8) uint64_t wbar[kMaxKb];
+  __shared__ float rs_s[kRows];
+  griddep_launch();
+
+  const int S = gridDim.y, rank = blockIdx.y;
+  const int K = W.K;
+  const int klen = K / S, kbeg = rank * klen, nkb = klen >> 6;
+  const uint32_t kb_bytes = FW * UNIT;  // one k-block of the tile
+  uint8_t* wsm = smem;                  // the CTA's weight tile
+  T* xs = reinterpret_cast<T*>(smem + ((nkb * kb_bytes + 127) & ~127u));  // [xrows][klen + 8]
+  const int xstride = klen + 8;
+  float* part = reinterpret_cast<float*>(xs);  // after the k-loop: [xrows][FT + 4]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int fl = warp * 16 + g;  // local feature row of this thread (and fl + 8)
+
+  // ---- the whole weight tile is in flight before the dependency wait: one
+  // TMA bulk copy per k-block, each on its own mbarrier so compute can start
+  // on the first k-block while the rest land
+  if (threadIdx.x == 0) {
+    const uint8_t* src = W.pk + (size_t)(blockIdx.x * S + rank) * nkb * kb_bytes;
+    for (int kb = 0; kb < nkb; ++kb) mbar_init(&wbar[kb], 1);
+    fence_barrier_init();
+    for (int kb = 0; kb < nkb; ++kb) {
+      mbar_arrive_expect_tx(&wbar[kb], kb_bytes);
+      bulk_load(wsm + kb * kb_bytes, src + (size_t)kb * kb_bytes, kb_bytes, &wbar[kb]);
+    }
+  }
+  griddep_wait();
+
+  const int n_rows = *n_rows_ptr;
+  const int row0 = blockIdx.z * kRows;
+  const int rows = max(0, min(min(kRows, xrows), n_rows - row0));
+  const int n_tiles = (rows + 7) >> 3;
+
+  if (rows > 0) {
+    // activation tile rows x klen (rows of a partial n-tile zero-filled)
+    const int cpr = klen >> 3;  // 16-byte chunks per row
+    for (int c = threadIdx.x; c < n_tiles * 8 * cpr; c += NT) {
+      const int r = c / cpr, ch = c - r * cpr;
+      const T* src = x;
+      int bytes = 0;
+      if (r < rows) {
+        src = x + (size_t)(row_map ? row_map[row0 + r] : row0 + r) * ldx + kbeg + ch * 8;
+        bytes = 16;
+      }
+      cp_async16(xs + (size_t)r * xstride + ch * 8, src, bytes);
+    }
+    cp_async_commit();
+    if constexpr (NORM) {
+      // rsqrt(mean(x^2) + eps) of each row from the per-tile sums of squares,
+      // read while the activation tile is in flight
+      for (int r = threadIdx.x; r < rows; r += NT) {
+        const int gr = row_map ? row_map[row0 + r] : row0 + r;
+        const float* sp = ep.ssq + (size_t)gr * ep.ssq_tiles;
+        float ss = 0.f;
+        for (int i = 0; i < ep.ssq_tiles; ++i) ss += sp[i];
+        rs_s[r] = rsqrtf(ss / K + ep.eps);
+      }
+    }
+    cp_async_wait<0>();
+    if constexpr (NORM) {
+      __syncthreads();  // rs_s
+      const T* nw = reinterpret_cast<const T*>(ep.norm_w) + kbeg;
+      for (int c = threadIdx.x; c < rows * cpr; c += NT) {
+        const int r = c / cpr, ch = c - r * cpr;
+        int4* p = reinterpret_cast<int4*>(xs + (size_t)r * xstride + ch * 8);
+        int4 v = *p;
+        const int4 wv = *reinterpret_cast<const int4*>(nw + ch * 8);
+        uint32_t* u = reinterpret_cast<uint32_t*>(&v);
+        const uint32_t* uw = reinterpret_cast<const uint32_t*>(&wv);
+        const float rsr = rs_s[r];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = Act<T>::unpack2(u[j]);
+          const float2 gw = Act<T>::unpack2(uw[j]);
+          u[j] = Act<T>::pack2(f.x * rsr * gw.x, f.y * rsr * gw.y);
+        }
+        *p = v;
+      }
+    }
+  }
+  __syncthreads();  // barrier inits (and rs_s) visible to all threads
+  if (rows == 0) {
+    // a whole cluster shares blockIdx.z, so it leaves together, but only
+    // after its copies into shared memory have landed
+    bool ok = true;
+    for (int kb = 0; kb < nkb; ++kb) ok &= mbar_wait_bounded(&wbar[kb], 0, kWaitLimit);
+    if (!ok) atomicExch(status, kStatusTimeout);
+    return;
+  }
+
+  float acc[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+  bool ok = true;
+  // not unrolled: the k-loop body is ~100 instructions, and a decode layer
+  // cycles through four GEMV variants, so code size shows up as i-cache misses
+#pragma unroll 1
+  for (int kb = 0; kb < nkb; ++kb) {
+    {
+      const bool landed = mbar_wait_bounded(&wbar[kb], 0, kWaitLimit);
+      ok &= landed;
+      if (landed) {
+        const uint8_t* u = wsm + kb * kb_bytes + warp * UNIT;
+        WRegs w;
+        w.a = *reinterpret_cast<const int4*>(u + lane * 16);
+        w.b = *reinterpret_cast<const int4*>(u + 512 + lane * 16);
+        if constexpr (Q8) {
+          const uint16_t* sc = reinterpret_cast<const uint16_t*>(u + 1024);
+          w.da = h2f_bits(sc[g * 2 + (t >> 1)]);
+          w.db = h2f_bits(sc[(g + 8) * 2 + (t >> 1)]);
+        } else {
+          w.c = *reinterpret_cast<const int4*>(u + 1024 + lane * 16);
+          w.d = *reinterpret_cast<const int4*>(u + 1536 + lane * 16);
+        }
+        uint32_t af[4][4];
+        gemv_afrag<T, Q8>(w, af);
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt) {
+          if (nt < n_tiles) {
+            const T* xr = xs + (size_t)(nt * 8 + g) * xstride + kb * 64 + 16 * t;
+            const int4 x0 = *reinterpret_cast<const int4*>(xr);
+            const int4 x1 = *reinterpret_cast<const int4*>(xr + 8);
+            const uint32_t xw[8] = {(uint32_t)x0.x, (uint32_t)x0.y, (uint32_t)x0.z, (uint32_t)x0.w,
+                                    (uint32_t)x1.x, (uint32_t)x1.y, (uint32_t)x1.z, (uint32_t)x1.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) mma16816<T>(acc[nt], af[j], xw[2 * j], xw[2 * j + 1]);
+          }
+        }
+      }
+    }
+  }
+  if (!ok) atomicExch(status, kStatusTimeout);
+  __syncthreads();  // the activation tile is dead: `part` reuses it
+
+  // ---- partial tile -> shared memory; the cluster sums it
+  constexpr int PS = FT + 4;  // part row stride (floats)
+#pragma unroll
+  for (int nt = 0; nt < 8; ++nt) {
+    if (nt < n_tiles) {
+      const int lr = nt * 8 + 2 * t;
+      part[lr * PS + fl] = acc[nt][0];
+      part[(lr + 1) * PS + fl] = acc[nt][1];
+      part[lr * PS + fl + 8] = acc[nt][2];
+      part[(lr + 1) * PS + fl + 8] = acc[nt][3];
+    }
+  }
+  cg::cluster_group cluster = cg::this_cluster();
+  cluster.sync();
+
+  // rank r owns rows r, r+S, ...; one warp per row, features across lanes
+  constexpr int FPL = FT / 32;  // features per lane (2 or 4)
+  for (int lr = rank + warp * S; lr < rows; lr += FW * S) {
+    float v[FPL];
+#pragma unroll
+    for (int i = 0; i < FPL; ++i) v[i] = 0.f;
+    for (int s = 0; s < S; ++s) {
+      const float* peer = cluster.map_shared_rank(part + lr * PS, s);
+#pragma unroll
+      for (int i = 0; i < FPL; ++i) v[i] += peer[lane * FPL + i];
+    }
+    const int r = row0 + lr;
+#pragma unroll
+    for (int i = 0; i < FPL; ++i) v[i] = rnd<T>(v[i]);
+
+    if constexpr (EPI == kGemvResid) {
+      T* xr = reinterpret_cast<T*>(ep.x) + (size_t)r * W.N + blockIdx.x * FT + lane * FPL;
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < FPL; ++i) {
+        const float nx = rnd<T>(Act<T>::to_f(xr[i]) + v[i]);
+        xr[i] = Act<T>::from_f(nx);
+        ss += nx * nx;
+      }
+      ss = warp_sum(ss);
+      if (lane == 0) ep.ssq_out[(size_t)r * ep.ssq_tiles + blockIdx.x] = ss;
+    } else if constexpr (EPI == kGemvSwiglu) {
+      // FT = 64: features [0, 32) gate, [32, 64) up of intermediate index
+      // tile*32 + j; lane l holds features 2l, 2l+1
+      const float g0 = __shfl_sync(0xffffffffu, v[0], lane >> 1), g1 = __shfl_sync(0xffffffffu, v[1], lane >> 1);
+      const float u0 = __shfl_sync(0xffffffffu, v[0], 16 + (lane >> 1));
+      const float u1 = __shfl_sync(0xffffffffu, v[1], 16 + (lane >> 1));
+      const float gv = (lane & 1) ? g1 : g0, uv = (lane & 1) ? u1 : u0;
+      const float sg = rnd<T>(gv / (1.f + expf(-gv)));
+      reinterpret_cast<T*>(ep.h)[(size_t)r * ep.I + blockIdx.x * 32 + lane] = Act<T>::from_f(sg * uv);
+    } else if constexpr (EPI == kGemvQkv) {
+      // FT = 128: one head; lane holds dims 4*lane .. 4*lane+3
+      const int hh = blockIdx.x, Hq = ep.Hq, Hkv = ep.Hkv;
+      const int pos = ep.plan.row_pos[r], slot = ep.plan.row_slot[r];
+      T* kvb = reinterpret_cast<T*>(ep.kv.base);
+      T* dst;
+      if (hh < Hq + Hkv) {
+        const T* nw = reinterpret_cast<const T*>(hh < Hq ? ep.qn_w : ep.kn_w);
+        const float ss = warp_sum(v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3]);
+        const float inv = rsqrtf(ss / kHeadDim + ep.eps);
+        float y[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) y[i] = rnd<T>(v[i] * inv * Act<T>::to_f(nw[lane * 4 + i]));
+        const T* cos_t = reinterpret_cast<const T*>(ep.cos);
+        const T* sin_t = reinterpret_cast<const T*>(ep.sin);
+        const int dd = (lane & 15) * 4;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float pr = __shfl_xor_sync(0xffffffffu, y[i], 16);
+          const float cs = Act<T>::to_f(cos_t[(size_t)pos * (kHeadDim / 2) + dd + i]);
+          const float sn = Act<T>::to_f(sin_t[(size_t)pos * (kHeadDim / 2) + dd + i]);
+          v[i] = lane < 16 ? y[i] * cs - pr * sn : pr * sn + y[i] * cs;
+        }
+        if (hh < Hq) {
+          dst = reinterpret_cast<T*>(ep.q_out) + (size_t)r * Hq * kHeadDim + hh * kHeadDim;
+        } else {
+          const int page = ep.kv.page_table[(size_t)slot * ep.kv.max_pages_per_slot + pos / kPageTokens];
+          dst = kvb + ep.kv.elem_offset(ep.layer, page, 0, hh - Hq) + (size_t)(pos % kPageTokens) * kHeadDim;
+        }
+      } else {
+        const int page = ep.kv.page_table[(size_t)slot * ep.kv.max_pages_per_slot + pos / kPageTokens];
+        dst = kvb + ep.kv.elem_offset(ep.layer, page, 1, hh - Hq - Hkv) + (size_t)(pos % kPageTokens) * kHeadDim;
+      }
+      uint2 o;
+      o.x = Act<T>::pack2(v[0], v[1]);
+      o.y = Act<T>::pack2(v[2], v[3]);
+      *reinterpret_cast<uint2*>(dst + lane * 4) = o;
+    } else {  // kGemvLogits: rounded logits and the tile's best per row
+      const int fb = blockIdx.x * FT + lane * FPL;
+      if (ep.logits) {
+#pragma unroll
+        for (int i = 0; i < FPL; ++i) ep.logits[(size_t)r * W.N + fb + i] = v[i];
+      }
+      float best = v[0];
+      int bi = fb;
+#pragma unroll
+      for (int i = 1; i < FPL; ++i)
+        if (v[i] > best) {
+          best = v[i];
+          bi = fb + i;
+        }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > best || (ov == best && oi < bi)) {
+          best = ov;
+          bi = oi;
+        }
+      }
+      if (lane == 0) {
+        ep.best_val[(size_t)r * gridDim.x + blockIdx.x] = best;
+        ep.best_idx[(size_t)r * gridDim.x + blockIdx.x] = bi;
+      }
+    }
+  }
+  cluster.sync();  // peers may still be reading this CTA's partial tile
+}
+
+// lm_head + greedy candidates as one persistent kernel (qwen3.rs:459-463,
+// engine.rs:550-559). The vocabulary projection is the largest weight of a
+// decode step (vocab x hidden) and the only one with more 128-feature tiles
+// than there are SMs, so here one CTA per SM keeps the normalised activation
+// tile resident and streams its share of tiles through a ring of TMA bulk
+// copies (one stage = one 64-wide k-block of a tile, 8.5 KB for Q8_0):
+//  * warp 8 (one lane) is the producer; warps 0-7 consume, each owning 16
+//    features of the 128-feature tile, and release a stage by arriving on its
+//    "empty" barrier. Every wait is bounded; a timeout stops the ring, sets
+//    the status word and drains the copies still in flight.
+//  * the tile order of the packed lm_head ([tile][k-split][k-block][warp]) is
+//    the full-K k-block order of each tile, so the ring walks it linearly.
+//  * each CTA keeps, per row, the best (rounded logit, lowest index) over its
+//    tiles and writes one candidate per (row, CTA); k_pick_reduce finishes.
+constexpr int kHeadWarps = 8;            // consumer warps: 128 features per tile
+constexpr int kHeadMaxStages = 16;
+constexpr int kHeadSmemBudget = 220 * 1024;
+
+template <typename T, bool Q8>
+__global__ void __launch_bounds__((kHeadWarps + 1) * 32) k_lm_head(const T* __restrict__ x, int ldx,
+                                                                  const int* __restrict__ row_map,
+                                                                  const int* __restrict__ n_rows_ptr, LinW W,
+                                                                  GemvEpi ep, int xrows, int stages,
+                                                                  int* __restrict__ status) {
+  constexpr int UNIT = Q8 ? kUnitQ8 : kUnitDense;
+  constexpr uint32_t kStage = kHeadWarps * UNIT;
+  constexpr int FT = kHeadWarps * 16;
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ __align__(8) uint64_t full[kHeadMaxStages], empty[kHeadMaxStages];
+  __shared__ float rs_s[kRows];
+  __shared__ float cand_v[kHeadWarps][kRows];
+  __shared__ int cand_i[kHeadWarps][kRows];
+  __shared__ int abort_s;
+  griddep_launch();
+
+  const int K = W.K, nkb = K / 64;
+  const int n_tiles = W.N / FT;
+  const int my_tiles = n_tiles > (int)blockIdx.x ? (n_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  const int n_units = my_tiles * nkb;
+  uint8_t* ring = smem;
+  T* xs = reinterpret_cast<T*>(smem + (size_t)stages * kStage);  // [xrows][K + 8]
+  const int xstride = K + 8;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < stages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kHeadWarps);
+    }
+    abort_s = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  if (warp == kHeadWarps) {
+    // ---- producer: weights do not depend on the previous kernel, so the
+    // ring starts filling before griddepcontrol.wait
+    if (lane == 0) {
+      for (int u = 0; u < n_units; ++u) {
+        const int st = u % stages;
+        if (u >= stages && !mbar_wait_bounded(&empty[st], ((u / stages) + 1) & 1, kWaitLimit)) {
+          atomicExch(&abort_s, 1);
+          break;
+        }
+        if (*reinterpret_cast<volatile int*>(&abort_s)) break;
+        const int tile = blockIdx.x + (u / nkb) * gridDim.x, kb = u % nkb;
+        mbar_arrive_expect_tx(&full[st], kStage);
+        bulk_load(ring + (size_t)st * kStage, W.pk + ((size_t)tile * nkb + kb) * kStage, kStage, &full[st]);
+      }
+    }
+    griddep_wait();
+    return;  // nothing below touches the producer warp
+  }
+
+  // ---- consumers (256 threads): normalised activation tile, then the ring
+  griddep_wait();
+  const int n_rows = *n_rows_ptr;
+  const int row0 = blockIdx.y * kRows;
+  const int rows = max(0, min(min(kRows, xrows), n_rows - row0));
+  const int n_nt = (rows + 7) >> 3;
+  constexpr int NT = kHeadWarps * 32;
+  const int cpr = K >> 3;
+  for (int c = threadIdx.x; c < n_nt * 8 * cpr; c += NT) {
+    const int r = c / cpr, ch = c - r * cpr;
+    const T* src = x;
+    int bytes = 0;
+    if (r < rows) {
+      src = x + (size_t)(row_map ? row_map[row0 + r] : row0 + r) * ldx + ch * 8;
+      bytes = 16;
+    }
+    cp_async16(xs + (size_t)r * xstride + ch * 8, src, bytes);
+  }
+  cp_async_commit();
+  for (int r = threadIdx.x; r < rows; r += NT) {
+    const int gr = row_map ? row_map[row0 + r] : row0 + r;
+    const float* sp = ep.ssq + (size_t)gr * ep.ssq_tiles;
+    float ss = 0.f;
+    for (int i = 0; i < ep.ssq_tiles; ++i) ss += sp[i];
+    rs_s[r] = rsqrtf(ss / K + ep.eps);
+  }
+  cp_async_wait<0>();
+  named_sync(1, NT);
+  {
+    const T* nw = reinterpret_cast<const T*>(ep.norm_w);
+    for (int c = threadIdx.x; c < rows * cpr; c += NT) {
+      const int r = c / cpr, ch = c - r * cpr;
+      int4* p = reinterpret_cast<int4*>(xs + (size_t)r * xstride + ch * 8);
+      int4 v = *p;
+      const int4 wv = *reinterpret_cast<const int4*>(nw + ch * 8);
+      uint32_t* u = reinterpret_cast<uint32_t*>(&v);
+      const uint32_t* uw = reinterpret_cast<const uint32_t*>(&wv);
+      const float rsr = rs_s[r];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = Act<T>::unpack2(u[j]);
+        const float2 gw = Act<T>::unpack2(uw[j]);
+        u[j] = Act<T>::pack2(f.x * rsr * gw.x, f.y * rsr * gw.y);
+      }
+      *p = v;
+    }
+  }
+  named_sync(1, NT);
+
+  // running best of this thread's rows (nt * 8 + 2t + {0, 1}) over its features
+  float bv[8][2];
+  int bi[8][2];
+#pragma unroll
+  for (int nt = 0; nt < 8; ++nt) {
+    bv[nt][0] = bv[nt][1] = -INFINITY;
+    bi[nt][0] = bi[nt][1] = 0x7fffffff;
+  }
+  bool ok = true;
+  int u = 0;
+  if (rows == 0) {
+    // the producer started before the row count was known: release every
+    // stage so that no copy is left in flight when the CTA retires
+    for (; u < n_units; ++u) {
+      const int st = u % stages;
+      if (*reinterpret_cast<volatile int*>(&abort_s) || !mbar_wait_bounded(&full[st], (u / stages) & 1, kWaitLimit)) {
+        atomicExch(&abort_s, 1);
+        ok = false;
+        break;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);
+    }
+  }
+  for (int i = 0; i < my_tiles && ok && rows > 0; ++i) {
+    const int tile = blockIdx.x + i * gridDim.x;
+    float acc[8][4];
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+#pragma unroll 1
+    for (int kb = 0; kb < nkb; ++kb, ++u) {
+      const int st = u % stages;
+      if (*reinterpret_cast<volatile int*>(&abort_s) || !mbar_wait_bounded(&full[st], (u / stages) & 1, kWaitLimit)) {
+        atomicExch(&abort_s, 1);
+        ok = false;
+        break;
+      }
+      const uint8_t* un = ring + (size_t)st * kStage + warp * UNIT;
+      WRegs w;
+      w.a = *reinterpret_cast<const int4*>(un + lane * 16);
+      w.b = *reinterpret_cast<const int4*>(un + 512 + lane * 16);
+      if constexpr (Q8) {
+        const uint16_t* sc = reinterpret_cast<const uint16_t*>(un + 1024);
+        w.da = h2f_bits(sc[g * 2 + (t >> 1)]);
+        w.db = h2f_bits(sc[(g + 8) * 2 + (t >> 1)]);
+      } else {
+        w.c = *reinterpret_cast<const int4*>(un + 1024 + lane * 16);
+        w.d = *reinterpret_cast<const int4*>(un + 1536 + lane * 16);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);  // this warp's fragments are in registers
+      uint32_t af[4][4];
+      gemv_afrag<T, Q8>(w, af);
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        if (nt < n_nt) {
+          const T* xr = xs + (size_t)(nt * 8 + g) * xstride + kb * 64 + 16 * t;
+          const int4 x0 = *reinterpret_cast<const int4*>(xr);
+          const int4 x1 = *reinterpret_cast<const int4*>(xr + 8);
+          const uint32_t xw[8] = {(uint32_t)x0.x, (uint32_t)x0.y, (uint32_t)x0.z, (uint32_t)x0.w,
+                                  (uint32_t)x1.x, (uint32_t)x1.y, (uint32_t)x1.z, (uint32_t)x1.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) mma16816<T>(acc[nt], af[j], xw[2 * j], xw[2 * j + 1]);
+        }
+      }
+    }
+    if (!ok) break;
+    // rounded logits (the reference rounds lm_head output to the activation
+    // type) and the running best; features fl and fl + 8 of this tile
+    const int f0 = tile * FT + warp * 16 + g;
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+      if (nt < n_nt) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int lr = nt * 8 + 2 * t + h;
+          const float va = rnd<T>(acc[nt][h]), vb = rnd<T>(acc[nt][2 + h]);
+          if (ep.logits && lr < rows) {
+            float* lg = ep.logits + (size_t)(row0 + lr) * W.N;
+            lg[f0] = va;
+            lg[f0 + 8] = vb;
+          }
+          if (va > bv[nt][h] || (va == bv[nt][h] && f0 < bi[nt][h])) {
+            bv[nt][h] = va;
+            bi[nt][h] = f0;
+          }
+          if (vb > bv[nt][h] || (vb == bv[nt][h] && f0 + 8 < bi[nt][h])) {
+            bv[nt][h] = vb;
+            bi[nt][h] = f0 + 8;
+          }
+        }
+      }
+    }
+  }
+  if (!ok && threadIdx.x == 0) atomicExch(status, kStatusTimeout);
+
+  // ---- per-row best over this CTA's tiles: lanes of equal t, then warps
+#pragma unroll
+  for (int nt = 0; nt < 8; ++nt) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      float v = bv[nt][h];
+      int ix = bi[nt][h];
+#pragma unroll
+      for (int o = 4; o < 32; o <<= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, ix, o);
+        if (ov > v || (ov == v && oi < ix)) {
+          v = ov;
+          ix = oi;
+        }
+      }
+      if (g == 0) {
+        cand_v[warp][nt * 8 + 2 * t + h] = v;
+        cand_i[warp][nt * 8 + 2 * t + h] = ix;
+      }
+    }
+  }
+  named_sync(1, NT);
+  for (int r = threadIdx.x; r < rows; r += NT) {
+    float v = cand_v[0][r];
+    int ix = cand_i[0][r];
+    for (int w = 1; w < kHeadWarps; ++w)
+      if (cand_v[w][r] > v || (cand_v[w][r] == v && cand_i[w][r] < ix)) {
+        v = cand_v[w][r];
+        ix = cand_i[w][r];
+      }
+    ep.best_val[(size_t)(row0 + r) * gridDim.x + blockIdx.x] = v;
+    ep.best_idx[(size_t)(row0 + r) * gridDim.x + blockIdx.x] = ix;
+  }
+
+  // drain: a copy still in flight must land before the CTA's shared memory
+  // is released (only after an abort can one be outstanding here)
+  if (threadIdx.x == 0 && *reinterpret_cast<volatile int*>(&abort_s)) {
+    for (int st = 0; st < stages && st < n_units; ++st) {
+      // the last use of stage st is unit ulast; wait for its phase
+      const int ulast = st + ((n_units - 1 - st) / stages) * stages;
+      mbar_wait_bounded(&full[st], (ulast / stages) & 1, kWaitLimit);
+    }
+  }
+}
+
+// Greedy pick (engine.rs:550-559): max over the per-tile candidates of a row,
+// lowest vocabulary index among equal maxima.
+__global__ void __launch_bounds__(256) k_pick_reduce(const int* __restrict__ n_sample_ptr,
+                                                     const float* __restrict__ best_val,
+                                                     const int* __restrict__ best_idx, int n_parts,
+                                                     int* __restrict__ next_ids) {
+  __shared__ float sv[8];
+  __shared__ int si[8];
+  griddep_launch();
+  griddep_wait();
+  const int n = *n_sample_ptr;
+  for (int r = blockIdx.x; r < n; r += gridDim.x) {
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = threadIdx.x; i < n_parts; i += blockDim.x) {
+      const float v = best_val[(size_t)r * n_parts + i];
+      const int ix = best_idx[(size_t)r * n_parts + i];
+      if (v > best || (v == best && ix < bi)) {
+        best = v;
+        bi = ix;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > best || (ov == best && oi < bi)) {
+        best = ov;
+        bi = oi;
+      }
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) {
+      sv[warp] = best;
+      si[warp] = bi;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      for (int w = 1; w < 8; ++w)
+        if (sv[w] > best || (sv[w] == best && si[w] < bi)) {
+          best = sv[w];
+          bi = si[w];
+        }
+      next_ids[r] = bi;
+    }
+    __syncthreads();
+  }
+}
+
+size_t gemv_smem_bytes(int FT, bool q8, int klen, int xrows) {
+  const size_t w = ((size_t)(klen / 64) * (FT / 16) * (q8 ? kUnitQ8 : kUnitDense) + 127) & ~(size_t)127;
+  const size_t xb = (size_t)xrows * (klen + 8) * 2;
+  const size_t pb = (size_t)xrows * (FT + 4) * 4;
+  return w + (xb > pb ? xb : pb);
+}
+
+template <typename T, bool Q8, int FW, int EPI, bool NORM>
+void launch_gemv_t(const LinW& W, int S, const void* x, int ldx, const int* row_map, const int* n_rows_ptr,
+                   int max_rows, const GemvEpi& ep, int* status, cudaStream_t s) {
+  const int xrows = ((max_rows < kRows ? max_rows : kRows) + 7) & ~7;
+  const size_t smem = gemv_smem_bytes(FW * 16, Q8, W.K / S, xrows);
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = 1;
+  attr[1].val.clusterDim.y = S;
+  attr[1].val.clusterDim.z = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(W.N / (FW * 16), S, (max_rows + kRows - 1) / kRows);
+  cfg.blockDim = dim3(FW * 32);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  cudaLaunchKernelEx(&cfg, k_gemv<T, Q8, FW, EPI, NORM>, (const T*)x, ldx, row_map, n_rows_ptr, W, ep, xrows, status);
+}
+
+
+template <typename T, bool Q8>
+int launch_lm_head_t(const LinW& W, const void* x, int ldx, const int* row_map, const int* n_rows_ptr,
+                     int max_rows, const GemvEpi& ep, int* status, cudaStream_t s) {
+  static int n_sm = 0;
+  if (n_sm == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
+    if (n_sm <= 0) n_sm = 148;
+  }
+  const int xrows = ((max_rows < kRows ? max_rows : kRows) + 7) & ~7;
+  const size_t xbytes = (size_t)xrows * (W.K + 8) * sizeof(T);
+  const size_t stage = (size_t)kHeadWarps * (Q8 ? kUnitQ8 : kUnitDense);
+  if (xbytes + 2 * stage > (size_t)kHeadSmemBudget) return 0;
+  int stages = (int)((kHeadSmemBudget - xbytes) / stage);
+  if (stages > kHeadMaxStages) stages = kHeadMaxStages;
+  const int n_tiles = W.N / (kHeadWarps * 16);
+  const int grid = n_tiles < n_sm ? n_tiles : n_sm;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, (max_rows + kRows - 1) / kRows, 1);
+  cfg.blockDim = dim3((kHeadWarps + 1) * 32);
+  cfg.dynamicSmemBytes = (size_t)stages * stage + xbytes;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, k_lm_head<T, Q8>, (const T*)x, ldx, row_map, n_rows_ptr, W, ep, xrows, stages, status);
+  return grid;
+}
+
+template <typename T, bool Q8>
+cudaError_t init_gemv_t() {
+  cudaError_t e = cudaSuccess;
+  const int lim = 226 * 1024;  // opt-in limit less room for the static barrier and row scales
+  for (cudaError_t r : {
+           cudaFuncSetAttribute(k_gemv<T, Q8, 8, kGemvQkv, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim),
+           cudaFuncSetAttribute(k_gemv<T, Q8, 8, kGemvQkv, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim),
+           cudaFuncSetAttribute(k_gemv<T, Q8, 4, kGemvResid, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim),
+           cudaFuncSetAttribute(k_gemv<T, Q8, 4, kGemvSwiglu, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim),
+           cudaFuncSetAttribute(k_gemv<T, Q8, 8, kGemvLogits, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim),
+           cudaFuncSetAttribute(k_lm_head<T, Q8>, cudaFuncAttributeMaxDynamicSharedMemorySize, kHeadSmemBudget)})
+    if (r != cudaSuccess) e = r;
+  return e;
+}
+
+}  // namespace
+
+cudaError_t init_gemv() {
+  for (cudaError_t e : {init_gemv_t<__nv_bfloat16, true>(), init_gemv_t<__nv_bfloat16, false>(),
+                        init_gemv_t<__half, true>(), init_gemv_t<__half, false>()})
+    if (e != cudaSuccess) return e;
+  return cudaSuccess;
+}
+
+
+int gemv_tile_features(int epi) { return (epi == kGemvQkv || epi == kGemvLogits) ? 128 : 64; }
+
+// K split of one projection: the widest cluster (<= 8, portable) whose slices
+// are whole 64-wide k-blocks, but for lm_head only 2, since its activation
+// tile is re-read by each of the vocab/128 feature tiles. 0 if no split keeps
+// a slice within kMaxKb k-blocks.
+int gemv_split(int epi, int K) {
+  for (int s = epi == kGemvLogits ? 2 : 8; s >= 1; s >>= 1)
+    if (K % (64 * s) == 0 && K / s <= 64 * kMaxKb) return s;
+  return 0;
+}
+
+size_t gemv_packed_bytes(int epi, int N, int K, bool q8) {
+  return (size_t)(N / 16) * (K / 64) * (q8 ? kUnitQ8 : kUnitDense);
+}
+
+// Tile (feature tile f, k-split s) is the contiguous range
+// [(f * S + s) * nkb * FW * UNIT, +nkb * FW * UNIT), k-block major.
+void gemv_pack(int epi, int N, int K, bool q8, const int8_t* qs, const uint16_t* d, const uint16_t* w,
+               uint8_t* out) {
+  const int FT = gemv_tile_features(epi), FW = FT / 16, S = gemv_split(epi, K);
+  const int klen = K / S, nkb = klen / 64, KB = K / kQ8Block;
+  const int unit = q8 ? kUnitQ8 : kUnitDense;
+  for (int f = 0; f < N / FT; ++f)
+    for (int s = 0; s < S; ++s)
+      for (int kb = 0; kb < nkb; ++kb)
+        for (int wp = 0; wp < FW; ++wp) {
+          uint8_t* u = out + ((((size_t)f * S + s) * nkb + kb) * FW + wp) * unit;
+          const int r0 = f * FT + wp * 16, k0 = s * klen + kb * 64;
+          for (int lane = 0; lane < 32; ++lane) {
+            const int g = lane >> 2, t = lane & 3;
+            const size_t a = (size_t)(r0 + g) * K + k0 + 16 * t, b = a + (size_t)8 * K;
+            if (q8) {
+              std::memcpy(u + lane * 16, qs + a, 16);
+              std::memcpy(u + 512 + lane * 16, qs + b, 16);
+            } else {
+              std::memcpy(u + lane * 16, w + a, 16);
+              std::memcpy(u + 512 + lane * 16, w + a + 8, 16);
+              std::memcpy(u + 1024 + lane * 16, w + b, 16);
+              std::memcpy(u + 1536 + lane * 16, w + b + 8, 16);
+            }
+          }
+          if (q8) {
+            uint16_t* sc = reinterpret_cast<uint16_t*>(u + 1024);
+            for (int j = 0; j < 32; ++j) sc[j] = d[(size_t)(r0 + (j >> 1)) * KB + k0 / kQ8Block + (j & 1)];
+          }
+        }
+}
+
+bool launch_gemv(ActType at, int epi, bool norm, const LinW& W, const void* x, int ldx, const int* row_map,
+                 const int* n_rows_ptr, int max_rows, const GemvEpi& ep, int* status, cudaStream_t s) {
+  const int S = gemv_split(epi, W.K);
+  if (S == 0 || W.pk == nullptr || W.N % gemv_tile_features(epi) != 0) return false;
+#define FMD_GEMV(T, Q8)                                                                                           \
+  switch (epi) {                                                                                                \
+    case kGemvQkv:                                                                                              \
+      if (norm) launch_gemv_t<T, Q8, 8, kGemvQkv, true>(W, S, x, ldx, row_map, n_rows_ptr, max_rows, ep, status, s);     \
+      else launch_gemv_t<T, Q8, 8, kGemvQkv, false>(W, S, x, ldx, row_map, n_rows_ptr, max_rows, ep, status, s);         \
+      break;                                                                                                    \
+    case kGemvResid: launch_gemv_t<T, Q8, 4, kGemvResid, false>(W, S, x, ldx, row_map, n_rows_ptr, max_rows, ep, status, s); break; \
+    case kGemvSwiglu: launch_gemv_t<T, Q8, 4, kGemvSwiglu, true>(W, S, x, ldx, row_map, n_rows_ptr, max_rows, ep, status, s); break; \
+    default: launch_gemv_t<T, Q8, 8, kGemvLogits, true>(W, S, x, ldx, row_map, n_rows_ptr, max_rows, ep, status, s); break; \
+  }
+  if (at == kBF16) {
+    if (W.q8) { FMD_GEMV(__nv_bfloat16, true) } else { FMD_GEMV(__nv_bfloat16, false) }
+  } else {
+    if (W.q8) { FMD_GEMV(__half, true) } else { FMD_GEMV(__half, false) }
+  }
+#undef FMD_GEMV
+  return true;
+}
+
+int launch_lm_head(ActType at, const LinW& W, const void* x, int ldx, const int* row_map, const int* n_rows_ptr,
+                   int max_rows, const GemvEpi& ep, int* status, cudaStream_t s) {
+  if (W.pk == nullptr || W.N % (kHeadWarps * 16) != 0 || W.K % 64 != 0) return 0;
+  int parts;
+  if (at == kBF16)
+    parts = W.q8 ? launch_lm_head_t<__nv_bfloat16, true>(W, x, ldx, row_map, n_rows_ptr, max_rows, ep, status, s)
+                 : launch_lm_head_t<__nv_bfloat16, false>(W, x, ldx, row_map, n_rows_ptr, max_rows, ep, status, s);
+  else
+    parts = W.q8 ? launch_lm_head_t<__half, true>(W, x, ldx, row_map, n_rows_ptr, max_rows, ep, status, s)
+                 : launch_lm_head_t<__half, false>(W, x, ldx, row_map, n_rows_ptr, max_rows, ep, status, s);
+  if (parts > 0) return parts;
+  // activation tile too large for the resident kernel: the cluster GEMV
+  return launch_gemv(at, kGemvLogits, true, W, x, ldx, row_map, n_rows_ptr, max_rows, ep, status, s)
+             ? W.N / gemv_tile_features(kGemvLogits)
+             : 0;
+}
+
+void launch_pick_reduce(const int* n_sample_ptr, int B, const float* best_val, const int* best_idx, int n_parts,
+                        int* next_ids, cudaStream_t s) {
+  launch_pdl(k_pick_reduce, dim3(B), dim3(256), 0, s, n_sample_ptr, best_val, best_idx, n_parts, next_ids);
+}
+
+}  // namespace fmd

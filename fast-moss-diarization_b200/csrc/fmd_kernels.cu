@@ -38,8 +38,10 @@ FMD_DEV float block_sum(float v, float* red) {
 template <typename T>
 __global__ void __launch_bounds__(128) k_embed_norm(Plan p, const T* __restrict__ table, const T* __restrict__ arena,
                                                     T* __restrict__ x, const T* __restrict__ w, T* __restrict__ xn,
-                                                    int H, float eps) {
+                                                    int H, float eps, float* __restrict__ ssq, int ssq_tiles) {
   __shared__ float red[4];
+  griddep_launch();
+  griddep_wait();
   const int n_rows = p.counts->n_rows;
   for (int r = blockIdx.x; r < n_rows; r += gridDim.x) {
   const int tok = p.row_tok[r];
@@ -56,7 +58,10 @@ __global__ void __launch_bounds__(128) k_embed_norm(Plan p, const T* __restrict_
       ss += f.x * f.x + f.y * f.y;
     }
   }
-  const float inv = rsqrtf(block_sum<128>(ss, red) / H + eps);
+  const float tot = block_sum<128>(ss, red);
+  const float inv = rsqrtf(tot / H + eps);
+  if (ssq != nullptr)
+    for (int i = threadIdx.x; i < ssq_tiles; i += 128) ssq[(size_t)r * ssq_tiles + i] = i == 0 ? tot : 0.f;
   for (int i = threadIdx.x * 8; i < H; i += 128 * 8) {
     const int4 v = *reinterpret_cast<const int4*>(src + i);
     const int4 wv = *reinterpret_cast<const int4*>(w + i);
@@ -85,6 +90,8 @@ __global__ void __launch_bounds__(128) k_residual_norm(const int* __restrict__ n
                                                        size_t split_stride, const T* __restrict__ w,
                                                        T* __restrict__ xn, int H, float eps) {
   __shared__ float red[4];
+  griddep_launch();
+  griddep_wait();
   const int n_rows = *n_rows_ptr;
   const int S = effective_split(split, n_rows);
   for (int r = blockIdx.x; r < n_rows; r += gridDim.x) {
@@ -98,7 +105,8 @@ __global__ void __launch_bounds__(128) k_residual_norm(const int* __restrict__ n
       const float* p0 = part + (size_t)r * H + i;
       float4 a = *reinterpret_cast<const float4*>(p0), b = *reinterpret_cast<const float4*>(p0 + 4);
       acc[0] = a.x; acc[1] = a.y; acc[2] = a.z; acc[3] = a.w; acc[4] = b.x; acc[5] = b.y; acc[6] = b.z; acc[7] = b.w;
-      for (int s = 1; s < S; ++s) {
+#pragma unroll 4
+      for (int s = 1; s < S; ++s) {  // unrolled: the partial loads are issued together
         const float* ps = p0 + (size_t)s * split_stride;
         a = *reinterpret_cast<const float4*>(ps);
         b = *reinterpret_cast<const float4*>(ps + 4);
@@ -159,18 +167,47 @@ struct WRaw {
 template <typename T, bool Q8>
 __global__ void __launch_bounds__(128) k_linear(const T* __restrict__ x, int ldx, const int* __restrict__ row_map,
                                                 const int* __restrict__ n_rows_ptr, LinW W, float* __restrict__ out,
-                                                size_t split_stride) {
+                                                size_t split_stride, int decode_only) {
   __shared__ __align__(16) T xs[2][64][72];
-  const int n_rows = *n_rows_ptr;
-  const int S = effective_split(W.split, n_rows);
-  if ((int)blockIdx.y >= S) return;
+  griddep_launch();
   const int K = W.K, N = W.N;
-  const int klen = K / S;
-  const int kbeg = blockIdx.y * klen;
-  const int nkb = klen >> 6;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int f0 = blockIdx.x * 64 + warp * 16 + g;
   const int KB = K / kQ8Block;
+  auto load_w_at = [&](int kbeg_, int kb, WRaw& w) {
+    const int k = kbeg_ + kb * 64 + 16 * t;
+    if constexpr (Q8) {
+      w.a = ld_stream16(W.qs + (size_t)f0 * K + k);
+      w.b = ld_stream16(W.qs + (size_t)(f0 + 8) * K + k);
+      w.da = h2f_bits(W.d[(size_t)f0 * KB + (k >> 5)]);
+      w.db = h2f_bits(W.d[(size_t)(f0 + 8) * KB + (k >> 5)]);
+    } else {
+      const T* wp = reinterpret_cast<const T*>(W.w);
+      w.a = ld_stream16(wp + (size_t)f0 * K + k);
+      w.b = ld_stream16(wp + (size_t)f0 * K + k + 8);
+      w.c = ld_stream16(wp + (size_t)(f0 + 8) * K + k);
+      w.d = ld_stream16(wp + (size_t)(f0 + 8) * K + k + 8);
+    }
+  };
+  // Decode-only passes use the full K split, known before the plan is read:
+  // the CTA's first two weight k-blocks are fetched while the previous kernel
+  // is still finishing.
+  WRaw wc, wn;
+  bool pre = false;
+  if (decode_only && (int)blockIdx.y < W.split) {
+    const int kbeg0 = blockIdx.y * (K / W.split);
+    load_w_at(kbeg0, 0, wc);
+    if ((K / W.split) >> 6 > 1) load_w_at(kbeg0, 1, wn);
+    pre = true;
+  }
+  griddep_wait();
+  const int n_rows = *n_rows_ptr;
+  const int S = effective_split(W.split, n_rows);
+  if ((int)blockIdx.y >= S) return;
+  const int klen = K / S;
+  const int kbeg = blockIdx.y * klen;
+  const int nkb = klen >> 6;
+  pre = pre && S == W.split;  // the prefetch matches this pass's split
 
   for (int row0 = blockIdx.z * 64; row0 < n_rows; row0 += gridDim.z * 64) {
     const int rows = min(64, n_rows - row0);
@@ -201,33 +238,18 @@ __global__ void __launch_bounds__(128) k_linear(const T* __restrict__ x, int ldx
       }
       cp_async_commit();
     };
-    auto load_w = [&](int kb, WRaw& w) {
-      const int k = kbeg + kb * 64 + 16 * t;
-      if constexpr (Q8) {
-        w.a = ld_stream16(W.qs + (size_t)f0 * K + k);
-        w.b = ld_stream16(W.qs + (size_t)(f0 + 8) * K + k);
-        w.da = h2f_bits(W.d[(size_t)f0 * KB + (k >> 5)]);
-        w.db = h2f_bits(W.d[(size_t)(f0 + 8) * KB + (k >> 5)]);
-      } else {
-        const T* wp = reinterpret_cast<const T*>(W.w);
-        w.a = ld_stream16(wp + (size_t)f0 * K + k);
-        w.b = ld_stream16(wp + (size_t)f0 * K + k + 8);
-        w.c = ld_stream16(wp + (size_t)(f0 + 8) * K + k);
-        w.d = ld_stream16(wp + (size_t)(f0 + 8) * K + k + 8);
-      }
-    };
+    auto load_w = [&](int kb, WRaw& w) { load_w_at(kbeg, kb, w); };
 
     float acc[8][4];
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
 
-    WRaw wc, wn;
     load_x(0, 0);
-    load_w(0, wc);
+    if (!pre) load_w(0, wc);
     for (int kb = 0; kb < nkb; ++kb) {
       if (kb + 1 < nkb) {
         load_x((kb + 1) & 1, kb + 1);
-        load_w(kb + 1, wn);
+        if (!(pre && kb == 0)) load_w(kb + 1, wn);
         cp_async_wait<1>();
       } else {
         cp_async_wait<0>();
@@ -284,6 +306,7 @@ __global__ void __launch_bounds__(128) k_linear(const T* __restrict__ x, int ldx
       wc = wn;
     }
 
+    pre = false;  // a further row tile streams its weights again
     float* o = out + (size_t)blockIdx.y * split_stride;
 #pragma unroll
     for (int nt = 0; nt < 8; ++nt) {
@@ -315,6 +338,8 @@ __global__ void __launch_bounds__(256) k_qkv_epilogue(Plan p, const float* __res
                                                       const T* __restrict__ qn_w, const T* __restrict__ kn_w,
                                                       const T* __restrict__ cos_t, const T* __restrict__ sin_t,
                                                       T* __restrict__ q_out, KvView kv, int layer, float eps) {
+  griddep_launch();
+  griddep_wait();
   const int n_rows = p.counts->n_rows;
   const int S = effective_split(split, n_rows);
   const int N = (Hq + 2 * Hkv) * kHeadDim;
@@ -330,7 +355,8 @@ __global__ void __launch_bounds__(256) k_qkv_epilogue(Plan p, const float* __res
     {
       const float* p0 = part + (size_t)r * N + c;
       float4 a = *reinterpret_cast<const float4*>(p0);
-      for (int s = 1; s < S; ++s) {
+#pragma unroll 8
+      for (int s = 1; s < S; ++s) {  // unrolled: the partial loads are issued together
         const float4 b = *reinterpret_cast<const float4*>(p0 + (size_t)s * split_stride);
         a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
       }
@@ -378,6 +404,8 @@ template <typename T>
 __global__ void __launch_bounds__(128) k_attn_prefill(Plan p, int Hq, const T* __restrict__ q, KvView kv, int layer,
                                                       float scale_log2, T* __restrict__ ctx) {
   extern __shared__ __align__(128) uint8_t smem[];
+  griddep_launch();
+  griddep_wait();
   const int n_blocks = p.counts->n_pblocks;
   for (int b = blockIdx.x; b < n_blocks; b += gridDim.x) {
   const int h = blockIdx.y;
@@ -528,21 +556,26 @@ __global__ void __launch_bounds__(128) k_attn_prefill(Plan p, int Hq, const T* _
 }
 
 // ---------------------------------------------------------------------------
-// SwiGLU (qwen3.rs:288-292): h = rnd(rnd(silu(rnd(gate))) * rnd(up)).
+// SwiGLU (qwen3.rs:288-292): h = rnd(rnd(silu(rnd(gate))) * rnd(up)); gate/up
+// columns are interleaved in 32-groups (gate_col / up_col).
 // ---------------------------------------------------------------------------
 template <typename T>
 __global__ void __launch_bounds__(256) k_silu_mul(const int* __restrict__ n_rows_ptr, const float* __restrict__ part,
                                                   int split, size_t split_stride, int I, T* __restrict__ h) {
+  griddep_launch();
+  griddep_wait();
   const int n_rows = *n_rows_ptr;
   const int S = effective_split(split, n_rows);
   for (int r = blockIdx.x; r < n_rows; r += gridDim.x) {
   const float* p0 = part + (size_t)r * 2 * I;
   for (int c = threadIdx.x * 4; c < I; c += blockDim.x * 4) {
-    float4 gs = *reinterpret_cast<const float4*>(p0 + c);
-    float4 us = *reinterpret_cast<const float4*>(p0 + I + c);
-    for (int s = 1; s < S; ++s) {
-      const float4 a = *reinterpret_cast<const float4*>(p0 + (size_t)s * split_stride + c);
-      const float4 b = *reinterpret_cast<const float4*>(p0 + (size_t)s * split_stride + I + c);
+    const int gc = gate_col(c), uc = up_col(c);  // 4 consecutive features never cross a 32-group
+    float4 gs = *reinterpret_cast<const float4*>(p0 + gc);
+    float4 us = *reinterpret_cast<const float4*>(p0 + uc);
+#pragma unroll 4
+    for (int s = 1; s < S; ++s) {  // unrolled: the partial loads are issued together
+      const float4 a = *reinterpret_cast<const float4*>(p0 + (size_t)s * split_stride + gc);
+      const float4 b = *reinterpret_cast<const float4*>(p0 + (size_t)s * split_stride + uc);
       gs.x += a.x; gs.y += a.y; gs.z += a.z; gs.w += a.w;
       us.x += b.x; us.y += b.y; us.z += b.z; us.w += b.w;
     }
@@ -573,6 +606,8 @@ __global__ void __launch_bounds__(1024) k_logits_argmax(const int* __restrict__ 
                                                         float* __restrict__ logits, int* __restrict__ next_ids) {
   __shared__ float sv[32];
   __shared__ int si[32];
+  griddep_launch();
+  griddep_wait();
   const int r = blockIdx.x;
   if (r >= *n_sample_ptr) return;
   const float* pr = part + (size_t)r * V;
@@ -639,27 +674,27 @@ __global__ void k_dequant(LinW W, float* __restrict__ out) {
   } while (0)
 
 void launch_embed_norm(ActType at, const Plan& p, int R, const void* table, const void* arena, void* x, const void* w,
-                       void* xn, int H, float eps, cudaStream_t s) {
-  FMD_DISPATCH(at, k_embed_norm<T><<<R, 128, 0, s>>>(p, (const T*)table, (const T*)arena, (T*)x, (const T*)w,
-                                                      (T*)xn, H, eps));
+                       void* xn, int H, float eps, float* ssq, int ssq_tiles, cudaStream_t s) {
+  FMD_DISPATCH(at, launch_pdl(k_embed_norm<T>, R, 128, 0, s, p, (const T*)table, (const T*)arena, (T*)x, (const T*)w,
+                                                      (T*)xn, H, eps, ssq, ssq_tiles));
 }
 
 void launch_linear(ActType at, const LinW& W, const void* x, int ldx, const int* row_map, const int* n_rows_ptr,
-                   int max_rows, float* out, size_t split_stride, cudaStream_t s) {
+                   int max_rows, float* out, size_t split_stride, bool decode_only, cudaStream_t s) {
   const int row_tiles = (max_rows + 63) / 64;
   dim3 grid(W.N / 64, W.split, row_tiles < 8 ? row_tiles : 8);
   FMD_DISPATCH(at, {
     if (W.q8)
-      k_linear<T, true><<<grid, 128, 0, s>>>((const T*)x, ldx, row_map, n_rows_ptr, W, out, split_stride);
+      launch_pdl(k_linear<T, true>, grid, 128, 0, s, (const T*)x, ldx, row_map, n_rows_ptr, W, out, split_stride, (int)decode_only);
     else
-      k_linear<T, false><<<grid, 128, 0, s>>>((const T*)x, ldx, row_map, n_rows_ptr, W, out, split_stride);
+      launch_pdl(k_linear<T, false>, grid, 128, 0, s, (const T*)x, ldx, row_map, n_rows_ptr, W, out, split_stride, (int)decode_only);
   });
 }
 
 void launch_qkv_epilogue(ActType at, const Plan& p, int R, const float* part, int split, size_t split_stride,
                          int Hq, int Hkv, const void* qn_w, const void* kn_w, const void* cos, const void* sin,
                          void* q_out, const KvView& kv, int layer, float eps, cudaStream_t s) {
-  FMD_DISPATCH(at, k_qkv_epilogue<T><<<R, 256, 0, s>>>(p, part, split, split_stride, Hq, Hkv, (const T*)qn_w,
+  FMD_DISPATCH(at, launch_pdl(k_qkv_epilogue<T>, R, 256, 0, s, p, part, split, split_stride, Hq, Hkv, (const T*)qn_w,
                                                         (const T*)kn_w, (const T*)cos, (const T*)sin, (T*)q_out, kv,
                                                         layer, eps));
 }
@@ -669,23 +704,23 @@ void launch_attn_prefill(ActType at, const Plan& p, int PB, int Hq, int Hkv, con
   const float scale_log2 = scale * 1.4426950408889634f;
   dim3 grid(PB, Hkv);
   const int smem = 65536;
-  FMD_DISPATCH(at, k_attn_prefill<T><<<grid, 128, smem, s>>>(p, Hq, (const T*)q, kv, layer, scale_log2, (T*)ctx));
+  FMD_DISPATCH(at, launch_pdl(k_attn_prefill<T>, grid, 128, smem, s, p, Hq, (const T*)q, kv, layer, scale_log2, (T*)ctx));
 }
 
 void launch_residual_norm(ActType at, const int* n_rows_ptr, int R, void* x, const float* part, int split,
                           size_t split_stride, const void* w, void* xn, int H, float eps, cudaStream_t s) {
-  FMD_DISPATCH(at, k_residual_norm<T><<<R, 128, 0, s>>>(n_rows_ptr, (T*)x, part, split, split_stride, (const T*)w,
+  FMD_DISPATCH(at, launch_pdl(k_residual_norm<T>, R, 128, 0, s, n_rows_ptr, (T*)x, part, split, split_stride, (const T*)w,
                                                          (T*)xn, H, eps));
 }
 
 void launch_silu_mul(ActType at, const int* n_rows_ptr, int R, const float* part, int split, size_t split_stride,
                      int I, void* h, cudaStream_t s) {
-  FMD_DISPATCH(at, k_silu_mul<T><<<R, 256, 0, s>>>(n_rows_ptr, part, split, split_stride, I, (T*)h));
+  FMD_DISPATCH(at, launch_pdl(k_silu_mul<T>, R, 256, 0, s, n_rows_ptr, part, split, split_stride, I, (T*)h));
 }
 
 void launch_logits_argmax(ActType at, const int* n_sample_ptr, int B, const float* part, int V, float* logits,
                           int* next_ids, cudaStream_t s) {
-  FMD_DISPATCH(at, k_logits_argmax<T><<<B, 1024, 0, s>>>(n_sample_ptr, part, V, logits, next_ids));
+  FMD_DISPATCH(at, launch_pdl(k_logits_argmax<T>, B, 1024, 0, s, n_sample_ptr, part, V, logits, next_ids));
 }
 
 cudaError_t init_kernels() {

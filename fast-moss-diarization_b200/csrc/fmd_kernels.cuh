@@ -2,6 +2,8 @@
 // host runtime, plus the launchers the runtime calls.
 #pragma once
 
+#include <utility>
+
 #include "fmd_common.cuh"
 
 namespace fmd {
@@ -104,6 +106,38 @@ struct LinW {
   const uint16_t* d = nullptr;
   const void* w = nullptr;
   int split = 1;  // K splits used when a pass has <= 64 rows
+  const uint8_t* pk = nullptr;  // decode-packed tiles of the decode-step GEMV
+};
+
+// gate/up projections are stored with their rows interleaved in 32-row
+// groups ([g0..g31, u0..u31, g32..g63, u32..u63, ...]) so a 64-row tile holds
+// matching gate and up features; output column of gate / up feature i:
+__host__ __device__ inline int gate_col(int i) { return (i >> 5) * 64 + (i & 31); }
+__host__ __device__ inline int up_col(int i) { return gate_col(i) + 32; }
+
+// Epilogue selector and arguments of the decode-step GEMV (fmd_gemv.cu).
+enum GemvEpiKind { kGemvQkv = 0, kGemvResid = 1, kGemvSwiglu = 2, kGemvLogits = 3 };
+struct GemvEpi {
+  // normalised input (NORM variants): xn = x * rsqrt(sum(ssq[row]) / K + eps) * norm_w
+  const float* ssq = nullptr;  // [rows][ssq_tiles] per-tile sums of squares of x
+  const void* norm_w = nullptr;
+  int ssq_tiles = 0;
+  float eps = 0.f;
+  void* x = nullptr;         // kGemvResid: residual stream [rows][N], updated in place
+  float* ssq_out = nullptr;  // kGemvResid: [rows][N / 64] sums of squares of the new x
+  void* h = nullptr;         // kGemvSwiglu: [rows][I]
+  int I = 0;
+  Plan plan{};               // kGemvQkv
+  const void* qn_w = nullptr;
+  const void* kn_w = nullptr;
+  const void* cos = nullptr;
+  const void* sin = nullptr;
+  void* q_out = nullptr;
+  KvView kv{};
+  int layer = 0, Hq = 0, Hkv = 0;
+  float* logits = nullptr;    // kGemvLogits: optional f32 logits [rows][N]
+  float* best_val = nullptr;  // kGemvLogits: per-tile (max, index) per row
+  int* best_idx = nullptr;
 };
 
 // Device-side K split actually used for a pass with `n_rows` rows.
@@ -111,11 +145,31 @@ __host__ __device__ inline int effective_split(int split, int n_rows) { return n
 
 enum ActType { kBF16 = 0, kF16 = 1 };
 
+// Launch with programmatic stream serialisation, so that inside a step (and
+// its CUDA graph) a kernel's launch overlaps the tail of its predecessor.
+template <typename... KArgs, typename... Args>
+inline void launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args&&... args) {
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 // ---- launchers (fmd_kernels.cu) -------------------------------------------------
+// also writes ssq[row][0] = sum of squares of the row, ssq[row][1..tiles) = 0, when ssq != nullptr
 void launch_embed_norm(ActType at, const Plan& p, int R, const void* table, const void* arena, void* x, const void* w,
-                       void* xn, int H, float eps, cudaStream_t s);
+                       void* xn, int H, float eps, float* ssq, int ssq_tiles, cudaStream_t s);
+// `decode_only`: every pass through this launch has <= 64 rows, so the K
+// split is known before the plan is read and weights are prefetched early.
 void launch_linear(ActType at, const LinW& W, const void* x, int ldx, const int* row_map, const int* n_rows_ptr,
-                   int max_rows, float* out, size_t split_stride, cudaStream_t s);
+                   int max_rows, float* out, size_t split_stride, bool decode_only, cudaStream_t s);
 void launch_qkv_epilogue(ActType at, const Plan& p, int R, const float* part, int split, size_t split_stride,
                          int Hq, int Hkv, const void* qn_w, const void* kn_w, const void* cos, const void* sin,
                          void* q_out, const KvView& kv, int layer, float eps, cudaStream_t s);
@@ -128,6 +182,27 @@ void launch_silu_mul(ActType at, const int* n_rows_ptr, int R, const float* part
 void launch_logits_argmax(ActType at, const int* n_sample_ptr, int B, const float* part, int V, float* logits,
                           int* next_ids, cudaStream_t s);
 void launch_dequant(ActType at, const LinW& W, float* out, cudaStream_t s);
+
+// fmd_gemv.cu: decode-step projections (cluster split-K, fused epilogues/norms).
+cudaError_t init_gemv();
+int gemv_split(int epi, int K);
+int gemv_tile_features(int epi);
+// Decode-packed copy of a projection for the GEMV of epilogue `epi`: q8 takes
+// qs [N][K] + d [N][K/32] (f16 bits), else w [N][K] 16-bit (host side).
+size_t gemv_packed_bytes(int epi, int N, int K, bool q8);
+void gemv_pack(int epi, int N, int K, bool q8, const int8_t* qs, const uint16_t* d, const uint16_t* w,
+               uint8_t* out);
+// false (nothing launched) if the projection has no packed tiles or no valid
+// K split for this epilogue.
+bool launch_gemv(ActType at, int epi, bool norm, const LinW& W, const void* x, int ldx, const int* row_map,
+                 const int* n_rows_ptr, int max_rows, const GemvEpi& ep, int* status, cudaStream_t s);
+// lm_head of the decode step (persistent kernel; the cluster GEMV when the
+// activation tile does not fit). Returns the candidates per row it writes
+// into ep.best_val / best_idx (0: nothing launched).
+int launch_lm_head(ActType at, const LinW& W, const void* x, int ldx, const int* row_map, const int* n_rows_ptr,
+                   int max_rows, const GemvEpi& ep, int* status, cudaStream_t s);
+void launch_pick_reduce(const int* n_sample_ptr, int B, const float* best_val, const int* best_idx, int n_parts,
+                        int* next_ids, cudaStream_t s);
 
 // fmd_attn_decode.cu: TMA-fed decode attention with the split-KV merge fused in.
 // `tmap` points at a CUtensorMap over the KV pool viewed as 2D

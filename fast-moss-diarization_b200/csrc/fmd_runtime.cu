@@ -124,12 +124,16 @@ struct fmd_handle {
   alignas(64) CUtensorMap kv_tmap;  // the KV pool as [rows][128] for TMA tile loads
   int* attn_counters = nullptr;     // [max_slots][kv_heads] split-KV merge counters
   int* d_status = nullptr;          // device-side error status (bounded waits)
+  bool launch_refused = false;      // a decode projection could not be launched
   int* d_page_table = nullptr;
   std::vector<int> h_page_table;
   std::vector<int> free_pages;           // host allocator (operator mode)
   std::vector<int> slot_cap, slot_len, slot_npages;
   void *x = nullptr, *xn = nullptr, *qbuf = nullptr, *ctx = nullptr, *hbuf = nullptr, *arena = nullptr;
   float *part = nullptr, *pacc = nullptr, *pml = nullptr, *logits = nullptr;
+  float* ssq = nullptr;       // [max_slots][hidden / 64] per-tile sums of squares of the residual stream
+  float* best_val = nullptr;  // [max_slots][vocab / 64] greedy candidates of the decode path
+  int* best_idx = nullptr;
   size_t split_stride = 0;
   int* next_ids = nullptr;
   PlanLayout layout{};
@@ -145,8 +149,11 @@ struct fmd_handle {
   int* eng_free = nullptr;
   EngineCounters* eng_ctr = nullptr;
   EngineCounters* h_ctr = nullptr;
-  cudaGraphExec_t graph_exec = nullptr;
+  cudaGraphExec_t graph_exec = nullptr;  // engine step that may carry a prefill chunk ("M")
+  cudaGraphExec_t graph_dec = nullptr;   // decode-only engine step ("D")
   int graph_batch = -1, graph_chunk = -1;
+  bool first_block = true;               // no counters polled since fmd_engine_start
+  int64_t launched_mixed = 0;
   bool engine_started = false;
   bool record_attn_events = false;             // set while capturing the step graph
   std::vector<cudaEvent_t> attn_events;        // [2 * layers] around each decode-attention launch
@@ -231,8 +238,26 @@ int upload_dense(fmd_handle* h, const fmd_tensor& t, size_t n, void** out, const
 }
 
 // Projection parts stacked along the output axis (linear.rs:220-265).
+// Reorder the rows of a two-part (N = 2 x half) matrix into 32-row groups
+// [a0..a31, b0..b31, a32..a63, b32..b63, ...] (see gate_col / up_col).
+template <typename E>
+void interleave_rows(std::vector<E>& m, int N, int cols) {
+  std::vector<E> out(m.size());
+  const int half = N / 2;
+  for (int r = 0; r < N; ++r) {
+    const int part = r / half, i = r % half;
+    std::memcpy(&out[(size_t)(part ? up_col(i) : gate_col(i)) * cols], &m[(size_t)r * cols], sizeof(E) * cols);
+  }
+  m.swap(out);
+}
+
+// `interleave16`: store the two parts' rows interleaved in 32-row groups.
+// Uploads one projection twice: [N][K] for the mixed-step k_linear and the
+// decode-packed tiles of the decode-step GEMV whose epilogue is `epi`.
+// `row_major` false: only the packed copy (W.w is set by the caller, as for
+// a 16-bit lm_head tied to the embedding table).
 int upload_linear(fmd_handle* h, const std::vector<std::pair<const fmd_tensor*, int>>& parts, int K, LinW& W,
-                  const char* what) {
+                  const char* what, int epi, bool interleave16 = false, bool row_major = true) {
   int N = 0;
   for (auto& p : parts) N += p.second;
   if (N % 64 || K % 64) return fail(h, FMD_ENOTSUP, std::string(what) + ": dims must be multiples of 64");
@@ -256,11 +281,19 @@ int upload_linear(fmd_handle* h, const std::vector<std::pair<const fmd_tensor*, 
       }
       off += n;
     }
+    if (interleave16) interleave_rows(bits, N, K);
     void* d;
-    int rc = dev_alloc(h, bits.size() * 2, &d, &h->weight_bytes);
-    if (rc) return rc;
-    if ((rc = upload(h, d, bits.data(), bits.size() * 2))) return rc;
-    W.w = d;
+    int rc;
+    if (row_major) {
+      if ((rc = dev_alloc(h, bits.size() * 2, &d, &h->weight_bytes))) return rc;
+      if ((rc = upload(h, d, bits.data(), bits.size() * 2))) return rc;
+      W.w = d;
+    }
+    std::vector<uint8_t> pk(gemv_packed_bytes(epi, N, K, false));
+    gemv_pack(epi, N, K, false, nullptr, nullptr, bits.data(), pk.data());
+    if ((rc = dev_alloc(h, pk.size(), &d, &h->weight_bytes))) return rc;
+    if ((rc = upload(h, d, pk.data(), pk.size()))) return rc;
+    W.pk = (const uint8_t*)d;
   } else {
     std::vector<int8_t> qs((size_t)N * K);
     std::vector<uint16_t> sc((size_t)N * (K / 32));
@@ -284,6 +317,10 @@ int upload_linear(fmd_handle* h, const std::vector<std::pair<const fmd_tensor*, 
       }
       row += rows;
     }
+    if (interleave16) {
+      interleave_rows(qs, N, K);
+      interleave_rows(sc, N, K / 32);
+    }
     void *dq, *dd;
     int rc = dev_alloc(h, qs.size(), &dq, &h->weight_bytes);
     if (rc) return rc;
@@ -292,6 +329,12 @@ int upload_linear(fmd_handle* h, const std::vector<std::pair<const fmd_tensor*, 
     if ((rc = upload(h, dd, sc.data(), sc.size() * 2))) return rc;
     W.qs = (const int8_t*)dq;
     W.d = (const uint16_t*)dd;
+    std::vector<uint8_t> pk(gemv_packed_bytes(epi, N, K, true));
+    gemv_pack(epi, N, K, true, qs.data(), sc.data(), nullptr, pk.data());
+    void* dp;
+    if ((rc = dev_alloc(h, pk.size(), &dp, &h->weight_bytes))) return rc;
+    if ((rc = upload(h, dp, pk.data(), pk.size()))) return rc;
+    W.pk = (const uint8_t*)dp;
   }
   // K split for passes with <= 64 rows: aim for >= ~2 CTAs per SM.
   int split = 1;
@@ -305,6 +348,10 @@ void release_graph(fmd_handle* h) {
   if (h->graph_exec) {
     cudaGraphExecDestroy(h->graph_exec);
     h->graph_exec = nullptr;
+  }
+  if (h->graph_dec) {
+    cudaGraphExecDestroy(h->graph_dec);
+    h->graph_dec = nullptr;
   }
   h->graph_batch = h->graph_chunk = -1;
 }
@@ -327,7 +374,78 @@ void trace(fmd_handle* h, const char* what, int layer) {
 }
 
 // ---- forward pass ------------------------------------------------------------------
-void run_forward(fmd_handle* h, float* logits_dev, const void* arena) {
+// Decode-only forward pass (every row is a one-token decode row): per layer
+// QKV (input norm folded in, q/k norm + RoPE + KV write fused) -> attention
+// -> O (+ residual) -> gate/up (post-attention norm folded in, SwiGLU fused)
+// -> down (+ residual); the split-K of each projection is reduced inside a
+// thread-block cluster.
+void run_forward_decode(fmd_handle* h, float* logits_dev, const void* arena) {
+  cudaStream_t s = h->stream;
+  const fmd_config& c = h->cfg;
+  const int R = h->max_slots, H = c.hidden_size, I = c.intermediate_size;
+  const int row_grid = std::min(R, 296);
+  const int* nrows = &h->plan.counts->n_rows;
+  const int* nsamp = &h->plan.counts->n_sample;
+  const float eps = c.rms_norm_eps;
+  const int ssq_tiles = H / 64;
+  launch_embed_norm(h->at, h->plan, row_grid, h->embed, arena, h->x, h->layers[0].in_norm, h->xn, H, eps, h->ssq,
+                    ssq_tiles, s);
+  trace(h, "embed_norm", -1);
+  GemvEpi qkv;
+  qkv.ssq = h->ssq;
+  qkv.ssq_tiles = ssq_tiles;
+  qkv.eps = eps;
+  qkv.plan = h->plan;
+  qkv.cos = h->rope_cos;
+  qkv.sin = h->rope_sin;
+  qkv.q_out = h->qbuf;
+  qkv.kv = h->kv;
+  qkv.Hq = h->Hq();
+  qkv.Hkv = h->Hkv();
+  GemvEpi res;
+  res.x = h->x;
+  res.ssq_out = h->ssq;
+  res.ssq_tiles = ssq_tiles;
+  GemvEpi glu = qkv;
+  glu.h = h->hbuf;
+  glu.I = I;
+  for (int l = 0; l < c.num_hidden_layers; ++l) {
+    const LayerDev& L = h->layers[l];
+    qkv.norm_w = L.in_norm;
+    qkv.qn_w = L.q_norm;
+    qkv.kn_w = L.k_norm;
+    qkv.layer = l;
+    if (!launch_gemv(h->at, kGemvQkv, true, L.qkv, h->x, H, nullptr, nrows, R, qkv, h->d_status, s)) h->launch_refused = true;
+    trace(h, "qkv", l);
+    if (h->record_attn_events) cudaEventRecordWithFlags(h->attn_events[2 * l], s, cudaEventRecordExternal);
+    launch_attn_decode_tma(h->at, &h->kv_tmap, h->plan, h->di_grid, h->Hq(), h->Hkv(), h->qbuf, h->kv, l,
+                           h->attn_scale, h->pacc, h->pml, h->attn_counters, h->ctx, h->d_status, s);
+    if (h->record_attn_events) cudaEventRecordWithFlags(h->attn_events[2 * l + 1], s, cudaEventRecordExternal);
+    trace(h, "attn_decode", l);
+    if (!launch_gemv(h->at, kGemvResid, false, L.o, h->ctx, h->Hq() * kHeadDim, nullptr, nrows, R, res, h->d_status, s)) h->launch_refused = true;
+    trace(h, "o_proj", l);
+    glu.norm_w = L.post_norm;
+    if (!launch_gemv(h->at, kGemvSwiglu, true, L.gate_up, h->x, H, nullptr, nrows, R, glu, h->d_status, s)) h->launch_refused = true;
+    trace(h, "gate_up", l);
+    if (!launch_gemv(h->at, kGemvResid, false, L.down, h->hbuf, I, nullptr, nrows, R, res, h->d_status, s)) h->launch_refused = true;
+    trace(h, "down", l);
+  }
+  GemvEpi head = qkv;
+  head.norm_w = h->final_norm;
+  head.logits = logits_dev;
+  head.best_val = h->best_val;
+  head.best_idx = h->best_idx;
+  const int parts = launch_lm_head(h->at, h->lm_head, h->x, H, h->plan.sample_row, nsamp, h->max_slots, head,
+                                   h->d_status, s);
+  if (parts == 0) h->launch_refused = true;
+  trace(h, "lm_head", -1);
+  launch_pick_reduce(nsamp, h->max_slots, h->best_val, h->best_idx, parts, h->next_ids, s);
+  trace(h, "argmax", -1);
+}
+
+// `decode_only`: every row is a one-token decode row (no prefill attention,
+// weights prefetched ahead of each projection's dependency wait).
+void run_forward(fmd_handle* h, float* logits_dev, const void* arena, bool decode_only = false) {
   cudaStream_t s = h->stream;
   const fmd_config& c = h->cfg;
   const int R = h->max_rows, H = c.hidden_size, I = c.intermediate_size;
@@ -336,11 +454,16 @@ void run_forward(fmd_handle* h, float* logits_dev, const void* arena) {
   const int* nsamp = &h->plan.counts->n_sample;
   const float eps = c.rms_norm_eps;
   const size_t ss = h->split_stride;
-  launch_embed_norm(h->at, h->plan, row_grid, h->embed, arena, h->x, h->layers[0].in_norm, h->xn, H, eps, s);
+  if (decode_only) {
+    run_forward_decode(h, logits_dev, arena);
+    return;
+  }
+  launch_embed_norm(h->at, h->plan, row_grid, h->embed, arena, h->x, h->layers[0].in_norm, h->xn, H, eps, nullptr,
+                    0, s);
   trace(h, "embed_norm", -1);
   for (int l = 0; l < c.num_hidden_layers; ++l) {
     const LayerDev& L = h->layers[l];
-    launch_linear(h->at, L.qkv, h->xn, H, nullptr, nrows, R, h->part, ss, s);
+    launch_linear(h->at, L.qkv, h->xn, H, nullptr, nrows, R, h->part, ss, decode_only, s);
     trace(h, "qkv", l);
     launch_qkv_epilogue(h->at, h->plan, row_grid, h->part, L.qkv.split, ss, h->Hq(), h->Hkv(), L.q_norm, L.k_norm,
                         h->rope_cos, h->rope_sin, h->qbuf, h->kv, l, eps, s);
@@ -350,23 +473,26 @@ void run_forward(fmd_handle* h, float* logits_dev, const void* arena) {
                            h->attn_scale, h->pacc, h->pml, h->attn_counters, h->ctx, h->d_status, s);
     if (h->record_attn_events) cudaEventRecordWithFlags(h->attn_events[2 * l + 1], s, cudaEventRecordExternal);
     trace(h, "attn_decode", l);
-    launch_attn_prefill(h->at, h->plan, h->pb_grid, h->Hq(), h->Hkv(), h->qbuf, h->kv, l, h->attn_scale, h->ctx, s);
-    trace(h, "attn_prefill", l);
-    launch_linear(h->at, L.o, h->ctx, h->Hq() * kHeadDim, nullptr, nrows, R, h->part, ss, s);
+    if (!decode_only) {
+      launch_attn_prefill(h->at, h->plan, h->pb_grid, h->Hq(), h->Hkv(), h->qbuf, h->kv, l, h->attn_scale, h->ctx,
+                          s);
+      trace(h, "attn_prefill", l);
+    }
+    launch_linear(h->at, L.o, h->ctx, h->Hq() * kHeadDim, nullptr, nrows, R, h->part, ss, decode_only, s);
     trace(h, "o_proj", l);
     launch_residual_norm(h->at, nrows, row_grid, h->x, h->part, L.o.split, ss, L.post_norm, h->xn, H, eps, s);
     trace(h, "res_norm1", l);
-    launch_linear(h->at, L.gate_up, h->xn, H, nullptr, nrows, R, h->part, ss, s);
+    launch_linear(h->at, L.gate_up, h->xn, H, nullptr, nrows, R, h->part, ss, decode_only, s);
     trace(h, "gate_up", l);
     launch_silu_mul(h->at, nrows, row_grid, h->part, L.gate_up.split, ss, I, h->hbuf, s);
     trace(h, "silu", l);
-    launch_linear(h->at, L.down, h->hbuf, I, nullptr, nrows, R, h->part, ss, s);
+    launch_linear(h->at, L.down, h->hbuf, I, nullptr, nrows, R, h->part, ss, decode_only, s);
     trace(h, "down", l);
     const void* next_norm = l + 1 < c.num_hidden_layers ? h->layers[l + 1].in_norm : h->final_norm;
     launch_residual_norm(h->at, nrows, row_grid, h->x, h->part, L.down.split, ss, next_norm, h->xn, H, eps, s);
     trace(h, "res_norm2", l);
   }
-  launch_linear(h->at, h->lm_head, h->xn, H, h->plan.sample_row, nsamp, h->max_slots, h->part, ss, s);
+  launch_linear(h->at, h->lm_head, h->xn, H, h->plan.sample_row, nsamp, h->max_slots, h->part, ss, decode_only, s);
   trace(h, "lm_head", -1);
   launch_logits_argmax(h->at, nsamp, h->max_slots, h->part, c.vocab_size, logits_dev, h->next_ids, s);
   trace(h, "argmax", -1);
@@ -444,6 +570,10 @@ int check_ready(fmd_handle* h) {
 }
 
 int sync_check(fmd_handle* h) {
+  if (h->launch_refused) {
+    h->launch_refused = false;
+    return fail(h, FMD_EIO, "a decode projection was not launched (no packed weight tiles or no valid K split)");
+  }
   cudaError_t e = cudaStreamSynchronize(h->stream);
   if (e != cudaSuccess) return fail(h, FMD_EIO, std::string("device error: ") + cudaGetErrorString(e));
   e = cudaGetLastError();
@@ -543,8 +673,16 @@ int fmd_create(const fmd_config* cfg, int32_t precision, int32_t device, fmd_han
   if (precision < FMD_PREC_F16 || precision > FMD_PREC_INT8_BF16) return FMD_EINVAL;
   if (cfg->head_dim != kHeadDim) return FMD_ENOTSUP;
   if (cfg->num_attention_heads != 2 * cfg->num_key_value_heads) return FMD_ENOTSUP;
-  if (cfg->hidden_size % 64 || cfg->intermediate_size % 64 || cfg->vocab_size % 64) return FMD_ENOTSUP;
+  if (cfg->hidden_size % 64 || cfg->intermediate_size % 64 || cfg->vocab_size % 64)
+    return FMD_ENOTSUP;
   if (cfg->num_hidden_layers < 1 || cfg->hidden_size <= 0) return FMD_EINVAL;
+  // decode-path projections: lm_head tiles are 128 features wide, and each
+  // contraction must split into slices the cluster GEMV holds
+  if (cfg->vocab_size % gemv_tile_features(kGemvLogits) ||
+      !gemv_split(kGemvQkv, cfg->hidden_size) || !gemv_split(kGemvLogits, cfg->hidden_size) ||
+      !gemv_split(kGemvResid, cfg->num_attention_heads * cfg->head_dim) ||
+      !gemv_split(kGemvResid, cfg->intermediate_size))
+    return FMD_ENOTSUP;
   int ndev = 0;
   if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev) {
     cudaGetLastError();
@@ -558,7 +696,7 @@ int fmd_create(const fmd_config* cfg, int32_t precision, int32_t device, fmd_han
   h->device = device;
   h->attn_scale = (float)(1.0 / std::sqrt((double)cfg->head_dim));
   if (cudaSetDevice(device) != cudaSuccess || cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking) != cudaSuccess ||
-      init_kernels() != cudaSuccess || init_attn_decode() != cudaSuccess) {
+      init_kernels() != cudaSuccess || init_attn_decode() != cudaSuccess || init_gemv() != cudaSuccess) {
     cudaGetLastError();
     delete h;
     return FMD_EIO;
@@ -603,22 +741,20 @@ int fmd_load_weights(fmd_handle* h, const fmd_weights* w) {
     if ((rc = upload_dense(h, s.post_attention_layernorm, H, &L.post_norm, "post_attention_layernorm"))) return rc;
     if ((rc = upload_dense(h, s.q_norm, kHeadDim, &L.q_norm, "q_norm"))) return rc;
     if ((rc = upload_dense(h, s.k_norm, kHeadDim, &L.k_norm, "k_norm"))) return rc;
-    if ((rc = upload_linear(h, {{&s.q_proj, qd}, {&s.k_proj, kvd}, {&s.v_proj, kvd}}, H, L.qkv, "qkv"))) return rc;
-    if ((rc = upload_linear(h, {{&s.o_proj, H}}, qd, L.o, "o_proj"))) return rc;
-    if ((rc = upload_linear(h, {{&s.gate_proj, I}, {&s.up_proj, I}}, H, L.gate_up, "gate_up"))) return rc;
-    if ((rc = upload_linear(h, {{&s.down_proj, H}}, I, L.down, "down_proj"))) return rc;
+    if ((rc = upload_linear(h, {{&s.q_proj, qd}, {&s.k_proj, kvd}, {&s.v_proj, kvd}}, H, L.qkv, "qkv", kGemvQkv))) return rc;
+    if ((rc = upload_linear(h, {{&s.o_proj, H}}, qd, L.o, "o_proj", kGemvResid))) return rc;
+    if ((rc = upload_linear(h, {{&s.gate_proj, I}, {&s.up_proj, I}}, H, L.gate_up, "gate_up", kGemvSwiglu, true))) return rc;
+    if ((rc = upload_linear(h, {{&s.down_proj, H}}, I, L.down, "down_proj", kGemvResid))) return rc;
   }
   // lm_head: tied to the embedding unless given (qwen3.rs:366-372); in int8 it
   // is quantised from the source values (qwen3.rs:566-578).
   const fmd_tensor& head = w->lm_head.data ? w->lm_head : w->embed_tokens;
   if (!h->q8 && !w->lm_head.data) {
-    h->lm_head.N = c.vocab_size;
-    h->lm_head.K = H;
-    h->lm_head.q8 = false;
     h->lm_head.w = h->embed;
-    h->lm_head.split = 1;
+    if ((rc = upload_linear(h, {{&head, c.vocab_size}}, H, h->lm_head, "lm_head", kGemvLogits, false, false)))
+      return rc;
   } else {
-    if ((rc = upload_linear(h, {{&head, c.vocab_size}}, H, h->lm_head, "lm_head"))) return rc;
+    if ((rc = upload_linear(h, {{&head, c.vocab_size}}, H, h->lm_head, "lm_head", kGemvLogits))) return rc;
   }
   h->lm_head.split = 1;
   // RoPE tables (qwen3.rs:116-136): inv_freq in f64 -> f32, pos*inv_freq in
@@ -746,6 +882,12 @@ int fmd_kv_reserve(fmd_handle* h, int32_t max_slots, int64_t max_tokens_total, i
   h->logits = (float*)p;
   if ((rc = A((size_t)max_slots * 4, &p))) return rc;
   h->next_ids = (int*)p;
+  if ((rc = A((size_t)max_slots * (H / 64) * 4, &p))) return rc;
+  h->ssq = (float*)p;
+  if ((rc = A((size_t)max_slots * (V / 64) * 4, &p))) return rc;
+  h->best_val = (float*)p;
+  if ((rc = A((size_t)max_slots * (V / 64) * 4, &p))) return rc;
+  h->best_idx = (int*)p;
   if ((rc = A((size_t)max_slots * c.num_key_value_heads * 4, &p))) return rc;
   CK(cudaMemset(p, 0, (size_t)max_slots * c.num_key_value_heads * 4));
   h->attn_counters = (int*)p;
@@ -915,7 +1057,7 @@ int fmd_decode_step(fmd_handle* h, int32_t n, const int32_t* slots, const int32_
     order[i] = i;
   }
   if ((rc = hp.commit())) return rc;
-  run_forward(h, logits ? h->logits : nullptr, h->arena);
+  run_forward(h, logits ? h->logits : nullptr, h->arena, true);
   for (int i = 0; i < n; ++i) h->slot_len[slots[i]] += 1;
   return copy_outputs(h, n, order, logits, next_ids);
 }
@@ -979,8 +1121,9 @@ int fmd_engine_load(fmd_handle* h, const fmd_request* reqs, int32_t n_reqs, cons
 }
 
 namespace {
-EngineDev make_engine_dev(fmd_handle* h, int max_batch, int chunk) {
+EngineDev make_engine_dev(fmd_handle* h, int max_batch, int chunk, int allow_prefill = 1) {
   EngineDev e{};
+  e.allow_prefill = allow_prefill;
   e.n_reqs = h->eng_n_reqs;
   e.n_pages = h->n_pages;
   e.consume_only = 0;
@@ -1042,20 +1185,32 @@ int fmd_engine_start(fmd_handle* h, int32_t max_batch, int32_t prefill_chunk) {
   }
   if (!h->graph_exec || h->graph_batch != max_batch || h->graph_chunk != prefill_chunk) {
     release_graph(h);
-    const EngineDev e = make_engine_dev(h, max_batch, prefill_chunk);
-    cudaGraph_t g;
-    CK(cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal));
-    h->record_attn_events = true;
-    launch_schedule(e, h->stream);
-    run_forward(h, nullptr, h->eng_arena.p);
-    h->record_attn_events = false;
-    CK(cudaStreamEndCapture(h->stream, &g));
-    cudaError_t ie = cudaGraphInstantiate(&h->graph_exec, g, 0);
-    cudaGraphDestroy(g);
-    if (ie != cudaSuccess) return fail(h, FMD_EIO, std::string("graph instantiate: ") + cudaGetErrorString(ie));
+    // two step graphs: "M" may carry a prefill chunk (split-K projections),
+    // "D" is decode-only (fused decode projections, no prefill attention)
+    for (int mixed = 1; mixed >= 0; --mixed) {
+      const EngineDev e = make_engine_dev(h, max_batch, prefill_chunk, mixed);
+      cudaGraph_t g;
+      CK(cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeThreadLocal));
+      h->record_attn_events = true;
+      launch_schedule(e, h->stream);
+      if (mixed)
+        run_forward(h, nullptr, h->eng_arena.p);
+      else
+        run_forward(h, nullptr, h->eng_arena.p, true);
+      h->record_attn_events = false;
+      CK(cudaStreamEndCapture(h->stream, &g));
+      if (h->launch_refused) {
+        cudaGraphDestroy(g);
+        return sync_check(h);
+      }
+      cudaError_t ie = cudaGraphInstantiate(mixed ? &h->graph_exec : &h->graph_dec, g, 0);
+      cudaGraphDestroy(g);
+      if (ie != cudaSuccess) return fail(h, FMD_EIO, std::string("graph instantiate: ") + cudaGetErrorString(ie));
+    }
     h->graph_batch = max_batch;
     h->graph_chunk = prefill_chunk;
   }
+  h->first_block = true;
   h->engine_started = true;
   return FMD_OK;
 }
@@ -1063,7 +1218,8 @@ int fmd_engine_start(fmd_handle* h, int32_t max_batch, int32_t prefill_chunk) {
 int fmd_engine_step(fmd_handle* h, int64_t max_steps, fmd_stats* stats) {
   int rc = check_ready(h);
   if (rc) return rc;
-  if (!h->engine_started || !h->graph_exec) return fail(h, FMD_EBUSY, "engine not started (fmd_engine_start)");
+  if (!h->engine_started || !h->graph_exec || !h->graph_dec)
+    return fail(h, FMD_EBUSY, "engine not started (fmd_engine_start)");
   if (max_steps < 0) return fail(h, FMD_EINVAL, "negative step count");
   CK(cudaSetDevice(h->device));
   const auto t0 = std::chrono::steady_clock::now();
@@ -1075,10 +1231,19 @@ int fmd_engine_step(fmd_handle* h, int64_t max_steps, fmd_stats* stats) {
   long long last_progress = -1;
   int idle_checks = 0;
   CK(cudaEventRecord(h->win_begin, h->stream));
+  int64_t mixed_launched = 0;
   while (!finished && launched < max_steps) {
     const int64_t k = std::min<int64_t>(kEngineCheckEvery, max_steps - launched);
-    for (int64_t i = 0; i < k; ++i) CK(cudaGraphLaunch(h->graph_exec, h->stream));
+    // Steps that may carry a prefill chunk ("M") first, as many as the prompt
+    // rows pending at the last poll need, then decode-only steps ("D").
+    // Before the first poll everything admitted is still to be prefilled.
+    int64_t n_m = k;
+    if (!h->first_block)
+      n_m = std::min<int64_t>(k, (h->h_ctr->pending_prefill + h->graph_chunk - 1) / h->graph_chunk);
+    for (int64_t i = 0; i < k; ++i) CK(cudaGraphLaunch(i < n_m ? h->graph_exec : h->graph_dec, h->stream));
     launched += k;
+    mixed_launched += n_m;
+    h->first_block = false;
     CK(cudaMemcpyAsync(h->h_ctr, h->eng_ctr, sizeof(EngineCounters), cudaMemcpyDeviceToHost, h->stream));
     if ((rc = sync_check(h))) return rc;
     finished = h->h_ctr->done >= h->eng_n_reqs;
@@ -1127,6 +1292,7 @@ int fmd_engine_step(fmd_handle* h, int64_t max_steps, fmd_stats* stats) {
     stats->attn_decode_ms = attn_ms;
     stats->attn_kv_tokens = kv_last;
     stats->attn_rows = rows_last;
+    stats->window_mixed_steps = mixed_launched;
   }
   return FMD_OK;
 }
@@ -1182,6 +1348,13 @@ int fmd_debug_weight(fmd_handle* h, int32_t layer, int32_t which, float* out, in
   cudaError_t e2 = cudaStreamSynchronize(h->stream);
   cudaFree(d);
   if (e != cudaSuccess || e2 != cudaSuccess) return fail(h, FMD_EIO, "dequant copy failed");
+  if (which == 2) {  // gate/up are stored interleaved in 32-row groups: restore [gate; up]
+    std::vector<float> tmp(out, out + n);
+    const int half = W->N / 2;
+    for (int r = 0; r < W->N; ++r)
+      std::memcpy(out + (size_t)r * W->K, tmp.data() + (size_t)((r / half) ? up_col(r % half) : gate_col(r % half)) * W->K,
+                  sizeof(float) * W->K);
+  }
   return FMD_OK;
 }
 

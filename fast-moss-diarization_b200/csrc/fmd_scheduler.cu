@@ -125,9 +125,11 @@ __global__ void __launch_bounds__(256) k_schedule(EngineDev e) {
     const int n_decode = rows;
     c->last_kv_tokens = kv_tokens;
     c->last_decode_rows = n_decode;
-    int budget_rows = e.prefill_chunk;
+    int budget_rows = e.allow_prefill ? e.prefill_chunk : 0;
+    long long pending = 0;
     for (int s = 0; s < e.max_batch; ++s) {
       if (e.slot_state[s] != kSlotPrefill) continue;
+      pending += e.reqs[e.slot_req[s]].prompt_len - e.slot_pdone[s];
       const DevRequest rq = e.reqs[e.slot_req[s]];
       const int left = rq.prompt_len - e.slot_pdone[s];
       int take = left < budget_rows ? left : budget_rows;
@@ -145,7 +147,9 @@ __global__ void __launch_bounds__(256) k_schedule(EngineDev e) {
       pblocks += (take + kRowsPerPBlock - 1) / kRowsPerPBlock;
       budget_rows -= take;
       c->prefill_tokens += take;
+      pending -= take;
     }
+    c->pending_prefill = pending;
     s_n_rows = rows;
     s_n_decode = n_decode;
     s_n_sample = samples;

@@ -31,12 +31,14 @@ struct EngineCounters {
   long long prefill_tokens;
   long long last_kv_tokens;    // sum of (pos + 1) over the decode rows of the latest plan
   long long last_decode_rows;
+  long long pending_prefill;   // prompt rows admitted but not yet planned
 };
 
 struct EngineDev {
   int n_reqs;
   int n_pages;         // pages in the pool
   int consume_only;    // book the previous samples, plan nothing
+  int allow_prefill;   // 0: plan decode rows only (decode-only step graph)
   int max_batch;       // slots in use (<= reserved slots)
   int prefill_chunk;   // prompt rows admitted per step
   int max_rows;        // plan capacity R

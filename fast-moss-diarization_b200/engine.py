@@ -44,6 +44,7 @@ class BatchStats:
     attn_decode_ms: float = 0.0
     attn_kv_tokens: int = 0
     attn_rows: int = 0
+    window_mixed_steps: int = 0
 
     @classmethod
     def from_c(cls, st) -> "BatchStats":
@@ -52,7 +53,7 @@ class BatchStats:
                    steps=int(st.steps), device_status=int(st.device_status), window_steps=int(st.window_steps),
                    window_tokens=int(st.window_tokens), window_device_ms=float(st.window_device_ms),
                    attn_decode_ms=float(st.attn_decode_ms), attn_kv_tokens=int(st.attn_kv_tokens),
-                   attn_rows=int(st.attn_rows))
+                   attn_rows=int(st.attn_rows), window_mixed_steps=int(st.window_mixed_steps))
 
     @property
     def decode_tokens_per_second(self) -> float:

@@ -139,6 +139,7 @@ typedef struct fmd_stats {
   double attn_decode_ms;    /* mean duration of one launch                       */
   int64_t attn_kv_tokens;   /* sum of key positions read by one launch           */
   int64_t attn_rows;        /* decode rows in that step                          */
+  int64_t window_mixed_steps; /* steps of the window that could carry prefill rows */
 } fmd_stats;
 
 /* ---- handle ------------------------------------------------------------- */
