@@ -7,6 +7,7 @@
 #include <stdint.h>
 
 #define FMD_DEV __device__ __forceinline__
+#define FMD_HD __host__ __device__ __forceinline__
 
 namespace fmd {
 
@@ -17,6 +18,7 @@ constexpr int kQ8Block = 32;      // GGML Q8_0 block length along the input axis
 // ---- activation dtype traits ------------------------------------------------
 template <typename T> struct Act;
 template <> struct Act<__nv_bfloat16> {
+  static constexpr bool kIsBf16 = true;
   static FMD_DEV float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
   static FMD_DEV __nv_bfloat16 from_f(float x) { return __float2bfloat16_rn(x); }
   static FMD_DEV uint32_t pack2(float lo, float hi) {
@@ -29,6 +31,7 @@ template <> struct Act<__nv_bfloat16> {
   }
 };
 template <> struct Act<__half> {
+  static constexpr bool kIsBf16 = false;
   static FMD_DEV float to_f(__half x) { return __half2float(x); }
   static FMD_DEV __half from_f(float x) { return __float2half_rn(x); }
   static FMD_DEV uint32_t pack2(float lo, float hi) {
@@ -167,5 +170,71 @@ FMD_DEV void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar
 }
 // Named barrier over `nthreads` threads (a subset of the CTA).
 FMD_DEV void named_sync(int id, int nthreads) { asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(nthreads) : "memory"); }
+
+// ---- tcgen05 (5th-generation tensor cores, accumulators in tensor memory) ----------
+// Tensor memory: 512 columns x 128 lanes of 32 bits per SM. A warp may only
+// touch the 32 lanes of its quarter (warp id % 4).
+
+// Allocates `ncols` (a power of two >= 32) columns; the base address is
+// written to *dst (shared memory). Executed by one whole warp.
+FMD_DEV void tmem_alloc(uint32_t* dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(dst)), "r"(ncols)
+               : "memory");
+}
+FMD_DEV void tmem_relinquish() { asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory"); }
+FMD_DEV void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// Order tcgen05 operations around a thread synchronisation (barrier,
+// mbarrier wait): "before" ahead of the signal, "after" behind the wait.
+FMD_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
+FMD_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
+
+// Shared-memory matrix descriptor of a K-major operand tile stored with the
+// 128-byte swizzle (rows of 128 bytes, 8-row atoms 1024 bytes apart, the tile
+// 1024-byte aligned): start address >> 4 in bits 0-13, leading byte offset
+// (unused by swizzled K-major layouts, 16 bytes) in 16-29, stride byte offset
+// 1024 >> 4 in 32-45, descriptor version 1 in 46-47, swizzle mode 2
+// (128-byte) in 61-63. Advancing along K inside the 128-byte row adds the
+// byte offset to the start address; the swizzle applies to absolute address
+// bits, hence the alignment.
+FMD_DEV uint64_t umma_desc_sw128(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+// Instruction descriptor of kind::f16 with f32 accumulation, A and B both
+// K-major and both f16 (bf16 = false) or both bf16: D format in bits 4-5,
+// A / B format in 7-9 / 10-12, N >> 3 in 17-22, M >> 4 in 24-28.
+FMD_HD constexpr uint32_t umma_idesc_f16(bool bf16, int M, int N) {
+  return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) | ((uint32_t)(N >> 3) << 17) |
+         ((uint32_t)(M >> 4) << 24);
+}
+// D[tmem] (+)= A[smem] x B[smem]^T, one instruction of K = 16; issued by one thread.
+FMD_DEV void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, bool accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"((uint32_t)accumulate)
+      : "memory");
+}
+// Arrive once on `bar` when every MMA this thread issued so far has completed.
+FMD_DEV void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(smem_u32(bar))
+               : "memory");
+}
+// 32 consecutive columns of this warp's 32 lanes: register i = column i of the
+// thread's lane. Followed by tmem_ld_wait() before the registers are read.
+FMD_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
+FMD_DEV void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
 
 }  // namespace fmd

@@ -371,7 +371,9 @@ __global__ void __launch_bounds__(FW * 32) k_gemv(const T* __restrict__ x, int l
 }
 
 // lm_head + greedy candidates as one persistent kernel (qwen3.rs:459-463,
-// engine.rs:550-559). The vocabulary projection is the largest weight of a
+// engine.rs:550-559). The final RMSNorm is applied to the staged rows from
+// the per-tile sums of squares (ep.ssq), or skipped when ep.ssq is null and
+// the rows are already normalised. The vocabulary projection is the largest weight of a
 // decode step (vocab x hidden) and the only one with more 128-feature tiles
 // than there are SMs, so here one CTA per SM keeps the normalised activation
 // tile resident and streams its share of tiles through a ring of TMA bulk
@@ -463,7 +465,8 @@ __global__ void __launch_bounds__((kHeadWarps + 1) * 32) k_lm_head(const T* __re
     cp_async16(xs + (size_t)r * xstride + ch * 8, src, bytes);
   }
   cp_async_commit();
-  for (int r = threadIdx.x; r < rows; r += NT) {
+  const bool norm = ep.ssq != nullptr;  // else x is already normalised
+  for (int r = threadIdx.x; norm && r < rows; r += NT) {
     const int gr = row_map ? row_map[row0 + r] : row0 + r;
     const float* sp = ep.ssq + (size_t)gr * ep.ssq_tiles;
     float ss = 0.f;
@@ -472,7 +475,7 @@ __global__ void __launch_bounds__((kHeadWarps + 1) * 32) k_lm_head(const T* __re
   }
   cp_async_wait<0>();
   named_sync(1, NT);
-  {
+  if (norm) {
     const T* nw = reinterpret_cast<const T*>(ep.norm_w);
     for (int c = threadIdx.x; c < rows * cpr; c += NT) {
       const int r = c / cpr, ch = c - r * cpr;
@@ -854,7 +857,9 @@ int launch_lm_head(ActType at, const LinW& W, const void* x, int ldx, const int*
     parts = W.q8 ? launch_lm_head_t<__half, true>(W, x, ldx, row_map, n_rows_ptr, max_rows, ep, status, s)
                  : launch_lm_head_t<__half, false>(W, x, ldx, row_map, n_rows_ptr, max_rows, ep, status, s);
   if (parts > 0) return parts;
-  // activation tile too large for the resident kernel: the cluster GEMV
+  // activation tile too large for the resident kernel: the cluster GEMV,
+  // which normalises on the fly and so needs the sums of squares
+  if (ep.ssq == nullptr) return 0;
   return launch_gemv(at, kGemvLogits, true, W, x, ldx, row_map, n_rows_ptr, max_rows, ep, status, s)
              ? W.N / gemv_tile_features(kGemvLogits)
              : 0;

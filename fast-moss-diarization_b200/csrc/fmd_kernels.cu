@@ -86,14 +86,14 @@ __global__ void __launch_bounds__(128) k_embed_norm(Plan p, const T* __restrict_
 // ---------------------------------------------------------------------------
 template <typename T>
 __global__ void __launch_bounds__(128) k_residual_norm(const int* __restrict__ n_rows_ptr, T* __restrict__ x,
-                                                       const float* __restrict__ part, int split,
+                                                       const float* __restrict__ part, PartSplit split,
                                                        size_t split_stride, const T* __restrict__ w,
                                                        T* __restrict__ xn, int H, float eps) {
   __shared__ float red[4];
   griddep_launch();
   griddep_wait();
   const int n_rows = *n_rows_ptr;
-  const int S = effective_split(split, n_rows);
+  const int S = split.at(n_rows);
   for (int r = blockIdx.x; r < n_rows; r += gridDim.x) {
   T* xr = x + (size_t)r * H;
   float ss = 0.f;
@@ -333,7 +333,7 @@ __global__ void __launch_bounds__(128) k_linear(const T* __restrict__ x, int ldx
 // lanes away.
 // ---------------------------------------------------------------------------
 template <typename T>
-__global__ void __launch_bounds__(256) k_qkv_epilogue(Plan p, const float* __restrict__ part, int split,
+__global__ void __launch_bounds__(256) k_qkv_epilogue(Plan p, const float* __restrict__ part, PartSplit split,
                                                       size_t split_stride, int Hq, int Hkv,
                                                       const T* __restrict__ qn_w, const T* __restrict__ kn_w,
                                                       const T* __restrict__ cos_t, const T* __restrict__ sin_t,
@@ -341,7 +341,7 @@ __global__ void __launch_bounds__(256) k_qkv_epilogue(Plan p, const float* __res
   griddep_launch();
   griddep_wait();
   const int n_rows = p.counts->n_rows;
-  const int S = effective_split(split, n_rows);
+  const int S = split.at(n_rows);
   const int N = (Hq + 2 * Hkv) * kHeadDim;
   for (int r = blockIdx.x; r < n_rows; r += gridDim.x) {
   const int pos = p.row_pos[r], slot = p.row_slot[r];
@@ -561,11 +561,11 @@ __global__ void __launch_bounds__(128) k_attn_prefill(Plan p, int Hq, const T* _
 // ---------------------------------------------------------------------------
 template <typename T>
 __global__ void __launch_bounds__(256) k_silu_mul(const int* __restrict__ n_rows_ptr, const float* __restrict__ part,
-                                                  int split, size_t split_stride, int I, T* __restrict__ h) {
+                                                  PartSplit split, size_t split_stride, int I, T* __restrict__ h) {
   griddep_launch();
   griddep_wait();
   const int n_rows = *n_rows_ptr;
-  const int S = effective_split(split, n_rows);
+  const int S = split.at(n_rows);
   for (int r = blockIdx.x; r < n_rows; r += gridDim.x) {
   const float* p0 = part + (size_t)r * 2 * I;
   for (int c = threadIdx.x * 4; c < I; c += blockDim.x * 4) {
@@ -691,7 +691,7 @@ void launch_linear(ActType at, const LinW& W, const void* x, int ldx, const int*
   });
 }
 
-void launch_qkv_epilogue(ActType at, const Plan& p, int R, const float* part, int split, size_t split_stride,
+void launch_qkv_epilogue(ActType at, const Plan& p, int R, const float* part, PartSplit split, size_t split_stride,
                          int Hq, int Hkv, const void* qn_w, const void* kn_w, const void* cos, const void* sin,
                          void* q_out, const KvView& kv, int layer, float eps, cudaStream_t s) {
   FMD_DISPATCH(at, launch_pdl(k_qkv_epilogue<T>, R, 256, 0, s, p, part, split, split_stride, Hq, Hkv, (const T*)qn_w,
@@ -707,13 +707,13 @@ void launch_attn_prefill(ActType at, const Plan& p, int PB, int Hq, int Hkv, con
   FMD_DISPATCH(at, launch_pdl(k_attn_prefill<T>, grid, 128, smem, s, p, Hq, (const T*)q, kv, layer, scale_log2, (T*)ctx));
 }
 
-void launch_residual_norm(ActType at, const int* n_rows_ptr, int R, void* x, const float* part, int split,
+void launch_residual_norm(ActType at, const int* n_rows_ptr, int R, void* x, const float* part, PartSplit split,
                           size_t split_stride, const void* w, void* xn, int H, float eps, cudaStream_t s) {
   FMD_DISPATCH(at, launch_pdl(k_residual_norm<T>, R, 128, 0, s, n_rows_ptr, (T*)x, part, split, split_stride, (const T*)w,
                                                          (T*)xn, H, eps));
 }
 
-void launch_silu_mul(ActType at, const int* n_rows_ptr, int R, const float* part, int split, size_t split_stride,
+void launch_silu_mul(ActType at, const int* n_rows_ptr, int R, const float* part, PartSplit split, size_t split_stride,
                      int I, void* h, cudaStream_t s) {
   FMD_DISPATCH(at, launch_pdl(k_silu_mul<T>, R, 256, 0, s, n_rows_ptr, part, split, split_stride, I, (T*)h));
 }

@@ -4,6 +4,8 @@
 
 #include <utility>
 
+#include <cuda.h>
+
 #include "fmd_common.cuh"
 
 namespace fmd {
@@ -143,6 +145,16 @@ struct GemvEpi {
 // Device-side K split actually used for a pass with `n_rows` rows.
 __host__ __device__ inline int effective_split(int split, int n_rows) { return n_rows <= 64 ? split : 1; }
 
+// How many K-split partials a projection left in the f32 buffer, by pass
+// size: k_linear splits only passes of <= 64 rows (effective_split), the
+// tensor-core GEMM splits every pass.
+struct PartSplit {
+  int small = 1;  // passes of <= 64 rows
+  int large = 1;  // larger passes
+  __host__ __device__ int at(int n_rows) const { return n_rows <= 64 ? small : large; }
+};
+inline PartSplit linear_split(int split) { return PartSplit{split, 1}; }
+
 enum ActType { kBF16 = 0, kF16 = 1 };
 
 // Launch with programmatic stream serialisation, so that inside a step (and
@@ -170,14 +182,14 @@ void launch_embed_norm(ActType at, const Plan& p, int R, const void* table, cons
 // split is known before the plan is read and weights are prefetched early.
 void launch_linear(ActType at, const LinW& W, const void* x, int ldx, const int* row_map, const int* n_rows_ptr,
                    int max_rows, float* out, size_t split_stride, bool decode_only, cudaStream_t s);
-void launch_qkv_epilogue(ActType at, const Plan& p, int R, const float* part, int split, size_t split_stride,
+void launch_qkv_epilogue(ActType at, const Plan& p, int R, const float* part, PartSplit split, size_t split_stride,
                          int Hq, int Hkv, const void* qn_w, const void* kn_w, const void* cos, const void* sin,
                          void* q_out, const KvView& kv, int layer, float eps, cudaStream_t s);
 void launch_attn_prefill(ActType at, const Plan& p, int PB, int Hq, int Hkv, const void* q, const KvView& kv,
                          int layer, float scale, void* ctx, cudaStream_t s);
-void launch_residual_norm(ActType at, const int* n_rows_ptr, int R, void* x, const float* part, int split,
+void launch_residual_norm(ActType at, const int* n_rows_ptr, int R, void* x, const float* part, PartSplit split,
                           size_t split_stride, const void* w, void* xn, int H, float eps, cudaStream_t s);
-void launch_silu_mul(ActType at, const int* n_rows_ptr, int R, const float* part, int split, size_t split_stride,
+void launch_silu_mul(ActType at, const int* n_rows_ptr, int R, const float* part, PartSplit split, size_t split_stride,
                      int I, void* h, cudaStream_t s);
 void launch_logits_argmax(ActType at, const int* n_sample_ptr, int B, const float* part, int V, float* logits,
                           int* next_ids, cudaStream_t s);
@@ -212,5 +224,23 @@ cudaError_t init_attn_decode();
 void launch_attn_decode_tma(ActType at, const void* tmap, const Plan& p, int grid, int Hq, int Hkv, const void* q,
                             const KvView& kv, int layer, float scale, float* part_acc, float* part_ml, int* counters,
                             void* ctx, int* status, cudaStream_t s);
+
+// ---- tensor-core projections of mixed steps (fmd_gemm_tc.cu) ----
+// W [N][K] 16-bit behind a TMA map with box {64, bn} and the 128-byte
+// swizzle; the output goes to out[split][rows][N] (f32).
+struct TcLinear {
+  alignas(64) CUtensorMap wmap;
+  int N = 0, K = 0, bn = 0, split = 1;
+  bool ok = false;
+};
+cudaError_t init_gemm_tc();
+// Tile width and K split for an N x K projection (false: not supported).
+bool tc_plan(int N, int K, int* bn, int* split);
+// 2D map over a row-major [outer][inner] 16-bit matrix, box {64, box_outer}.
+bool tc_make_map(void* encode_fn, CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer,
+                 uint32_t box_outer);
+// false (nothing launched) if W has no tensor-core plan.
+bool launch_gemm_tc(ActType at, const CUtensorMap& amap, const TcLinear& W, const int* n_rows_ptr, int max_rows,
+                    float* out, size_t split_stride, int* status, cudaStream_t s);
 
 }  // namespace fmd

@@ -48,6 +48,7 @@ struct LayerDev {
   void* q_norm = nullptr;
   void* k_norm = nullptr;
   LinW qkv, o, gate_up, down;
+  TcLinear tc_qkv, tc_o, tc_gate_up, tc_down;  // the same projections for mixed steps (tcgen05)
 };
 
 uint16_t f32_to_bf16_bits(float f) {
@@ -122,6 +123,10 @@ struct fmd_handle {
   int pb_max = 0, di_max = 0, di_grid = 0, pb_grid = 0;
   KvView kv{};
   alignas(64) CUtensorMap kv_tmap;  // the KV pool as [rows][128] for TMA tile loads
+  // activation operands of the mixed-step tensor-core projections
+  alignas(64) CUtensorMap amap_xn, amap_ctx, amap_hbuf;
+  bool tc_ready = false;
+  void* tmap_encode = nullptr;      // cuTensorMapEncodeTiled
   int* attn_counters = nullptr;     // [max_slots][kv_heads] split-KV merge counters
   int* d_status = nullptr;          // device-side error status (bounded waits)
   bool launch_refused = false;      // a decode projection could not be launched
@@ -256,8 +261,41 @@ void interleave_rows(std::vector<E>& m, int N, int cols) {
 // decode-packed tiles of the decode-step GEMV whose epilogue is `epi`.
 // `row_major` false: only the packed copy (W.w is set by the caller, as for
 // a 16-bit lm_head tied to the embedding table).
+// cuTensorMapEncodeTiled, looked up once through the runtime's driver entry point.
+int tmap_encoder(fmd_handle* h, void** fn) {
+  if (h->tmap_encode == nullptr) {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult qr;
+    CK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &qr));
+    if (f == nullptr || qr != cudaDriverEntryPointSuccess)
+      return fail(h, FMD_EIO, "cuTensorMapEncodeTiled is unavailable in this driver");
+    h->tmap_encode = f;
+  }
+  *fn = h->tmap_encode;
+  return FMD_OK;
+}
+
+// Tensor-core plan and weight map of one projection; a shape without a plan
+// keeps tc->ok false and mixed steps use k_linear for it.
+int tc_prepare(fmd_handle* h, const void* w16, int N, int K, TcLinear* tc) {
+  tc->N = N;
+  tc->K = K;
+  tc->ok = false;
+  if (!tc_plan(N, K, &tc->bn, &tc->split)) return FMD_OK;
+  void* fn;
+  int rc = tmap_encoder(h, &fn);
+  if (rc) return rc;
+  if (!tc_make_map(fn, &tc->wmap, w16, (uint64_t)K, (uint64_t)N, (uint32_t)tc->bn))
+    return fail(h, FMD_EIO, "tensor map of a projection's weights could not be encoded");
+  tc->ok = true;
+  return FMD_OK;
+}
+
+// `tc`: also build the tensor-core operand of mixed steps (the 16-bit [N][K]
+// matrix: the dense weights themselves, or the Q8_0 weights' expansion).
 int upload_linear(fmd_handle* h, const std::vector<std::pair<const fmd_tensor*, int>>& parts, int K, LinW& W,
-                  const char* what, int epi, bool interleave16 = false, bool row_major = true) {
+                  const char* what, int epi, bool interleave16 = false, bool row_major = true,
+                  TcLinear* tc = nullptr) {
   int N = 0;
   for (auto& p : parts) N += p.second;
   if (N % 64 || K % 64) return fail(h, FMD_ENOTSUP, std::string(what) + ": dims must be multiples of 64");
@@ -294,6 +332,7 @@ int upload_linear(fmd_handle* h, const std::vector<std::pair<const fmd_tensor*, 
     if ((rc = dev_alloc(h, pk.size(), &d, &h->weight_bytes))) return rc;
     if ((rc = upload(h, d, pk.data(), pk.size()))) return rc;
     W.pk = (const uint8_t*)d;
+    if (tc && (rc = tc_prepare(h, W.w, N, K, tc))) return rc;
   } else {
     std::vector<int8_t> qs((size_t)N * K);
     std::vector<uint16_t> sc((size_t)N * (K / 32));
@@ -335,6 +374,22 @@ int upload_linear(fmd_handle* h, const std::vector<std::pair<const fmd_tensor*, 
     if ((rc = dev_alloc(h, pk.size(), &dp, &h->weight_bytes))) return rc;
     if ((rc = upload(h, dp, pk.data(), pk.size()))) return rc;
     W.pk = (const uint8_t*)dp;
+    if (tc) {
+      // dequantised values, rounded to the activation type as the kernels
+      // dequantise them (q * scale is exact in f32)
+      const bool bf = h->at == kBF16;
+      std::vector<uint16_t> wx((size_t)N * K);
+      for (size_t r = 0; r < (size_t)N; ++r)
+        for (int k = 0; k < K; ++k) {
+          const float d = f16_bits_to_f32(sc[r * (K / 32) + k / 32]);
+          const float v = (float)qs[r * K + k] * d;
+          wx[r * K + k] = bf ? f32_to_bf16_bits(v) : f32_to_f16_bits(v);
+        }
+      void* dw;
+      if ((rc = dev_alloc(h, wx.size() * 2, &dw, &h->weight_bytes))) return rc;
+      if ((rc = upload(h, dw, wx.data(), wx.size() * 2))) return rc;
+      if ((rc = tc_prepare(h, dw, N, K, tc))) return rc;
+    }
   }
   // K split for passes with <= 64 rows: aim for >= ~2 CTAs per SM.
   int split = 1;
@@ -443,6 +498,19 @@ void run_forward_decode(fmd_handle* h, float* logits_dev, const void* arena) {
   trace(h, "argmax", -1);
 }
 
+// One projection of a mixed step over all of its rows: tcgen05 GEMM when the
+// projection has a tensor-core plan, else k_linear. Returns the K splits the
+// f32 partials in h->part carry.
+PartSplit mixed_linear(fmd_handle* h, const LinW& W, const TcLinear& tc, const void* x, const CUtensorMap& amap,
+                       int ldx) {
+  if (h->tc_ready && launch_gemm_tc(h->at, amap, tc, &h->plan.counts->n_rows, h->max_rows, h->part, h->split_stride,
+                                    h->d_status, h->stream))
+    return PartSplit{tc.split, tc.split};
+  launch_linear(h->at, W, x, ldx, nullptr, &h->plan.counts->n_rows, h->max_rows, h->part, h->split_stride, false,
+                h->stream);
+  return linear_split(W.split);
+}
+
 // `decode_only`: every row is a one-token decode row (no prefill attention,
 // weights prefetched ahead of each projection's dependency wait).
 void run_forward(fmd_handle* h, float* logits_dev, const void* arena, bool decode_only = false) {
@@ -463,9 +531,9 @@ void run_forward(fmd_handle* h, float* logits_dev, const void* arena, bool decod
   trace(h, "embed_norm", -1);
   for (int l = 0; l < c.num_hidden_layers; ++l) {
     const LayerDev& L = h->layers[l];
-    launch_linear(h->at, L.qkv, h->xn, H, nullptr, nrows, R, h->part, ss, decode_only, s);
+    const PartSplit sp_qkv = mixed_linear(h, L.qkv, L.tc_qkv, h->xn, h->amap_xn, H);
     trace(h, "qkv", l);
-    launch_qkv_epilogue(h->at, h->plan, row_grid, h->part, L.qkv.split, ss, h->Hq(), h->Hkv(), L.q_norm, L.k_norm,
+    launch_qkv_epilogue(h->at, h->plan, row_grid, h->part, sp_qkv, ss, h->Hq(), h->Hkv(), L.q_norm, L.k_norm,
                         h->rope_cos, h->rope_sin, h->qbuf, h->kv, l, eps, s);
     trace(h, "qkv_epi", l);
     if (h->record_attn_events) cudaEventRecordWithFlags(h->attn_events[2 * l], s, cudaEventRecordExternal);
@@ -478,23 +546,34 @@ void run_forward(fmd_handle* h, float* logits_dev, const void* arena, bool decod
                           s);
       trace(h, "attn_prefill", l);
     }
-    launch_linear(h->at, L.o, h->ctx, h->Hq() * kHeadDim, nullptr, nrows, R, h->part, ss, decode_only, s);
+    const PartSplit sp_o = mixed_linear(h, L.o, L.tc_o, h->ctx, h->amap_ctx, h->Hq() * kHeadDim);
     trace(h, "o_proj", l);
-    launch_residual_norm(h->at, nrows, row_grid, h->x, h->part, L.o.split, ss, L.post_norm, h->xn, H, eps, s);
+    launch_residual_norm(h->at, nrows, row_grid, h->x, h->part, sp_o, ss, L.post_norm, h->xn, H, eps, s);
     trace(h, "res_norm1", l);
-    launch_linear(h->at, L.gate_up, h->xn, H, nullptr, nrows, R, h->part, ss, decode_only, s);
+    const PartSplit sp_gu = mixed_linear(h, L.gate_up, L.tc_gate_up, h->xn, h->amap_xn, H);
     trace(h, "gate_up", l);
-    launch_silu_mul(h->at, nrows, row_grid, h->part, L.gate_up.split, ss, I, h->hbuf, s);
+    launch_silu_mul(h->at, nrows, row_grid, h->part, sp_gu, ss, I, h->hbuf, s);
     trace(h, "silu", l);
-    launch_linear(h->at, L.down, h->hbuf, I, nullptr, nrows, R, h->part, ss, decode_only, s);
+    const PartSplit sp_down = mixed_linear(h, L.down, L.tc_down, h->hbuf, h->amap_hbuf, I);
     trace(h, "down", l);
     const void* next_norm = l + 1 < c.num_hidden_layers ? h->layers[l + 1].in_norm : h->final_norm;
-    launch_residual_norm(h->at, nrows, row_grid, h->x, h->part, L.down.split, ss, next_norm, h->xn, H, eps, s);
+    launch_residual_norm(h->at, nrows, row_grid, h->x, h->part, sp_down, ss, next_norm, h->xn, H, eps, s);
     trace(h, "res_norm2", l);
   }
-  launch_linear(h->at, h->lm_head, h->xn, H, h->plan.sample_row, nsamp, h->max_slots, h->part, ss, decode_only, s);
+  // the rows are normalised already (the last residual_norm applied the final norm)
+  GemvEpi head{};
+  head.logits = logits_dev;
+  head.best_val = h->best_val;
+  head.best_idx = h->best_idx;
+  const int parts = launch_lm_head(h->at, h->lm_head, h->xn, H, h->plan.sample_row, nsamp, h->max_slots, head,
+                                   h->d_status, s);
   trace(h, "lm_head", -1);
-  launch_logits_argmax(h->at, nsamp, h->max_slots, h->part, c.vocab_size, logits_dev, h->next_ids, s);
+  if (parts > 0) {
+    launch_pick_reduce(nsamp, h->max_slots, h->best_val, h->best_idx, parts, h->next_ids, s);
+  } else {
+    launch_linear(h->at, h->lm_head, h->xn, H, h->plan.sample_row, nsamp, h->max_slots, h->part, ss, decode_only, s);
+    launch_logits_argmax(h->at, nsamp, h->max_slots, h->part, c.vocab_size, logits_dev, h->next_ids, s);
+  }
   trace(h, "argmax", -1);
 }
 
@@ -696,7 +775,8 @@ int fmd_create(const fmd_config* cfg, int32_t precision, int32_t device, fmd_han
   h->device = device;
   h->attn_scale = (float)(1.0 / std::sqrt((double)cfg->head_dim));
   if (cudaSetDevice(device) != cudaSuccess || cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking) != cudaSuccess ||
-      init_kernels() != cudaSuccess || init_attn_decode() != cudaSuccess || init_gemv() != cudaSuccess) {
+      init_kernels() != cudaSuccess || init_attn_decode() != cudaSuccess || init_gemv() != cudaSuccess ||
+      init_gemm_tc() != cudaSuccess) {
     cudaGetLastError();
     delete h;
     return FMD_EIO;
@@ -741,10 +821,14 @@ int fmd_load_weights(fmd_handle* h, const fmd_weights* w) {
     if ((rc = upload_dense(h, s.post_attention_layernorm, H, &L.post_norm, "post_attention_layernorm"))) return rc;
     if ((rc = upload_dense(h, s.q_norm, kHeadDim, &L.q_norm, "q_norm"))) return rc;
     if ((rc = upload_dense(h, s.k_norm, kHeadDim, &L.k_norm, "k_norm"))) return rc;
-    if ((rc = upload_linear(h, {{&s.q_proj, qd}, {&s.k_proj, kvd}, {&s.v_proj, kvd}}, H, L.qkv, "qkv", kGemvQkv))) return rc;
-    if ((rc = upload_linear(h, {{&s.o_proj, H}}, qd, L.o, "o_proj", kGemvResid))) return rc;
-    if ((rc = upload_linear(h, {{&s.gate_proj, I}, {&s.up_proj, I}}, H, L.gate_up, "gate_up", kGemvSwiglu, true))) return rc;
-    if ((rc = upload_linear(h, {{&s.down_proj, H}}, I, L.down, "down_proj", kGemvResid))) return rc;
+    if ((rc = upload_linear(h, {{&s.q_proj, qd}, {&s.k_proj, kvd}, {&s.v_proj, kvd}}, H, L.qkv, "qkv", kGemvQkv, false, true, &L.tc_qkv)))
+      return rc;
+    if ((rc = upload_linear(h, {{&s.o_proj, H}}, qd, L.o, "o_proj", kGemvResid, false, true, &L.tc_o))) return rc;
+    if ((rc = upload_linear(h, {{&s.gate_proj, I}, {&s.up_proj, I}}, H, L.gate_up, "gate_up", kGemvSwiglu, true, true,
+                             &L.tc_gate_up)))
+      return rc;
+    if ((rc = upload_linear(h, {{&s.down_proj, H}}, I, L.down, "down_proj", kGemvResid, false, true, &L.tc_down)))
+      return rc;
   }
   // lm_head: tied to the embedding unless given (qwen3.rs:366-372); in int8 it
   // is quantised from the source values (qwen3.rs:566-578).
@@ -824,10 +908,7 @@ int fmd_kv_reserve(fmd_handle* h, int32_t max_slots, int64_t max_tokens_total, i
     const uint64_t rows = (uint64_t)c.num_hidden_layers * h->n_pages * 2 * c.num_key_value_heads * kPageTokens;
     if (rows > (uint64_t)INT32_MAX) return fail(h, FMD_ENOTSUP, "KV pool too large for 32-bit TMA row coordinates");
     void* fn = nullptr;
-    cudaDriverEntryPointQueryResult qr;
-    CK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &qr));
-    if (fn == nullptr || qr != cudaDriverEntryPointSuccess)
-      return fail(h, FMD_EIO, "cuTensorMapEncodeTiled is unavailable in this driver");
+    if ((rc = tmap_encoder(h, &fn))) return rc;
     auto encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
     const cuuint64_t dims[2] = {(cuuint64_t)kHeadDim, (cuuint64_t)rows};
     const cuuint64_t strides[1] = {(cuuint64_t)kHeadDim * 2};
@@ -852,8 +933,11 @@ int fmd_kv_reserve(fmd_handle* h, int32_t max_slots, int64_t max_tokens_total, i
   // work buffers
   const int R = h->max_rows;
   int max_split = 1;
-  for (auto& L : h->layers)
+  for (auto& L : h->layers) {
     for (const LinW* W : {&L.qkv, &L.o, &L.gate_up, &L.down}) max_split = std::max(max_split, W->split);
+    for (const TcLinear* W : {&L.tc_qkv, &L.tc_o, &L.tc_gate_up, &L.tc_down})
+      if (W->ok) max_split = std::max(max_split, W->split);
+  }
   const int Nmax = std::max({h->qkvN(), 2 * I, H});
   h->split_stride = (size_t)std::max(R, 64) * Nmax;
   const size_t part_elems = std::max({h->split_stride * max_split, (size_t)max_slots * V});
@@ -898,6 +982,14 @@ int fmd_kv_reserve(fmd_handle* h, int32_t max_slots, int64_t max_tokens_total, i
   if ((rc = A(h->layout.total * 4, &p))) return rc;
   CK(cudaMemset(p, 0, h->layout.total * 4));
   h->d_plan = (int*)p;
+  {
+    // activation operands of the tensor-core projections: 128-row boxes
+    void* fn = nullptr;
+    if ((rc = tmap_encoder(h, &fn))) return rc;
+    h->tc_ready = tc_make_map(fn, &h->amap_xn, h->xn, (uint64_t)H, (uint64_t)R, 128) &&
+                  tc_make_map(fn, &h->amap_ctx, h->ctx, (uint64_t)HqD, (uint64_t)R, 128) &&
+                  tc_make_map(fn, &h->amap_hbuf, h->hbuf, (uint64_t)I, (uint64_t)R, 128);
+  }
   h->plan = h->layout.bind(h->d_plan);
   CK(cudaMallocHost((void**)&h->h_plan, h->layout.total * 4));
   std::memset(h->h_plan, 0, h->layout.total * 4);
