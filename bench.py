@@ -49,10 +49,12 @@ METRIC = "decoded tokens/s per GPU (Q8_0, bf16) and % of HBM roofline; audio s/s
 UNIT = "tokens/s"
 PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
 TRAFFIC_FILE = ROOT / "profiles" / "attn_decode_config3.md"
-# kernels per engine step: scheduler + embed + per layer + lm_head/greedy; a step
-# that may carry prefill rows runs 11 kernels per layer, a decode-only step 7
-KERNELS_MIXED = lambda layers: 1 + 1 + 11 * layers + 2  # noqa: E731
-KERNELS_DECODE = lambda layers: 1 + 1 + 7 * layers + 2  # noqa: E731
+# kernels per engine step: scheduler + embed + per layer + lm_head and greedy
+# pick. A step that may carry prefill rows runs 10 per layer (4 tensor-core
+# projections, their 4 epilogues counting the two residual norms, decode and
+# prefill attention); a decode-only step 5 (4 fused GEMVs + decode attention).
+KERNELS_MIXED = lambda layers: 1 + 1 + 10 * layers + 2  # noqa: E731
+KERNELS_DECODE = lambda layers: 1 + 1 + 5 * layers + 2  # noqa: E731
 
 
 def parse_args():
@@ -88,7 +90,7 @@ class Dist:
             import torch.distributed as dist
 
             torch.cuda.set_device(self.local)
-            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                     device_id=torch.device("cuda", self.local))
             self.pg = dist
 
@@ -242,10 +244,21 @@ def cpu_sample(cfg, w, wl, seconds: float = 12.0, n_seq: int = 4, steps: int | N
             "seconds": el}
 
 
-def run_reference(args, dist: Dist):
+def workload_config(args, cfg, n_requests: int, world: int) -> dict:
+    """The `config` object both arms report."""
+    return {"workload": "BASELINE config 3: Q8_0 decoder + lm_head, bf16 activations, batch 32 "
+                        "continuous batching over a 256-request queue (prompts log-uniform 300-8000, "
+                        "geometric stops mean 600 cap 4096), on-GPU refill, 2048-row prefill chunks",
+            "requests_per_gpu": n_requests, "batch": args.batch, "prefill_chunk": args.chunk,
+            "layers": cfg.num_hidden_layers, "step": f"{args.window} device steps",
+            "l2": "working set >> L2 (no flush needed)",
+            "parallelism": f"dp{world} (request-sharded, no collective)"}
+
+
+def run_reference(args):
     """`--impl reference`: the reference's CPU path (restated) on a bounded
-    sample of the same workload; rank 0 only."""
-    if dist.rank != 0:
+    sample of the same workload; rank 0 alone, the other ranks exit at once."""
+    if int(os.environ.get("RANK", "0")) != 0:
         return
     pkg, cfg, w, wl = build_model_and_queue(args, 0)
     res = cpu_sample(cfg, w, wl, steps=max(args.steps, 1), warmup=max(args.warmup, 0), n_seq=4)
@@ -253,8 +266,8 @@ def run_reference(args, dist: Dist):
             "warmup": args.warmup, "ms_per_step": 1000.0 * res["seconds"] / max(args.steps, 1),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "impl": "reference",
-            "config": {"workload": "config3: Q8_0 decoder, batch-32 continuous batching, 256-request queue",
-                       "sample": "decode-only", "model": "qwen3-0.6B shape, random init"},
+            "config": dict(workload_config(args, cfg, len(wl.prompt_lens), args.gpus),
+                           sample="decode-only steps of 4 sequences (see cpu_baseline.sample)"),
             "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": res["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -262,13 +275,10 @@ def run_reference(args, dist: Dist):
 
 def main():
     args = parse_args()
-    dist = Dist()
     if args.impl == "reference":
-        try:
-            run_reference(args, dist)
-        finally:
-            dist.close()
+        run_reference(args)  # host cores only: no process group
         return
+    dist = Dist()
 
     pkg, cfg, w, wl = build_model_and_queue(args, dist.rank)
     dec = pkg.Qwen3Decoder(cfg, wl.precision, device=dist.local)
@@ -352,13 +362,8 @@ def main():
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": dist.world, "steps": len(wins),
             "warmup": args.warmup, "ms_per_step": max_ms / max(len(wins), 1), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16 activations, Q8_0 weights", "data": "synthetic",
-            "config": {"workload": "BASELINE config 3: Q8_0 decoder + lm_head, bf16 activations, batch 32 "
-                                   "continuous batching over a 256-request queue (prompts log-uniform 300-8000, "
-                                   "geometric stops mean 600 cap 4096), on-GPU refill, 2048-row prefill chunks",
-                       "requests_per_gpu": len(wl.prompt_lens), "batch": args.batch, "prefill_chunk": args.chunk,
-                       "layers": cfg.num_hidden_layers, "step": f"{args.window} device steps",
-                       "device_steps_timed": int(steps_run), "l2": "working set >> L2 (no flush needed)",
-                       "parallelism": f"dp{dist.world} (request-sharded, no collective)"},
+            "config": dict(workload_config(args, cfg, len(wl.prompt_lens), dist.world),
+                           device_steps_timed=int(steps_run)),
             "roofline": {"bound": "hbm", "kernel": "k_attn_decode (split-KV GQA decode attention)",
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "traffic": (tpk * kv_per_launch) if tpk else None, "peak_kind": peak_kind,
@@ -371,7 +376,7 @@ def main():
             "e2e": e2e,
             "cpu_baseline": cpu,
             "gpu_launches": int(mixed_run * KERNELS_MIXED(cfg.num_hidden_layers)
-                                + (steps_run - mixed_run) * KERNELS_DECODE(cfg.num_hidden_layers) + len(wins)),
+                                + (steps_run - mixed_run) * KERNELS_DECODE(cfg.num_hidden_layers)),
             "mixed_steps_timed": int(mixed_run),
             "tokens_timed": int(tot_tokens),
         }

@@ -70,6 +70,25 @@ struct WRegs {
   float da, db;
 };
 
+// rs[r] = rsqrt(mean(x^2) + eps) of rows r < rows from the per-tile sums of
+// squares ssq[row][tiles]: one thread per row, each chunk of 16 partials
+// loaded together (one round trip per chunk), summed in order.
+FMD_DEV void rows_rsqrt(const float* __restrict__ ssq, int tiles, const int* __restrict__ row_map, int row0, int rows,
+                        int K, float eps, float* __restrict__ rs, int nthreads) {
+  for (int r = threadIdx.x; r < rows; r += nthreads) {
+    const float* sp = ssq + (size_t)(row_map ? row_map[row0 + r] : row0 + r) * tiles;
+    float ss = 0.f;
+    for (int i0 = 0; i0 < tiles; i0 += 16) {
+      float v[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i] = i0 + i < tiles ? sp[i0 + i] : 0.f;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) ss += v[i];
+    }
+    rs[r] = rsqrtf(ss / K + eps);
+  }
+}
+
 // A fragments of the 4 MMAs of one 64-wide k-block (see the k permutation in
 // the header of fmd_kernels.cu's k_linear): thread (g, t) holds weights
 // [16t, 16t+16) of rows f0 and f0+8.
@@ -108,11 +127,14 @@ FMD_DEV void gemv_afrag(const WRegs& w, uint32_t (&af)[4][4]) {
   }
 }
 
-template <typename T, bool Q8, int FW, int EPI, bool NORM>
-__global__ void __launch_bounds__(FW * 32) k_gemv(const T* __restrict__ x, int ldx, const int* __restrict__ row_map,
+// KG warp groups split a CTA's k-blocks (KG = 2 only where the grid leaves
+// SMs free: the doubled block would otherwise cost resident CTAs).
+template <typename T, bool Q8, int FW, int EPI, bool NORM, int KG>
+__global__ void __launch_bounds__(FW * KG * 32) k_gemv(const T* __restrict__ x, int ldx, const int* __restrict__ row_map,
                                                  const int* __restrict__ n_rows_ptr, LinW W, GemvEpi ep, int xrows,
                                                  int* __restrict__ status) {
-  constexpr int NT = FW * 32;
+  constexpr int NW = FW * KG;  // warps: FW feature slices x KG k-block groups
+  constexpr int NT = NW * 32;
   constexpr int FT = FW * 16;
   constexpr int UNIT = Q8 ? kUnitQ8 : kUnitDense;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -129,7 +151,8 @@ __global__ void __launch_bounds__(FW * 32) k_gemv(const T* __restrict__ x, int l
   const int xstride = klen + 8;
   float* part = reinterpret_cast<float*>(xs);  // after the k-loop: [xrows][FT + 4]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  const int fl = warp * 16 + g;  // local feature row of this thread (and fl + 8)
+  const int kgrp = warp / FW;     // this warp's k-blocks: kgrp, kgrp + KG, ...
+  const int fl = (warp % FW) * 16 + g;  // local feature row of this thread (and fl + 8)
 
   // ---- the whole weight tile is in flight before the dependency wait: one
   // TMA bulk copy per k-block, each on its own mbarrier so compute can start
@@ -143,12 +166,49 @@ __global__ void __launch_bounds__(FW * 32) k_gemv(const T* __restrict__ x, int l
       bulk_load(wsm + kb * kb_bytes, src + (size_t)kb * kb_bytes, kb_bytes, &wbar[kb]);
     }
   }
+  // q/k RMSNorm weights of this CTA's head (constant: fetched before the wait)
+  float hnw[4] = {1.f, 1.f, 1.f, 1.f};
+  if constexpr (EPI == kGemvQkv) {
+    if ((int)blockIdx.x < ep.Hq + ep.Hkv) {
+      const T* nw = reinterpret_cast<const T*>((int)blockIdx.x < ep.Hq ? ep.qn_w : ep.kn_w) + lane * 4;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) hnw[i] = Act<T>::to_f(nw[i]);
+    }
+  }
   griddep_wait();
 
   const int n_rows = *n_rows_ptr;
   const int row0 = blockIdx.z * kRows;
   const int rows = max(0, min(min(kRows, xrows), n_rows - row0));
   const int n_tiles = (rows + 7) >> 3;
+
+  // epilogue operands written by earlier kernels, fetched now so that their
+  // latency hides behind the k-loop: the first kPre rows this warp will own
+  // after the cluster reduction (lr = rank + warp * S + i * NW * S)
+  constexpr int FPL = FT / 32;  // features per lane in the epilogue (2 or 4)
+  constexpr int kPre = 2;
+  float xpre[kPre][FPL];
+  int ppos[kPre], pslot[kPre], ppage[kPre];
+#pragma unroll
+  for (int i = 0; i < kPre; ++i) {
+    const int lr = rank + warp * S + i * NW * S;
+    ppos[i] = pslot[i] = ppage[i] = 0;
+#pragma unroll
+    for (int f = 0; f < FPL; ++f) xpre[i][f] = 0.f;
+    if (lr < rows) {
+      const int r = row0 + lr;
+      if constexpr (EPI == kGemvResid) {
+        const T* xr = reinterpret_cast<const T*>(ep.x) + (size_t)r * W.N + blockIdx.x * FT + lane * FPL;
+#pragma unroll
+        for (int f = 0; f < FPL; ++f) xpre[i][f] = Act<T>::to_f(xr[f]);
+      } else if constexpr (EPI == kGemvQkv) {
+        ppos[i] = ep.plan.row_pos[r];
+        pslot[i] = ep.plan.row_slot[r];
+        if ((int)blockIdx.x >= ep.Hq)
+          ppage[i] = ep.kv.page_table[(size_t)pslot[i] * ep.kv.max_pages_per_slot + ppos[i] / kPageTokens];
+      }
+    }
+  }
 
   if (rows > 0) {
     // activation tile rows x klen (rows of a partial n-tile zero-filled)
@@ -164,17 +224,8 @@ __global__ void __launch_bounds__(FW * 32) k_gemv(const T* __restrict__ x, int l
       cp_async16(xs + (size_t)r * xstride + ch * 8, src, bytes);
     }
     cp_async_commit();
-    if constexpr (NORM) {
-      // rsqrt(mean(x^2) + eps) of each row from the per-tile sums of squares,
-      // read while the activation tile is in flight
-      for (int r = threadIdx.x; r < rows; r += NT) {
-        const int gr = row_map ? row_map[row0 + r] : row0 + r;
-        const float* sp = ep.ssq + (size_t)gr * ep.ssq_tiles;
-        float ss = 0.f;
-        for (int i = 0; i < ep.ssq_tiles; ++i) ss += sp[i];
-        rs_s[r] = rsqrtf(ss / K + ep.eps);
-      }
-    }
+    // rsqrt(mean(x^2) + eps) of each row, read while the activation tile is in flight
+    if constexpr (NORM) rows_rsqrt(ep.ssq, ep.ssq_tiles, row_map, row0, rows, K, ep.eps, rs_s, NT);
     cp_async_wait<0>();
     if constexpr (NORM) {
       __syncthreads();  // rs_s
@@ -197,6 +248,29 @@ __global__ void __launch_bounds__(FW * 32) k_gemv(const T* __restrict__ x, int l
       }
     }
   }
+  // RoPE factors of the prefetched rows (their positions have landed by now);
+  // in flight during the k-loop
+  float rcs[kPre][4], rsn[kPre][4];
+#pragma unroll
+  for (int i = 0; i < kPre; ++i)
+#pragma unroll
+    for (int f = 0; f < 4; ++f) rcs[i][f] = rsn[i][f] = 0.f;
+  if constexpr (EPI == kGemvQkv) {
+    if ((int)blockIdx.x < ep.Hq + ep.Hkv) {
+      const int dd = (lane & 15) * 4;
+#pragma unroll
+      for (int i = 0; i < kPre; ++i)
+        if (rank + warp * S + i * NW * S < rows) {
+          const T* ct = reinterpret_cast<const T*>(ep.cos) + (size_t)ppos[i] * (kHeadDim / 2) + dd;
+          const T* st = reinterpret_cast<const T*>(ep.sin) + (size_t)ppos[i] * (kHeadDim / 2) + dd;
+#pragma unroll
+          for (int f = 0; f < 4; ++f) {
+            rcs[i][f] = Act<T>::to_f(ct[f]);
+            rsn[i][f] = Act<T>::to_f(st[f]);
+          }
+        }
+    }
+  }
   __syncthreads();  // barrier inits (and rs_s) visible to all threads
   if (rows == 0) {
     // a whole cluster shares blockIdx.z, so it leaves together, but only
@@ -214,12 +288,12 @@ __global__ void __launch_bounds__(FW * 32) k_gemv(const T* __restrict__ x, int l
   // not unrolled: the k-loop body is ~100 instructions, and a decode layer
   // cycles through four GEMV variants, so code size shows up as i-cache misses
 #pragma unroll 1
-  for (int kb = 0; kb < nkb; ++kb) {
+  for (int kb = kgrp; kb < nkb; kb += KG) {
     {
       const bool landed = mbar_wait_bounded(&wbar[kb], 0, kWaitLimit);
       ok &= landed;
       if (landed) {
-        const uint8_t* u = wsm + kb * kb_bytes + warp * UNIT;
+        const uint8_t* u = wsm + kb * kb_bytes + (warp % FW) * UNIT;
         WRegs w;
         w.a = *reinterpret_cast<const int4*>(u + lane * 16);
         w.b = *reinterpret_cast<const int4*>(u + 512 + lane * 16);
@@ -251,32 +325,68 @@ __global__ void __launch_bounds__(FW * 32) k_gemv(const T* __restrict__ x, int l
   if (!ok) atomicExch(status, kStatusTimeout);
   __syncthreads();  // the activation tile is dead: `part` reuses it
 
-  // ---- partial tile -> shared memory; the cluster sums it
+  // ---- partial tile -> shared memory (k-block group 1, then group 0 adds
+  // its own: a fixed order); the cluster sums the CTAs' tiles
   constexpr int PS = FT + 4;  // part row stride (floats)
+  static_assert(KG == 1 || KG == 2, "one or two k-block groups");
+  if (kgrp == KG - 1) {
 #pragma unroll
-  for (int nt = 0; nt < 8; ++nt) {
-    if (nt < n_tiles) {
-      const int lr = nt * 8 + 2 * t;
-      part[lr * PS + fl] = acc[nt][0];
-      part[(lr + 1) * PS + fl] = acc[nt][1];
-      part[lr * PS + fl + 8] = acc[nt][2];
-      part[(lr + 1) * PS + fl + 8] = acc[nt][3];
+    for (int nt = 0; nt < 8; ++nt) {
+      if (nt < n_tiles) {
+        const int lr = nt * 8 + 2 * t;
+        part[lr * PS + fl] = acc[nt][0];
+        part[(lr + 1) * PS + fl] = acc[nt][1];
+        part[lr * PS + fl + 8] = acc[nt][2];
+        part[(lr + 1) * PS + fl + 8] = acc[nt][3];
+      }
+    }
+  }
+  if (KG == 2) __syncthreads();
+  if (KG == 2 && kgrp == 0) {
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+      if (nt < n_tiles) {
+        const int lr = nt * 8 + 2 * t;
+        part[lr * PS + fl] = acc[nt][0] + part[lr * PS + fl];
+        part[(lr + 1) * PS + fl] = acc[nt][1] + part[(lr + 1) * PS + fl];
+        part[lr * PS + fl + 8] = acc[nt][2] + part[lr * PS + fl + 8];
+        part[(lr + 1) * PS + fl + 8] = acc[nt][3] + part[(lr + 1) * PS + fl + 8];
+      }
     }
   }
   cg::cluster_group cluster = cg::this_cluster();
   cluster.sync();
 
   // rank r owns rows r, r+S, ...; one warp per row, features across lanes
-  constexpr int FPL = FT / 32;  // features per lane (2 or 4)
-  for (int lr = rank + warp * S; lr < rows; lr += FW * S) {
+  int pi = 0;  // index of this row among the warp's rows
+  for (int lr = rank + warp * S; lr < rows; lr += NW * S, ++pi) {
     float v[FPL];
 #pragma unroll
     for (int i = 0; i < FPL; ++i) v[i] = 0.f;
-    for (int s = 0; s < S; ++s) {
-      const float* peer = cluster.map_shared_rank(part + lr * PS, s);
+    // the S peer loads issue together (fixed summation order s = 0 .. S-1)
+    float pv[8][FPL];
 #pragma unroll
-      for (int i = 0; i < FPL; ++i) v[i] += peer[lane * FPL + i];
-    }
+    for (int s = 0; s < 8; ++s)
+      if (s < S) {
+        // one vector load per peer: a warp reads the row's FT floats contiguously
+        const float* peer = cluster.map_shared_rank(part + lr * PS, s) + lane * FPL;
+        if constexpr (FPL == 4) {
+          const float4 q = *reinterpret_cast<const float4*>(peer);
+          pv[s][0] = q.x;
+          pv[s][1] = q.y;
+          pv[s][2] = q.z;
+          pv[s][3] = q.w;
+        } else {
+          const float2 q = *reinterpret_cast<const float2*>(peer);
+          pv[s][0] = q.x;
+          pv[s][1] = q.y;
+        }
+      }
+#pragma unroll
+    for (int s = 0; s < 8; ++s)
+      if (s < S)
+#pragma unroll
+        for (int i = 0; i < FPL; ++i) v[i] += pv[s][i];
     const int r = row0 + lr;
 #pragma unroll
     for (int i = 0; i < FPL; ++i) v[i] = rnd<T>(v[i]);
@@ -286,7 +396,8 @@ __global__ void __launch_bounds__(FW * 32) k_gemv(const T* __restrict__ x, int l
       float ss = 0.f;
 #pragma unroll
       for (int i = 0; i < FPL; ++i) {
-        const float nx = rnd<T>(Act<T>::to_f(xr[i]) + v[i]);
+        const float xo = pi < kPre ? (pi == 0 ? xpre[0][i] : xpre[1][i]) : Act<T>::to_f(xr[i]);
+        const float nx = rnd<T>(xo + v[i]);
         xr[i] = Act<T>::from_f(nx);
         ss += nx * nx;
       }
@@ -304,35 +415,39 @@ __global__ void __launch_bounds__(FW * 32) k_gemv(const T* __restrict__ x, int l
     } else if constexpr (EPI == kGemvQkv) {
       // FT = 128: one head; lane holds dims 4*lane .. 4*lane+3
       const int hh = blockIdx.x, Hq = ep.Hq, Hkv = ep.Hkv;
-      const int pos = ep.plan.row_pos[r], slot = ep.plan.row_slot[r];
+      const int pos = pi < kPre ? (pi == 0 ? ppos[0] : ppos[1]) : ep.plan.row_pos[r];
+      const int slot = pi < kPre ? (pi == 0 ? pslot[0] : pslot[1]) : ep.plan.row_slot[r];
+      const int kvpage = pi < kPre ? (pi == 0 ? ppage[0] : ppage[1])
+                                   : (hh >= Hq ? ep.kv.page_table[(size_t)slot * ep.kv.max_pages_per_slot +
+                                                                  pos / kPageTokens]
+                                               : 0);
       T* kvb = reinterpret_cast<T*>(ep.kv.base);
       T* dst;
       if (hh < Hq + Hkv) {
-        const T* nw = reinterpret_cast<const T*>(hh < Hq ? ep.qn_w : ep.kn_w);
         const float ss = warp_sum(v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3]);
         const float inv = rsqrtf(ss / kHeadDim + ep.eps);
         float y[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) y[i] = rnd<T>(v[i] * inv * Act<T>::to_f(nw[lane * 4 + i]));
+        for (int i = 0; i < 4; ++i) y[i] = rnd<T>(v[i] * inv * hnw[i]);
         const T* cos_t = reinterpret_cast<const T*>(ep.cos);
         const T* sin_t = reinterpret_cast<const T*>(ep.sin);
         const int dd = (lane & 15) * 4;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const float pr = __shfl_xor_sync(0xffffffffu, y[i], 16);
-          const float cs = Act<T>::to_f(cos_t[(size_t)pos * (kHeadDim / 2) + dd + i]);
-          const float sn = Act<T>::to_f(sin_t[(size_t)pos * (kHeadDim / 2) + dd + i]);
+          const float cs = pi < kPre ? (pi == 0 ? rcs[0][i] : rcs[1][i])
+                                     : Act<T>::to_f(cos_t[(size_t)pos * (kHeadDim / 2) + dd + i]);
+          const float sn = pi < kPre ? (pi == 0 ? rsn[0][i] : rsn[1][i])
+                                     : Act<T>::to_f(sin_t[(size_t)pos * (kHeadDim / 2) + dd + i]);
           v[i] = lane < 16 ? y[i] * cs - pr * sn : pr * sn + y[i] * cs;
         }
         if (hh < Hq) {
           dst = reinterpret_cast<T*>(ep.q_out) + (size_t)r * Hq * kHeadDim + hh * kHeadDim;
         } else {
-          const int page = ep.kv.page_table[(size_t)slot * ep.kv.max_pages_per_slot + pos / kPageTokens];
-          dst = kvb + ep.kv.elem_offset(ep.layer, page, 0, hh - Hq) + (size_t)(pos % kPageTokens) * kHeadDim;
+          dst = kvb + ep.kv.elem_offset(ep.layer, kvpage, 0, hh - Hq) + (size_t)(pos % kPageTokens) * kHeadDim;
         }
       } else {
-        const int page = ep.kv.page_table[(size_t)slot * ep.kv.max_pages_per_slot + pos / kPageTokens];
-        dst = kvb + ep.kv.elem_offset(ep.layer, page, 1, hh - Hq - Hkv) + (size_t)(pos % kPageTokens) * kHeadDim;
+        dst = kvb + ep.kv.elem_offset(ep.layer, kvpage, 1, hh - Hq - Hkv) + (size_t)(pos % kPageTokens) * kHeadDim;
       }
       uint2 o;
       o.x = Act<T>::pack2(v[0], v[1]);
@@ -367,7 +482,11 @@ __global__ void __launch_bounds__(FW * 32) k_gemv(const T* __restrict__ x, int l
       }
     }
   }
-  cluster.sync();  // peers may still be reading this CTA's partial tile
+  // peers may still be reading this CTA's partial tile: wait for every CTA of
+  // the cluster to pass its reduction (a relaxed arrive: the epilogue's
+  // global stores need not be performed first)
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;\n" ::: "memory");
+  asm volatile("barrier.cluster.wait.aligned;\n" ::: "memory");
 }
 
 // lm_head + greedy candidates as one persistent kernel (qwen3.rs:459-463,
@@ -430,16 +549,24 @@ __global__ void __launch_bounds__((kHeadWarps + 1) * 32) k_lm_head(const T* __re
     // ---- producer: weights do not depend on the previous kernel, so the
     // ring starts filling before griddepcontrol.wait
     if (lane == 0) {
+      // stage / phase / tile / k-block advance incrementally (no divisions)
+      int st = 0, ph = 0, tile = blockIdx.x, kb = 0;
       for (int u = 0; u < n_units; ++u) {
-        const int st = u % stages;
-        if (u >= stages && !mbar_wait_bounded(&empty[st], ((u / stages) + 1) & 1, kWaitLimit)) {
+        if (u >= stages && !mbar_wait_bounded(&empty[st], ph ^ 1, kWaitLimit)) {
           atomicExch(&abort_s, 1);
           break;
         }
         if (*reinterpret_cast<volatile int*>(&abort_s)) break;
-        const int tile = blockIdx.x + (u / nkb) * gridDim.x, kb = u % nkb;
         mbar_arrive_expect_tx(&full[st], kStage);
         bulk_load(ring + (size_t)st * kStage, W.pk + ((size_t)tile * nkb + kb) * kStage, kStage, &full[st]);
+        if (++kb == nkb) {
+          kb = 0;
+          tile += gridDim.x;
+        }
+        if (++st == stages) {
+          st = 0;
+          ph ^= 1;
+        }
       }
     }
     griddep_wait();
@@ -466,13 +593,7 @@ __global__ void __launch_bounds__((kHeadWarps + 1) * 32) k_lm_head(const T* __re
   }
   cp_async_commit();
   const bool norm = ep.ssq != nullptr;  // else x is already normalised
-  for (int r = threadIdx.x; norm && r < rows; r += NT) {
-    const int gr = row_map ? row_map[row0 + r] : row0 + r;
-    const float* sp = ep.ssq + (size_t)gr * ep.ssq_tiles;
-    float ss = 0.f;
-    for (int i = 0; i < ep.ssq_tiles; ++i) ss += sp[i];
-    rs_s[r] = rsqrtf(ss / K + ep.eps);
-  }
+  if (norm) rows_rsqrt(ep.ssq, ep.ssq_tiles, row_map, row0, rows, K, ep.eps, rs_s, NT);
   cp_async_wait<0>();
   named_sync(1, NT);
   if (norm) {
@@ -505,19 +626,22 @@ __global__ void __launch_bounds__((kHeadWarps + 1) * 32) k_lm_head(const T* __re
     bi[nt][0] = bi[nt][1] = 0x7fffffff;
   }
   bool ok = true;
-  int u = 0;
+  int st = 0, ph = 0;  // ring position of the next unit
   if (rows == 0) {
     // the producer started before the row count was known: release every
     // stage so that no copy is left in flight when the CTA retires
-    for (; u < n_units; ++u) {
-      const int st = u % stages;
-      if (*reinterpret_cast<volatile int*>(&abort_s) || !mbar_wait_bounded(&full[st], (u / stages) & 1, kWaitLimit)) {
+    for (int u = 0; u < n_units; ++u) {
+      if (*reinterpret_cast<volatile int*>(&abort_s) || !mbar_wait_bounded(&full[st], ph, kWaitLimit)) {
         atomicExch(&abort_s, 1);
         ok = false;
         break;
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[st]);
+      if (++st == stages) {
+        st = 0;
+        ph ^= 1;
+      }
     }
   }
   for (int i = 0; i < my_tiles && ok && rows > 0; ++i) {
@@ -526,9 +650,8 @@ __global__ void __launch_bounds__((kHeadWarps + 1) * 32) k_lm_head(const T* __re
 #pragma unroll
     for (int nt = 0; nt < 8; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
 #pragma unroll 1
-    for (int kb = 0; kb < nkb; ++kb, ++u) {
-      const int st = u % stages;
-      if (*reinterpret_cast<volatile int*>(&abort_s) || !mbar_wait_bounded(&full[st], (u / stages) & 1, kWaitLimit)) {
+    for (int kb = 0; kb < nkb; ++kb) {
+      if (*reinterpret_cast<volatile int*>(&abort_s) || !mbar_wait_bounded(&full[st], ph, kWaitLimit)) {
         atomicExch(&abort_s, 1);
         ok = false;
         break;
@@ -547,6 +670,10 @@ __global__ void __launch_bounds__((kHeadWarps + 1) * 32) k_lm_head(const T* __re
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[st]);  // this warp's fragments are in registers
+      if (++st == stages) {
+        st = 0;
+        ph ^= 1;
+      }
       uint32_t af[4][4];
       gemv_afrag<T, Q8>(w, af);
 #pragma unroll
@@ -694,7 +821,7 @@ size_t gemv_smem_bytes(int FT, bool q8, int klen, int xrows) {
   return w + (xb > pb ? xb : pb);
 }
 
-template <typename T, bool Q8, int FW, int EPI, bool NORM>
+template <typename T, bool Q8, int FW, int EPI, bool NORM, int KG>
 void launch_gemv_t(const LinW& W, int S, const void* x, int ldx, const int* row_map, const int* n_rows_ptr,
                    int max_rows, const GemvEpi& ep, int* status, cudaStream_t s) {
   const int xrows = ((max_rows < kRows ? max_rows : kRows) + 7) & ~7;
@@ -708,12 +835,12 @@ void launch_gemv_t(const LinW& W, int S, const void* x, int ldx, const int* row_
   attr[1].val.clusterDim.z = 1;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(W.N / (FW * 16), S, (max_rows + kRows - 1) / kRows);
-  cfg.blockDim = dim3(FW * 32);
+  cfg.blockDim = dim3(FW * KG * 32);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  cudaLaunchKernelEx(&cfg, k_gemv<T, Q8, FW, EPI, NORM>, (const T*)x, ldx, row_map, n_rows_ptr, W, ep, xrows, status);
+  cudaLaunchKernelEx(&cfg, k_gemv<T, Q8, FW, EPI, NORM, KG>, (const T*)x, ldx, row_map, n_rows_ptr, W, ep, xrows, status);
 }
 
 
@@ -754,11 +881,11 @@ cudaError_t init_gemv_t() {
   cudaError_t e = cudaSuccess;
   const int lim = 226 * 1024;  // opt-in limit less room for the static barrier and row scales
   for (cudaError_t r : {
-           cudaFuncSetAttribute(k_gemv<T, Q8, 8, kGemvQkv, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim),
-           cudaFuncSetAttribute(k_gemv<T, Q8, 8, kGemvQkv, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim),
-           cudaFuncSetAttribute(k_gemv<T, Q8, 4, kGemvResid, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim),
-           cudaFuncSetAttribute(k_gemv<T, Q8, 4, kGemvSwiglu, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim),
-           cudaFuncSetAttribute(k_gemv<T, Q8, 8, kGemvLogits, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim),
+           cudaFuncSetAttribute(k_gemv<T, Q8, 8, kGemvQkv, true, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim),
+           cudaFuncSetAttribute(k_gemv<T, Q8, 8, kGemvQkv, false, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim),
+           cudaFuncSetAttribute(k_gemv<T, Q8, 4, kGemvResid, false, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim),
+           cudaFuncSetAttribute(k_gemv<T, Q8, 4, kGemvSwiglu, true, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim),
+           cudaFuncSetAttribute(k_gemv<T, Q8, 8, kGemvLogits, true, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim),
            cudaFuncSetAttribute(k_lm_head<T, Q8>, cudaFuncAttributeMaxDynamicSharedMemorySize, kHeadSmemBudget)})
     if (r != cudaSuccess) e = r;
   return e;
@@ -830,12 +957,12 @@ bool launch_gemv(ActType at, int epi, bool norm, const LinW& W, const void* x, i
 #define FMD_GEMV(T, Q8)                                                                                           \
   switch (epi) {                                                                                                \
     case kGemvQkv:                                                                                              \
-      if (norm) launch_gemv_t<T, Q8, 8, kGemvQkv, true>(W, S, x, ldx, row_map, n_rows_ptr, max_rows, ep, status, s);     \
-      else launch_gemv_t<T, Q8, 8, kGemvQkv, false>(W, S, x, ldx, row_map, n_rows_ptr, max_rows, ep, status, s);         \
+      if (norm) launch_gemv_t<T, Q8, 8, kGemvQkv, true, 1>(W, S, x, ldx, row_map, n_rows_ptr, max_rows, ep, status, s);     \
+      else launch_gemv_t<T, Q8, 8, kGemvQkv, false, 1>(W, S, x, ldx, row_map, n_rows_ptr, max_rows, ep, status, s);         \
       break;                                                                                                    \
-    case kGemvResid: launch_gemv_t<T, Q8, 4, kGemvResid, false>(W, S, x, ldx, row_map, n_rows_ptr, max_rows, ep, status, s); break; \
-    case kGemvSwiglu: launch_gemv_t<T, Q8, 4, kGemvSwiglu, true>(W, S, x, ldx, row_map, n_rows_ptr, max_rows, ep, status, s); break; \
-    default: launch_gemv_t<T, Q8, 8, kGemvLogits, true>(W, S, x, ldx, row_map, n_rows_ptr, max_rows, ep, status, s); break; \
+    case kGemvResid: launch_gemv_t<T, Q8, 4, kGemvResid, false, 2>(W, S, x, ldx, row_map, n_rows_ptr, max_rows, ep, status, s); break; \
+    case kGemvSwiglu: launch_gemv_t<T, Q8, 4, kGemvSwiglu, true, 1>(W, S, x, ldx, row_map, n_rows_ptr, max_rows, ep, status, s); break; \
+    default: launch_gemv_t<T, Q8, 8, kGemvLogits, true, 1>(W, S, x, ldx, row_map, n_rows_ptr, max_rows, ep, status, s); break; \
   }
   if (at == kBF16) {
     if (W.q8) { FMD_GEMV(__nv_bfloat16, true) } else { FMD_GEMV(__nv_bfloat16, false) }

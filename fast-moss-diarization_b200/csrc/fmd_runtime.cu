@@ -755,6 +755,7 @@ int fmd_create(const fmd_config* cfg, int32_t precision, int32_t device, fmd_han
   if (cfg->hidden_size % 64 || cfg->intermediate_size % 64 || cfg->vocab_size % 64)
     return FMD_ENOTSUP;
   if (cfg->num_hidden_layers < 1 || cfg->hidden_size <= 0) return FMD_EINVAL;
+  if (cfg->hidden_size > 64 * 64) return FMD_ENOTSUP;  // per-row norm partials: at most 64 tiles of 64
   // decode-path projections: lm_head tiles are 128 features wide, and each
   // contraction must split into slices the cluster GEMV holds
   if (cfg->vocab_size % gemv_tile_features(kGemvLogits) ||
