@@ -186,15 +186,24 @@ def traffic_per_kv_token() -> float | None:
 
 
 # ---- model + workload ---------------------------------------------------------------------
-def build_model_and_queue(args, rank: int):
+def build_model_and_queue(args, rank: int, world: int = 1):
+    """Model and this rank's request queue. The global queue holds
+    `args.requests` requests per GPU (weak scaling); every rank derives the
+    same LPT partition of it (fmd_b200.dp) and builds prompt embeddings for
+    its own shard only."""
     pkg = __graft_entry__.load_package()
     import importlib
 
     syn = importlib.import_module("fmd_b200.synthetic")
+    dp = importlib.import_module("fmd_b200.dp")
     cfg = pkg.TextConfig(num_hidden_layers=args.layers)
     w = syn.make_weights(cfg, seed=args.seed, prequantized=True)
-    wl = syn.workload(3, cfg, w["embed"], seed=args.seed + 1000 * rank, n_requests=args.requests)
-    wl.max_new = np.minimum(wl.max_new, args.max_new)
+    glob = syn.workload(3, cfg, w["embed"], seed=args.seed, n_requests=args.requests * world, with_arena=False)
+    glob.max_new = np.minimum(glob.max_new, args.max_new)
+    part = dp.partition(glob.prompt_lens, glob.max_new, world, expected_new=glob.forced_stop)
+    wl = glob.subset(part.shard(rank))
+    wl.arena = syn.build_prompt_arena(cfg, w["embed"], wl.prompt_lens, args.seed + 7 * 3 + 1000 * rank,
+                                      out_bf16=True)
     return pkg, cfg, w, wl
 
 
@@ -252,7 +261,7 @@ def workload_config(args, cfg, n_requests: int, world: int) -> dict:
             "requests_per_gpu": n_requests, "batch": args.batch, "prefill_chunk": args.chunk,
             "layers": cfg.num_hidden_layers, "step": f"{args.window} device steps",
             "l2": "working set >> L2 (no flush needed)",
-            "parallelism": f"dp{world} (request-sharded, no collective)"}
+            "parallelism": f"dp{world} (LPT request shards of a {n_requests * world}-request queue, no collective)"}
 
 
 def run_reference(args):
@@ -280,7 +289,7 @@ def main():
         return
     dist = Dist()
 
-    pkg, cfg, w, wl = build_model_and_queue(args, dist.rank)
+    pkg, cfg, w, wl = build_model_and_queue(args, dist.rank, dist.world)
     dec = pkg.Qwen3Decoder(cfg, wl.precision, device=dist.local)
     dec.load_weights(w)
     top = np.sort(wl.prompt_lens)[-args.batch:]

@@ -84,6 +84,13 @@ class Workload:
     arena_dtype: str = "f32"
     meta: dict = field(default_factory=dict)
 
+    def subset(self, idx) -> "Workload":
+        """The requests `idx` (in that order) as their own queue, without an
+        arena (build one with `build_prompt_arena` for the subset)."""
+        idx = np.asarray(idx, dtype=np.int64)
+        return Workload(self.name, self.prompt_lens[idx], self.max_new[idx], self.forced_stop[idx], self.max_batch,
+                        self.prefill_chunk, self.precision, None, self.arena_dtype, dict(self.meta))
+
     @property
     def embed_rows(self) -> np.ndarray:
         off = np.zeros(len(self.prompt_lens), dtype=np.int64)
@@ -137,8 +144,9 @@ def config1_prompts(cfg: TextConfig, embed: np.ndarray, seed: int = 0):
 
 
 def workload(config: int, cfg: TextConfig, embed: np.ndarray, seed: int = 0, n_requests: int | None = None,
-             out_bf16: bool = True) -> Workload:
-    """Request queues of BASELINE configs 2, 3 and 5 (and 4's decoders)."""
+             out_bf16: bool = True, with_arena: bool = True) -> Workload:
+    """Request queues of BASELINE configs 2, 3 and 5 (and 4's decoders);
+    `with_arena=False` leaves the prompt embeddings out (lengths only)."""
     rng = np.random.default_rng(seed + 100 * config)
     if config == 2:
         n = n_requests or 8
@@ -162,6 +170,7 @@ def workload(config: int, cfg: TextConfig, embed: np.ndarray, seed: int = 0, n_r
     else:
         raise ValueError(f"no request-queue workload for config {config}")
     # the forced stop is the n-th generated token; geometric draws are >= 1
-    wl.arena = build_prompt_arena(cfg, embed, wl.prompt_lens, seed + 7 * config, out_bf16=out_bf16)
     wl.arena_dtype = "bf16" if out_bf16 else "f32"
+    if with_arena:
+        wl.arena = build_prompt_arena(cfg, embed, wl.prompt_lens, seed + 7 * config, out_bf16=out_bf16)
     return wl
