@@ -220,6 +220,9 @@ void launch_pick_reduce(const int* n_sample_ptr, int B, const float* best_val, c
 // `tmap` points at a CUtensorMap over the KV pool viewed as 2D
 // [layers*pages*2*kv_heads*64 rows][128 dims], box 64x64, 128B swizzle.
 size_t attn_decode_smem_bytes();
+// floats of the split-segment partials of a decode-attention grid of `grid`
+// CTAs (two slots per CTA, both query heads of a kv head, acc + m + l)
+size_t attn_decode_partial_floats(int grid);
 cudaError_t init_attn_decode();
 void launch_attn_decode_tma(ActType at, const void* tmap, const Plan& p, int grid, int Hq, int Hkv, const void* q,
                             const KvView& kv, int layer, float scale, float* part_acc, float* part_ml, int* counters,

@@ -959,10 +959,10 @@ int fmd_kv_reserve(fmd_handle* h, int32_t max_slots, int64_t max_tokens_total, i
   h->arena_rows = R;
   if ((rc = A(part_elems * 4, &p))) return rc;
   h->part = (float*)p;
-  if ((rc = A((size_t)h->di_max * HqD * 4, &p))) return rc;
+  // decode attention split-segment partials: acc [2 * grid][2][128], then m/l [2 * grid][2][2]
+  if ((rc = A(attn_decode_partial_floats(h->di_grid) * 4, &p))) return rc;
   h->pacc = (float*)p;
-  if ((rc = A((size_t)h->di_max * h->Hq() * 2 * 4, &p))) return rc;
-  h->pml = (float*)p;
+  h->pml = h->pacc + (size_t)2 * h->di_grid * 2 * kHeadDim;
   if ((rc = A((size_t)max_slots * V * 4, &p))) return rc;
   h->logits = (float*)p;
   if ((rc = A((size_t)max_slots * 4, &p))) return rc;
