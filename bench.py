@@ -9,7 +9,9 @@ engine (finished slots refilled on the device, prompts prefilled in 2048-row
 chunks inside decode steps).
 
 One bench "step" = one window of `--window` device steps of that engine with
-the queue and weights resident in HBM; `value` = tokens emitted in the K timed
+the queue and weights resident in HBM, requests admitted in the workload's
+seeded (unsorted) order so that the timed windows see the steady-state mix of
+context lengths; `value` = tokens emitted in the K timed
 windows / their CUDA-event time (max over ranks), summed over ranks. `e2e` =
 the same queue through the public host-buffer entry point (`fmd_generate`:
 pinned host arena -> device, run to completion, tokens -> host), wall clock.
@@ -259,6 +261,8 @@ def workload_config(args, cfg, n_requests: int, world: int) -> dict:
                         "continuous batching over a 256-request queue (prompts log-uniform 300-8000, "
                         "geometric stops mean 600 cap 4096), on-GPU refill, 2048-row prefill chunks",
             "requests_per_gpu": n_requests, "batch": args.batch, "prefill_chunk": args.chunk,
+            "arrival": "seeded workload order for the timed windows; e2e through Engine.generate "
+                       "(length-sorted queue, engine.rs:385)",
             "layers": cfg.num_hidden_layers, "step": f"{args.window} device steps",
             "l2": "working set >> L2 (no flush needed)",
             "parallelism": f"dp{world} (LPT request shards of a {n_requests * world}-request queue, no collective)"}
@@ -297,7 +301,10 @@ def main():
     dec.reserve(max_slots=args.batch, max_tokens=pool_tokens, max_rows=args.batch + args.chunk)
     eng = pkg.Engine(dec)
     forced = wl.forced_stop
-    eng.load(wl.prompt_lens, wl.max_new, forced, wl.arena)
+    # requests arrive in the workload's seeded order (no length sort): the
+    # continuous-batching steady state of a serving queue, so the timed
+    # windows see the workload's mix of context lengths
+    eng.load(wl.prompt_lens, wl.max_new, forced, wl.arena, sort_by_length=False)
     eng.start(args.batch, args.chunk)
 
     # warm-up windows (untimed), then K timed windows

@@ -36,7 +36,7 @@ FINISH_STOP, FINISH_LENGTH, FINISH_ERROR = 0, 1, 2
 # every symbol the header declares
 EXPORTS = [
     "fmd_create", "fmd_destroy", "fmd_last_error", "fmd_status_string", "fmd_version", "fmd_load_weights",
-    "fmd_kv_reserve", "fmd_cache_bytes", "fmd_memory_bytes", "fmd_embed", "fmd_slot_open", "fmd_slot_release",
+    "fmd_kv_reserve", "fmd_cache_bytes", "fmd_memory_bytes", "fmd_embed", "fmd_splice_audio", "fmd_slot_open", "fmd_slot_release",
     "fmd_slot_len", "fmd_prefill", "fmd_decode_step", "fmd_engine_load", "fmd_engine_start", "fmd_engine_step",
     "fmd_engine_run", "fmd_engine_fetch",
     "fmd_generate", "fmd_debug_weight", "fmd_debug_kv", "fmd_q8_0_quantize", "fmd_greedy_pick_noalloc",
@@ -116,6 +116,7 @@ def load() -> C.CDLL:
         "fmd_cache_bytes": (I64, [C.POINTER(Config), I32, I64, I64]),
         "fmd_memory_bytes": (C.c_int, [P, C.POINTER(I64), C.POINTER(I64), C.POINTER(I64)]),
         "fmd_embed": (C.c_int, [P, IP, I64, P]),
+        "fmd_splice_audio": (C.c_int, [P, IP, I64, P, I64, I32, I32, P]),
         "fmd_slot_open": (C.c_int, [P, I32, I32]),
         "fmd_slot_release": (C.c_int, [P, I32]),
         "fmd_slot_len": (C.c_int, [P, I32, IP]),

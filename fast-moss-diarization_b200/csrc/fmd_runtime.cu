@@ -149,6 +149,7 @@ struct fmd_handle {
 
   // engine
   DevBuf eng_reqs, eng_arena, eng_tokens, eng_results;
+  DevBuf splice_src;  // per-position source codes of fmd_splice_audio
   int eng_n_reqs = 0, eng_tok_stride = 0;
   int* eng_slot = nullptr;  // 7 arrays of max_slots
   int* eng_free = nullptr;
@@ -795,7 +796,7 @@ int fmd_destroy(fmd_handle* h) {
   if (h->win_begin) cudaEventDestroy(h->win_begin);
   if (h->win_end) cudaEventDestroy(h->win_end);
   for (auto& a : h->allocs) cudaFree(a.p);
-  for (DevBuf* b : {&h->eng_reqs, &h->eng_arena, &h->eng_tokens, &h->eng_results})
+  for (DevBuf* b : {&h->eng_reqs, &h->eng_arena, &h->eng_tokens, &h->eng_results, &h->splice_src})
     if (b->p) cudaFree(b->p);
   if (h->h_plan) cudaFreeHost(h->h_plan);
   if (h->h_ctr) cudaFreeHost(h->h_ctr);
@@ -1021,6 +1022,67 @@ int fmd_embed(fmd_handle* h, const int32_t* ids, int64_t n, void* out) {
   return sync_check(h);
 }
 
+namespace {
+// true when `p` is device memory of `device` (or managed memory)
+bool on_device(const void* p, int device) {
+  cudaPointerAttributes a{};
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return (a.type == cudaMemoryTypeDevice && a.device == device) || a.type == cudaMemoryTypeManaged;
+}
+}  // namespace
+
+int fmd_splice_audio(fmd_handle* h, const int32_t* token_ids, int64_t n_ids, const void* audio_embeds,
+                     int64_t n_audio, int32_t audio_dtype, int32_t audio_token_id, void* out) {
+  if (!h) return FMD_EINVAL;
+  if (!h->loaded) return fail(h, FMD_EBUSY, "no weights loaded (fmd_load_weights)");
+  const int H = h->H();
+  if (!token_ids || n_ids < 1 || n_ids >= (1LL << 31) || !out || n_audio < 0 || (n_audio > 0 && !audio_embeds))
+    return fail(h, FMD_EINVAL, "bad splice arguments");
+  const bool f32 = audio_dtype == FMD_DT_F32;
+  const bool act = (h->at == kBF16 && audio_dtype == FMD_DT_BF16) || (h->at == kF16 && audio_dtype == FMD_DT_F16);
+  if (!f32 && !act) return fail(h, FMD_EINVAL, "audio embeddings must be f32 or the activation dtype");
+  if (H % 8 != 0) return fail(h, FMD_ENOTSUP, "hidden size must be a multiple of 8");
+  CK(cudaSetDevice(h->device));
+  if (!on_device(out, h->device) || (n_audio > 0 && !on_device(audio_embeds, h->device)))
+    return fail(h, FMD_EINVAL, "splice buffers must be device memory of the handle's device");
+  if ((reinterpret_cast<uintptr_t>(out) & 15) || (reinterpret_cast<uintptr_t>(audio_embeds) & 15))
+    return fail(h, FMD_EINVAL, "splice buffers must be 16-byte aligned");
+  // one source code per position: the text id, or -(audio row) - 1, in
+  // prompt order (the alternating text / audio runs of mod.rs:159-176)
+  std::vector<int32_t> src((size_t)n_ids);
+  int64_t used = 0;
+  for (int64_t i = 0; i < n_ids; ++i) {
+    const int32_t id = token_ids[i];
+    if (id == audio_token_id) {
+      src[i] = used < n_audio ? (int32_t)(-used - 1) : 0;
+      ++used;
+    } else {
+      if (id < 0 || id >= h->cfg.vocab_size) return fail(h, FMD_EINVAL, "token id out of range");
+      src[i] = id;
+    }
+  }
+  if (used != n_audio)  // mod.rs:143-150
+    return fail(h, FMD_EINVAL, "prompt has " + std::to_string(used) + " audio placeholders but the encoder produced " +
+                                   std::to_string(n_audio) + " embeddings");
+  const size_t bytes = (size_t)n_ids * sizeof(int32_t);
+  if (h->splice_src.bytes < bytes) {
+    if (h->splice_src.p) cudaFree(h->splice_src.p);
+    h->splice_src = DevBuf{};
+    if (cudaMalloc(&h->splice_src.p, bytes) != cudaSuccess) {
+      cudaGetLastError();
+      h->splice_src.p = nullptr;
+      return fail(h, FMD_ENOMEM, "splice index allocation failed");
+    }
+    h->splice_src.bytes = bytes;
+  }
+  CK(cudaMemcpyAsync(h->splice_src.p, src.data(), bytes, cudaMemcpyHostToDevice, h->stream));
+  launch_splice(h->at, (const int*)h->splice_src.p, n_ids, h->embed, audio_embeds, f32, H, out, h->stream);
+  return sync_check(h);
+}
+
 int fmd_slot_open(fmd_handle* h, int32_t slot, int32_t capacity) {
   int rc = check_ready(h);
   if (rc) return rc;
@@ -1197,7 +1259,11 @@ int fmd_engine_load(fmd_handle* h, const fmd_request* reqs, int32_t n_reqs, cons
   // buffer
   const size_t rowb = (size_t)h->H() * (embeds_dtype == FMD_DT_F32 ? 4 : 2);
   const bool same = (h->at == kBF16 && embeds_dtype == FMD_DT_BF16) || (h->at == kF16 && embeds_dtype == FMD_DT_F16);
-  if (same) CK(cudaMemcpy(h->eng_arena.p, embeds, arena_bytes, cudaMemcpyHostToDevice));
+  // an arena already in device memory (e.g. written by fmd_splice_audio) is
+  // copied on the device; it must be in the activation dtype
+  const bool dev_arena = on_device(embeds, h->device);
+  if (dev_arena && !same) return fail(h, FMD_EINVAL, "a device-memory arena must be in the activation dtype");
+  if (same) CK(cudaMemcpy(h->eng_arena.p, embeds, arena_bytes, dev_arena ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice));
   std::vector<uint16_t> act;
   for (int64_t r = 0; !same && r < embed_rows; r += 65536) {
     const int64_t nr = std::min<int64_t>(65536, embed_rows - r);

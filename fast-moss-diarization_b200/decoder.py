@@ -140,6 +140,20 @@ class Qwen3Decoder:
                                        out.ctypes.data))
         return self._act_to_f32(out)
 
+    def splice_audio(self, token_ids, audio_ptr: int, n_audio: int, audio_dtype: str, audio_token_id: int,
+                     out_ptr: int) -> None:
+        """`MossModel::splice_audio` (model/mod.rs:134-180) on the GPU: writes the
+        prompt rows of `token_ids` (host ids, `audio_token_id` at audio
+        positions) to the device buffer at `out_ptr` (len(token_ids) x hidden,
+        activation dtype), taking audio positions from the `n_audio` device rows
+        at `audio_ptr` ("f32" or the activation dtype), in order. Pointers are
+        device addresses (e.g. a torch tensor's `data_ptr()`)."""
+        ids = np.ascontiguousarray(np.asarray(token_ids, dtype=np.int32).reshape(-1))
+        dt = {"f32": _lib.DT_F32, "bf16": _lib.DT_BF16, "f16": _lib.DT_F16}[audio_dtype]
+        self._check(self.lib.fmd_splice_audio(self._h, ids.ctypes.data_as(C.POINTER(C.c_int32)), ids.size,
+                                              C.c_void_p(audio_ptr), n_audio, dt, audio_token_id,
+                                              C.c_void_p(out_ptr)))
+
     def open_slot(self, slot: int, capacity: int) -> None:
         self._check(self.lib.fmd_slot_open(self._h, slot, capacity))
 

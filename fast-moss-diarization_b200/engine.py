@@ -75,6 +75,25 @@ class Engine:
         """Queue requests. `arena` holds all prompt rows (f32, or uint16 bits of
         the activation dtype); request i reads `prompt_lens[i]` rows from
         `embed_rows[i]` (default: back to back)."""
+        if arena.dtype == np.uint16:
+            dt = _lib.DT_BF16 if self.dec.act == "bf16" else _lib.DT_F16
+        else:
+            arena = np.ascontiguousarray(arena, dtype=np.float32)
+            dt = _lib.DT_F32
+        arena = np.ascontiguousarray(arena)
+        self._load(prompt_lens, max_new_tokens, forced_stop, arena.ctypes.data, arena.shape[0], dt, embed_rows,
+                   sort_by_length)
+
+    def load_device(self, prompt_lens, max_new_tokens, forced_stop, arena_ptr: int, arena_rows: int,
+                    embed_rows=None, sort_by_length: bool = True) -> None:
+        """`load` from an arena already in device memory (activation dtype,
+        `arena_rows` x hidden at device address `arena_ptr`), such as the rows
+        `Qwen3Decoder.splice_audio` writes: no host round trip."""
+        dt = _lib.DT_BF16 if self.dec.act == "bf16" else _lib.DT_F16
+        self._load(prompt_lens, max_new_tokens, forced_stop, arena_ptr, arena_rows, dt, embed_rows, sort_by_length)
+
+    def _load(self, prompt_lens, max_new_tokens, forced_stop, arena_ptr, arena_rows, dt, embed_rows,
+              sort_by_length) -> None:
         lens = np.asarray(prompt_lens, dtype=np.int64)
         n = len(lens)
         if embed_rows is None:
@@ -89,13 +108,7 @@ class Engine:
             reqs[j].max_new_tokens = int(mx[i])
             reqs[j].forced_stop = int(fs[i])
             reqs[j].embed_row = int(embed_rows[i])
-        if arena.dtype == np.uint16:
-            dt = _lib.DT_BF16 if self.dec.act == "bf16" else _lib.DT_F16
-        else:
-            arena = np.ascontiguousarray(arena, dtype=np.float32)
-            dt = _lib.DT_F32
-        arena = np.ascontiguousarray(arena)
-        self.lib_check(self.lib.fmd_engine_load(self.dec.handle, reqs, n, arena.ctypes.data, arena.shape[0], dt))
+        self.lib_check(self.lib.fmd_engine_load(self.dec.handle, reqs, n, C.c_void_p(arena_ptr), arena_rows, dt))
         self.n = n
         self.order = order
         self.max_new = int(mx.max()) if n else 0

@@ -175,6 +175,20 @@ int fmd_memory_bytes(const fmd_handle* h, int64_t* weights, int64_t* kv_pool, in
 /* `Qwen3::embed` (qwen3.rs:405-412): `n` ids -> n x hidden rows (act dtype). */
 int fmd_embed(fmd_handle* h, const int32_t* ids, int64_t n, void* out);
 
+/* `MossModel::splice_audio` (crates/fmd-core/src/model/mod.rs:134-180): the
+ * prompt embedding of one sequence, assembled on the GPU. `token_ids` (host,
+ * `n_ids` ids) is the prompt with `audio_token_id` at every audio position;
+ * text ids are looked up in the embedding table and the audio positions take
+ * the rows of `audio_embeds` (device, `n_audio` x hidden, FMD_DT_F32 or the
+ * activation dtype) in order. `out` (device, n_ids x hidden, activation dtype)
+ * can be the caller's prompt arena, e.g. the buffer later passed to
+ * fmd_engine_load. Both device buffers must be 16-byte aligned memory of the
+ * handle's device. A placeholder count different from `n_audio` is
+ * FMD_EINVAL, as in the reference (mod.rs:143-150). Needs weights, not a KV
+ * reservation. */
+int fmd_splice_audio(fmd_handle* h, const int32_t* token_ids, int64_t n_ids, const void* audio_embeds,
+                     int64_t n_audio, int32_t audio_dtype, int32_t audio_token_id, void* out);
+
 /* Open a sequence slot with room for `capacity` positions: the per-sequence
  * analogue of `KvCache::new` (qwen3.rs:41-55). Fails with FMD_ENOMEM when the
  * pool has too few free pages. */
@@ -204,7 +218,10 @@ int fmd_decode_step(fmd_handle* h, int32_t n, const int32_t* slots, const int32_
 
 /* Copy a request queue and its prompt-embedding arena (`embed_rows` x hidden,
  * dtype `embeds_dtype`) into device memory. Requests are served in the given
- * order; sort them by prompt length first to mirror engine.rs:385. */
+ * order; sort them by prompt length first to mirror engine.rs:385. The arena
+ * may be host memory, or device memory of the handle's device in the
+ * activation dtype (e.g. rows written by fmd_splice_audio), which is copied on
+ * the device. */
 int fmd_engine_load(fmd_handle* h, const fmd_request* reqs, int32_t n_reqs,
                     const void* embeds, int64_t embed_rows, int32_t embeds_dtype);
 

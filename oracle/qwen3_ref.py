@@ -457,3 +457,33 @@ def generate(model: Qwen3Ref, embeds, budget: int, eos_id: int = EOS_TOKEN_ID,
             break
         logits = model.decode_step(tok, caches)
     return out, hist
+
+
+def splice_audio(model: Qwen3Ref, token_ids, audio_embeds, audio_token_id: int) -> torch.Tensor:
+    """`MossModel::splice_audio` (model/mod.rs:134-180): the prompt embedding of
+    one sequence. The ids are walked as alternating runs of text and audio
+    placeholders; text runs are embedded, audio runs are taken in order from
+    `audio_embeds` (converted to the activation dtype, mod.rs:141), and the
+    parts are concatenated. A placeholder count different from the number of
+    audio rows is an error (mod.rs:143-150). Returns `(len(ids), hidden)`."""
+    ids = [int(i) for i in np.asarray(token_ids).reshape(-1)]
+    audio = model.act.r(torch.as_tensor(np.asarray(audio_embeds, dtype=np.float32)).reshape(-1, model.cfg.hidden_size))
+    n_slots = sum(1 for i in ids if i == audio_token_id)
+    if n_slots != audio.shape[0]:
+        raise ValueError(f"prompt has {n_slots} audio placeholders but the encoder produced "
+                         f"{audio.shape[0]} embeddings")
+    if n_slots == 0:
+        return model.embed(ids)
+    parts, used, i = [], 0, 0
+    while i < len(ids):
+        is_audio = ids[i] == audio_token_id
+        j = i
+        while j < len(ids) and (ids[j] == audio_token_id) == is_audio:
+            j += 1
+        if is_audio:
+            parts.append(audio[used:used + (j - i)])
+            used += j - i
+        else:
+            parts.append(model.embed(ids[i:j]))
+        i = j
+    return torch.cat(parts, 0)
