@@ -1,0 +1,333 @@
+// Chunked-prefill flash attention over the paged KV cache on the
+// 5th-generation tensor cores.
+//
+// Computes `Attention::forward` of crates/fmd-core/src/model/qwen3.rs:229-257
+// for the prompt rows of a step (`Qwen3::prefill`, qwen3.rs:475-496): causal
+// scores of each query row against every cached key up to its own position,
+// softmax, weighted sum of the values, for the two query heads that share a kv
+// head (GQA 16/8, qwen3.rs:237-241).
+//
+// One CTA per (prefill block of <= 64 consecutive rows of one sequence, kv
+// head h). The block's rows of query heads 2h and 2h+1 are stacked into one
+// 128-row MMA tile (rows 0-63 head 2h, 64-127 head 2h+1), so every K/V page
+// tile is read once for both heads:
+//  * warp 0 (one lane): TMA loads of the query tile (four 64x64 boxes,
+//    128-byte swizzle) and of each key page's K and V tiles (2 x 16 KB) into a
+//    3-stage full/empty mbarrier ring;
+//  * warp 1 (one lane): tcgen05.mma, f32 accumulators in tensor memory:
+//    S_j = Q K_j^T (M 128, N 64 keys, K 128 dims; double-buffered S), then
+//    O_j = P_j V_j (M 128, N 128 dims, K 64 keys; V read MN-major straight
+//    from the page tile);
+//  * warps 2-5 (one thread per tile row = tensor-memory lane): the online
+//    softmax in the exp2 domain. Each thread loads its row of S_j, applies the
+//    causal bound (key <= the row's position), writes P_j = exp2(S - m) as
+//    16-bit values into a 128-byte-swizzled shared tile (the A operand of the
+//    PV MMA), and folds the previous tile's O_{j-1} into a register
+//    accumulator rescaled to the running maximum; at the end it divides by
+//    the row sum and stores ctx.
+// Every wait is bounded; a timeout sets the status word, stops issuing work,
+// waits (bounded) for copies and MMAs in flight and frees tensor memory.
+#include <cuda.h>
+#include <float.h>
+#include <math.h>
+
+#include "fmd_kernels.cuh"
+
+namespace fmd {
+
+namespace {
+
+constexpr int kPfStages = 3;
+constexpr int kPfQBytes = 32768;   // 128 rows x 128 dims x 2 bytes
+constexpr int kPfKvBytes = 32768;  // K (16 KB) + V (16 KB) of one 64-position page
+constexpr int kPfPBytes = 16384;   // 128 rows x 64 keys x 2 bytes
+constexpr int kPfBox = 8192;       // one 64 x 64 TMA box
+constexpr uint32_t kPfWaitLimit = 1u << 24;
+constexpr int kPfStatusTimeout = -110;
+constexpr int kPfTmemCols = 256;   // S0 [0, 64), S1 [64, 128), O [128, 256)
+
+// Shared-memory descriptor of an MN-major operand with the 128-byte swizzle:
+// 64 contiguous elements of the MN dimension per 128-byte row, one row per K
+// index, 8-row atoms 1024 bytes apart along K (stride byte offset), 64-element
+// MN blocks `mn_block_bytes` apart (leading byte offset).
+FMD_DEV uint64_t umma_desc_sw128_mn(uint32_t saddr, uint32_t mn_block_bytes) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((mn_block_bytes >> 4) & 0x3FFFu) << 16) |
+         ((uint64_t)(1024 >> 4) << 32) | ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+FMD_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
+
+template <typename T>
+__global__ void __launch_bounds__(192, 1)
+    k_attn_prefill_tc(const __grid_constant__ CUtensorMap kvmap, const __grid_constant__ CUtensorMap qmap, Plan p,
+                      int Hq, int Hkv, KvView kv, int layer, float scale_log2, T* __restrict__ ctx,
+                      int* __restrict__ status) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t q_full, kv_full[kPfStages], kv_empty[kPfStages], s_full[2], s_empty[2], p_full,
+      o_full, mma_done;
+  __shared__ uint32_t tmem_base_s;
+  __shared__ int abort_s;
+  griddep_launch();
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;  // swizzle atoms need 1024-byte alignment
+  uint8_t* base_p = smem_raw + (base - raw);
+  const uint32_t q_s = base, p_s = base + kPfQBytes, kv_s = p_s + kPfPBytes;
+  uint8_t* p_sp = base_p + kPfQBytes;
+
+  griddep_wait();  // q, the KV rows of this step and the plan come from earlier kernels
+  const int n_blocks = p.counts->n_pblocks;
+  if ((int)blockIdx.x >= n_blocks) return;  // whole CTA, before any barrier or tensor memory exists
+  // the last blocks of a chunk see the longest histories: start those first
+  const int b = n_blocks - 1 - (int)blockIdx.x, h = blockIdx.y;
+  const int r0 = p.pb_row0[b], n = p.pb_n[b];
+  const int slot = p.row_slot[r0], pos0 = p.row_pos[r0];
+  const int kv_len = pos0 + n;
+  const int T_tiles = (kv_len + kPageTokens - 1) / kPageTokens;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&q_full, 1);
+    for (int s = 0; s < kPfStages; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&s_full[s], 1);
+      mbar_init(&s_empty[s], 128);
+    }
+    mbar_init(&p_full, 128);
+    mbar_init(&o_full, 1);
+    mbar_init(&mma_done, 1);
+    abort_s = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&tmem_base_s, kPfTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base_s;
+  volatile int* abort_v = &abort_s;
+
+  if (warp == 0) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      prefetch_tmap(&kvmap);
+      prefetch_tmap(&qmap);
+      mbar_arrive_expect_tx(&q_full, kPfQBytes);
+      const int xq0 = 2 * h * kHeadDim, xq1 = (2 * h + 1) * kHeadDim;
+      tma_load_2d(base_p + 0 * kPfBox, &qmap, xq0, r0, &q_full);        // rows 0-63: head 2h, dims 0-63
+      tma_load_2d(base_p + 1 * kPfBox, &qmap, xq1, r0, &q_full);        // rows 64-127: head 2h+1, dims 0-63
+      tma_load_2d(base_p + 2 * kPfBox, &qmap, xq0 + 64, r0, &q_full);   // dims 64-127
+      tma_load_2d(base_p + 3 * kPfBox, &qmap, xq1 + 64, r0, &q_full);
+      const int* ptab = kv.page_table + (size_t)slot * kv.max_pages_per_slot;
+      int issued = 0;
+      for (int j = 0; j < T_tiles; ++j) {
+        const int st = j % kPfStages;
+        if (j >= kPfStages &&
+            (*abort_v || !mbar_wait_bounded(&kv_empty[st], ((j / kPfStages) - 1) & 1, kPfWaitLimit))) {
+          *abort_v = 1;
+          break;
+        }
+        const int page = ptab[j];
+        const int yk = (int)(((((size_t)layer * kv.n_pages + page) * 2 + 0) * Hkv + h) * kPageTokens);
+        const int yv = yk + Hkv * kPageTokens;
+        uint8_t* dst = base_p + kPfQBytes + kPfPBytes + st * kPfKvBytes;
+        mbar_arrive_expect_tx(&kv_full[st], kPfKvBytes);
+        tma_load_2d(dst, &kvmap, 0, yk, &kv_full[st]);
+        tma_load_2d(dst + kPfBox, &kvmap, 64, yk, &kv_full[st]);
+        tma_load_2d(dst + 2 * kPfBox, &kvmap, 0, yv, &kv_full[st]);
+        tma_load_2d(dst + 3 * kPfBox, &kvmap, 64, yv, &kv_full[st]);
+        issued = j + 1;
+      }
+      // copies still in flight must land before the CTA can retire (bounded)
+      mbar_wait_bounded(&q_full, 0, kPfWaitLimit);
+      for (int j = issued > kPfStages ? issued - kPfStages : 0; j < issued; ++j)
+        mbar_wait_bounded(&kv_full[j % kPfStages], (j / kPfStages) & 1, kPfWaitLimit);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr bool kBf = Act<T>::kIsBf16;
+      constexpr uint32_t idesc_s = umma_idesc_f16(kBf, 128, 64);
+      constexpr uint32_t idesc_o = umma_idesc_f16(kBf, 128, 128) | (1u << 16);  // B (V) MN-major
+      const uint32_t o_tmem = tmem + 128;
+      auto pv = [&](int i) -> bool {
+        if (*abort_v || !mbar_wait_bounded(&p_full, i & 1, kPfWaitLimit)) return false;
+        tc_fence_after();
+        const uint32_t v = kv_s + (i % kPfStages) * kPfKvBytes + 2 * kPfBox;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          umma_f16(o_tmem, umma_desc_sw128(p_s + kk * 32), umma_desc_sw128_mn(v + kk * 2048, kPfBox), idesc_o,
+                   kk != 0);
+        umma_commit(&o_full);
+        umma_commit(&kv_empty[i % kPfStages]);
+        return true;
+      };
+      bool ok = !*abort_v && mbar_wait_bounded(&q_full, 0, kPfWaitLimit);
+      for (int j = 0; ok && j < T_tiles; ++j) {
+        const int st = j % kPfStages, sb = j & 1;
+        if (*abort_v || !mbar_wait_bounded(&kv_full[st], (j / kPfStages) & 1, kPfWaitLimit) ||
+            (j >= 2 && !mbar_wait_bounded(&s_empty[sb], ((j >> 1) - 1) & 1, kPfWaitLimit))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t k = kv_s + st * kPfKvBytes;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t a = q_s + (kk < 4 ? kk * 32 : 2 * kPfBox + (kk - 4) * 32);
+          const uint32_t bk = k + (kk < 4 ? kk * 32 : kPfBox + (kk - 4) * 32);
+          umma_f16(tmem + sb * 64, umma_desc_sw128(a), umma_desc_sw128(bk), idesc_s, kk != 0);
+        }
+        umma_commit(&s_full[sb]);
+        if (j >= 1 && !pv(j - 1)) {
+          ok = false;
+          break;
+        }
+      }
+      if (ok) ok = pv(T_tiles - 1);
+      if (!ok) *abort_v = 1;
+      umma_commit(&mma_done);  // every MMA issued so far has completed when this fires
+      mbar_wait_bounded(&mma_done, 0, kPfWaitLimit);
+    }
+  } else {
+    // ---------------- softmax + output: one thread per tile row ----------------
+    const int q4 = warp & 3;
+    const int row = q4 * 32 + lane;
+    const int hs = row >> 6, ri = row & 63;
+    const int qpos = pos0 + ri;
+    const uint32_t lane_addr = tmem + ((uint32_t)(q4 * 32) << 16);
+    float o[128];
+#pragma unroll
+    for (int i = 0; i < 128; ++i) o[i] = 0.f;
+    float m = -INFINITY, l = 0.f, m_o = -INFINITY;
+    bool ok = true;
+    auto fold_o = [&](int i, float m_p) {
+      // O_reg = O_reg * exp2(m_o - m_p) + O_i, O_i computed with maximum m_p
+      if (!ok || *abort_v || !mbar_wait_bounded(&o_full, i & 1, kPfWaitLimit)) {
+        ok = false;
+        return;
+      }
+      tc_fence_after();
+      const float f = exp2f(m_o - m_p);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld32(lane_addr + 128 + c * 32, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i2 = 0; i2 < 32; ++i2) o[c * 32 + i2] = fmaf(o[c * 32 + i2], f, __uint_as_float(v[i2]));
+      }
+      m_o = m_p;
+    };
+    float m_pend = -INFINITY;  // maximum that P of the pending tile was computed with
+    for (int j = 0; j < T_tiles && ok; ++j) {
+      const int sb = j & 1;
+      if (*abort_v || !mbar_wait_bounded(&s_full[sb], (j >> 1) & 1, kPfWaitLimit)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float s[64];
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t v[32];
+        tmem_ld32(lane_addr + sb * 64 + c * 32, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i2 = 0; i2 < 32; ++i2) s[c * 32 + i2] = __uint_as_float(v[i2]);
+      }
+      tc_fence_before();
+      mbar_arrive(&s_empty[sb]);
+      const int key0 = j * kPageTokens;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 64; ++c) {
+        s[c] = key0 + c <= qpos ? s[c] * scale_log2 : -INFINITY;
+        mx = fmaxf(mx, s[c]);
+      }
+      const float mn = fmaxf(m, mx);  // finite from the first tile on: key 0 <= qpos
+      const float corr = exp2f(m - mn);
+      float ps = 0.f;
+#pragma unroll
+      for (int c = 0; c < 64; ++c) {
+        s[c] = exp2f(s[c] - mn);
+        ps += s[c];
+      }
+      l = l * corr + ps;
+      m = mn;
+      if (j >= 1) fold_o(j - 1, m_pend);  // PV_{j-1} done: P and O buffers are free again
+      if (!ok) break;
+      // P_j -> the 128-byte-swizzled A tile: row `row`, 16-byte chunk c holds keys 8c .. 8c+7
+      uint8_t* prow = p_sp + row * 128;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        uint4 u;
+        u.x = Act<T>::pack2(s[8 * c + 0], s[8 * c + 1]);
+        u.y = Act<T>::pack2(s[8 * c + 2], s[8 * c + 3]);
+        u.z = Act<T>::pack2(s[8 * c + 4], s[8 * c + 5]);
+        u.w = Act<T>::pack2(s[8 * c + 6], s[8 * c + 7]);
+        *reinterpret_cast<uint4*>(prow + ((c ^ (row & 7)) << 4)) = u;
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&p_full);
+      m_pend = mn;
+    }
+    if (ok) fold_o(T_tiles - 1, m_pend);
+    if (!ok) *abort_v = 1;
+    if (ok && ri < n) {
+      const float inv = 1.f / l;
+      T* dst = ctx + (size_t)(r0 + ri) * Hq * kHeadDim + (2 * h + hs) * kHeadDim;
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        uint4 u;
+        u.x = Act<T>::pack2(o[8 * c + 0] * inv, o[8 * c + 1] * inv);
+        u.y = Act<T>::pack2(o[8 * c + 2] * inv, o[8 * c + 3] * inv);
+        u.z = Act<T>::pack2(o[8 * c + 4] * inv, o[8 * c + 5] * inv);
+        u.w = Act<T>::pack2(o[8 * c + 6] * inv, o[8 * c + 7] * inv);
+        *reinterpret_cast<uint4*>(dst + 8 * c) = u;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0 && abort_s) atomicExch(status, kPfStatusTimeout);
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kPfTmemCols);
+  }
+}
+
+size_t attn_prefill_smem_bytes() { return 1024 + kPfQBytes + kPfPBytes + kPfStages * kPfKvBytes; }
+
+}  // namespace
+
+cudaError_t init_attn_prefill() {
+  const int bytes = (int)attn_prefill_smem_bytes();
+  cudaError_t e = cudaFuncSetAttribute(k_attn_prefill_tc<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       bytes);
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(k_attn_prefill_tc<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+}
+
+void launch_attn_prefill_tc(ActType at, const void* kv_tmap, const void* q_tmap, const Plan& p, int PB, int Hq,
+                            int Hkv, const KvView& kv, int layer, float scale, void* ctx, int* status,
+                            cudaStream_t s) {
+  const float scale_log2 = scale * 1.4426950408889634f;
+  const CUtensorMap& km = *reinterpret_cast<const CUtensorMap*>(kv_tmap);
+  const CUtensorMap& qm = *reinterpret_cast<const CUtensorMap*>(q_tmap);
+  const size_t smem = attn_prefill_smem_bytes();
+  if (at == kBF16)
+    launch_pdl(k_attn_prefill_tc<__nv_bfloat16>, dim3(PB, Hkv), dim3(192), smem, s, km, qm, p, Hq, Hkv, kv, layer,
+               scale_log2, (__nv_bfloat16*)ctx, status);
+  else
+    launch_pdl(k_attn_prefill_tc<__half>, dim3(PB, Hkv), dim3(192), smem, s, km, qm, p, Hq, Hkv, kv, layer,
+               scale_log2, (__half*)ctx, status);
+}
+
+}  // namespace fmd

@@ -392,170 +392,6 @@ __global__ void __launch_bounds__(256) k_qkv_epilogue(Plan p, const float* __res
 }
 
 // ---------------------------------------------------------------------------
-// Chunked-prefill flash attention (qwen3.rs:229-257 with the causal mask of
-// :523-562): one CTA per (block of <= 32 query rows of one sequence, kv head)
-// covers both query heads of the group (4 warps = 2 heads x 2 x 16 rows) so
-// each K/V tile is loaded once. K/V tiles = one 64-position page, cp.async
-// double-buffered into XOR-swizzled shared memory; QK^T and PV on mma.sync.
-// Positions at or beyond the cached length are zero-filled, so masked columns
-// never multiply a stale value.
-// ---------------------------------------------------------------------------
-template <typename T>
-__global__ void __launch_bounds__(128) k_attn_prefill(Plan p, int Hq, const T* __restrict__ q, KvView kv, int layer,
-                                                      float scale_log2, T* __restrict__ ctx) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  griddep_launch();
-  griddep_wait();
-  const int n_blocks = p.counts->n_pblocks;
-  for (int b = blockIdx.x; b < n_blocks; b += gridDim.x) {
-  const int h = blockIdx.y;
-  const int r0 = p.pb_row0[b], n = p.pb_n[b];
-  const int slot = p.row_slot[r0], pos0 = p.row_pos[r0];
-  const int kv_len = pos0 + n;
-  const int n_tiles = (kv_len + 63) >> 6;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  const int qh = 2 * h + (warp >> 1);
-  const int tq0 = (warp & 1) * 16;
-  const int ra = tq0 + g, rb = ra + 8;
-  const int qpa = pos0 + ra, qpb = pos0 + rb;
-  const int* ptab = kv.page_table + (size_t)slot * kv.max_pages_per_slot;
-  const T* kvb = reinterpret_cast<const T*>(kv.base);
-  const size_t v_off = (size_t)kv.kv_heads * kPageTokens * kHeadDim;
-
-  uint32_t qf[8][4];
-  {
-    const uint32_t* qa = reinterpret_cast<const uint32_t*>(q + (size_t)(r0 + ra) * Hq * kHeadDim + qh * kHeadDim);
-    const uint32_t* qb = reinterpret_cast<const uint32_t*>(q + (size_t)(r0 + rb) * Hq * kHeadDim + qh * kHeadDim);
-#pragma unroll
-    for (int ks = 0; ks < 8; ++ks) {
-      qf[ks][0] = ra < n ? qa[ks * 8 + t] : 0u;
-      qf[ks][1] = rb < n ? qb[ks * 8 + t] : 0u;
-      qf[ks][2] = ra < n ? qa[ks * 8 + 4 + t] : 0u;
-      qf[ks][3] = rb < n ? qb[ks * 8 + 4 + t] : 0u;
-    }
-  }
-  float o[16][4];
-#pragma unroll
-  for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-  float m_a = -FLT_MAX, m_b = -FLT_MAX, l_a = 0.f, l_b = 0.f;
-
-  auto load_tile = [&](int stage, int kt) {
-    const int page = ptab[kt];
-    const T* ksrc = kvb + kv.elem_offset(layer, page, 0, h);
-    const T* vsrc = ksrc + v_off;
-    const int valid = min(64, kv_len - kt * 64);
-    uint8_t* ks = smem + stage * 32768;
-    uint8_t* vs = ks + 16384;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int c = threadIdx.x + i * 128;
-      const int row = c >> 4, ch = c & 15;
-      const int soff = row * 256 + ((ch ^ (row & 7)) << 4);
-      const int bytes = row < valid ? 16 : 0;
-      cp_async16(ks + soff, ksrc + row * kHeadDim + ch * 8, bytes);
-      cp_async16(vs + soff, vsrc + row * kHeadDim + ch * 8, bytes);
-    }
-    cp_async_commit();
-  };
-
-  load_tile(0, 0);
-  for (int kt = 0; kt < n_tiles; ++kt) {
-    if (kt + 1 < n_tiles) {
-      load_tile((kt + 1) & 1, kt + 1);
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
-    __syncthreads();
-    const uint32_t ks_base = smem_u32(smem + (kt & 1) * 32768);
-    const uint32_t vs_base = ks_base + 16384;
-
-    float s[8][4];
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
-      s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
-      const int key = nt * 8 + (lane & 7);
-#pragma unroll
-      for (int kp = 0; kp < 4; ++kp) {
-        const int ch = 4 * kp + (lane >> 3);
-        uint32_t rr[4];
-        ldmatrix_x4(rr, ks_base + key * 256 + ((ch ^ (key & 7)) << 4));
-        mma16816<T>(s[nt], qf[2 * kp], rr[0], rr[1]);
-        mma16816<T>(s[nt], qf[2 * kp + 1], rr[2], rr[3]);
-      }
-    }
-    float mx_a = -FLT_MAX, mx_b = -FLT_MAX;
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
-      const int key = kt * 64 + nt * 8 + 2 * t;
-      s[nt][0] = key <= qpa ? s[nt][0] * scale_log2 : -FLT_MAX;
-      s[nt][1] = key + 1 <= qpa ? s[nt][1] * scale_log2 : -FLT_MAX;
-      s[nt][2] = key <= qpb ? s[nt][2] * scale_log2 : -FLT_MAX;
-      s[nt][3] = key + 1 <= qpb ? s[nt][3] * scale_log2 : -FLT_MAX;
-      mx_a = fmaxf(mx_a, fmaxf(s[nt][0], s[nt][1]));
-      mx_b = fmaxf(mx_b, fmaxf(s[nt][2], s[nt][3]));
-    }
-    mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 1));
-    mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, 2));
-    mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 1));
-    mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, 2));
-    const float mn_a = fmaxf(m_a, mx_a), mn_b = fmaxf(m_b, mx_b);
-    const float ca = exp2f(m_a - mn_a), cb = exp2f(m_b - mn_b);
-    float sum_a = 0.f, sum_b = 0.f;
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
-      s[nt][0] = exp2f(s[nt][0] - mn_a);
-      s[nt][1] = exp2f(s[nt][1] - mn_a);
-      s[nt][2] = exp2f(s[nt][2] - mn_b);
-      s[nt][3] = exp2f(s[nt][3] - mn_b);
-      sum_a += s[nt][0] + s[nt][1];
-      sum_b += s[nt][2] + s[nt][3];
-    }
-    l_a = l_a * ca + sum_a;
-    l_b = l_b * cb + sum_b;
-    m_a = mn_a;
-    m_b = mn_b;
-#pragma unroll
-    for (int dn = 0; dn < 16; ++dn) {
-      o[dn][0] *= ca; o[dn][1] *= ca;
-      o[dn][2] *= cb; o[dn][3] *= cb;
-    }
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-      uint32_t pa[4];
-      pa[0] = Act<T>::pack2(s[2 * kk][0], s[2 * kk][1]);
-      pa[1] = Act<T>::pack2(s[2 * kk][2], s[2 * kk][3]);
-      pa[2] = Act<T>::pack2(s[2 * kk + 1][0], s[2 * kk + 1][1]);
-      pa[3] = Act<T>::pack2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
-      const int key = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-#pragma unroll
-      for (int dp = 0; dp < 8; ++dp) {
-        const int ch = 2 * dp + (lane >> 4);
-        uint32_t rr[4];
-        ldmatrix_x4_trans(rr, vs_base + key * 256 + ((ch ^ (key & 7)) << 4));
-        mma16816<T>(o[2 * dp], pa, rr[0], rr[1]);
-        mma16816<T>(o[2 * dp + 1], pa, rr[2], rr[3]);
-      }
-    }
-    __syncthreads();
-  }
-  l_a += __shfl_xor_sync(0xffffffffu, l_a, 1);
-  l_a += __shfl_xor_sync(0xffffffffu, l_a, 2);
-  l_b += __shfl_xor_sync(0xffffffffu, l_b, 1);
-  l_b += __shfl_xor_sync(0xffffffffu, l_b, 2);
-  const float ia = 1.f / l_a, ib = 1.f / l_b;
-  T* ca_ = ctx + (size_t)(r0 + ra) * Hq * kHeadDim + qh * kHeadDim;
-  T* cb_ = ctx + (size_t)(r0 + rb) * Hq * kHeadDim + qh * kHeadDim;
-#pragma unroll
-  for (int dn = 0; dn < 16; ++dn) {
-    if (ra < n) *reinterpret_cast<uint32_t*>(ca_ + dn * 8 + 2 * t) = Act<T>::pack2(o[dn][0] * ia, o[dn][1] * ia);
-    if (rb < n) *reinterpret_cast<uint32_t*>(cb_ + dn * 8 + 2 * t) = Act<T>::pack2(o[dn][2] * ib, o[dn][3] * ib);
-  }
-  __syncthreads();
-  }
-}
-
-// ---------------------------------------------------------------------------
 // SwiGLU (qwen3.rs:288-292): h = rnd(rnd(silu(rnd(gate))) * rnd(up)); gate/up
 // columns are interleaved in 32-groups (gate_col / up_col).
 // ---------------------------------------------------------------------------
@@ -699,14 +535,6 @@ void launch_qkv_epilogue(ActType at, const Plan& p, int R, const float* part, Pa
                                                         layer, eps));
 }
 
-void launch_attn_prefill(ActType at, const Plan& p, int PB, int Hq, int Hkv, const void* q, const KvView& kv,
-                         int layer, float scale, void* ctx, cudaStream_t s) {
-  const float scale_log2 = scale * 1.4426950408889634f;
-  dim3 grid(PB, Hkv);
-  const int smem = 65536;
-  FMD_DISPATCH(at, launch_pdl(k_attn_prefill<T>, grid, 128, smem, s, p, Hq, (const T*)q, kv, layer, scale_log2, (T*)ctx));
-}
-
 void launch_residual_norm(ActType at, const int* n_rows_ptr, int R, void* x, const float* part, PartSplit split,
                           size_t split_stride, const void* w, void* xn, int H, float eps, cudaStream_t s) {
   FMD_DISPATCH(at, launch_pdl(k_residual_norm<T>, R, 128, 0, s, n_rows_ptr, (T*)x, part, split, split_stride, (const T*)w,
@@ -723,11 +551,7 @@ void launch_logits_argmax(ActType at, const int* n_sample_ptr, int B, const floa
   FMD_DISPATCH(at, launch_pdl(k_logits_argmax<T>, B, 1024, 0, s, n_sample_ptr, part, V, logits, next_ids));
 }
 
-cudaError_t init_kernels() {
-  cudaError_t e = cudaFuncSetAttribute(k_attn_prefill<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, 65536);
-  if (e != cudaSuccess) return e;
-  return cudaFuncSetAttribute(k_attn_prefill<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, 65536);
-}
+cudaError_t init_kernels() { return cudaSuccess; }
 
 void launch_dequant(ActType at, const LinW& W, float* out, cudaStream_t s) {
   FMD_DISPATCH(at, k_dequant<T><<<1024, 256, 0, s>>>(W, out));

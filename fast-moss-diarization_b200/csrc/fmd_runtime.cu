@@ -120,11 +120,13 @@ struct fmd_handle {
   // kv pool + work buffers
   bool reserved = false;
   int max_slots = 0, max_rows = 0, n_pages = 0, max_pages_per_slot = 0;
-  int pb_max = 0, di_max = 0, di_grid = 0, pb_grid = 0;
+  int pb_max = 0, di_max = 0, di_grid = 0;
   KvView kv{};
   alignas(64) CUtensorMap kv_tmap;  // the KV pool as [rows][128] for TMA tile loads
   // activation operands of the mixed-step tensor-core projections
   alignas(64) CUtensorMap amap_xn, amap_ctx, amap_hbuf;
+  alignas(64) CUtensorMap qmap;  // the query buffer as [rows][Hq x 128] (prefill attention tiles)
+  bool q_ready = false;
   bool tc_ready = false;
   void* tmap_encode = nullptr;      // cuTensorMapEncodeTiled
   int* attn_counters = nullptr;     // [max_slots][kv_heads] split-KV merge counters
@@ -543,8 +545,8 @@ void run_forward(fmd_handle* h, float* logits_dev, const void* arena, bool decod
     if (h->record_attn_events) cudaEventRecordWithFlags(h->attn_events[2 * l + 1], s, cudaEventRecordExternal);
     trace(h, "attn_decode", l);
     if (!decode_only) {
-      launch_attn_prefill(h->at, h->plan, h->pb_grid, h->Hq(), h->Hkv(), h->qbuf, h->kv, l, h->attn_scale, h->ctx,
-                          s);
+      launch_attn_prefill_tc(h->at, &h->kv_tmap, &h->qmap, h->plan, h->pb_max, h->Hq(), h->Hkv(), h->kv, l,
+                             h->attn_scale, h->ctx, h->d_status, s);
       trace(h, "attn_prefill", l);
     }
     const PartSplit sp_o = mixed_linear(h, L.o, L.tc_o, h->ctx, h->amap_ctx, h->Hq() * kHeadDim);
@@ -777,7 +779,7 @@ int fmd_create(const fmd_config* cfg, int32_t precision, int32_t device, fmd_han
   h->device = device;
   h->attn_scale = (float)(1.0 / std::sqrt((double)cfg->head_dim));
   if (cudaSetDevice(device) != cudaSuccess || cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking) != cudaSuccess ||
-      init_kernels() != cudaSuccess || init_attn_decode() != cudaSuccess || init_gemv() != cudaSuccess ||
+      init_kernels() != cudaSuccess || init_attn_decode() != cudaSuccess || init_attn_prefill() != cudaSuccess || init_gemv() != cudaSuccess ||
       init_gemm_tc() != cudaSuccess) {
     cudaGetLastError();
     delete h;
@@ -947,7 +949,6 @@ int fmd_kv_reserve(fmd_handle* h, int32_t max_slots, int64_t max_tokens_total, i
   h->di_max = (int)std::min<int64_t>((int64_t)max_slots * h->max_pages_per_slot,
                                      (int64_t)h->n_pages * kPageTokens / kDecodeItemTokens + 2 * max_slots + 1);
   h->di_grid = 296;
-  h->pb_grid = std::min(h->pb_max, 148);
   const int HqD = h->Hq() * kHeadDim;
   void* p;
   auto A = [&](size_t bytes, void** dst) { return dev_alloc(h, bytes, dst, &h->work_bytes); };
@@ -991,6 +992,8 @@ int fmd_kv_reserve(fmd_handle* h, int32_t max_slots, int64_t max_tokens_total, i
     h->tc_ready = tc_make_map(fn, &h->amap_xn, h->xn, (uint64_t)H, (uint64_t)R, 128) &&
                   tc_make_map(fn, &h->amap_ctx, h->ctx, (uint64_t)HqD, (uint64_t)R, 128) &&
                   tc_make_map(fn, &h->amap_hbuf, h->hbuf, (uint64_t)I, (uint64_t)R, 128);
+    h->q_ready = tc_make_map(fn, &h->qmap, h->qbuf, (uint64_t)HqD, (uint64_t)R, 64);
+    if (!h->q_ready) return fail(h, FMD_EIO, "tensor map of the query buffer could not be encoded");
   }
   h->plan = h->layout.bind(h->d_plan);
   CK(cudaMallocHost((void**)&h->h_plan, h->layout.total * 4));

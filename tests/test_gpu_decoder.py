@@ -221,3 +221,40 @@ def test_full_layer_shapes(prec):
             want = m.decode_step(int(t), caches).numpy()
             assert rel_err(lg[0], want) < LOGIT_RTOL
             check_pick(int(nxt[0]), lg[0], want)
+
+
+def test_long_chunked_prefill_full_shapes():
+    """Chunked prefill at the BASELINE head shapes with histories past 2k
+    positions (qwen3.rs:475-496): two sequences prefilled together in chunks of
+    up to 1000 rows (tens of 64-row attention blocks per chunk, up to 41 key
+    pages per block), then a decode step; logits against the oracle."""
+    cfg = mid_config(num_hidden_layers=1)
+    w = syn.make_weights(cfg, seed=23)
+    m = oracle_model(cfg, w, "bf16", max_len=4096)
+    rng = np.random.default_rng(9)
+    lens = [2600, 1333]
+    prompts = [rng.standard_normal((n, cfg.hidden_size), dtype=np.float32) for n in lens]
+    with make_decoder(cfg, w, "bf16", slots=2, tokens=8192, rows=2048) as dec:
+        for s, n in enumerate(lens):
+            dec.open_slot(s, n + 8)
+        done = [0, 0]
+        last = [None, None]
+        while min(d - n for d, n in zip(done, lens)) < 0:
+            slots, parts = [], []
+            for s, n in enumerate(lens):
+                if done[s] < n:
+                    take = min(1000, n - done[s])
+                    slots.append(s)
+                    parts.append(prompts[s][done[s]:done[s] + take])
+                    done[s] += take
+            lg, _ = dec.prefill(slots, parts)
+            for i, s in enumerate(slots):
+                last[s] = lg[i]
+        for s, n in enumerate(lens):
+            caches = m.new_caches(1, n + 8)
+            want = m.logits(m.prefill(prompts[s][None], caches))[0, 0].numpy()
+            assert rel_err(last[s], want) < LOGIT_RTOL, s
+            tok = int(np.argmax(want))
+            lg, _ = dec.decode_step([s], [tok])
+            want = m.decode_step(tok, caches).numpy()
+            assert rel_err(lg[0], want) < LOGIT_RTOL, s
