@@ -10,21 +10,22 @@
 // One CTA per (prefill block of <= 64 consecutive rows of one sequence, kv
 // head h). The block's rows of query heads 2h and 2h+1 are stacked into one
 // 128-row MMA tile (rows 0-63 head 2h, 64-127 head 2h+1), so every K/V page
-// tile is read once for both heads:
+// tile is read once for both heads. CTAs take the blocks longest history
+// first (rank by kv length), so the longest blocks do not start last:
 //  * warp 0 (one lane): TMA loads of the query tile (four 64x64 boxes,
 //    128-byte swizzle) and of each key page's K and V tiles (2 x 16 KB) into a
 //    3-stage full/empty mbarrier ring;
 //  * warp 1 (one lane): tcgen05.mma, f32 accumulators in tensor memory:
-//    S_j = Q K_j^T (M 128, N 64 keys, K 128 dims; double-buffered S), then
-//    O_j = P_j V_j (M 128, N 128 dims, K 64 keys; V read MN-major straight
-//    from the page tile);
+//    S_j = Q K_j^T (M 128, N 64 keys, K 128 dims; S double-buffered), then
+//    O += P_j V_j (M 128, N 128 dims, K 64 keys; V read MN-major straight from
+//    the page tile; O stays in tensor memory for the whole block);
 //  * warps 2-5 (one thread per tile row = tensor-memory lane): the online
-//    softmax in the exp2 domain. Each thread loads its row of S_j, applies the
-//    causal bound (key <= the row's position), writes P_j = exp2(S - m) as
-//    16-bit values into a 128-byte-swizzled shared tile (the A operand of the
-//    PV MMA), and folds the previous tile's O_{j-1} into a register
-//    accumulator rescaled to the running maximum; at the end it divides by
-//    the row sum and stores ctx.
+//    softmax in the exp2 domain with a lazily updated reference maximum: P_j =
+//    exp2(S_j - m_ref) goes as 16-bit values into a double-buffered
+//    128-byte-swizzled shared tile (the A operand of the PV MMA); m_ref only
+//    moves when a row maximum exceeds it by more than 2^8, and only then is
+//    the row of O in tensor memory rescaled (load, scale, store). At the end
+//    each thread divides its row of O by the row sum and stores ctx.
 // Every wait is bounded; a timeout sets the status word, stops issuing work,
 // waits (bounded) for copies and MMAs in flight and frees tensor memory.
 #include <cuda.h>
@@ -40,11 +41,12 @@ namespace {
 constexpr int kPfStages = 3;
 constexpr int kPfQBytes = 32768;   // 128 rows x 128 dims x 2 bytes
 constexpr int kPfKvBytes = 32768;  // K (16 KB) + V (16 KB) of one 64-position page
-constexpr int kPfPBytes = 16384;   // 128 rows x 64 keys x 2 bytes
+constexpr int kPfPBytes = 16384;   // one P buffer: 128 rows x 64 keys x 2 bytes (two buffers)
 constexpr int kPfBox = 8192;       // one 64 x 64 TMA box
 constexpr uint32_t kPfWaitLimit = 1u << 24;
 constexpr int kPfStatusTimeout = -110;
 constexpr int kPfTmemCols = 256;   // S0 [0, 64), S1 [64, 128), O [128, 256)
+constexpr float kPfRescale = 8.f;  // log2 headroom before the reference maximum moves
 
 // Shared-memory descriptor of an MN-major operand with the 128-byte swizzle:
 // 64 contiguous elements of the MN dimension per 128-byte row, one row per K
@@ -63,24 +65,37 @@ __global__ void __launch_bounds__(192, 1)
                       int Hq, int Hkv, KvView kv, int layer, float scale_log2, T* __restrict__ ctx,
                       int* __restrict__ status) {
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t q_full, kv_full[kPfStages], kv_empty[kPfStages], s_full[2], s_empty[2], p_full,
-      o_full, mma_done;
+  __shared__ __align__(8) uint64_t q_full, kv_full[kPfStages], kv_empty[kPfStages], s_full[2], s_empty[2],
+      p_full[2], p_empty[2], o_full, o_final, mma_done;
   __shared__ uint32_t tmem_base_s;
-  __shared__ int abort_s;
+  __shared__ int abort_s, block_s;
+  __shared__ int klen_s[kMaxPrefillBlocks];
   griddep_launch();
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;  // swizzle atoms need 1024-byte alignment
   uint8_t* base_p = smem_raw + (base - raw);
-  const uint32_t q_s = base, p_s = base + kPfQBytes, kv_s = p_s + kPfPBytes;
+  const uint32_t q_s = base, p_s = base + kPfQBytes, kv_s = p_s + 2 * kPfPBytes;
   uint8_t* p_sp = base_p + kPfQBytes;
 
   griddep_wait();  // q, the KV rows of this step and the plan come from earlier kernels
-  const int n_blocks = p.counts->n_pblocks;
+  const int n_blocks = min(p.counts->n_pblocks, kMaxPrefillBlocks);
   if ((int)blockIdx.x >= n_blocks) return;  // whole CTA, before any barrier or tensor memory exists
-  // the last blocks of a chunk see the longest histories: start those first
-  const int b = n_blocks - 1 - (int)blockIdx.x, h = blockIdx.y;
+  // CTA x takes the block of rank x by kv length (longest first, ties by index)
+  for (int i = threadIdx.x; i < n_blocks; i += blockDim.x) klen_s[i] = p.row_pos[p.pb_row0[i]] + p.pb_n[i];
+  __syncthreads();
+  for (int i = threadIdx.x; i < n_blocks; i += blockDim.x) {
+    const int ki = klen_s[i];
+    int rank = 0;
+    for (int k = 0; k < n_blocks; ++k) {
+      const int kk = klen_s[k];
+      rank += (kk > ki) || (kk == ki && k < i);
+    }
+    if (rank == (int)blockIdx.x) block_s = i;
+  }
+  __syncthreads();
+  const int b = block_s, h = blockIdx.y;
   const int r0 = p.pb_row0[b], n = p.pb_n[b];
   const int slot = p.row_slot[r0], pos0 = p.row_pos[r0];
   const int kv_len = pos0 + n;
@@ -95,9 +110,11 @@ __global__ void __launch_bounds__(192, 1)
     for (int s = 0; s < 2; ++s) {
       mbar_init(&s_full[s], 1);
       mbar_init(&s_empty[s], 128);
+      mbar_init(&p_full[s], 128);
+      mbar_init(&p_empty[s], 1);
     }
-    mbar_init(&p_full, 128);
     mbar_init(&o_full, 1);
+    mbar_init(&o_final, 1);
     mbar_init(&mma_done, 1);
     abort_s = 0;
     fence_barrier_init();
@@ -112,6 +129,10 @@ __global__ void __launch_bounds__(192, 1)
   const uint32_t tmem = tmem_base_s;
   volatile int* abort_v = &abort_s;
 
+  // Parity waits never alias: each waits for a phase whose successor needs
+  // work that the waiting role itself releases later, and whose predecessor
+  // has completed (MMAs of one thread complete in issue order, and s_full(j)
+  // fires only after PV_{j-2}); the final O has a barrier of its own.
   if (warp == 0) {
     // ---------------- producer ----------------
     if (lane == 0) {
@@ -135,7 +156,7 @@ __global__ void __launch_bounds__(192, 1)
         const int page = ptab[j];
         const int yk = (int)(((((size_t)layer * kv.n_pages + page) * 2 + 0) * Hkv + h) * kPageTokens);
         const int yv = yk + Hkv * kPageTokens;
-        uint8_t* dst = base_p + kPfQBytes + kPfPBytes + st * kPfKvBytes;
+        uint8_t* dst = base_p + kPfQBytes + 2 * kPfPBytes + st * kPfKvBytes;
         mbar_arrive_expect_tx(&kv_full[st], kPfKvBytes);
         tma_load_2d(dst, &kvmap, 0, yk, &kv_full[st]);
         tma_load_2d(dst + kPfBox, &kvmap, 64, yk, &kv_full[st]);
@@ -156,14 +177,17 @@ __global__ void __launch_bounds__(192, 1)
       constexpr uint32_t idesc_o = umma_idesc_f16(kBf, 128, 128) | (1u << 16);  // B (V) MN-major
       const uint32_t o_tmem = tmem + 128;
       auto pv = [&](int i) -> bool {
-        if (*abort_v || !mbar_wait_bounded(&p_full, i & 1, kPfWaitLimit)) return false;
+        const int pb = i & 1;
+        if (*abort_v || !mbar_wait_bounded(&p_full[pb], (i >> 1) & 1, kPfWaitLimit)) return false;
         tc_fence_after();
         const uint32_t v = kv_s + (i % kPfStages) * kPfKvBytes + 2 * kPfBox;
+        const uint32_t pa = p_s + pb * kPfPBytes;
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
-          umma_f16(o_tmem, umma_desc_sw128(p_s + kk * 32), umma_desc_sw128_mn(v + kk * 2048, kPfBox), idesc_o,
-                   kk != 0);
+          umma_f16(o_tmem, umma_desc_sw128(pa + kk * 32), umma_desc_sw128_mn(v + kk * 2048, kPfBox), idesc_o,
+                   (i | kk) != 0);
         umma_commit(&o_full);
+        umma_commit(&p_empty[pb]);
         umma_commit(&kv_empty[i % kPfStages]);
         return true;
       };
@@ -190,6 +214,7 @@ __global__ void __launch_bounds__(192, 1)
         }
       }
       if (ok) ok = pv(T_tiles - 1);
+      if (ok) umma_commit(&o_final);  // a phase of its own: the last o_full phase could alias
       if (!ok) *abort_v = 1;
       umma_commit(&mma_done);  // every MMA issued so far has completed when this fires
       mbar_wait_bounded(&mma_done, 0, kPfWaitLimit);
@@ -201,30 +226,9 @@ __global__ void __launch_bounds__(192, 1)
     const int hs = row >> 6, ri = row & 63;
     const int qpos = pos0 + ri;
     const uint32_t lane_addr = tmem + ((uint32_t)(q4 * 32) << 16);
-    float o[128];
-#pragma unroll
-    for (int i = 0; i < 128; ++i) o[i] = 0.f;
-    float m = -INFINITY, l = 0.f, m_o = -INFINITY;
+    const uint32_t o_addr = lane_addr + 128;
+    float m_ref = -INFINITY, l = 0.f;
     bool ok = true;
-    auto fold_o = [&](int i, float m_p) {
-      // O_reg = O_reg * exp2(m_o - m_p) + O_i, O_i computed with maximum m_p
-      if (!ok || *abort_v || !mbar_wait_bounded(&o_full, i & 1, kPfWaitLimit)) {
-        ok = false;
-        return;
-      }
-      tc_fence_after();
-      const float f = exp2f(m_o - m_p);
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        tmem_ld32(lane_addr + 128 + c * 32, v);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i2 = 0; i2 < 32; ++i2) o[c * 32 + i2] = fmaf(o[c * 32 + i2], f, __uint_as_float(v[i2]));
-      }
-      m_o = m_p;
-    };
-    float m_pend = -INFINITY;  // maximum that P of the pending tile was computed with
     for (int j = 0; j < T_tiles && ok; ++j) {
       const int sb = j & 1;
       if (*abort_v || !mbar_wait_bounded(&s_full[sb], (j >> 1) & 1, kPfWaitLimit)) {
@@ -250,20 +254,43 @@ __global__ void __launch_bounds__(192, 1)
         s[c] = key0 + c <= qpos ? s[c] * scale_log2 : -INFINITY;
         mx = fmaxf(mx, s[c]);
       }
-      const float mn = fmaxf(m, mx);  // finite from the first tile on: key 0 <= qpos
-      const float corr = exp2f(m - mn);
+      if (j == 0) {
+        m_ref = mx;  // finite: key 0 <= qpos
+      } else if (mx > m_ref + kPfRescale) {
+        // move the reference maximum: O (all PVs so far) and l scale by 2^(m_ref - mx)
+        if (*abort_v || !mbar_wait_bounded(&o_full, (j - 1) & 1, kPfWaitLimit)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const float f = exp2f(m_ref - mx);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t v[32];
+          tmem_ld32(o_addr + c * 32, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i2 = 0; i2 < 32; ++i2) v[i2] = __float_as_uint(__uint_as_float(v[i2]) * f);
+          tmem_st32(o_addr + c * 32, v);
+        }
+        tmem_st_wait();
+        l *= f;
+        m_ref = mx;
+      }
       float ps = 0.f;
 #pragma unroll
       for (int c = 0; c < 64; ++c) {
-        s[c] = exp2f(s[c] - mn);
+        s[c] = exp2f(s[c] - m_ref);
         ps += s[c];
       }
-      l = l * corr + ps;
-      m = mn;
-      if (j >= 1) fold_o(j - 1, m_pend);  // PV_{j-1} done: P and O buffers are free again
-      if (!ok) break;
+      l += ps;
+      // P buffer j&1 was last read by PV_{j-2}
+      if (j >= 2 && (*abort_v || !mbar_wait_bounded(&p_empty[sb], ((j - 2) >> 1) & 1, kPfWaitLimit))) {
+        ok = false;
+        break;
+      }
       // P_j -> the 128-byte-swizzled A tile: row `row`, 16-byte chunk c holds keys 8c .. 8c+7
-      uint8_t* prow = p_sp + row * 128;
+      uint8_t* prow = p_sp + sb * kPfPBytes + row * 128;
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
         uint4 u;
@@ -275,22 +302,30 @@ __global__ void __launch_bounds__(192, 1)
       }
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(&p_full);
-      m_pend = mn;
+      mbar_arrive(&p_full[sb]);
     }
-    if (ok) fold_o(T_tiles - 1, m_pend);
+    if (ok && (*abort_v || !mbar_wait_bounded(&o_final, 0, kPfWaitLimit))) ok = false;
     if (!ok) *abort_v = 1;
-    if (ok && ri < n) {
+    if (ok) {
+      tc_fence_after();
       const float inv = 1.f / l;
       T* dst = ctx + (size_t)(r0 + ri) * Hq * kHeadDim + (2 * h + hs) * kHeadDim;
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        uint4 u;
-        u.x = Act<T>::pack2(o[8 * c + 0] * inv, o[8 * c + 1] * inv);
-        u.y = Act<T>::pack2(o[8 * c + 2] * inv, o[8 * c + 3] * inv);
-        u.z = Act<T>::pack2(o[8 * c + 4] * inv, o[8 * c + 5] * inv);
-        u.w = Act<T>::pack2(o[8 * c + 6] * inv, o[8 * c + 7] * inv);
-        *reinterpret_cast<uint4*>(dst + 8 * c) = u;
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld32(o_addr + c * 32, v);
+        tmem_ld_wait();
+        if (ri < n) {
+#pragma unroll
+          for (int q8 = 0; q8 < 4; ++q8) {
+            uint4 u;
+            u.x = Act<T>::pack2(__uint_as_float(v[8 * q8 + 0]) * inv, __uint_as_float(v[8 * q8 + 1]) * inv);
+            u.y = Act<T>::pack2(__uint_as_float(v[8 * q8 + 2]) * inv, __uint_as_float(v[8 * q8 + 3]) * inv);
+            u.z = Act<T>::pack2(__uint_as_float(v[8 * q8 + 4]) * inv, __uint_as_float(v[8 * q8 + 5]) * inv);
+            u.w = Act<T>::pack2(__uint_as_float(v[8 * q8 + 6]) * inv, __uint_as_float(v[8 * q8 + 7]) * inv);
+            *reinterpret_cast<uint4*>(dst + c * 32 + 8 * q8) = u;
+          }
+        }
       }
     }
   }
@@ -303,7 +338,7 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
-size_t attn_prefill_smem_bytes() { return 1024 + kPfQBytes + kPfPBytes + kPfStages * kPfKvBytes; }
+size_t attn_prefill_smem_bytes() { return 1024 + kPfQBytes + 2 * kPfPBytes + kPfStages * kPfKvBytes; }
 
 }  // namespace
 

@@ -84,6 +84,7 @@ struct PlanLayout {
   }
 };
 
+constexpr int kMaxPrefillBlocks = 1024;  // prefill attention blocks one pass may carry
 constexpr int kRowsPerPBlock = 64;   // query rows per prefill attention block (x 2 heads = one 128-row MMA tile)
 constexpr int kDecodeItemTokens = 256;  // keys per decode attention split item
 

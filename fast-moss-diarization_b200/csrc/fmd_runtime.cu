@@ -888,6 +888,8 @@ int fmd_kv_reserve(fmd_handle* h, int32_t max_slots, int64_t max_tokens_total, i
   if (h->reserved) return fail(h, FMD_EBUSY, "KV pool already reserved");
   if (max_slots < 1 || max_slots > kMaxSlotsLimit || max_tokens_total < 1 || max_rows_per_step < max_slots)
     return fail(h, FMD_EINVAL, "bad KV reservation sizes (need 1 <= max_slots <= 256, rows >= slots)");
+  if (max_rows_per_step / kRowsPerPBlock + max_slots > kMaxPrefillBlocks)
+    return fail(h, FMD_ENOTSUP, "max_rows_per_step too large for the prefill attention");
   CK(cudaSetDevice(h->device));
   const fmd_config& c = h->cfg;
   const int H = c.hidden_size, I = c.intermediate_size, V = c.vocab_size;
