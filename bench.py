@@ -51,12 +51,6 @@ METRIC = "decoded tokens/s per GPU (Q8_0, bf16) and % of HBM roofline; audio s/s
 UNIT = "tokens/s"
 PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
 TRAFFIC_FILE = ROOT / "profiles" / "attn_decode_config3.md"
-# kernels per engine step: scheduler + embed + per layer + lm_head and greedy
-# pick. A step that may carry prefill rows runs 10 per layer (4 tensor-core
-# projections, their 4 epilogues counting the two residual norms, decode and
-# prefill attention); a decode-only step 5 (4 fused GEMVs + decode attention).
-KERNELS_MIXED = lambda layers: 1 + 1 + 10 * layers + 2  # noqa: E731
-KERNELS_DECODE = lambda layers: 1 + 1 + 5 * layers + 2  # noqa: E731
 
 
 def parse_args():
@@ -391,8 +385,11 @@ def main():
             "clocks": clk,
             "e2e": e2e,
             "cpu_baseline": cpu,
-            "gpu_launches": int(mixed_run * KERNELS_MIXED(cfg.num_hidden_layers)
-                                + (steps_run - mixed_run) * KERNELS_DECODE(cfg.num_hidden_layers)),
+            # kernel nodes of the two captured step graphs (counted by the library) x their replays
+            "gpu_launches": int(mixed_run * wins[-1].graph_kernels_mixed
+                                + (steps_run - mixed_run) * wins[-1].graph_kernels_decode),
+            "kernels_per_step": {"decode_only": wins[-1].graph_kernels_decode,
+                                 "with_prefill": wins[-1].graph_kernels_mixed},
             "mixed_steps_timed": int(mixed_run),
             "tokens_timed": int(tot_tokens),
         }

@@ -89,7 +89,8 @@ class Stats(C.Structure):
                 ("requests_done", C.c_int64), ("generate_seconds", C.c_double), ("device_status", C.c_int32),
                 ("reserved", C.c_int32), ("window_steps", C.c_int64), ("window_tokens", C.c_int64),
                 ("window_device_ms", C.c_double), ("attn_decode_ms", C.c_double), ("attn_kv_tokens", C.c_int64),
-                ("attn_rows", C.c_int64), ("window_mixed_steps", C.c_int64)]
+                ("attn_rows", C.c_int64), ("window_mixed_steps", C.c_int64), ("graph_kernels_mixed", C.c_int64),
+                ("graph_kernels_decode", C.c_int64)]
 
 
 _lib = None

@@ -160,6 +160,7 @@ struct fmd_handle {
   cudaGraphExec_t graph_exec = nullptr;  // engine step that may carry a prefill chunk ("M")
   cudaGraphExec_t graph_dec = nullptr;   // decode-only engine step ("D")
   int graph_batch = -1, graph_chunk = -1;
+  int64_t graph_kernels_mixed = 0, graph_kernels_decode = 0;
   bool first_block = true;               // no counters polled since fmd_engine_start
   int64_t launched_mixed = 0;
   bool engine_started = false;
@@ -1363,6 +1364,20 @@ int fmd_engine_start(fmd_handle* h, int32_t max_batch, int32_t prefill_chunk) {
         run_forward(h, nullptr, h->eng_arena.p, true);
       h->record_attn_events = false;
       CK(cudaStreamEndCapture(h->stream, &g));
+      {
+        // kernels per replay of this graph (reported in fmd_stats)
+        size_t n_nodes = 0;
+        CK(cudaGraphGetNodes(g, nullptr, &n_nodes));
+        std::vector<cudaGraphNode_t> nodes(n_nodes);
+        CK(cudaGraphGetNodes(g, nodes.data(), &n_nodes));
+        int64_t kernels = 0;
+        for (cudaGraphNode_t nd : nodes) {
+          cudaGraphNodeType ty;
+          CK(cudaGraphNodeGetType(nd, &ty));
+          kernels += ty == cudaGraphNodeTypeKernel;
+        }
+        (mixed ? h->graph_kernels_mixed : h->graph_kernels_decode) = kernels;
+      }
       if (h->launch_refused) {
         cudaGraphDestroy(g);
         return sync_check(h);
@@ -1457,6 +1472,8 @@ int fmd_engine_step(fmd_handle* h, int64_t max_steps, fmd_stats* stats) {
     stats->attn_kv_tokens = kv_last;
     stats->attn_rows = rows_last;
     stats->window_mixed_steps = mixed_launched;
+    stats->graph_kernels_mixed = h->graph_kernels_mixed;
+    stats->graph_kernels_decode = h->graph_kernels_decode;
   }
   return FMD_OK;
 }

@@ -45,6 +45,8 @@ class BatchStats:
     attn_kv_tokens: int = 0
     attn_rows: int = 0
     window_mixed_steps: int = 0
+    graph_kernels_mixed: int = 0
+    graph_kernels_decode: int = 0
 
     @classmethod
     def from_c(cls, st) -> "BatchStats":
@@ -53,7 +55,8 @@ class BatchStats:
                    steps=int(st.steps), device_status=int(st.device_status), window_steps=int(st.window_steps),
                    window_tokens=int(st.window_tokens), window_device_ms=float(st.window_device_ms),
                    attn_decode_ms=float(st.attn_decode_ms), attn_kv_tokens=int(st.attn_kv_tokens),
-                   attn_rows=int(st.attn_rows), window_mixed_steps=int(st.window_mixed_steps))
+                   attn_rows=int(st.attn_rows), window_mixed_steps=int(st.window_mixed_steps),
+                   graph_kernels_mixed=int(st.graph_kernels_mixed), graph_kernels_decode=int(st.graph_kernels_decode))
 
     @property
     def decode_tokens_per_second(self) -> float:

@@ -140,6 +140,8 @@ typedef struct fmd_stats {
   int64_t attn_kv_tokens;   /* sum of key positions read by one launch           */
   int64_t attn_rows;        /* decode rows in that step                          */
   int64_t window_mixed_steps; /* steps of the window that could carry prefill rows */
+  int64_t graph_kernels_mixed;  /* kernels in one replay of the step graph that may carry prefill rows */
+  int64_t graph_kernels_decode; /* kernels in one replay of the decode-only step graph */
 } fmd_stats;
 
 /* ---- handle ------------------------------------------------------------- */

@@ -258,3 +258,34 @@ def test_long_chunked_prefill_full_shapes():
             lg, _ = dec.decode_step([s], [tok])
             want = m.decode_step(tok, caches).numpy()
             assert rel_err(lg[0], want) < LOGIT_RTOL, s
+
+
+@pytest.mark.parametrize("prec", ["int8_bf16", "int8"])
+def test_decode_batch_of_32_full_shapes(prec):
+    """A decode step of 32 sequences at the BASELINE shapes (two layers), the
+    batch size of config 3: four 8-row n-tiles in every decode GEMV. Every
+    row's logits and greedy id against the oracle's solo run of that
+    sequence."""
+    cfg = mid_config()
+    w = syn.make_weights(cfg, seed=27)
+    m = oracle_model(cfg, w, prec)
+    rng = np.random.default_rng(13)
+    n = 32
+    lens = rng.integers(1, 40, n)
+    prompts = [rng.standard_normal((int(k), cfg.hidden_size), dtype=np.float32) for k in lens]
+    with make_decoder(cfg, w, prec, slots=n, tokens=n * 128, rows=2048) as dec:
+        for s in range(n):
+            dec.open_slot(s, int(lens[s]) + 4)
+        dec.prefill(list(range(n)), prompts)
+        caches = []
+        for s in range(n):
+            cs = m.new_caches(1, int(lens[s]) + 4)
+            m.prefill(prompts[s][None], cs)
+            caches.append(cs)
+        for _ in range(2):
+            toks = rng.integers(0, cfg.vocab_size, n)
+            lg, ids = dec.decode_step(list(range(n)), toks)
+            for s in range(n):
+                want = m.decode_step(int(toks[s]), caches[s]).numpy()
+                assert rel_err(lg[s], want) < LOGIT_RTOL, s
+                check_pick(int(ids[s]), lg[s], want)
