@@ -323,8 +323,8 @@ def main():
     max_ms = dist.reduce(dev_ms, "max")
     value = tot_tokens / (max_ms / 1000.0) if max_ms > 0 else 0.0
 
-    # dominant kernel: decode attention (CUDA events around each launch of
-    # the last step of every timed window)
+    # dominant kernel: decode attention (CUDA events around the middle layer's
+    # launch in the last step of every timed window)
     peak, peak_kind = load_peaks()
     samples = [(s.attn_kv_tokens, s.attn_decode_ms, s.attn_rows) for s in wins if s.attn_decode_ms > 0]
     kv_per_launch = statistics.mean(x[0] for x in samples) if samples else 0.0

@@ -132,7 +132,7 @@ FMD_DEV void gemv_afrag(const WRegs& w, uint32_t (&af)[4][4]) {
 template <typename T, bool Q8, int FW, int EPI, bool NORM, int KG>
 __global__ void __launch_bounds__(FW * KG * 32) k_gemv(const T* __restrict__ x, int ldx, const int* __restrict__ row_map,
                                                  const int* __restrict__ n_rows_ptr, LinW W, GemvEpi ep, int xrows,
-                                                 int* __restrict__ status) {
+                                                 int max_rows, int* __restrict__ status) {
   constexpr int NW = FW * KG;  // warps: FW feature slices x KG k-block groups
   constexpr int NT = NW * 32;
   constexpr int FT = FW * 16;
@@ -179,6 +179,19 @@ __global__ void __launch_bounds__(FW * KG * 32) k_gemv(const T* __restrict__ x, 
 
   const int n_rows = *n_rows_ptr;
   const int row0 = blockIdx.z * kRows;
+  const int cpr = klen >> 3;  // 16-byte chunks per activation row
+  // Without a row map every row this tile can hold exists in x (the pass has
+  // at most `max_rows` rows), so its copies are issued before the row count
+  // arrives; rows past the count are never stored.
+  const bool eager = row_map == nullptr;
+  if (eager) {
+    const int avail = min(min(kRows, xrows), max_rows - row0);
+    for (int c = threadIdx.x; c < avail * cpr; c += NT) {
+      const int r = c / cpr, ch = c - r * cpr;
+      cp_async16(xs + (size_t)r * xstride + ch * 8, x + (size_t)(row0 + r) * ldx + kbeg + ch * 8, 16);
+    }
+    cp_async_commit();
+  }
   const int rows = max(0, min(min(kRows, xrows), n_rows - row0));
   const int n_tiles = (rows + 7) >> 3;
 
@@ -210,9 +223,9 @@ __global__ void __launch_bounds__(FW * KG * 32) k_gemv(const T* __restrict__ x, 
     }
   }
 
-  if (rows > 0) {
-    // activation tile rows x klen (rows of a partial n-tile zero-filled)
-    const int cpr = klen >> 3;  // 16-byte chunks per row
+  if (rows > 0 && !eager) {
+    // activation tile rows x klen through the row map (rows of a partial
+    // n-tile zero-filled)
     for (int c = threadIdx.x; c < n_tiles * 8 * cpr; c += NT) {
       const int r = c / cpr, ch = c - r * cpr;
       const T* src = x;
@@ -224,6 +237,8 @@ __global__ void __launch_bounds__(FW * KG * 32) k_gemv(const T* __restrict__ x, 
       cp_async16(xs + (size_t)r * xstride + ch * 8, src, bytes);
     }
     cp_async_commit();
+  }
+  if (rows > 0) {
     // rsqrt(mean(x^2) + eps) of each row, read while the activation tile is in flight
     if constexpr (NORM) rows_rsqrt(ep.ssq, ep.ssq_tiles, row_map, row0, rows, K, ep.eps, rs_s, NT);
     cp_async_wait<0>();
@@ -275,6 +290,7 @@ __global__ void __launch_bounds__(FW * KG * 32) k_gemv(const T* __restrict__ x, 
   if (rows == 0) {
     // a whole cluster shares blockIdx.z, so it leaves together, but only
     // after its copies into shared memory have landed
+    cp_async_wait<0>();
     bool ok = true;
     for (int kb = 0; kb < nkb; ++kb) ok &= mbar_wait_bounded(&wbar[kb], 0, kWaitLimit);
     if (!ok) atomicExch(status, kStatusTimeout);
@@ -840,7 +856,8 @@ void launch_gemv_t(const LinW& W, int S, const void* x, int ldx, const int* row_
   cfg.stream = s;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  cudaLaunchKernelEx(&cfg, k_gemv<T, Q8, FW, EPI, NORM, KG>, (const T*)x, ldx, row_map, n_rows_ptr, W, ep, xrows, status);
+  cudaLaunchKernelEx(&cfg, k_gemv<T, Q8, FW, EPI, NORM, KG>, (const T*)x, ldx, row_map, n_rows_ptr, W, ep, xrows,
+                     max_rows, status);
 }
 
 

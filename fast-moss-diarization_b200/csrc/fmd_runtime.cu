@@ -165,7 +165,10 @@ struct fmd_handle {
   int64_t launched_mixed = 0;
   bool engine_started = false;
   bool record_attn_events = false;             // set while capturing the step graph
-  std::vector<cudaEvent_t> attn_events;        // [2 * layers] around each decode-attention launch
+  // around the decode attention of one layer only: an event node between two
+  // kernels of the graph removes their programmatic-dependent-launch overlap
+  std::vector<cudaEvent_t> attn_events;        // [2]
+  int attn_probe_layer() const { return cfg.num_hidden_layers / 2; }
   cudaEvent_t win_begin = nullptr, win_end = nullptr;
 
   int elem() const { return 2; }
@@ -476,10 +479,11 @@ void run_forward_decode(fmd_handle* h, float* logits_dev, const void* arena) {
     qkv.layer = l;
     if (!launch_gemv(h->at, kGemvQkv, true, L.qkv, h->x, H, nullptr, nrows, R, qkv, h->d_status, s)) h->launch_refused = true;
     trace(h, "qkv", l);
-    if (h->record_attn_events) cudaEventRecordWithFlags(h->attn_events[2 * l], s, cudaEventRecordExternal);
+    const bool probe = h->record_attn_events && l == h->attn_probe_layer();
+    if (probe) cudaEventRecordWithFlags(h->attn_events[0], s, cudaEventRecordExternal);
     launch_attn_decode_tma(h->at, &h->kv_tmap, h->plan, h->di_grid, h->Hq(), h->Hkv(), h->qbuf, h->kv, l,
                            h->attn_scale, h->pacc, h->pml, h->attn_counters, h->ctx, h->d_status, s);
-    if (h->record_attn_events) cudaEventRecordWithFlags(h->attn_events[2 * l + 1], s, cudaEventRecordExternal);
+    if (probe) cudaEventRecordWithFlags(h->attn_events[1], s, cudaEventRecordExternal);
     trace(h, "attn_decode", l);
     if (!launch_gemv(h->at, kGemvResid, false, L.o, h->ctx, h->Hq() * kHeadDim, nullptr, nrows, R, res, h->d_status, s)) h->launch_refused = true;
     trace(h, "o_proj", l);
@@ -540,10 +544,11 @@ void run_forward(fmd_handle* h, float* logits_dev, const void* arena, bool decod
     launch_qkv_epilogue(h->at, h->plan, row_grid, h->part, sp_qkv, ss, h->Hq(), h->Hkv(), L.q_norm, L.k_norm,
                         h->rope_cos, h->rope_sin, h->qbuf, h->kv, l, eps, s);
     trace(h, "qkv_epi", l);
-    if (h->record_attn_events) cudaEventRecordWithFlags(h->attn_events[2 * l], s, cudaEventRecordExternal);
+    const bool probe = h->record_attn_events && l == h->attn_probe_layer();
+    if (probe) cudaEventRecordWithFlags(h->attn_events[0], s, cudaEventRecordExternal);
     launch_attn_decode_tma(h->at, &h->kv_tmap, h->plan, h->di_grid, h->Hq(), h->Hkv(), h->qbuf, h->kv, l,
                            h->attn_scale, h->pacc, h->pml, h->attn_counters, h->ctx, h->d_status, s);
-    if (h->record_attn_events) cudaEventRecordWithFlags(h->attn_events[2 * l + 1], s, cudaEventRecordExternal);
+    if (probe) cudaEventRecordWithFlags(h->attn_events[1], s, cudaEventRecordExternal);
     trace(h, "attn_decode", l);
     if (!decode_only) {
       launch_attn_prefill_tc(h->at, &h->kv_tmap, &h->qmap, h->plan, h->pb_max, h->Hq(), h->Hkv(), h->kv, l,
@@ -1343,7 +1348,7 @@ int fmd_engine_start(fmd_handle* h, int32_t max_batch, int32_t prefill_chunk) {
   CK(cudaMemsetAsync(h->eng_results.p, 0, sizeof(DevResult) * h->eng_n_reqs, h->stream));
   CK(cudaStreamSynchronize(h->stream));
   if (h->attn_events.empty()) {
-    h->attn_events.resize(2 * h->cfg.num_hidden_layers);
+    h->attn_events.resize(2);
     for (auto& e : h->attn_events) CK(cudaEventCreate(&e));
     CK(cudaEventCreate(&h->win_begin));
     CK(cudaEventCreate(&h->win_end));
@@ -1449,12 +1454,9 @@ int fmd_engine_step(fmd_handle* h, int64_t max_steps, fmd_stats* stats) {
   if (launched > 0) CK(cudaEventElapsedTime(&win_ms, h->win_begin, h->win_end));
   double attn_ms = 0.0;
   if (launched > 0) {
-    for (int l = 0; l < h->cfg.num_hidden_layers; ++l) {
-      float ms = 0.f;
-      CK(cudaEventElapsedTime(&ms, h->attn_events[2 * l], h->attn_events[2 * l + 1]));
-      attn_ms += ms;
-    }
-    attn_ms /= h->cfg.num_hidden_layers;
+    float ms = 0.f;
+    CK(cudaEventElapsedTime(&ms, h->attn_events[0], h->attn_events[1]));
+    attn_ms = ms;
   }
   const auto t1 = std::chrono::steady_clock::now();
   if (stats) {

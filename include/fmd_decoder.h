@@ -136,7 +136,7 @@ typedef struct fmd_stats {
   double window_device_ms;  /* CUDA-event time on the engine stream              */
   /* decode attention of the window's last step (CUDA events around each of
    * its per-layer launches inside the step graph) */
-  double attn_decode_ms;    /* mean duration of one launch                       */
+  double attn_decode_ms;    /* duration of the middle layer's launch in the last step */
   int64_t attn_kv_tokens;   /* sum of key positions read by one launch           */
   int64_t attn_rows;        /* decode rows in that step                          */
   int64_t window_mixed_steps; /* steps of the window that could carry prefill rows */
