@@ -508,37 +508,53 @@ __global__ void __launch_bounds__(FW * KG * 32) k_gemv(const T* __restrict__ x, 
 // lm_head + greedy candidates as one persistent kernel (qwen3.rs:459-463,
 // engine.rs:550-559). The final RMSNorm is applied to the staged rows from
 // the per-tile sums of squares (ep.ssq), or skipped when ep.ssq is null and
-// the rows are already normalised. The vocabulary projection is the largest weight of a
-// decode step (vocab x hidden) and the only one with more 128-feature tiles
-// than there are SMs, so here one CTA per SM keeps the normalised activation
-// tile resident and streams its share of tiles through a ring of TMA bulk
-// copies (one stage = one 64-wide k-block of a tile, 8.5 KB for Q8_0):
-//  * warp 8 (one lane) is the producer; warps 0-7 consume, each owning 16
-//    features of the 128-feature tile, and release a stage by arriving on its
-//    "empty" barrier. Every wait is bounded; a timeout stops the ring, sets
-//    the status word and drains the copies still in flight.
+// the rows are already normalised. The vocabulary projection is the largest
+// weight of a decode step (vocab x hidden) and the only one with more
+// 128-feature tiles than there are SMs, so here one CTA per SM keeps the
+// normalised activation tile resident and streams its share of tiles through
+// a ring of TMA bulk copies (one stage = one 64-wide k-block of a tile, 8.5 KB
+// for Q8_0):
+//  * the last warp (one lane) is the producer; the others consume in G groups
+//    of eight, each warp owning 16 features of a 128-feature tile. Group g
+//    takes the CTA's tiles g, g + G, ...; the producer interleaves the
+//    k-blocks of G tiles, so the groups stream at once. The register-level
+//    Q8_0 dequantisation makes this instruction-bound, hence two groups
+//    where the registers allow (batches up to 32 rows). A warp releases a
+//    stage by arriving on its "empty" barrier. Every
+//    wait is bounded; a timeout stops the ring, sets the status word and
+//    drains the copies still in flight.
 //  * the tile order of the packed lm_head ([tile][k-split][k-block][warp]) is
-//    the full-K k-block order of each tile, so the ring walks it linearly.
+//    the full-K k-block order of each tile.
 //  * each CTA keeps, per row, the best (rounded logit, lowest index) over its
 //    tiles and writes one candidate per (row, CTA); k_pick_reduce finishes.
-constexpr int kHeadWarps = 8;            // consumer warps: 128 features per tile
+constexpr int kHeadWarps = 8;            // warps per group: 128 features per tile
 constexpr int kHeadMaxStages = 16;
 constexpr int kHeadSmemBudget = 220 * 1024;
 
-template <typename T, bool Q8>
-__global__ void __launch_bounds__((kHeadWarps + 1) * 32) k_lm_head(const T* __restrict__ x, int ldx,
-                                                                  const int* __restrict__ row_map,
-                                                                  const int* __restrict__ n_rows_ptr, LinW W,
-                                                                  GemvEpi ep, int xrows, int stages,
-                                                                  int* __restrict__ status) {
+// ring position of (CTA-local tile i, k-block kb) with G consumer groups: the
+// k-blocks of the G tiles of a group of tiles alternate
+template <int G>
+FMD_DEV int head_unit(int i, int kb, int nkb, int my_tiles) {
+  const int p = i / G, in_grp = min(G, my_tiles - G * p);
+  return G * p * nkb + kb * in_grp + (i - G * p);
+}
+
+// NTL: MMA n-tiles (8 rows each) of a row tile; G: consumer groups. Two
+// groups (17 warps) leave 96 registers per thread, enough for 4 n-tiles.
+template <typename T, bool Q8, int NTL, int G>
+__global__ void __launch_bounds__((G * kHeadWarps + 1) * 32, 1)
+    k_lm_head(const T* __restrict__ x, int ldx, const int* __restrict__ row_map, const int* __restrict__ n_rows_ptr,
+              LinW W, GemvEpi ep, int xrows, int stages, int* __restrict__ status) {
   constexpr int UNIT = Q8 ? kUnitQ8 : kUnitDense;
   constexpr uint32_t kStage = kHeadWarps * UNIT;
   constexpr int FT = kHeadWarps * 16;
+  constexpr int NCW = G * kHeadWarps;  // consumer warps
+  constexpr int NT = NCW * 32;
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t full[kHeadMaxStages], empty[kHeadMaxStages];
   __shared__ float rs_s[kRows];
-  __shared__ float cand_v[kHeadWarps][kRows];
-  __shared__ int cand_i[kHeadWarps][kRows];
+  __shared__ float cand_v[NCW][NTL * 8];
+  __shared__ int cand_i[NCW][NTL * 8];
   __shared__ int abort_s;
   griddep_launch();
 
@@ -550,52 +566,51 @@ __global__ void __launch_bounds__((kHeadWarps + 1) * 32) k_lm_head(const T* __re
   T* xs = reinterpret_cast<T*>(smem + (size_t)stages * kStage);  // [xrows][K + 8]
   const int xstride = K + 8;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int grp = warp / kHeadWarps, fw = warp % kHeadWarps;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < stages; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], kHeadWarps);
+      mbar_init(&empty[i], kHeadWarps);  // one group consumes each stage
     }
     abort_s = 0;
     fence_barrier_init();
   }
   __syncthreads();
 
-  if (warp == kHeadWarps) {
+  if (warp == NCW) {
     // ---- producer: weights do not depend on the previous kernel, so the
     // ring starts filling before griddepcontrol.wait
     if (lane == 0) {
-      // stage / phase / tile / k-block advance incrementally (no divisions)
-      int st = 0, ph = 0, tile = blockIdx.x, kb = 0;
-      for (int u = 0; u < n_units; ++u) {
-        if (u >= stages && !mbar_wait_bounded(&empty[st], ph ^ 1, kWaitLimit)) {
-          atomicExch(&abort_s, 1);
-          break;
-        }
-        if (*reinterpret_cast<volatile int*>(&abort_s)) break;
-        mbar_arrive_expect_tx(&full[st], kStage);
-        bulk_load(ring + (size_t)st * kStage, W.pk + ((size_t)tile * nkb + kb) * kStage, kStage, &full[st]);
-        if (++kb == nkb) {
-          kb = 0;
-          tile += gridDim.x;
-        }
-        if (++st == stages) {
-          st = 0;
-          ph ^= 1;
+      int u = 0;
+      for (int p = 0; G * p < my_tiles; ++p) {
+        const int in_grp = min(G, my_tiles - G * p);
+        for (int kb = 0; kb < nkb; ++kb) {
+          for (int j = 0; j < in_grp; ++j, ++u) {
+            const int st = u % stages, ph = (u / stages) & 1;
+            if (u >= stages && !mbar_wait_bounded(&empty[st], ph ^ 1, kWaitLimit)) {
+              atomicExch(&abort_s, 1);
+              goto produced;
+            }
+            if (*reinterpret_cast<volatile int*>(&abort_s)) goto produced;
+            const int tile = blockIdx.x + (G * p + j) * gridDim.x;
+            mbar_arrive_expect_tx(&full[st], kStage);
+            bulk_load(ring + (size_t)st * kStage, W.pk + ((size_t)tile * nkb + kb) * kStage, kStage, &full[st]);
+          }
         }
       }
+    produced:;
     }
     griddep_wait();
     return;  // nothing below touches the producer warp
   }
 
-  // ---- consumers (256 threads): normalised activation tile, then the ring
+  // ---- consumers (512 threads): normalised activation tile, then the ring
   griddep_wait();
   const int n_rows = *n_rows_ptr;
-  const int row0 = blockIdx.y * kRows;
-  const int rows = max(0, min(min(kRows, xrows), n_rows - row0));
+  const int row0 = blockIdx.y * NTL * 8;
+  const int rows = max(0, min(min(NTL * 8, xrows), n_rows - row0));
   const int n_nt = (rows + 7) >> 3;
-  constexpr int NT = kHeadWarps * 32;
   const int cpr = K >> 3;
   for (int c = threadIdx.x; c < n_nt * 8 * cpr; c += NT) {
     const int r = c / cpr, ch = c - r * cpr;
@@ -634,45 +649,44 @@ __global__ void __launch_bounds__((kHeadWarps + 1) * 32) k_lm_head(const T* __re
   named_sync(1, NT);
 
   // running best of this thread's rows (nt * 8 + 2t + {0, 1}) over its features
-  float bv[8][2];
-  int bi[8][2];
+  float bv[NTL][2];
+  int bi[NTL][2];
 #pragma unroll
-  for (int nt = 0; nt < 8; ++nt) {
+  for (int nt = 0; nt < NTL; ++nt) {
     bv[nt][0] = bv[nt][1] = -INFINITY;
     bi[nt][0] = bi[nt][1] = 0x7fffffff;
   }
   bool ok = true;
-  int st = 0, ph = 0;  // ring position of the next unit
   if (rows == 0) {
     // the producer started before the row count was known: release every
-    // stage so that no copy is left in flight when the CTA retires
-    for (int u = 0; u < n_units; ++u) {
-      if (*reinterpret_cast<volatile int*>(&abort_s) || !mbar_wait_bounded(&full[st], ph, kWaitLimit)) {
-        atomicExch(&abort_s, 1);
-        ok = false;
-        break;
+    // stage of this group's tiles so that no copy is left in flight when the
+    // CTA retires
+    for (int i = grp; i < my_tiles && ok; i += G)
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int u = head_unit<G>(i, kb, nkb, my_tiles), st = u % stages;
+        if (*reinterpret_cast<volatile int*>(&abort_s) || !mbar_wait_bounded(&full[st], (u / stages) & 1, kWaitLimit)) {
+          atomicExch(&abort_s, 1);
+          ok = false;
+          break;
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[st]);
-      if (++st == stages) {
-        st = 0;
-        ph ^= 1;
-      }
-    }
   }
-  for (int i = 0; i < my_tiles && ok && rows > 0; ++i) {
+  for (int i = grp; i < my_tiles && ok && rows > 0; i += G) {
     const int tile = blockIdx.x + i * gridDim.x;
-    float acc[8][4];
+    float acc[NTL][4];
 #pragma unroll
-    for (int nt = 0; nt < 8; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+    for (int nt = 0; nt < NTL; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
 #pragma unroll 1
     for (int kb = 0; kb < nkb; ++kb) {
-      if (*reinterpret_cast<volatile int*>(&abort_s) || !mbar_wait_bounded(&full[st], ph, kWaitLimit)) {
+      const int u = head_unit<G>(i, kb, nkb, my_tiles), st = u % stages;
+      if (*reinterpret_cast<volatile int*>(&abort_s) || !mbar_wait_bounded(&full[st], (u / stages) & 1, kWaitLimit)) {
         atomicExch(&abort_s, 1);
         ok = false;
         break;
       }
-      const uint8_t* un = ring + (size_t)st * kStage + warp * UNIT;
+      const uint8_t* un = ring + (size_t)st * kStage + fw * UNIT;
       WRegs w;
       w.a = *reinterpret_cast<const int4*>(un + lane * 16);
       w.b = *reinterpret_cast<const int4*>(un + 512 + lane * 16);
@@ -686,14 +700,10 @@ __global__ void __launch_bounds__((kHeadWarps + 1) * 32) k_lm_head(const T* __re
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[st]);  // this warp's fragments are in registers
-      if (++st == stages) {
-        st = 0;
-        ph ^= 1;
-      }
       uint32_t af[4][4];
       gemv_afrag<T, Q8>(w, af);
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
+      for (int nt = 0; nt < NTL; ++nt) {
         if (nt < n_nt) {
           const T* xr = xs + (size_t)(nt * 8 + g) * xstride + kb * 64 + 16 * t;
           const int4 x0 = *reinterpret_cast<const int4*>(xr);
@@ -708,9 +718,9 @@ __global__ void __launch_bounds__((kHeadWarps + 1) * 32) k_lm_head(const T* __re
     if (!ok) break;
     // rounded logits (the reference rounds lm_head output to the activation
     // type) and the running best; features fl and fl + 8 of this tile
-    const int f0 = tile * FT + warp * 16 + g;
+    const int f0 = tile * FT + fw * 16 + g;
 #pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
+    for (int nt = 0; nt < NTL; ++nt) {
       if (nt < n_nt) {
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
@@ -737,7 +747,7 @@ __global__ void __launch_bounds__((kHeadWarps + 1) * 32) k_lm_head(const T* __re
 
   // ---- per-row best over this CTA's tiles: lanes of equal t, then warps
 #pragma unroll
-  for (int nt = 0; nt < 8; ++nt) {
+  for (int nt = 0; nt < NTL; ++nt) {
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       float v = bv[nt][h];
@@ -761,7 +771,7 @@ __global__ void __launch_bounds__((kHeadWarps + 1) * 32) k_lm_head(const T* __re
   for (int r = threadIdx.x; r < rows; r += NT) {
     float v = cand_v[0][r];
     int ix = cand_i[0][r];
-    for (int w = 1; w < kHeadWarps; ++w)
+    for (int w = 1; w < NCW; ++w)
       if (cand_v[w][r] > v || (cand_v[w][r] == v && cand_i[w][r] < ix)) {
         v = cand_v[w][r];
         ix = cand_i[w][r];
@@ -861,7 +871,7 @@ void launch_gemv_t(const LinW& W, int S, const void* x, int ldx, const int* row_
 }
 
 
-template <typename T, bool Q8>
+template <typename T, bool Q8, int NTL, int G>
 int launch_lm_head_t(const LinW& W, const void* x, int ldx, const int* row_map, const int* n_rows_ptr,
                      int max_rows, const GemvEpi& ep, int* status, cudaStream_t s) {
   static int n_sm = 0;
@@ -871,7 +881,8 @@ int launch_lm_head_t(const LinW& W, const void* x, int ldx, const int* row_map, 
     cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
     if (n_sm <= 0) n_sm = 148;
   }
-  const int xrows = ((max_rows < kRows ? max_rows : kRows) + 7) & ~7;
+  constexpr int kTileRows = NTL * 8;
+  const int xrows = ((max_rows < kTileRows ? max_rows : kTileRows) + 7) & ~7;
   const size_t xbytes = (size_t)xrows * (W.K + 8) * sizeof(T);
   const size_t stage = (size_t)kHeadWarps * (Q8 ? kUnitQ8 : kUnitDense);
   if (xbytes + 2 * stage > (size_t)kHeadSmemBudget) return 0;
@@ -883,13 +894,14 @@ int launch_lm_head_t(const LinW& W, const void* x, int ldx, const int* row_map, 
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid, (max_rows + kRows - 1) / kRows, 1);
-  cfg.blockDim = dim3((kHeadWarps + 1) * 32);
+  cfg.gridDim = dim3(grid, (max_rows + kTileRows - 1) / kTileRows, 1);
+  cfg.blockDim = dim3((G * kHeadWarps + 1) * 32);
   cfg.dynamicSmemBytes = (size_t)stages * stage + xbytes;
   cfg.stream = s;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaLaunchKernelEx(&cfg, k_lm_head<T, Q8>, (const T*)x, ldx, row_map, n_rows_ptr, W, ep, xrows, stages, status);
+  cudaLaunchKernelEx(&cfg, k_lm_head<T, Q8, NTL, G>, (const T*)x, ldx, row_map, n_rows_ptr, W, ep, xrows, stages,
+                     status);
   return grid;
 }
 
@@ -903,7 +915,8 @@ cudaError_t init_gemv_t() {
            cudaFuncSetAttribute(k_gemv<T, Q8, 4, kGemvResid, false, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim),
            cudaFuncSetAttribute(k_gemv<T, Q8, 4, kGemvSwiglu, true, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim),
            cudaFuncSetAttribute(k_gemv<T, Q8, 8, kGemvLogits, true, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim),
-           cudaFuncSetAttribute(k_lm_head<T, Q8>, cudaFuncAttributeMaxDynamicSharedMemorySize, kHeadSmemBudget)})
+           cudaFuncSetAttribute(k_lm_head<T, Q8, 4, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kHeadSmemBudget),
+           cudaFuncSetAttribute(k_lm_head<T, Q8, 8, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kHeadSmemBudget)})
     if (r != cudaSuccess) e = r;
   return e;
 }
@@ -994,12 +1007,15 @@ int launch_lm_head(ActType at, const LinW& W, const void* x, int ldx, const int*
                    int max_rows, const GemvEpi& ep, int* status, cudaStream_t s) {
   if (W.pk == nullptr || W.N % (kHeadWarps * 16) != 0 || W.K % 64 != 0) return 0;
   int parts;
+  // row tiles of 32 rows (4 MMA n-tiles) up to a batch of 32, else 64
+#define FMD_HEAD(T, Q8)                                                                                        \
+  (max_rows <= 32 ? launch_lm_head_t<T, Q8, 4, 2>(W, x, ldx, row_map, n_rows_ptr, max_rows, ep, status, s)    \
+                  : launch_lm_head_t<T, Q8, 8, 1>(W, x, ldx, row_map, n_rows_ptr, max_rows, ep, status, s))
   if (at == kBF16)
-    parts = W.q8 ? launch_lm_head_t<__nv_bfloat16, true>(W, x, ldx, row_map, n_rows_ptr, max_rows, ep, status, s)
-                 : launch_lm_head_t<__nv_bfloat16, false>(W, x, ldx, row_map, n_rows_ptr, max_rows, ep, status, s);
+    parts = W.q8 ? FMD_HEAD(__nv_bfloat16, true) : FMD_HEAD(__nv_bfloat16, false);
   else
-    parts = W.q8 ? launch_lm_head_t<__half, true>(W, x, ldx, row_map, n_rows_ptr, max_rows, ep, status, s)
-                 : launch_lm_head_t<__half, false>(W, x, ldx, row_map, n_rows_ptr, max_rows, ep, status, s);
+    parts = W.q8 ? FMD_HEAD(__half, true) : FMD_HEAD(__half, false);
+#undef FMD_HEAD
   if (parts > 0) return parts;
   // activation tile too large for the resident kernel: the cluster GEMV,
   // which normalises on the fly and so needs the sums of squares
