@@ -28,20 +28,51 @@ __global__ void __launch_bounds__(256) k_schedule(EngineDev e) {
   __shared__ long long s_seg_emb0[kMaxSlots];
   __shared__ int s_seg_sample[kMaxSlots];
   __shared__ int s_n_rows, s_n_decode, s_n_sample, s_n_pblocks, s_n_items, s_finished;
+  // shared copies of the slot state: every global array is read once, in
+  // parallel, so the serial bookkeeping below runs on shared memory
+  __shared__ int st_state[kMaxSlots], st_req[kMaxSlots], st_len[kMaxSlots], st_pdone[kMaxSlots],
+      st_ngen[kMaxSlots], st_last[kMaxSlots], st_npages[kMaxSlots];
+  __shared__ DevRequest st_rq[kMaxSlots];  // request of each occupied slot
+  __shared__ int smp_slot[kMaxSlots], smp_tok[kMaxSlots];
+  __shared__ EngineCounters s_ctr;
+  __shared__ int s_prev;
   PlanCounts* cnt = e.plan.counts;
+  const int nb = e.max_batch;
 
   if (threadIdx.x == 0) {
-    EngineCounters* c = e.ctr;
+    s_ctr = *e.ctr;
+    s_prev = cnt->n_sample;
+  }
+  for (int s = threadIdx.x; s < nb; s += blockDim.x) {
+    st_state[s] = e.slot_state[s];
+    st_req[s] = e.slot_req[s];
+    st_len[s] = e.slot_len[s];
+    st_pdone[s] = e.slot_pdone[s];
+    st_ngen[s] = e.slot_ngen[s];
+    st_last[s] = e.slot_last[s];
+    st_npages[s] = e.slot_npages[s];
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < s_prev; i += blockDim.x) {
+    smp_slot[i] = e.plan.sample_slot[i];
+    smp_tok[i] = e.next_ids[i];
+  }
+  for (int s = threadIdx.x; s < nb; s += blockDim.x)
+    if (st_state[s] != kSlotFree) st_rq[s] = e.reqs[st_req[s]];
+  __syncthreads();
+
+  if (threadIdx.x == 0) {
+    EngineCounters* c = &s_ctr;
     // ---- 1. consume the previous step's samples ----
-    const int prev = cnt->n_sample;
+    const int prev = s_prev;
     long long emitted = 0;
     for (int i = 0; i < prev; ++i) {
-      const int slot = e.plan.sample_slot[i];
-      const int tok = e.next_ids[i];
-      if (e.slot_state[slot] == kSlotFree) continue;
-      const int req = e.slot_req[slot];
-      const DevRequest rq = e.reqs[req];
-      const int ng = e.slot_ngen[slot];
+      const int slot = smp_slot[i];
+      const int tok = smp_tok[i];
+      if (st_state[slot] == kSlotFree) continue;
+      const int req = st_req[slot];
+      const DevRequest rq = st_rq[slot];
+      const int ng = st_ngen[slot];
       int finish = -1;
       if (rq.max_new_tokens <= 0) {
         finish = kFinishLength;
@@ -49,20 +80,20 @@ __global__ void __launch_bounds__(256) k_schedule(EngineDev e) {
         finish = kFinishStop;
       } else {
         e.out_tokens[(size_t)req * e.tok_stride + ng] = tok;
-        e.slot_ngen[slot] = ng + 1;
-        e.slot_last[slot] = tok;
-        e.slot_state[slot] = kSlotDecode;
+        st_ngen[slot] = ng + 1;
+        st_last[slot] = tok;
+        st_state[slot] = kSlotDecode;
         ++emitted;
         if (ng + 1 >= rq.max_new_tokens) finish = kFinishLength;
       }
       if (finish >= 0) {
-        e.results[req].n_tokens = e.slot_ngen[slot];
+        e.results[req].n_tokens = st_ngen[slot];
         e.results[req].finish_reason = finish;
-        const int np = e.slot_npages[slot];
-        int* pt = e.page_table + (size_t)slot * e.max_pages_per_slot;
+        const int np = st_npages[slot];
+        const int* pt = e.page_table + (size_t)slot * e.max_pages_per_slot;
         for (int k = 0; k < np; ++k) e.free_stack[c->free_top++] = pt[k];
-        e.slot_npages[slot] = 0;
-        e.slot_state[slot] = kSlotFree;
+        st_npages[slot] = 0;
+        st_state[slot] = kSlotFree;
         c->done += 1;
       }
     }
@@ -72,13 +103,12 @@ __global__ void __launch_bounds__(256) k_schedule(EngineDev e) {
       cnt->finished = c->done >= e.n_reqs ? 1 : 0;
     }
   }
-  if (e.consume_only) return;
-  if (threadIdx.x == 0) {
-    EngineCounters* c = e.ctr;
+  if (!e.consume_only && threadIdx.x == 0) {
+    EngineCounters* c = &s_ctr;
 
     // ---- 2. admit queued requests into free slots ----
-    for (int s = 0; s < e.max_batch && c->next_req < e.n_reqs; ++s) {
-      if (e.slot_state[s] != kSlotFree) continue;
+    for (int s = 0; s < nb && c->next_req < e.n_reqs; ++s) {
+      if (st_state[s] != kSlotFree) continue;
       const DevRequest rq = e.reqs[c->next_req];
       const int budget = rq.max_new_tokens > 0 ? rq.max_new_tokens : 0;
       const int need = (rq.prompt_len + budget + e.page_tokens - 1) / e.page_tokens;
@@ -95,29 +125,30 @@ __global__ void __launch_bounds__(256) k_schedule(EngineDev e) {
       if (need > c->free_top) break;  // wait for pages to come back (FIFO)
       int* pt = e.page_table + (size_t)s * e.max_pages_per_slot;
       for (int k = 0; k < need; ++k) pt[k] = e.free_stack[--c->free_top];
-      e.slot_npages[s] = need;
-      e.slot_state[s] = kSlotPrefill;
-      e.slot_req[s] = c->next_req;
-      e.slot_len[s] = 0;
-      e.slot_pdone[s] = 0;
-      e.slot_ngen[s] = 0;
+      st_npages[s] = need;
+      st_state[s] = kSlotPrefill;
+      st_req[s] = c->next_req;
+      st_rq[s] = rq;
+      st_len[s] = 0;
+      st_pdone[s] = 0;
+      st_ngen[s] = 0;
       c->next_req += 1;
     }
 
     // ---- 3. lay out the next plan (segment descriptors) ----
     int rows = 0, items = 0, samples = 0, pblocks = 0;
     long long kv_tokens = 0;
-    for (int s = 0; s < e.max_batch; ++s) {
+    for (int s = 0; s < nb; ++s) {
       s_seg_n[s] = 0;
-      if (e.slot_state[s] == kSlotDecode && rows < e.max_rows) {
-        kv_tokens += e.slot_len[s] + 1;
+      if (st_state[s] == kSlotDecode && rows < e.max_rows) {
+        kv_tokens += st_len[s] + 1;
         s_seg_row0[s] = rows;
         s_seg_n[s] = 1;
-        s_seg_pos0[s] = e.slot_len[s];
+        s_seg_pos0[s] = st_len[s];
         s_seg_item0[s] = items;
         s_seg_sample[s] = samples;
-        e.slot_len[s] += 1;
-        items += (e.slot_len[s] + kDecodeItemTokens - 1) / kDecodeItemTokens;
+        st_len[s] += 1;
+        items += (st_len[s] + kDecodeItemTokens - 1) / kDecodeItemTokens;
         rows += 1;
         samples += 1;
       }
@@ -127,22 +158,22 @@ __global__ void __launch_bounds__(256) k_schedule(EngineDev e) {
     c->last_decode_rows = n_decode;
     int budget_rows = e.allow_prefill ? e.prefill_chunk : 0;
     long long pending = 0;
-    for (int s = 0; s < e.max_batch; ++s) {
-      if (e.slot_state[s] != kSlotPrefill) continue;
-      pending += e.reqs[e.slot_req[s]].prompt_len - e.slot_pdone[s];
-      const DevRequest rq = e.reqs[e.slot_req[s]];
-      const int left = rq.prompt_len - e.slot_pdone[s];
+    for (int s = 0; s < nb; ++s) {
+      if (st_state[s] != kSlotPrefill) continue;
+      const DevRequest rq = st_rq[s];
+      pending += rq.prompt_len - st_pdone[s];
+      const int left = rq.prompt_len - st_pdone[s];
       int take = left < budget_rows ? left : budget_rows;
       if (take > e.max_rows - rows) take = e.max_rows - rows;
       if (take <= 0) continue;
       s_seg_row0[s] = rows;
       s_seg_n[s] = take;
-      s_seg_pos0[s] = e.slot_len[s];
-      s_seg_emb0[s] = rq.embed_row + e.slot_pdone[s];
+      s_seg_pos0[s] = st_len[s];
+      s_seg_emb0[s] = rq.embed_row + st_pdone[s];
       s_seg_item0[s] = pblocks;
       s_seg_sample[s] = take == left ? samples++ : -1;
-      e.slot_pdone[s] += take;
-      e.slot_len[s] += take;
+      st_pdone[s] += take;
+      st_len[s] += take;
       rows += take;
       pblocks += (take + kRowsPerPBlock - 1) / kRowsPerPBlock;
       budget_rows -= take;
@@ -159,6 +190,18 @@ __global__ void __launch_bounds__(256) k_schedule(EngineDev e) {
     if (rows > 0) c->steps += 1;
   }
   __syncthreads();
+  // ---- write the slot state and counters back ----
+  for (int s = threadIdx.x; s < nb; s += blockDim.x) {
+    e.slot_state[s] = st_state[s];
+    e.slot_req[s] = st_req[s];
+    e.slot_len[s] = st_len[s];
+    e.slot_pdone[s] = st_pdone[s];
+    e.slot_ngen[s] = st_ngen[s];
+    e.slot_last[s] = st_last[s];
+    e.slot_npages[s] = st_npages[s];
+  }
+  if (threadIdx.x == 0) *e.ctr = s_ctr;
+  if (e.consume_only) return;
 
   // ---- 4. fill the plan arrays in parallel ----
   for (int s = 0; s < e.max_batch; ++s) {
@@ -170,7 +213,7 @@ __global__ void __launch_bounds__(256) k_schedule(EngineDev e) {
       const int r = row0 + i;
       e.plan.row_slot[r] = s;
       e.plan.row_pos[r] = pos0 + i;
-      e.plan.row_tok[r] = dec ? e.slot_last[s] : -1;
+      e.plan.row_tok[r] = dec ? st_last[s] : -1;
       e.plan.row_emb[r] = dec ? 0 : (int)(s_seg_emb0[s] + i);
     }
     if (dec) {
