@@ -69,6 +69,10 @@ def parse_args():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--max-new", type=int, default=4096,
                     help="cap on max_new_tokens per request (bounds the KV pool for profiling runs)")
+    ap.add_argument("--workload", type=int, choices=[3, 4], default=3,
+                    help="3: the headline queue; 4: BASELINE config 4 (chunked prefill of 8 x 16k prompts "
+                         "mixed with 24 decoding sequences), a separate report")
+    ap.add_argument("--precision", default="int8_bf16", help="precision of the --workload 4 report")
     return ap.parse_args()
 
 
@@ -280,8 +284,76 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_config4(args):
+    """BASELINE config 4 on one GPU: 24 sequences decode while 8 prompts of
+    16,384 rows are prefilled in 2,048-row chunks inside the same steps. The
+    24 decoders' prompts are prefilled first (untimed); the timed windows are
+    the steps that prefill the long prompts. Reports prefill rows/s, decoded
+    tokens/s and the tensor-core work rate of the prefill rows (projection
+    GEMMs + causal attention) against the measured bf16 peak."""
+    import importlib
+
+    pkg = __graft_entry__.load_package()
+    syn = importlib.import_module("fmd_b200.synthetic")
+    cfg = pkg.TextConfig(num_hidden_layers=args.layers)
+    prec = args.precision
+    w = syn.make_weights(cfg, seed=args.seed, prequantized=prec.startswith("int8"))
+    wl = syn.workload(4, cfg, w["embed"], seed=args.seed, out_bf16=True)
+    n_dec = wl.meta["n_decoders"]
+    dec = pkg.Qwen3Decoder(cfg, prec, device=0)
+    dec.load_weights(w)
+    dec.reserve(max_slots=32, max_tokens=int(np.sum(wl.prompt_lens + wl.max_new + 64)), max_rows=32 + 2048)
+    eng = pkg.Engine(dec)
+    eng.load(wl.prompt_lens, wl.max_new, wl.forced_stop, wl.arena, sort_by_length=False)
+    eng.start(32, 2048)
+    dec_rows = int(np.sum(wl.prompt_lens[:n_dec]))
+    long_len = int(wl.prompt_lens[-1])
+    st = eng.step(8)
+    while st.prefill_tokens < dec_rows + 2048:  # decoders running, long prefill under way (warm-up)
+        st = eng.step(8)
+    clocks = ClockSampler(0)
+    clocks.start()
+    t_ms = p_rows = d_tok = steps = mixed = 0
+    attn_pos = 0.0
+    p0 = st.prefill_tokens
+    while st.prefill_tokens < dec_rows + 8 * long_len:
+        before = st.prefill_tokens
+        st = eng.step(8)
+        t_ms += st.window_device_ms
+        d_tok += st.window_tokens
+        steps += st.window_steps
+        mixed += st.window_mixed_steps
+        # causal attention work of the long-prompt rows prefilled in this window:
+        # a row at offset o of its prompt attends to o + 1 keys
+        for o in range(before - dec_rows, st.prefill_tokens - dec_rows):
+            attn_pos += (o % long_len) + 1
+    clk = clocks.stop()
+    p_rows = st.prefill_tokens - p0
+    lin_params = cfg.n_params(with_head=False)  # the projections, lm_head excluded
+    per_pos = 4 * cfg.num_attention_heads * cfg.head_dim * cfg.num_hidden_layers
+    flops = 2.0 * lin_params * p_rows + per_pos * attn_pos
+    secs = t_ms / 1000.0
+    peaks = json.loads(PEAKS_FILE.read_text()) if PEAKS_FILE.exists() else {}
+    peak = float(peaks.get("bf16_tflops_sustained", 1381.0))
+    line = {"metric": "config 4: prefill rows/s and decoded tokens/s of mixed steps", "workload":
+            "BASELINE config 4: 8 x 16,384-row prompts prefilled in 2,048-row chunks while 24 sequences "
+            "(contexts log-uniform 1k-8k) decode, batch 32", "precision": prec, "layers": cfg.num_hidden_layers,
+            "timed_steps": int(steps), "mixed_steps": int(mixed), "ms_per_step": t_ms / max(steps, 1),
+            "prefill_rows_per_s": p_rows / secs, "decode_tokens_per_s": d_tok / secs,
+            "prefill_tflops_per_s": flops / secs / 1e12,
+            "prefill_tensor_frac": flops / secs / 1e12 / peak, "peak_tflops": peak,
+            "peak_kind": "measured sustained bf16 (cuBLAS)",
+            "note": "time of whole steps (the 24 decode rows included) against the prefill rows' FLOPs",
+            "clocks": clk}
+    print(json.dumps(line), flush=True)
+    dec.close()
+
+
 def main():
     args = parse_args()
+    if args.workload == 4:
+        run_config4(args)
+        return
     if args.impl == "reference":
         run_reference(args)  # host cores only: no process group
         return

@@ -52,6 +52,7 @@ constexpr int kRows = 64;   // rows per row tile (decode steps carry one row per
 constexpr int kMaxKb = 16;  // 64-wide k-blocks per CTA (K / S <= 1024)
 constexpr uint32_t kWaitLimit = 1u << 22;
 constexpr int kStatusTimeout = -110;
+constexpr int kStatusNonFinite = -5;  // FMD_EIO: a greedy pick saw no finite logit
 
 // Decode-packed weights. Each CTA's slice (FT features x K/S) is one
 // contiguous tile in HBM, ordered [k-block][warp][fragment] so that a k-block
@@ -796,7 +797,8 @@ __global__ void __launch_bounds__((G * kHeadWarps + 1) * 32, 1)
 __global__ void __launch_bounds__(256) k_pick_reduce(const int* __restrict__ n_sample_ptr,
                                                      const float* __restrict__ best_val,
                                                      const int* __restrict__ best_idx, int n_parts,
-                                                     int* __restrict__ next_ids) {
+                                                     int* __restrict__ next_ids, int vocab,
+                                                     int* __restrict__ status) {
   __shared__ float sv[8];
   __shared__ int si[8];
   griddep_launch();
@@ -834,6 +836,12 @@ __global__ void __launch_bounds__(256) k_pick_reduce(const int* __restrict__ n_s
           best = sv[w];
           bi = si[w];
         }
+      // no finite logit in the row (all candidates NaN): report it instead of
+      // handing an index outside the vocabulary to the next step
+      if (bi < 0 || bi >= vocab) {
+        bi = 0;
+        atomicExch(status, kStatusNonFinite);
+      }
       next_ids[r] = bi;
     }
     __syncthreads();
@@ -1026,8 +1034,9 @@ int launch_lm_head(ActType at, const LinW& W, const void* x, int ldx, const int*
 }
 
 void launch_pick_reduce(const int* n_sample_ptr, int B, const float* best_val, const int* best_idx, int n_parts,
-                        int* next_ids, cudaStream_t s) {
-  launch_pdl(k_pick_reduce, dim3(B), dim3(256), 0, s, n_sample_ptr, best_val, best_idx, n_parts, next_ids);
+                        int* next_ids, int vocab, int* status, cudaStream_t s) {
+  launch_pdl(k_pick_reduce, dim3(B), dim3(256), 0, s, n_sample_ptr, best_val, best_idx, n_parts, next_ids, vocab,
+             status);
 }
 
 }  // namespace fmd

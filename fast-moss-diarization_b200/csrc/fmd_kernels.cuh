@@ -222,8 +222,10 @@ bool launch_gemv(ActType at, int epi, bool norm, const LinW& W, const void* x, i
 // into ep.best_val / best_idx (0: nothing launched).
 int launch_lm_head(ActType at, const LinW& W, const void* x, int ldx, const int* row_map, const int* n_rows_ptr,
                    int max_rows, const GemvEpi& ep, int* status, cudaStream_t s);
+// next_ids[r] = the lowest-index maximum of row r; a row without a finite
+// candidate gets 0 and sets *status to FMD_EIO
 void launch_pick_reduce(const int* n_sample_ptr, int B, const float* best_val, const int* best_idx, int n_parts,
-                        int* next_ids, cudaStream_t s);
+                        int* next_ids, int vocab, int* status, cudaStream_t s);
 
 // fmd_attn_decode.cu: TMA-fed decode attention with the split-KV merge fused in.
 // `tmap` points at a CUtensorMap over the KV pool viewed as 2D

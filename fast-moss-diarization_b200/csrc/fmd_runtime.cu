@@ -502,7 +502,8 @@ void run_forward_decode(fmd_handle* h, float* logits_dev, const void* arena) {
                                    h->d_status, s);
   if (parts == 0) h->launch_refused = true;
   trace(h, "lm_head", -1);
-  launch_pick_reduce(nsamp, h->max_slots, h->best_val, h->best_idx, parts, h->next_ids, s);
+  launch_pick_reduce(nsamp, h->max_slots, h->best_val, h->best_idx, parts, h->next_ids, c.vocab_size,
+                       h->d_status, s);
   trace(h, "argmax", -1);
 }
 
@@ -578,7 +579,8 @@ void run_forward(fmd_handle* h, float* logits_dev, const void* arena, bool decod
                                    h->d_status, s);
   trace(h, "lm_head", -1);
   if (parts > 0) {
-    launch_pick_reduce(nsamp, h->max_slots, h->best_val, h->best_idx, parts, h->next_ids, s);
+    launch_pick_reduce(nsamp, h->max_slots, h->best_val, h->best_idx, parts, h->next_ids, c.vocab_size,
+                       h->d_status, s);
   } else {
     launch_linear(h->at, h->lm_head, h->xn, H, h->plan.sample_row, nsamp, h->max_slots, h->part, ss, decode_only, s);
     launch_logits_argmax(h->at, nsamp, h->max_slots, h->part, c.vocab_size, logits_dev, h->next_ids, s);
@@ -672,7 +674,8 @@ int sync_check(fmd_handle* h) {
     if (e != cudaSuccess) return fail(h, FMD_EIO, std::string("status read: ") + cudaGetErrorString(e));
     if (st != 0) {
       cudaMemset(h->d_status, 0, sizeof(int));
-      return fail(h, st, "a bounded device-side wait gave up (status " + std::to_string(st) + ")");
+      return fail(h, st, st == FMD_EIO ? std::string("a greedy pick found no finite logit (non-finite activations)")
+                                       : "a bounded device-side wait gave up (status " + std::to_string(st) + ")");
     }
   }
   return FMD_OK;
@@ -1302,6 +1305,7 @@ EngineDev make_engine_dev(fmd_handle* h, int max_batch, int chunk, int allow_pre
   e.max_rows = h->max_rows;
   e.max_pages_per_slot = h->max_pages_per_slot;
   e.eos = h->cfg.eos_token_id;
+  e.vocab = h->cfg.vocab_size;
   e.page_tokens = kPageTokens;
   e.tok_stride = h->eng_tok_stride;
   e.reqs = (const DevRequest*)h->eng_reqs.p;

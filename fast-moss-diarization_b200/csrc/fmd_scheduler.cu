@@ -22,6 +22,7 @@ namespace {
 constexpr int kMaxSlots = 256;
 constexpr int kFinishStop = 0, kFinishLength = 1, kFinishError = 2;
 constexpr int kStatusNoMem = -12;
+constexpr int kStatusBadToken = -5;  // FMD_EIO
 
 __global__ void __launch_bounds__(256) k_schedule(EngineDev e) {
   __shared__ int s_seg_row0[kMaxSlots], s_seg_n[kMaxSlots], s_seg_pos0[kMaxSlots], s_seg_item0[kMaxSlots];
@@ -76,6 +77,11 @@ __global__ void __launch_bounds__(256) k_schedule(EngineDev e) {
       int finish = -1;
       if (rq.max_new_tokens <= 0) {
         finish = kFinishLength;
+      } else if (tok < 0 || tok >= e.vocab) {
+        // never fed back: an id outside the vocabulary would index past the
+        // embedding table (the greedy pick has already flagged the step)
+        finish = kFinishError;
+        c->status = kStatusBadToken;
       } else if (tok == e.eos || (rq.forced_stop >= 0 && ng == rq.forced_stop)) {
         finish = kFinishStop;
       } else {

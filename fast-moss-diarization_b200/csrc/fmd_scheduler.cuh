@@ -44,6 +44,7 @@ struct EngineDev {
   int max_rows;        // plan capacity R
   int max_pages_per_slot;
   int eos;
+  int vocab;           // token ids outside [0, vocab) end their request with an error
   int page_tokens;
   int tok_stride;
   const DevRequest* reqs;

@@ -145,7 +145,7 @@ def config1_prompts(cfg: TextConfig, embed: np.ndarray, seed: int = 0):
 
 def workload(config: int, cfg: TextConfig, embed: np.ndarray, seed: int = 0, n_requests: int | None = None,
              out_bf16: bool = True, with_arena: bool = True) -> Workload:
-    """Request queues of BASELINE configs 2, 3 and 5 (and 4's decoders);
+    """Request queues of BASELINE configs 2 to 5;
     `with_arena=False` leaves the prompt embeddings out (lengths only)."""
     rng = np.random.default_rng(seed + 100 * config)
     if config == 2:
@@ -161,6 +161,17 @@ def workload(config: int, cfg: TextConfig, embed: np.ndarray, seed: int = 0, n_r
         stops = np.minimum(rng.geometric(1.0 / 600, n), 4096)
         wl = Workload("q8_0_b32_continuous", lens, np.full(n, 4096), stops, max_batch=32, prefill_chunk=2048,
                       precision="int8_bf16")
+    elif config == 4:
+        # 24 decoders first (contexts log-uniform 1k-8k, decoding throughout),
+        # then 8 prompts of 16k tokens prefilled in 2048-row chunks while the
+        # 24 decode (FIFO admission puts the long prompts behind them)
+        n_dec = 24
+        dec_lens = log_uniform_lengths(rng, n_dec, 1000, 8000)
+        lens = np.concatenate([dec_lens, np.full(8, 16384, dtype=np.int64)])
+        max_new = np.concatenate([np.full(n_dec, 4096), np.full(8, 16)])
+        forced = np.full(n_dec + 8, -1)
+        wl = Workload("chunked_prefill_mixed", lens, max_new, forced, max_batch=32, prefill_chunk=2048,
+                      precision="int8_bf16", meta={"n_decoders": n_dec})
     elif config == 5:
         n = n_requests or 2048
         lens = log_uniform_lengths(rng, n, 300, 16000)
