@@ -39,7 +39,7 @@ EXPORTS = [
     "fmd_kv_reserve", "fmd_cache_bytes", "fmd_memory_bytes", "fmd_embed", "fmd_splice_audio", "fmd_slot_open", "fmd_slot_release",
     "fmd_slot_len", "fmd_prefill", "fmd_decode_step", "fmd_engine_load", "fmd_engine_start", "fmd_engine_step",
     "fmd_engine_run", "fmd_engine_fetch",
-    "fmd_generate", "fmd_debug_weight", "fmd_debug_kv", "fmd_q8_0_quantize", "fmd_greedy_pick_noalloc",
+    "fmd_generate", "fmd_debug_weight", "fmd_debug_kv", "fmd_q8_0_quantize", "fmd_q8_0_quantize_device", "fmd_greedy_pick_noalloc",
 ]
 
 
@@ -133,6 +133,7 @@ def load() -> C.CDLL:
         "fmd_debug_weight": (C.c_int, [P, I32, I32, C.POINTER(C.c_float), I64]),
         "fmd_debug_kv": (C.c_int, [P, I32, I32, I32, I32, P, P]),
         "fmd_q8_0_quantize": (C.c_int, [C.POINTER(C.c_float), I64, I64, P]),
+        "fmd_q8_0_quantize_device": (C.c_int, [P, I32, I64, I64, P, P, P]),
         "fmd_greedy_pick_noalloc": (C.c_int, [P, I32, I32, P, P]),
     }
     for name, (res, args) in sig.items():

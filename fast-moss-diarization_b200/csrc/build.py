@@ -22,7 +22,8 @@ ROOT = PKG.parent
 LIB = PKG / "libfmd_decoder.so"
 OBJ_DIR = PKG / "_build"
 SOURCES = ["fmd_kernels.cu", "fmd_gemv.cu", "fmd_gemm_tc.cu", "fmd_attn_decode.cu", "fmd_scheduler.cu", "fmd_runtime.cu",
-           "fmd_noalloc.cu", "fmd_splice.cu", "fmd_attn_prefill.cu"]
+           "fmd_noalloc.cu", "fmd_splice.cu", "fmd_attn_prefill.cu",
+           "fmd_quant.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

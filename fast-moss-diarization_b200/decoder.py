@@ -26,6 +26,18 @@ def _f32(a) -> np.ndarray:
     return np.ascontiguousarray(a, dtype=np.float32)
 
 
+def _host(a) -> tuple:
+    """(contiguous array, FMD_DT_*) of a host tensor: bf16 bit patterns (uint16)
+    and f16 are passed as stored (checkpoint views stay memory-mapped),
+    anything else as f32."""
+    a = np.asarray(a)
+    if a.dtype == np.uint16:
+        return np.ascontiguousarray(a), _lib.DT_BF16
+    if a.dtype == np.float16:
+        return np.ascontiguousarray(a), _lib.DT_F16
+    return _f32(a), _lib.DT_F32
+
+
 def _q8_blocks(qs: np.ndarray, d: np.ndarray) -> np.ndarray:
     """(qs, d) -> GGML 34-byte blocks, shape (rows, cols/32, 34)."""
     rows, cols = qs.shape
@@ -77,7 +89,8 @@ class Qwen3Decoder:
     # -- weights -------------------------------------------------------------------------
     def load_weights(self, w: dict) -> None:
         """`Qwen3::load` (qwen3.rs:354-390) from a host weight dictionary
-        (see `synthetic.make_weights`)."""
+        (`synthetic.make_weights`, or `checkpoint.load_checkpoint` for a real
+        checkpoint: arrays may be f32, f16 or bf16 bit patterns)."""
         keep: list = []
 
         def t(arr, dtype=_lib.DT_F32) -> _lib.Tensor:
@@ -90,22 +103,22 @@ class Qwen3Decoder:
         layers = (_lib.LayerWeights * self.cfg.num_hidden_layers)()
         for i, lw in enumerate(w["layers"]):
             L = layers[i]
-            L.input_layernorm = t(_f32(lw["input_norm"]))
-            L.post_attention_layernorm = t(_f32(lw["post_norm"]))
-            L.q_norm = t(_f32(lw["q_norm"]))
-            L.k_norm = t(_f32(lw["k_norm"]))
+            L.input_layernorm = t(*_host(lw["input_norm"]))
+            L.post_attention_layernorm = t(*_host(lw["post_norm"]))
+            L.q_norm = t(*_host(lw["q_norm"]))
+            L.k_norm = t(*_host(lw["k_norm"]))
             for cname, key in (("q_proj", "q"), ("k_proj", "k"), ("v_proj", "v"), ("o_proj", "o"),
                                ("gate_proj", "gate"), ("up_proj", "up"), ("down_proj", "down")):
                 if pre is not None:
                     qs, d = pre["layers"][i][key]
                     setattr(L, cname, t(_q8_blocks(qs, d), _lib.DT_Q8_0))
                 else:
-                    setattr(L, cname, t(_f32(lw[key])))
+                    setattr(L, cname, t(*_host(lw[key])))
         ws = _lib.Weights()
-        ws.embed_tokens = t(_f32(w["embed"]))
-        ws.norm = t(_f32(w["norm"]))
+        ws.embed_tokens = t(*_host(w["embed"]))
+        ws.norm = t(*_host(w["norm"]))
         head = w.get("lm_head")
-        ws.lm_head = t(_f32(head)) if head is not None else _lib.Tensor(None, _lib.DT_F32)
+        ws.lm_head = t(*_host(head)) if head is not None else _lib.Tensor(None, _lib.DT_F32)
         ws.layers = layers
         keep.append(layers)
         self._check(self.lib.fmd_load_weights(self._h, C.byref(ws)))

@@ -294,6 +294,17 @@ int fmd_greedy_pick_noalloc(const float* logits, int32_t n_rows, int32_t vocab, 
  * linear.rs:197): rows x cols f32 -> rows x cols/32 34-byte blocks. */
 int fmd_q8_0_quantize(const float* src, int64_t rows, int64_t cols, void* blocks);
 
+/* The same quantisation on the GPU, for weights already in device memory (a
+ * checkpoint uploaded as stored): `src` is rows x cols of FMD_DT_F32, F16 or
+ * BF16 (each value taken as its exact f32), `qs` receives rows x cols int8 and
+ * `d` rows x cols/32 f16 scales (bit patterns), the structure-of-arrays form of
+ * the 34-byte blocks; bit-identical to fmd_q8_0_quantize. All three pointers
+ * are device memory; the work is queued on `stream` (a cudaStream_t, NULL =
+ * legacy default stream) and the call does not synchronise. cols must be a
+ * multiple of 32. */
+int fmd_q8_0_quantize_device(const void* src, int32_t src_dtype, int64_t rows, int64_t cols, int8_t* qs,
+                             uint16_t* d, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
