@@ -69,9 +69,11 @@ def parse_args():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--max-new", type=int, default=4096,
                     help="cap on max_new_tokens per request (bounds the KV pool for profiling runs)")
-    ap.add_argument("--workload", type=int, choices=[3, 4], default=3,
+    ap.add_argument("--workload", choices=["3", "4", "encoder"], default="3",
                     help="3: the headline queue; 4: BASELINE config 4 (chunked prefill of 8 x 16k prompts "
-                         "mixed with 24 decoding sequences), a separate report")
+                         "mixed with 24 decoding sequences), a separate report; encoder: the Whisper encoder "
+                         "+ adaptor over 30 s mel chunks (MossModel::encode_audio), a separate report")
+    ap.add_argument("--chunks", type=int, default=64, help="mel chunks per step of --workload encoder")
     ap.add_argument("--precision", default="int8_bf16", help="precision of the --workload 4 report")
     return ap.parse_args()
 
@@ -349,9 +351,91 @@ def run_config4(args):
     dec.close()
 
 
+def run_encoder(args):
+    """The audio tower (Whisper-Medium encoder, 24 layers, + VQ adaptor) over
+    `--chunks` 30 s log-mel chunks per step, as `MossModel::encode_audio` runs
+    them (encoder batches of 16 chunks, model/mod.rs:20-23): 8 audios, each
+    with full 375-token chunks and a 125-token final chunk. `value` = chunks/s
+    with the mel resident on the device (CUDA events around each call's device
+    work); `e2e` = the same through the host API (f32 mel in host memory,
+    embeddings copied back). The CPU baseline runs the f32 oracle on one chunk."""
+    import torch
+
+    pkg = __graft_entry__.load_package()
+    from oracle.whisper_ref import AudioConfig as RefConfig
+    from oracle.whisper_ref import WhisperRef, random_audio_weights
+
+    cfg = pkg.AudioConfig()
+    w = random_audio_weights(RefConfig(**cfg.oracle_kwargs()), args.seed)
+    n = args.chunks
+    per_audio = max(1, n // 8)
+    tokens = [cfg.tokens_per_chunk if (i + 1) % per_audio else 125 for i in range(n)]
+    mapping = [min(i // per_audio, 7) for i in range(n)]
+    n_audios = max(mapping) + 1
+    mel = np.random.default_rng(args.seed + 1).standard_normal((n, cfg.num_mel_bins, cfg.mel_frames),
+                                                               dtype=np.float32)
+    prec = "bf16" if args.precision == "int8_bf16" else args.precision
+    enc = pkg.AudioEncoder(cfg, w, prec, device=0, max_batch=16)
+    mel_dev = torch.from_numpy(mel).cuda()
+    out, off = enc.encode_audio_device(mel_dev, tokens, mapping, n_audios)
+    for _ in range(args.warmup):
+        enc.encode_audio_device(mel_dev, tokens, mapping, n_audios, out=out)
+    clocks = ClockSampler(0)
+    clocks.start()
+    dev_ms, kernels = [], 0
+    for _ in range(args.steps):
+        enc.encode_audio_device(mel_dev, tokens, mapping, n_audios, out=out)
+        ms, k = enc.last_timing()
+        dev_ms.append(ms)
+        kernels += k
+    clk = clocks.stop()
+    e2e_s = []
+    for _ in range(max(2, args.steps // 2)):
+        t0 = time.perf_counter()
+        host = enc.encode_audio(mel, tokens, mapping, n_audios)
+        e2e_s.append(time.perf_counter() - t0)
+    mean_ms = float(np.mean(dev_ms))
+    flops = pkg.audio.encoder_flops(cfg, n)
+    peaks = json.loads(PEAKS_FILE.read_text()) if PEAKS_FILE.exists() else {}
+    peak = float(peaks.get("bf16_tflops_sustained", 1381.0))
+    achieved = flops / (mean_ms / 1000.0) / 1e12
+    cpu = None
+    if not args.no_cpu:
+        ref = WhisperRef(RefConfig(**cfg.oracle_kwargs()), w)
+        torch.set_num_threads(os.cpu_count() or 1)
+        t0 = time.perf_counter()
+        ref.encode_audio(mel[:1], tokens[:1], [0], 1)
+        cpu_s = time.perf_counter() - t0
+        cpu = {"value": 1.0 / cpu_s, "unit": "chunks/s", "cores": torch.get_num_threads(), "kind": "port",
+               "sample": "one 30 s chunk through the f32 oracle (24 encoder layers + adaptor), torch on the "
+                         "host cores"}
+    e2e_mean = float(np.mean(e2e_s))
+    line = {"metric": "audio encoder chunks/s (Whisper-Medium encoder + VQ adaptor, 30 s chunks)",
+            "value": n / (mean_ms / 1000.0), "unit": "chunks/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": mean_ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": prec, "data": "synthetic (seeded N(0,1) mel, random-init weights)",
+            "audio_seconds_per_s": 30.0 * n / (mean_ms / 1000.0),
+            "config": {"workload": f"encode_audio over {n} chunks of 30 s (8 audios, final chunk of each 125 "
+                                   "tokens), encoder batch 16, 24 layers d_model 1024 heads 16 ffn 4096, "
+                                   "adaptor 4096->1024->1024", "chunks": n, "encoder_batch": 16,
+                       "l2": "working set >> L2 (no flush needed)"},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "traffic": None,
+                         "note": "whole encode_audio call (all kernels) against the measured sustained bf16 "
+                                 "peak; FLOPs = conv + 24 x (projections + attention) + adaptor"},
+            "e2e": {"value": n / e2e_mean, "unit": "chunks/s", "h2d_bytes_per_step": int(mel.nbytes),
+                    "d2h_bytes_per_step": int(sum(h.size for h in host) * 2)},
+            "gpu_launches": int(kernels), "cpu_baseline": cpu, "clocks": clk}
+    print(json.dumps(line), flush=True)
+    enc.close()
+
+
 def main():
     args = parse_args()
-    if args.workload == 4:
+    if args.workload == "encoder":
+        run_encoder(args)
+        return
+    if args.workload == "4":
         run_config4(args)
         return
     if args.impl == "reference":

@@ -4,17 +4,20 @@ The hot path of cnmoro/fast-moss-diarization -- the Qwen3 decoder step driven
 by `Engine::generate_batch` -- rebuilt as sm_100a kernels behind a C ABI
 (`include/fmd_decoder.h`, `libfmd_decoder.so`). This package is the Python
 host side: `Qwen3Decoder` (the decoder-forward operator surface of
-`qwen3.rs`), `Engine` (continuous batching with on-GPU slot refill), seeded
+`qwen3.rs`), `Engine` (continuous batching with on-GPU slot refill),
+`AudioEncoder` (the Whisper encoder + VQ adaptor that produce the audio
+embeddings, include/fmd_audio.h), seeded
 synthetic workloads, and the request-sharded multi-GPU launcher.
 """
 
 from . import _lib
 from ._lib import FmdError
+from .audio import AudioConfig, AudioEncoder
 from .config import EOS_TOKEN_ID, TextConfig, parse_precision
 from .decoder import Qwen3Decoder
 from .engine import BatchStats, Engine, Generated
 
-__all__ = ["FmdError", "EOS_TOKEN_ID", "TextConfig", "parse_precision", "Qwen3Decoder", "Engine", "BatchStats",
+__all__ = ["AudioConfig", "AudioEncoder", "FmdError", "EOS_TOKEN_ID", "TextConfig", "parse_precision", "Qwen3Decoder", "Engine", "BatchStats",
            "Generated", "library_path", "load_library"]
 
 

@@ -40,6 +40,9 @@ EXPORTS = [
     "fmd_slot_len", "fmd_prefill", "fmd_decode_step", "fmd_engine_load", "fmd_engine_start", "fmd_engine_step",
     "fmd_engine_run", "fmd_engine_fetch",
     "fmd_generate", "fmd_debug_weight", "fmd_debug_kv", "fmd_q8_0_quantize", "fmd_q8_0_quantize_device", "fmd_greedy_pick_noalloc",
+    # include/fmd_audio.h
+    "fmd_audio_create", "fmd_audio_destroy", "fmd_audio_last_error", "fmd_audio_memory_bytes", "fmd_audio_encode",
+    "fmd_audio_encode_audio", "fmd_audio_last_timing",
 ]
 
 
@@ -93,6 +96,28 @@ class Stats(C.Structure):
                 ("graph_kernels_decode", C.c_int64)]
 
 
+class AudioConfig(C.Structure):
+    _fields_ = [(n, C.c_int32) for n in (
+        "num_mel_bins", "d_model", "encoder_layers", "encoder_attention_heads", "encoder_ffn_dim",
+        "max_source_positions", "audio_merge_size", "adaptor_input_dim", "hidden_size")] + [
+        ("adaptor_norm_eps", C.c_float)]
+
+
+class EncoderLayerWeights(C.Structure):
+    _fields_ = [(n, Tensor) for n in (
+        "q_proj_w", "q_proj_b", "k_proj_w", "v_proj_w", "v_proj_b", "out_proj_w", "out_proj_b",
+        "self_attn_layer_norm_w", "self_attn_layer_norm_b", "fc1_w", "fc1_b", "fc2_w", "fc2_b",
+        "final_layer_norm_w", "final_layer_norm_b")]
+
+
+class AudioWeights(C.Structure):
+    _fields_ = [("conv1_w", Tensor), ("conv1_b", Tensor), ("conv2_w", Tensor), ("conv2_b", Tensor),
+                ("embed_positions", Tensor), ("layers", C.POINTER(EncoderLayerWeights)),
+                ("layer_norm_w", Tensor), ("layer_norm_b", Tensor), ("adaptor_fc1_w", Tensor),
+                ("adaptor_fc1_b", Tensor), ("adaptor_fc2_w", Tensor), ("adaptor_fc2_b", Tensor),
+                ("adaptor_norm_w", Tensor), ("adaptor_norm_b", Tensor)]
+
+
 _lib = None
 
 
@@ -135,6 +160,14 @@ def load() -> C.CDLL:
         "fmd_q8_0_quantize": (C.c_int, [C.POINTER(C.c_float), I64, I64, P]),
         "fmd_q8_0_quantize_device": (C.c_int, [P, I32, I64, I64, P, P, P]),
         "fmd_greedy_pick_noalloc": (C.c_int, [P, I32, I32, P, P]),
+        "fmd_audio_create": (C.c_int, [C.POINTER(AudioConfig), C.POINTER(AudioWeights), I32, I32, I32,
+                                       C.POINTER(P)]),
+        "fmd_audio_destroy": (C.c_int, [P]),
+        "fmd_audio_last_error": (C.c_char_p, [P]),
+        "fmd_audio_memory_bytes": (C.c_int, [P, C.POINTER(I64), C.POINTER(I64)]),
+        "fmd_audio_encode": (C.c_int, [P, P, I32, I32, P]),
+        "fmd_audio_encode_audio": (C.c_int, [P, P, I32, I32, IP, IP, I32, I32, P, C.POINTER(I64)]),
+        "fmd_audio_last_timing": (C.c_int, [P, C.POINTER(C.c_double), C.POINTER(I64)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

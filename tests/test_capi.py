@@ -12,7 +12,7 @@ from conftest import PKG, ROOT
 
 
 def _declared_symbols() -> list[str]:
-    text = (ROOT / "include" / "fmd_decoder.h").read_text()
+    text = "\n".join(p.read_text() for p in sorted((ROOT / "include").glob("*.h")))
     text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
     return sorted(set(re.findall(r"\b(fmd_[a-z0-9_]+)\s*\(", text)))
 
