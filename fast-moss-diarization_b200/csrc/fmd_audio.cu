@@ -211,11 +211,15 @@ int run_encoder(fmd_audio* h, const void* mel, int mel_dt, int n, void* out, int
     e.period = Tp;
     gemm(h, kEpiGeluPos, a2_m, h->conv2_m, M2, D, 3 * D, e, kernels);
   }
-  const float qk_scale = std::pow(64.f, -0.25f);  // head_dim^-1/4 on q and on k (whisper_encoder.rs:40, :52-55)
+  // head_dim^-1/4 on q and on k (whisper_encoder.rs:40, :52-55); q also carries
+  // log2(e), so the attention kernel's scores are already in the exp2 domain
+  const float qk_scale = std::pow(64.f, -0.25f), log2e = 1.4426950408889634f;
   for (const EncLayer& L : h->layers) {
     launch_layernorm(h->at, h->x, nullptr, M2, D, L.ln1_w, L.ln1_b, kLnEps, h->hbuf, s);
     EncEpiArgs e = epi_args(h->bufB, L.qkv_b);
+    e.q_cols = D;
     e.scale_cols = 2 * D;
+    e.scale_q = qk_scale * log2e;
     e.scale = qk_scale;
     gemm(h, kEpiQkv, h_m, L.qkv_m, M2, 3 * D, D, e, kernels);
     launch_enc_attn(h->at, qkv3_m, n, Tp, D, h->H, h->bufA, h->d_status, s);

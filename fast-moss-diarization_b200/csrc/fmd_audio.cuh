@@ -9,7 +9,7 @@ namespace fmd {
 
 // Fused epilogues of the encoder GEMM, v = acc + bias[n]:
 enum EncEpi : int {
-  kEpiQkv = 0,      // out_T = v * (n < scale_cols ? scale : 1)   (q, k scaled by head_dim^-1/4)
+  kEpiQkv = 0,      // out_T = v * (n < q_cols ? scale_q : n < scale_cols ? scale : 1)  (q, k scaling)
   kEpiGelu = 1,     // out_T = gelu_erf(v)                         (conv1, fc1)
   kEpiResid = 2,    // out_f32 += v                                (out_proj, fc2: residual adds)
   kEpiGeluPos = 3,  // out_f32 = gelu_erf(v) + pos[m % period][n]  (conv2 + learned positions)
@@ -22,7 +22,9 @@ struct EncEpiArgs {
   void* out = nullptr;          // [M][N], act dtype or f32 by epilogue
   const float* pos = nullptr;   // [period][N] (kEpiGeluPos)
   int period = 1;
+  int q_cols = 0;
   int scale_cols = 0;
+  float scale_q = 1.f;
   float scale = 1.f;
 };
 
@@ -45,7 +47,8 @@ void launch_enc_gemm(ActType at, int epi, const CUtensorMap& amap, const CUtenso
                      int K, const EncEpiArgs& ep, int* status, cudaStream_t s);
 
 // Bidirectional attention of every (chunk, head): qkv [chunks * frames][3 D]
-// (q | k | v, q and k pre-scaled), through `qkv_map` (enc_make_map3 over it);
+// (q | k | v; k pre-scaled by head_dim^-1/4, q by head_dim^-1/4 x log2(e), so the
+// scores come out in the exp2 domain), through `qkv_map` (enc_make_map3 over it);
 // ctx [chunks * frames][D]. head_dim 64.
 void launch_enc_attn(ActType at, const CUtensorMap& qkv_map, int n_chunks, int frames, int D, int heads, void* ctx,
                      int* status, cudaStream_t s);

@@ -5,7 +5,8 @@
 // for every 30 s chunk and head: softmax(q k^T) v over all `frames` positions
 // of the chunk, no mask (every chunk is exactly 30 s, whisper_encoder.rs:1-5).
 // q and k arrive pre-scaled by head_dim^-1/4 (the QKV GEMM's epilogue), as in
-// the reference (whisper_encoder.rs:52-55).
+// the reference (whisper_encoder.rs:52-55); q also carries the factor log2(e),
+// so S = q k^T is the score in the exp2 domain.
 //
 // One CTA per (128-query tile, head, chunk); two CTAs fit on an SM:
 //  * warp 0 (one lane): TMA loads through a 3D tensor map
@@ -43,7 +44,6 @@ constexpr uint32_t kEaWaitLimit = 1u << 24;
 constexpr int kEaStatusTimeout = -110;
 constexpr int kEaTmemCols = 256;           // S0 [0, 64), S1 [64, 128), O [128, 192)
 constexpr float kEaRescale = 8.f;          // log2 headroom before the reference maximum moves
-constexpr float kLog2e = 1.4426950408889634f;
 
 FMD_DEV void tma_load_3d(void* dst, const void* tmap, int x, int y, int z, uint64_t* bar) {
   asm volatile(
@@ -58,6 +58,14 @@ FMD_DEV void tma_load_3d(void* dst, const void* tmap, int x, int y, int z, uint6
 FMD_DEV uint64_t desc_sw128_mn(uint32_t saddr) {
   return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)(kEaBox >> 4) << 16) | ((uint64_t)(1024 >> 4) << 32) |
          ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// 2^x with the MUFU approximation (PTX ex2.approx.ftz.f32: relative error
+// below 2^-22, 2^-inf = 0), ample for probabilities stored as 16-bit values.
+FMD_DEV float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 FMD_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
@@ -202,23 +210,28 @@ __global__ void __launch_bounds__(192, 2)
       }
       tc_fence_after();
       float s[64];
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint32_t v[32];
-        tmem_ld32(lane_addr + sb * 64 + c * 32, v);
+      {
+        uint32_t v0[32], v1[32];
+        tmem_ld32(lane_addr + sb * 64, v0);
+        tmem_ld32(lane_addr + sb * 64 + 32, v1);
         tmem_ld_wait();
 #pragma unroll
-        for (int i2 = 0; i2 < 32; ++i2) s[c * 32 + i2] = __uint_as_float(v[i2]);
+        for (int i2 = 0; i2 < 32; ++i2) {
+          s[i2] = __uint_as_float(v0[i2]);
+          s[32 + i2] = __uint_as_float(v1[i2]);
+        }
       }
       tc_fence_before();
       mbar_arrive(&s_empty[sb]);
       const int valid = frames - j * 64;  // keys of this tile inside the chunk (>= 1)
-      float mx = -INFINITY;
+      if (valid < 64) {  // only the chunk's last tile (uniform across the CTA)
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        s[c] = c < valid ? s[c] * kLog2e : -INFINITY;
-        mx = fmaxf(mx, s[c]);
+        for (int c = 0; c < 64; ++c) s[c] = c < valid ? s[c] : -INFINITY;
       }
+      float m4[4] = {s[0], s[1], s[2], s[3]};
+#pragma unroll
+      for (int c = 4; c < 64; ++c) m4[c & 3] = fmaxf(m4[c & 3], s[c]);
+      const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
       if (j == 0) {
         m_ref = mx;  // finite: key 0 is inside the chunk
       } else if (mx > m_ref + kEaRescale) {
@@ -227,7 +240,7 @@ __global__ void __launch_bounds__(192, 2)
           break;
         }
         tc_fence_after();
-        const float f = exp2f(m_ref - mx);
+        const float f = ex2(m_ref - mx);
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
           uint32_t v[32];
@@ -241,13 +254,13 @@ __global__ void __launch_bounds__(192, 2)
         l *= f;
         m_ref = mx;
       }
-      float ps = 0.f;
+      float p4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c = 0; c < 64; ++c) {
-        s[c] = exp2f(s[c] - m_ref);
-        ps += s[c];
+        s[c] = ex2(s[c] - m_ref);
+        p4[c & 3] += s[c];
       }
-      l += ps;
+      l += (p4[0] + p4[1]) + (p4[2] + p4[3]);
       if (j >= 2 && (*abort_v || !mbar_wait_bounded(&p_empty[sb], ((j - 2) >> 1) & 1, kEaWaitLimit))) {
         ok = false;
         break;

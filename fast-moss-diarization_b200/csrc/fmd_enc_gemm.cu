@@ -67,8 +67,9 @@ FMD_DEV void epilogue32(const uint32_t (&r)[32], int row, int col0, int N, const
   }
   if constexpr (EPI == kEpiQkv) {
     if (col0 < ep.scale_cols) {
+      const float sc = col0 < ep.q_cols ? ep.scale_q : ep.scale;  // q_cols, scale_cols: multiples of 32
 #pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] *= ep.scale;
+      for (int i = 0; i < 32; ++i) v[i] *= sc;
     }
   } else if constexpr (EPI == kEpiGelu || EPI == kEpiGeluPos) {
 #pragma unroll
