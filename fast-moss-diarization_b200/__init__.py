@@ -6,18 +6,18 @@ by `Engine::generate_batch` -- rebuilt as sm_100a kernels behind a C ABI
 host side: `Qwen3Decoder` (the decoder-forward operator surface of
 `qwen3.rs`), `Engine` (continuous batching with on-GPU slot refill),
 `AudioEncoder` (the Whisper encoder + VQ adaptor that produce the audio
-embeddings, include/fmd_audio.h), seeded
+embeddings) and `MelFrontend` (the log-mel frontend), include/fmd_audio.h; seeded
 synthetic workloads, and the request-sharded multi-GPU launcher.
 """
 
 from . import _lib
 from ._lib import FmdError
-from .audio import AudioConfig, AudioEncoder
+from .audio import AudioConfig, AudioEncoder, AudioFeatures, FeatureConfig, MelFrontend, extract_features
 from .config import EOS_TOKEN_ID, TextConfig, parse_precision
 from .decoder import Qwen3Decoder
 from .engine import BatchStats, Engine, Generated
 
-__all__ = ["AudioConfig", "AudioEncoder", "FmdError", "EOS_TOKEN_ID", "TextConfig", "parse_precision", "Qwen3Decoder", "Engine", "BatchStats",
+__all__ = ["AudioConfig", "AudioEncoder", "AudioFeatures", "FeatureConfig", "MelFrontend", "extract_features", "FmdError", "EOS_TOKEN_ID", "TextConfig", "parse_precision", "Qwen3Decoder", "Engine", "BatchStats",
            "Generated", "library_path", "load_library"]
 
 

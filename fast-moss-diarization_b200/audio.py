@@ -1,5 +1,9 @@
-"""Host side of the audio tower (include/fmd_audio.h): the Whisper encoder and
-the VQ adaptor on the GPU.
+"""Host side of the audio tower (include/fmd_audio.h): the log-mel frontend,
+the Whisper encoder and the VQ adaptor on the GPU.
+
+`MelFrontend` mirrors `MelFrontend::log_mel` (crates/fmd-core/src/audio/mel.rs:84-133)
+and `extract_features` the chunk planning of `extract_features`
+(crates/fmd-core/src/audio/mod.rs:47-116), with the mel computed on the GPU.
 
 `AudioEncoder` mirrors the reference's `WhisperEncoder::forward`
 (crates/fmd-core/src/model/whisper_encoder.rs:142-163) as `forward`, and
@@ -242,3 +246,144 @@ def encoder_flops(cfg: AudioConfig, n_chunks: int) -> float:
     groups = Tp // cfg.audio_merge_size
     adaptor = 2 * groups * cfg.hidden_size * (cfg.adaptor_input_dim + cfg.hidden_size)
     return float(n_chunks) * (conv + cfg.encoder_layers * layer + adaptor)
+
+
+# ---- log-mel frontend (include/fmd_audio.h: fmd_mel_*) -------------------------------
+WHISPER_ENCODER_STRIDE = 2  # config.rs:210
+
+
+@dataclass
+class FeatureConfig:
+    """`FeatureConfig` (config.rs:121-166): the Whisper log-mel frontend."""
+    feature_size: int = 80
+    sampling_rate: int = 16_000
+    hop_length: int = 160
+    n_fft: int = 400
+    n_samples: int = 480_000
+    nb_max_frames: int = 3_000
+
+    def to_c(self) -> _lib.FeatureConfig:
+        return _lib.FeatureConfig(**asdict(self))
+
+
+def audio_token_length(num_samples: int, hop_length: int, merge_size: int) -> int:
+    """Audio tokens of a chunk of `num_samples` samples (config.rs:212-223)."""
+    if num_samples == 0:
+        return 0
+    return (num_samples - 1) // (hop_length * WHISPER_ENCODER_STRIDE * merge_size) + 1
+
+
+def plan_chunks(lengths, cfg: FeatureConfig, merge_size: int):
+    """Chunk layout of `extract_features` (audio/mod.rs:57-82): 30 s windows per
+    waveform (an empty waveform still yields one empty window). Returns
+    ([(audio, start, end)], chunk_token_lengths, chunk_mapping, tokens_per_audio)."""
+    chunks, tokens, mapping, per_audio = [], [], [], [0] * len(lengths)
+    for a, n in enumerate(lengths):
+        start, total = 0, max(int(n), 1)
+        while start < total:
+            end = min(start + cfg.n_samples, int(n))
+            t = audio_token_length(end - start, cfg.hop_length, merge_size)
+            per_audio[a] += t
+            chunks.append((a, start, end))
+            tokens.append(t)
+            mapping.append(a)
+            start += cfg.n_samples
+    return chunks, tokens, mapping, per_audio
+
+
+@dataclass
+class AudioFeatures:
+    """`AudioFeatures` (audio/mod.rs:17-39) with the mel on the device."""
+    mel: object                 # torch tensor (n_chunks, n_mels, frames), f32, on the device
+    chunk_token_lengths: list
+    chunk_mapping: list
+    tokens_per_audio: list
+
+    @property
+    def n_chunks(self) -> int:
+        return len(self.chunk_token_lengths)
+
+
+class MelFrontend:
+    """`MelFrontend` (mel.rs:29-133) on the GPU."""
+
+    def __init__(self, cfg: FeatureConfig = FeatureConfig(), device: int = 0):
+        self.lib = _lib.load()
+        self.cfg = cfg
+        self.device = device
+        self._h = C.c_void_p()
+        st = self.lib.fmd_mel_create(C.byref(cfg.to_c()), device, C.byref(self._h))
+        if st != _lib.FMD_OK:
+            msg = self.lib.fmd_mel_last_error(self._h).decode() if self._h else ""
+            self.close()
+            raise _lib.FmdError(st, f"fmd_mel_create: {msg or self.lib.fmd_status_string(st).decode()}")
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            self.lib.fmd_mel_destroy(self._h)
+            self._h = C.c_void_p()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def n_mels(self) -> int:
+        return self.cfg.feature_size
+
+    def num_frames(self, num_samples: int) -> int:  # mel.rs:76-82
+        return num_samples // self.cfg.hop_length
+
+    def log_mel_ptr(self, samples_ptr: int, n_chunks: int, out_ptr: int) -> None:
+        st = self.lib.fmd_mel_log_mel(self._h, C.c_void_p(samples_ptr), n_chunks, C.c_void_p(out_ptr))
+        if st != _lib.FMD_OK:
+            raise _lib.FmdError(st, self.lib.fmd_mel_last_error(self._h).decode())
+
+    def log_mel_device(self, windows):
+        """(n_chunks, n_samples) zero-padded windows (host array or device
+        tensor, f32) -> device tensor (n_chunks, n_mels, frames)."""
+        import torch
+
+        if isinstance(windows, torch.Tensor):
+            n, ptr, hold = windows.shape[0], windows.data_ptr(), windows
+        else:
+            hold = np.ascontiguousarray(np.asarray(windows, dtype=np.float32).reshape(-1, self.cfg.n_samples))
+            n, ptr = hold.shape[0], hold.ctypes.data
+        out = torch.empty((n, self.cfg.feature_size, self.cfg.nb_max_frames), dtype=torch.float32,
+                          device=f"cuda:{self.device}")
+        self.log_mel_ptr(ptr, n, out.data_ptr())
+        del hold
+        return out
+
+    def log_mel(self, samples) -> np.ndarray:
+        """`MelFrontend::log_mel` of one window of n_samples samples -> (n_mels, frames)."""
+        return self.log_mel_device(np.asarray(samples, dtype=np.float32)[None])[0].cpu().numpy()
+
+
+def extract_features(waveforms, cfg: FeatureConfig, frontend: MelFrontend, merge_size: int) -> AudioFeatures:
+    """`extract_features` (audio/mod.rs:47-116): plan the 30 s chunks on the host,
+    zero-pad each to the window and run the log-mel frontend on the GPU."""
+    chunks, tokens, mapping, per_audio = plan_chunks([len(w) for w in waveforms], cfg, merge_size)
+    windows = np.zeros((len(chunks), cfg.n_samples), dtype=np.float32)
+    for i, (a, s, e) in enumerate(chunks):
+        windows[i, : e - s] = np.asarray(waveforms[a], dtype=np.float32)[s:e]
+    mel = frontend.log_mel_device(windows)
+    return AudioFeatures(mel, tokens, mapping, per_audio)
+
+
+def mel_filters(cfg: FeatureConfig = FeatureConfig()) -> np.ndarray:
+    """The library's Slaney filterbank (n_mels, n_fft / 2 + 1), host only."""
+    lib = _lib.load()
+    out = np.empty((cfg.feature_size, cfg.n_fft // 2 + 1), dtype=np.float32)
+    st = lib.fmd_mel_filters(C.byref(cfg.to_c()), out.ctypes.data_as(C.POINTER(C.c_float)))
+    if st != _lib.FMD_OK:
+        raise _lib.FmdError(st, "fmd_mel_filters")
+    return out

@@ -118,6 +118,43 @@ int fmd_audio_encode_audio(fmd_audio* h, const void* mel, int32_t mel_dtype, int
  * number of kernels it launched. */
 int fmd_audio_last_timing(const fmd_audio* h, double* device_ms, int64_t* kernels);
 
+/* ---- log-mel frontend ----------------------------------------------------
+ * `MelFrontend` (crates/fmd-core/src/audio/mel.rs:29-133): periodic Hann
+ * window, centred STFT with reflect padding, power spectrum, Slaney mel
+ * filterbank, log10 with a 1e-10 floor, the per-chunk clamp at peak - 8 and
+ * the (v + 4) / 4 rescale. `extract_features` (audio/mod.rs:47-116) runs it
+ * on every zero-padded 30 s chunk; the chunk planning stays on the host. */
+
+typedef struct fmd_mel fmd_mel;
+
+/* `FeatureConfig` (crates/fmd-core/src/config.rs:121-166). */
+typedef struct fmd_feature_config {
+  int32_t feature_size;  /* n_mels: 80                                        */
+  int32_t sampling_rate; /* 16000                                             */
+  int32_t hop_length;    /* 160                                               */
+  int32_t n_fft;         /* 400; n_fft / 2 + 1 <= 256 frequency bins          */
+  int32_t n_samples;     /* 480000 samples per chunk (30 s)                   */
+  int32_t nb_max_frames; /* 3000 = n_samples / hop_length                     */
+} fmd_feature_config;
+
+/* `MelFrontend::new`: the window, the DFT basis and the filterbank on
+ * `device`. Unsupported shapes are FMD_ENOTSUP. On a failure after the handle
+ * was made, `*out` holds it for fmd_mel_last_error; release it with
+ * fmd_mel_destroy. */
+int fmd_mel_create(const fmd_feature_config* cfg, int32_t device, fmd_mel** out);
+int fmd_mel_destroy(fmd_mel* h);
+const char* fmd_mel_last_error(const fmd_mel* h);
+
+/* `MelFrontend::log_mel` of `n_chunks` windows of n_samples f32 samples each
+ * (host or device memory, each already zero-padded to the window as
+ * extract_features does, audio/mod.rs:100-106) -> `out` (device, f32,
+ * n_chunks x feature_size x nb_max_frames), the encoder's mel input. */
+int fmd_mel_log_mel(fmd_mel* h, const float* samples, int32_t n_chunks, float* out);
+
+/* The Slaney filterbank `mel_filter_bank` (mel.rs:183-240) as a dense host
+ * matrix (feature_size x (n_fft / 2 + 1)) f32. Host only. */
+int fmd_mel_filters(const fmd_feature_config* cfg, float* out);
+
 #ifdef __cplusplus
 }
 #endif
