@@ -19,6 +19,15 @@ Tensors stay memory-mapped in their stored dtype (bf16 as uint16 bit
 patterns, f16, f32); the library converts them and, in the int8 precisions,
 quantises the projections from their f32 values (`linear.rs:104-107`).
 `write_safetensors` writes the same format (used by the tests).
+
+`load_audio_checkpoint(directory)` reads the audio tower the same way: the
+Whisper encoder under `model.whisper_encoder` (whisper_encoder.rs:28-41,
+:74-83, :115-131: `conv1`, `conv2`, `embed_positions`,
+`layers.{i}.self_attn.{q,k,v,out}_proj` (k without bias),
+`self_attn_layer_norm`, `fc1`, `fc2`, `final_layer_norm`, `layer_norm`) and the
+adaptor under `model.vq_adaptor` (adaptor.rs:18-36: `layers.0`, `layers.2`, the
+`layers.3` norm), with `AudioConfig` from config.json (`audio_config`,
+`audio_merge_size`, `adaptor_input_dim`, the text width; config.rs:61-90).
 """
 
 from __future__ import annotations
@@ -141,4 +150,57 @@ def load_checkpoint(directory, prefix: str = PREFIX):
         if key in tensors:
             w["lm_head"] = tensors[key]
             break
+    return cfg, w
+
+
+ENCODER_PREFIX = "model.whisper_encoder"
+ADAPTOR_PREFIX = "model.vq_adaptor"
+
+
+def audio_config(directory):
+    """`AudioConfig` of the audio tower from config.json."""
+    from .audio import AudioConfig
+
+    return AudioConfig.from_model_config(json.loads((Path(directory) / "config.json").read_text()))
+
+
+def load_audio_checkpoint(directory, encoder_prefix: str = ENCODER_PREFIX, adaptor_prefix: str = ADAPTOR_PREFIX):
+    """(AudioConfig, weights) of the audio tower, the dictionary `AudioEncoder` takes."""
+    cfg = audio_config(directory)
+    tensors: dict = {}
+    for shard in shard_files(directory):
+        tensors.update(read_safetensors(shard))
+
+    def get(prefix, name, shape):
+        key = f"{prefix}.{name}"
+        if key not in tensors:
+            raise KeyError(f"checkpoint has no tensor {key}")
+        arr = tensors[key]
+        if tuple(arr.shape) != tuple(shape):
+            raise ValueError(f"{key}: shape {tuple(arr.shape)}, expected {tuple(shape)}")
+        return arr
+
+    D, FF, M = cfg.d_model, cfg.encoder_ffn_dim, cfg.num_mel_bins
+    e = lambda name, shape: get(encoder_prefix, name, shape)  # noqa: E731
+    w = {"conv1_w": e("conv1.weight", (D, M, 3)), "conv1_b": e("conv1.bias", (D,)),
+         "conv2_w": e("conv2.weight", (D, D, 3)), "conv2_b": e("conv2.bias", (D,)),
+         "positions": e("embed_positions.weight", (cfg.max_source_positions, D)),
+         "ln_w": e("layer_norm.weight", (D,)), "ln_b": e("layer_norm.bias", (D,)), "layers": []}
+    for i in range(cfg.encoder_layers):
+        p = f"layers.{i}."
+        w["layers"].append({
+            "q_w": e(p + "self_attn.q_proj.weight", (D, D)), "q_b": e(p + "self_attn.q_proj.bias", (D,)),
+            "k_w": e(p + "self_attn.k_proj.weight", (D, D)),
+            "v_w": e(p + "self_attn.v_proj.weight", (D, D)), "v_b": e(p + "self_attn.v_proj.bias", (D,)),
+            "o_w": e(p + "self_attn.out_proj.weight", (D, D)), "o_b": e(p + "self_attn.out_proj.bias", (D,)),
+            "ln1_w": e(p + "self_attn_layer_norm.weight", (D,)), "ln1_b": e(p + "self_attn_layer_norm.bias", (D,)),
+            "fc1_w": e(p + "fc1.weight", (FF, D)), "fc1_b": e(p + "fc1.bias", (FF,)),
+            "fc2_w": e(p + "fc2.weight", (D, FF)), "fc2_b": e(p + "fc2.bias", (D,)),
+            "ln2_w": e(p + "final_layer_norm.weight", (D,)), "ln2_b": e(p + "final_layer_norm.bias", (D,)),
+        })
+    hid, K = cfg.hidden_size, cfg.adaptor_input_dim
+    a = lambda name, shape: get(adaptor_prefix, name, shape)  # noqa: E731
+    w.update({"ad1_w": a("layers.0.weight", (hid, K)), "ad1_b": a("layers.0.bias", (hid,)),
+              "ad2_w": a("layers.2.weight", (hid, hid)), "ad2_b": a("layers.2.bias", (hid,)),
+              "adn_w": a("layers.3.weight", (hid,)), "adn_b": a("layers.3.bias", (hid,))})
     return cfg, w

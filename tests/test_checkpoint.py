@@ -112,3 +112,77 @@ def test_interop_with_the_safetensors_package(tmp_path):
     st.save_file({"a": a, "b": b}, str(tmp_path / "theirs.safetensors"))
     mine = ckpt.read_safetensors(tmp_path / "theirs.safetensors")
     assert np.array_equal(mine["a"], a) and np.array_equal(mine["b"], b)
+
+
+# ---- the audio tower (whisper_encoder.rs:28-41, :74-83, :115-131; adaptor.rs:18-36) ----
+_ENC_LAYER = {"q_w": "self_attn.q_proj.weight", "q_b": "self_attn.q_proj.bias", "k_w": "self_attn.k_proj.weight",
+              "v_w": "self_attn.v_proj.weight", "v_b": "self_attn.v_proj.bias", "o_w": "self_attn.out_proj.weight",
+              "o_b": "self_attn.out_proj.bias", "ln1_w": "self_attn_layer_norm.weight",
+              "ln1_b": "self_attn_layer_norm.bias", "fc1_w": "fc1.weight", "fc1_b": "fc1.bias", "fc2_w": "fc2.weight",
+              "fc2_b": "fc2.bias", "ln2_w": "final_layer_norm.weight", "ln2_b": "final_layer_norm.bias"}
+_ENC_TOP = {"conv1_w": "conv1.weight", "conv1_b": "conv1.bias", "conv2_w": "conv2.weight", "conv2_b": "conv2.bias",
+            "positions": "embed_positions.weight", "ln_w": "layer_norm.weight", "ln_b": "layer_norm.bias"}
+_ADAPTOR = {"ad1_w": "layers.0.weight", "ad1_b": "layers.0.bias", "ad2_w": "layers.2.weight",
+            "ad2_b": "layers.2.bias", "adn_w": "layers.3.weight", "adn_b": "layers.3.bias"}
+
+
+def audio_tensors(w):
+    out = {f"model.whisper_encoder.{n}": w[k] for k, n in _ENC_TOP.items()}
+    for i, lw in enumerate(w["layers"]):
+        out.update({f"model.whisper_encoder.layers.{i}.{n}": lw[k] for k, n in _ENC_LAYER.items()})
+    out.update({f"model.vq_adaptor.{n}": w[k] for k, n in _ADAPTOR.items()})
+    return out
+
+
+def write_audio_checkpoint(d, acfg, w, bf16=True):
+    """A Moss-style checkpoint directory holding the audio tower (matrices as
+    bf16 bits when `bf16`) and a config.json with `audio_config`."""
+    tensors = {k: (syn.f32_to_bf16_bits(np.asarray(v, np.float32)) if bf16 and np.ndim(v) >= 2
+                   else np.asarray(v, np.float32)) for k, v in audio_tensors(w).items()}
+    doc = {"audio_config": {k: getattr(acfg, k) for k in ("num_mel_bins", "d_model", "encoder_layers",
+                                                           "encoder_attention_heads", "encoder_ffn_dim",
+                                                           "max_source_positions")},
+           "text_config": {"hidden_size": acfg.hidden_size, "rms_norm_eps": acfg.adaptor_norm_eps},
+           "audio_merge_size": acfg.audio_merge_size, "adaptor_input_dim": acfg.adaptor_input_dim,
+           "audio_token_id": 151654}
+    (d / "config.json").write_text(json.dumps(doc))
+    ckpt.write_safetensors(d / "model.safetensors", tensors)
+    return tensors
+
+
+def _small_audio():
+    from conftest import PKG
+    from oracle.whisper_ref import AudioConfig as RefConfig
+    from oracle.whisper_ref import random_audio_weights
+
+    acfg = PKG.AudioConfig(d_model=256, encoder_layers=2, encoder_attention_heads=4, encoder_ffn_dim=512,
+                           max_source_positions=100, adaptor_input_dim=1024, hidden_size=256)
+    return acfg, random_audio_weights(RefConfig(**acfg.oracle_kwargs()), 91)
+
+
+def test_audio_checkpoint_round_trip(tmp_path):
+    acfg, w = _small_audio()
+    written = write_audio_checkpoint(tmp_path, acfg, w)
+    cfg, got = ckpt.load_audio_checkpoint(tmp_path)
+    assert cfg == acfg
+    for k in _ENC_TOP:
+        assert np.array_equal(np.asarray(got[k]), written[f"model.whisper_encoder.{_ENC_TOP[k]}"]), k
+    for i in range(acfg.encoder_layers):
+        for k, n in _ENC_LAYER.items():
+            assert np.array_equal(np.asarray(got["layers"][i][k]),
+                                  written[f"model.whisper_encoder.layers.{i}.{n}"]), (i, k)
+    for k, n in _ADAPTOR.items():
+        assert np.array_equal(np.asarray(got[k]), written[f"model.vq_adaptor.{n}"]), k
+
+
+def test_audio_checkpoint_errors(tmp_path):
+    acfg, w = _small_audio()
+    written = write_audio_checkpoint(tmp_path, acfg, w)
+    written.pop("model.whisper_encoder.layers.1.fc2.bias")
+    ckpt.write_safetensors(tmp_path / "model.safetensors", written)
+    with pytest.raises(KeyError, match="layers.1.fc2.bias"):
+        ckpt.load_audio_checkpoint(tmp_path)
+    written["model.whisper_encoder.layers.1.fc2.bias"] = np.zeros(7, np.float32)
+    ckpt.write_safetensors(tmp_path / "model.safetensors", written)
+    with pytest.raises(ValueError, match="shape"):
+        ckpt.load_audio_checkpoint(tmp_path)

@@ -88,3 +88,30 @@ def test_decoder_from_checkpoint_equals_in_memory(tmp_path, prec):
             outs.append(res)
     for a, b in zip(*outs):
         assert np.array_equal(a, b)
+
+
+def test_audio_encoder_from_checkpoint_equals_in_memory(tmp_path):
+    """The audio tower loaded from a checkpoint (bf16 matrices, f32 vectors,
+    the reference's tensor names) gives the same frames and embeddings, bit for
+    bit, as the same values handed over in memory."""
+    import torch
+
+    from oracle.whisper_ref import round_weights
+    from test_checkpoint import _small_audio, write_audio_checkpoint
+
+    acfg, w = _small_audio()
+    write_audio_checkpoint(tmp_path, acfg, w)
+    cfg, wc = ckpt.load_audio_checkpoint(tmp_path)
+    wr = round_weights(w, "bf16")
+    for k in ("conv1_b", "conv2_b", "ln_w", "ln_b", "ad1_b", "ad2_b", "adn_w", "adn_b"):
+        wr[k] = np.asarray(w[k], np.float32)  # vectors stay f32 in the checkpoint
+    for lw, src in zip(wr["layers"], w["layers"]):
+        for k in ("q_b", "v_b", "o_b", "ln1_w", "ln1_b", "fc1_b", "fc2_b", "ln2_w", "ln2_b"):
+            lw[k] = np.asarray(src[k], np.float32)
+    mel = np.random.default_rng(92).standard_normal((2, 80, cfg.mel_frames), dtype=np.float32)
+    with PKG.AudioEncoder(cfg, wc, "bf16", max_batch=2) as a, PKG.AudioEncoder(cfg, wr, "bf16", max_batch=2) as b:
+        fa, fb = a.forward_device(mel), b.forward_device(mel)
+        assert torch.equal(fa, fb)
+        ea, _ = a.encode_audio_device(mel, [25, 9], [0, 1], 2)
+        eb, _ = b.encode_audio_device(mel, [25, 9], [0, 1], 2)
+        assert torch.equal(ea, eb)
