@@ -108,3 +108,16 @@ def test_library_filterbank_matches_the_oracle_and_rejects_bad_shapes():
     assert lib.fmd_mel_create(C.byref(bad.to_c()), 0, C.byref(h)) == PKG._lib.FMD_EINVAL and not h
     wide = PKG.FeatureConfig(n_fft=1024)  # 513 frequency bins: more than one CTA's threads
     assert lib.fmd_mel_create(C.byref(wide.to_c()), 0, C.byref(h)) == PKG._lib.FMD_ENOTSUP and not h
+
+
+def test_chunk_planning_matches_the_oracle_on_random_lengths():
+    rng = np.random.default_rng(7)
+    cfg_o, cfg_p = M.FeatureConfig(), PKG.FeatureConfig()
+    for _ in range(200):
+        lengths = [int(x) for x in rng.integers(0, 5 * 480_000, size=int(rng.integers(1, 6)))]
+        for merge in (1, 2, 4):
+            assert PKG.audio.plan_chunks(lengths, cfg_p, merge) == M.plan_chunks(lengths, cfg_o, merge)
+            _, tokens, _, per_audio = M.plan_chunks(lengths, cfg_o, merge)
+            # every full window is the reference's 480000 / (160 x 2 x merge) tokens
+            assert max(tokens) <= 480_000 // (160 * 2 * merge) + 1
+            assert sum(per_audio) == sum(tokens)
