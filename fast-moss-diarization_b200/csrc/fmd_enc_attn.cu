@@ -19,8 +19,7 @@
 //    O += P_j V_j (M 128, N 64 dims, K 64 keys; V read MN-major from its tile);
 //  * warps 2-5 (one thread per query row = tensor-memory lane): online softmax
 //    in the exp2 domain with a lazily moved reference maximum (O is rescaled in
-//    tensor memory only when a row maximum exceeds it by more than 2^8), a third
-//    of the exponentials on the FMA pipe and the rest on MUFU; keys
+//    tensor memory only when a row maximum exceeds it by more than 2^8); keys
 //    past the chunk end are masked; P_j goes as 16-bit values into a
 //    double-buffered 128-byte-swizzled shared tile (the A operand of PV). At the
 //    end each thread divides its row of O by the row sum and stores ctx.
@@ -67,20 +66,6 @@ FMD_DEV float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
-}
-
-// 2^x on the FMA pipe, to take part of the exponentials off the MUFU pipe:
-// x = n + r with n = rint(x) (the 1.5 x 2^23 rounding trick) and r in
-// [-0.5, 0.5]; 2^r by a degree-3 polynomial fitted here for minimax relative
-// error on [-0.5, 0.5] (Lawson's iteratively reweighted least squares; max
-// relative error 8.4e-5, far below the 16-bit P it feeds); 2^n by adding n to
-// the exponent field. Exactly 0 below 2^-125.
-FMD_DEV float ex2_fma(float x) {
-  const float t = x + 12582912.f;
-  const float r = x - (t - 12582912.f);
-  const float p = fmaf(fmaf(fmaf(0.05521305f, r, 0.24271414f), r, 0.69326216f), r, 0.9999196f);
-  const float y = __int_as_float(__float_as_int(p) + ((__float_as_int(t) - 0x4B400000) << 23));
-  return x < -125.f ? 0.f : y;
 }
 
 FMD_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
@@ -272,8 +257,7 @@ __global__ void __launch_bounds__(192, 2)
       float p4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c = 0; c < 64; ++c) {
-        // one in three on the FMA pipe balances it against the MUFU pipe
-        s[c] = (c % 3 == 2) ? ex2_fma(s[c] - m_ref) : ex2(s[c] - m_ref);
+        s[c] = ex2(s[c] - m_ref);
         p4[c & 3] += s[c];
       }
       l += (p4[0] + p4[1]) + (p4[2] + p4[3]);
