@@ -70,11 +70,17 @@ struct fmd_audio {
   alignas(64) CUtensorMap conv1_m, conv2_m, ad1_m, ad2_m;
   // work buffers for max_batch chunks (bufA/B/C are shared by the front convolutions and the layers)
   int max_batch = 0;
-  void* mel_stage = nullptr;
+  // host mel is staged batch by batch through two pinned + two device slots on
+  // a copy stream, so batch k + 1 is copied while batch k computes
+  void* mel_dev[2] = {nullptr, nullptr};
+  void* pinned[2] = {nullptr, nullptr};
   size_t mel_stage_bytes = 0;
+  cudaStream_t copy_stream = nullptr;
+  cudaEvent_t ev_copied[2] = {nullptr, nullptr}, ev_consumed[2] = {nullptr, nullptr};
+  int2* rowmap_all = nullptr;  // the adaptor row maps of every batch of a call
+  size_t rowmap_cap = 0;
   void *bufA = nullptr, *bufB = nullptr, *bufC = nullptr, *hbuf = nullptr, *enc = nullptr, *ah = nullptr;
   float *x = nullptr, *af = nullptr;
-  int2* rowmap = nullptr;
   int* d_status = nullptr;
   void* stage = nullptr;  // weight upload staging
   size_t stage_bytes = 0;
@@ -237,7 +243,7 @@ int run_encoder(fmd_audio* h, const void* mel, int mel_dt, int n, void* out, int
 
 // Adaptor over the frames of n chunks in h->enc; rowmap (device) places
 // `rows` kept tokens in `out`.
-int run_adaptor(fmd_audio* h, int n, int rows, void* out, int64_t* kernels) {
+int run_adaptor(fmd_audio* h, int n, int rows, const int2* rowmap, void* out, int64_t* kernels) {
   const int Mg = n * h->Tp / h->merge, hid = h->hid, K = h->merge * h->D;
   alignas(64) CUtensorMap e_m, ah_m;
   int rc;
@@ -245,23 +251,40 @@ int run_adaptor(fmd_audio* h, int n, int rows, void* out, int64_t* kernels) {
   gemm(h, kEpiSilu, e_m, h->ad1_m, Mg, hid, K, epi_args(h->ah, h->ad1_b), kernels);
   gemm(h, kEpiF32, ah_m, h->ad2_m, Mg, hid, hid, epi_args(h->af, h->ad2_b), kernels);
   if (rows > 0) {
-    launch_layernorm(h->at, h->af, h->rowmap, rows, hid, h->adn_w, h->adn_b, h->cfg.adaptor_norm_eps, out, h->stream);
+    launch_layernorm(h->at, h->af, rowmap, rows, hid, h->adn_w, h->adn_b, h->cfg.adaptor_norm_eps, out, h->stream);
     ++*kernels;
   }
   ACK(cudaGetLastError());
   return FMD_OK;
 }
 
-// Chunks [start, start + n) of `mel` to a device pointer the im2col kernel can read.
-int stage_mel(fmd_audio* h, const void* mel, int32_t mel_dt, bool dev, int start, int n, const void** out) {
+// Chunks [start, start + n) of `mel` (encoder batch `batch` of the call) to a
+// device pointer the im2col kernel can read. Host mel goes through slot
+// batch % 2: wait until the slot's previous copy has landed, fill the pinned
+// buffer, copy on the copy stream once the device slot's previous reader has
+// run, and make the compute stream wait for the copy.
+int stage_mel(fmd_audio* h, const void* mel, int32_t mel_dt, bool dev, int start, int n, int batch,
+              const void** out) {
   const size_t per = (size_t)h->n_mels * h->F * dt_size(mel_dt);
   const uint8_t* src = static_cast<const uint8_t*>(mel) + (size_t)start * per;
   if (dev) {
     *out = src;
     return FMD_OK;
   }
-  ACK(cudaMemcpyAsync(h->mel_stage, src, (size_t)n * per, cudaMemcpyHostToDevice, h->stream));
-  *out = h->mel_stage;
+  const int s = batch & 1;
+  ACK(cudaEventSynchronize(h->ev_copied[s]));
+  std::memcpy(h->pinned[s], src, (size_t)n * per);
+  ACK(cudaStreamWaitEvent(h->copy_stream, h->ev_consumed[s], 0));
+  ACK(cudaMemcpyAsync(h->mel_dev[s], h->pinned[s], (size_t)n * per, cudaMemcpyHostToDevice, h->copy_stream));
+  ACK(cudaEventRecord(h->ev_copied[s], h->copy_stream));
+  ACK(cudaStreamWaitEvent(h->stream, h->ev_copied[s], 0));
+  *out = h->mel_dev[s];
+  return FMD_OK;
+}
+
+// After the batch that read slot batch % 2 has been launched.
+int release_mel(fmd_audio* h, bool dev, int batch) {
+  if (!dev) ACK(cudaEventRecord(h->ev_consumed[batch & 1], h->stream));
   return FMD_OK;
 }
 
@@ -337,8 +360,13 @@ int fmd_audio_create(const fmd_audio_config* cfg, const fmd_audio_weights* w, in
   ACK(cudaSetDevice(device));
   ACK(init_enc_kernels());
   ACK(cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking));
+  ACK(cudaStreamCreateWithFlags(&h->copy_stream, cudaStreamNonBlocking));
   ACK(cudaEventCreate(&h->ev0));
   ACK(cudaEventCreate(&h->ev1));
+  for (int s = 0; s < 2; ++s) {
+    ACK(cudaEventCreateWithFlags(&h->ev_copied[s], cudaEventDisableTiming));
+    ACK(cudaEventCreateWithFlags(&h->ev_consumed[s], cudaEventDisableTiming));
+  }
   int rc = encoder_fn(h);
   if (rc) return rc;
 
@@ -430,13 +458,14 @@ int fmd_audio_create(const fmd_audio_config* cfg, const fmd_audio_weights* w, in
               {reinterpret_cast<void**>(&h->x), rows * D * 4},
               {&h->ah, groups * hid * 2},
               {reinterpret_cast<void**>(&h->af), groups * hid * 4},
-              {reinterpret_cast<void**>(&h->rowmap), groups * sizeof(int2)},
               {reinterpret_cast<void**>(&h->d_status), 16},
-              {&h->mel_stage, h->mel_stage_bytes}};
+              {&h->mel_dev[0], h->mel_stage_bytes},
+              {&h->mel_dev[1], h->mel_stage_bytes}};
   for (B& b : bufs) {
     if ((rc = alloc(h, b.n, b.p, &h->work_bytes))) return rc;
     ACK(cudaMemsetAsync(*b.p, 0, b.n, h->stream));
   }
+  for (int s = 0; s < 2; ++s) ACK(cudaHostAlloc(&h->pinned[s], h->mel_stage_bytes, cudaHostAllocDefault));
   ACK(cudaStreamSynchronize(h->stream));
   return FMD_OK;
 }
@@ -445,9 +474,17 @@ int fmd_audio_destroy(fmd_audio* h) {
   if (h == nullptr) return FMD_OK;
   cudaSetDevice(h->device);
   if (h->stream) cudaStreamSynchronize(h->stream);
+  if (h->copy_stream) cudaStreamSynchronize(h->copy_stream);
   for (void* p : h->allocs) cudaFree(p);
+  if (h->rowmap_all) cudaFree(h->rowmap_all);
+  for (int s = 0; s < 2; ++s) {
+    if (h->pinned[s]) cudaFreeHost(h->pinned[s]);
+    if (h->ev_copied[s]) cudaEventDestroy(h->ev_copied[s]);
+    if (h->ev_consumed[s]) cudaEventDestroy(h->ev_consumed[s]);
+  }
   if (h->ev0) cudaEventDestroy(h->ev0);
   if (h->ev1) cudaEventDestroy(h->ev1);
+  if (h->copy_stream) cudaStreamDestroy(h->copy_stream);
   if (h->stream) cudaStreamDestroy(h->stream);
   delete h;
   return FMD_OK;
@@ -480,12 +517,13 @@ int fmd_audio_encode(fmd_audio* h, const void* mel, int32_t mel_dtype, int32_t n
     return fail(h, FMD_EINVAL, "frames_out must be 16-byte aligned device memory");
   if ((rc = begin(h))) return rc;
   const size_t per_chunk = (size_t)h->Tp * h->D * 2;
-  for (int start = 0; start < n_chunks; start += h->max_batch) {
+  for (int start = 0, batch = 0; start < n_chunks; start += h->max_batch, ++batch) {
     const int n = std::min(h->max_batch, n_chunks - start);
     const void* src = nullptr;
-    if ((rc = stage_mel(h, mel, mel_dtype, dev, start, n, &src))) return rc;
+    if ((rc = stage_mel(h, mel, mel_dtype, dev, start, n, batch, &src))) return rc;
     void* out = static_cast<uint8_t*>(frames_out) + (size_t)start * per_chunk;
     if ((rc = run_encoder(h, src, mel_dtype, n, out, &h->last_kernels))) return rc;
+    if ((rc = release_mel(h, dev, batch))) return rc;
   }
   return finish(h);
 }
@@ -523,26 +561,41 @@ int fmd_audio_encode_audio(fmd_audio* h, const void* mel, int32_t mel_dtype, int
     return fail(h, FMD_EINVAL, "out must be 16-byte aligned device memory");
 
   const int eb = std::min(std::max(encoder_batch, 1), h->max_batch);
+  // the adaptor row maps of every batch, uploaded once: entry {row of the
+  // batch's merged frames, output row}
   std::vector<int64_t> next(audio_offsets, audio_offsets + num_audios);
   std::vector<int2> map;
-  if ((rc = begin(h))) return rc;
+  std::vector<size_t> batch_at;
   for (int start = 0; start < n_chunks; start += eb) {
+    batch_at.push_back(map.size());
     const int n = std::min(eb, n_chunks - start);
-    const void* src = nullptr;
-    if ((rc = stage_mel(h, mel, mel_dtype, dev, start, n, &src))) return rc;
-    if ((rc = run_encoder(h, src, mel_dtype, n, h->enc, &h->last_kernels))) return rc;
-    map.clear();
     for (int b = 0; b < n; ++b) {
       const int g = start + b, a = chunk_mapping[g];
       const int keep = std::min(chunk_token_lengths[g], per_chunk);
       for (int j = 0; j < keep; ++j) map.push_back(make_int2(b * per_chunk + j, (int)(next[a] + j)));
       next[a] += keep;
     }
-    if (!map.empty())
-      ACK(cudaMemcpyAsync(h->rowmap, map.data(), map.size() * sizeof(int2), cudaMemcpyHostToDevice, h->stream));
-    if ((rc = run_adaptor(h, n, (int)map.size(), out, &h->last_kernels))) return rc;
-    // the row map is rewritten by the next batch: keep the host copy alive until it is consumed
+  }
+  batch_at.push_back(map.size());
+  if ((rc = begin(h))) return rc;
+  if (map.size() > h->rowmap_cap) {
     ACK(cudaStreamSynchronize(h->stream));
+    if (h->rowmap_all) cudaFree(h->rowmap_all);
+    h->rowmap_all = nullptr;
+    h->rowmap_cap = 0;
+    ACK(cudaMalloc(&h->rowmap_all, map.size() * sizeof(int2)));
+    h->rowmap_cap = map.size();
+  }
+  if (!map.empty())
+    ACK(cudaMemcpyAsync(h->rowmap_all, map.data(), map.size() * sizeof(int2), cudaMemcpyHostToDevice, h->stream));
+  for (int start = 0, batch = 0; start < n_chunks; start += eb, ++batch) {
+    const int n = std::min(eb, n_chunks - start);
+    const void* src = nullptr;
+    if ((rc = stage_mel(h, mel, mel_dtype, dev, start, n, batch, &src))) return rc;
+    if ((rc = run_encoder(h, src, mel_dtype, n, h->enc, &h->last_kernels))) return rc;
+    if ((rc = release_mel(h, dev, batch))) return rc;
+    const int rows = (int)(batch_at[batch + 1] - batch_at[batch]);
+    if ((rc = run_adaptor(h, n, rows, h->rowmap_all + batch_at[batch], out, &h->last_kernels))) return rc;
   }
   return finish(h);
 }
