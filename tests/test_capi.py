@@ -50,3 +50,22 @@ def test_host_quantiser_matches_the_oracle_bit_for_bit():
     st = lib.fmd_q8_0_quantize(w.ctypes.data_as(C.POINTER(C.c_float)), 64, 256, blocks.ctypes.data)
     assert st == 0
     assert np.array_equal(blocks, q8_0.to_blocks(*q8_0.quantize(w)))
+
+
+def test_headers_are_plain_c_and_cxx(tmp_path):
+    """Every public header compiles as C99 (what a cgo / bindgen / ctypes user
+    parses) and as C++17, on its own and together."""
+    import shutil
+    import subprocess
+
+    inc = ROOT / "include"
+    headers = sorted(inc.glob("*.h"))
+    src = tmp_path / "all.c"
+    src.write_text("".join(f'#include "{h.name}"\n' for h in headers) + "int main(void) { return 0; }\n")
+    for cc, std, lang in (("gcc", "-std=c99", "c"), ("g++", "-std=c++17", "c++")):
+        if shutil.which(cc) is None:
+            continue
+        for f in [*headers, src]:
+            r = subprocess.run([cc, std, "-Wall", "-Wextra", "-Werror", "-pedantic", "-fsyntax-only", "-x", lang,
+                                "-I", str(inc), str(f)], capture_output=True, text=True)
+            assert r.returncode == 0, f"{cc} {f.name}:\n{r.stderr}"
