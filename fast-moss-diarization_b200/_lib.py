@@ -42,7 +42,7 @@ EXPORTS = [
     "fmd_generate", "fmd_debug_weight", "fmd_debug_kv", "fmd_q8_0_quantize", "fmd_q8_0_quantize_device", "fmd_greedy_pick_noalloc",
     # include/fmd_audio.h
     "fmd_audio_create", "fmd_audio_destroy", "fmd_audio_last_error", "fmd_audio_memory_bytes", "fmd_audio_encode",
-    "fmd_audio_encode_audio", "fmd_audio_last_timing", "fmd_mel_create", "fmd_mel_destroy", "fmd_mel_last_error",
+    "fmd_audio_encode_audio", "fmd_audio_token_offsets", "fmd_audio_last_timing", "fmd_mel_create", "fmd_mel_destroy", "fmd_mel_last_error",
     "fmd_mel_log_mel", "fmd_mel_filters",
 ]
 
@@ -173,6 +173,7 @@ def load() -> C.CDLL:
         "fmd_audio_memory_bytes": (C.c_int, [P, C.POINTER(I64), C.POINTER(I64)]),
         "fmd_audio_encode": (C.c_int, [P, P, I32, I32, P]),
         "fmd_audio_encode_audio": (C.c_int, [P, P, I32, I32, IP, IP, I32, I32, P, C.POINTER(I64)]),
+        "fmd_audio_token_offsets": (C.c_int, [C.POINTER(AudioConfig), I32, IP, IP, I32, C.POINTER(I64)]),
         "fmd_audio_last_timing": (C.c_int, [P, C.POINTER(C.c_double), C.POINTER(I64)]),
         "fmd_mel_create": (C.c_int, [C.POINTER(FeatureConfig), I32, C.POINTER(P)]),
         "fmd_mel_destroy": (C.c_int, [P]),

@@ -238,6 +238,24 @@ class AudioEncoder:
         return w.value, s.value
 
 
+def token_offsets(cfg: AudioConfig, chunk_token_lengths, chunk_mapping, num_audios: int) -> np.ndarray:
+    """First output row of every audio in `encode_audio`'s output
+    (`fmd_audio_token_offsets`, host only; num_audios + 1 entries)."""
+    lib = _lib.load()
+    tl = np.ascontiguousarray(np.asarray(chunk_token_lengths, dtype=np.int32).reshape(-1))
+    cm = np.ascontiguousarray(np.asarray(chunk_mapping, dtype=np.int32).reshape(-1))
+    if tl.size != cm.size:
+        raise ValueError("chunk_token_lengths and chunk_mapping differ in length")
+    off = np.zeros(num_audios + 1, dtype=np.int64)
+    IP = C.POINTER(C.c_int32)
+    st = lib.fmd_audio_token_offsets(C.byref(cfg.to_c()), tl.size, tl.ctypes.data_as(IP), cm.ctypes.data_as(IP),
+                                     num_audios, off.ctypes.data_as(C.POINTER(C.c_int64)))
+    if st != _lib.FMD_OK:
+        raise _lib.FmdError(st, "fmd_audio_token_offsets: bad chunk layout (an audio without chunks, a mapping "
+                                "out of range or a negative token count)")
+    return off
+
+
 def encoder_flops(cfg: AudioConfig, n_chunks: int) -> float:
     """Multiply-add FLOPs (x2) of one encoder pass + adaptor over n chunks."""
     D, FF, Tp, F = cfg.d_model, cfg.encoder_ffn_dim, cfg.max_source_positions, cfg.mel_frames

@@ -298,6 +298,41 @@ int check_mel(fmd_audio* h, const void* mel, int32_t mel_dt, int32_t n_chunks, b
   return FMD_OK;
 }
 
+// Output rows of every audio (fmd_audio_token_offsets); `err` gets the reason of a failure.
+int token_offsets(int per_chunk, int32_t n_chunks, const int32_t* tokens, const int32_t* mapping,
+                  int32_t num_audios, int64_t* offsets, std::string* err) {
+  if (num_audios < 0 || offsets == nullptr || n_chunks < 0) {
+    *err = "bad n_chunks, num_audios or audio_offsets";
+    return FMD_EINVAL;
+  }
+  if (n_chunks > 0 && (tokens == nullptr || mapping == nullptr)) {
+    *err = "chunk_token_lengths / chunk_mapping is NULL";
+    return FMD_EINVAL;
+  }
+  std::vector<int64_t> count(num_audios, 0), chunks(num_audios, 0);
+  for (int i = 0; i < n_chunks; ++i) {
+    if (mapping[i] < 0 || mapping[i] >= num_audios) {
+      *err = "chunk_mapping[" + std::to_string(i) + "] is out of range";
+      return FMD_EINVAL;
+    }
+    if (tokens[i] < 0) {
+      *err = "negative chunk_token_lengths";
+      return FMD_EINVAL;
+    }
+    count[mapping[i]] += std::min(tokens[i], per_chunk);
+    ++chunks[mapping[i]];
+  }
+  offsets[0] = 0;
+  for (int a = 0; a < num_audios; ++a) {
+    if (chunks[a] == 0) {
+      *err = "audio " + std::to_string(a) + " has no chunks";
+      return FMD_EINVAL;
+    }
+    offsets[a + 1] = offsets[a] + count[a];
+  }
+  return FMD_OK;
+}
+
 int begin(fmd_audio* h) {
   ACK(cudaSetDevice(h->device));
   ACK(cudaMemsetAsync(h->d_status, 0, sizeof(int), h->stream));
@@ -499,6 +534,14 @@ int fmd_audio_memory_bytes(const fmd_audio* h, int64_t* weights, int64_t* worksp
   return FMD_OK;
 }
 
+int fmd_audio_token_offsets(const fmd_audio_config* cfg, int32_t n_chunks, const int32_t* chunk_token_lengths,
+                            const int32_t* chunk_mapping, int32_t num_audios, int64_t* audio_offsets) {
+  if (cfg == nullptr || cfg->audio_merge_size < 1 || cfg->max_source_positions < 1) return FMD_EINVAL;
+  std::string err;
+  return token_offsets(cfg->max_source_positions / cfg->audio_merge_size, n_chunks, chunk_token_lengths,
+                       chunk_mapping, num_audios, audio_offsets, &err);
+}
+
 int fmd_audio_last_timing(const fmd_audio* h, double* device_ms, int64_t* kernels) {
   if (h == nullptr) return FMD_EINVAL;
   if (device_ms) *device_ms = h->last_ms;
@@ -533,26 +576,12 @@ int fmd_audio_encode_audio(fmd_audio* h, const void* mel, int32_t mel_dtype, int
                            int32_t encoder_batch, void* out, int64_t* audio_offsets) {
   if (h == nullptr) return FMD_EINVAL;
   h->err.clear();
-  if (num_audios < 0 || audio_offsets == nullptr) return fail(h, FMD_EINVAL, "bad num_audios or audio_offsets");
-  if (n_chunks > 0 && (chunk_token_lengths == nullptr || chunk_mapping == nullptr))
-    return fail(h, FMD_EINVAL, "chunk_token_lengths / chunk_mapping is NULL");
-  if (n_chunks < 0) return fail(h, FMD_EINVAL, "n_chunks < 0");
   // Rows kept per chunk: tokens * merge frames, at most the chunk's frames
   // (mod.rs:110-116), merged back into min(tokens, Tp / merge) rows.
   const int per_chunk = h->Tp / h->merge;
-  std::vector<int64_t> count(num_audios, 0), chunks(num_audios, 0);
-  for (int i = 0; i < n_chunks; ++i) {
-    if (chunk_mapping[i] < 0 || chunk_mapping[i] >= num_audios)
-      return fail(h, FMD_EINVAL, "chunk_mapping[" + std::to_string(i) + "] is out of range");
-    if (chunk_token_lengths[i] < 0) return fail(h, FMD_EINVAL, "negative chunk_token_lengths");
-    count[chunk_mapping[i]] += std::min(chunk_token_lengths[i], per_chunk);
-    ++chunks[chunk_mapping[i]];
-  }
-  audio_offsets[0] = 0;
-  for (int a = 0; a < num_audios; ++a) {
-    if (chunks[a] == 0) return fail(h, FMD_EINVAL, "audio " + std::to_string(a) + " has no chunks");
-    audio_offsets[a + 1] = audio_offsets[a] + count[a];
-  }
+  int rc0 = token_offsets(per_chunk, n_chunks, chunk_token_lengths, chunk_mapping, num_audios, audio_offsets,
+                          &h->err);
+  if (rc0) return rc0;
   if (out == nullptr || n_chunks == 0) return FMD_OK;
   bool dev = false;
   int rc = check_mel(h, mel, mel_dtype, n_chunks, &dev);

@@ -114,6 +114,15 @@ int fmd_audio_encode_audio(fmd_audio* h, const void* mel, int32_t mel_dtype, int
                            const int32_t* chunk_token_lengths, const int32_t* chunk_mapping, int32_t num_audios,
                            int32_t encoder_batch, void* out, int64_t* audio_offsets);
 
+/* The output layout of fmd_audio_encode_audio without a handle or a device:
+ * audio a owns rows [offsets[a], offsets[a+1]) where each chunk i of audio
+ * chunk_mapping[i] contributes min(chunk_token_lengths[i],
+ * max_source_positions / audio_merge_size) rows, in chunk order
+ * (mod.rs:108-125). `audio_offsets` has num_audios + 1 entries. Same errors as
+ * fmd_audio_encode_audio (FMD_EINVAL for an audio without chunks). Host only. */
+int fmd_audio_token_offsets(const fmd_audio_config* cfg, int32_t n_chunks, const int32_t* chunk_token_lengths,
+                            const int32_t* chunk_mapping, int32_t num_audios, int64_t* audio_offsets);
+
 /* CUDA-event time (ms) of the device work of the last encode call, and the
  * number of kernels it launched. */
 int fmd_audio_last_timing(const fmd_audio* h, double* device_ms, int64_t* kernels);

@@ -126,3 +126,26 @@ def test_package_config_matches_the_oracle_config():
            "text_config": {"hidden_size": 1024, "rms_norm_eps": 1e-6}, "audio_merge_size": 4,
            "adaptor_input_dim": 4096}
     assert PKG.AudioConfig.from_model_config(doc) == PKG.AudioConfig()
+
+
+def test_token_offsets_match_the_oracle_layout():
+    """The library's host-only layout of encode_audio's output
+    (fmd_audio_token_offsets) against the row counts of the oracle's
+    encode_audio (trim to min(tokens, frames / merge), join in chunk order)."""
+    cfg = _small_cfg()
+    ref = WhisperRef(cfg, random_audio_weights(cfg, 5))
+    mel = np.random.default_rng(6).standard_normal((6, 80, 32), dtype=np.float32)
+    pcfg = PKG.AudioConfig(**cfg.__dict__)
+    rng = np.random.default_rng(8)
+    for _ in range(5):
+        tokens = [int(t) for t in rng.integers(0, 7, 6)]  # up to past the 4 rows a chunk holds
+        mapping = sorted(int(m) for m in rng.integers(0, 3, 6))
+        mapping[:3] = [0, 1, 2]
+        mapping.sort()
+        out = ref.encode_audio(mel, tokens, mapping, 3, encoder_batch=4)
+        off = PKG.audio.token_offsets(pcfg, tokens, mapping, 3)
+        assert np.diff(off).tolist() == [o.shape[0] for o in out]
+    with pytest.raises(PKG.FmdError):
+        PKG.audio.token_offsets(pcfg, [1, 2], [0, 0], 2)  # audio 1 has no chunks
+    with pytest.raises(PKG.FmdError):
+        PKG.audio.token_offsets(pcfg, [1, -2], [0, 1], 2)
