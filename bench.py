@@ -539,9 +539,17 @@ def main():
         el_max = dist.reduce(el, "max")
         h2d = wl.arena.nbytes + 24 * len(wl.prompt_lens)
         d2h = 4 * len(wl.prompt_lens) * int(np.max(wl.max_new)) + 8 * len(wl.prompt_lens)
+        # audio transcribed: each prompt's N(0,1) span stands for audio at the
+        # reference's 12.5 audio tokens per second (16 kHz / (hop 160 x encoder
+        # stride 2 x merge 4), config.rs:210-223)
+        audio_s = dist.reduce(float(sum(round(0.75 * int(n)) for n in wl.prompt_lens)) / 12.5, "sum")
         e2e = {"value": tot / el_max, "unit": UNIT, "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
                "step": "whole queue through fmd_generate (pinned host arena in, tokens out)",
-               "seconds": el_max, "tokens": int(tot)}
+               "seconds": el_max, "tokens": int(tot),
+               "audio_seconds_per_s": audio_s / el_max,
+               "audio_seconds_note": "decoder only: audio-span rows of the queue's prompts / 12.5 tokens per s, "
+                                     "over the whole-queue wall time; the audio tower's own rate is "
+                                     "bench.py --workload encoder"}
 
     cpu = None
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu:
