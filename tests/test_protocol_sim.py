@@ -1,0 +1,329 @@
+"""CPU simulation of the mbarrier protocols of the audio-tower kernels.
+
+A discrete-event model of `k_enc_gemm` (fmd_enc_gemm.cu) and `k_enc_attn`
+(fmd_enc_attn.cu): every role (TMA producer, MMA issuer, epilogue / softmax
+warps) runs as a coroutine, asynchronous work (TMA copies landing, MMA groups
+completing and their tcgen05.commit arrivals) completes at random later
+times, and the scheduler interleaves everything in random order. The model
+follows the PTX semantics of a parity wait: `try_wait.parity(P)` succeeds
+when the barrier's current (incomplete) phase has parity != P. Checked on
+every interleaving:
+  * no wait succeeds on an aliased phase (the phase it means has completed);
+  * no wait falls two phases behind (which would never succeed on hardware);
+  * no buffer (ring stage, accumulator, S / P / O tile) is overwritten while
+    its previous contents are still to be read, and every read sees the
+    contents of the step it expects;
+  * the run finishes (no deadlock).
+"""
+
+from __future__ import annotations
+
+import random
+
+import pytest
+
+
+class Bar:
+    """An mbarrier: `count` arrivals plus transaction bytes complete a phase."""
+
+    def __init__(self, name, count):
+        self.name, self.count, self.pending, self.tx, self.done = name, count, count, 0, 0
+
+    def arrive(self, expect_tx=0):
+        self.tx += expect_tx
+        self.pending -= 1
+        assert self.pending >= 0, f"{self.name}: too many arrivals"
+        self._flip()
+
+    def complete_tx(self, n):
+        self.tx -= n
+        self._flip()
+
+    def _flip(self):
+        if self.pending == 0 and self.tx == 0:
+            self.done += 1
+            self.pending = self.count
+
+    def try_wait(self, phase):
+        """Wait for phase index `phase` with its parity, as the kernels do."""
+        ok = (self.done & 1) != (phase & 1)
+        if ok:
+            assert self.done >= phase + 1, f"{self.name}: parity alias (waited phase {phase}, {self.done} done)"
+        else:
+            assert self.done <= phase + 1, f"{self.name}: waiter fell behind (phase {phase}, {self.done} done)"
+        return ok
+
+
+class Sim:
+    def __init__(self, seed):
+        self.rng = random.Random(seed)
+        self.roles = []
+        self.events = []  # pending asynchronous completions (callables)
+
+    def spawn(self, gen):
+        self.roles.append([gen, None])
+
+    def later(self, fn):
+        self.events.append(fn)
+
+    def run(self, limit=2_000_000):
+        for _ in range(limit):
+            live = [r for r in self.roles if r[0] is not None]
+            if not live and not self.events:
+                return
+            choices = []
+            for r in live:
+                cond = r[1]
+                if cond is None or cond():
+                    choices.append(("role", r))
+            choices += [("event", i) for i in range(len(self.events))]
+            assert choices, "deadlock: every role waits and nothing is in flight"
+            kind, x = self.rng.choice(choices)
+            if kind == "event":
+                self.events.pop(x)()
+            else:
+                try:
+                    x[1] = next(x[0])
+                except StopIteration:
+                    x[0] = None
+        raise AssertionError("simulation did not finish")
+
+
+class Buf:
+    """A buffer whose contents are tagged; writers must find it released."""
+
+    def __init__(self, name):
+        self.name, self.tag, self.readers = name, None, 0
+
+    def write(self, tag):
+        assert self.readers == 0, f"{self.name}: overwritten while {self.readers} reads are pending"
+        self.tag = tag
+
+    def check(self, tag):
+        assert self.tag == tag, f"{self.name}: read {self.tag}, expected {tag}"
+
+
+# ---- k_enc_gemm ----------------------------------------------------------------------------
+def gemm_protocol(sim, stages, n_tiles, nk, epi_warps=8, bug=None):
+    """`bug` plants a protocol mistake in the model (to show the checks bite):
+    "acc_early" waits one accumulator release too early, "ring_early" one
+    ring release too early."""
+    full = [Bar(f"full{s}", 1) for s in range(stages)]
+    empty = [Bar(f"empty{s}", 1) for s in range(stages)]
+    acc_full = [Bar(f"acc_full{b}", 1) for b in range(2)]
+    acc_empty = [Bar(f"acc_empty{b}", epi_warps) for b in range(2)]
+    ring = [Buf(f"stage{s}") for s in range(stages)]
+    acc = [Buf(f"acc{b}") for b in range(2)]
+    STAGE = 48 * 1024
+
+    def producer():
+        g = 0
+        for t in range(n_tiles):
+            for kb in range(nk):
+                st = g % stages
+                if g >= stages:
+                    ph = g // stages - 1  # wait parity ((g / S) + 1) & 1 == the release of use g - S
+                    if bug == "ring_early":
+                        ph -= 1
+                    yield lambda b=empty[st], p=ph: b.try_wait(p)
+                full[st].arrive(expect_tx=STAGE)
+
+                def land(st=st, tag=(t, kb)):
+                    ring[st].write(tag)
+                    full[st].complete_tx(STAGE)
+                sim.later(land)
+                g += 1
+
+    pending = []  # completions of issued MMA groups; MMAs of one thread complete in issue order
+
+    def drain_one():
+        pending.pop(0)()
+
+    def submit(fn):
+        pending.append(fn)
+        sim.later(drain_one)
+
+    def mma():
+        g = 0
+        for i in range(n_tiles):
+            buf = i & 1
+            if i >= 2:
+                ph = (i >> 1) - 1 + (1 if bug == "acc_early" else 0)
+                yield lambda b=acc_empty[buf], p=ph: b.try_wait(p)
+            acc[buf].write(("acc", i))  # the tile's first MMA overwrites the accumulator
+            for kb in range(nk):
+                st = g % stages
+                yield lambda b=full[st], p=g // stages: b.try_wait(p)
+                ring[st].check((i, kb))
+                ring[st].readers += 1
+
+                def mma_done(st=st):
+                    ring[st].readers -= 1
+                    empty[st].arrive()  # tcgen05.commit -> empty[st]
+                submit(mma_done)
+                g += 1
+            submit(lambda buf=buf: acc_full[buf].arrive())  # commit after the k-loop
+
+    def epilogue(w):
+        for i in range(n_tiles):
+            buf = i & 1
+            yield lambda b=acc_full[buf], p=i >> 1: b.try_wait(p)
+            acc[buf].check(("acc", i))
+            acc[buf].readers += 1
+            yield None  # tcgen05.ld + processing
+            acc[buf].readers -= 1
+            acc_empty[buf].arrive()
+
+    sim.spawn(producer())
+    sim.spawn(mma())
+    for w in range(epi_warps):
+        sim.spawn(epilogue(w))
+
+
+@pytest.mark.parametrize("seed", range(40))
+@pytest.mark.parametrize("stages,n_tiles,nk", [(4, 5, 16), (4, 3, 1), (6, 4, 3), (4, 1, 64), (2, 6, 5)])
+def test_enc_gemm_protocol(seed, stages, n_tiles, nk):
+    sim = Sim(seed * 7919 + stages * 31 + n_tiles * 17 + nk)
+    gemm_protocol(sim, stages, n_tiles, nk)
+    sim.run()
+
+
+@pytest.mark.parametrize("bug", ["acc_early", "ring_early"])
+def test_the_simulation_catches_a_planted_protocol_mistake(bug):
+    failures = 0
+    for seed in range(20):
+        sim = Sim(seed)
+        gemm_protocol(sim, 4, 5, 16, bug=bug)
+        try:
+            sim.run()
+        except AssertionError:
+            failures += 1
+    assert failures == 20
+
+
+# ---- k_enc_attn -----------------------------------------------------------------------------
+def attn_protocol(sim, stages, n_tiles, rescale_at):
+    """One CTA: producer (Q, then K/V tiles into a ring), MMA issuer (S_j = QK_j^T
+    into S[j & 1], then PV_{j-1}), 128 softmax threads modelled as one role per
+    warp (4) since each barrier counts 128 arrivals: a warp arrives 32 times.
+    (The model also shows that the s_empty and p_empty waits are implied by the
+    issue order -- PV_{j-2} waits for softmax j-2 before S_j is issued, and MMAs
+    complete in issue order -- so they never block; the kernel keeps them as
+    explicit guards.)"""
+    q_full = Bar("q_full", 1)
+    kv_full = [Bar(f"kv_full{s}", 1) for s in range(stages)]
+    kv_empty = [Bar(f"kv_empty{s}", 1) for s in range(stages)]
+    s_full = [Bar(f"s_full{b}", 1) for b in range(2)]
+    s_empty = [Bar(f"s_empty{b}", 128) for b in range(2)]
+    p_full = [Bar(f"p_full{b}", 128) for b in range(2)]
+    p_empty = [Bar(f"p_empty{b}", 1) for b in range(2)]
+    o_full, o_final = Bar("o_full", 1), Bar("o_final", 1)
+    kv = [Buf(f"kv{s}") for s in range(stages)]
+    S = [Buf(f"S{b}") for b in range(2)]
+    P = [Buf(f"P{b}") for b in range(2)]
+    O = Buf("O")
+    inflight = []  # MMA groups in issue order; each completes only after its predecessors
+
+    def issue(group_tag, reads, on_done):
+        for b in reads:
+            b.readers += 1
+        inflight.append(group_tag)
+
+        def done():
+            assert inflight[0] == group_tag, "MMA groups complete in issue order"
+            inflight.pop(0)
+            for b in reads:
+                b.readers -= 1
+            on_done()
+        return done
+
+    def producer():
+        q_full.arrive(expect_tx=1)
+        sim.later(lambda: q_full.complete_tx(1))
+        for j in range(n_tiles):
+            st = j % stages
+            if j >= stages:
+                yield lambda b=kv_empty[st], p=j // stages - 1: b.try_wait(p)
+            kv_full[st].arrive(expect_tx=2)
+
+            def land(st=st, j=j):
+                kv[st].write(("kv", j))
+                kv_full[st].complete_tx(2)
+            sim.later(land)
+
+    pending = []  # completions of issued MMA groups, run strictly in issue order
+
+    def drain_one():
+        pending.pop(0)()
+
+    def submit(fn):
+        pending.append(fn)
+        sim.later(drain_one)
+
+    def mma():
+        yield lambda: q_full.try_wait(0)
+
+        def pv(i):
+            pb = i & 1
+            yield lambda b=p_full[pb], p=i >> 1: b.try_wait(p)
+            P[pb].check(("P", i))
+            st = i % stages
+            kv[st].check(("kv", i))
+            O.write(("O", i))
+
+            def fin(pb=pb, st=st):
+                o_full.arrive()
+                p_empty[pb].arrive()
+                kv_empty[st].arrive()
+            submit(issue(("pv", i), [P[pb], kv[st]], fin))
+
+        for j in range(n_tiles):
+            st, sb = j % stages, j & 1
+            yield lambda b=kv_full[st], p=j // stages: b.try_wait(p)
+            if j >= 2:
+                yield lambda b=s_empty[sb], p=(j >> 1) - 1: b.try_wait(p)
+            kv[st].check(("kv", j))
+            S[sb].write(("S", j))
+            submit(issue(("s", j), [kv[st]], lambda sb=sb: s_full[sb].arrive()))
+            if j >= 1:
+                yield from pv(j - 1)
+        yield from pv(n_tiles - 1)
+        submit(issue(("final",), [], lambda: o_final.arrive()))
+
+    def softmax(w):
+        for j in range(n_tiles):
+            sb = j & 1
+            yield lambda b=s_full[sb], p=j >> 1: b.try_wait(p)
+            S[sb].check(("S", j))
+            S[sb].readers += 1
+            yield None  # tcgen05.ld of the S tile
+            S[sb].readers -= 1
+            for _ in range(32):
+                s_empty[sb].arrive()
+            rescaling = j in rescale_at
+            if rescaling:  # O of PVs 0 .. j-1 is rescaled in tensor memory (load, scale, store)
+                yield lambda p=j - 1: o_full.try_wait(p)
+                O.check(("O", j - 1))
+                O.readers += 1
+            if j >= 2:
+                yield lambda b=p_empty[sb], p=(j - 2) >> 1: b.try_wait(p)
+            P[sb].write(("P", j))
+            if rescaling:
+                O.readers -= 1  # tcgen05.st of the rescaled O waited before P is published
+            for _ in range(32):
+                p_full[sb].arrive()
+        yield lambda: o_final.try_wait(0)
+        O.check(("O", n_tiles - 1))
+
+    sim.spawn(producer())
+    sim.spawn(mma())
+    for w in range(4):
+        sim.spawn(softmax(w))
+
+
+@pytest.mark.parametrize("seed", range(40))
+@pytest.mark.parametrize("stages,n_tiles,rescale", [(3, 24, (1, 5, 23)), (3, 1, ()), (3, 2, (1,)), (3, 7, (2, 3, 4))])
+def test_enc_attn_protocol(seed, stages, n_tiles, rescale):
+    sim = Sim(seed * 104729 + n_tiles * 13 + len(rescale))
+    attn_protocol(sim, stages, n_tiles, set(rescale))
+    sim.run()
