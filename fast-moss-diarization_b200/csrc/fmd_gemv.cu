@@ -896,6 +896,13 @@ int launch_lm_head_t(const LinW& W, const void* x, int ldx, const int* row_map, 
   if (xbytes + 2 * stage > (size_t)kHeadSmemBudget) return 0;
   int stages = (int)((kHeadSmemBudget - xbytes) / stage);
   if (stages > kHeadMaxStages) stages = kHeadMaxStages;
+  // With G groups the units of a tile group alternate between the groups; a
+  // stage count that is a multiple of G keeps every stage with one group, so
+  // a group's parity wait on a stage only ever follows its own previous use.
+  // (An odd count hands consecutive uses of a stage to different groups: a
+  // group that runs ahead can then pass a parity wait on the other group's
+  // phase while that copy is still in flight.)
+  stages -= stages % G;
   const int n_tiles = W.N / (kHeadWarps * 16);
   const int grid = n_tiles < n_sm ? n_tiles : n_sm;
   cudaLaunchAttribute attr[1];
