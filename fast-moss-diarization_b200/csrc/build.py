@@ -2,13 +2,16 @@
 
 Usage: python build.py [--force] [--verbose]
 The library lands next to the package (`fast-moss-diarization_b200/libfmd_decoder.so`)
-so it travels with the source tree. Objects are rebuilt only when a source or
-header is newer than the library.
+so it travels with the source tree. Without --force the library is rebuilt
+unless it was built from exactly the current sources, headers and flags (a
+SHA-256 of them is stored next to the objects), so a stale binary is never
+reused because of file times.
 """
 
 from __future__ import annotations
 
 import argparse
+import hashlib
 import os
 import shutil
 import subprocess
@@ -35,14 +38,33 @@ def nvcc() -> str:
 
 
 def _deps() -> list[Path]:
-    return [HERE / s for s in SOURCES] + sorted(HERE.glob("*.cuh")) + sorted((ROOT / "include").glob("*.h"))
+    return ([HERE / s for s in SOURCES] + sorted(HERE.glob("*.cuh")) + sorted(HERE.glob("*.h")) +
+            sorted((ROOT / "include").glob("*.h")))
+
+
+HASH_FILE = OBJ_DIR / "srchash"
+
+
+def source_hash() -> str:
+    """SHA-256 over the names and contents of every source and header plus the
+    compiler flags."""
+    h = hashlib.sha256()
+    h.update(" ".join(ARCH + _flags()).encode())
+    for p in _deps():
+        h.update(p.name.encode())
+        h.update(p.read_bytes())
+    return h.hexdigest()
 
 
 def needs_build() -> bool:
-    if not LIB.exists():
+    if not LIB.exists() or not HASH_FILE.exists():
         return True
-    t = LIB.stat().st_mtime
-    return any(p.stat().st_mtime > t for p in _deps())
+    return HASH_FILE.read_text().strip() != source_hash()
+
+
+def _flags() -> list[str]:
+    return ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O2", "--expt-relaxed-constexpr",
+            "-I", str(ROOT / "include")]
 
 
 def build(force: bool = False, verbose: bool = False) -> Path:
@@ -50,8 +72,8 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         return LIB
     OBJ_DIR.mkdir(exist_ok=True)
     cc = nvcc()
-    flags = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O2", "--expt-relaxed-constexpr",
-                    "-I", str(ROOT / "include")]
+    digest = source_hash()
+    flags = ARCH + _flags()
     if verbose:
         flags += ["-Xptxas", "-v"]
 
@@ -73,6 +95,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     if r.returncode != 0:
         raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
     os.replace(tmp, LIB)
+    HASH_FILE.write_text(digest + "\n")
     return LIB
 
 

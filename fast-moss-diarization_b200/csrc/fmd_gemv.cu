@@ -520,10 +520,16 @@ __global__ void __launch_bounds__(FW * KG * 32) k_gemv(const T* __restrict__ x, 
 //    takes the CTA's tiles g, g + G, ...; the producer interleaves the
 //    k-blocks of G tiles, so the groups stream at once. The register-level
 //    Q8_0 dequantisation makes this instruction-bound, hence two groups
-//    where the registers allow (batches up to 32 rows). A warp releases a
-//    stage by arriving on its "empty" barrier. Every
-//    wait is bounded; a timeout stops the ring, sets the status word and
-//    drains the copies still in flight.
+//    where the registers allow (batches up to 32 rows).
+//  * each group owns its own ring of S/G stages: the q-th unit (k-block) of
+//    group g uses stage g * S/G + q mod S/G in phase q / (S/G). A stage is
+//    therefore only ever filled for, and released by, one group, so a
+//    group's parity wait can only match its own copy, whatever order the
+//    copies land in and however far one group runs ahead (a ring shared by
+//    the groups lets a group pass a wait on the other group's phase).
+//  * a warp releases a stage by arriving on its "empty" barrier. Every wait
+//    is bounded; a timeout stops the ring, sets the status word and drains
+//    the copies still in flight.
 //  * the tile order of the packed lm_head ([tile][k-split][k-block][warp]) is
 //    the full-K k-block order of each tile.
 //  * each CTA keeps, per row, the best (rounded logit, lowest index) over its
@@ -532,13 +538,16 @@ constexpr int kHeadWarps = 8;            // warps per group: 128 features per ti
 constexpr int kHeadMaxStages = 16;
 constexpr int kHeadSmemBudget = 220 * 1024;
 
-// ring position of (CTA-local tile i, k-block kb) with G consumer groups: the
-// k-blocks of the G tiles of a group of tiles alternate
-template <int G>
-FMD_DEV int head_unit(int i, int kb, int nkb, int my_tiles) {
-  const int p = i / G, in_grp = min(G, my_tiles - G * p);
-  return G * p * nkb + kb * in_grp + (i - G * p);
-}
+// Stage and phase of a group's ring, advanced one unit at a time.
+struct RingPos {
+  int st, ph;
+  FMD_DEV void next(int sg) {
+    if (++st == sg) {
+      st = 0;
+      ph ^= 1;
+    }
+  }
+};
 
 // NTL: MMA n-tiles (8 rows each) of a row tile; G: consumer groups. Two
 // groups (17 warps) leave 96 registers per thread, enough for 4 n-tiles.
@@ -562,7 +571,6 @@ __global__ void __launch_bounds__((G * kHeadWarps + 1) * 32, 1)
   const int K = W.K, nkb = K / 64;
   const int n_tiles = W.N / FT;
   const int my_tiles = n_tiles > (int)blockIdx.x ? (n_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-  const int n_units = my_tiles * nkb;
   uint8_t* ring = smem;
   T* xs = reinterpret_cast<T*>(smem + (size_t)stages * kStage);  // [xrows][K + 8]
   const int xstride = K + 8;
@@ -579,17 +587,24 @@ __global__ void __launch_bounds__((G * kHeadWarps + 1) * 32, 1)
   }
   __syncthreads();
 
+  const int SG = stages / G;  // stages per group
   if (warp == NCW) {
     // ---- producer: weights do not depend on the previous kernel, so the
     // ring starts filling before griddepcontrol.wait
     if (lane == 0) {
-      int u = 0;
+      RingPos pos[G];
+      int q[G];
+#pragma unroll
+      for (int j = 0; j < G; ++j) pos[j] = RingPos{0, 0}, q[j] = 0;
       for (int p = 0; G * p < my_tiles; ++p) {
         const int in_grp = min(G, my_tiles - G * p);
         for (int kb = 0; kb < nkb; ++kb) {
-          for (int j = 0; j < in_grp; ++j, ++u) {
-            const int st = u % stages, ph = (u / stages) & 1;
-            if (u >= stages && !mbar_wait_bounded(&empty[st], ph ^ 1, kWaitLimit)) {
+#pragma unroll
+          for (int j = 0; j < G; ++j) {
+            if (j >= in_grp) continue;
+            const int st = j * SG + pos[j].st;
+            // the stage's previous use (unit q - SG of this group) must be released
+            if (q[j] >= SG && !mbar_wait_bounded(&empty[st], pos[j].ph ^ 1, kWaitLimit)) {
               atomicExch(&abort_s, 1);
               goto produced;
             }
@@ -597,6 +612,8 @@ __global__ void __launch_bounds__((G * kHeadWarps + 1) * 32, 1)
             const int tile = blockIdx.x + (G * p + j) * gridDim.x;
             mbar_arrive_expect_tx(&full[st], kStage);
             bulk_load(ring + (size_t)st * kStage, W.pk + ((size_t)tile * nkb + kb) * kStage, kStage, &full[st]);
+            pos[j].next(SG);
+            ++q[j];
           }
         }
       }
@@ -658,20 +675,22 @@ __global__ void __launch_bounds__((G * kHeadWarps + 1) * 32, 1)
     bi[nt][0] = bi[nt][1] = 0x7fffffff;
   }
   bool ok = true;
+  RingPos rp{0, 0};  // this group's ring position
   if (rows == 0) {
     // the producer started before the row count was known: release every
     // stage of this group's tiles so that no copy is left in flight when the
     // CTA retires
     for (int i = grp; i < my_tiles && ok; i += G)
       for (int kb = 0; kb < nkb; ++kb) {
-        const int u = head_unit<G>(i, kb, nkb, my_tiles), st = u % stages;
-        if (*reinterpret_cast<volatile int*>(&abort_s) || !mbar_wait_bounded(&full[st], (u / stages) & 1, kWaitLimit)) {
+        const int st = grp * SG + rp.st;
+        if (*reinterpret_cast<volatile int*>(&abort_s) || !mbar_wait_bounded(&full[st], rp.ph, kWaitLimit)) {
           atomicExch(&abort_s, 1);
           ok = false;
           break;
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[st]);
+        rp.next(SG);
       }
   }
   for (int i = grp; i < my_tiles && ok && rows > 0; i += G) {
@@ -681,12 +700,13 @@ __global__ void __launch_bounds__((G * kHeadWarps + 1) * 32, 1)
     for (int nt = 0; nt < NTL; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
 #pragma unroll 1
     for (int kb = 0; kb < nkb; ++kb) {
-      const int u = head_unit<G>(i, kb, nkb, my_tiles), st = u % stages;
-      if (*reinterpret_cast<volatile int*>(&abort_s) || !mbar_wait_bounded(&full[st], (u / stages) & 1, kWaitLimit)) {
+      const int st = grp * SG + rp.st;
+      if (*reinterpret_cast<volatile int*>(&abort_s) || !mbar_wait_bounded(&full[st], rp.ph, kWaitLimit)) {
         atomicExch(&abort_s, 1);
         ok = false;
         break;
       }
+      rp.next(SG);
       const uint8_t* un = ring + (size_t)st * kStage + fw * UNIT;
       WRegs w;
       w.a = *reinterpret_cast<const int4*>(un + lane * 16);
@@ -784,10 +804,13 @@ __global__ void __launch_bounds__((G * kHeadWarps + 1) * 32, 1)
   // drain: a copy still in flight must land before the CTA's shared memory
   // is released (only after an abort can one be outstanding here)
   if (threadIdx.x == 0 && *reinterpret_cast<volatile int*>(&abort_s)) {
-    for (int st = 0; st < stages && st < n_units; ++st) {
-      // the last use of stage st is unit ulast; wait for its phase
-      const int ulast = st + ((n_units - 1 - st) / stages) * stages;
-      mbar_wait_bounded(&full[st], (ulast / stages) & 1, kWaitLimit);
+    for (int j = 0; j < G; ++j) {
+      const int n_j = (my_tiles > j ? (my_tiles - j + G - 1) / G : 0) * nkb;  // units of group j
+      for (int sl = 0; sl < SG && sl < n_j; ++sl) {
+        // the last use of the group's stage sl is its unit qlast
+        const int qlast = sl + ((n_j - 1 - sl) / SG) * SG;
+        mbar_wait_bounded(&full[j * SG + sl], (qlast / SG) & 1, kWaitLimit);
+      }
     }
   }
 }
@@ -896,12 +919,7 @@ int launch_lm_head_t(const LinW& W, const void* x, int ldx, const int* row_map, 
   if (xbytes + 2 * stage > (size_t)kHeadSmemBudget) return 0;
   int stages = (int)((kHeadSmemBudget - xbytes) / stage);
   if (stages > kHeadMaxStages) stages = kHeadMaxStages;
-  // With G groups the units of a tile group alternate between the groups; a
-  // stage count that is a multiple of G keeps every stage with one group, so
-  // a group's parity wait on a stage only ever follows its own previous use.
-  // (An odd count hands consecutive uses of a stage to different groups: a
-  // group that runs ahead can then pass a parity wait on the other group's
-  // phase while that copy is still in flight.)
+  // each of the G groups owns stages / G of the stages (its own ring)
   stages -= stages % G;
   const int n_tiles = W.N / (kHeadWarps * 16);
   const int grid = n_tiles < n_sm ? n_tiles : n_sm;

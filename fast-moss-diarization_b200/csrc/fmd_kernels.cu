@@ -551,6 +551,22 @@ void launch_logits_argmax(ActType at, const int* n_sample_ptr, int B, const floa
   FMD_DISPATCH(at, launch_pdl(k_logits_argmax<T>, B, 1024, 0, s, n_sample_ptr, part, V, logits, next_ids));
 }
 
+// One bounded mbarrier wait on a barrier that nothing arrives on, with the
+// caller's iteration limit: the wait every ring kernel uses, made to run out.
+// The timeout path is the one the kernels take (status word set, no copy in
+// flight, the CTA returns), so the host can check that a wait which gives up
+// surfaces as FMD_ETIMEDOUT and leaves the context usable.
+__global__ void k_wait_probe(uint32_t limit, int* __restrict__ status) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+    if (!mbar_wait_bounded(&bar, 0, limit)) atomicExch(status, -110);  // FMD_ETIMEDOUT
+  }
+}
+
+void launch_wait_probe(uint32_t limit, int* status, cudaStream_t s) { k_wait_probe<<<1, 32, 0, s>>>(limit, status); }
+
 cudaError_t init_kernels() { return cudaSuccess; }
 
 void launch_dequant(ActType at, const LinW& W, float* out, cudaStream_t s) {

@@ -199,6 +199,9 @@ void launch_silu_mul(ActType at, const int* n_rows_ptr, int R, const float* part
 void launch_logits_argmax(ActType at, const int* n_sample_ptr, int B, const float* part, int V, float* logits,
                           int* next_ids, cudaStream_t s);
 void launch_dequant(ActType at, const LinW& W, float* out, cudaStream_t s);
+// One bounded wait that runs out after `limit` tries and sets *status to
+// FMD_ETIMEDOUT (the failure path of every ring kernel's waits).
+void launch_wait_probe(uint32_t limit, int* status, cudaStream_t s);
 // fmd_splice.cu: prompt rows from vocabulary ids (src >= 0) or audio rows
 // (src = -row - 1), H a multiple of 8, every pointer 16-byte aligned.
 void launch_splice(ActType at, const int* src, long long n, const void* table, const void* audio, bool audio_f32,

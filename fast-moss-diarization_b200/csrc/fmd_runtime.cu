@@ -19,6 +19,7 @@
 #include "../../include/fmd_decoder.h"
 #include "fmd_kernels.cuh"
 #include "fmd_scheduler.cuh"
+#include "fmd_watch.h"
 
 namespace fmd {
 cudaError_t init_kernels();
@@ -31,6 +32,7 @@ namespace {
 constexpr int kVersion = 1;
 constexpr int kMaxSlotsLimit = 256;
 constexpr int kEngineCheckEvery = 16;
+constexpr int kEngineIdlePolls = 4;  // polls without progress before FMD_ETIMEDOUT
 
 struct Status {
   int code;
@@ -1416,8 +1418,7 @@ int fmd_engine_step(fmd_handle* h, int64_t max_steps, fmd_stats* stats) {
   const long long tokens0 = h->h_ctr->gen_tokens;
   bool finished = h->h_ctr->done >= h->eng_n_reqs;
   int64_t launched = 0;
-  long long last_progress = -1;
-  int idle_checks = 0;
+  ProgressWatch watch(kEngineIdlePolls);
   CK(cudaEventRecord(h->win_begin, h->stream));
   int64_t mixed_launched = 0;
   while (!finished && launched < max_steps) {
@@ -1437,12 +1438,11 @@ int fmd_engine_step(fmd_handle* h, int64_t max_steps, fmd_stats* stats) {
     finished = h->h_ctr->done >= h->eng_n_reqs;
     // every live step emits a token or consumes prompt rows; a run of checks
     // without either means the queue cannot make progress
-    const long long progress = h->h_ctr->gen_tokens + h->h_ctr->prefill_tokens + h->h_ctr->done;
-    idle_checks = progress == last_progress ? idle_checks + 1 : 0;
-    last_progress = progress;
-    if (!finished && idle_checks >= 4)
-      return fail(h, FMD_ETIMEDOUT, "engine made no progress for " + std::to_string(4 * kEngineCheckEvery) +
-                                        " steps (requests done " + std::to_string(h->h_ctr->done) + ")");
+    const bool stalled = watch.stalled(h->h_ctr->gen_tokens, h->h_ctr->prefill_tokens, h->h_ctr->done);
+    if (!finished && stalled)
+      return fail(h, FMD_ETIMEDOUT, "engine made no progress for " +
+                                        std::to_string(kEngineIdlePolls * kEngineCheckEvery) + " steps (requests done " +
+                                        std::to_string(h->h_ctr->done) + ")");
   }
   // a consume-only scheduler pass books the samples of the last step run
   EngineDev e = make_engine_dev(h, h->graph_batch, h->graph_chunk);
@@ -1563,6 +1563,15 @@ int fmd_debug_kv(fmd_handle* h, int32_t slot, int32_t layer, int32_t pos, int32_
         CK(cudaMemcpyAsync(dst, src, rowb, cudaMemcpyDeviceToHost, h->stream));
       }
   }
+  return sync_check(h);
+}
+
+int fmd_debug_wait_timeout(fmd_handle* h, int32_t limit) {
+  int rc = check_ready(h);
+  if (rc) return rc;
+  if (limit < 1) return fail(h, FMD_EINVAL, "limit must be >= 1");
+  CK(cudaSetDevice(h->device));
+  launch_wait_probe((uint32_t)limit, h->d_status, h->stream);
   return sync_check(h);
 }
 

@@ -233,6 +233,11 @@ class Qwen3Decoder:
                                               out.ctypes.data_as(C.POINTER(C.c_float)), out.size))
         return out
 
+    def debug_wait_timeout(self, limit: int) -> None:
+        """Run one bounded device wait that runs out (`fmd_debug_wait_timeout`):
+        raises FmdError with FMD_ETIMEDOUT, after which the handle stays usable."""
+        self._check(self.lib.fmd_debug_wait_timeout(self._h, int(limit)))
+
     def debug_kv(self, slot: int, layer: int, pos: int, n: int):
         shape = (n, self.cfg.num_key_value_heads, self.cfg.head_dim)
         k = np.empty(shape, dtype=np.uint16)

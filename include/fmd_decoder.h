@@ -266,6 +266,14 @@ int fmd_debug_weight(fmd_handle* h, int32_t layer, int32_t which, float* out, in
 int fmd_debug_kv(fmd_handle* h, int32_t slot, int32_t layer, int32_t pos, int32_t n, void* k_out,
                  void* v_out);
 
+/* Failure detection check (no reference counterpart; the reference has no
+ * device-side waits): runs one bounded mbarrier wait, the wait every ring
+ * kernel of this library uses, on a barrier nothing arrives on, with at most
+ * `limit` tries. The wait gives up, the device status word is set and the
+ * call returns FMD_ETIMEDOUT as a step whose wait ran out would; no copy is
+ * in flight, so the context and the handle stay usable. */
+int fmd_debug_wait_timeout(fmd_handle* h, int32_t limit);
+
 /* ---- greedy pick without allocation -------------------------------------- */
 
 /* No counterpart in the reference. Greedy ids (per-row argmax, lowest index
@@ -284,10 +292,21 @@ int fmd_debug_kv(fmd_handle* h, int32_t slot, int32_t layer, int32_t pos, int32_
  * Limits: 1 <= n_rows <= 64 and 1 <= vocab <= 1048576; larger sizes return
  * FMD_EINVAL without launching anything. The first call on each device looks
  * up the scratch's device address with that device current, so make that
- * first call before any stream capture on that device. All calls share the
- * one scratch array, which keeps the last call's contents. Each call writes
- * every entry it reads, so nothing needs clearing, but calls whose kernels
- * overlap on the GPU (different streams or host threads) race. */
+ * first call before any stream capture on that device (a call after
+ * cudaDeviceReset looks it up again, so the same applies to it). All calls
+ * share the one scratch array, which keeps the last call's contents. Each
+ * call writes every entry it reads, so nothing needs clearing, but calls
+ * whose kernels overlap on the GPU (different streams or host threads) race.
+ *
+ * Values: NaN logits are never picked. A row whose logits are all -inf gets
+ * its first column (0), as np.argmax does; a row with no non-NaN logit gets
+ * the id -1, which no vocabulary id equals (the call does not synchronise,
+ * so it cannot report this as a status).
+ *
+ * Errors: if a CUDA error from earlier work is already pending in the calling
+ * thread, the call launches nothing, returns FMD_EIO and leaves that error
+ * pending for its owner. A failure of the call's own launches returns
+ * FMD_EIO and is consumed (cleared) by the call. */
 int fmd_greedy_pick_noalloc(const float* logits, int32_t n_rows, int32_t vocab, int32_t* next_ids, void* stream);
 
 /* Host-side GGML Q8_0 quantiser (the `QTensor::quantize` step of

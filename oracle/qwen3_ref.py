@@ -310,9 +310,15 @@ class Qwen3Ref:
 
     def _attention(self, lw: LayerWeights, xs, cache: KvCache, offset: int, mask) -> torch.Tensor:
         """`Attention::forward` (qwen3.rs:203-259)."""
+        qkv = self.act.r(xs @ lw.qkv.T)  # FusedLinear::forward (linear.rs:85-95)
+        return self.act.r(self._context(lw, qkv, cache, offset, mask) @ lw.o.T)
+
+    def _context(self, lw: LayerWeights, qkv, cache: KvCache, offset: int, mask) -> torch.Tensor:
+        """The part of `Attention::forward` between the fused QKV projection and
+        the output projection (qwen3.rs:211-257): split, per-head q/k norm,
+        RoPE at `offset`, cache append, grouped attention."""
         a, c = self.act, self.cfg
-        b, t, _ = xs.shape
-        qkv = a.r(xs @ lw.qkv.T)  # FusedLinear::forward (linear.rs:85-95)
+        b, t, _ = qkv.shape
         q = qkv[..., :c.q_dim].reshape(b, t, c.num_attention_heads, c.head_dim)
         k = qkv[..., c.q_dim:c.q_dim + c.kv_dim].reshape(b, t, c.num_key_value_heads, c.head_dim)
         v = qkv[..., c.q_dim + c.kv_dim:].reshape(b, t, c.num_key_value_heads, c.head_dim)
@@ -324,8 +330,7 @@ class Qwen3Ref:
         q = rope_apply(q, cos, sin, a)
         k = rope_apply(k, cos, sin, a)
         k_all, v_all = cache.append(k, v)
-        ctx = _grouped_attention(q, k_all, v_all, mask, c.kv_repeat, self.scale, a)
-        return a.r(ctx @ lw.o.T)
+        return _grouped_attention(q, k_all, v_all, mask, c.kv_repeat, self.scale, a)
 
     def _mlp(self, lw: LayerWeights, xs) -> torch.Tensor:
         """`Mlp::forward` (qwen3.rs:288-292): down(silu(gate) * up)."""
@@ -381,6 +386,21 @@ class Qwen3Ref:
         emb = self.embed([[token]])
         hidden = self.forward_embeds(emb, caches, off, self._causal(off, 1, off + 1))
         return self.logits(hidden)[0, 0]
+
+    def decode_step_ragged(self, tokens, caches: list[list[KvCache]]) -> torch.Tensor:
+        """Solo-mode decode of several sequences in one pass: row i is
+        `decode_step(tokens[i], caches[i])` (each sequence at its own position,
+        with its own caches). The projections run over all rows at once, the
+        attention per sequence. Returns f32 logits `(len(tokens), vocab)`."""
+        a, c = self.act, self.cfg
+        xs = self.embed([[int(t)] for t in tokens])
+        for li, lw in enumerate(self.layers):
+            qkv = a.r(rms_norm(xs, lw.input_norm, c.rms_norm_eps, a) @ lw.qkv.T)
+            ctx = torch.cat([self._context(lw, qkv[i:i + 1], caches[i][li], caches[i][li].len, None)
+                             for i in range(len(tokens))], 0)
+            xs = a.r(xs + a.r(ctx @ lw.o.T))
+            xs = a.r(xs + self._mlp(lw, rms_norm(xs, lw.post_norm, c.rms_norm_eps, a)))
+        return self.logits(rms_norm(xs, self.norm, c.rms_norm_eps, a))[:, 0]
 
     # --- left-padded batch mode: the reference's own batching ----------------------
 
@@ -457,6 +477,29 @@ def generate(model: Qwen3Ref, embeds, budget: int, eos_id: int = EOS_TOKEN_ID,
             break
         logits = model.decode_step(tok, caches)
     return out, hist
+
+
+def teacher_forced_logits(model: Qwen3Ref, prompts, streams) -> list[list[torch.Tensor]]:
+    """The logits the greedy loop of `Engine::generate_batch` (engine.rs:505-538)
+    sees at every step when it is fed the given token streams instead of its
+    own picks: `out[i][s]` are sequence i's f32 logits before its s-th pick
+    (the prefill's last position for s = 0, then one decode step per token of
+    `streams[i]`), so `out[i]` has `len(streams[i]) + 1` entries. Sequences run
+    in solo mode (positions from 0), batched per step with
+    `decode_step_ragged`."""
+    caches, out = [], []
+    for p, toks in zip(prompts, streams):
+        p = torch.as_tensor(np.asarray(p, dtype=np.float32))
+        n = p.shape[-2]
+        cs = model.new_caches(1, n + len(toks) + 1)
+        caches.append(cs)
+        out.append([model.logits(model.prefill(p.reshape(1, n, -1), cs))[0, 0]])
+    for s in range(max((len(t) for t in streams), default=0)):
+        live = [i for i, t in enumerate(streams) if s < len(t)]
+        lg = model.decode_step_ragged([streams[i][s] for i in live], [caches[i] for i in live])
+        for j, i in enumerate(live):
+            out[i].append(lg[j])
+    return out
 
 
 def splice_audio(model: Qwen3Ref, token_ids, audio_embeds, audio_token_id: int) -> torch.Tensor:

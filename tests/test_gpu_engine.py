@@ -9,25 +9,29 @@ import importlib
 import numpy as np
 import pytest
 
-from conftest import PKG, oracle_model, tiny_config
+from conftest import PKG, check_greedy_stream, gpu_teacher_forced, oracle_model, tiny_config
 
 syn = importlib.import_module("fmd_b200.synthetic")
 pytestmark = pytest.mark.gpu
 
 
-def _compare_greedy(got_tokens, got_reason, ref_gen, hist):
-    """Tokens must agree step by step while the oracle's top-1/top-2 margin is
-    clear; a near-tie may legitimately flip, after which sequences diverge."""
-    for step, tok in enumerate(got_tokens):
-        if step >= len(ref_gen.tokens):
-            break
-        lg = hist[step].numpy()
-        top2 = np.sort(lg)[-2:]
-        if top2[1] - top2[0] < 0.05:
-            return
-        assert tok == ref_gen.tokens[step], (step, tok, ref_gen.tokens[step])
-    assert len(got_tokens) == len(ref_gen.tokens)
-    assert got_reason == ref_gen.finish_reason
+def _check_streams(dec, m, prompts, out, budgets, forced, eos_id):
+    """Every pick of the engine's free-running streams against the oracle fed
+    the same streams (near-ties may flip only within twice the observed logit
+    error, measured on the operator path over the same streams). Returns the
+    number of picks compared."""
+    from oracle import qwen3_ref as ref
+
+    streams = [o.tokens for o in out]
+    got = gpu_teacher_forced(dec, prompts, streams)
+    want = ref.teacher_forced_logits(m, prompts, streams)
+    compared = 0
+    for i in range(len(prompts)):
+        err = max(float(np.abs(g - r.numpy()).max()) for g, r in zip(got[i], want[i]))
+        res = check_greedy_stream(streams[i], out[i].finish_reason, want[i], 2.0 * err + 1e-6, budgets[i], eos_id,
+                                  forced[i])
+        compared += res["compared"]
+    return compared
 
 
 def _setup(seed=11):
@@ -37,8 +41,6 @@ def _setup(seed=11):
 
 
 def test_engine_refill_matches_oracle():
-    from oracle import qwen3_ref as ref
-
     cfg, w = _setup()
     rng = np.random.default_rng(7)
     lens = [30, 100, 64, 1, 250, 77]
@@ -49,40 +51,45 @@ def test_engine_refill_matches_oracle():
     m = oracle_model(cfg, w, "bf16")
     with PKG.Qwen3Decoder(cfg, "bf16") as dec:
         dec.load_weights(w)
-        dec.reserve(max_slots=2, max_tokens=2048, max_rows=128)
+        dec.reserve(max_slots=6, max_tokens=2048, max_rows=256)
         eng = PKG.Engine(dec)
         out, stats = eng.generate(lens, max_new, forced, arena, max_batch=2, prefill_chunk=64)
         out1, _ = eng.generate(lens, max_new, forced, arena, max_batch=1, prefill_chunk=100)
-    assert stats.requests == len(lens)
-    assert stats.prefill_tokens == sum(lens)
-    assert stats.generated_tokens == sum(len(o.tokens) for o in out)
-    for i, p in enumerate(prompts):
-        g, hist = ref.generate(m, p, budget=max_new[i], forced_stop=None if forced[i] < 0 else forced[i],
-                               record_logits=True)
-        _compare_greedy(out[i].tokens, out[i].finish_reason, g, hist)
-        _compare_greedy(out1[i].tokens, out1[i].finish_reason, g, hist)
+        assert stats.requests == len(lens)
+        assert stats.prefill_tokens == sum(lens)
+        assert stats.generated_tokens == sum(len(o.tokens) for o in out)
+        n = _check_streams(dec, m, prompts, out, max_new, forced, cfg.eos_token_id)
+        n1 = _check_streams(dec, m, prompts, out1, max_new, forced, cfg.eos_token_id)
+    # every emitted token (and every EOS stop) was compared: 6 + 2 + 10 + 3 + 5 + 0
+    assert n >= 26 and n1 >= 26, (n, n1)
     assert out[1].finish_reason == "stop" and len(out[1].tokens) == 2
     assert out[5].tokens == [] and out[5].finish_reason == "length"
 
 
 def test_engine_eos_ends_a_sequence():
-    """EOS is not emitted and ends the sequence with reason "stop" (engine.rs:513-516)."""
+    """EOS is not emitted and ends the sequence with reason "stop"
+    (engine.rs:513-516). The EOS id is set to the oracle's first pick of a
+    prompt whose top-2 margin is clear, so the assertion always applies."""
     from oracle import qwen3_ref as ref
 
     cfg, w = _setup(seed=12)
-    rng = np.random.default_rng(8)
-    prompt = rng.standard_normal((40, cfg.hidden_size), dtype=np.float32)
     m = oracle_model(cfg, w, "bf16")
-    g, hist = ref.generate(m, prompt, budget=4, eos_id=-1, record_logits=True)
-    first = g.tokens[0]
-    cfg_eos = dataclasses.replace(cfg, eos_token_id=int(first))
+    rng = np.random.default_rng(8)
+    for _ in range(20):
+        prompt = rng.standard_normal((40, cfg.hidden_size), dtype=np.float32)
+        first = ref.teacher_forced_logits(m, [prompt], [[]])[0][0].numpy()
+        top2 = np.sort(first)[-2:]
+        if top2[1] - top2[0] > 0.05:
+            break
+    else:
+        pytest.fail("no prompt with a clear first pick in 20 draws")
+    cfg_eos = dataclasses.replace(cfg, eos_token_id=int(np.argmax(first)))
     with PKG.Qwen3Decoder(cfg_eos, "bf16") as dec:
         dec.load_weights(w)
         dec.reserve(max_slots=2, max_tokens=1024, max_rows=128)
         out, stats = PKG.Engine(dec).generate([40], [8], None, prompt, max_batch=2, prefill_chunk=64)
-    top2 = np.sort(hist[0].numpy())[-2:]
-    if top2[1] - top2[0] > 0.05:
-        assert out[0].tokens == [] and out[0].finish_reason == "stop"
+    assert out[0].tokens == [] and out[0].finish_reason == "stop"
+    assert stats.generated_tokens == 0 and stats.requests == 1
 
 
 def test_engine_many_requests_page_recycling():

@@ -56,15 +56,23 @@ class Bar:
 
 
 class Sim:
-    def __init__(self, seed):
+    """`hold`: tags of asynchronous completions (copy landings) that the
+    scheduler keeps back for as long as anything else can run, the worst
+    case of out-of-order landing."""
+
+    def __init__(self, seed, hold=()):
         self.rng = random.Random(seed)
         self.roles = []
         self.events = []  # pending asynchronous completions (callables)
+        self.hold = set(hold)
+        self.held = set()  # ids of pending events that carry a held tag
 
     def spawn(self, gen):
         self.roles.append([gen, None])
 
-    def later(self, fn):
+    def later(self, fn, tag=None):
+        if tag is not None and tag in self.hold:
+            self.held.add(id(fn))
         self.events.append(fn)
 
     def run(self, limit=2_000_000):
@@ -77,7 +85,11 @@ class Sim:
                 cond = r[1]
                 if cond is None or cond():
                     choices.append(("role", r))
-            choices += [("event", i) for i in range(len(self.events))]
+            free = [i for i, f in enumerate(self.events) if id(f) not in self.held]
+            if choices or free:
+                choices += [("event", i) for i in free]
+            else:
+                choices = [("event", i) for i in range(len(self.events))]
             assert choices, "deadlock: every role waits and nothing is in flight"
             kind, x = self.rng.choice(choices)
             if kind == "event":
@@ -331,44 +343,55 @@ def test_enc_attn_protocol(seed, stages, n_tiles, rescale):
 
 
 # ---- k_lm_head (decoder) ------------------------------------------------------------------
-def head_unit(G, i, kb, nkb, my_tiles):
-    """Ring position of (CTA-local tile i, k-block kb): the k-blocks of the G
-    tiles of a group of tiles alternate (fmd_gemv.cu, head_unit)."""
-    p = i // G
-    in_grp = min(G, my_tiles - G * p)
-    return G * p * nkb + kb * in_grp + (i - G * p)
-
-
-def lm_head_protocol(sim, G, stages, my_tiles, nkb, warps=8):
+def lm_head_protocol(sim, G, stages, my_tiles, nkb, warps=8, layout="per_group"):
+    """`k_lm_head`'s ring. The producer interleaves the k-blocks of G tiles
+    (tile G*p + j is group j's p-th tile, so its k-block kb is the group's
+    unit q = p*nkb + kb). `layout="per_group"` (the kernel): group j's unit q
+    uses stage j*S/G + q % (S/G) in phase q // (S/G). `layout="shared"` (the
+    earlier design): the u-th copy in issue order uses stage u % S in phase
+    u // S, so with an odd tile count the groups share stages."""
     full = [Bar(f"full{s}", 1) for s in range(stages)]
     empty = [Bar(f"empty{s}", warps) for s in range(stages)]  # one group of 8 warps consumes a stage
     ring = [Buf(f"stage{s}") for s in range(stages)]
-    order = []
+    sg = stages // G
+    order = []  # (tile, kb) in issue order
     for p in range((my_tiles + G - 1) // G):
         in_grp = min(G, my_tiles - G * p)
         for kb in range(nkb):
             for j in range(in_grp):
                 order.append((G * p + j, kb))
-    assert [head_unit(G, i, kb, nkb, my_tiles) for i, kb in order] == list(range(len(order)))
+
+    def slot(u, tile, kb):
+        if layout == "shared":
+            return u % stages, u // stages
+        q = (tile // G) * nkb + kb
+        return (tile % G) * sg + q % sg, q // sg
+
+    where = {tag: slot(u, *tag) for u, tag in enumerate(order)}
+    uses = {}  # stage -> phases in issue order
+    for tag in order:
+        st, ph = where[tag]
+        uses.setdefault(st, []).append(ph)
+    for st, phs in uses.items():  # every stage cycles through consecutive phases
+        assert phs == list(range(len(phs))), (layout, st, phs)
 
     def producer():
-        for u, tag in enumerate(order):
-            st = u % stages
-            if u >= stages:
-                yield lambda b=empty[st], p=u // stages - 1: b.try_wait(p)
+        for tag in order:
+            st, ph = where[tag]
+            if ph > 0:
+                yield lambda b=empty[st], p=ph - 1: b.try_wait(p)
             full[st].arrive(expect_tx=1)
 
             def land(st=st, tag=tag):
                 ring[st].write(tag)
                 full[st].complete_tx(1)
-            sim.later(land)
+            sim.later(land, tag=tag)
 
     def consumer(g, w):
         for i in range(g, my_tiles, G):
             for kb in range(nkb):
-                u = head_unit(G, i, kb, nkb, my_tiles)
-                st = u % stages
-                yield lambda b=full[st], p=u // stages: b.try_wait(p)
+                st, ph = where[(i, kb)]
+                yield lambda b=full[st], p=ph: b.try_wait(p)
                 ring[st].check((i, kb))
                 ring[st].readers += 1
                 yield None  # the warp's fragment to registers
@@ -393,15 +416,57 @@ def test_lm_head_ring_protocol(seed, G, stages, my_tiles):
     sim.run()
 
 
-def test_an_odd_stage_count_with_two_groups_is_a_hazard():
-    """Why the launcher rounds the stage count down to a multiple of G: with 9
-    stages consecutive uses of a stage alternate between the two groups, and a
-    group that runs ahead passes a parity wait on the other group's phase
-    while that copy is still in flight (copies may land out of order)."""
+def _last_tile_held_copy(G, stages, my_tiles, nkb):
+    """The tag of the copy whose late landing exposes a shared ring: the first
+    k-block group 0 streams alone for an odd last tile lands in a stage group
+    1 used last; holding back the copy 7 units before it (in issue order)
+    lets group 0 reach that stage while the other group's phase is open."""
+    order = []
+    for p in range((my_tiles + G - 1) // G):
+        in_grp = min(G, my_tiles - G * p)
+        for kb in range(nkb):
+            for j in range(in_grp):
+                order.append((G * p + j, kb))
+    base = (my_tiles // G) * G * nkb  # first unit of the last (odd) tile
+    return order[base - 7]
+
+
+@pytest.mark.parametrize("seed", range(50))
+@pytest.mark.parametrize("stages,nkb", [(16, 16), (8, 16)])
+def test_per_group_rings_survive_a_late_copy(seed, stages, nkb):
+    """With one copy held back until nothing else can run, the per-group
+    rings of the kernel still never alias, for an odd tile count too."""
+    held = _last_tile_held_copy(2, stages, 9, nkb)
+    sim = Sim(seed, hold=[held])
+    lm_head_protocol(sim, 2, stages, 9, nkb=nkb, layout="per_group")
+    sim.run()
+
+
+def test_a_shared_ring_aliases_under_a_late_copy():
+    """The same schedule breaks the earlier shared-ring layout (stage u % S
+    over the interleaved issue order): with 9 tiles the last tile's k-blocks
+    reach stages the other group used last, and a wait passes on the other
+    group's phase. The check must bite, or the passing test above proves
+    nothing."""
+    hits = 0
+    for seed in range(50):
+        sim = Sim(seed, hold=[_last_tile_held_copy(2, 16, 9, 16)])
+        lm_head_protocol(sim, 2, 16, 9, nkb=16, layout="shared")
+        try:
+            sim.run()
+        except AssertionError as e:
+            assert "alias" in str(e) or "overwritten" in str(e) or "read" in str(e), e
+            hits += 1
+    assert hits > 0
+
+
+def test_an_odd_stage_count_with_a_shared_ring_is_a_hazard():
+    """The shared layout with 9 stages: consecutive uses of a stage alternate
+    between the two groups and random landing orders already alias."""
     hits = 0
     for seed in range(300):
         sim = Sim(seed)
-        lm_head_protocol(sim, 2, 9, 8, nkb=16)
+        lm_head_protocol(sim, 2, 9, 8, nkb=16, layout="shared")
         try:
             sim.run()
         except AssertionError:

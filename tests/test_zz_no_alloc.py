@@ -77,3 +77,30 @@ def test_noalloc_greedy_pick_ties_and_limits():
     # sizes beyond the stated maximum are refused before any launch
     assert _pick(lib, dev, 65, vocab, out, stream) == PKG._lib.FMD_EINVAL
     assert _pick(lib, dev, 2, (1 << 20) + 1, out, stream) == PKG._lib.FMD_EINVAL
+
+
+def test_noalloc_greedy_pick_rows_without_a_finite_logit():
+    """A row of -inf logits picks its first column (np.argmax's answer); a
+    row of NaNs gets the documented sentinel -1 instead of an id outside the
+    vocabulary; NaNs next to finite values are skipped. Run twice: the second
+    call reuses the scratch the first one left behind."""
+    import torch
+
+    lib = PKG.load_library()
+    vocab = 151_936
+    x = np.zeros((4, vocab), dtype=np.float32)
+    x[0] = -np.inf
+    x[1] = np.nan
+    x[2] = np.nan
+    x[2, 77_777] = -5.0                         # the only non-NaN value of the row
+    x[3] = -np.inf
+    x[3, 150_000] = np.nan
+    x[3, 9_000] = -1.0
+    dev = torch.from_numpy(x).to("cuda")
+    out = torch.full((4,), -7, dtype=torch.int32, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    for _ in range(2):
+        assert _pick(lib, dev, 4, vocab, out, stream) == 0
+        torch.cuda.synchronize()
+        assert out.cpu().tolist() == [0, -1, 77_777, 9_000]
+    assert int(np.argmax(x[0])) == 0
