@@ -60,8 +60,11 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--window", type=int, default=128, help="device steps per bench step")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--requests", type=int, default=256)
-    ap.add_argument("--batch", type=int, default=32)
+    ap.add_argument("--requests", type=int, default=0,
+                    help="requests per GPU (configs 2, 3) or in total (config 5); 0: the workload's own")
+    ap.add_argument("--batch", type=int, default=0, help="0: the workload's batch (8, 32 or 64)")
+    ap.add_argument("--e2e-requests", type=int, default=256,
+                    help="the e2e leg runs the first N requests of the shard (the whole shard of configs 2, 3)")
     ap.add_argument("--chunk", type=int, default=2048)
     ap.add_argument("--layers", type=int, default=28)
     ap.add_argument("--no-e2e", action="store_true")
@@ -69,10 +72,12 @@ def parse_args():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--max-new", type=int, default=4096,
                     help="cap on max_new_tokens per request (bounds the KV pool for profiling runs)")
-    ap.add_argument("--workload", choices=["3", "4", "encoder"], default="3",
-                    help="3: the headline queue; 4: BASELINE config 4 (chunked prefill of 8 x 16k prompts "
-                         "mixed with 24 decoding sequences), a separate report; encoder: the Whisper encoder "
-                         "+ adaptor over 30 s mel chunks (MossModel::encode_audio), a separate report")
+    ap.add_argument("--workload", choices=["2", "3", "4", "5", "encoder"], default="3",
+                    help="3: the headline queue (BASELINE config 3); 2: config 2 (dense bf16, batch 8, forced end "
+                         "of turn); 5: config 5 (Q8_0, batch 64 per GPU, one 2048-request queue over the GPUs); "
+                         "4: config 4 (chunked prefill of 8 x 16k prompts mixed with 24 decoding sequences), a "
+                         "separate report; encoder: the Whisper encoder + adaptor over 30 s mel chunks "
+                         "(MossModel::encode_audio), a separate report")
     ap.add_argument("--chunks", type=int, default=64, help="mel chunks per step of --workload encoder")
     ap.add_argument("--precision", default="int8_bf16", help="precision of the --workload 4 report")
     return ap.parse_args()
@@ -188,54 +193,93 @@ def traffic_per_kv_token() -> float | None:
 
 
 # ---- model + workload ---------------------------------------------------------------------
+# Request-queue workloads (3, 5): precision, requests per
+# GPU (weak scaling) or in total (strong), the prior mean generation length
+# the partitioner may use (the workload's configured mean, never the drawn
+# stop steps, which a server cannot know), and the description.
+WORKLOADS = {
+    "2": dict(precision="bf16", requests=64, per_gpu=True, mean_new=384,
+              desc="BASELINE config 2: dense bf16 decoder, batch 8, prompts log-uniform 1.2k-5k, forced end of "
+                   "turn at a step drawn uniformly from 256-512 (queue of 8-request rounds), bf16 KV cache"),
+    "3": dict(precision="int8_bf16", requests=256, per_gpu=True, mean_new=600,
+              desc="BASELINE config 3: Q8_0 decoder + lm_head, bf16 activations, batch 32 continuous batching over "
+                   "a 256-request queue (prompts log-uniform 300-8000, geometric stops mean 600 cap 4096), on-GPU "
+                   "refill, 2048-row prefill chunks"),
+    "5": dict(precision="int8_bf16", requests=2048, per_gpu=False, mean_new=800,
+              desc="BASELINE config 5: Q8_0 + bf16, batch 64 per GPU, one 2048-request queue (prompts log-uniform "
+                   "300-16k, geometric stops mean 800 cap 4096) length-balanced over the GPUs"),
+}
+
+
 def build_model_and_queue(args, rank: int, world: int = 1):
-    """Model and this rank's request queue. The global queue holds
-    `args.requests` requests per GPU (weak scaling); every rank derives the
-    same LPT partition of it (fmd_b200.dp) and builds prompt embeddings for
-    its own shard only."""
+    """Model and this rank's request queue. Configs 2 and 3 hold
+    `args.requests` requests per GPU (weak scaling); config 5 is one queue
+    split over the GPUs (strong scaling). Every rank derives the same LPT
+    partition (fmd_b200.dp) from prompt lengths, budgets and the workload's
+    prior mean generation length, and builds prompt embeddings for its own
+    shard only."""
     pkg = __graft_entry__.load_package()
     import importlib
 
     syn = importlib.import_module("fmd_b200.synthetic")
     dp = importlib.import_module("fmd_b200.dp")
+    spec = WORKLOADS[args.workload]
     cfg = pkg.TextConfig(num_hidden_layers=args.layers)
-    w = syn.make_weights(cfg, seed=args.seed, prequantized=True)
-    glob = syn.workload(3, cfg, w["embed"], seed=args.seed, n_requests=args.requests * world, with_arena=False)
+    q8 = spec["precision"].startswith("int8")
+    w = syn.make_weights(cfg, seed=args.seed, prequantized=q8)
+    n_req = args.requests or spec["requests"]
+    n_total = n_req * world if spec["per_gpu"] else n_req
+    glob = syn.workload(int(args.workload), cfg, w["embed"], seed=args.seed, n_requests=n_total, with_arena=False)
     glob.max_new = np.minimum(glob.max_new, args.max_new)
-    part = dp.partition(glob.prompt_lens, glob.max_new, world, expected_new=glob.forced_stop)
+    prior = np.full(len(glob.prompt_lens), spec["mean_new"])
+    part = dp.partition(glob.prompt_lens, glob.max_new, world, expected_new=prior)
     wl = glob.subset(part.shard(rank))
     wl.arena = syn.build_prompt_arena(cfg, w["embed"], wl.prompt_lens, args.seed + 7 * 3 + 1000 * rank,
                                       out_bf16=True)
     return pkg, cfg, w, wl
 
 
-def cpu_sample(cfg, w, wl, seconds: float = 12.0, n_seq: int = 4, steps: int | None = None, warmup: int = 0):
-    """Decode-only sample of the workload on the host cores with the CPU
-    restatement (oracle/): `n_seq` sequences at the workload's prompt lengths,
-    KV caches filled with seeded N(0,1) values (prefill not timed)."""
+CPU_LENS = [412, 797, 1190, 1500]  # BASELINE config 1's prompts
+
+
+def cpu_sample(cfg, w, seconds: float = 15.0, steps: int | None = None, warmup: int = 0):
+    """The reference's CPU decode path on the host cores: precision f32 (the
+    only CPU precision, precision.rs:60-68), the four config-1 prompts decoded
+    together as `Engine::generate_batch` does (left-padded batch, shared
+    positions plus the padding mask, engine.rs:476-538, qwen3.rs:499-511),
+    restated by the oracle. Weights given as Q8_0 are dequantised to their
+    exact f32 values. KV caches are pre-filled with seeded values at the
+    padded length (prefill not timed); each step is one batched decode of 4
+    tokens."""
     import torch
 
+    from oracle import q8_0
     from oracle import qwen3_ref as ref
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    model = ref.Qwen3Ref(ref.TextConfig(**cfg.oracle_kwargs()), w, "int8_bf16", max_len=8192 + 64)
+    if "q8" in w:  # the f32 values of the Q8_0 projections
+        layers = []
+        for lw, qw in zip(w["layers"], w["q8"]["layers"]):
+            d = dict(lw)
+            for k in ("q", "k", "v", "o", "gate", "up", "down"):
+                d[k] = q8_0.dequantize(*qw[k])
+            layers.append(d)
+        w = dict(w, layers=layers, lm_head=q8_0.dequantize(*q8_0.quantize(w["embed"])))
+    tmax = max(CPU_LENS)
+    model = ref.Qwen3Ref(ref.TextConfig(**cfg.oracle_kwargs()), w, "f32", max_len=tmax + 128)
     rng = torch.Generator().manual_seed(7)
-    lens = [int(x) for x in wl.prompt_lens[:n_seq]]
-    caches = []
-    for L in lens:
-        cs = model.new_caches(1, L + 64)
-        for c in cs:
-            c.k[:, :, :L] = model.act.r(torch.randn(c.k[:, :, :L].shape, generator=rng))
-            c.v[:, :, :L] = model.act.r(torch.randn(c.v[:, :, :L].shape, generator=rng))
-            c.len = L
-        caches.append(cs)
-    tok = [int(t) for t in np.random.default_rng(3).integers(0, cfg.vocab_size, n_seq)]
+    caches = model.new_caches(len(CPU_LENS), tmax + 96)
+    pads = [tmax - n for n in CPU_LENS]
+    for c in caches:
+        c.k[:, :, :tmax] = torch.randn(c.k[:, :, :tmax].shape, generator=rng)
+        c.v[:, :, :tmax] = torch.randn(c.v[:, :, :tmax].shape, generator=rng)
+        c.len = tmax
+    tok = [int(t) for t in np.random.default_rng(3).integers(0, cfg.vocab_size, len(CPU_LENS))]
 
     def one_step():
-        for i in range(n_seq):
-            lg = model.decode_step(tok[i], caches[i])
-            tok[i] = int(torch.argmax(lg))
+        lg = model.decode_step_padded(tok, caches, pads)
+        tok[:] = ref.argmax_rows(lg)
 
     for _ in range(warmup):
         one_step()
@@ -248,39 +292,54 @@ def cpu_sample(cfg, w, wl, seconds: float = 12.0, n_seq: int = 4, steps: int | N
         if (steps is not None and done >= steps) or (steps is None and (el >= seconds or done >= 64)):
             break
     el = time.perf_counter() - t0
-    return {"value": n_seq * done / el, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"{done} greedy decode steps x {n_seq} sequences (prompt lengths {lens}) of the config-3 "
-                      f"workload, KV caches pre-filled with seeded values (prefill not timed), 28-layer Q8_0 model, "
-                      f"torch fp32 CPU restatement of qwen3.rs with bf16 rounding, {threads} threads",
+    n = len(CPU_LENS)
+    return {"value": n * done / el, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{done} batched greedy decode steps of the 4 BASELINE config-1 prompts (lengths {CPU_LENS}, "
+                      f"left-padded to {tmax} as engine.rs:476-491 does, KV caches pre-filled with seeded values, "
+                      f"prefill not timed), {cfg.num_hidden_layers}-layer model in f32 (the reference's CPU precision, "
+                      f"precision.rs:60-68; Q8_0 weights dequantised to f32), oracle restatement of qwen3.rs / "
+                      f"engine.rs on torch with {threads} threads",
             "seconds": el}
 
 
 def workload_config(args, cfg, n_requests: int, world: int) -> dict:
     """The `config` object both arms report."""
-    return {"workload": "BASELINE config 3: Q8_0 decoder + lm_head, bf16 activations, batch 32 "
-                        "continuous batching over a 256-request queue (prompts log-uniform 300-8000, "
-                        "geometric stops mean 600 cap 4096), on-GPU refill, 2048-row prefill chunks",
+    spec = WORKLOADS[args.workload]
+    scale = (f"LPT request shards of a {n_requests * world}-request queue" if spec["per_gpu"] else
+             f"LPT request shards of one {spec['requests'] if not args.requests else args.requests}-request queue")
+    return {"workload": spec["desc"], "precision": spec["precision"],
             "requests_per_gpu": n_requests, "batch": args.batch, "prefill_chunk": args.chunk,
             "arrival": "seeded workload order for the timed windows; e2e through Engine.generate "
                        "(length-sorted queue, engine.rs:385)",
             "layers": cfg.num_hidden_layers, "step": f"{args.window} device steps",
             "l2": "working set >> L2 (no flush needed)",
-            "parallelism": f"dp{world} (LPT request shards of a {n_requests * world}-request queue, no collective)"}
+            "partition": f"greedy LPT on prompt length + budget + the workload's prior mean generation length "
+                         f"({spec['mean_new']} tokens); drawn stop steps are not read",
+            "parallelism": f"dp{world} ({scale}, no collective)"}
 
 
 def run_reference(args):
     """`--impl reference`: the reference's CPU path (restated) on a bounded
-    sample of the same workload; rank 0 alone, the other ranks exit at once."""
+    sample; rank 0 alone, the other ranks exit at once."""
     if int(os.environ.get("RANK", "0")) != 0:
         return
-    pkg, cfg, w, wl = build_model_and_queue(args, 0)
-    res = cpu_sample(cfg, w, wl, steps=max(args.steps, 1), warmup=max(args.warmup, 0), n_seq=4)
+    pkg = __graft_entry__.load_package()
+    import importlib
+
+    syn = importlib.import_module("fmd_b200.synthetic")
+    cfg = pkg.TextConfig(num_hidden_layers=args.layers)
+    w = syn.make_weights(cfg, seed=args.seed, prequantized=WORKLOADS[args.workload]["precision"].startswith("int8"))
+    res = cpu_sample(cfg, w, steps=max(args.steps, 1), warmup=max(args.warmup, 0))
+    args.batch = args.batch or {"2": 8, "3": 32, "5": 64}[args.workload]
+    args.chunk = args.chunk or 2048
+    n_req = args.requests or WORKLOADS[args.workload]["requests"]
     line = {"metric": METRIC, "value": res["value"], "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1000.0 * res["seconds"] / max(args.steps, 1),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "higher_is_better": True, "scaling": "weak" if WORKLOADS[args.workload]["per_gpu"] else "strong",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "impl": "reference",
-            "config": dict(workload_config(args, cfg, len(wl.prompt_lens), args.gpus),
-                           sample="decode-only steps of 4 sequences (see cpu_baseline.sample)"),
+            "config": dict(workload_config(args, cfg, n_req, args.gpus),
+                           sample="batched decode steps of the 4 config-1 prompts (see cpu_baseline.sample)"),
             "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": res["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -469,6 +528,8 @@ def main():
     dist = Dist()
 
     pkg, cfg, w, wl = build_model_and_queue(args, dist.rank, dist.world)
+    args.batch = args.batch or wl.max_batch
+    args.chunk = args.chunk or wl.prefill_chunk
     dec = pkg.Qwen3Decoder(cfg, wl.precision, device=dist.local)
     dec.load_weights(w)
     top = np.sort(wl.prompt_lens)[-args.batch:]
@@ -517,7 +578,7 @@ def main():
     tpk = traffic_per_kv_token()
 
     # whole-step HBM roofline at the measured mean context
-    w_bytes = cfg.n_params() * 34 / 32
+    w_bytes = cfg.n_params() * (34 / 32 if wl.precision.startswith("int8") else 2)
     mean_kv = kv_per_launch
     step_bytes = w_bytes + mean_kv * cfg.kv_bytes_per_token() + rows * cfg.kv_bytes_per_token()
     step_ms = dev_ms / max(steps_run, 1)
@@ -526,25 +587,33 @@ def main():
     if not args.no_e2e:
         import torch
 
-        arena_pinned = torch.from_numpy(wl.arena).pin_memory()
+        # configs 2 and 3: the whole shard; config 5: its first --e2e-requests
+        # requests (the whole 2048-request queue on one GPU runs for minutes)
+        sub = wl if WORKLOADS[args.workload]["per_gpu"] else wl.subset(np.arange(min(args.e2e_requests,
+                                                                                       len(wl.prompt_lens))))
+        if sub is not wl:
+            rows = int(np.sum(sub.prompt_lens))
+            sub.arena = wl.arena[:rows]  # the shard's first requests sit first in its arena
+        arena_pinned = torch.from_numpy(sub.arena).pin_memory()
         arena_np = arena_pinned.numpy()
         eng2 = pkg.Engine(dec)
         dist.barrier()
         t0 = time.perf_counter()
-        out, st2 = eng2.generate(wl.prompt_lens, wl.max_new, forced, arena_np, max_batch=args.batch,
+        out, st2 = eng2.generate(sub.prompt_lens, sub.max_new, sub.forced_stop, arena_np, max_batch=args.batch,
                                  prefill_chunk=args.chunk)
         el = time.perf_counter() - t0
         gen = sum(len(o.tokens) for o in out)
         tot = dist.reduce(float(gen), "sum")
         el_max = dist.reduce(el, "max")
-        h2d = wl.arena.nbytes + 24 * len(wl.prompt_lens)
-        d2h = 4 * len(wl.prompt_lens) * int(np.max(wl.max_new)) + 8 * len(wl.prompt_lens)
+        h2d = sub.arena.nbytes + 24 * len(sub.prompt_lens)
+        d2h = 4 * len(sub.prompt_lens) * int(np.max(sub.max_new)) + 8 * len(sub.prompt_lens)
         # audio transcribed: each prompt's N(0,1) span stands for audio at the
         # reference's 12.5 audio tokens per second (16 kHz / (hop 160 x encoder
         # stride 2 x merge 4), config.rs:210-223)
-        audio_s = dist.reduce(float(sum(round(0.75 * int(n)) for n in wl.prompt_lens)) / 12.5, "sum")
+        audio_s = dist.reduce(float(sum(round(0.75 * int(n)) for n in sub.prompt_lens)) / 12.5, "sum")
         e2e = {"value": tot / el_max, "unit": UNIT, "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
-               "step": "whole queue through fmd_generate (pinned host arena in, tokens out)",
+               "step": f"whole queue ({len(sub.prompt_lens)} requests per GPU) through fmd_generate (pinned host "
+                       f"arena in, tokens out)",
                "seconds": el_max, "tokens": int(tot),
                "audio_seconds_per_s": audio_s / el_max,
                "audio_seconds_note": "decoder only: audio-span rows of the queue's prompts / 12.5 tokens per s, "
@@ -553,14 +622,16 @@ def main():
 
     cpu = None
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu:
-        cpu = cpu_sample(cfg, w, wl)
+        cpu = cpu_sample(cfg, w)
         cpu.pop("seconds", None)
 
     if dist.rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": dist.world, "steps": len(wins),
             "warmup": args.warmup, "ms_per_step": max_ms / max(len(wins), 1), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16 activations, Q8_0 weights", "data": "synthetic",
+            "scaling": "weak" if WORKLOADS[args.workload]["per_gpu"] else "strong", "vs_baseline": None,
+            "dtype": {"bf16": "bf16 activations, bf16 weights", "int8_bf16": "bf16 activations, Q8_0 weights"}[
+                wl.precision], "data": "synthetic",
             "config": dict(workload_config(args, cfg, len(wl.prompt_lens), dist.world),
                            device_steps_timed=int(steps_run)),
             "roofline": {"bound": "hbm", "kernel": "k_attn_decode (split-KV GQA decode attention)",

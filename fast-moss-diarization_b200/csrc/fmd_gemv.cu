@@ -58,18 +58,30 @@ constexpr int kStatusNonFinite = -5;  // FMD_EIO: a greedy pick saw no finite lo
 // contiguous tile in HBM, ordered [k-block][warp][fragment] so that a k-block
 // is one TMA bulk copy and a warp's fragment reads are 512 consecutive bytes
 // (conflict-free, no padding). One (k-block, warp) unit covers 16 features x
-// 64 k; lane (g, t) owns k [16t, 16t + 16) of features g and g + 8:
+// 64 k (two Q8_0 blocks of 32):
 //  * Q8_0: [0, 512) lane-major 16 bytes of feature g, [512, 1024) feature
 //    g + 8, [1024, 1088) the f16 scales of the unit's 16 features x 2 blocks
-//    (feature-major), so the scales travel with the quants;
-//  * 16-bit: four 512-byte planes: feature g k 0-7 | 8-15, g + 8 k 0-7 | 8-15.
+//    (feature-major), so the scales travel with the quants. Lane (g, t)
+//    holds k [8t, 8t + 8) of block 0 followed by k [32 + 8t, 32 + 8t + 8) of
+//    block 1, so that two k16 MMAs cover exactly one block;
+//  * 16-bit: four 512-byte planes: feature g k 16t + 0-7 | 8-15, g + 8 the
+//    same.
 constexpr int kUnitQ8 = 1088;
 constexpr int kUnitDense = 2048;
 
 struct WRegs {
   int4 a, b, c, d;
-  float da, db;
+  uint32_t sg, sh;  // Q8_0: f16 scales of (feature g | g + 8) x (block 0, block 1)
 };
+
+// Activation row stride (elements) of a staged tile: the Q8_0 fragments read
+// 16 bytes at k 8t and 32 + 8t, the dense ones at 16t and 16t + 8; a row
+// stride of 64 (Q8_0) or 16 (dense) bytes modulo 128 keeps the 8 lanes of a
+// quarter-warp on distinct banks.
+template <bool Q8>
+constexpr int x_pad() {
+  return Q8 ? 32 : 8;
+}
 
 // rs[r] = rsqrt(mean(x^2) + eps) of rows r < rows from the per-tile sums of
 // squares ssq[row][tiles]: one thread per row, each chunk of 16 partials
@@ -90,9 +102,60 @@ FMD_DEV void rows_rsqrt(const float* __restrict__ ssq, int tiles, const int* __r
   }
 }
 
-// A fragments of the 4 MMAs of one 64-wide k-block (see the k permutation in
-// the header of fmd_kernels.cu's k_linear): thread (g, t) holds weights
-// [16t, 16t+16) of rows f0 and f0+8.
+// Four int8 weights (one 32-bit word) -> two packed 16-bit operands holding
+// exactly the same integers (|q| <= 127 is exact in f16 and bf16):
+// lo = (q0, q1), hi = (q2, q3).
+template <typename T>
+FMD_DEV void i8x4_to_act(uint32_t w, uint32_t& lo, uint32_t& hi);
+template <>
+FMD_DEV void i8x4_to_act<__half>(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  // biased bytes u = q + 128 as the low mantissa bits of 1024 (f16 0x6400):
+  // the f16 value 1024 + u, minus 1152 = q, all steps exact
+  const uint32_t v = w ^ 0x80808080u;
+  uint32_t a = __byte_perm(v, 0x64646464u, 0x4140u), b = __byte_perm(v, 0x64646464u, 0x4342u);
+  const __half2 bias = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));
+  const __half2 qa = __hsub2(*reinterpret_cast<__half2*>(&a), bias), qb = __hsub2(*reinterpret_cast<__half2*>(&b), bias);
+  lo = *reinterpret_cast<const uint32_t*>(&qa);
+  hi = *reinterpret_cast<const uint32_t*>(&qb);
+}
+template <>
+FMD_DEV void i8x4_to_act<__nv_bfloat16>(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  // biased bytes as the low mantissa bits of 2^23 (f32 0x4B000000): the f32
+  // value 2^23 + u, minus 2^23 + 128 = q exactly; bf16 packing of an integer
+  // of at most 7 bits is exact
+  const uint32_t v = w ^ 0x80808080u;
+  float f[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) f[i] = __int_as_float(__byte_perm(v, 0x4B000000u, 0x7440u | i)) - 8388736.f;
+  lo = Act<__nv_bfloat16>::pack2(f[0], f[1]);
+  hi = Act<__nv_bfloat16>::pack2(f[2], f[3]);
+}
+
+// d = a * b + 0 (the accumulator starts at zero: one block's partial sum)
+template <typename T>
+FMD_DEV void mma16816_z(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1);
+template <>
+FMD_DEV void mma16816_z<__nv_bfloat16>(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%10,%10,%10,%10};\n"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(0.f));
+}
+template <>
+FMD_DEV void mma16816_z<__half>(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%10,%10,%10,%10};\n"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(0.f));
+}
+
+// A fragments of the 4 MMAs of one 64-wide k-block.
+//  * Q8_0: MMA j covers block j >> 1, k 32 (j >> 1) + 8t + 4 (j & 1) + {0..3}
+//    for lane t (k16 fragment order: logical k 2t, 2t+1 -> the first two,
+//    2t+8, 2t+9 -> the last two), i.e. word j of the lane's 16 bytes;
+//  * 16-bit: MMA j covers k 16t + 4j + {0..3} (the same logical-to-physical
+//    k permutation as fmd_kernels.cu's k_linear).
+// The activation fragments use the same k permutation (gemv_xfrag).
 template <typename T, bool Q8>
 FMD_DEV void gemv_afrag(const WRegs& w, uint32_t (&af)[4][4]) {
   if constexpr (Q8) {
@@ -100,16 +163,8 @@ FMD_DEV void gemv_afrag(const WRegs& w, uint32_t (&af)[4][4]) {
     const uint32_t* ub = reinterpret_cast<const uint32_t*>(&w.b);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      float e[4], f[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        e[i] = (__int_as_float(__byte_perm(ua[j] ^ 0x80808080u, 0x4B000000u, 0x7440u | i)) - 8388736.f) * w.da;
-        f[i] = (__int_as_float(__byte_perm(ub[j] ^ 0x80808080u, 0x4B000000u, 0x7440u | i)) - 8388736.f) * w.db;
-      }
-      af[j][0] = Act<T>::pack2(e[0], e[1]);
-      af[j][1] = Act<T>::pack2(f[0], f[1]);
-      af[j][2] = Act<T>::pack2(e[2], e[3]);
-      af[j][3] = Act<T>::pack2(f[2], f[3]);
+      i8x4_to_act<T>(ua[j], af[j][0], af[j][2]);
+      i8x4_to_act<T>(ub[j], af[j][1], af[j][3]);
     }
   } else {
     const uint32_t* ua = reinterpret_cast<const uint32_t*>(&w.a);
@@ -125,6 +180,57 @@ FMD_DEV void gemv_afrag(const WRegs& w, uint32_t (&af)[4][4]) {
       af[j][1] = r1[(2 * j) & 3];
       af[j][3] = r1[(2 * j + 1) & 3];
     }
+  }
+}
+
+// One warp's fragment registers of a staged (k-block, warp) unit.
+template <bool Q8>
+FMD_DEV void gemv_wload(const uint8_t* u, int lane, WRegs& w) {
+  w.a = *reinterpret_cast<const int4*>(u + lane * 16);
+  w.b = *reinterpret_cast<const int4*>(u + 512 + lane * 16);
+  if constexpr (Q8) {
+    const int g = lane >> 2;
+    const uint32_t* sc = reinterpret_cast<const uint32_t*>(u + 1024);
+    w.sg = sc[g];
+    w.sh = sc[g + 8];
+  } else {
+    w.c = *reinterpret_cast<const int4*>(u + 1024 + lane * 16);
+    w.d = *reinterpret_cast<const int4*>(u + 1536 + lane * 16);
+  }
+}
+
+// The activation fragment words of one 8-row n-tile for a 64-wide k-block:
+// `xr` points at the lane's row (g) and k-block start.
+template <typename T, bool Q8>
+FMD_DEV void gemv_xfrag(const T* xr, int t, uint32_t (&xw)[8]) {
+  const int4 x0 = *reinterpret_cast<const int4*>(xr + (Q8 ? 8 * t : 16 * t));
+  const int4 x1 = *reinterpret_cast<const int4*>(xr + (Q8 ? 32 + 8 * t : 16 * t + 8));
+  xw[0] = (uint32_t)x0.x, xw[1] = (uint32_t)x0.y, xw[2] = (uint32_t)x0.z, xw[3] = (uint32_t)x0.w;
+  xw[4] = (uint32_t)x1.x, xw[5] = (uint32_t)x1.y, xw[6] = (uint32_t)x1.z, xw[7] = (uint32_t)x1.w;
+}
+
+// acc (16 features x 8 rows, the mma C layout) += W_kblock x X_kblock.
+// Q8_0: each 32-wide block's product of the exact int8 weights is summed on
+// its own and then scaled by the block's f16 scale in f32, i.e.
+// sum_b d_b * sum_{k in b} q_k x_k: the reference's dequantise-then-matmul
+// (q * d in f32) up to the f32 summation order.
+template <typename T, bool Q8>
+FMD_DEV void gemv_kblock(float (&acc)[4], const uint32_t (&af)[4][4], const uint32_t (&xw)[8], const WRegs& w) {
+  if constexpr (Q8) {
+    float t0[4], t1[4];
+    mma16816_z<T>(t0, af[0], xw[0], xw[1]);
+    mma16816<T>(t0, af[1], xw[2], xw[3]);
+    mma16816_z<T>(t1, af[2], xw[4], xw[5]);
+    mma16816<T>(t1, af[3], xw[6], xw[7]);
+    const float2 dg = __half22float2(*reinterpret_cast<const __half2*>(&w.sg));
+    const float2 dh = __half22float2(*reinterpret_cast<const __half2*>(&w.sh));
+    acc[0] = fmaf(dg.y, t1[0], fmaf(dg.x, t0[0], acc[0]));
+    acc[1] = fmaf(dg.y, t1[1], fmaf(dg.x, t0[1], acc[1]));
+    acc[2] = fmaf(dh.y, t1[2], fmaf(dh.x, t0[2], acc[2]));
+    acc[3] = fmaf(dh.y, t1[3], fmaf(dh.x, t0[3], acc[3]));
+  } else {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) mma16816<T>(acc, af[j], xw[2 * j], xw[2 * j + 1]);
   }
 }
 
@@ -148,8 +254,8 @@ __global__ void __launch_bounds__(FW * KG * 32) k_gemv(const T* __restrict__ x, 
   const int klen = K / S, kbeg = rank * klen, nkb = klen >> 6;
   const uint32_t kb_bytes = FW * UNIT;  // one k-block of the tile
   uint8_t* wsm = smem;                  // the CTA's weight tile
-  T* xs = reinterpret_cast<T*>(smem + ((nkb * kb_bytes + 127) & ~127u));  // [xrows][klen + 8]
-  const int xstride = klen + 8;
+  T* xs = reinterpret_cast<T*>(smem + ((nkb * kb_bytes + 127) & ~127u));  // [xrows][klen + pad]
+  const int xstride = klen + x_pad<Q8>();
   float* part = reinterpret_cast<float*>(xs);  // after the k-loop: [xrows][FT + 4]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int kgrp = warp / FW;     // this warp's k-blocks: kgrp, kgrp + KG, ...
@@ -312,28 +418,15 @@ __global__ void __launch_bounds__(FW * KG * 32) k_gemv(const T* __restrict__ x, 
       if (landed) {
         const uint8_t* u = wsm + kb * kb_bytes + (warp % FW) * UNIT;
         WRegs w;
-        w.a = *reinterpret_cast<const int4*>(u + lane * 16);
-        w.b = *reinterpret_cast<const int4*>(u + 512 + lane * 16);
-        if constexpr (Q8) {
-          const uint16_t* sc = reinterpret_cast<const uint16_t*>(u + 1024);
-          w.da = h2f_bits(sc[g * 2 + (t >> 1)]);
-          w.db = h2f_bits(sc[(g + 8) * 2 + (t >> 1)]);
-        } else {
-          w.c = *reinterpret_cast<const int4*>(u + 1024 + lane * 16);
-          w.d = *reinterpret_cast<const int4*>(u + 1536 + lane * 16);
-        }
+        gemv_wload<Q8>(u, lane, w);
         uint32_t af[4][4];
         gemv_afrag<T, Q8>(w, af);
 #pragma unroll
         for (int nt = 0; nt < 8; ++nt) {
           if (nt < n_tiles) {
-            const T* xr = xs + (size_t)(nt * 8 + g) * xstride + kb * 64 + 16 * t;
-            const int4 x0 = *reinterpret_cast<const int4*>(xr);
-            const int4 x1 = *reinterpret_cast<const int4*>(xr + 8);
-            const uint32_t xw[8] = {(uint32_t)x0.x, (uint32_t)x0.y, (uint32_t)x0.z, (uint32_t)x0.w,
-                                    (uint32_t)x1.x, (uint32_t)x1.y, (uint32_t)x1.z, (uint32_t)x1.w};
-#pragma unroll
-            for (int j = 0; j < 4; ++j) mma16816<T>(acc[nt], af[j], xw[2 * j], xw[2 * j + 1]);
+            uint32_t xw[8];
+            gemv_xfrag<T, Q8>(xs + (size_t)(nt * 8 + g) * xstride + kb * 64, t, xw);
+            gemv_kblock<T, Q8>(acc[nt], af, xw, w);
           }
         }
       }
@@ -572,8 +665,8 @@ __global__ void __launch_bounds__((G * kHeadWarps + 1) * 32, 1)
   const int n_tiles = W.N / FT;
   const int my_tiles = n_tiles > (int)blockIdx.x ? (n_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
   uint8_t* ring = smem;
-  T* xs = reinterpret_cast<T*>(smem + (size_t)stages * kStage);  // [xrows][K + 8]
-  const int xstride = K + 8;
+  T* xs = reinterpret_cast<T*>(smem + (size_t)stages * kStage);  // [xrows][K + pad]
+  const int xstride = K + x_pad<Q8>();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int grp = warp / kHeadWarps, fw = warp % kHeadWarps;
 
@@ -709,16 +802,7 @@ __global__ void __launch_bounds__((G * kHeadWarps + 1) * 32, 1)
       rp.next(SG);
       const uint8_t* un = ring + (size_t)st * kStage + fw * UNIT;
       WRegs w;
-      w.a = *reinterpret_cast<const int4*>(un + lane * 16);
-      w.b = *reinterpret_cast<const int4*>(un + 512 + lane * 16);
-      if constexpr (Q8) {
-        const uint16_t* sc = reinterpret_cast<const uint16_t*>(un + 1024);
-        w.da = h2f_bits(sc[g * 2 + (t >> 1)]);
-        w.db = h2f_bits(sc[(g + 8) * 2 + (t >> 1)]);
-      } else {
-        w.c = *reinterpret_cast<const int4*>(un + 1024 + lane * 16);
-        w.d = *reinterpret_cast<const int4*>(un + 1536 + lane * 16);
-      }
+      gemv_wload<Q8>(un, lane, w);
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[st]);  // this warp's fragments are in registers
       uint32_t af[4][4];
@@ -726,13 +810,9 @@ __global__ void __launch_bounds__((G * kHeadWarps + 1) * 32, 1)
 #pragma unroll
       for (int nt = 0; nt < NTL; ++nt) {
         if (nt < n_nt) {
-          const T* xr = xs + (size_t)(nt * 8 + g) * xstride + kb * 64 + 16 * t;
-          const int4 x0 = *reinterpret_cast<const int4*>(xr);
-          const int4 x1 = *reinterpret_cast<const int4*>(xr + 8);
-          const uint32_t xw[8] = {(uint32_t)x0.x, (uint32_t)x0.y, (uint32_t)x0.z, (uint32_t)x0.w,
-                                  (uint32_t)x1.x, (uint32_t)x1.y, (uint32_t)x1.z, (uint32_t)x1.w};
-#pragma unroll
-          for (int j = 0; j < 4; ++j) mma16816<T>(acc[nt], af[j], xw[2 * j], xw[2 * j + 1]);
+          uint32_t xw[8];
+          gemv_xfrag<T, Q8>(xs + (size_t)(nt * 8 + g) * xstride + kb * 64, t, xw);
+          gemv_kblock<T, Q8>(acc[nt], af, xw, w);
         }
       }
     }
@@ -873,7 +953,7 @@ __global__ void __launch_bounds__(256) k_pick_reduce(const int* __restrict__ n_s
 
 size_t gemv_smem_bytes(int FT, bool q8, int klen, int xrows) {
   const size_t w = ((size_t)(klen / 64) * (FT / 16) * (q8 ? kUnitQ8 : kUnitDense) + 127) & ~(size_t)127;
-  const size_t xb = (size_t)xrows * (klen + 8) * 2;
+  const size_t xb = (size_t)xrows * (klen + (q8 ? x_pad<true>() : x_pad<false>())) * 2;
   const size_t pb = (size_t)xrows * (FT + 4) * 4;
   return w + (xb > pb ? xb : pb);
 }
@@ -914,7 +994,7 @@ int launch_lm_head_t(const LinW& W, const void* x, int ldx, const int* row_map, 
   }
   constexpr int kTileRows = NTL * 8;
   const int xrows = ((max_rows < kTileRows ? max_rows : kTileRows) + 7) & ~7;
-  const size_t xbytes = (size_t)xrows * (W.K + 8) * sizeof(T);
+  const size_t xbytes = (size_t)xrows * (W.K + x_pad<Q8>()) * sizeof(T);
   const size_t stage = (size_t)kHeadWarps * (Q8 ? kUnitQ8 : kUnitDense);
   if (xbytes + 2 * stage > (size_t)kHeadSmemBudget) return 0;
   int stages = (int)((kHeadSmemBudget - xbytes) / stage);
@@ -997,8 +1077,12 @@ void gemv_pack(int epi, int N, int K, bool q8, const int8_t* qs, const uint16_t*
             const int g = lane >> 2, t = lane & 3;
             const size_t a = (size_t)(r0 + g) * K + k0 + 16 * t, b = a + (size_t)8 * K;
             if (q8) {
-              std::memcpy(u + lane * 16, qs + a, 16);
-              std::memcpy(u + 512 + lane * 16, qs + b, 16);
+              // k [8t, 8t + 8) of block 0, then k [32 + 8t, 32 + 8t + 8) of block 1
+              const size_t qa = (size_t)(r0 + g) * K + k0 + 8 * t, qb = qa + (size_t)8 * K;
+              std::memcpy(u + lane * 16, qs + qa, 8);
+              std::memcpy(u + lane * 16 + 8, qs + qa + 32, 8);
+              std::memcpy(u + 512 + lane * 16, qs + qb, 8);
+              std::memcpy(u + 512 + lane * 16 + 8, qs + qb + 32, 8);
             } else {
               std::memcpy(u + lane * 16, w + a, 16);
               std::memcpy(u + 512 + lane * 16, w + a + 8, 16);

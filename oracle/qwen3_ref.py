@@ -159,9 +159,20 @@ def build_mask(
     return m.unsqueeze(1)
 
 
+def _mm32(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    return a @ b
+
+
+def _mm64(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """The same product accumulated in f64 (then stored as f32): an equally
+    valid evaluation order, used to measure how far two correct
+    implementations drift apart through the rounding points."""
+    return (a.double() @ b.double()).float()
+
+
 def _grouped_attention(
     q: torch.Tensor, k_all: torch.Tensor, v_all: torch.Tensor, mask: torch.Tensor | None,
-    repeat: int, scale: float, act: _Act,
+    repeat: int, scale: float, act: _Act, mm=_mm32,
 ) -> torch.Tensor:
     """Grouped-query attention core of `Attention::forward` (qwen3.rs:240-257).
 
@@ -171,11 +182,11 @@ def _grouped_attention(
     b, heads, t, d = q.shape
     kv_heads = heads // repeat
     grouped = q.reshape(b, kv_heads, repeat * t, d)
-    scores = act.r(act.r(grouped @ k_all.transpose(-1, -2)) * scale)
+    scores = act.r(act.r(mm(grouped, k_all.transpose(-1, -2))) * scale)
     if mask is not None:
         scores = scores + mask
     probs = act.r(torch.softmax(scores, dim=-1))
-    ctx = act.r(probs @ v_all)
+    ctx = act.r(mm(probs, v_all))
     return ctx.reshape(b, kv_heads, repeat, t, d).permute(0, 3, 1, 2, 4).reshape(b, t, heads * d)
 
 
@@ -233,12 +244,17 @@ class Qwen3Ref:
 
     `weights` is the host weight dictionary produced by the synthetic
     generator (f32 "checkpoint" values, plus optional pre-quantised Q8_0
-    `(qs, d)` tensors under `weights["q8"]`).
+    `(qs, d)` tensors under `weights["q8"]`). `accumulate="f64"` evaluates
+    every matmul in f64 (same rounding points): the distance between the two
+    variants is the noise floor that any second implementation of the same
+    arithmetic inherits.
     """
 
-    def __init__(self, cfg: TextConfig, weights: dict, precision: str = "bf16", max_len: int = 65_536):
+    def __init__(self, cfg: TextConfig, weights: dict, precision: str = "bf16", max_len: int = 65_536,
+                 accumulate: str = "f32"):
         if precision not in ACT_DTYPES:
             raise ValueError(f"unknown precision {precision!r}")
+        self.mm = {"f32": _mm32, "f64": _mm64}[accumulate]
         self.cfg = cfg
         self.precision = precision
         self.act = _Act(ACT_DTYPES[precision])
@@ -310,8 +326,8 @@ class Qwen3Ref:
 
     def _attention(self, lw: LayerWeights, xs, cache: KvCache, offset: int, mask) -> torch.Tensor:
         """`Attention::forward` (qwen3.rs:203-259)."""
-        qkv = self.act.r(xs @ lw.qkv.T)  # FusedLinear::forward (linear.rs:85-95)
-        return self.act.r(self._context(lw, qkv, cache, offset, mask) @ lw.o.T)
+        qkv = self.act.r(self.mm(xs, lw.qkv.T))  # FusedLinear::forward (linear.rs:85-95)
+        return self.act.r(self.mm(self._context(lw, qkv, cache, offset, mask), lw.o.T))
 
     def _context(self, lw: LayerWeights, qkv, cache: KvCache, offset: int, mask) -> torch.Tensor:
         """The part of `Attention::forward` between the fused QKV projection and
@@ -330,14 +346,14 @@ class Qwen3Ref:
         q = rope_apply(q, cos, sin, a)
         k = rope_apply(k, cos, sin, a)
         k_all, v_all = cache.append(k, v)
-        return _grouped_attention(q, k_all, v_all, mask, c.kv_repeat, self.scale, a)
+        return _grouped_attention(q, k_all, v_all, mask, c.kv_repeat, self.scale, a, self.mm)
 
     def _mlp(self, lw: LayerWeights, xs) -> torch.Tensor:
         """`Mlp::forward` (qwen3.rs:288-292): down(silu(gate) * up)."""
         a, i = self.act, self.cfg.intermediate_size
-        gu = a.r(xs @ lw.gate_up.T)
+        gu = a.r(self.mm(xs, lw.gate_up.T))
         gated = a.r(torch.nn.functional.silu(gu[..., :i]))
-        return a.r(a.r(gated * gu[..., i:]) @ lw.down.T)
+        return a.r(self.mm(a.r(gated * gu[..., i:]), lw.down.T))
 
     def forward_embeds(self, embeds, caches: list[KvCache], offset: int, mask) -> torch.Tensor:
         """`Qwen3::forward_embeds` + `Layer::forward` (qwen3.rs:444-456, :322-339)."""
@@ -352,7 +368,7 @@ class Qwen3Ref:
 
     def logits(self, hidden) -> torch.Tensor:
         """`Qwen3::logits` (qwen3.rs:459-463): lm_head in the activation dtype, then f32."""
-        return self.act.r(hidden @ self.lm_head.T)
+        return self.act.r(self.mm(hidden, self.lm_head.T))
 
     # --- solo (ragged) mode: one sequence, positions 0..len ---------------------
 
@@ -395,10 +411,10 @@ class Qwen3Ref:
         a, c = self.act, self.cfg
         xs = self.embed([[int(t)] for t in tokens])
         for li, lw in enumerate(self.layers):
-            qkv = a.r(rms_norm(xs, lw.input_norm, c.rms_norm_eps, a) @ lw.qkv.T)
+            qkv = a.r(self.mm(rms_norm(xs, lw.input_norm, c.rms_norm_eps, a), lw.qkv.T))
             ctx = torch.cat([self._context(lw, qkv[i:i + 1], caches[i][li], caches[i][li].len, None)
                              for i in range(len(tokens))], 0)
-            xs = a.r(xs + a.r(ctx @ lw.o.T))
+            xs = a.r(xs + a.r(self.mm(ctx, lw.o.T)))
             xs = a.r(xs + self._mlp(lw, rms_norm(xs, lw.post_norm, c.rms_norm_eps, a)))
         return self.logits(rms_norm(xs, self.norm, c.rms_norm_eps, a))[:, 0]
 
