@@ -33,15 +33,20 @@ FMD_DEV float block_sum(float v, float* red) {
 // ---------------------------------------------------------------------------
 // Embedding gather (qwen3.rs:405-412) fused with layer 0's input RMSNorm
 // (linear.rs:293-302). Rows come from the token table or, for prompt rows,
-// from the prompt-embedding arena (the spliced audio/text embeddings).
+// from the prompt-embedding arena (the spliced audio/text embeddings). As the
+// first kernel of a decode step it also clears the step's synchronisation
+// counters (`zero`, `zero_n` ints) of the persistent layer-tail kernels.
 // ---------------------------------------------------------------------------
 template <typename T>
 __global__ void __launch_bounds__(128) k_embed_norm(Plan p, const T* __restrict__ table, const T* __restrict__ arena,
                                                     T* __restrict__ x, const T* __restrict__ w, T* __restrict__ xn,
-                                                    int H, float eps, float* __restrict__ ssq, int ssq_tiles) {
+                                                    int H, float eps, float* __restrict__ ssq, int ssq_tiles,
+                                                    int* __restrict__ zero, int zero_n) {
   __shared__ float red[4];
   griddep_launch();
   griddep_wait();
+  if (zero != nullptr)
+    for (int i = blockIdx.x * 128 + threadIdx.x; i < zero_n; i += gridDim.x * 128) zero[i] = 0;
   const int n_rows = p.counts->n_rows;
   for (int r = blockIdx.x; r < n_rows; r += gridDim.x) {
   const int tok = p.row_tok[r];
@@ -510,9 +515,9 @@ __global__ void k_dequant(LinW W, float* __restrict__ out) {
   } while (0)
 
 void launch_embed_norm(ActType at, const Plan& p, int R, const void* table, const void* arena, void* x, const void* w,
-                       void* xn, int H, float eps, float* ssq, int ssq_tiles, cudaStream_t s) {
+                       void* xn, int H, float eps, float* ssq, int ssq_tiles, cudaStream_t s, int* zero, int zero_n) {
   FMD_DISPATCH(at, launch_pdl(k_embed_norm<T>, R, 128, 0, s, p, (const T*)table, (const T*)arena, (T*)x, (const T*)w,
-                                                      (T*)xn, H, eps, ssq, ssq_tiles));
+                                                      (T*)xn, H, eps, ssq, ssq_tiles, zero, zero_n));
 }
 
 void launch_linear(ActType at, const LinW& W, const void* x, int ldx, const int* row_map, const int* n_rows_ptr,

@@ -143,6 +143,44 @@ struct GemvEpi {
   int* best_idx = nullptr;
 };
 
+// The persistent tail of a decode layer (fmd_chain.cu): o_proj (+ residual)
+// -> gate/up (post-attention RMSNorm, SwiGLU) -> down (+ residual) -> the next
+// layer's qkv (its input RMSNorm, q/k norm, RoPE, KV write) in one launch.
+// A phase is one projection in the decode-packed Q8_0 layout of the GEMV:
+// `ft`-feature tiles split `S` ways along K.
+struct ChainPhase {
+  const uint8_t* pk = nullptr;
+  int N = 0, K = 0, ft = 0, S = 0;
+};
+constexpr int kChainMaxRows = 64;    // decode rows the layer tail serves
+constexpr int kChainMaxTiles = 128;  // feature tiles of one phase
+constexpr int kChainSyncInts = 4 * kChainMaxTiles + 4;  // per layer: tile counters, then 3 grid barriers
+struct ChainArgs {
+  ChainPhase ph[4];            // o, gate_up, down, next layer's qkv
+  int n_phases = 4;            // 3 for the last layer (no qkv)
+  const int* n_rows_ptr = nullptr;
+  const void* ctx = nullptr;   // [rows][Hq x 128] attention output
+  void* x = nullptr;           // [rows][H] residual stream
+  void* h = nullptr;           // [rows][I] SwiGLU output
+  float* ssq = nullptr;        // [rows][ssq_tiles] per-64-feature sums of squares of x
+  int ssq_tiles = 0;
+  float eps = 0.f;
+  const void* post_norm = nullptr;  // this layer's post-attention norm
+  const void* in_norm = nullptr;    // the next layer's input norm, q_norm, k_norm
+  const void* qn_w = nullptr;
+  const void* kn_w = nullptr;
+  const void* cos = nullptr;
+  const void* sin = nullptr;
+  void* q_out = nullptr;
+  KvView kv{};
+  Plan plan{};
+  int layer = 0;               // the next layer (its KV cache is written)
+  int Hq = 0, Hkv = 0, H = 0, I = 0;
+  float* part = nullptr;       // f32 split-K partials [S][kChainMaxRows][N]
+  int* sync = nullptr;         // this layer's kChainSyncInts counters, zero at launch
+  int* status = nullptr;
+};
+
 // Device-side K split actually used for a pass with `n_rows` rows.
 __host__ __device__ inline int effective_split(int split, int n_rows) { return n_rows <= 64 ? split : 1; }
 
@@ -178,7 +216,8 @@ inline void launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
 // ---- launchers (fmd_kernels.cu) -------------------------------------------------
 // also writes ssq[row][0] = sum of squares of the row, ssq[row][1..tiles) = 0, when ssq != nullptr
 void launch_embed_norm(ActType at, const Plan& p, int R, const void* table, const void* arena, void* x, const void* w,
-                       void* xn, int H, float eps, float* ssq, int ssq_tiles, cudaStream_t s);
+                       void* xn, int H, float eps, float* ssq, int ssq_tiles, cudaStream_t s,
+                       int* zero = nullptr, int zero_n = 0);
 // `decode_only`: every pass through this launch has <= 64 rows, so the K
 // split is known before the plan is read and weights are prefetched early.
 void launch_linear(ActType at, const LinW& W, const void* x, int ldx, const int* row_map, const int* n_rows_ptr,
@@ -199,6 +238,12 @@ void launch_silu_mul(ActType at, const int* n_rows_ptr, int R, const float* part
 void launch_logits_argmax(ActType at, const int* n_sample_ptr, int B, const float* part, int V, float* logits,
                           int* next_ids, cudaStream_t s);
 void launch_dequant(ActType at, const LinW& W, float* out, cudaStream_t s);
+// fmd_chain.cu: shared-memory bytes of the layer tail on `n_sm` CTAs for
+// `max_rows` rows (0 when it does not fit), and its launch.
+size_t chain_smem_bytes(const ChainArgs& a, int n_sm, int max_rows);
+cudaError_t init_chain(size_t smem);
+int chain_blocks_per_sm(ActType at, size_t smem);
+void launch_layer_tail(ActType at, const ChainArgs& a, int n_sm, size_t smem, cudaStream_t s);
 // One bounded wait that runs out after `limit` tries and sets *status to
 // FMD_ETIMEDOUT (the failure path of every ring kernel's waits).
 void launch_wait_probe(uint32_t limit, int* status, cudaStream_t s);
@@ -246,13 +291,18 @@ void launch_attn_decode_tma(ActType at, const void* tmap, const Plan& p, int gri
 // W [N][K] 16-bit behind a TMA map with box {64, bn} and the 128-byte
 // swizzle; the output goes to out[split][rows][N] (f32).
 struct TcLinear {
-  alignas(64) CUtensorMap wmap;
+  alignas(64) CUtensorMap wmap;  // 16-bit [N][K] weights, or (q8) the int8 [N][K] Q8_0 quants
   int N = 0, K = 0, bn = 0, split = 1;
   bool ok = false;
+  bool q8 = false;
+  const uint16_t* d = nullptr;   // q8: f16 scales [N][K / 32]
 };
 cudaError_t init_gemm_tc();
 // Tile width and K split for an N x K projection (false: not supported).
 bool tc_plan(int N, int K, int* bn, int* split);
+// 2D map over a row-major int8 [outer][inner] matrix, box {64, box_outer}, no swizzle.
+bool tc_make_map_i8(void* encode_fn, CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer,
+                    uint32_t box_outer);
 // 2D map over a row-major [outer][inner] 16-bit matrix, box {64, box_outer}.
 bool tc_make_map(void* encode_fn, CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer,
                  uint32_t box_outer);

@@ -132,6 +132,14 @@ struct fmd_handle {
   bool tc_ready = false;
   void* tmap_encode = nullptr;      // cuTensorMapEncodeTiled
   int* attn_counters = nullptr;     // [max_slots][kv_heads] split-KV merge counters
+  // persistent layer tail (fmd_chain.cu) of decode steps: Q8_0 weights and
+  // at most kChainMaxRows rows; FMD_LAYER_TAIL=0 in the environment at
+  // fmd_create selects the per-projection GEMV launches instead
+  int n_sm = 0;
+  bool chain_allowed = true;
+  bool chain_ok = false;
+  size_t chain_smem = 0;
+  int* chain_sync = nullptr;        // [layers][kChainSyncInts], cleared by each decode step's first kernel
   int* d_status = nullptr;          // device-side error status (bounded waits)
   bool launch_refused = false;      // a decode projection could not be launched
   int* d_page_table = nullptr;
@@ -300,8 +308,26 @@ int tc_prepare(fmd_handle* h, const void* w16, int N, int K, TcLinear* tc) {
   return FMD_OK;
 }
 
-// `tc`: also build the tensor-core operand of mixed steps (the 16-bit [N][K]
-// matrix: the dense weights themselves, or the Q8_0 weights' expansion).
+// The same for Q8_0 weights: the GEMM reads the int8 [N][K] quants through
+// the map and their f16 scales directly, and dequantises in shared memory.
+int tc_prepare_q8(fmd_handle* h, const int8_t* qs, const uint16_t* d, int N, int K, TcLinear* tc) {
+  tc->N = N;
+  tc->K = K;
+  tc->ok = false;
+  if (!tc_plan(N, K, &tc->bn, &tc->split)) return FMD_OK;
+  void* fn;
+  int rc = tmap_encoder(h, &fn);
+  if (rc) return rc;
+  if (!tc_make_map_i8(fn, &tc->wmap, qs, (uint64_t)K, (uint64_t)N, (uint32_t)tc->bn))
+    return fail(h, FMD_EIO, "tensor map of a projection's Q8_0 weights could not be encoded");
+  tc->q8 = true;
+  tc->d = d;
+  tc->ok = true;
+  return FMD_OK;
+}
+
+// `tc`: also build the tensor-core operand of mixed steps (the dense 16-bit
+// [N][K] weights themselves, or the Q8_0 quants and scales).
 int upload_linear(fmd_handle* h, const std::vector<std::pair<const fmd_tensor*, int>>& parts, int K, LinW& W,
                   const char* what, int epi, bool interleave16 = false, bool row_major = true,
                   TcLinear* tc = nullptr) {
@@ -383,22 +409,7 @@ int upload_linear(fmd_handle* h, const std::vector<std::pair<const fmd_tensor*, 
     if ((rc = dev_alloc(h, pk.size(), &dp, &h->weight_bytes))) return rc;
     if ((rc = upload(h, dp, pk.data(), pk.size()))) return rc;
     W.pk = (const uint8_t*)dp;
-    if (tc) {
-      // dequantised values, rounded to the activation type as the kernels
-      // dequantise them (q * scale is exact in f32)
-      const bool bf = h->at == kBF16;
-      std::vector<uint16_t> wx((size_t)N * K);
-      for (size_t r = 0; r < (size_t)N; ++r)
-        for (int k = 0; k < K; ++k) {
-          const float d = f16_bits_to_f32(sc[r * (K / 32) + k / 32]);
-          const float v = (float)qs[r * K + k] * d;
-          wx[r * K + k] = bf ? f32_to_bf16_bits(v) : f32_to_f16_bits(v);
-        }
-      void* dw;
-      if ((rc = dev_alloc(h, wx.size() * 2, &dw, &h->weight_bytes))) return rc;
-      if ((rc = upload(h, dw, wx.data(), wx.size() * 2))) return rc;
-      if ((rc = tc_prepare(h, dw, N, K, tc))) return rc;
-    }
+    if (tc && (rc = tc_prepare_q8(h, W.qs, W.d, N, K, tc))) return rc;
   }
   // K split for passes with <= 64 rows: aim for >= ~2 CTAs per SM.
   int split = 1;
@@ -437,6 +448,49 @@ void trace(fmd_handle* h, const char* what, int layer) {
   std::fprintf(stderr, "[fmd] %-16s layer %3d  %8.3f ms  %s\n", what, layer, ms, cudaGetErrorString(e));
 }
 
+// The layer tail of layer l: its o, gate/up and down projections and, except
+// for the last layer, the next layer's qkv.
+ChainArgs make_chain(fmd_handle* h, int l) {
+  const fmd_config& c = h->cfg;
+  const LayerDev& L = h->layers[l];
+  const int H = c.hidden_size, I = c.intermediate_size, qd = h->Hq() * kHeadDim;
+  ChainArgs a;
+  a.ph[0] = ChainPhase{L.o.pk, H, qd, gemv_tile_features(kGemvResid), gemv_split(kGemvResid, qd)};
+  a.ph[1] = ChainPhase{L.gate_up.pk, 2 * I, H, gemv_tile_features(kGemvSwiglu), gemv_split(kGemvSwiglu, H)};
+  a.ph[2] = ChainPhase{L.down.pk, H, I, gemv_tile_features(kGemvResid), gemv_split(kGemvResid, I)};
+  const bool last = l + 1 >= c.num_hidden_layers;
+  a.n_phases = last ? 3 : 4;
+  if (!last) {
+    const LayerDev& Ln = h->layers[l + 1];
+    a.ph[3] = ChainPhase{Ln.qkv.pk, h->qkvN(), H, gemv_tile_features(kGemvQkv), gemv_split(kGemvQkv, H)};
+    a.in_norm = Ln.in_norm;
+    a.qn_w = Ln.q_norm;
+    a.kn_w = Ln.k_norm;
+    a.layer = l + 1;
+  }
+  a.n_rows_ptr = &h->plan.counts->n_rows;
+  a.ctx = h->ctx;
+  a.x = h->x;
+  a.h = h->hbuf;
+  a.ssq = h->ssq;
+  a.ssq_tiles = H / 64;
+  a.eps = c.rms_norm_eps;
+  a.post_norm = L.post_norm;
+  a.cos = h->rope_cos;
+  a.sin = h->rope_sin;
+  a.q_out = h->qbuf;
+  a.kv = h->kv;
+  a.plan = h->plan;
+  a.Hq = h->Hq();
+  a.Hkv = h->Hkv();
+  a.H = H;
+  a.I = I;
+  a.part = h->part;
+  a.sync = h->chain_sync ? h->chain_sync + (size_t)l * kChainSyncInts : nullptr;
+  a.status = h->d_status;
+  return a;
+}
+
 // ---- forward pass ------------------------------------------------------------------
 // Decode-only forward pass (every row is a one-token decode row): per layer
 // QKV (input norm folded in, q/k norm + RoPE + KV write fused) -> attention
@@ -452,8 +506,9 @@ void run_forward_decode(fmd_handle* h, float* logits_dev, const void* arena) {
   const int* nsamp = &h->plan.counts->n_sample;
   const float eps = c.rms_norm_eps;
   const int ssq_tiles = H / 64;
+  const int L = c.num_hidden_layers;
   launch_embed_norm(h->at, h->plan, row_grid, h->embed, arena, h->x, h->layers[0].in_norm, h->xn, H, eps, h->ssq,
-                    ssq_tiles, s);
+                    ssq_tiles, s, h->chain_ok ? h->chain_sync : nullptr, h->chain_ok ? L * kChainSyncInts : 0);
   trace(h, "embed_norm", -1);
   GemvEpi qkv;
   qkv.ssq = h->ssq;
@@ -473,26 +528,34 @@ void run_forward_decode(fmd_handle* h, float* logits_dev, const void* arena) {
   GemvEpi glu = qkv;
   glu.h = h->hbuf;
   glu.I = I;
-  for (int l = 0; l < c.num_hidden_layers; ++l) {
-    const LayerDev& L = h->layers[l];
-    qkv.norm_w = L.in_norm;
-    qkv.qn_w = L.q_norm;
-    qkv.kn_w = L.k_norm;
-    qkv.layer = l;
-    if (!launch_gemv(h->at, kGemvQkv, true, L.qkv, h->x, H, nullptr, nrows, R, qkv, h->d_status, s)) h->launch_refused = true;
-    trace(h, "qkv", l);
+  for (int l = 0; l < L; ++l) {
+    const LayerDev& Ly = h->layers[l];
+    if (l == 0 || !h->chain_ok) {
+      qkv.norm_w = Ly.in_norm;
+      qkv.qn_w = Ly.q_norm;
+      qkv.kn_w = Ly.k_norm;
+      qkv.layer = l;
+      if (!launch_gemv(h->at, kGemvQkv, true, Ly.qkv, h->x, H, nullptr, nrows, R, qkv, h->d_status, s)) h->launch_refused = true;
+      trace(h, "qkv", l);
+    }
     const bool probe = h->record_attn_events && l == h->attn_probe_layer();
     if (probe) cudaEventRecordWithFlags(h->attn_events[0], s, cudaEventRecordExternal);
     launch_attn_decode_tma(h->at, &h->kv_tmap, h->plan, h->di_grid, h->Hq(), h->Hkv(), h->qbuf, h->kv, l,
                            h->attn_scale, h->pacc, h->pml, h->attn_counters, h->ctx, h->d_status, s);
     if (probe) cudaEventRecordWithFlags(h->attn_events[1], s, cudaEventRecordExternal);
     trace(h, "attn_decode", l);
-    if (!launch_gemv(h->at, kGemvResid, false, L.o, h->ctx, h->Hq() * kHeadDim, nullptr, nrows, R, res, h->d_status, s)) h->launch_refused = true;
+    if (h->chain_ok) {
+      // o -> gate/up -> down -> the next layer's qkv in one persistent launch
+      launch_layer_tail(h->at, make_chain(h, l), h->n_sm, h->chain_smem, s);
+      trace(h, "layer_tail", l);
+      continue;
+    }
+    if (!launch_gemv(h->at, kGemvResid, false, Ly.o, h->ctx, h->Hq() * kHeadDim, nullptr, nrows, R, res, h->d_status, s)) h->launch_refused = true;
     trace(h, "o_proj", l);
-    glu.norm_w = L.post_norm;
-    if (!launch_gemv(h->at, kGemvSwiglu, true, L.gate_up, h->x, H, nullptr, nrows, R, glu, h->d_status, s)) h->launch_refused = true;
+    glu.norm_w = Ly.post_norm;
+    if (!launch_gemv(h->at, kGemvSwiglu, true, Ly.gate_up, h->x, H, nullptr, nrows, R, glu, h->d_status, s)) h->launch_refused = true;
     trace(h, "gate_up", l);
-    if (!launch_gemv(h->at, kGemvResid, false, L.down, h->hbuf, I, nullptr, nrows, R, res, h->d_status, s)) h->launch_refused = true;
+    if (!launch_gemv(h->at, kGemvResid, false, Ly.down, h->hbuf, I, nullptr, nrows, R, res, h->d_status, s)) h->launch_refused = true;
     trace(h, "down", l);
   }
   GemvEpi head = qkv;
@@ -789,6 +852,15 @@ int fmd_create(const fmd_config* cfg, int32_t precision, int32_t device, fmd_han
   h->at = (precision == FMD_PREC_BF16 || precision == FMD_PREC_INT8_BF16) ? kBF16 : kF16;
   h->device = device;
   h->attn_scale = (float)(1.0 / std::sqrt((double)cfg->head_dim));
+  {
+    const char* v = std::getenv("FMD_LAYER_TAIL");
+    h->chain_allowed = !(v != nullptr && v[0] == '0');
+  }
+  if (cudaDeviceGetAttribute(&h->n_sm, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || h->n_sm < 1) {
+    cudaGetLastError();
+    delete h;
+    return FMD_EIO;
+  }
   if (cudaSetDevice(device) != cudaSuccess || cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking) != cudaSuccess ||
       init_kernels() != cudaSuccess || init_attn_decode() != cudaSuccess || init_attn_prefill() != cudaSuccess || init_gemv() != cudaSuccess ||
       init_gemm_tc() != cudaSuccess) {
@@ -957,7 +1029,21 @@ int fmd_kv_reserve(fmd_handle* h, int32_t max_slots, int64_t max_tokens_total, i
   }
   const int Nmax = std::max({h->qkvN(), 2 * I, H});
   h->split_stride = (size_t)std::max(R, 64) * Nmax;
-  const size_t part_elems = std::max({h->split_stride * max_split, (size_t)max_slots * V});
+  size_t part_elems = std::max({h->split_stride * max_split, (size_t)max_slots * V});
+  // the persistent layer tail: Q8_0 weights, decode steps of <= 64 rows, one
+  // CTA per SM with the layer's weights resident in shared memory
+  h->chain_ok = false;
+  if (h->q8 && h->chain_allowed && max_slots <= kChainMaxRows && c.num_hidden_layers > 0) {
+    const ChainArgs a = make_chain(h, 0);
+    const size_t smem = chain_smem_bytes(a, h->n_sm, max_slots);
+    if (smem > 0 && smem <= 226 * 1024 && init_chain(smem) == cudaSuccess && chain_blocks_per_sm(h->at, smem) >= 1) {
+      h->chain_ok = true;
+      h->chain_smem = smem;
+      for (int p = 0; p < a.n_phases; ++p)
+        part_elems = std::max(part_elems, (size_t)a.ph[p].S * kChainMaxRows * a.ph[p].N);
+    }
+    cudaGetLastError();
+  }
   h->pb_max = R / kRowsPerPBlock + max_slots;
   h->di_max = (int)std::min<int64_t>((int64_t)max_slots * h->max_pages_per_slot,
                                      (int64_t)h->n_pages * kPageTokens / kDecodeItemTokens + 2 * max_slots + 1);
@@ -994,6 +1080,12 @@ int fmd_kv_reserve(fmd_handle* h, int32_t max_slots, int64_t max_tokens_total, i
   if ((rc = A(sizeof(int), &p))) return rc;
   CK(cudaMemset(p, 0, sizeof(int)));
   h->d_status = (int*)p;
+  if (h->chain_ok) {
+    const size_t n = (size_t)c.num_hidden_layers * kChainSyncInts * sizeof(int);
+    if ((rc = A(n, &p))) return rc;
+    CK(cudaMemset(p, 0, n));
+    h->chain_sync = (int*)p;
+  }
   h->layout.init(R, max_slots, h->pb_max, h->di_max);
   if ((rc = A(h->layout.total * 4, &p))) return rc;
   CK(cudaMemset(p, 0, h->layout.total * 4));

@@ -1,0 +1,65 @@
+"""The persistent layer tail of decode steps (fmd_chain.cu: o_proj -> gate/up
+-> down -> the next layer's qkv in one launch, one CTA per SM, grid
+barriers) against the oracle, next to the per-projection GEMV path it
+replaces (FMD_LAYER_TAIL=0 at handle creation selects that path).
+
+Both paths serve Q8_0 decode steps of up to 64 rows; they must each match
+the oracle's logits within 2e-2 (north_star) at the full layer widths, for
+batches that fill whole and partial 8-row MMA tiles, with every sequence at
+its own position (ragged, page edges), and with decode rows that are a subset
+of the open slots.
+"""
+
+from __future__ import annotations
+
+import importlib
+
+import numpy as np
+import pytest
+
+from conftest import PKG, mid_config, oracle_model, rel_err
+
+syn = importlib.import_module("fmd_b200.synthetic")
+pytestmark = pytest.mark.gpu
+
+LOGIT_RTOL = 2e-2
+
+
+@pytest.fixture(scope="module")
+def mid_w():
+    return syn.make_weights(mid_config(), seed=41, norm_jitter=0.2)
+
+
+@pytest.mark.parametrize("tail", ["1", "0"])
+@pytest.mark.parametrize("prec,n_seq", [("int8_bf16", 33), ("int8", 64), ("int8_bf16", 5)])
+def test_decode_steps_match_the_oracle_on_both_paths(tail, prec, n_seq, mid_w, monkeypatch):
+    from oracle import qwen3_ref as ref
+
+    monkeypatch.setenv("FMD_LAYER_TAIL", tail)
+    cfg = mid_config()
+    m = oracle_model(cfg, mid_w, prec, max_len=1024)
+    rng = np.random.default_rng(n_seq)
+    lens = [int(x) for x in rng.integers(1, 200, n_seq)]
+    lens[:3] = [1, 64, 65][: len(lens[:3])]  # a single-token prompt and page edges
+    prompts = [rng.standard_normal((n, cfg.hidden_size), dtype=np.float32) for n in lens]
+    with PKG.Qwen3Decoder(cfg, prec) as dec:
+        dec.load_weights(mid_w)
+        dec.reserve(max_slots=64, max_tokens=64 * 256, max_rows=512)
+        streams = [[int(t) for t in rng.integers(0, cfg.vocab_size, 3)] for _ in range(n_seq)]
+        # decode steps over all slots, then over every other slot only
+        for i in range(n_seq):
+            dec.open_slot(i, lens[i] + 4)
+        dec.prefill(list(range(n_seq)), prompts, want_logits=False)
+        caches = []
+        for p in prompts:
+            cs = m.new_caches(1, p.shape[0] + 4)
+            m.prefill(p[None], cs)
+            caches.append(cs)
+        for step in range(3):
+            live = list(range(n_seq)) if step < 2 else list(range(0, n_seq, 2))
+            got, ids = dec.decode_step(live, [streams[i][step] for i in live])
+            want = m.decode_step_ragged([streams[i][step] for i in live], [caches[i] for i in live]).numpy()
+            for j in range(len(live)):
+                err = rel_err(got[j], want[j])
+                assert err < LOGIT_RTOL, (tail, prec, step, live[j], err)
+                assert int(ids[j]) == int(np.argmax(got[j]))
