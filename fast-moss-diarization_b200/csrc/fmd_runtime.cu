@@ -174,6 +174,7 @@ struct fmd_handle {
   bool first_block = true;               // no counters polled since fmd_engine_start
   int64_t launched_mixed = 0;
   bool engine_started = false;
+  ProgressWatch watch{kEngineIdlePolls};  // polls without progress, over every fmd_engine_step call since the start
   bool record_attn_events = false;             // set while capturing the step graph
   // around the decode attention of one layer only: an event node between two
   // kernels of the graph removes their programmatic-dependent-launch overlap
@@ -1493,6 +1494,7 @@ int fmd_engine_start(fmd_handle* h, int32_t max_batch, int32_t prefill_chunk) {
     h->graph_chunk = prefill_chunk;
   }
   h->first_block = true;
+  h->watch = ProgressWatch(kEngineIdlePolls);
   h->engine_started = true;
   return FMD_OK;
 }
@@ -1510,7 +1512,7 @@ int fmd_engine_step(fmd_handle* h, int64_t max_steps, fmd_stats* stats) {
   const long long tokens0 = h->h_ctr->gen_tokens;
   bool finished = h->h_ctr->done >= h->eng_n_reqs;
   int64_t launched = 0;
-  ProgressWatch watch(kEngineIdlePolls);
+  ProgressWatch& watch = h->watch;
   CK(cudaEventRecord(h->win_begin, h->stream));
   int64_t mixed_launched = 0;
   while (!finished && launched < max_steps) {

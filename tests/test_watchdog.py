@@ -84,5 +84,8 @@ def test_progress_on_any_one_counter_counts(harness):
 def test_the_limit_is_the_engines(harness):
     """The runtime passes kEngineIdlePolls = 4 polls of 16 steps each."""
     src = (CSRC / "fmd_runtime.cu").read_text()
-    assert "constexpr int kEngineIdlePolls = 4;" in src and "ProgressWatch watch(kEngineIdlePolls);" in src
+    assert "constexpr int kEngineIdlePolls = 4;" in src and "ProgressWatch watch{kEngineIdlePolls};" in src
+    # one detector per handle, reset when the engine starts: polls of several
+    # short fmd_engine_step calls add up
+    assert "h->watch = ProgressWatch(kEngineIdlePolls);" in src and "ProgressWatch& watch = h->watch;" in src
     assert harness([(1, 1, 1)] * 3, limit=2) == 2
