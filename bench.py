@@ -369,9 +369,14 @@ def run_config4(args):
     eng.start(32, 2048)
     dec_rows = int(np.sum(wl.prompt_lens[:n_dec]))
     long_len = int(wl.prompt_lens[-1])
-    st = eng.step(8)
+    def advance(prev):
+        # the engine reports FMD_ETIMEDOUT after 4 polls without progress
+        # (over consecutive calls), so a stalled queue ends the run
+        return eng.step(16)
+
+    st = advance(None)
     while st.prefill_tokens < dec_rows + 2048:  # decoders running, long prefill under way (warm-up)
-        st = eng.step(8)
+        st = advance(st)
     clocks = ClockSampler(0)
     clocks.start()
     t_ms = p_rows = d_tok = steps = mixed = 0
@@ -379,7 +384,7 @@ def run_config4(args):
     p0 = st.prefill_tokens
     while st.prefill_tokens < dec_rows + 8 * long_len:
         before = st.prefill_tokens
-        st = eng.step(8)
+        st = advance(st)
         t_ms += st.window_device_ms
         d_tok += st.window_tokens
         steps += st.window_steps

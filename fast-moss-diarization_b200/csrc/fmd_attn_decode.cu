@@ -47,7 +47,6 @@ constexpr int kRedStride = 130;    // 128 dims + m + l
 constexpr int kQBytes = 512;       // query rows of the two heads of a kv head (2 x 128 x 2 bytes)
 constexpr int kMaxRows = 256;      // decode rows per pass (the slot limit)
 constexpr uint32_t kWaitLimit = 1u << 22;
-constexpr int kStatusTimeout = -110;
 
 FMD_DEV uint32_t swz(int row, int chunk) {
   // byte offset of 16-byte `chunk` (0..15) of tile row `row` under the TMA
@@ -179,7 +178,7 @@ __global__ void __launch_bounds__(160, 2)
       }
     }
     if (!ok && lane == 0) {
-      atomicExch(status, kStatusTimeout);
+      report_timeout(status, kSiteAttnDecode);
       // let the copies already issued land before the CTA can retire (bounded)
       for (int i = issued > kStages ? issued - kStages : 0; i < issued; ++i)
         mbar_wait_bounded(&full[i % kStages], (i / kStages) & 1, kWaitLimit);
@@ -358,7 +357,7 @@ __global__ void __launch_bounds__(160, 2)
       }
     }
   }
-  if (aborted && tid == 0) atomicExch(status, kStatusTimeout);
+  if (aborted && tid == 0) report_timeout(status, kSiteAttnDecode);
 }
 
 }  // namespace

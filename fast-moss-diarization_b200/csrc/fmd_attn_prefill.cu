@@ -44,7 +44,6 @@ constexpr int kPfKvBytes = 32768;  // K (16 KB) + V (16 KB) of one 64-position p
 constexpr int kPfPBytes = 16384;   // one P buffer: 128 rows x 64 keys x 2 bytes (two buffers)
 constexpr int kPfBox = 8192;       // one 64 x 64 TMA box
 constexpr uint32_t kPfWaitLimit = 1u << 24;
-constexpr int kPfStatusTimeout = -110;
 constexpr int kPfTmemCols = 256;   // S0 [0, 64), S1 [64, 128), O [128, 256)
 constexpr float kPfRescale = 8.f;  // log2 headroom before the reference maximum moves
 
@@ -331,7 +330,7 @@ __global__ void __launch_bounds__(192, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (threadIdx.x == 0 && abort_s) atomicExch(status, kPfStatusTimeout);
+  if (threadIdx.x == 0 && abort_s) report_timeout(status, kSiteAttnPrefill);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, kPfTmemCols);

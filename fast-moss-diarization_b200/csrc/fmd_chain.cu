@@ -50,7 +50,6 @@ constexpr int kWarps = kThreads / 32;
 constexpr int kMaxUnits = 16;  // weight units (bulk copies) one CTA may own over the four phases
 constexpr uint32_t kWaitLimit = 1u << 22;
 constexpr uint32_t kSpinLimit = 1u << 17;  // polls of a global counter (each after a short sleep): ~0.1 s
-constexpr int kStatusTimeout = -110;
 
 struct Geom {
   int T, S, ft, fw, klen, nkb, U;
@@ -81,23 +80,41 @@ FMD_DEV int ld_acquire(const int* p) {
   asm volatile("ld.acquire.gpu.global.s32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+// Add with release semantics: every write this thread has observed (the
+// CTA's writes, after a __syncthreads) is visible before the count.
+FMD_DEV void red_release(int* p, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
+}
+FMD_DEV int atom_add_acq_rel(int* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;\n" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
 
 // Thread 0 polls *p until it reaches `target` (bounded); false if it gave up.
 FMD_DEV bool spin_until(const int* p, int target) {
+  const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 0; i < kSpinLimit; ++i) {
     if (ld_acquire(p) >= target) return true;
-    __nanosleep(64);
+    if ((i & 63) == 63 && globaltimer_ns() - t0 > kWaitNsCap) return false;
+    __nanosleep(32);
   }
   return false;
 }
 
 // All CTAs of the grid: every write before it is visible to every CTA after.
+// Two levels, so that no address takes more than ~16 atomics: CTA c counts
+// on group counter c % 16; the last arrival of a group counts on the top
+// counter, which every CTA then polls. `bar` holds 17 counters.
+constexpr int kBarGroups = 16;
 FMD_DEV void grid_barrier(int* bar, int* status) {
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence();
-    atomicAdd(bar, 1);
-    if (!spin_until(bar, (int)gridDim.x)) atomicExch(status, kStatusTimeout);
+    const int grp = blockIdx.x % kBarGroups;
+    const int members = ((int)gridDim.x - grp + kBarGroups - 1) / kBarGroups;
+    const int groups = min((int)gridDim.x, kBarGroups);
+    if (atom_add_acq_rel(bar + 1 + grp, 1) == members - 1) red_release(bar, 1);
+    if (!spin_until(bar, groups)) report_timeout(status, kSiteLayerTail);
   }
   __syncthreads();
 }
@@ -160,7 +177,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_layer_tail(ChainArgs a) {
   const int n_rows = min(*a.n_rows_ptr, kChainMaxRows);
   const int n_nt = (n_rows + 7) >> 3;
   bool ok = true;
-  int* const bars = a.sync + 4 * kChainMaxTiles;
+  int* const bars = a.sync + 4 * kChainMaxTiles;  // 3 barriers of 1 + kBarGroups counters
 
   for (int p = 0; p < np; ++p) {
     const Geom q = geom_of(a.ph[p]);
@@ -187,10 +204,18 @@ __global__ void __launch_bounds__(kThreads, 1) k_layer_tail(ChainArgs a) {
       cp_async_commit();
       if (norm_w != nullptr) {
         // rsqrt(mean(x^2) + eps) from the per-64-feature sums of squares the
-        // residual epilogues wrote
+        // residual epilogues wrote: a row's 16 partials in flight together,
+        // summed in order
         for (int r = threadIdx.x; r < n_rows; r += kThreads) {
+          const float* sp = a.ssq + (size_t)r * a.ssq_tiles;
           float ss = 0.f;
-          for (int i = 0; i < a.ssq_tiles; ++i) ss += __ldcg(a.ssq + (size_t)r * a.ssq_tiles + i);
+          for (int i0 = 0; i0 < a.ssq_tiles; i0 += 16) {
+            float v[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] = i0 + i < a.ssq_tiles ? __ldcg(sp + i0 + i) : 0.f;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) ss += v[i];
+          }
           rs_s[r] = rsqrtf(ss / a.H + a.eps);
         }
       }
@@ -266,39 +291,60 @@ __global__ void __launch_bounds__(kThreads, 1) k_layer_tail(ChainArgs a) {
         }
       }
       __syncthreads();
-      if (threadIdx.x == 0) {
-        __threadfence();  // the partials before the count (release)
-        for (int u = u0; u < u1; ++u) atomicAdd(ctr + u % q.T, 1);
-      }
+      if (threadIdx.x == 0)  // the CTA's partials before the counts
+        for (int u = u0; u < u1; ++u) red_release(ctr + u % q.T, 1);
     }
 
-    // ---- reduction + epilogue: unit (tile, s) finishes rows r = s (mod S)
-    for (int u = u0; u < u1 && n_rows > 0; ++u) {
-      const int tile = u % q.T, s = u / q.T;
+    // ---- reduction + epilogue: unit (tile, s) finishes rows r = s (mod S).
+    // One poll over the tile counters of all of this CTA's units, then every
+    // (unit, row) pair on its own warp, all in parallel.
+    if (u1 > u0 && n_rows > 0) {
       __shared__ int wait_ok;
-      if (threadIdx.x == 0) wait_ok = spin_until(ctr + tile, q.S);
+      if (threadIdx.x == 0) {
+        bool all = true;
+        const uint64_t t0 = globaltimer_ns();
+        for (uint32_t it = 0;; ++it) {
+          all = true;
+          for (int u = u0; u < u1; ++u) all &= ld_acquire(ctr + u % q.T) >= q.S;
+          if (all || it >= kSpinLimit || ((it & 63) == 63 && globaltimer_ns() - t0 > kWaitNsCap)) break;
+          __nanosleep(32);
+        }
+        wait_ok = all;
+      }
       __syncthreads();
       if (!wait_ok) ok = false;
-      for (int r = s + q.S * warp; r < n_rows; r += q.S * kWarps) {
+      const int rows_per = (n_rows + q.S - 1) / q.S;  // rows of residue s: s, s + S, ...
+      const int n_work = (u1 - u0) * rows_per;
+      for (int wi = warp; wi < n_work; wi += kWarps) {
+        const int u = u0 + wi / rows_per, tile = u % q.T, s = u / q.T;
+        const int r = s + q.S * (wi % rows_per);
+        if (r >= n_rows) continue;
         float v[4] = {0.f, 0.f, 0.f, 0.f};
         const float* pr = a.part + (size_t)r * N + tile * q.ft;
+        T* xr = reinterpret_cast<T*>(a.x) + (size_t)r * a.H + tile * 64 + lane * 2;
+        float2 xo = make_float2(0.f, 0.f);
+        if (p == 0 || p == 2) xo = ldcg_act2(xr);  // in flight with the partials
         if (q.ft == 128) {
-          for (int sp = 0; sp < q.S; ++sp) {
-            const float4 z = ldcg_f4(pr + (size_t)sp * kChainMaxRows * N + lane * 4);
-            v[0] += z.x, v[1] += z.y, v[2] += z.z, v[3] += z.w;
-          }
+          float4 z[8];
+#pragma unroll
+          for (int sp = 0; sp < 8; ++sp)
+            if (sp < q.S) z[sp] = ldcg_f4(pr + (size_t)sp * kChainMaxRows * N + lane * 4);
+#pragma unroll
+          for (int sp = 0; sp < 8; ++sp)
+            if (sp < q.S) v[0] += z[sp].x, v[1] += z[sp].y, v[2] += z[sp].z, v[3] += z[sp].w;
         } else {
-          for (int sp = 0; sp < q.S; ++sp) {
-            const float2 z = ldcg_f2(pr + (size_t)sp * kChainMaxRows * N + lane * 2);
-            v[0] += z.x, v[1] += z.y;
-          }
+          float2 z[8];
+#pragma unroll
+          for (int sp = 0; sp < 8; ++sp)
+            if (sp < q.S) z[sp] = ldcg_f2(pr + (size_t)sp * kChainMaxRows * N + lane * 2);
+#pragma unroll
+          for (int sp = 0; sp < 8; ++sp)
+            if (sp < q.S) v[0] += z[sp].x, v[1] += z[sp].y;
         }
 #pragma unroll
         for (int i = 0; i < 4; ++i) v[i] = rnd<T>(v[i]);
         if (p == 0 || p == 2) {
           // x <- rnd(x + rnd(y)) and the tile's sum of squares of the new x
-          T* xr = reinterpret_cast<T*>(a.x) + (size_t)r * a.H + tile * 64 + lane * 2;
-          const float2 xo = ldcg_act2(xr);
           const float n0 = rnd<T>(xo.x + v[0]), n1 = rnd<T>(xo.y + v[1]);
           *reinterpret_cast<uint32_t*>(xr) = Act<T>::pack2(n0, n1);
           const float ss = warp_sum(n0 * n0 + n1 * n1);
@@ -350,14 +396,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_layer_tail(ChainArgs a) {
         }
       }
     }
-    if (p + 1 < np) grid_barrier(bars + p, a.status);
+    if (p + 1 < np) grid_barrier(bars + p * (1 + kBarGroups), a.status);
   }
-  if (!ok && threadIdx.x == 0) atomicExch(a.status, kStatusTimeout);
+  if (!ok && threadIdx.x == 0) report_timeout(a.status, kSiteLayerTail);
   // no copy may still be landing when the CTA's shared memory is released
   // (units whose tasks were skipped: no rows, or a wait that gave up)
   if (threadIdx.x == 0)
     for (int i = 0; i < nunits; ++i)
-      if (!mbar_wait_bounded(&wbar[i], 0, kWaitLimit)) atomicExch(a.status, kStatusTimeout);
+      if (!mbar_wait_bounded(&wbar[i], 0, kWaitLimit)) report_timeout(a.status, kSiteLayerTail);
 }
 
 }  // namespace

@@ -142,11 +142,41 @@ FMD_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait: returns false if the phase did not complete within `limit` polls.
+// Nanosecond wall clock of the GPU.
+FMD_DEV uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
+  return t;
+}
+// Wall-time cap of every bounded wait: far beyond any wait of a healthy
+// launch (a whole decode step takes a few ms), short enough that a wait
+// which can never complete surfaces as FMD_ETIMEDOUT within about a second.
+constexpr uint64_t kWaitNsCap = 500ull * 1000 * 1000;
+// Bounded wait: returns false if the phase did not complete within `limit`
+// polls or kWaitNsCap of wall time, whichever comes first.
 FMD_DEV bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint32_t limit) {
-  for (uint32_t i = 0; i < limit; ++i)
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1; i < limit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 63) == 0 && globaltimer_ns() - t0 > kWaitNsCap) return false;
+  }
   return false;
+}
+// Which kernel's wait gave up, recorded next to the status word (status[1],
+// first writer wins) so that the host can name it.
+enum TimeoutSite {
+  kSiteGemv = 1,
+  kSiteLmHead = 2,
+  kSiteAttnDecode = 3,
+  kSiteAttnPrefill = 4,
+  kSiteGemmTc = 5,
+  kSiteLayerTail = 6,
+  kSiteWaitProbe = 7,
+};
+FMD_DEV void report_timeout(int* status, int site) {
+  atomicExch(status, -110);  // FMD_ETIMEDOUT
+  atomicCAS(status + 1, 0, site);
 }
 // 2D tiled TMA load global -> shared, completion counted on `bar` (no multicast).
 FMD_DEV void tma_load_2d(void* dst, const void* tmap, int x, int y, uint64_t* bar) {

@@ -35,7 +35,6 @@ namespace {
 constexpr int kTcBM = 128;  // rows per tile (MMA M)
 constexpr int kTcBK = 64;   // 64 16-bit values = one 128-byte swizzle row
 constexpr uint32_t kTcWaitLimit = 1u << 24;
-constexpr int kTcStatusTimeout = -110;
 
 // One converter lane's 16 int8 weights (16 bytes) times their block scale,
 // rounded to the activation type: 8 packed words, k order preserved.
@@ -200,7 +199,7 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
   }
-  if (!ok) atomicExch(status, kTcStatusTimeout);
+  if (!ok) report_timeout(status, kSiteGemmTc);
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {

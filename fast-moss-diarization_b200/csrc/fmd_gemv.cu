@@ -52,7 +52,6 @@ namespace {
 constexpr int kRows = 64;   // rows per row tile (decode steps carry one row per sequence)
 constexpr int kMaxKb = 16;  // 64-wide k-blocks per CTA (K / S <= 1024)
 constexpr uint32_t kWaitLimit = 1u << 22;
-constexpr int kStatusTimeout = -110;
 constexpr int kStatusNonFinite = -5;  // FMD_EIO: a greedy pick saw no finite logit
 
 // KG warp groups split a CTA's k-blocks (KG = 2 only where the grid leaves
@@ -221,7 +220,7 @@ __global__ void __launch_bounds__(FW * KG * 32) k_gemv(const T* __restrict__ x, 
     cp_async_wait<0>();
     bool ok = true;
     for (int kb = 0; kb < nkb; ++kb) ok &= mbar_wait_bounded(&wbar[kb], 0, kWaitLimit);
-    if (!ok) atomicExch(status, kStatusTimeout);
+    if (!ok) report_timeout(status, kSiteGemv);
     return;
   }
 
@@ -253,7 +252,7 @@ __global__ void __launch_bounds__(FW * KG * 32) k_gemv(const T* __restrict__ x, 
       }
     }
   }
-  if (!ok) atomicExch(status, kStatusTimeout);
+  if (!ok) report_timeout(status, kSiteGemv);
   __syncthreads();  // the activation tile is dead: `part` reuses it
 
   // ---- partial tile -> shared memory (k-block group 1, then group 0 adds
@@ -665,7 +664,7 @@ __global__ void __launch_bounds__((G * kHeadWarps + 1) * 32, 1)
       }
     }
   }
-  if (!ok && threadIdx.x == 0) atomicExch(status, kStatusTimeout);
+  if (!ok && threadIdx.x == 0) report_timeout(status, kSiteLmHead);
 
   // ---- per-row best over this CTA's tiles: lanes of equal t, then warps
 #pragma unroll

@@ -566,7 +566,7 @@ __global__ void k_wait_probe(uint32_t limit, int* __restrict__ status) {
   if (threadIdx.x == 0) {
     mbar_init(&bar, 1);
     fence_barrier_init();
-    if (!mbar_wait_bounded(&bar, 0, limit)) atomicExch(status, -110);  // FMD_ETIMEDOUT
+    if (!mbar_wait_bounded(&bar, 0, limit)) report_timeout(status, kSiteWaitProbe);
   }
 }
 

@@ -154,7 +154,7 @@ struct ChainPhase {
 };
 constexpr int kChainMaxRows = 64;    // decode rows the layer tail serves
 constexpr int kChainMaxTiles = 128;  // feature tiles of one phase
-constexpr int kChainSyncInts = 4 * kChainMaxTiles + 4;  // per layer: tile counters, then 3 grid barriers
+constexpr int kChainSyncInts = 4 * kChainMaxTiles + 3 * 17;  // per layer: tile counters, then 3 two-level grid barriers
 struct ChainArgs {
   ChainPhase ph[4];            // o, gate_up, down, next layer's qkv
   int n_phases = 4;            // 3 for the last layer (no qkv)

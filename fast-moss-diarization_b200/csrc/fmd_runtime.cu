@@ -735,13 +735,17 @@ int sync_check(fmd_handle* h) {
   e = cudaGetLastError();
   if (e != cudaSuccess) return fail(h, FMD_EIO, std::string("launch error: ") + cudaGetErrorString(e));
   if (h->d_status) {
-    int st = 0;
-    e = cudaMemcpy(&st, h->d_status, sizeof(int), cudaMemcpyDeviceToHost);
+    int st[2] = {0, 0};
+    e = cudaMemcpy(st, h->d_status, 2 * sizeof(int), cudaMemcpyDeviceToHost);
     if (e != cudaSuccess) return fail(h, FMD_EIO, std::string("status read: ") + cudaGetErrorString(e));
-    if (st != 0) {
-      cudaMemset(h->d_status, 0, sizeof(int));
-      return fail(h, st, st == FMD_EIO ? std::string("a greedy pick found no finite logit (non-finite activations)")
-                                       : "a bounded device-side wait gave up (status " + std::to_string(st) + ")");
+    if (st[0] != 0) {
+      cudaMemset(h->d_status, 0, 2 * sizeof(int));
+      static const char* const kSites[] = {"?", "k_gemv", "k_lm_head", "k_attn_decode_tma", "k_attn_prefill_tc",
+                                           "k_gemm_tc", "k_layer_tail", "k_wait_probe"};
+      const char* site = st[1] >= 1 && st[1] <= 7 ? kSites[st[1]] : "?";
+      return fail(h, st[0], st[0] == FMD_EIO ? std::string("a greedy pick found no finite logit (non-finite activations)")
+                                             : "a bounded device-side wait gave up in " + std::string(site) +
+                                                   " (status " + std::to_string(st[0]) + ")");
     }
   }
   return FMD_OK;
@@ -1078,8 +1082,9 @@ int fmd_kv_reserve(fmd_handle* h, int32_t max_slots, int64_t max_tokens_total, i
   if ((rc = A((size_t)max_slots * c.num_key_value_heads * 4, &p))) return rc;
   CK(cudaMemset(p, 0, (size_t)max_slots * c.num_key_value_heads * 4));
   h->attn_counters = (int*)p;
-  if ((rc = A(sizeof(int), &p))) return rc;
-  CK(cudaMemset(p, 0, sizeof(int)));
+  // status word, then the site of the first wait that gave up (TimeoutSite)
+  if ((rc = A(4 * sizeof(int), &p))) return rc;
+  CK(cudaMemset(p, 0, 4 * sizeof(int)));
   h->d_status = (int*)p;
   if (h->chain_ok) {
     const size_t n = (size_t)c.num_hidden_layers * kChainSyncInts * sizeof(int);

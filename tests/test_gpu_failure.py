@@ -37,7 +37,7 @@ def test_a_wait_that_runs_out_reports_etimedout_and_the_handle_stays_usable():
             with pytest.raises(PKG.FmdError) as e:
                 dec.debug_wait_timeout(1000)
             assert e.value.status == PKG._lib.FMD_ETIMEDOUT
-            assert "wait" in str(e.value)
+            assert "wait gave up in k_wait_probe" in str(e.value)
         lg, _ = dec.prefill([0], [prompt])
         caches = m.new_caches(1, 128)
         want = m.logits(m.prefill(prompt[None], caches))[0, 0].numpy()
