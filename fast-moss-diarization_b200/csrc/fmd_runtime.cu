@@ -133,10 +133,12 @@ struct fmd_handle {
   void* tmap_encode = nullptr;      // cuTensorMapEncodeTiled
   int* attn_counters = nullptr;     // [max_slots][kv_heads] split-KV merge counters
   // persistent layer tail (fmd_chain.cu) of decode steps: Q8_0 weights and
-  // at most kChainMaxRows rows; FMD_LAYER_TAIL=0 in the environment at
-  // fmd_create selects the per-projection GEMV launches instead
+  // at most kChainMaxRows rows, opt-in with FMD_LAYER_TAIL=1 in the
+  // environment at fmd_create. Measured slower than the per-projection GEMV
+  // launches on B200 (each of its ~10 dependent global round trips per
+  // projection costs ~1 us), so the GEMVs are the default.
   int n_sm = 0;
-  bool chain_allowed = true;
+  bool chain_allowed = false;
   bool chain_ok = false;
   size_t chain_smem = 0;
   int* chain_sync = nullptr;        // [layers][kChainSyncInts], cleared by each decode step's first kernel
@@ -859,7 +861,7 @@ int fmd_create(const fmd_config* cfg, int32_t precision, int32_t device, fmd_han
   h->attn_scale = (float)(1.0 / std::sqrt((double)cfg->head_dim));
   {
     const char* v = std::getenv("FMD_LAYER_TAIL");
-    h->chain_allowed = !(v != nullptr && v[0] == '0');
+    h->chain_allowed = v != nullptr && v[0] == '1';
   }
   if (cudaDeviceGetAttribute(&h->n_sm, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || h->n_sm < 1) {
     cudaGetLastError();
@@ -1457,7 +1459,13 @@ int fmd_engine_start(fmd_handle* h, int32_t max_batch, int32_t prefill_chunk) {
     CK(cudaEventCreate(&h->win_begin));
     CK(cudaEventCreate(&h->win_end));
   }
-  if (!h->graph_exec || h->graph_batch != max_batch || h->graph_chunk != prefill_chunk) {
+  if (trace_enabled()) {
+    // launch tracing synchronises after every kernel, which a stream capture
+    // forbids: the traced engine launches each step's kernels directly
+    release_graph(h);
+    h->graph_batch = max_batch;
+    h->graph_chunk = prefill_chunk;
+  } else if (!h->graph_exec || h->graph_batch != max_batch || h->graph_chunk != prefill_chunk) {
     release_graph(h);
     // two step graphs: "M" may carry a prefill chunk (split-K projections),
     // "D" is decode-only (fused decode projections, no prefill attention)
@@ -1507,7 +1515,7 @@ int fmd_engine_start(fmd_handle* h, int32_t max_batch, int32_t prefill_chunk) {
 int fmd_engine_step(fmd_handle* h, int64_t max_steps, fmd_stats* stats) {
   int rc = check_ready(h);
   if (rc) return rc;
-  if (!h->engine_started || !h->graph_exec || !h->graph_dec)
+  if (!h->engine_started || (!trace_enabled() && (!h->graph_exec || !h->graph_dec)))
     return fail(h, FMD_EBUSY, "engine not started (fmd_engine_start)");
   if (max_steps < 0) return fail(h, FMD_EINVAL, "negative step count");
   CK(cudaSetDevice(h->device));
@@ -1528,7 +1536,16 @@ int fmd_engine_step(fmd_handle* h, int64_t max_steps, fmd_stats* stats) {
     int64_t n_m = k;
     if (!h->first_block)
       n_m = std::min<int64_t>(k, (h->h_ctr->pending_prefill + h->graph_chunk - 1) / h->graph_chunk);
-    for (int64_t i = 0; i < k; ++i) CK(cudaGraphLaunch(i < n_m ? h->graph_exec : h->graph_dec, h->stream));
+    for (int64_t i = 0; i < k; ++i) {
+      if (trace_enabled()) {
+        const EngineDev e = make_engine_dev(h, h->graph_batch, h->graph_chunk, i < n_m ? 1 : 0);
+        launch_schedule(e, h->stream);
+        trace(h, "schedule", -1);
+        run_forward(h, nullptr, h->eng_arena.p, i >= n_m);
+      } else {
+        CK(cudaGraphLaunch(i < n_m ? h->graph_exec : h->graph_dec, h->stream));
+      }
+    }
     launched += k;
     mixed_launched += n_m;
     h->first_block = false;
@@ -1556,7 +1573,7 @@ int fmd_engine_step(fmd_handle* h, int64_t max_steps, fmd_stats* stats) {
   float win_ms = 0.f;
   if (launched > 0) CK(cudaEventElapsedTime(&win_ms, h->win_begin, h->win_end));
   double attn_ms = 0.0;
-  if (launched > 0) {
+  if (launched > 0 && !trace_enabled()) {
     float ms = 0.f;
     CK(cudaEventElapsedTime(&ms, h->attn_events[0], h->attn_events[1]));
     attn_ms = ms;
