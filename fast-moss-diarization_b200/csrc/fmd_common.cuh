@@ -173,6 +173,7 @@ enum TimeoutSite {
   kSiteGemmTc = 5,
   kSiteLayerTail = 6,
   kSiteWaitProbe = 7,
+  kSiteProjTc = 8,
 };
 FMD_DEV void report_timeout(int* status, int site) {
   atomicExch(status, -110);  // FMD_ETIMEDOUT
@@ -266,6 +267,16 @@ FMD_DEV void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "memory");
 }
 FMD_DEV void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
+// 16 consecutive columns of this warp's 32 lanes (as tmem_ld32).
+FMD_DEV void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
 // Store 32 consecutive columns of this warp's 32 lanes (register i -> column
 // i of the thread's lane); tmem_st_wait() orders it before later tcgen05 work.
 FMD_DEV void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {

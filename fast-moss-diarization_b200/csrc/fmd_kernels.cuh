@@ -181,6 +181,23 @@ struct ChainArgs {
   int* status = nullptr;
 };
 
+// Epilogue of the persistent mixed-step projection GEMM (fmd_proj_tc.cu).
+enum ProjEpiKind { kProjF32 = 0, kProjQkv = 1, kProjSwiglu = 2 };
+struct ProjEpi {
+  float* out = nullptr;  // kProjF32: [rows][N]
+  Plan plan{};           // kProjQkv: row positions / slots, KV pages, norms, RoPE tables
+  KvView kv{};
+  const void* qn_w = nullptr;
+  const void* kn_w = nullptr;
+  const void* cos = nullptr;
+  const void* sin = nullptr;
+  void* q_out = nullptr;
+  int layer = 0, Hq = 0, Hkv = 0;
+  float eps = 0.f;
+  void* h = nullptr;     // kProjSwiglu: [rows][I]
+  int I = 0;
+};
+
 // Device-side K split actually used for a pass with `n_rows` rows.
 __host__ __device__ inline int effective_split(int split, int n_rows) { return n_rows <= 64 ? split : 1; }
 
@@ -309,5 +326,11 @@ bool tc_make_map(void* encode_fn, CUtensorMap* m, const void* base, uint64_t inn
 // false (nothing launched) if W has no tensor-core plan.
 bool launch_gemm_tc(ActType at, const CUtensorMap& amap, const TcLinear& W, const int* n_rows_ptr, int max_rows,
                     float* out, size_t split_stride, int* status, cudaStream_t s);
+cudaError_t init_proj_tc();
+// false (nothing launched) if the projection's tensor-core plan does not fit
+// the epilogue (qkv / gate-up: 256-feature tiles, f32 rows: 128).
+bool launch_proj_tc(ActType at, int epi, const CUtensorMap& amap, const TcLinear& W, const int* n_rows_ptr,
+                    int max_rows, const ProjEpi& ep, int n_sm, int* status, cudaStream_t s);
+
 
 }  // namespace fmd

@@ -138,6 +138,7 @@ struct fmd_handle {
   // launches on B200 (each of its ~10 dependent global round trips per
   // projection costs ~1 us), so the GEMVs are the default.
   int n_sm = 0;
+  bool proj_allowed = true;  // mixed steps on k_proj_tc (fused epilogues); FMD_PROJ_TC=0 selects k_gemm_tc
   bool chain_allowed = false;
   bool chain_ok = false;
   size_t chain_smem = 0;
@@ -297,11 +298,12 @@ int tmap_encoder(fmd_handle* h, void** fn) {
 
 // Tensor-core plan and weight map of one projection; a shape without a plan
 // keeps tc->ok false and mixed steps use k_linear for it.
-int tc_prepare(fmd_handle* h, const void* w16, int N, int K, TcLinear* tc) {
+int tc_prepare(fmd_handle* h, const void* w16, int N, int K, TcLinear* tc, int want_bn) {
   tc->N = N;
   tc->K = K;
   tc->ok = false;
   if (!tc_plan(N, K, &tc->bn, &tc->split)) return FMD_OK;
+  if (N % want_bn == 0) tc->bn = want_bn;
   void* fn;
   int rc = tmap_encoder(h, &fn);
   if (rc) return rc;
@@ -311,13 +313,19 @@ int tc_prepare(fmd_handle* h, const void* w16, int N, int K, TcLinear* tc) {
   return FMD_OK;
 }
 
+// Tile width of a projection on the persistent mixed-step GEMM: qkv and
+// gate/up fuse their epilogues over 256-feature tiles, o and down write f32
+// rows in 128-feature tiles.
+int proj_bn(int epi) { return (epi == kGemvQkv || epi == kGemvSwiglu) ? 256 : 128; }
+
 // The same for Q8_0 weights: the GEMM reads the int8 [N][K] quants through
 // the map and their f16 scales directly, and dequantises in shared memory.
-int tc_prepare_q8(fmd_handle* h, const int8_t* qs, const uint16_t* d, int N, int K, TcLinear* tc) {
+int tc_prepare_q8(fmd_handle* h, const int8_t* qs, const uint16_t* d, int N, int K, TcLinear* tc, int want_bn) {
   tc->N = N;
   tc->K = K;
   tc->ok = false;
   if (!tc_plan(N, K, &tc->bn, &tc->split)) return FMD_OK;
+  if (N % want_bn == 0) tc->bn = want_bn;
   void* fn;
   int rc = tmap_encoder(h, &fn);
   if (rc) return rc;
@@ -370,7 +378,7 @@ int upload_linear(fmd_handle* h, const std::vector<std::pair<const fmd_tensor*, 
     if ((rc = dev_alloc(h, pk.size(), &d, &h->weight_bytes))) return rc;
     if ((rc = upload(h, d, pk.data(), pk.size()))) return rc;
     W.pk = (const uint8_t*)d;
-    if (tc && (rc = tc_prepare(h, W.w, N, K, tc))) return rc;
+    if (tc && (rc = tc_prepare(h, W.w, N, K, tc, proj_bn(epi)))) return rc;
   } else {
     std::vector<int8_t> qs((size_t)N * K);
     std::vector<uint16_t> sc((size_t)N * (K / 32));
@@ -412,7 +420,7 @@ int upload_linear(fmd_handle* h, const std::vector<std::pair<const fmd_tensor*, 
     if ((rc = dev_alloc(h, pk.size(), &dp, &h->weight_bytes))) return rc;
     if ((rc = upload(h, dp, pk.data(), pk.size()))) return rc;
     W.pk = (const uint8_t*)dp;
-    if (tc && (rc = tc_prepare_q8(h, W.qs, W.d, N, K, tc))) return rc;
+    if (tc && (rc = tc_prepare_q8(h, W.qs, W.d, N, K, tc, proj_bn(epi)))) return rc;
   }
   // K split for passes with <= 64 rows: aim for >= ~2 CTAs per SM.
   int split = 1;
@@ -606,33 +614,66 @@ void run_forward(fmd_handle* h, float* logits_dev, const void* arena, bool decod
   launch_embed_norm(h->at, h->plan, row_grid, h->embed, arena, h->x, h->layers[0].in_norm, h->xn, H, eps, nullptr,
                     0, s);
   trace(h, "embed_norm", -1);
+  // the persistent projection GEMM with fused epilogues when the projection
+  // has a plan for it (k_gemm_tc + the split-K epilogue kernels otherwise)
+  const bool proj = h->tc_ready && h->proj_allowed;
+  auto run_proj = [&](const TcLinear& tc, const CUtensorMap& amap, int epi, const ProjEpi& ep) {
+    return proj && launch_proj_tc(h->at, epi, amap, tc, nrows, R, ep, h->n_sm, h->d_status, s);
+  };
+  ProjEpi pf32;
+  pf32.out = h->part;
   for (int l = 0; l < c.num_hidden_layers; ++l) {
     const LayerDev& L = h->layers[l];
-    const PartSplit sp_qkv = mixed_linear(h, L.qkv, L.tc_qkv, h->xn, h->amap_xn, H);
-    trace(h, "qkv", l);
-    launch_qkv_epilogue(h->at, h->plan, row_grid, h->part, sp_qkv, ss, h->Hq(), h->Hkv(), L.q_norm, L.k_norm,
-                        h->rope_cos, h->rope_sin, h->qbuf, h->kv, l, eps, s);
-    trace(h, "qkv_epi", l);
+    ProjEpi pq;
+    pq.plan = h->plan;
+    pq.kv = h->kv;
+    pq.qn_w = L.q_norm;
+    pq.kn_w = L.k_norm;
+    pq.cos = h->rope_cos;
+    pq.sin = h->rope_sin;
+    pq.q_out = h->qbuf;
+    pq.layer = l;
+    pq.Hq = h->Hq();
+    pq.Hkv = h->Hkv();
+    pq.eps = eps;
+    if (run_proj(L.tc_qkv, h->amap_xn, kProjQkv, pq)) {
+      trace(h, "qkv_proj", l);
+    } else {
+      const PartSplit sp_qkv = mixed_linear(h, L.qkv, L.tc_qkv, h->xn, h->amap_xn, H);
+      trace(h, "qkv", l);
+      launch_qkv_epilogue(h->at, h->plan, row_grid, h->part, sp_qkv, ss, h->Hq(), h->Hkv(), L.q_norm, L.k_norm,
+                          h->rope_cos, h->rope_sin, h->qbuf, h->kv, l, eps, s);
+      trace(h, "qkv_epi", l);
+    }
     const bool probe = h->record_attn_events && l == h->attn_probe_layer();
     if (probe) cudaEventRecordWithFlags(h->attn_events[0], s, cudaEventRecordExternal);
     launch_attn_decode_tma(h->at, &h->kv_tmap, h->plan, h->di_grid, h->Hq(), h->Hkv(), h->qbuf, h->kv, l,
                            h->attn_scale, h->pacc, h->pml, h->attn_counters, h->ctx, h->d_status, s);
     if (probe) cudaEventRecordWithFlags(h->attn_events[1], s, cudaEventRecordExternal);
     trace(h, "attn_decode", l);
-    if (!decode_only) {
-      launch_attn_prefill_tc(h->at, &h->kv_tmap, &h->qmap, h->plan, h->pb_max, h->Hq(), h->Hkv(), h->kv, l,
-                             h->attn_scale, h->ctx, h->d_status, s);
-      trace(h, "attn_prefill", l);
-    }
-    const PartSplit sp_o = mixed_linear(h, L.o, L.tc_o, h->ctx, h->amap_ctx, h->Hq() * kHeadDim);
+    launch_attn_prefill_tc(h->at, &h->kv_tmap, &h->qmap, h->plan, h->pb_max, h->Hq(), h->Hkv(), h->kv, l,
+                           h->attn_scale, h->ctx, h->d_status, s);
+    trace(h, "attn_prefill", l);
+    const PartSplit sp_o = run_proj(L.tc_o, h->amap_ctx, kProjF32, pf32)
+                               ? PartSplit{1, 1}
+                               : mixed_linear(h, L.o, L.tc_o, h->ctx, h->amap_ctx, h->Hq() * kHeadDim);
     trace(h, "o_proj", l);
     launch_residual_norm(h->at, nrows, row_grid, h->x, h->part, sp_o, ss, L.post_norm, h->xn, H, eps, s);
     trace(h, "res_norm1", l);
-    const PartSplit sp_gu = mixed_linear(h, L.gate_up, L.tc_gate_up, h->xn, h->amap_xn, H);
-    trace(h, "gate_up", l);
-    launch_silu_mul(h->at, nrows, row_grid, h->part, sp_gu, ss, I, h->hbuf, s);
-    trace(h, "silu", l);
-    const PartSplit sp_down = mixed_linear(h, L.down, L.tc_down, h->hbuf, h->amap_hbuf, I);
+    ProjEpi pg;
+    pg.h = h->hbuf;
+    pg.I = I;
+    if (run_proj(L.tc_gate_up, h->amap_xn, kProjSwiglu, pg)) {
+      trace(h, "gate_up_proj", l);
+    } else {
+      const PartSplit sp_gu = mixed_linear(h, L.gate_up, L.tc_gate_up, h->xn, h->amap_xn, H);
+      trace(h, "gate_up", l);
+      launch_silu_mul(h->at, nrows, row_grid, h->part, sp_gu, ss, I, h->hbuf, s);
+      trace(h, "silu", l);
+    }
+    const PartSplit sp_down = run_proj(L.tc_down, h->amap_hbuf, kProjF32, pf32)
+                                  ? PartSplit{1, 1}
+                                  : mixed_linear(h, L.down, L.tc_down, h->hbuf, h->amap_hbuf, I);
     trace(h, "down", l);
     const void* next_norm = l + 1 < c.num_hidden_layers ? h->layers[l + 1].in_norm : h->final_norm;
     launch_residual_norm(h->at, nrows, row_grid, h->x, h->part, sp_down, ss, next_norm, h->xn, H, eps, s);
@@ -862,6 +903,8 @@ int fmd_create(const fmd_config* cfg, int32_t precision, int32_t device, fmd_han
   {
     const char* v = std::getenv("FMD_LAYER_TAIL");
     h->chain_allowed = v != nullptr && v[0] == '1';
+    const char* p = std::getenv("FMD_PROJ_TC");
+    h->proj_allowed = !(p != nullptr && p[0] == '0');
   }
   if (cudaDeviceGetAttribute(&h->n_sm, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || h->n_sm < 1) {
     cudaGetLastError();
@@ -870,7 +913,7 @@ int fmd_create(const fmd_config* cfg, int32_t precision, int32_t device, fmd_han
   }
   if (cudaSetDevice(device) != cudaSuccess || cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking) != cudaSuccess ||
       init_kernels() != cudaSuccess || init_attn_decode() != cudaSuccess || init_attn_prefill() != cudaSuccess || init_gemv() != cudaSuccess ||
-      init_gemm_tc() != cudaSuccess) {
+      init_gemm_tc() != cudaSuccess || init_proj_tc() != cudaSuccess) {
     cudaGetLastError();
     delete h;
     return FMD_EIO;

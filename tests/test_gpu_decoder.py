@@ -223,18 +223,24 @@ def test_full_layer_shapes(prec):
             check_pick(int(nxt[0]), lg[0], want)
 
 
-def test_long_chunked_prefill_full_shapes():
+@pytest.mark.parametrize("proj", ["1", "0"])
+@pytest.mark.parametrize("prec", ["bf16", "int8_bf16"])
+def test_long_chunked_prefill_full_shapes(prec, proj, monkeypatch):
     """Chunked prefill at the BASELINE head shapes with histories past 2k
     positions (qwen3.rs:475-496): two sequences prefilled together in chunks of
     up to 1000 rows (tens of 64-row attention blocks per chunk, up to 41 key
-    pages per block), then a decode step; logits against the oracle."""
+    pages per block), then a decode step; logits against the oracle. Both
+    mixed-step GEMM paths: the persistent projection GEMM with fused qkv and
+    SwiGLU epilogues (default) and k_gemm_tc with the split-K epilogue kernels
+    (FMD_PROJ_TC=0), dense and Q8_0 weights."""
+    monkeypatch.setenv("FMD_PROJ_TC", proj)
     cfg = mid_config(num_hidden_layers=1)
     w = syn.make_weights(cfg, seed=23)
-    m = oracle_model(cfg, w, "bf16", max_len=4096)
+    m = oracle_model(cfg, w, prec, max_len=4096)
     rng = np.random.default_rng(9)
     lens = [2600, 1333]
     prompts = [rng.standard_normal((n, cfg.hidden_size), dtype=np.float32) for n in lens]
-    with make_decoder(cfg, w, "bf16", slots=2, tokens=8192, rows=2048) as dec:
+    with make_decoder(cfg, w, prec, slots=2, tokens=8192, rows=2048) as dec:
         for s, n in enumerate(lens):
             dec.open_slot(s, n + 8)
         done = [0, 0]
