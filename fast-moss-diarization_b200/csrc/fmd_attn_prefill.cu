@@ -227,10 +227,17 @@ __global__ void __launch_bounds__(192, 1)
     const uint32_t lane_addr = tmem + ((uint32_t)(q4 * 32) << 16);
     const uint32_t o_addr = lane_addr + 128;
     float m_ref = -INFINITY, l = 0.f;
+    // tcgen05.ld / st are warp-wide (.sync.aligned): every branch around them
+    // is taken by the whole warp. A wait counts as passed only when it passed
+    // for all 32 lanes, so no lane goes on to a tensor-memory access alone.
+    auto wwait = [&](uint64_t* bar, uint32_t parity) -> bool {
+      const bool mine = !*abort_v && mbar_wait_bounded(bar, parity, kPfWaitLimit);
+      return __all_sync(0xffffffffu, mine);
+    };
     bool ok = true;
     for (int j = 0; j < T_tiles && ok; ++j) {
       const int sb = j & 1;
-      if (*abort_v || !mbar_wait_bounded(&s_full[sb], (j >> 1) & 1, kPfWaitLimit)) {
+      if (!wwait(&s_full[sb], (j >> 1) & 1)) {
         ok = false;
         break;
       }
@@ -253,16 +260,23 @@ __global__ void __launch_bounds__(192, 1)
         s[c] = key0 + c <= qpos ? s[c] * scale_log2 : -INFINITY;
         mx = fmaxf(mx, s[c]);
       }
-      if (j == 0) {
+      // a row moves its reference maximum when its new maximum exceeds it by
+      // more than 2^8; its O (all PVs so far) and l then scale by
+      // 2^(m_ref - mx). The rescale reads and writes O in tensor memory, a
+      // warp-wide operation: the warp does it when any of its rows moves,
+      // and the rows that do not move scale by 1 (their O is unchanged).
+      bool moves = false;
+      if (j == 0)
         m_ref = mx;  // finite: key 0 <= qpos
-      } else if (mx > m_ref + kPfRescale) {
-        // move the reference maximum: O (all PVs so far) and l scale by 2^(m_ref - mx)
-        if (*abort_v || !mbar_wait_bounded(&o_full, (j - 1) & 1, kPfWaitLimit)) {
+      else
+        moves = mx > m_ref + kPfRescale;
+      if (__any_sync(0xffffffffu, moves)) {
+        if (!wwait(&o_full, (j - 1) & 1)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const float f = exp2f(m_ref - mx);
+        const float f = moves ? exp2f(m_ref - mx) : 1.f;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t v[32];
@@ -273,8 +287,10 @@ __global__ void __launch_bounds__(192, 1)
           tmem_st32(o_addr + c * 32, v);
         }
         tmem_st_wait();
-        l *= f;
-        m_ref = mx;
+        if (moves) {
+          l *= f;
+          m_ref = mx;
+        }
       }
       float ps = 0.f;
 #pragma unroll
@@ -284,7 +300,7 @@ __global__ void __launch_bounds__(192, 1)
       }
       l += ps;
       // P buffer j&1 was last read by PV_{j-2}
-      if (j >= 2 && (*abort_v || !mbar_wait_bounded(&p_empty[sb], ((j - 2) >> 1) & 1, kPfWaitLimit))) {
+      if (j >= 2 && !wwait(&p_empty[sb], ((j - 2) >> 1) & 1)) {
         ok = false;
         break;
       }
@@ -303,7 +319,7 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_before();
       mbar_arrive(&p_full[sb]);
     }
-    if (ok && (*abort_v || !mbar_wait_bounded(&o_final, 0, kPfWaitLimit))) ok = false;
+    if (ok && !wwait(&o_final, 0)) ok = false;
     if (!ok) *abort_v = 1;
     if (ok) {
       tc_fence_after();

@@ -201,10 +201,17 @@ __global__ void __launch_bounds__(192, 2)
     const uint32_t lane_addr = tmem + ((uint32_t)(q4 * 32) << 16);
     const uint32_t o_addr = lane_addr + 128;
     float m_ref = -INFINITY, l = 0.f;
+    // tcgen05.ld / st are warp-wide (.sync.aligned): every branch around them
+    // is taken by the whole warp. A wait counts as passed only when it passed
+    // for all 32 lanes, so no lane goes on to a tensor-memory access alone.
+    auto wwait = [&](uint64_t* bar, uint32_t parity) -> bool {
+      const bool mine = !*abort_v && mbar_wait_bounded(bar, parity, kEaWaitLimit);
+      return __all_sync(0xffffffffu, mine);
+    };
     bool ok = true;
     for (int j = 0; j < n_tiles && ok; ++j) {
       const int sb = j & 1;
-      if (*abort_v || !mbar_wait_bounded(&s_full[sb], (j >> 1) & 1, kEaWaitLimit)) {
+      if (!wwait(&s_full[sb], (j >> 1) & 1)) {
         ok = false;
         break;
       }
@@ -232,15 +239,21 @@ __global__ void __launch_bounds__(192, 2)
 #pragma unroll
       for (int c = 4; c < 64; ++c) m4[c & 3] = fmaxf(m4[c & 3], s[c]);
       const float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
-      if (j == 0) {
+      // a row moves its reference maximum past 2^8 of headroom; the rescale
+      // of O in tensor memory is warp-wide, so the warp does it when any of
+      // its rows moves and the others scale by 1 (their O is unchanged)
+      bool moves = false;
+      if (j == 0)
         m_ref = mx;  // finite: key 0 is inside the chunk
-      } else if (mx > m_ref + kEaRescale) {
-        if (*abort_v || !mbar_wait_bounded(&o_full, (j - 1) & 1, kEaWaitLimit)) {
+      else
+        moves = mx > m_ref + kEaRescale;
+      if (__any_sync(0xffffffffu, moves)) {
+        if (!wwait(&o_full, (j - 1) & 1)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const float f = ex2(m_ref - mx);
+        const float f = moves ? ex2(m_ref - mx) : 1.f;
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
           uint32_t v[32];
@@ -251,8 +264,10 @@ __global__ void __launch_bounds__(192, 2)
           tmem_st32(o_addr + c * 32, v);
         }
         tmem_st_wait();
-        l *= f;
-        m_ref = mx;
+        if (moves) {
+          l *= f;
+          m_ref = mx;
+        }
       }
       float p4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -261,7 +276,7 @@ __global__ void __launch_bounds__(192, 2)
         p4[c & 3] += s[c];
       }
       l += (p4[0] + p4[1]) + (p4[2] + p4[3]);
-      if (j >= 2 && (*abort_v || !mbar_wait_bounded(&p_empty[sb], ((j - 2) >> 1) & 1, kEaWaitLimit))) {
+      if (j >= 2 && !wwait(&p_empty[sb], ((j - 2) >> 1) & 1)) {
         ok = false;
         break;
       }
@@ -279,7 +294,7 @@ __global__ void __launch_bounds__(192, 2)
       tc_fence_before();
       mbar_arrive(&p_full[sb]);
     }
-    if (ok && (*abort_v || !mbar_wait_bounded(&o_final, 0, kEaWaitLimit))) ok = false;
+    if (ok && !wwait(&o_final, 0)) ok = false;
     if (!ok) *abort_v = 1;
     if (ok) {
       tc_fence_after();

@@ -224,7 +224,10 @@ __global__ void __launch_bounds__(kEgThreads, 1)
     int i = 0;
     for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++i) {
       const int buf = i & 1;
-      if (*abort_v || !mbar_wait_bounded(&acc_full[buf], (i >> 1) & 1, kEgWaitLimit)) {
+      // the tensor-memory loads below are warp-wide: the warp goes on only
+      // if the wait passed for all of its lanes
+      const bool got = !*abort_v && mbar_wait_bounded(&acc_full[buf], (i >> 1) & 1, kEgWaitLimit);
+      if (!__all_sync(0xffffffffu, got)) {
         *abort_v = 1;
         break;
       }
