@@ -145,16 +145,15 @@ struct GemvEpi {
 
 // The persistent tail of a decode layer (fmd_chain.cu): o_proj (+ residual)
 // -> gate/up (post-attention RMSNorm, SwiGLU) -> down (+ residual) -> the next
-// layer's qkv (its input RMSNorm, q/k norm, RoPE, KV write) in one launch.
-// A phase is one projection in the decode-packed Q8_0 layout of the GEMV:
-// `ft`-feature tiles split `S` ways along K.
+// layer's qkv (its input RMSNorm, q/k norm, RoPE, KV write) in one launch of
+// 8-CTA clusters. A phase is one projection in the decode-packed Q8_0 layout
+// of the GEMV: `ft`-feature tiles split `S` (= 8) ways along K.
 struct ChainPhase {
   const uint8_t* pk = nullptr;
   int N = 0, K = 0, ft = 0, S = 0;
 };
-constexpr int kChainMaxRows = 64;    // decode rows the layer tail serves
-constexpr int kChainMaxTiles = 128;  // feature tiles of one phase
-constexpr int kChainSyncInts = 4 * kChainMaxTiles + 3 * 17;  // per layer: tile counters, then 3 two-level grid barriers
+constexpr int kChainMaxRows = 32;  // decode rows the layer tail serves
+constexpr int kChainSyncInts = 4;  // per layer: the 3 grid-barrier counters (+1 spare), zero at launch
 struct ChainArgs {
   ChainPhase ph[4];            // o, gate_up, down, next layer's qkv
   int n_phases = 4;            // 3 for the last layer (no qkv)
@@ -176,7 +175,6 @@ struct ChainArgs {
   Plan plan{};
   int layer = 0;               // the next layer (its KV cache is written)
   int Hq = 0, Hkv = 0, H = 0, I = 0;
-  float* part = nullptr;       // f32 split-K partials [S][kChainMaxRows][N]
   int* sync = nullptr;         // this layer's kChainSyncInts counters, zero at launch
   int* status = nullptr;
 };
@@ -255,12 +253,11 @@ void launch_silu_mul(ActType at, const int* n_rows_ptr, int R, const float* part
 void launch_logits_argmax(ActType at, const int* n_sample_ptr, int B, const float* part, int V, float* logits,
                           int* next_ids, cudaStream_t s);
 void launch_dequant(ActType at, const LinW& W, float* out, cudaStream_t s);
-// fmd_chain.cu: shared-memory bytes of the layer tail on `n_sm` CTAs for
-// `max_rows` rows (0 when it does not fit), and its launch.
-size_t chain_smem_bytes(const ChainArgs& a, int n_sm, int max_rows);
-cudaError_t init_chain(size_t smem);
-int chain_blocks_per_sm(ActType at, size_t smem);
-void launch_layer_tail(ActType at, const ChainArgs& a, int n_sm, size_t smem, cudaStream_t s);
+// fmd_chain.cu: the cluster count and shared-memory bytes of the layer tail
+// for up to `max_rows` rows on `n_sm` SMs (false when it cannot run; sets the
+// kernels' shared-memory limit), and its launch.
+bool chain_plan(ActType at, const ChainArgs& a, int n_sm, int max_rows, int* n_clusters, size_t* smem);
+void launch_layer_tail(ActType at, const ChainArgs& a, int n_clusters, size_t smem, cudaStream_t s);
 // One bounded wait that runs out after `limit` tries and sets *status to
 // FMD_ETIMEDOUT (the failure path of every ring kernel's waits).
 void launch_wait_probe(uint32_t limit, int* status, cudaStream_t s);

@@ -134,14 +134,13 @@ struct fmd_handle {
   int* attn_counters = nullptr;     // [max_slots][kv_heads] split-KV merge counters
   // persistent layer tail (fmd_chain.cu) of decode steps: Q8_0 weights and
   // at most kChainMaxRows rows, opt-in with FMD_LAYER_TAIL=1 in the
-  // environment at fmd_create. Measured slower than the per-projection GEMV
-  // launches on B200 (each of its ~10 dependent global round trips per
-  // projection costs ~1 us), so the GEMVs are the default.
+  // environment at fmd_create.
   int n_sm = 0;
   bool proj_allowed = true;  // mixed steps on k_proj_tc (fused epilogues); FMD_PROJ_TC=0 selects k_gemm_tc
   bool chain_allowed = false;
   bool chain_ok = false;
   size_t chain_smem = 0;
+  int chain_clusters = 0;
   int* chain_sync = nullptr;        // [layers][kChainSyncInts], cleared by each decode step's first kernel
   int* d_status = nullptr;          // device-side error status (bounded waits)
   bool launch_refused = false;      // a decode projection could not be launched
@@ -496,7 +495,6 @@ ChainArgs make_chain(fmd_handle* h, int l) {
   a.Hkv = h->Hkv();
   a.H = H;
   a.I = I;
-  a.part = h->part;
   a.sync = h->chain_sync ? h->chain_sync + (size_t)l * kChainSyncInts : nullptr;
   a.status = h->d_status;
   return a;
@@ -557,7 +555,7 @@ void run_forward_decode(fmd_handle* h, float* logits_dev, const void* arena) {
     trace(h, "attn_decode", l);
     if (h->chain_ok) {
       // o -> gate/up -> down -> the next layer's qkv in one persistent launch
-      launch_layer_tail(h->at, make_chain(h, l), h->n_sm, h->chain_smem, s);
+      launch_layer_tail(h->at, make_chain(h, l), h->chain_clusters, h->chain_smem, s);
       trace(h, "layer_tail", l);
       continue;
     }
@@ -784,8 +782,9 @@ int sync_check(fmd_handle* h) {
     if (st[0] != 0) {
       cudaMemset(h->d_status, 0, 2 * sizeof(int));
       static const char* const kSites[] = {"?", "k_gemv", "k_lm_head", "k_attn_decode_tma", "k_attn_prefill_tc",
-                                           "k_gemm_tc", "k_layer_tail", "k_wait_probe"};
-      const char* site = st[1] >= 1 && st[1] <= 7 ? kSites[st[1]] : "?";
+                                           "k_gemm_tc", "k_layer_tail", "k_wait_probe", "k_proj_tc"};
+      constexpr int kNumSites = (int)(sizeof(kSites) / sizeof(kSites[0]));
+      const char* site = st[1] >= 1 && st[1] < kNumSites ? kSites[st[1]] : "?";
       return fail(h, st[0], st[0] == FMD_EIO ? std::string("a greedy pick found no finite logit (non-finite activations)")
                                              : "a bounded device-side wait gave up in " + std::string(site) +
                                                    " (status " + std::to_string(st[0]) + ")");
@@ -1084,14 +1083,8 @@ int fmd_kv_reserve(fmd_handle* h, int32_t max_slots, int64_t max_tokens_total, i
   // CTA per SM with the layer's weights resident in shared memory
   h->chain_ok = false;
   if (h->q8 && h->chain_allowed && max_slots <= kChainMaxRows && c.num_hidden_layers > 0) {
-    const ChainArgs a = make_chain(h, 0);
-    const size_t smem = chain_smem_bytes(a, h->n_sm, max_slots);
-    if (smem > 0 && smem <= 226 * 1024 && init_chain(smem) == cudaSuccess && chain_blocks_per_sm(h->at, smem) >= 1) {
-      h->chain_ok = true;
-      h->chain_smem = smem;
-      for (int p = 0; p < a.n_phases; ++p)
-        part_elems = std::max(part_elems, (size_t)a.ph[p].S * kChainMaxRows * a.ph[p].N);
-    }
+    // every layer has the shapes of layer 0
+    h->chain_ok = chain_plan(h->at, make_chain(h, 0), h->n_sm, max_slots, &h->chain_clusters, &h->chain_smem);
     cudaGetLastError();
   }
   h->pb_max = R / kRowsPerPBlock + max_slots;
@@ -1732,6 +1725,12 @@ int fmd_debug_wait_timeout(fmd_handle* h, int32_t limit) {
   CK(cudaSetDevice(h->device));
   launch_wait_probe((uint32_t)limit, h->d_status, h->stream);
   return sync_check(h);
+}
+
+int fmd_debug_paths(const fmd_handle* h, int32_t* flags) {
+  if (!h || !flags) return FMD_EINVAL;
+  *flags = (h->chain_ok ? FMD_PATH_LAYER_TAIL : 0) | (h->tc_ready && h->proj_allowed ? FMD_PATH_PROJ_TC : 0);
+  return FMD_OK;
 }
 
 int fmd_q8_0_quantize(const float* src, int64_t rows, int64_t cols, void* blocks) {

@@ -238,6 +238,14 @@ class Qwen3Decoder:
         raises FmdError with FMD_ETIMEDOUT, after which the handle stays usable."""
         self._check(self.lib.fmd_debug_wait_timeout(self._h, int(limit)))
 
+    def debug_paths(self) -> dict:
+        """Which kernels serve this handle's steps (`fmd_debug_paths`):
+        {"layer_tail": decode steps on the persistent layer tail,
+        "proj_tc": mixed steps on the persistent projection GEMM}."""
+        f = C.c_int32(0)
+        self._check(self.lib.fmd_debug_paths(self._h, C.byref(f)))
+        return {"layer_tail": bool(f.value & 1), "proj_tc": bool(f.value & 2)}
+
     def debug_kv(self, slot: int, layer: int, pos: int, n: int):
         shape = (n, self.cfg.num_key_value_heads, self.cfg.head_dim)
         k = np.empty(shape, dtype=np.uint16)

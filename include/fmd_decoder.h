@@ -274,6 +274,14 @@ int fmd_debug_kv(fmd_handle* h, int32_t slot, int32_t layer, int32_t pos, int32_
  * in flight, so the context and the handle stay usable. */
 int fmd_debug_wait_timeout(fmd_handle* h, int32_t limit);
 
+/* Which kernels serve this handle's steps after fmd_kv_reserve (no reference
+ * counterpart): bit 0 = decode steps run the persistent layer tail
+ * (FMD_LAYER_TAIL=1, Q8_0 weights, max_slots <= 32), bit 1 = mixed steps run
+ * the persistent projection GEMM k_proj_tc. */
+#define FMD_PATH_LAYER_TAIL 1
+#define FMD_PATH_PROJ_TC 2
+int fmd_debug_paths(const fmd_handle* h, int32_t* flags);
+
 /* ---- greedy pick without allocation -------------------------------------- */
 
 /* No counterpart in the reference. Greedy ids (per-row argmax, lowest index
