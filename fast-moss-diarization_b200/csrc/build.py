@@ -25,7 +25,7 @@ ROOT = PKG.parent
 LIB = PKG / "libfmd_decoder.so"
 OBJ_DIR = PKG / "_build"
 SOURCES = ["fmd_kernels.cu", "fmd_gemv.cu", "fmd_gemm_tc.cu", "fmd_attn_decode.cu", "fmd_scheduler.cu", "fmd_runtime.cu",
-           "fmd_noalloc.cu", "fmd_splice.cu", "fmd_attn_prefill.cu", "fmd_chain.cu", "fmd_proj_tc.cu",
+           "fmd_noalloc.cu", "fmd_splice.cu", "fmd_attn_prefill.cu", "fmd_chain.cu", "fmd_proj_tc.cu", "fmd_lm_head_tc.cu",
            "fmd_quant.cu", "fmd_enc_gemm.cu", "fmd_enc_attn.cu", "fmd_enc_misc.cu", "fmd_audio.cu", "fmd_mel.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

@@ -110,6 +110,10 @@ __global__ void __launch_bounds__(192, 2)
     abort_s = 0;
     fence_barrier_init();
   }
+  // Tensor memory only after the dependency wait: the previous kernel has
+  // then finished, so none of its CTAs can hold the columns this CTA needs
+  // while it waits for this one.
+  griddep_wait();  // qkv comes from the previous kernel
   if (warp == 1) {
     tmem_alloc(&tmem_base_s, kEaTmemCols);
     tmem_relinquish();
@@ -119,7 +123,6 @@ __global__ void __launch_bounds__(192, 2)
   tc_fence_after();
   const uint32_t tmem = tmem_base_s;
   volatile int* abort_v = &abort_s;
-  griddep_wait();  // qkv comes from the previous kernel
 
   // Parity waits never alias: each waits for a phase whose successor needs
   // work that the waiting role itself releases later, and whose predecessor

@@ -146,6 +146,10 @@ __global__ void __launch_bounds__(kEgThreads, 1)
     abort_s = 0;
     fence_barrier_init();
   }
+  // Tensor memory only after the dependency wait: the previous kernel has
+  // then finished, so none of its CTAs can hold the columns this CTA needs
+  // while it waits for this one.
+  griddep_wait();  // A (and the residual stream) come from earlier kernels
   if (warp == 1) {
     tmem_alloc(&tmem_base_s, TMEM_COLS);
     tmem_relinquish();
@@ -155,7 +159,6 @@ __global__ void __launch_bounds__(kEgThreads, 1)
   tc_fence_after();
   const uint32_t tmem = tmem_base_s;
   volatile int* abort_v = &abort_s;
-  griddep_wait();  // A (and the residual stream) come from earlier kernels
 
   // Parity waits never alias: the ring and the two accumulators are each
   // waited on in use order by one role, which has already seen the previous

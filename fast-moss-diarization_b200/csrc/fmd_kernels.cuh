@@ -279,11 +279,16 @@ void gemv_pack(int epi, int N, int K, bool q8, const int8_t* qs, const uint16_t*
 // K split for this epilogue.
 bool launch_gemv(ActType at, int epi, bool norm, const LinW& W, const void* x, int ldx, const int* row_map,
                  const int* n_rows_ptr, int max_rows, const GemvEpi& ep, int* status, cudaStream_t s);
-// lm_head of the decode step (persistent kernel; the cluster GEMV when the
-// activation tile does not fit). Returns the candidates per row it writes
-// into ep.best_val / best_idx (0: nothing launched).
+// lm_head of the decode step: Q8_0 weights and up to 64 rows on the tensor
+// cores (k_lm_head_tc, when `tc`), else the persistent mma.sync kernel, else
+// the cluster GEMV when the activation tile does not fit. Returns the
+// candidates per row it writes into ep.best_val / best_idx (0: nothing
+// launched).
 int launch_lm_head(ActType at, const LinW& W, const void* x, int ldx, const int* row_map, const int* n_rows_ptr,
-                   int max_rows, const GemvEpi& ep, int* status, cudaStream_t s);
+                   int max_rows, const GemvEpi& ep, int* status, cudaStream_t s, bool tc = true);
+// fmd_lm_head_tc.cu: the tensor-core lm_head (0 when it cannot serve the shapes).
+int launch_lm_head_tc(ActType at, const LinW& W, const void* x, int ldx, const int* row_map, const int* n_rows_ptr,
+                      int max_rows, const GemvEpi& ep, int* status, cudaStream_t s);
 // next_ids[r] = the lowest-index maximum of row r; a row without a finite
 // candidate gets 0 and sets *status to FMD_EIO
 void launch_pick_reduce(const int* n_sample_ptr, int B, const float* best_val, const int* best_idx, int n_parts,

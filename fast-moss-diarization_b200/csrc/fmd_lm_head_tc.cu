@@ -1,0 +1,458 @@
+// lm_head + greedy candidates of a decode step on the 5th-generation tensor
+// cores (qwen3.rs:459-463, engine.rs:550-559), for Q8_0 weights and up to 64
+// sampled rows.
+//
+// The reference dequantises each Q8_0 block (q * d, linear.rs:179-265) and
+// multiplies in f32. Here the int8 values themselves go through the MMA
+// (exact in f16 and bf16), every 32-wide block into its own f32 accumulator
+// in tensor memory, and the block's f16 scale is applied in f32 on the way
+// out: y = sum_b d_b * (sum_{k in b} q_k x_k), the reference's sum up to the
+// f32 summation order, as the mma.sync kernel (k_lm_head) computes it.
+//
+// One CTA per SM walks 128-feature tiles (tile blockIdx.x + i * gridDim.x);
+// a tile's k-blocks of 64 are stages:
+//  * warp 0 (one lane): TMA bulk copies of the decode-packed stages (8 units
+//    of 16 features x 64 k, 8.5 KB, the k_lm_head layout) into a ring of RAW
+//    stages. Weights depend on no earlier kernel, so the ring fills before
+//    the dependency wait;
+//  * warps 2-9 (converters): warp w takes unit w of each stage, turns its
+//    int8 values into 16-bit operands and writes them as 16 rows of the
+//    stage's A tile (128 features x 64 k, K-major, 128-byte swizzle) in a
+//    ring of CONV slots, releasing the raw stage as soon as its fragments are
+//    in registers;
+//  * warp 1 (one lane): tcgen05.mma M = 128 (features) x N = NR (rows) x
+//    K = 16, two per Q8_0 block, each block into the next of 256 / NR
+//    accumulators; tcgen05.commit releases the A slot and signals the block's
+//    accumulator;
+//  * warps 10-13 (epilogue): before the loop they stage the rows (final
+//    RMSNorm applied) as the B operand, resident for the whole launch. Per
+//    block, warp w reads tensor-memory lanes 32 (w % 4) .. (the thread's
+//    feature) x NR columns (the rows), frees the accumulator and adds
+//    d * value in f32. After a tile, the logits are rounded to the
+//    activation type (as the reference's lm_head output is) and reduced
+//    per row to the best (value, lowest index) through shared memory.
+// Each CTA writes one candidate per row; k_pick_reduce finishes the pick.
+// Every wait is bounded; a timeout sets the status word, each role stops,
+// and the CTA waits (bounded) for its copies and MMAs in flight before it
+// frees its tensor memory.
+#include <cuda_runtime.h>
+#include <math.h>
+
+#include "fmd_gemv.cuh"
+#include "fmd_kernels.cuh"
+
+namespace fmd {
+
+namespace {
+
+constexpr int kLhFeat = 128;                       // features of a tile = MMA M = tensor-memory lanes
+constexpr int kLhUnits = kLhFeat / 16;             // 16-feature units of a stage
+constexpr uint32_t kLhRaw = kLhUnits * kUnitQ8;    // packed stage: 8704 bytes
+constexpr uint32_t kLhConv = kLhFeat * 128;        // converted A tile: 128 rows x 64 k x 2 bytes
+constexpr int kLhConvWarps = kLhUnits;             // one unit per converter warp
+constexpr int kLhEpiWarps = 4;
+constexpr int kLhThreads = (2 + kLhConvWarps + kLhEpiWarps) * 32;  // 448
+constexpr int kLhTmemCols = 256;
+constexpr int kLhLgStride = 132;                   // row stride (floats) of the rounded-logit tile
+constexpr uint32_t kLhWaitLimit = 1u << 24;
+
+template <int NR>
+struct LhCfg {
+  static constexpr int RAW = NR == 32 ? 6 : 5;   // packed stages in flight
+  static constexpr int CONV = NR == 32 ? 4 : 2;  // converted A slots
+  static constexpr int ACC = kLhTmemCols / NR;   // block accumulators
+};
+
+// Dynamic shared memory: B (rows, K-major, swizzled) | CONV A slots | RAW
+// packed stages | rounded logits of 32 rows x 128 features; 1024-byte
+// aligned for the swizzle atoms.
+template <int NR>
+size_t lh_smem(int K) {
+  using C = LhCfg<NR>;
+  return 1024 + (size_t)NR * K * 2 + (size_t)C::CONV * kLhConv + (size_t)C::RAW * kLhRaw +
+         (size_t)32 * kLhLgStride * 4;
+}
+
+template <typename T, int NR>
+__global__ void __launch_bounds__(kLhThreads, 1)
+    k_lm_head_tc(const T* __restrict__ x, int ldx, const int* __restrict__ row_map, const int* __restrict__ n_rows_ptr,
+                 LinW W, GemvEpi ep, int* __restrict__ status) {
+  using C = LhCfg<NR>;
+  constexpr int RAW = C::RAW, CONV = C::CONV, ACC = C::ACC;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t full[RAW], empty[RAW], conv_full[CONV], conv_empty[CONV], acc_full[ACC],
+      acc_empty[ACC], mma_done;
+  __shared__ uint32_t tmem_base_s;
+  __shared__ float rs_s[NR];
+  __shared__ int abort_s, stop_s;
+  griddep_launch();
+
+  const int K = W.K, nkb = K / 64;
+  const int n_tiles = W.N / kLhFeat;
+  const int my_tiles = n_tiles > (int)blockIdx.x ? (n_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  const int n_stages = my_tiles * nkb;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  const uint32_t raw_u = smem_u32(smem_raw);
+  const uint32_t base = (raw_u + 1023u) & ~1023u;
+  uint8_t* base_p = smem_raw + (base - raw_u);
+  const uint32_t xs = base;                                    // B: nkb blocks of NR rows x 128 bytes
+  const uint32_t cv = xs + (uint32_t)NR * K * 2;               // A slots
+  uint8_t* xs_p = base_p;
+  uint8_t* cv_p = base_p + (size_t)NR * K * 2;
+  uint8_t* rw_p = cv_p + (size_t)CONV * kLhConv;               // packed stages
+  float* lg = reinterpret_cast<float*>(rw_p + (size_t)RAW * kLhRaw);  // [32][kLhLgStride]
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < RAW; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kLhConvWarps);
+    }
+    for (int i = 0; i < CONV; ++i) {
+      mbar_init(&conv_full[i], kLhConvWarps);
+      mbar_init(&conv_empty[i], 1);  // tcgen05.commit after the stage's MMAs
+    }
+    for (int i = 0; i < ACC; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], kLhEpiWarps);
+    }
+    mbar_init(&mma_done, 1);
+    abort_s = 0;
+    stop_s = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  volatile int* abort_v = &abort_s;
+
+  // Parity waits never alias: each ring is waited on in use order by one
+  // role, which has already seen the previous use of the same slot complete.
+  if (warp == 0) {
+    if (lane == 0) {
+      int g = 0;
+      bool ok = true;
+      for (int i = 0; ok && i < my_tiles; ++i) {
+        const int tile = blockIdx.x + i * gridDim.x;
+        for (int kb = 0; kb < nkb; ++kb, ++g) {
+          const int s = g % RAW;
+          if (g >= RAW && (*abort_v || !mbar_wait_bounded(&empty[s], ((g / RAW) + 1) & 1, kLhWaitLimit))) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], kLhRaw);
+          bulk_load(rw_p + (size_t)s * kLhRaw, W.pk + ((size_t)tile * nkb + kb) * kLhRaw, kLhRaw, &full[s]);
+        }
+      }
+      if (!ok) *abort_v = 1;
+      // copies still in flight land before the CTA retires (bounded)
+      for (int j = g - RAW > 0 ? g - RAW : 0; j < g; ++j)
+        mbar_wait_bounded(&full[j % RAW], (j / RAW) & 1, kLhWaitLimit);
+    }
+  } else if (warp == 1) {
+    // tensor memory only after the dependency wait: the previous kernel has
+    // then finished, so none of its CTAs can wait for these columns
+    griddep_wait();
+    tmem_alloc(&tmem_base_s, kLhTmemCols);
+    tmem_relinquish();
+    tc_fence_before();
+    named_sync(2, (1 + kLhEpiWarps) * 32);  // with the epilogue: rows staged, columns allocated
+    tc_fence_after();
+    const uint32_t tmem = tmem_base_s;
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_f16(Act<T>::kIsBf16, kLhFeat, NR);
+      bool ok = true;
+      for (int g = 0; ok && g < n_stages; ++g) {
+        const int c = g % CONV, kb = g % nkb;
+        if (*abort_v || !mbar_wait_bounded(&conv_full[c], (g / CONV) & 1, kLhWaitLimit)) {
+          ok = false;
+          break;
+        }
+        for (int b = 0; b < 2; ++b) {
+          const int B = 2 * g + b, a = B % ACC;
+          if (B >= ACC && (*abort_v || !mbar_wait_bounded(&acc_empty[a], ((B / ACC) + 1) & 1, kLhWaitLimit))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t at = cv + (uint32_t)c * kLhConv + b * 64, bt = xs + (uint32_t)kb * NR * 128 + b * 64;
+          umma_f16(tmem + (uint32_t)(a * NR), umma_desc_sw128(at), umma_desc_sw128(bt), idesc, false);
+          umma_f16(tmem + (uint32_t)(a * NR), umma_desc_sw128(at + 32), umma_desc_sw128(bt + 32), idesc, true);
+          umma_commit(&acc_full[a]);
+        }
+        if (!ok) break;
+        umma_commit(&conv_empty[c]);  // the A slot is free once these MMAs have read it
+      }
+      if (!ok) *abort_v = 1;
+      umma_commit(&mma_done);  // every MMA issued so far has completed when this fires
+      mbar_wait_bounded(&mma_done, 0, kLhWaitLimit);
+    }
+    __syncwarp();
+  } else if (warp < 2 + kLhConvWarps) {
+    // ---- converters: unit u of every stage -> rows 16u .. 16u + 15 of the A tile
+    const int u = warp - 2, gq = lane >> 2, t = lane & 3;
+    bool ok = true;
+    for (int g = 0; ok && g < n_stages; ++g) {
+      const int s = g % RAW, c = g % CONV;
+      if (g >= CONV && (*abort_v || !mbar_wait_bounded(&conv_empty[c], ((g / CONV) + 1) & 1, kLhWaitLimit))) {
+        ok = false;
+        break;
+      }
+      if (*abort_v || !mbar_wait_bounded(&full[s], (g / RAW) & 1, kLhWaitLimit)) {
+        ok = false;
+        break;
+      }
+      const uint8_t* un = rw_p + (size_t)s * kLhRaw + (size_t)u * kUnitQ8;
+      const int4 qa = *reinterpret_cast<const int4*>(un + lane * 16);        // feature gq
+      const int4 qb = *reinterpret_cast<const int4*>(un + 512 + lane * 16);  // feature gq + 8
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+      // lane (gq, t) holds k [8t, 8t + 8) of block 0 and [32 + 8t, +8) of
+      // block 1: 16-byte chunks t and 4 + t of the row. Odd rows store their
+      // block-1 chunk first, so each quarter-warp store covers all 32 banks.
+      uint8_t* tile = cv_p + (size_t)c * kLhConv;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int4 q = h ? qb : qa;
+        const int r = u * 16 + gq + 8 * h;
+        uint32_t o[8];
+        i8x4_to_act<T>((uint32_t)q.x, o[0], o[1]);
+        i8x4_to_act<T>((uint32_t)q.y, o[2], o[3]);
+        i8x4_to_act<T>((uint32_t)q.z, o[4], o[5]);
+        i8x4_to_act<T>((uint32_t)q.w, o[6], o[7]);
+        const int4 c0 = make_int4(o[0], o[1], o[2], o[3]), c1 = make_int4(o[4], o[5], o[6], o[7]);
+        uint8_t* rowp = tile + r * 128;
+        const int j0 = t ^ (r & 7), j1 = (4 + t) ^ (r & 7);
+        if (r & 1) {
+          *reinterpret_cast<int4*>(rowp + (j1 << 4)) = c1;
+          *reinterpret_cast<int4*>(rowp + (j0 << 4)) = c0;
+        } else {
+          *reinterpret_cast<int4*>(rowp + (j0 << 4)) = c0;
+          *reinterpret_cast<int4*>(rowp + (j1 << 4)) = c1;
+        }
+      }
+      asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // visible to tcgen05.mma
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&conv_full[c]);
+    }
+    if (!ok) *abort_v = 1;
+  } else {
+    // ---- epilogue warps: stage the rows, then the accumulators
+    constexpr int NE = kLhEpiWarps * 32;
+    const int et = threadIdx.x - (2 + kLhConvWarps) * 32;
+    griddep_wait();
+    const int rows = min(*n_rows_ptr, NR);
+    const bool norm = ep.ssq != nullptr;  // else the rows are already normalised
+    if (norm) {
+      for (int r = et; r < rows; r += NE) {
+        const float* sp = ep.ssq + (size_t)(row_map ? row_map[r] : r) * ep.ssq_tiles;
+        float ss = 0.f;
+        for (int i0 = 0; i0 < ep.ssq_tiles; i0 += 16) {
+          float v[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) v[i] = i0 + i < ep.ssq_tiles ? sp[i0 + i] : 0.f;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) ss += v[i];
+        }
+        rs_s[r] = rsqrtf(ss / K + ep.eps);
+      }
+      named_sync(1, NE);
+    }
+    {
+      // 16-byte chunk ch of row r: k-block ch / 8, chunk ch % 8 of the row,
+      // stored swizzled (chunk j of row r at j ^ (r % 8))
+      const int cpr = K >> 3;
+      const T* nw = reinterpret_cast<const T*>(ep.norm_w);
+      for (int i0 = et; i0 < NR * cpr; i0 += 4 * NE) {
+        int4 v[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int idx = i0 + j * NE, r = idx / cpr, ch = idx - r * cpr;
+          v[j] = make_int4(0, 0, 0, 0);
+          if (idx < NR * cpr && r < rows)
+            v[j] = *reinterpret_cast<const int4*>(x + (size_t)(row_map ? row_map[r] : r) * ldx + ch * 8);
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int idx = i0 + j * NE, r = idx / cpr, ch = idx - r * cpr;
+          if (idx >= NR * cpr) continue;
+          if (norm && r < rows) {
+            const int4 wv = *reinterpret_cast<const int4*>(nw + ch * 8);
+            uint32_t* uv = reinterpret_cast<uint32_t*>(&v[j]);
+            const uint32_t* uw = reinterpret_cast<const uint32_t*>(&wv);
+            const float rsr = rs_s[r];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 f = Act<T>::unpack2(uv[e]);
+              const float2 gw = Act<T>::unpack2(uw[e]);
+              uv[e] = Act<T>::pack2(f.x * rsr * gw.x, f.y * rsr * gw.y);
+            }
+          }
+          const int kb = ch >> 3, jj = ch & 7;
+          *reinterpret_cast<int4*>(xs_p + (size_t)kb * NR * 128 + r * 128 + ((jj ^ (r & 7)) << 4)) = v[j];
+        }
+      }
+    }
+    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // the rows, visible to tcgen05.mma
+    named_sync(2, (1 + kLhEpiWarps) * 32);
+    tc_fence_after();
+    const uint32_t tmem = tmem_base_s;
+    const int q = warp & 3, fl = q * 32 + lane;  // this thread's feature of a tile
+    const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
+    // running best of rows j (+ 32) over this CTA's tiles: thread 4 j + fq
+    // scans features [32 fq, 32 fq + 32) of row j of each tile
+    const int jr = et >> 2, fq = et & 3;
+    float rb_v[NR / 32];
+    int rb_i[NR / 32];
+#pragma unroll
+    for (int h = 0; h < NR / 32; ++h) rb_v[h] = -INFINITY, rb_i[h] = 0x7fffffff;
+    bool ok = true;  // this warp's waits all passed
+    int g = 0;
+    // scale words (block 0 | block 1 f16) of this feature, one stage ahead
+    auto scale_at = [&](int i, int kb) -> uint32_t {
+      const int tile = blockIdx.x + i * gridDim.x;
+      const uint8_t* un = W.pk + ((size_t)tile * nkb + kb) * kLhRaw + (size_t)(fl >> 4) * kUnitQ8 + 1024;
+      return __ldg(reinterpret_cast<const uint32_t*>(un) + (fl & 15));
+    };
+    uint32_t sc_next = n_stages > 0 ? scale_at(0, 0) : 0u;
+    // The four warps take every tile's named barriers together whatever
+    // their waits did: a warp whose wait gave up skips its tensor-memory
+    // work, and all stop after the tile on a flag read between barriers.
+    for (int i = 0; i < my_tiles; ++i) {
+      const int tile = blockIdx.x + i * gridDim.x;
+      float acc[NR];
+#pragma unroll
+      for (int j = 0; j < NR; ++j) acc[j] = 0.f;
+      for (int kb = 0; kb < nkb && ok; ++kb, ++g) {
+        const uint32_t sc = sc_next;
+        if (g + 1 < n_stages) sc_next = kb + 1 < nkb ? scale_at(i, kb + 1) : scale_at(i + 1, 0);
+        const float2 d = __half22float2(*reinterpret_cast<const __half2*>(&sc));
+        for (int b = 0; b < 2 && ok; ++b) {
+          const int B = 2 * g + b, a = B % ACC;
+          // the tensor-memory loads are warp-wide: the warp goes on only if
+          // the wait passed for all of its lanes
+          const bool got = !*abort_v && mbar_wait_bounded(&acc_full[a], (B / ACC) & 1, kLhWaitLimit);
+          if (!__all_sync(0xffffffffu, got)) {
+            ok = false;
+            *abort_v = 1;
+            break;
+          }
+          tc_fence_after();
+          const float db = b ? d.y : d.x;
+#pragma unroll
+          for (int c0 = 0; c0 < NR; c0 += 32) {
+            uint32_t r[32];
+            tmem_ld32(lane_base + (uint32_t)(a * NR + c0), r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) acc[c0 + j] = fmaf(db, __uint_as_float(r[j]), acc[c0 + j]);
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_empty[a]);
+        }
+      }
+      // rounded logits; per row the best (value, lowest index) of the tile
+      const int f0 = tile * kLhFeat;
+#pragma unroll
+      for (int h = 0; h < NR / 32; ++h) {
+        named_sync(1, NE);  // the previous half's reads are done
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float v = rnd<T>(acc[h * 32 + j]);
+          lg[j * kLhLgStride + fl] = v;
+          if (ep.logits && h * 32 + j < rows) ep.logits[(size_t)(h * 32 + j) * W.N + f0 + fl] = v;
+        }
+        named_sync(1, NE);
+        float bv = -INFINITY;
+        int bi = 0x7fffffff;
+        const float* lr = lg + jr * kLhLgStride + fq * 32;
+#pragma unroll 8
+        for (int k = 0; k < 32; ++k) {
+          const int kk = (k + fq) & 31;  // lanes of a warp on 32 distinct banks
+          const float v = lr[kk];
+          const int ix = f0 + fq * 32 + kk;
+          if (v > bv || (v == bv && ix < bi)) bv = v, bi = ix;
+        }
+#pragma unroll
+        for (int o = 1; o < 4; o <<= 1) {
+          const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+          const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+          if (ov > bv || (ov == bv && oi < bi)) bv = ov, bi = oi;
+        }
+        if (bv > rb_v[h] || (bv == rb_v[h] && bi < rb_i[h])) rb_v[h] = bv, rb_i[h] = bi;
+      }
+      named_sync(1, NE);
+      if (et == 0) stop_s = *abort_v;
+      named_sync(1, NE);
+      if (stop_s) break;
+    }
+    if (fq == 0) {
+#pragma unroll
+      for (int h = 0; h < NR / 32; ++h) {
+        const int r = h * 32 + jr;
+        if (r < rows) {
+          ep.best_val[(size_t)r * gridDim.x + blockIdx.x] = rb_v[h];
+          ep.best_idx[(size_t)r * gridDim.x + blockIdx.x] = rb_i[h];
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && *abort_v) report_timeout(status, kSiteLmHead);
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base_s, kLhTmemCols);
+  }
+}
+
+template <typename T, int NR>
+int launch_t(const LinW& W, const void* x, int ldx, const int* row_map, const int* n_rows_ptr, const GemvEpi& ep,
+             int* status, int n_sm, cudaStream_t s) {
+  const size_t smem = lh_smem<NR>(W.K);
+  if (smem > 226 * 1024) return 0;
+  static bool attr_set = false;
+  if (!attr_set) {
+    if (cudaFuncSetAttribute(k_lm_head_tc<T, NR>, cudaFuncAttributeMaxDynamicSharedMemorySize, 226 * 1024) !=
+        cudaSuccess) {
+      cudaGetLastError();
+      return 0;
+    }
+    attr_set = true;
+  }
+  const int n_tiles = W.N / kLhFeat;
+  const int grid = n_tiles < n_sm ? n_tiles : n_sm;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kLhThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, k_lm_head_tc<T, NR>, (const T*)x, ldx, row_map, n_rows_ptr, W, ep, status);
+  return grid;
+}
+
+}  // namespace
+
+int launch_lm_head_tc(ActType at, const LinW& W, const void* x, int ldx, const int* row_map, const int* n_rows_ptr,
+                      int max_rows, const GemvEpi& ep, int* status, cudaStream_t s) {
+  if (!W.q8 || W.pk == nullptr || max_rows > 64 || max_rows < 1 ||
+      W.N % kLhFeat != 0 || W.K % 64 != 0 || ep.best_val == nullptr || ep.best_idx == nullptr)
+    return 0;
+  static int n_sm = 0;
+  if (n_sm == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
+    if (n_sm <= 0) n_sm = 148;
+  }
+  if (at == kBF16)
+    return max_rows <= 32 ? launch_t<__nv_bfloat16, 32>(W, x, ldx, row_map, n_rows_ptr, ep, status, n_sm, s)
+                          : launch_t<__nv_bfloat16, 64>(W, x, ldx, row_map, n_rows_ptr, ep, status, n_sm, s);
+  return max_rows <= 32 ? launch_t<__half, 32>(W, x, ldx, row_map, n_rows_ptr, ep, status, n_sm, s)
+                        : launch_t<__half, 64>(W, x, ldx, row_map, n_rows_ptr, ep, status, n_sm, s);
+}
+
+}  // namespace fmd

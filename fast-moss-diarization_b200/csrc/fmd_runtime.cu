@@ -137,6 +137,7 @@ struct fmd_handle {
   // environment at fmd_create.
   int n_sm = 0;
   bool proj_allowed = true;  // mixed steps on k_proj_tc (fused epilogues); FMD_PROJ_TC=0 selects k_gemm_tc
+  bool lm_tc_allowed = true;  // Q8_0 lm_head on the tensor cores; FMD_LM_HEAD_TC=0 selects the mma.sync kernel
   bool chain_allowed = false;
   bool chain_ok = false;
   size_t chain_smem = 0;
@@ -573,7 +574,7 @@ void run_forward_decode(fmd_handle* h, float* logits_dev, const void* arena) {
   head.best_val = h->best_val;
   head.best_idx = h->best_idx;
   const int parts = launch_lm_head(h->at, h->lm_head, h->x, H, h->plan.sample_row, nsamp, h->max_slots, head,
-                                   h->d_status, s);
+                                   h->d_status, s, h->lm_tc_allowed);
   if (parts == 0) h->launch_refused = true;
   trace(h, "lm_head", -1);
   launch_pick_reduce(nsamp, h->max_slots, h->best_val, h->best_idx, parts, h->next_ids, c.vocab_size,
@@ -683,7 +684,7 @@ void run_forward(fmd_handle* h, float* logits_dev, const void* arena, bool decod
   head.best_val = h->best_val;
   head.best_idx = h->best_idx;
   const int parts = launch_lm_head(h->at, h->lm_head, h->xn, H, h->plan.sample_row, nsamp, h->max_slots, head,
-                                   h->d_status, s);
+                                   h->d_status, s, h->lm_tc_allowed);
   trace(h, "lm_head", -1);
   if (parts > 0) {
     launch_pick_reduce(nsamp, h->max_slots, h->best_val, h->best_idx, parts, h->next_ids, c.vocab_size,
@@ -904,6 +905,8 @@ int fmd_create(const fmd_config* cfg, int32_t precision, int32_t device, fmd_han
     h->chain_allowed = v != nullptr && v[0] == '1';
     const char* p = std::getenv("FMD_PROJ_TC");
     h->proj_allowed = !(p != nullptr && p[0] == '0');
+    const char* lt = std::getenv("FMD_LM_HEAD_TC");
+    h->lm_tc_allowed = !(lt != nullptr && lt[0] == '0');
   }
   if (cudaDeviceGetAttribute(&h->n_sm, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || h->n_sm < 1) {
     cudaGetLastError();
@@ -1729,7 +1732,8 @@ int fmd_debug_wait_timeout(fmd_handle* h, int32_t limit) {
 
 int fmd_debug_paths(const fmd_handle* h, int32_t* flags) {
   if (!h || !flags) return FMD_EINVAL;
-  *flags = (h->chain_ok ? FMD_PATH_LAYER_TAIL : 0) | (h->tc_ready && h->proj_allowed ? FMD_PATH_PROJ_TC : 0);
+  *flags = (h->chain_ok ? FMD_PATH_LAYER_TAIL : 0) | (h->tc_ready && h->proj_allowed ? FMD_PATH_PROJ_TC : 0) |
+           (h->lm_tc_allowed && h->lm_head.q8 && h->max_slots <= 64 ? FMD_PATH_LM_HEAD_TC : 0);
   return FMD_OK;
 }
 

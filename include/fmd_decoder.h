@@ -277,9 +277,11 @@ int fmd_debug_wait_timeout(fmd_handle* h, int32_t limit);
 /* Which kernels serve this handle's steps after fmd_kv_reserve (no reference
  * counterpart): bit 0 = decode steps run the persistent layer tail
  * (FMD_LAYER_TAIL=1, Q8_0 weights, max_slots <= 32), bit 1 = mixed steps run
- * the persistent projection GEMM k_proj_tc. */
+ * the persistent projection GEMM k_proj_tc, bit 2 = the lm_head runs on the
+ * tensor cores (Q8_0 lm_head, max_slots <= 64; FMD_LM_HEAD_TC=0 turns it off). */
 #define FMD_PATH_LAYER_TAIL 1
 #define FMD_PATH_PROJ_TC 2
+#define FMD_PATH_LM_HEAD_TC 4
 int fmd_debug_paths(const fmd_handle* h, int32_t* flags);
 
 /* ---- greedy pick without allocation -------------------------------------- */

@@ -295,3 +295,41 @@ def test_decode_batch_of_32_full_shapes(prec):
                 want = m.decode_step(int(toks[s]), caches[s]).numpy()
                 assert rel_err(lg[s], want) < LOGIT_RTOL, s
                 check_pick(int(ids[s]), lg[s], want)
+
+
+@pytest.mark.parametrize("prec,n", [("int8_bf16", 5), ("int8_bf16", 32), ("int8", 32), ("int8_bf16", 48),
+                                    ("int8", 64)])
+def test_lm_head_on_the_tensor_cores(prec, n, monkeypatch):
+    """The Q8_0 lm_head on tcgen05 (fmd_lm_head_tc.cu: the exact int8 values
+    through the MMA, one tensor-memory accumulator per 32-wide block, the f16
+    block scale applied in f32) against the mma.sync kernel it replaces
+    (FMD_LM_HEAD_TC=0) and the oracle, for 1-32 rows (N = 32) and 33-64
+    rows (N = 64): the same arithmetic up to the f32 summation order, so the
+    two kernels' rounded logits differ by at most one unit in the last place
+    of the activation type, and each pick is the row's lowest-index maximum."""
+    cfg = mid_config(num_hidden_layers=1)
+    w = syn.make_weights(cfg, seed=29)
+    m = oracle_model(cfg, w, prec)
+    rng = np.random.default_rng(n)
+    lens = rng.integers(1, 30, n)
+    prompts = [rng.standard_normal((int(k), cfg.hidden_size), dtype=np.float32) for k in lens]
+    toks = rng.integers(0, cfg.vocab_size, n)
+    got = {}
+    for tc in ("1", "0"):
+        monkeypatch.setenv("FMD_LM_HEAD_TC", tc)
+        with make_decoder(cfg, w, prec, slots=n, tokens=n * 64, rows=1024) as dec:
+            assert dec.debug_paths()["lm_head_tc"] == (tc == "1")
+            for s in range(n):
+                dec.open_slot(s, int(lens[s]) + 2)
+            dec.prefill(list(range(n)), prompts, want_logits=False)
+            got[tc] = dec.decode_step(list(range(n)), toks)
+    lg_tc, ids_tc = got["1"]
+    lg_ref, _ = got["0"]
+    ulp = np.spacing(np.abs(lg_ref).astype(np.float32)) * (2.0 ** (16 if prec == "int8_bf16" else 13))
+    assert np.all(np.abs(lg_tc - lg_ref) <= ulp + 1e-30), float(np.max(np.abs(lg_tc - lg_ref) / (ulp + 1e-30)))
+    for s in range(n):
+        cs = m.new_caches(1, int(lens[s]) + 2)
+        m.prefill(prompts[s][None], cs)
+        want = m.decode_step(int(toks[s]), cs).numpy()
+        assert rel_err(lg_tc[s], want) < LOGIT_RTOL, s
+        check_pick(int(ids_tc[s]), lg_tc[s], want)
