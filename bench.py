@@ -581,6 +581,13 @@ def main():
     alg_bytes = kv_per_launch * kvh * hd * 2 * 2 + rows * hq * hd * 2 * 2
     achieved = alg_bytes / (ms_per_launch / 1000.0) / 1e9 if ms_per_launch > 0 else 0.0
     tpk = traffic_per_kv_token()
+    # the lm_head launch of each window's last step: its weights (Q8_0: 34
+    # bytes per 32 values) and the sampled rows in
+    lm_ms = [s.lm_head_ms for s in wins if s.lm_head_ms > 0]
+    lm_ms = statistics.mean(lm_ms) if lm_ms else 0.0
+    lm_bytes = cfg.vocab_size * cfg.hidden_size * (34 / 32 if wl.precision.startswith("int8") else 2) \
+        + rows * cfg.hidden_size * 2
+    lm_gbs = lm_bytes / (lm_ms / 1000.0) / 1e9 if lm_ms > 0 else 0.0
 
     # whole-step HBM roofline at the measured mean context
     w_bytes = cfg.n_params() * (34 / 32 if wl.precision.startswith("int8") else 2)
@@ -643,6 +650,10 @@ def main():
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "traffic": (tpk * kv_per_launch) if tpk else None, "peak_kind": peak_kind,
                          "alg_bytes_per_launch": alg_bytes, "ms_per_launch": ms_per_launch},
+            "lm_head": {"kernel": "k_lm_head_tc (tcgen05, Q8_0)" if wl.precision.startswith("int8") and
+                        os.environ.get("FMD_LM_HEAD_TC", "1") != "0" and args.batch <= 64 else "k_lm_head (mma.sync)",
+                        "ms_per_launch": lm_ms, "alg_bytes_per_launch": lm_bytes, "achieved_gbs": lm_gbs,
+                        "frac": lm_gbs / peak if peak else None},
             "step_roofline": {"bytes_per_step": step_bytes, "ms_per_step": step_ms,
                               "achieved_gbs": step_bytes / (step_ms / 1000.0) / 1e9 if step_ms > 0 else 0.0,
                               "frac": (step_bytes / (step_ms / 1000.0) / 1e9) / peak if step_ms > 0 else 0.0,

@@ -95,7 +95,7 @@ class Stats(C.Structure):
                 ("reserved", C.c_int32), ("window_steps", C.c_int64), ("window_tokens", C.c_int64),
                 ("window_device_ms", C.c_double), ("attn_decode_ms", C.c_double), ("attn_kv_tokens", C.c_int64),
                 ("attn_rows", C.c_int64), ("window_mixed_steps", C.c_int64), ("graph_kernels_mixed", C.c_int64),
-                ("graph_kernels_decode", C.c_int64)]
+                ("graph_kernels_decode", C.c_int64), ("lm_head_ms", C.c_double)]
 
 
 class AudioConfig(C.Structure):

@@ -181,7 +181,7 @@ struct fmd_handle {
   bool record_attn_events = false;             // set while capturing the step graph
   // around the decode attention of one layer only: an event node between two
   // kernels of the graph removes their programmatic-dependent-launch overlap
-  std::vector<cudaEvent_t> attn_events;        // [2]
+  std::vector<cudaEvent_t> attn_events;        // [4]: the probe layer's attention, then the lm_head
   int attn_probe_layer() const { return cfg.num_hidden_layers / 2; }
   cudaEvent_t win_begin = nullptr, win_end = nullptr;
 
@@ -573,8 +573,10 @@ void run_forward_decode(fmd_handle* h, float* logits_dev, const void* arena) {
   head.logits = logits_dev;
   head.best_val = h->best_val;
   head.best_idx = h->best_idx;
+  if (h->record_attn_events) cudaEventRecordWithFlags(h->attn_events[2], s, cudaEventRecordExternal);
   const int parts = launch_lm_head(h->at, h->lm_head, h->x, H, h->plan.sample_row, nsamp, h->max_slots, head,
                                    h->d_status, s, h->lm_tc_allowed);
+  if (h->record_attn_events) cudaEventRecordWithFlags(h->attn_events[3], s, cudaEventRecordExternal);
   if (parts == 0) h->launch_refused = true;
   trace(h, "lm_head", -1);
   launch_pick_reduce(nsamp, h->max_slots, h->best_val, h->best_idx, parts, h->next_ids, c.vocab_size,
@@ -683,8 +685,10 @@ void run_forward(fmd_handle* h, float* logits_dev, const void* arena, bool decod
   head.logits = logits_dev;
   head.best_val = h->best_val;
   head.best_idx = h->best_idx;
+  if (h->record_attn_events) cudaEventRecordWithFlags(h->attn_events[2], s, cudaEventRecordExternal);
   const int parts = launch_lm_head(h->at, h->lm_head, h->xn, H, h->plan.sample_row, nsamp, h->max_slots, head,
                                    h->d_status, s, h->lm_tc_allowed);
+  if (h->record_attn_events) cudaEventRecordWithFlags(h->attn_events[3], s, cudaEventRecordExternal);
   trace(h, "lm_head", -1);
   if (parts > 0) {
     launch_pick_reduce(nsamp, h->max_slots, h->best_val, h->best_idx, parts, h->next_ids, c.vocab_size,
@@ -1493,7 +1497,7 @@ int fmd_engine_start(fmd_handle* h, int32_t max_batch, int32_t prefill_chunk) {
   CK(cudaMemsetAsync(h->eng_results.p, 0, sizeof(DevResult) * h->eng_n_reqs, h->stream));
   CK(cudaStreamSynchronize(h->stream));
   if (h->attn_events.empty()) {
-    h->attn_events.resize(2);
+    h->attn_events.resize(4);
     for (auto& e : h->attn_events) CK(cudaEventCreate(&e));
     CK(cudaEventCreate(&h->win_begin));
     CK(cudaEventCreate(&h->win_end));
@@ -1611,11 +1615,13 @@ int fmd_engine_step(fmd_handle* h, int64_t max_steps, fmd_stats* stats) {
   // from the slot state, so the window boundary changes no result.
   float win_ms = 0.f;
   if (launched > 0) CK(cudaEventElapsedTime(&win_ms, h->win_begin, h->win_end));
-  double attn_ms = 0.0;
+  double attn_ms = 0.0, lm_ms = 0.0;
   if (launched > 0 && !trace_enabled()) {
     float ms = 0.f;
     CK(cudaEventElapsedTime(&ms, h->attn_events[0], h->attn_events[1]));
     attn_ms = ms;
+    CK(cudaEventElapsedTime(&ms, h->attn_events[2], h->attn_events[3]));
+    lm_ms = ms;
   }
   const auto t1 = std::chrono::steady_clock::now();
   if (stats) {
@@ -1630,6 +1636,7 @@ int fmd_engine_step(fmd_handle* h, int64_t max_steps, fmd_stats* stats) {
     stats->window_tokens = h->h_ctr->gen_tokens - tokens0;
     stats->window_device_ms = win_ms;
     stats->attn_decode_ms = attn_ms;
+    stats->lm_head_ms = lm_ms;
     stats->attn_kv_tokens = kv_last;
     stats->attn_rows = rows_last;
     stats->window_mixed_steps = mixed_launched;

@@ -47,6 +47,7 @@ class BatchStats:
     window_mixed_steps: int = 0
     graph_kernels_mixed: int = 0
     graph_kernels_decode: int = 0
+    lm_head_ms: float = 0.0
 
     @classmethod
     def from_c(cls, st) -> "BatchStats":
@@ -56,7 +57,8 @@ class BatchStats:
                    window_tokens=int(st.window_tokens), window_device_ms=float(st.window_device_ms),
                    attn_decode_ms=float(st.attn_decode_ms), attn_kv_tokens=int(st.attn_kv_tokens),
                    attn_rows=int(st.attn_rows), window_mixed_steps=int(st.window_mixed_steps),
-                   graph_kernels_mixed=int(st.graph_kernels_mixed), graph_kernels_decode=int(st.graph_kernels_decode))
+                   graph_kernels_mixed=int(st.graph_kernels_mixed), graph_kernels_decode=int(st.graph_kernels_decode),
+                   lm_head_ms=float(st.lm_head_ms))
 
     @property
     def decode_tokens_per_second(self) -> float:

@@ -142,6 +142,7 @@ typedef struct fmd_stats {
   int64_t window_mixed_steps; /* steps of the window that could carry prefill rows */
   int64_t graph_kernels_mixed;  /* kernels in one replay of the step graph that may carry prefill rows */
   int64_t graph_kernels_decode; /* kernels in one replay of the decode-only step graph */
+  double lm_head_ms;        /* duration of the lm_head launch of the window's last step */
 } fmd_stats;
 
 /* ---- handle ------------------------------------------------------------- */
