@@ -32,6 +32,8 @@
 #include <float.h>
 #include <math.h>
 
+#include <algorithm>
+
 #include "fmd_kernels.cuh"
 
 namespace fmd {
@@ -353,24 +355,458 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
+// ---- persistent, two query tiles per CTA ------------------------------------
+// The same arithmetic as k_attn_prefill_tc, scheduled for the tensor cores:
+//  * a work item is a pair of consecutive 64-row blocks of one sequence (A, B)
+//    for one kv head: both tiles need the same key pages (B's history is A's
+//    plus at most one page), so each K/V page tile is read once for four
+//    query-head rows sets. A sequence's odd last block is an item of its own;
+//  * items are ranked by key tiles (longest first), work w = (item w / Hkv,
+//    head w % Hkv); CTA c of G takes works c, 2G - 1 - c, 2G + c, ... (snake
+//    order), so the long items are spread over the CTAs and the short ones
+//    even out their totals;
+//  * warp 0: TMA of both query tiles and of the page tiles (3-stage ring);
+//    warp 1: tcgen05.mma for both tiles, S_A(j), S_B(j), then PV_A(j - 1),
+//    PV_B(j - 1): while one softmax group works on its scores the tensor core
+//    runs the other tile's MMAs;
+//  * warps 2-5 / 6-9: the online softmax of tile A / B, one thread per tile
+//    row, as in k_attn_prefill_tc; P goes through one shared buffer per tile
+//    (the PV that read the previous P has completed before it is rewritten);
+//    O of each tile stays in tensor memory for the whole item (512 columns:
+//    per tile two S buffers and O).
+// Ring positions, S buffers, P and PV counts continue across a CTA's items;
+// each barrier is waited on in use order by one role, which has already
+// seen the previous use of the same slot complete, so no parity wait aliases.
+constexpr int kPpThreads = 320;
+constexpr int kPpTmemCols = 512;
+
+size_t attn_pp_smem_bytes() {
+  return 1024 + 2 * kPfQBytes + 2 * kPfPBytes + kPfStages * kPfKvBytes + (size_t)3 * kMaxPrefillBlocks * 4;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kPpThreads, 1)
+    k_attn_prefill_pp(const __grid_constant__ CUtensorMap kvmap, const __grid_constant__ CUtensorMap qmap, Plan p,
+                      int Hq, int Hkv, KvView kv, int layer, float scale_log2, T* __restrict__ ctx,
+                      int* __restrict__ status) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t q_full, q_empty, kv_full[kPfStages], kv_empty[kPfStages], s_full[2][2],
+      s_empty[2][2], p_full[2], pv_done[2], o_final[2], o_empty[2], mma_done;
+  __shared__ uint32_t tmem_base_s;
+  __shared__ int abort_s, n_items_s;
+  griddep_launch();
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;  // swizzle atoms need 1024-byte alignment
+  uint8_t* base_p = smem_raw + (base - raw);
+  // Q_A | Q_B | P_A | P_B | K/V stages | block slots | item costs | item order
+  const uint32_t q_s = base, p_s = base + 2 * kPfQBytes, kv_s = p_s + 2 * kPfPBytes;
+  uint8_t* p_sp = base_p + 2 * kPfQBytes;
+  int* s_slot = reinterpret_cast<int*>(base_p + 2 * kPfQBytes + 2 * kPfPBytes + kPfStages * kPfKvBytes);
+  int* s_cost = s_slot + kMaxPrefillBlocks;
+  int* s_order = s_cost + kMaxPrefillBlocks;
+
+  griddep_wait();  // q, the KV rows of this step and the plan come from earlier kernels
+  const int n_blocks = min(p.counts->n_pblocks, kMaxPrefillBlocks);
+  if (n_blocks == 0) return;  // whole CTA, before any barrier or tensor memory exists
+  auto tiles_of = [&](int b) { return (p.row_pos[p.pb_row0[b]] + p.pb_n[b] + kPageTokens - 1) / kPageTokens; };
+  // ---- items: a block at an even position of its sequence's run starts one
+  if (threadIdx.x == 0) n_items_s = 0;
+  for (int b = threadIdx.x; b < n_blocks; b += kPpThreads) s_slot[b] = p.row_slot[p.pb_row0[b]];
+  __syncthreads();
+  for (int b = threadIdx.x; b < n_blocks; b += kPpThreads) {
+    int j = 0;
+    while (b - j - 1 >= 0 && s_slot[b - j - 1] == s_slot[b]) ++j;
+    int cost = 0;
+    if ((j & 1) == 0) {
+      const bool pair = b + 1 < n_blocks && s_slot[b + 1] == s_slot[b];
+      cost = tiles_of(b) + (pair ? tiles_of(b + 1) : 0);
+      atomicAdd(&n_items_s, 1);
+    }
+    s_cost[b] = cost;  // 0: not an item start (every item has >= 1 tile)
+  }
+  __syncthreads();
+  for (int b = threadIdx.x; b < n_blocks; b += kPpThreads) {
+    const int cb = s_cost[b];
+    if (cb == 0) continue;
+    int rank = 0;
+    for (int k = 0; k < n_blocks; ++k) {
+      const int ck = s_cost[k];
+      rank += (ck > cb) || (ck == cb && k < b);
+    }
+    s_order[rank] = b;
+  }
+  __syncthreads();
+  const int G = gridDim.x, c = blockIdx.x;
+  const int n_works = n_items_s * Hkv;
+  if (c >= n_works) return;  // whole CTA, before any barrier or tensor memory exists
+  auto work_at = [&](int r) -> int { return r * G + ((r & 1) ? G - 1 - c : c); };
+
+  if (threadIdx.x == 0) {
+    mbar_init(&q_full, 1);
+    mbar_init(&q_empty, 1);
+    for (int s = 0; s < kPfStages; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int x = 0; x < 2; ++x) {
+      for (int s = 0; s < 2; ++s) {
+        mbar_init(&s_full[x][s], 1);
+        mbar_init(&s_empty[x][s], 128);
+      }
+      mbar_init(&p_full[x], 128);
+      mbar_init(&pv_done[x], 1);
+      mbar_init(&o_final[x], 1);
+      mbar_init(&o_empty[x], 128);
+    }
+    mbar_init(&mma_done, 1);
+    abort_s = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&tmem_base_s, kPpTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base_s;
+  volatile int* abort_v = &abort_s;
+
+  // the work of round r: tiles A, B (B = -1 for a lone block) and kv head h
+  struct Work {
+    int a, b, h;
+  };
+  auto work = [&](int r, Work& w) -> bool {
+    const int wi = work_at(r);
+    if (wi >= n_works) return false;
+    w.a = s_order[wi / Hkv];
+    w.h = wi % Hkv;
+    w.b = w.a + 1 < n_blocks && s_slot[w.a + 1] == s_slot[w.a] ? w.a + 1 : -1;
+    return true;
+  };
+
+  if (warp == 0) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      prefetch_tmap(&kvmap);
+      prefetch_tmap(&qmap);
+      int g = 0, k = 0;  // page tiles and query loads issued
+      bool ok = true;
+      Work w;
+      for (int r = 0; ok && work(r, w); ++r) {
+        if (k >= 1 && (*abort_v || !mbar_wait_bounded(&q_empty, (k - 1) & 1, kPfWaitLimit))) {
+          ok = false;
+          break;
+        }
+        const int nq = w.b >= 0 ? 2 : 1;
+        mbar_arrive_expect_tx(&q_full, nq * kPfQBytes);
+        ++k;
+        for (int x = 0; x < nq; ++x) {
+          const int r0 = p.pb_row0[x ? w.b : w.a];
+          const int xq0 = 2 * w.h * kHeadDim, xq1 = (2 * w.h + 1) * kHeadDim;
+          uint8_t* qd = base_p + x * kPfQBytes;
+          tma_load_2d(qd + 0 * kPfBox, &qmap, xq0, r0, &q_full);       // rows 0-63: head 2h, dims 0-63
+          tma_load_2d(qd + 1 * kPfBox, &qmap, xq1, r0, &q_full);       // rows 64-127: head 2h+1, dims 0-63
+          tma_load_2d(qd + 2 * kPfBox, &qmap, xq0 + 64, r0, &q_full);  // dims 64-127
+          tma_load_2d(qd + 3 * kPfBox, &qmap, xq1 + 64, r0, &q_full);
+        }
+        const int slot = s_slot[w.a];
+        const int* ptab = kv.page_table + (size_t)slot * kv.max_pages_per_slot;
+        const int T = tiles_of(w.b >= 0 ? w.b : w.a);
+        for (int j = 0; j < T; ++j, ++g) {
+          const int st = g % kPfStages;
+          if (g >= kPfStages &&
+              (*abort_v || !mbar_wait_bounded(&kv_empty[st], ((g / kPfStages) + 1) & 1, kPfWaitLimit))) {
+            ok = false;
+            break;
+          }
+          const int page = ptab[j];
+          const int yk = (int)(((((size_t)layer * kv.n_pages + page) * 2 + 0) * Hkv + w.h) * kPageTokens);
+          const int yv = yk + Hkv * kPageTokens;
+          uint8_t* dst = base_p + 2 * kPfQBytes + 2 * kPfPBytes + st * kPfKvBytes;
+          mbar_arrive_expect_tx(&kv_full[st], kPfKvBytes);
+          tma_load_2d(dst, &kvmap, 0, yk, &kv_full[st]);
+          tma_load_2d(dst + kPfBox, &kvmap, 64, yk, &kv_full[st]);
+          tma_load_2d(dst + 2 * kPfBox, &kvmap, 0, yv, &kv_full[st]);
+          tma_load_2d(dst + 3 * kPfBox, &kvmap, 64, yv, &kv_full[st]);
+        }
+      }
+      if (!ok) *abort_v = 1;
+      // copies still in flight must land before the CTA can retire (bounded)
+      if (k >= 1) mbar_wait_bounded(&q_full, (k - 1) & 1, kPfWaitLimit);
+      for (int j = g > kPfStages ? g - kPfStages : 0; j < g; ++j)
+        mbar_wait_bounded(&kv_full[j % kPfStages], (j / kPfStages) & 1, kPfWaitLimit);
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr bool kBf = Act<T>::kIsBf16;
+      constexpr uint32_t idesc_s = umma_idesc_f16(kBf, 128, 64);
+      constexpr uint32_t idesc_o = umma_idesc_f16(kBf, 128, 128) | (1u << 16);  // B (V) MN-major
+      int g = 0, k = 0;
+      int sn[2] = {0, 0}, pn[2] = {0, 0}, wn[2] = {0, 0};  // S tiles, PVs, items per tile role
+      bool ok = true;
+      // O_x += P_x V for key tile i of the item (first of the item: O_x = P_x V)
+      auto pv = [&](int x, int i, int st) -> bool {
+        if (i == 0 && wn[x] >= 1 &&
+            (*abort_v || !mbar_wait_bounded(&o_empty[x], (wn[x] - 1) & 1, kPfWaitLimit)))
+          return false;
+        if (*abort_v || !mbar_wait_bounded(&p_full[x], pn[x] & 1, kPfWaitLimit)) return false;
+        tc_fence_after();
+        const uint32_t v = kv_s + st * kPfKvBytes + 2 * kPfBox;
+        const uint32_t pa = p_s + x * kPfPBytes;
+        const uint32_t o_tmem = tmem + x * 256 + 128;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          umma_f16(o_tmem, umma_desc_sw128(pa + kk * 32), umma_desc_sw128_mn(v + kk * 2048, kPfBox), idesc_o,
+                   (i | kk) != 0);
+        umma_commit(&pv_done[x]);  // P_x is free and O_x holds this PV when it fires
+        ++pn[x];
+        return true;
+      };
+      Work w;
+      for (int r = 0; ok && work(r, w); ++r, ++k) {
+        const int Tx[2] = {tiles_of(w.a), w.b >= 0 ? tiles_of(w.b) : 0};
+        const int T = w.b >= 0 ? Tx[1] : Tx[0];
+        if (*abort_v || !mbar_wait_bounded(&q_full, k & 1, kPfWaitLimit)) {
+          ok = false;
+          break;
+        }
+        const int g0 = g;
+        for (int j = 0; ok && j <= T; ++j) {
+          if (j < T) {
+            const int st = (g0 + j) % kPfStages;
+            if (*abort_v || !mbar_wait_bounded(&kv_full[st], ((g0 + j) / kPfStages) & 1, kPfWaitLimit)) {
+              ok = false;
+              break;
+            }
+            const uint32_t kt = kv_s + st * kPfKvBytes;
+            for (int x = 0; x < 2; ++x) {
+              if (j >= Tx[x]) continue;
+              const int n = sn[x], sb = n & 1;
+              if (n >= 2 && (*abort_v || !mbar_wait_bounded(&s_empty[x][sb], ((n >> 1) + 1) & 1, kPfWaitLimit))) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              const uint32_t qa = q_s + x * kPfQBytes;
+#pragma unroll
+              for (int kk = 0; kk < 8; ++kk) {
+                const uint32_t a = qa + (kk < 4 ? kk * 32 : 2 * kPfBox + (kk - 4) * 32);
+                const uint32_t bk = kt + (kk < 4 ? kk * 32 : kPfBox + (kk - 4) * 32);
+                umma_f16(tmem + x * 256 + sb * 64, umma_desc_sw128(a), umma_desc_sw128(bk), idesc_s, kk != 0);
+              }
+              umma_commit(&s_full[x][sb]);
+              ++sn[x];
+            }
+            if (!ok) break;
+            if (j == T - 1) umma_commit(&q_empty);  // the item's last score MMAs have read Q
+          }
+          if (j >= 1) {
+            const int i = j - 1, st = (g0 + i) % kPfStages;
+            for (int x = 0; x < 2 && ok; ++x)
+              if (i < Tx[x]) ok = pv(x, i, st);
+            if (!ok) break;
+            umma_commit(&kv_empty[st]);  // the page tile is free once its MMAs have read it
+          }
+        }
+        if (!ok) break;
+        g = g0 + T;
+        for (int x = 0; x < 2; ++x)
+          if (Tx[x] > 0) {
+            umma_commit(&o_final[x]);  // the item's O_x is complete when this fires
+            ++wn[x];
+          }
+      }
+      if (!ok) *abort_v = 1;
+      umma_commit(&mma_done);  // every MMA issued so far has completed when this fires
+      mbar_wait_bounded(&mma_done, 0, kPfWaitLimit);
+    }
+  } else {
+    // ---------------- softmax + output of tile x: one thread per tile row ----------------
+    const int x = (warp - 2) >> 2;
+    const int q4 = warp & 3;
+    const int row = q4 * 32 + lane;
+    const int hs = row >> 6, ri = row & 63;
+    const uint32_t lane_addr = tmem + ((uint32_t)(q4 * 32) << 16) + x * 256;
+    const uint32_t o_addr = lane_addr + 128;
+    // tcgen05.ld / st are warp-wide (.sync.aligned): every branch around them
+    // is taken by the whole warp. A wait counts as passed only when it passed
+    // for all 32 lanes, so no lane goes on to a tensor-memory access alone.
+    auto wwait = [&](uint64_t* bar, uint32_t parity) -> bool {
+      const bool mine = !*abort_v && mbar_wait_bounded(bar, parity, kPfWaitLimit);
+      return __all_sync(0xffffffffu, mine);
+    };
+    int sn = 0, pn = 0, wn = 0;
+    bool ok = true;
+    Work w;
+    for (int r = 0; ok && work(r, w); ++r) {
+      const int blk = x ? w.b : w.a;
+      if (blk < 0) continue;  // a lone block: no tile B
+      const int r0 = p.pb_row0[blk], n = p.pb_n[blk];
+      const int pos0 = p.row_pos[r0];
+      const int qpos = pos0 + ri;
+      const int Tt = tiles_of(blk);
+      float m_ref = -INFINITY, l = 0.f;
+      for (int j = 0; j < Tt && ok; ++j) {
+        const int sb = sn & 1;
+        if (!wwait(&s_full[x][sb], (sn >> 1) & 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        float s[64];
+#pragma unroll
+        for (int c2 = 0; c2 < 2; ++c2) {
+          uint32_t v[32];
+          tmem_ld32(lane_addr + sb * 64 + c2 * 32, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i2 = 0; i2 < 32; ++i2) s[c2 * 32 + i2] = __uint_as_float(v[i2]);
+        }
+        tc_fence_before();
+        mbar_arrive(&s_empty[x][sb]);
+        ++sn;
+        const int key0 = j * kPageTokens;
+        float mx = -INFINITY;
+#pragma unroll
+        for (int c2 = 0; c2 < 64; ++c2) {
+          s[c2] = key0 + c2 <= qpos ? s[c2] * scale_log2 : -INFINITY;
+          mx = fmaxf(mx, s[c2]);
+        }
+        // lazy rescale (as k_attn_prefill_tc): the warp reads and writes O
+        // when any of its rows moves its reference maximum; the previous PV
+        // of this tile (the pn - 1-th) must have completed
+        bool moves = false;
+        if (j == 0)
+          m_ref = mx;  // finite: key 0 <= qpos
+        else
+          moves = mx > m_ref + kPfRescale;
+        if (__any_sync(0xffffffffu, moves)) {
+          if (!wwait(&pv_done[x], (pn - 1) & 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const float f = moves ? exp2f(m_ref - mx) : 1.f;
+#pragma unroll
+          for (int c2 = 0; c2 < 4; ++c2) {
+            uint32_t v[32];
+            tmem_ld32(o_addr + c2 * 32, v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i2 = 0; i2 < 32; ++i2) v[i2] = __float_as_uint(__uint_as_float(v[i2]) * f);
+            tmem_st32(o_addr + c2 * 32, v);
+          }
+          tmem_st_wait();
+          if (moves) {
+            l *= f;
+            m_ref = mx;
+          }
+        }
+        float ps = 0.f;
+#pragma unroll
+        for (int c2 = 0; c2 < 64; ++c2) {
+          s[c2] = exp2f(s[c2] - m_ref);
+          ps += s[c2];
+        }
+        l += ps;
+        // the P buffer was last read by the previous PV of this tile role
+        if (pn >= 1 && !wwait(&pv_done[x], (pn - 1) & 1)) {
+          ok = false;
+          break;
+        }
+        // P -> the 128-byte-swizzled A tile: row `row`, 16-byte chunk c holds keys 8c .. 8c+7
+        uint8_t* prow = p_sp + x * kPfPBytes + row * 128;
+#pragma unroll
+        for (int c2 = 0; c2 < 8; ++c2) {
+          uint4 u;
+          u.x = Act<T>::pack2(s[8 * c2 + 0], s[8 * c2 + 1]);
+          u.y = Act<T>::pack2(s[8 * c2 + 2], s[8 * c2 + 3]);
+          u.z = Act<T>::pack2(s[8 * c2 + 4], s[8 * c2 + 5]);
+          u.w = Act<T>::pack2(s[8 * c2 + 6], s[8 * c2 + 7]);
+          *reinterpret_cast<uint4*>(prow + ((c2 ^ (row & 7)) << 4)) = u;
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        mbar_arrive(&p_full[x]);
+        ++pn;
+      }
+      if (!ok) break;
+      if (!wwait(&o_final[x], wn & 1)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const float inv = 1.f / l;
+      T* dst = ctx + (size_t)(r0 + ri) * Hq * kHeadDim + (2 * w.h + hs) * kHeadDim;
+#pragma unroll
+      for (int c2 = 0; c2 < 4; ++c2) {
+        uint32_t v[32];
+        tmem_ld32(o_addr + c2 * 32, v);
+        tmem_ld_wait();
+        if (ri < n) {
+#pragma unroll
+          for (int q8 = 0; q8 < 4; ++q8) {
+            uint4 u;
+            u.x = Act<T>::pack2(__uint_as_float(v[8 * q8 + 0]) * inv, __uint_as_float(v[8 * q8 + 1]) * inv);
+            u.y = Act<T>::pack2(__uint_as_float(v[8 * q8 + 2]) * inv, __uint_as_float(v[8 * q8 + 3]) * inv);
+            u.z = Act<T>::pack2(__uint_as_float(v[8 * q8 + 4]) * inv, __uint_as_float(v[8 * q8 + 5]) * inv);
+            u.w = Act<T>::pack2(__uint_as_float(v[8 * q8 + 6]) * inv, __uint_as_float(v[8 * q8 + 7]) * inv);
+            *reinterpret_cast<uint4*>(dst + c2 * 32 + 8 * q8) = u;
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&o_empty[x]);  // O_x may be overwritten by the next item's first PV
+      ++wn;
+    }
+    if (!ok) *abort_v = 1;
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0 && abort_s) report_timeout(status, kSiteAttnPrefill);
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kPpTmemCols);
+  }
+}
+
 size_t attn_prefill_smem_bytes() { return 1024 + kPfQBytes + 2 * kPfPBytes + kPfStages * kPfKvBytes; }
 
 }  // namespace
 
 cudaError_t init_attn_prefill() {
-  const int bytes = (int)attn_prefill_smem_bytes();
-  cudaError_t e = cudaFuncSetAttribute(k_attn_prefill_tc<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       bytes);
-  if (e != cudaSuccess) return e;
-  return cudaFuncSetAttribute(k_attn_prefill_tc<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  const int bytes = (int)attn_prefill_smem_bytes(), pp = (int)attn_pp_smem_bytes();
+  for (cudaError_t e :
+       {cudaFuncSetAttribute(k_attn_prefill_tc<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes),
+        cudaFuncSetAttribute(k_attn_prefill_tc<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes),
+        cudaFuncSetAttribute(k_attn_prefill_pp<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, pp),
+        cudaFuncSetAttribute(k_attn_prefill_pp<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, pp)})
+    if (e != cudaSuccess) return e;
+  return cudaSuccess;
 }
 
 void launch_attn_prefill_tc(ActType at, const void* kv_tmap, const void* q_tmap, const Plan& p, int PB, int Hq,
                             int Hkv, const KvView& kv, int layer, float scale, void* ctx, int* status,
-                            cudaStream_t s) {
+                            cudaStream_t s, int persistent_ctas) {
   const float scale_log2 = scale * 1.4426950408889634f;
   const CUtensorMap& km = *reinterpret_cast<const CUtensorMap*>(kv_tmap);
   const CUtensorMap& qm = *reinterpret_cast<const CUtensorMap*>(q_tmap);
+  if (persistent_ctas > 0) {
+    // at most one work per CTA is never idle: PB * Hkv bounds the works
+    const int grid = std::min(persistent_ctas, PB * Hkv);
+    const size_t smem = attn_pp_smem_bytes();
+    if (at == kBF16)
+      launch_pdl(k_attn_prefill_pp<__nv_bfloat16>, dim3(grid), dim3(kPpThreads), smem, s, km, qm, p, Hq, Hkv, kv,
+                 layer, scale_log2, (__nv_bfloat16*)ctx, status);
+    else
+      launch_pdl(k_attn_prefill_pp<__half>, dim3(grid), dim3(kPpThreads), smem, s, km, qm, p, Hq, Hkv, kv, layer,
+                 scale_log2, (__half*)ctx, status);
+    return;
+  }
   const size_t smem = attn_prefill_smem_bytes();
   if (at == kBF16)
     launch_pdl(k_attn_prefill_tc<__nv_bfloat16>, dim3(PB, Hkv), dim3(192), smem, s, km, qm, p, Hq, Hkv, kv, layer,

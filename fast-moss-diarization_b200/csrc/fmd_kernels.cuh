@@ -240,12 +240,14 @@ void launch_linear(ActType at, const LinW& W, const void* x, int ldx, const int*
 void launch_qkv_epilogue(ActType at, const Plan& p, int R, const float* part, PartSplit split, size_t split_stride,
                          int Hq, int Hkv, const void* qn_w, const void* kn_w, const void* cos, const void* sin,
                          void* q_out, const KvView& kv, int layer, float eps, cudaStream_t s);
-// fmd_attn_prefill.cu: chunked-prefill flash attention on tcgen05, one CTA per
-// (prefill block, kv head); `q_tmap` views the query buffer as [rows][Hq x 128].
+// fmd_attn_prefill.cu: chunked-prefill flash attention on tcgen05; `q_tmap`
+// views the query buffer as [rows][Hq x 128]. With persistent_ctas > 0,
+// that many persistent CTAs (k_attn_prefill_pp, two query tiles per CTA),
+// else one CTA per (prefill block, kv head) (k_attn_prefill_tc).
 cudaError_t init_attn_prefill();
 void launch_attn_prefill_tc(ActType at, const void* kv_tmap, const void* q_tmap, const Plan& p, int PB, int Hq,
                             int Hkv, const KvView& kv, int layer, float scale, void* ctx, int* status,
-                            cudaStream_t s);
+                            cudaStream_t s, int persistent_ctas = 0);
 void launch_residual_norm(ActType at, const int* n_rows_ptr, int R, void* x, const float* part, PartSplit split,
                           size_t split_stride, const void* w, void* xn, int H, float eps, cudaStream_t s);
 void launch_silu_mul(ActType at, const int* n_rows_ptr, int R, const float* part, PartSplit split, size_t split_stride,

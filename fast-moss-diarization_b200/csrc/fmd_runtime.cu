@@ -138,6 +138,7 @@ struct fmd_handle {
   int n_sm = 0;
   bool proj_allowed = true;  // mixed steps on k_proj_tc (fused epilogues); FMD_PROJ_TC=0 selects k_gemm_tc
   bool lm_tc_allowed = true;  // Q8_0 lm_head on the tensor cores; FMD_LM_HEAD_TC=0 selects the mma.sync kernel
+  bool pf_pp_allowed = true;  // persistent two-tile prefill attention; FMD_PREFILL_PP=0 selects one CTA per block
   bool chain_allowed = false;
   bool chain_ok = false;
   size_t chain_smem = 0;
@@ -653,7 +654,7 @@ void run_forward(fmd_handle* h, float* logits_dev, const void* arena, bool decod
     if (probe) cudaEventRecordWithFlags(h->attn_events[1], s, cudaEventRecordExternal);
     trace(h, "attn_decode", l);
     launch_attn_prefill_tc(h->at, &h->kv_tmap, &h->qmap, h->plan, h->pb_max, h->Hq(), h->Hkv(), h->kv, l,
-                           h->attn_scale, h->ctx, h->d_status, s);
+                           h->attn_scale, h->ctx, h->d_status, s, h->pf_pp_allowed ? h->n_sm : 0);
     trace(h, "attn_prefill", l);
     const PartSplit sp_o = run_proj(L.tc_o, h->amap_ctx, kProjF32, pf32)
                                ? PartSplit{1, 1}
@@ -911,6 +912,8 @@ int fmd_create(const fmd_config* cfg, int32_t precision, int32_t device, fmd_han
     h->proj_allowed = !(p != nullptr && p[0] == '0');
     const char* lt = std::getenv("FMD_LM_HEAD_TC");
     h->lm_tc_allowed = !(lt != nullptr && lt[0] == '0');
+    const char* pp = std::getenv("FMD_PREFILL_PP");
+    h->pf_pp_allowed = !(pp != nullptr && pp[0] == '0');
   }
   if (cudaDeviceGetAttribute(&h->n_sm, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || h->n_sm < 1) {
     cudaGetLastError();
@@ -1740,7 +1743,8 @@ int fmd_debug_wait_timeout(fmd_handle* h, int32_t limit) {
 int fmd_debug_paths(const fmd_handle* h, int32_t* flags) {
   if (!h || !flags) return FMD_EINVAL;
   *flags = (h->chain_ok ? FMD_PATH_LAYER_TAIL : 0) | (h->tc_ready && h->proj_allowed ? FMD_PATH_PROJ_TC : 0) |
-           (h->lm_tc_allowed && h->lm_head.q8 && h->max_slots <= 64 ? FMD_PATH_LM_HEAD_TC : 0);
+           (h->lm_tc_allowed && h->lm_head.q8 && h->max_slots <= 64 ? FMD_PATH_LM_HEAD_TC : 0) |
+           (h->pf_pp_allowed ? FMD_PATH_PREFILL_PP : 0);
   return FMD_OK;
 }
 

@@ -333,3 +333,48 @@ def test_lm_head_on_the_tensor_cores(prec, n, monkeypatch):
         want = m.decode_step(int(toks[s]), cs).numpy()
         assert rel_err(lg_tc[s], want) < LOGIT_RTOL, s
         check_pick(int(ids_tc[s]), lg_tc[s], want)
+
+
+@pytest.mark.parametrize("prec", ["bf16", "int8"])
+def test_prefill_attention_persistent_two_tile_is_bit_identical(prec, monkeypatch):
+    """Prefill attention on persistent CTAs with two query tiles each
+    (k_attn_prefill_pp: pairs of consecutive 64-row blocks of a sequence per
+    kv head, the snake work order, S / P / PV counts carried across a CTA's
+    items) computes exactly what the one-CTA-per-block kernel does (the same
+    MMAs, softmax and lazy rescale per tile): the logits of both paths are
+    bit-identical, and match the oracle. Sequences with an even and an odd
+    number of blocks, a lone block, a one-row block and histories across
+    chunks."""
+    cfg = mid_config(num_hidden_layers=1)
+    w = syn.make_weights(cfg, seed=31)
+    m = oracle_model(cfg, w, prec, max_len=4096)
+    rng = np.random.default_rng(17)
+    lens = [2600, 1333, 64, 65, 1, 700]
+    prompts = [rng.standard_normal((n, cfg.hidden_size), dtype=np.float32) for n in lens]
+    got = {}
+    for pp in ("1", "0"):
+        monkeypatch.setenv("FMD_PREFILL_PP", pp)
+        with make_decoder(cfg, w, prec, slots=len(lens), tokens=8192, rows=2048) as dec:
+            assert dec.debug_paths()["prefill_pp"] == (pp == "1")
+            for s, n in enumerate(lens):
+                dec.open_slot(s, n + 8)
+            done = [0] * len(lens)
+            last = [None] * len(lens)
+            while any(d < n for d, n in zip(done, lens)):
+                slots, parts, budget = [], [], 2000
+                for s, n in enumerate(lens):
+                    take = min(1000, n - done[s], budget)
+                    if take > 0:
+                        slots.append(s)
+                        parts.append(prompts[s][done[s]:done[s] + take])
+                        done[s] += take
+                        budget -= take
+                lg, _ = dec.prefill(slots, parts)
+                for i, s in enumerate(slots):
+                    last[s] = lg[i]
+            got[pp] = np.stack(last)
+    assert np.array_equal(got["1"], got["0"])
+    for s, n in enumerate(lens):
+        caches = m.new_caches(1, n + 8)
+        want = m.logits(m.prefill(prompts[s][None], caches))[0, 0].numpy()
+        assert rel_err(got["1"][s], want) < LOGIT_RTOL, s
