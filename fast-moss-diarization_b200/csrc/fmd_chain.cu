@@ -41,6 +41,7 @@
 #include <math.h>
 
 #include <algorithm>
+#include <cstdio>
 
 #include "fmd_gemv.cuh"
 #include "fmd_kernels.cuh"
@@ -424,16 +425,24 @@ cudaError_t max_clusters(size_t smem, int* n) {
 // The cluster count and shared memory of the layer tail for rows <= 32:
 // as many clusters as the GPU holds at once (at most one per 8 SMs), fewer
 // if the weights of the CTAs then no longer fit. False if it cannot run.
-bool chain_plan(ActType at, const ChainArgs& a, int n_sm, int max_rows, int* n_clusters, size_t* smem) {
-  if (max_rows > kChainMaxRows || n_sm < kCS) return false;
+bool chain_plan(ActType at, const ChainArgs& a, int n_sm, int max_rows, int* n_clusters, size_t* smem, char* why,
+                size_t why_len) {
+  if (max_rows > kChainMaxRows || n_sm < kCS) {
+    snprintf(why, why_len, "max_rows %d > %d or %d SMs", max_rows, kChainMaxRows, n_sm);
+    return false;
+  }
   int nc = n_sm / kCS;
   for (int iter = 0; iter < 8 && nc >= 1; ++iter) {
     const size_t b = tail_smem(a, nc);
-    if (b == 0 || b > 226 * 1024) return false;
+    if (b == 0 || b > 226 * 1024) {
+      snprintf(why, why_len, "%d clusters: shared memory %zu bytes (0 = shapes not served)", nc, b);
+      return false;
+    }
     int fit = 0;
     const cudaError_t e =
         at == kBF16 ? max_clusters<__nv_bfloat16>(b, &fit) : max_clusters<__half>(b, &fit);
     if (e != cudaSuccess) {
+      snprintf(why, why_len, "%d clusters of %zu bytes: %s", nc, b, cudaGetErrorString(e));
       cudaGetLastError();
       return false;
     }
@@ -442,6 +451,7 @@ bool chain_plan(ActType at, const ChainArgs& a, int n_sm, int max_rows, int* n_c
       *smem = b;
       return true;
     }
+    snprintf(why, why_len, "%d clusters of %zu bytes requested, %d resident at once", nc, b, fit);
     nc = fit;
   }
   return false;

@@ -84,6 +84,10 @@ FMD_DEV uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_g
 FMD_DEV void cp_async16(void* smem, const void* gmem, int bytes = 16) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(smem_u32(smem)), "l"(gmem), "r"(bytes));
 }
+// 4-byte async copy global->shared (through L1: .ca is the only mode for 4 bytes).
+FMD_DEV void cp_async4(void* smem, const void* gmem) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(smem_u32(smem)), "l"(gmem));
+}
 FMD_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
 template <int N> FMD_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
 

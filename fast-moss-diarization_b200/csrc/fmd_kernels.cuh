@@ -258,7 +258,8 @@ void launch_dequant(ActType at, const LinW& W, float* out, cudaStream_t s);
 // fmd_chain.cu: the cluster count and shared-memory bytes of the layer tail
 // for up to `max_rows` rows on `n_sm` SMs (false when it cannot run; sets the
 // kernels' shared-memory limit), and its launch.
-bool chain_plan(ActType at, const ChainArgs& a, int n_sm, int max_rows, int* n_clusters, size_t* smem);
+bool chain_plan(ActType at, const ChainArgs& a, int n_sm, int max_rows, int* n_clusters, size_t* smem, char* why,
+                size_t why_len);
 void launch_layer_tail(ActType at, const ChainArgs& a, int n_clusters, size_t smem, cudaStream_t s);
 // One bounded wait that runs out after `limit` tries and sets *status to
 // FMD_ETIMEDOUT (the failure path of every ring kernel's waits).

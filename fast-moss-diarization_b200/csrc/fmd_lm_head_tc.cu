@@ -55,6 +55,7 @@ constexpr int kLhThreads = (2 + kLhConvWarps + kLhEpiWarps) * 32;  // 448
 constexpr int kLhTmemCols = 256;
 constexpr int kLhLgStride = 132;                   // row stride (floats) of the rounded-logit tile
 constexpr uint32_t kLhWaitLimit = 1u << 24;
+constexpr int kScaleAhead = 8;                     // stages of block scales in flight per epilogue thread
 
 template <int NR>
 struct LhCfg {
@@ -84,6 +85,7 @@ __global__ void __launch_bounds__(kLhThreads, 1)
       acc_empty[ACC], mma_done;
   __shared__ uint32_t tmem_base_s;
   __shared__ float rs_s[NR];
+  __shared__ uint32_t sc_ring[kScaleAhead][kLhFeat];
   __shared__ int abort_s, stop_s;
   griddep_launch();
 
@@ -306,13 +308,18 @@ __global__ void __launch_bounds__(kLhThreads, 1)
     for (int h = 0; h < NR / 32; ++h) rb_v[h] = -INFINITY, rb_i[h] = 0x7fffffff;
     bool ok = true;  // this warp's waits all passed
     int g = 0;
-    // scale words (block 0 | block 1 f16) of this feature, one stage ahead
-    auto scale_at = [&](int i, int kb) -> uint32_t {
-      const int tile = blockIdx.x + i * gridDim.x;
-      const uint8_t* un = W.pk + ((size_t)tile * nkb + kb) * kLhRaw + (size_t)(fl >> 4) * kUnitQ8 + 1024;
-      return __ldg(reinterpret_cast<const uint32_t*>(un) + (fl & 15));
+    // scale words (block 0 | block 1 f16) of this feature: each thread copies
+    // its own word of stage g + kScaleAhead into a private ring slot with
+    // cp.async (one group per stage), far enough ahead to hide the L2 latency
+    auto scale_fetch = [&](int gs) {
+      if (gs < n_stages) {
+        const int tile = blockIdx.x + (gs / nkb) * gridDim.x, kb = gs % nkb;
+        const uint8_t* un = W.pk + ((size_t)tile * nkb + kb) * kLhRaw + (size_t)(fl >> 4) * kUnitQ8 + 1024;
+        cp_async4(&sc_ring[gs % kScaleAhead][fl], reinterpret_cast<const uint32_t*>(un) + (fl & 15));
+      }
+      cp_async_commit();  // an empty group past the end keeps the group count per stage
     };
-    uint32_t sc_next = n_stages > 0 ? scale_at(0, 0) : 0u;
+    for (int gs = 0; gs < kScaleAhead - 1; ++gs) scale_fetch(gs);
     // The four warps take every tile's named barriers together whatever
     // their waits did: a warp whose wait gave up skips its tensor-memory
     // work, and all stop after the tile on a flag read between barriers.
@@ -322,8 +329,9 @@ __global__ void __launch_bounds__(kLhThreads, 1)
 #pragma unroll
       for (int j = 0; j < NR; ++j) acc[j] = 0.f;
       for (int kb = 0; kb < nkb && ok; ++kb, ++g) {
-        const uint32_t sc = sc_next;
-        if (g + 1 < n_stages) sc_next = kb + 1 < nkb ? scale_at(i, kb + 1) : scale_at(i + 1, 0);
+        scale_fetch(g + kScaleAhead - 1);
+        cp_async_wait<kScaleAhead - 1>();  // this stage's group has landed
+        const uint32_t sc = sc_ring[g % kScaleAhead][fl];
         const float2 d = __half22float2(*reinterpret_cast<const __half2*>(&sc));
         for (int b = 0; b < 2 && ok; ++b) {
           const int B = 2 * g + b, a = B % ACC;
@@ -385,6 +393,7 @@ __global__ void __launch_bounds__(kLhThreads, 1)
       named_sync(1, NE);
       if (stop_s) break;
     }
+    cp_async_wait<0>();  // no scale copy may land after the CTA retires
     if (fq == 0) {
 #pragma unroll
       for (int h = 0; h < NR / 32; ++h) {

@@ -1094,8 +1094,11 @@ int fmd_kv_reserve(fmd_handle* h, int32_t max_slots, int64_t max_tokens_total, i
   h->chain_ok = false;
   if (h->q8 && h->chain_allowed && max_slots <= kChainMaxRows && c.num_hidden_layers > 0) {
     // every layer has the shapes of layer 0
-    h->chain_ok = chain_plan(h->at, make_chain(h, 0), h->n_sm, max_slots, &h->chain_clusters, &h->chain_smem);
+    char why[160] = "";
+    h->chain_ok = chain_plan(h->at, make_chain(h, 0), h->n_sm, max_slots, &h->chain_clusters, &h->chain_smem, why,
+                             sizeof(why));
     cudaGetLastError();
+    if (!h->chain_ok) std::fprintf(stderr, "[fmd] layer tail requested but unavailable: %s\n", why);
   }
   h->pb_max = R / kRowsPerPBlock + max_slots;
   h->di_max = (int)std::min<int64_t>((int64_t)max_slots * h->max_pages_per_slot,

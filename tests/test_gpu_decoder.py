@@ -325,14 +325,26 @@ def test_lm_head_on_the_tensor_cores(prec, n, monkeypatch):
             got[tc] = dec.decode_step(list(range(n)), toks)
     lg_tc, ids_tc = got["1"]
     lg_ref, _ = got["0"]
-    ulp = np.spacing(np.abs(lg_ref).astype(np.float32)) * (2.0 ** (16 if prec == "int8_bf16" else 13))
-    assert np.all(np.abs(lg_tc - lg_ref) <= ulp + 1e-30), float(np.max(np.abs(lg_tc - lg_ref) / (ulp + 1e-30)))
+    worst = (0.0, None)
     for s in range(n):
         cs = m.new_caches(1, int(lens[s]) + 2)
         m.prefill(prompts[s][None], cs)
         want = m.decode_step(int(toks[s]), cs).numpy()
-        assert rel_err(lg_tc[s], want) < LOGIT_RTOL, s
+        e_tc, e_ref = rel_err(lg_tc[s], want), rel_err(lg_ref[s], want)
+        # the two kernels differ by the f32 summation order inside a block
+        # and across blocks: elementwise within one unit in the last place
+        # of the activation type at the row's largest logit
+        scale = float(np.abs(want).max())
+        d = np.abs(lg_tc[s] - lg_ref[s])
+        j = int(np.argmax(d))
+        if d[j] / scale > worst[0]:
+            worst = (float(d[j] / scale), (s, j, float(lg_tc[s][j]), float(lg_ref[s][j]), float(want[j])))
+        assert e_tc < LOGIT_RTOL, s
+        assert e_tc <= 1.25 * e_ref + 1e-4, (s, e_tc, e_ref)
         check_pick(int(ids_tc[s]), lg_tc[s], want)
+    print(f"\nlm_head tc [{prec}, {n} rows]: largest difference to the mma.sync kernel {worst[0]:.3g} of the row "
+          f"max (row, col, tc, mma.sync, oracle) = {worst[1]}")
+    assert worst[0] <= 2.0 ** (-7 if prec == "int8_bf16" else -10), worst
 
 
 @pytest.mark.parametrize("prec", ["bf16", "int8"])
