@@ -75,8 +75,11 @@ __global__ void __launch_bounds__(160, 2)
   uint64_t* empty = full + kStages;
   __shared__ int s_last;
 
-  griddep_launch();
-  griddep_wait();
+  // The plan, the page table and the KV rows of earlier steps come from
+  // grids that completed before this one started (griddep_launch): the
+  // prologue and the first page tiles go ahead of the dependency wait. The
+  // query rows and each row's newest K/V (the last tile of its segment) come
+  // from the kernel right before: the producer waits before those copies.
   const int nd = min(p.counts->n_decode, kMaxRows);
   if (nd == 0) return;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
@@ -143,8 +146,11 @@ __global__ void __launch_bounds__(160, 2)
 
   if (warp == 4) {
     // ---------------- producer warp: TMA tiles + query rows, runs ahead ----------------
-    bool ok = true;
+    bool ok = true, waited = false;
     int issued = 0;
+    // copies held back until the dependency wait: stage s's query rows
+    // (row, head) and its newest K/V page
+    int held_q[kStages], held_kv[kStages], held_y[kStages];
     for (int b0 = 0; b0 < ntl && ok; b0 += 32) {
       // lane i looks up tile b0 + i: its row, head, tile index and page
       int lr = 0, lh = 0, lj = 0, lpage = 0;
@@ -157,25 +163,70 @@ __global__ void __launch_bounds__(160, 2)
         const int r = __shfl_sync(0xffffffffu, lr, i), h = __shfl_sync(0xffffffffu, lh, i);
         const int j = __shfl_sync(0xffffffffu, lj, i), page = __shfl_sync(0xffffffffu, lpage, i);
         const int tt = b0 + i, s = tt % kStages;
+        if (!waited && tt >= kStages) {
+          // the ring is full: wait for the kernel before, then issue what was held back
+          griddep_wait();
+          griddep_launch();  // only after the wait: see griddep_launch
+          waited = true;
+          if (lane == 0)
+            for (int k = 0; k < kStages; ++k) {
+              uint8_t* dst = stages + k * kTileBytes;
+              if (held_kv[k]) {
+                tma_load_2d(dst, &tmap, 0, held_y[k], &full[k]);
+                tma_load_2d(dst + kBoxBytes, &tmap, 64, held_y[k], &full[k]);
+                tma_load_2d(dst + 2 * kBoxBytes, &tmap, 0, held_y[k] + Hkv * kPageTokens, &full[k]);
+                tma_load_2d(dst + 3 * kBoxBytes, &tmap, 64, held_y[k] + Hkv * kPageTokens, &full[k]);
+              }
+              if (held_q[k] >= 0) bulk_load(qbuf + k * kQBytes, q + (size_t)held_q[k], kQBytes, &full[k]);
+            }
+          __syncwarp();
+        }
         if (tt >= kStages && !mbar_wait_bounded(&empty[s], ((tt / kStages) - 1) & 1, kWaitLimit)) {
           ok = false;
           break;
         }
         if (lane == 0) {
           const bool first = tt == 0 || j == 0;
+          const bool newest = j == ((s_len[r] + 63) >> 6) - 1;  // holds the row's own (new) position
           const int yk = (int)(((((size_t)layer * kv.n_pages + page) * 2 + 0) * Hkv + h) * kPageTokens);
           const int yv = yk + Hkv * kPageTokens;
           uint8_t* dst = stages + s * kTileBytes;
+          const int qoff = r * Hq * kHeadDim + 2 * h * kHeadDim;
           mbar_arrive_expect_tx(&full[s], kTileBytes + (first ? kQBytes : 0));
-          tma_load_2d(dst, &tmap, 0, yk, &full[s]);
-          tma_load_2d(dst + kBoxBytes, &tmap, 64, yk, &full[s]);
-          tma_load_2d(dst + 2 * kBoxBytes, &tmap, 0, yv, &full[s]);
-          tma_load_2d(dst + 3 * kBoxBytes, &tmap, 64, yv, &full[s]);
-          if (first) bulk_load(qbuf + s * kQBytes, q + (size_t)r * Hq * kHeadDim + 2 * h * kHeadDim, kQBytes, &full[s]);
+          if (waited || !newest) {
+            tma_load_2d(dst, &tmap, 0, yk, &full[s]);
+            tma_load_2d(dst + kBoxBytes, &tmap, 64, yk, &full[s]);
+            tma_load_2d(dst + 2 * kBoxBytes, &tmap, 0, yv, &full[s]);
+            tma_load_2d(dst + 3 * kBoxBytes, &tmap, 64, yv, &full[s]);
+          }
+          if (first && waited) bulk_load(qbuf + s * kQBytes, q + (size_t)qoff, kQBytes, &full[s]);
+          if (!waited) {
+            held_kv[s] = newest;
+            held_y[s] = yk;
+            held_q[s] = first ? qoff : -1;
+          }
         }
         __syncwarp();
         issued = tt + 1;
       }
+    }
+    if (!waited) {
+      // fewer tiles than stages: everything held back goes out now
+      griddep_wait();
+      griddep_launch();  // only after the wait: see griddep_launch
+      waited = true;
+      if (lane == 0 && ok)
+        for (int k = 0; k < kStages && k < issued; ++k) {
+          uint8_t* dst = stages + k * kTileBytes;
+          if (held_kv[k]) {
+            tma_load_2d(dst, &tmap, 0, held_y[k], &full[k]);
+            tma_load_2d(dst + kBoxBytes, &tmap, 64, held_y[k], &full[k]);
+            tma_load_2d(dst + 2 * kBoxBytes, &tmap, 0, held_y[k] + Hkv * kPageTokens, &full[k]);
+            tma_load_2d(dst + 3 * kBoxBytes, &tmap, 64, held_y[k] + Hkv * kPageTokens, &full[k]);
+          }
+          if (held_q[k] >= 0) bulk_load(qbuf + k * kQBytes, q + (size_t)held_q[k], kQBytes, &full[k]);
+        }
+      __syncwarp();
     }
     if (!ok && lane == 0) {
       report_timeout(status, kSiteAttnDecode);
@@ -187,6 +238,10 @@ __global__ void __launch_bounds__(160, 2)
   }
 
   // ---------------- consumer warps 0..3: 16 positions of every tile each ----------------
+  // ctx, the split partials and the merge counters are written only after
+  // the kernel before has completed (it may still read ctx of the layer
+  // before); the first tile's query rows arrive only after that anyway
+  griddep_wait();
   bool aborted = false;
   int cr, ch, cj;  // the tile being consumed, walked forward from x0
   locate(x0, cr, ch, cj);

@@ -71,7 +71,6 @@ __global__ void __launch_bounds__(192, 1)
   __shared__ uint32_t tmem_base_s;
   __shared__ int abort_s, block_s;
   __shared__ int klen_s[kMaxPrefillBlocks];
-  griddep_launch();
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t raw = smem_u32(smem_raw);
@@ -81,6 +80,7 @@ __global__ void __launch_bounds__(192, 1)
   uint8_t* p_sp = base_p + kPfQBytes;
 
   griddep_wait();  // q, the KV rows of this step and the plan come from earlier kernels
+  griddep_launch();  // only after the wait: see griddep_launch
   const int n_blocks = min(p.counts->n_pblocks, kMaxPrefillBlocks);
   if ((int)blockIdx.x >= n_blocks) return;  // whole CTA, before any barrier or tensor memory exists
   // CTA x takes the block of rank x by kv length (longest first, ties by index)
@@ -394,7 +394,6 @@ __global__ void __launch_bounds__(kPpThreads, 1)
       s_empty[2][2], p_full[2], pv_done[2], o_final[2], o_empty[2], mma_done;
   __shared__ uint32_t tmem_base_s;
   __shared__ int abort_s, n_items_s;
-  griddep_launch();
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t raw = smem_u32(smem_raw);
@@ -408,6 +407,7 @@ __global__ void __launch_bounds__(kPpThreads, 1)
   int* s_order = s_cost + kMaxPrefillBlocks;
 
   griddep_wait();  // q, the KV rows of this step and the plan come from earlier kernels
+  griddep_launch();  // only after the wait: see griddep_launch
   const int n_blocks = min(p.counts->n_pblocks, kMaxPrefillBlocks);
   if (n_blocks == 0) return;  // whole CTA, before any barrier or tensor memory exists
   auto tiles_of = [&](int b) { return (p.row_pos[p.pb_row0[b]] + p.pb_n[b] + kPageTokens - 1) / kPageTokens; };

@@ -130,7 +130,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_layer_tail(ChainArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t wbar[kMaxUnits];
   __shared__ float rs_s[kTailRows];
-  griddep_launch();
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = (int)cluster.block_rank();
   const int NC = gridDim.x / kCS, cl = blockIdx.x / kCS;
@@ -177,6 +176,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_layer_tail(ChainArgs a) {
   }
   __syncthreads();  // barrier initialisation visible to every thread
   griddep_wait();   // ctx (attention) and every earlier write are visible
+  griddep_launch();  // only after the wait: see griddep_launch
 
   const int n_rows = min(*a.n_rows_ptr, kTailRows);
   const int n_nt = (n_rows + 7) >> 3;

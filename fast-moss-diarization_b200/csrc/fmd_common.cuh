@@ -114,12 +114,14 @@ FMD_DEV int4 ld_stream16(const void* p) {
 // f16 bits -> f32 (exact).
 FMD_DEV float h2f_bits(uint16_t b) { return __half2float(__ushort_as_half(b)); }
 
-// Programmatic dependent launch: every kernel of a step lets the next one be
-// scheduled as soon as it starts (griddep_launch), and touches data written
-// by earlier kernels only after griddep_wait, which returns once the
-// preceding grid has completed and its writes are visible. Work that reads
-// nothing from earlier kernels (weight prefetch, barrier set-up) goes before
-// the wait. Both are no-ops for a kernel launched without the attribute.
+// Programmatic dependent launch. griddep_wait returns once the preceding
+// grid has completed and its writes are visible; a kernel touches data of
+// the kernel right before it only after the wait. Every kernel lets the next
+// one be scheduled (griddep_launch) only after its own wait: a kernel that
+// starts therefore finds every grid before its predecessor completed, and
+// may read their results (the step's plan, the page table, KV rows of
+// earlier steps) and prefetch weights before its own wait. Both are no-ops
+// for a kernel launched without the attribute.
 FMD_DEV void griddep_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
 FMD_DEV void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
 

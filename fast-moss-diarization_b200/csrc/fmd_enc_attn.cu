@@ -79,7 +79,6 @@ __global__ void __launch_bounds__(192, 2)
       p_full[2], p_empty[2], o_full, o_final, mma_done;
   __shared__ uint32_t tmem_base_s;
   __shared__ int abort_s;
-  griddep_launch();
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t raw = smem_u32(smem_raw);
@@ -114,6 +113,7 @@ __global__ void __launch_bounds__(192, 2)
   // then finished, so none of its CTAs can hold the columns this CTA needs
   // while it waits for this one.
   griddep_wait();  // qkv comes from the previous kernel
+  griddep_launch();  // only after the wait: see griddep_launch
   if (warp == 1) {
     tmem_alloc(&tmem_base_s, kEaTmemCols);
     tmem_relinquish();

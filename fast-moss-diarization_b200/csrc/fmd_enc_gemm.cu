@@ -123,7 +123,6 @@ __global__ void __launch_bounds__(kEgThreads, 1)
   __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES], acc_full[2], acc_empty[2], mma_done;
   __shared__ uint32_t tmem_base_s;
   __shared__ int abort_s;
-  griddep_launch();
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t raw = smem_u32(smem_raw);
@@ -150,6 +149,7 @@ __global__ void __launch_bounds__(kEgThreads, 1)
   // then finished, so none of its CTAs can hold the columns this CTA needs
   // while it waits for this one.
   griddep_wait();  // A (and the residual stream) come from earlier kernels
+  griddep_launch();  // only after the wait: see griddep_launch
   if (warp == 1) {
     tmem_alloc(&tmem_base_s, TMEM_COLS);
     tmem_relinquish();

@@ -64,7 +64,6 @@ __global__ void __launch_bounds__(192, 1)
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES], conv[STAGES], done;
   __shared__ uint32_t tmem_base_s;
-  griddep_launch();
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t raw = smem_u32(smem_raw);
@@ -72,6 +71,7 @@ __global__ void __launch_bounds__(192, 1)
   uint8_t* tiles_p = smem_raw + (tiles - raw);
 
   griddep_wait();  // X and the row count come from earlier kernels
+  griddep_launch();  // only after the wait: see griddep_launch
   const int n_rows = *n_rows_ptr;
   const int row0 = blockIdx.x * kTcBM;
   if (row0 >= n_rows) return;  // whole CTA, before any barrier or tensor memory exists

@@ -67,7 +67,6 @@ __global__ void __launch_bounds__(FW * KG * 32) k_gemv(const T* __restrict__ x, 
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t wbar[kMaxKb];
   __shared__ float rs_s[kRows];
-  griddep_launch();
 
   const int S = gridDim.y, rank = blockIdx.y;
   const int K = W.K;
@@ -103,6 +102,7 @@ __global__ void __launch_bounds__(FW * KG * 32) k_gemv(const T* __restrict__ x, 
     }
   }
   griddep_wait();
+  griddep_launch();  // only after the wait: see griddep_launch
 
   const int n_rows = *n_rows_ptr;
   const int row0 = blockIdx.z * kRows;
@@ -479,7 +479,6 @@ __global__ void __launch_bounds__((G * kHeadWarps + 1) * 32, 1)
   __shared__ float cand_v[NCW][NTL * 8];
   __shared__ int cand_i[NCW][NTL * 8];
   __shared__ int abort_s;
-  griddep_launch();
 
   const int K = W.K, nkb = K / 64;
   const int n_tiles = W.N / FT;
@@ -533,11 +532,13 @@ __global__ void __launch_bounds__((G * kHeadWarps + 1) * 32, 1)
     produced:;
     }
     griddep_wait();
+    griddep_launch();  // only after the wait: see griddep_launch
     return;  // nothing below touches the producer warp
   }
 
   // ---- consumers (512 threads): normalised activation tile, then the ring
   griddep_wait();
+  griddep_launch();  // only after the wait: see griddep_launch
   const int n_rows = *n_rows_ptr;
   const int row0 = blockIdx.y * NTL * 8;
   const int rows = max(0, min(min(NTL * 8, xrows), n_rows - row0));
@@ -724,8 +725,8 @@ __global__ void __launch_bounds__(256) k_pick_reduce(const int* __restrict__ n_s
                                                      int* __restrict__ status) {
   __shared__ float sv[8];
   __shared__ int si[8];
-  griddep_launch();
   griddep_wait();
+  griddep_launch();  // only after the wait: see griddep_launch
   const int n = *n_sample_ptr;
   for (int r = blockIdx.x; r < n; r += gridDim.x) {
     float best = -INFINITY;

@@ -43,8 +43,8 @@ __global__ void __launch_bounds__(128) k_embed_norm(Plan p, const T* __restrict_
                                                     int H, float eps, float* __restrict__ ssq, int ssq_tiles,
                                                     int* __restrict__ zero, int zero_n) {
   __shared__ float red[4];
-  griddep_launch();
   griddep_wait();
+  griddep_launch();  // only after the wait: see griddep_launch
   if (zero != nullptr)
     for (int i = blockIdx.x * 128 + threadIdx.x; i < zero_n; i += gridDim.x * 128) zero[i] = 0;
   const int n_rows = p.counts->n_rows;
@@ -95,8 +95,8 @@ __global__ void __launch_bounds__(128) k_residual_norm(const int* __restrict__ n
                                                        size_t split_stride, const T* __restrict__ w,
                                                        T* __restrict__ xn, int H, float eps) {
   __shared__ float red[4];
-  griddep_launch();
   griddep_wait();
+  griddep_launch();  // only after the wait: see griddep_launch
   const int n_rows = *n_rows_ptr;
   const int S = split.at(n_rows);
   for (int r = blockIdx.x; r < n_rows; r += gridDim.x) {
@@ -174,7 +174,6 @@ __global__ void __launch_bounds__(128) k_linear(const T* __restrict__ x, int ldx
                                                 const int* __restrict__ n_rows_ptr, LinW W, float* __restrict__ out,
                                                 size_t split_stride, int decode_only) {
   __shared__ __align__(16) T xs[2][64][72];
-  griddep_launch();
   const int K = W.K, N = W.N;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int f0 = blockIdx.x * 64 + warp * 16 + g;
@@ -206,6 +205,7 @@ __global__ void __launch_bounds__(128) k_linear(const T* __restrict__ x, int ldx
     pre = true;
   }
   griddep_wait();
+  griddep_launch();  // only after the wait: see griddep_launch
   const int n_rows = *n_rows_ptr;
   const int S = effective_split(W.split, n_rows);
   if ((int)blockIdx.y >= S) return;
@@ -343,8 +343,8 @@ __global__ void __launch_bounds__(256) k_qkv_epilogue(Plan p, const float* __res
                                                       const T* __restrict__ qn_w, const T* __restrict__ kn_w,
                                                       const T* __restrict__ cos_t, const T* __restrict__ sin_t,
                                                       T* __restrict__ q_out, KvView kv, int layer, float eps) {
-  griddep_launch();
   griddep_wait();
+  griddep_launch();  // only after the wait: see griddep_launch
   const int n_rows = p.counts->n_rows;
   const int S = split.at(n_rows);
   const int N = (Hq + 2 * Hkv) * kHeadDim;
@@ -403,8 +403,8 @@ __global__ void __launch_bounds__(256) k_qkv_epilogue(Plan p, const float* __res
 template <typename T>
 __global__ void __launch_bounds__(256) k_silu_mul(const int* __restrict__ n_rows_ptr, const float* __restrict__ part,
                                                   PartSplit split, size_t split_stride, int I, T* __restrict__ h) {
-  griddep_launch();
   griddep_wait();
+  griddep_launch();  // only after the wait: see griddep_launch
   const int n_rows = *n_rows_ptr;
   const int S = split.at(n_rows);
   for (int r = blockIdx.x; r < n_rows; r += gridDim.x) {
@@ -447,8 +447,8 @@ __global__ void __launch_bounds__(1024) k_logits_argmax(const int* __restrict__ 
                                                         float* __restrict__ logits, int* __restrict__ next_ids) {
   __shared__ float sv[32];
   __shared__ int si[32];
-  griddep_launch();
   griddep_wait();
+  griddep_launch();  // only after the wait: see griddep_launch
   const int r = blockIdx.x;
   if (r >= *n_sample_ptr) return;
   const float* pr = part + (size_t)r * V;

@@ -87,7 +87,6 @@ __global__ void __launch_bounds__(kLhThreads, 1)
   __shared__ float rs_s[NR];
   __shared__ uint32_t sc_ring[kScaleAhead][kLhFeat];
   __shared__ int abort_s, stop_s;
-  griddep_launch();
 
   const int K = W.K, nkb = K / 64;
   const int n_tiles = W.N / kLhFeat;
@@ -153,6 +152,7 @@ __global__ void __launch_bounds__(kLhThreads, 1)
     // tensor memory only after the dependency wait: the previous kernel has
     // then finished, so none of its CTAs can wait for these columns
     griddep_wait();
+    griddep_launch();  // only after the wait: see griddep_launch
     tmem_alloc(&tmem_base_s, kLhTmemCols);
     tmem_relinquish();
     tc_fence_before();
@@ -241,6 +241,7 @@ __global__ void __launch_bounds__(kLhThreads, 1)
     constexpr int NE = kLhEpiWarps * 32;
     const int et = threadIdx.x - (2 + kLhConvWarps) * 32;
     griddep_wait();
+    griddep_launch();  // only after the wait: see griddep_launch
     const int rows = min(*n_rows_ptr, NR);
     const bool norm = ep.ssq != nullptr;  // else the rows are already normalised
     if (norm) {

@@ -215,7 +215,6 @@ __global__ void __launch_bounds__(proj_threads<Q8>(), 1)
   __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES], conv[STAGES], acc_full[2], acc_empty[2], mma_done;
   __shared__ uint32_t tmem_base_s;
   __shared__ int abort_s;
-  griddep_launch();
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t raw = smem_u32(smem_raw);
@@ -240,6 +239,7 @@ __global__ void __launch_bounds__(proj_threads<Q8>(), 1)
   // kernel has then finished, so no CTA of it can be left waiting for the
   // columns this CTA holds.
   griddep_wait();  // the activations and the row count come from earlier kernels
+  griddep_launch();  // only after the wait: see griddep_launch
   if (warp == 1) {
     tmem_alloc(&tmem_base_s, TMEM_COLS);
     tmem_relinquish();
