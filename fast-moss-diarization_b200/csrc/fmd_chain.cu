@@ -58,6 +58,7 @@ constexpr int kCS = 8;            // CTAs per cluster = the K split of every pro
 constexpr int kMaxUnits = 16;     // weight units (bulk copies) one CTA may own over the four projections
 constexpr int kTailRows = kChainMaxRows;  // rows served (4 MMA n-tiles)
 static_assert(kTailRows == 32, "the MMA loops hold 4 n-tiles of 8 rows");
+constexpr int kMaxRounds = 4;     // warp tasks (tile, 16 features) per warp and projection
 constexpr uint32_t kWaitLimit = 1u << 22;
 constexpr uint32_t kSpinLimit = 1u << 17;
 
@@ -153,13 +154,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_layer_tail(ChainArgs a) {
       nunits += ntl[p];
     }
   }
-  // then the activation slice of the widest projection, then the f32
-  // partial tiles [tile][row][feature] (rows padded by 4 floats: the MMA
-  // fragment stores hit 32 distinct banks)
-  uint32_t slice_max = 0;
-  for (int p = 0; p < np; ++p) slice_max = max(slice_max, slice_bytes(geom_of(a.ph[p])));
+  // then the activation slice. After a projection's MMAs, its f32 partial
+  // tiles [row][feature] (rows padded by 4 floats: the MMA fragment stores
+  // hit 32 distinct banks) take the place of its weight units.
   uint8_t* act = smem + ((wtot + 127u) & ~127u);
-  float* part = reinterpret_cast<float*>(act + slice_max);
   if (threadIdx.x == 0) {
     for (int i = 0; i < nunits; ++i) mbar_init(&wbar[i], 1);
     fence_barrier_init();
@@ -238,17 +236,22 @@ __global__ void __launch_bounds__(kThreads, 1) k_layer_tail(ChainArgs a) {
         }
         __syncthreads();
       }
-      // warp tasks (tile, 16-feature slice) into the f32 partial tiles
+      // warp tasks (tile, 16-feature slice), up to kMaxRounds per warp, held
+      // in registers until every warp is done with the projection's weights:
+      // tile i's f32 partials then overwrite tile i's weight unit
       const int n_tasks = nt * q.fw;
-      for (int task = warp; task < n_tasks; task += kWarps) {
+      float res[kMaxRounds][4][4];
+#pragma unroll
+      for (int rd = 0; rd < kMaxRounds; ++rd) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) res[rd][i][0] = res[rd][i][1] = res[rd][i][2] = res[rd][i][3] = 0.f;
+        const int task = rd * kWarps + warp;
+        if (task >= n_tasks) continue;
         const int ti = task / q.fw, f = task - ti * q.fw;
         if (!mbar_wait_bounded(&wbar[bidx[p] + ti], 0, kWaitLimit)) {
           ok = false;
           continue;
         }
-        float c4[4][4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) c4[i][0] = c4[i][1] = c4[i][2] = c4[i][3] = 0.f;
         const uint8_t* wu = smem + woff[p] + (uint32_t)ti * q.ubytes;
 #pragma unroll 1
         for (int kb = 0; kb < q.nkb; ++kb) {
@@ -261,21 +264,28 @@ __global__ void __launch_bounds__(kThreads, 1) k_layer_tail(ChainArgs a) {
             if (n8 < n_nt) {
               uint32_t xw[8];
               gemv_xfrag<T, true>(xs + (size_t)(n8 * 8 + g) * xstride + kb * 64, t, xw);
-              gemv_kblock<T, true>(c4[n8], af, xw, w);
+              gemv_kblock<T, true>(res[rd][n8], af, xw, w);
             }
           }
         }
+      }
+      __syncthreads();  // the projection's weight units are dead from here on
+#pragma unroll
+      for (int rd = 0; rd < kMaxRounds; ++rd) {
+        const int task = rd * kWarps + warp;
+        if (task >= n_tasks) continue;
+        const int ti = task / q.fw, f = task - ti * q.fw;
         // D fragment: features f*16 + g (+8), rows n8*8 + 2t (+1)
-        float* pt = part + (size_t)ti * kTailRows * PS;
+        float* pt = reinterpret_cast<float*>(smem + woff[p] + (uint32_t)ti * q.ubytes);
         const int fl = f * 16 + g;
 #pragma unroll
         for (int n8 = 0; n8 < 4; ++n8) {
           if (n8 < n_nt) {
             const int lr = n8 * 8 + 2 * t;
-            pt[lr * PS + fl] = c4[n8][0];
-            pt[(lr + 1) * PS + fl] = c4[n8][1];
-            pt[lr * PS + fl + 8] = c4[n8][2];
-            pt[(lr + 1) * PS + fl + 8] = c4[n8][3];
+            pt[lr * PS + fl] = res[rd][n8][0];
+            pt[(lr + 1) * PS + fl] = res[rd][n8][1];
+            pt[lr * PS + fl + 8] = res[rd][n8][2];
+            pt[(lr + 1) * PS + fl + 8] = res[rd][n8][3];
           }
         }
       }
@@ -294,7 +304,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_layer_tail(ChainArgs a) {
       T* xr = reinterpret_cast<T*>(a.x) + (size_t)r * a.H + tile * 64 + lane * 2;
       float2 xo = make_float2(0.f, 0.f);
       if (p == 0 || p == 2) xo = ldcg_act2(xr);  // in flight with the peer reads
-      const float* mine = part + (size_t)ti * kTailRows * PS + (size_t)r * PS + lane * FPL;
+      const float* mine =
+          reinterpret_cast<const float*>(smem + woff[p] + (uint32_t)ti * q.ubytes) + (size_t)r * PS + lane * FPL;
 #pragma unroll
       for (int s = 0; s < kCS; ++s) {
         const float* peer = cluster.map_shared_rank(mine, s);
@@ -377,11 +388,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_layer_tail(ChainArgs a) {
 }
 
 // Shared memory of a CTA for `n_clusters` clusters: the weight units of the
-// CTA holding the most, the widest activation slice, and the partial tiles
-// of the projection with the most (cluster 0 owns the most tiles). 0 if the
-// layer tail cannot serve the shapes.
+// CTA holding the most, then the widest activation slice. 0 if the layer
+// tail cannot serve the shapes (each partial tile must fit in its weight
+// unit, and each warp holds at most kMaxRounds tasks of a projection).
 size_t tail_smem(const ChainArgs& a, int n_clusters) {
-  size_t wmax = 0, slice = 0, parts = 0;
+  size_t wmax = 0, slice = 0;
   for (int c = 0; c < n_clusters; ++c) {
     size_t w = 0;
     int units = 0;
@@ -396,10 +407,11 @@ size_t tail_smem(const ChainArgs& a, int n_clusters) {
   for (int p = 0; p < a.n_phases; ++p) {
     const Geom q = geom_of(a.ph[p]);
     if (q.S != kCS || q.klen % 64 != 0 || (q.ft != 64 && q.ft != 128) || q.T * q.ft != a.ph[p].N) return 0;
+    if ((size_t)kTailRows * (q.ft + 4) * 4 > q.ubytes) return 0;
+    if (tiles_of(q.T, 0, n_clusters) * q.fw > kMaxRounds * kWarps) return 0;
     slice = std::max(slice, (size_t)slice_bytes(q));
-    parts = std::max(parts, (size_t)tiles_of(q.T, 0, n_clusters) * kTailRows * (q.ft + 4) * 4);
   }
-  return ((wmax + 127) & ~(size_t)127) + slice + parts;
+  return ((wmax + 127) & ~(size_t)127) + slice;
 }
 
 template <typename T>
