@@ -942,10 +942,14 @@ bool launch_gemv(ActType at, int epi, bool norm, const LinW& W, const void* x, i
 }
 
 int launch_lm_head(ActType at, const LinW& W, const void* x, int ldx, const int* row_map, const int* n_rows_ptr,
-                   int max_rows, const GemvEpi& ep, int* status, cudaStream_t s, bool tc) {
+                   int max_rows, const GemvEpi& ep, int* status, cudaStream_t s, bool tc, bool* used_tc) {
+  if (used_tc) *used_tc = false;
   if (W.pk == nullptr || W.N % (kHeadWarps * 16) != 0 || W.K % 64 != 0) return 0;
   int parts = tc ? launch_lm_head_tc(at, W, x, ldx, row_map, n_rows_ptr, max_rows, ep, status, s) : 0;
-  if (parts > 0) return parts;
+  if (parts > 0) {
+    if (used_tc) *used_tc = true;
+    return parts;
+  }
   // row tiles of 32 rows (4 MMA n-tiles) up to a batch of 32, else 64
 #define FMD_HEAD(T, Q8)                                                                                        \
   (max_rows <= 32 ? launch_lm_head_t<T, Q8, 4, 2>(W, x, ldx, row_map, n_rows_ptr, max_rows, ep, status, s)    \

@@ -288,7 +288,8 @@ bool launch_gemv(ActType at, int epi, bool norm, const LinW& W, const void* x, i
 // candidates per row it writes into ep.best_val / best_idx (0: nothing
 // launched).
 int launch_lm_head(ActType at, const LinW& W, const void* x, int ldx, const int* row_map, const int* n_rows_ptr,
-                   int max_rows, const GemvEpi& ep, int* status, cudaStream_t s, bool tc = true);
+                   int max_rows, const GemvEpi& ep, int* status, cudaStream_t s, bool tc = true,
+                   bool* used_tc = nullptr);
 // fmd_lm_head_tc.cu: the tensor-core lm_head (0 when it cannot serve the shapes).
 int launch_lm_head_tc(ActType at, const LinW& W, const void* x, int ldx, const int* row_map, const int* n_rows_ptr,
                       int max_rows, const GemvEpi& ep, int* status, cudaStream_t s);

@@ -38,6 +38,8 @@
 #include <cuda_runtime.h>
 #include <math.h>
 
+#include <cstdio>
+
 #include "fmd_gemv.cuh"
 #include "fmd_kernels.cuh"
 
@@ -57,10 +59,13 @@ constexpr int kLhLgStride = 132;                   // row stride (floats) of the
 constexpr uint32_t kLhWaitLimit = 1u << 24;
 constexpr int kScaleAhead = 8;                     // stages of block scales in flight per epilogue thread
 
+// The weight stream needs ~100 KB in flight per SM to run at the HBM rate
+// (bytes in flight = bandwidth x loaded latency), so most of the shared
+// memory goes to packed stages; two converted slots keep the MMAs fed.
 template <int NR>
 struct LhCfg {
-  static constexpr int RAW = NR == 32 ? 6 : 5;   // packed stages in flight
-  static constexpr int CONV = NR == 32 ? 4 : 2;  // converted A slots
+  static constexpr int RAW = NR == 32 ? 12 : 5;  // packed stages in flight
+  static constexpr int CONV = 2;                 // converted A slots
   static constexpr int ACC = kLhTmemCols / NR;   // block accumulators
 };
 
@@ -418,15 +423,21 @@ template <typename T, int NR>
 int launch_t(const LinW& W, const void* x, int ldx, const int* row_map, const int* n_rows_ptr, const GemvEpi& ep,
              int* status, int n_sm, cudaStream_t s) {
   const size_t smem = lh_smem<NR>(W.K);
-  if (smem > 226 * 1024) return 0;
-  static bool attr_set = false;
-  if (!attr_set) {
-    if (cudaFuncSetAttribute(k_lm_head_tc<T, NR>, cudaFuncAttributeMaxDynamicSharedMemorySize, 226 * 1024) !=
-        cudaSuccess) {
+  // the opt-in limit covers dynamic plus static shared memory
+  static size_t attr_set = 0;
+  if (attr_set < smem) {
+    const cudaError_t e = cudaFuncSetAttribute(k_lm_head_tc<T, NR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               (int)smem);
+    if (e != cudaSuccess) {
       cudaGetLastError();
+      static bool told = false;
+      if (!told)
+        std::fprintf(stderr, "[fmd] tensor-core lm_head unavailable (%zu bytes of shared memory: %s); "
+                             "the mma.sync kernel runs instead\n", smem, cudaGetErrorString(e));
+      told = true;
       return 0;
     }
-    attr_set = true;
+    attr_set = smem;
   }
   const int n_tiles = W.N / kLhFeat;
   const int grid = n_tiles < n_sm ? n_tiles : n_sm;

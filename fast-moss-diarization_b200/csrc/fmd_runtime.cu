@@ -138,6 +138,7 @@ struct fmd_handle {
   int n_sm = 0;
   bool proj_allowed = true;  // mixed steps on k_proj_tc (fused epilogues); FMD_PROJ_TC=0 selects k_gemm_tc
   bool lm_tc_allowed = true;  // Q8_0 lm_head on the tensor cores; FMD_LM_HEAD_TC=0 selects the mma.sync kernel
+  bool lm_tc_used = false;     // the last lm_head launch (or graph capture) used the tensor-core kernel
   bool pf_pp_allowed = true;  // persistent two-tile prefill attention; FMD_PREFILL_PP=0 selects one CTA per block
   bool chain_allowed = false;
   bool chain_ok = false;
@@ -576,7 +577,7 @@ void run_forward_decode(fmd_handle* h, float* logits_dev, const void* arena) {
   head.best_idx = h->best_idx;
   if (h->record_attn_events) cudaEventRecordWithFlags(h->attn_events[2], s, cudaEventRecordExternal);
   const int parts = launch_lm_head(h->at, h->lm_head, h->x, H, h->plan.sample_row, nsamp, h->max_slots, head,
-                                   h->d_status, s, h->lm_tc_allowed);
+                                   h->d_status, s, h->lm_tc_allowed, &h->lm_tc_used);
   if (h->record_attn_events) cudaEventRecordWithFlags(h->attn_events[3], s, cudaEventRecordExternal);
   if (parts == 0) h->launch_refused = true;
   trace(h, "lm_head", -1);
@@ -688,7 +689,7 @@ void run_forward(fmd_handle* h, float* logits_dev, const void* arena, bool decod
   head.best_idx = h->best_idx;
   if (h->record_attn_events) cudaEventRecordWithFlags(h->attn_events[2], s, cudaEventRecordExternal);
   const int parts = launch_lm_head(h->at, h->lm_head, h->xn, H, h->plan.sample_row, nsamp, h->max_slots, head,
-                                   h->d_status, s, h->lm_tc_allowed);
+                                   h->d_status, s, h->lm_tc_allowed, &h->lm_tc_used);
   if (h->record_attn_events) cudaEventRecordWithFlags(h->attn_events[3], s, cudaEventRecordExternal);
   trace(h, "lm_head", -1);
   if (parts > 0) {
@@ -1746,7 +1747,7 @@ int fmd_debug_wait_timeout(fmd_handle* h, int32_t limit) {
 int fmd_debug_paths(const fmd_handle* h, int32_t* flags) {
   if (!h || !flags) return FMD_EINVAL;
   *flags = (h->chain_ok ? FMD_PATH_LAYER_TAIL : 0) | (h->tc_ready && h->proj_allowed ? FMD_PATH_PROJ_TC : 0) |
-           (h->lm_tc_allowed && h->lm_head.q8 && h->max_slots <= 64 ? FMD_PATH_LM_HEAD_TC : 0) |
+           (h->lm_tc_used ? FMD_PATH_LM_HEAD_TC : 0) |
            (h->pf_pp_allowed ? FMD_PATH_PREFILL_PP : 0);
   return FMD_OK;
 }

@@ -278,8 +278,9 @@ int fmd_debug_wait_timeout(fmd_handle* h, int32_t limit);
 /* Which kernels serve this handle's steps after fmd_kv_reserve (no reference
  * counterpart): bit 0 = decode steps run the persistent layer tail
  * (FMD_LAYER_TAIL=1, Q8_0 weights, max_slots <= 32), bit 1 = mixed steps run
- * the persistent projection GEMM k_proj_tc, bit 2 = the lm_head runs on the
- * tensor cores (Q8_0 lm_head, max_slots <= 64; FMD_LM_HEAD_TC=0 turns it off),
+ * the persistent projection GEMM k_proj_tc, bit 2 = the last lm_head launch
+ * (or step-graph capture) ran on the tensor cores (Q8_0 lm_head, max_slots
+ * <= 64; FMD_LM_HEAD_TC=0 turns it off),
  * bit 3 = prefill attention on persistent CTAs with two query tiles each
  * (FMD_PREFILL_PP=0 selects one CTA per prefill block and kv head). */
 #define FMD_PATH_LAYER_TAIL 1

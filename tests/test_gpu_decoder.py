@@ -318,11 +318,11 @@ def test_lm_head_on_the_tensor_cores(prec, n, monkeypatch):
     for tc in ("1", "0"):
         monkeypatch.setenv("FMD_LM_HEAD_TC", tc)
         with make_decoder(cfg, w, prec, slots=n, tokens=n * 64, rows=1024) as dec:
-            assert dec.debug_paths()["lm_head_tc"] == (tc == "1")
             for s in range(n):
                 dec.open_slot(s, int(lens[s]) + 2)
             dec.prefill(list(range(n)), prompts, want_logits=False)
             got[tc] = dec.decode_step(list(range(n)), toks)
+            assert dec.debug_paths()["lm_head_tc"] == (tc == "1")  # the kernel that ran
     lg_tc, ids_tc = got["1"]
     lg_ref, _ = got["0"]
     worst = (0.0, None)
