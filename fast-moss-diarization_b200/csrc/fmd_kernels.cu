@@ -578,4 +578,22 @@ void launch_dequant(ActType at, const LinW& W, float* out, cudaStream_t s) {
   FMD_DISPATCH(at, k_dequant<T><<<1024, 256, 0, s>>>(W, out));
 }
 
+// The two halves of a split decode step: rows [0, split) and [split, n).
+__global__ void k_half_counts(const PlanCounts* __restrict__ full, PlanCounts* __restrict__ halves, int split) {
+  griddep_wait();
+  griddep_launch();  // only after the wait: see griddep_launch
+  if (threadIdx.x == 0) {
+    const int n = full->n_decode;
+    PlanCounts lo{}, hi{};
+    lo.n_rows = lo.n_decode = lo.n_sample = n < split ? n : split;
+    hi.n_rows = hi.n_decode = hi.n_sample = n > split ? n - split : 0;
+    halves[0] = lo;
+    halves[1] = hi;
+  }
+}
+
+void launch_half_counts(const PlanCounts* full, PlanCounts* halves, int split, cudaStream_t s) {
+  launch_pdl(k_half_counts, dim3(1), dim3(32), 0, s, full, halves, split);
+}
+
 }  // namespace fmd

@@ -261,6 +261,9 @@ void launch_dequant(ActType at, const LinW& W, float* out, cudaStream_t s);
 bool chain_plan(ActType at, const ChainArgs& a, int n_sm, int max_rows, int* n_clusters, size_t* smem, char* why,
                 size_t why_len);
 void launch_layer_tail(ActType at, const ChainArgs& a, int n_clusters, size_t smem, cudaStream_t s);
+// halves[0] / halves[1]: the row counts of rows [0, split) / [split, n) of
+// a decode-only pass (a step split over two streams).
+void launch_half_counts(const PlanCounts* full, PlanCounts* halves, int split, cudaStream_t s);
 // One bounded wait that runs out after `limit` tries and sets *status to
 // FMD_ETIMEDOUT (the failure path of every ring kernel's waits).
 void launch_wait_probe(uint32_t limit, int* status, cudaStream_t s);

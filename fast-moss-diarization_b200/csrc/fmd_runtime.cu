@@ -153,6 +153,15 @@ struct fmd_handle {
   std::vector<int> slot_cap, slot_len, slot_npages;
   void *x = nullptr, *xn = nullptr, *qbuf = nullptr, *ctx = nullptr, *hbuf = nullptr, *arena = nullptr;
   float *part = nullptr, *pacc = nullptr, *pml = nullptr, *logits = nullptr;
+  // decode-only steps split over two streams (FMD_DECODE_SPLIT=1): rows
+  // [0, max_slots / 2) on `stream`, the rest on `stream2`, so that one half's
+  // latency-bound projections overlap the other half's attention
+  bool split_allowed = false;
+  bool split_ok = false;
+  cudaStream_t stream2 = nullptr;
+  cudaEvent_t fork_ev = nullptr, join_ev = nullptr;
+  PlanCounts* half_counts = nullptr;  // [2]
+  float *pacc2 = nullptr, *pml2 = nullptr;
   float* ssq = nullptr;       // [max_slots][hidden / 64] per-tile sums of squares of the residual stream
   float* best_val = nullptr;  // [max_slots][vocab / 64] greedy candidates of the decode path
   int* best_idx = nullptr;
@@ -509,36 +518,81 @@ ChainArgs make_chain(fmd_handle* h, int l) {
 // -> O (+ residual) -> gate/up (post-attention norm folded in, SwiGLU fused)
 // -> down (+ residual); the split-K of each projection is reduced inside a
 // thread-block cluster.
-void run_forward_decode(fmd_handle* h, float* logits_dev, const void* arena) {
-  cudaStream_t s = h->stream;
+// Rows [r0, r0 + max_rows) of a decode-only pass: the plan's counts for
+// them (plan.counts) and every per-row array and buffer from row r0.
+struct DecodeView {
+  Plan plan;
+  int max_rows;
+  void *x, *qbuf, *ctx, *hbuf;
+  float *ssq, *pacc, *pml;
+  int* counters;
+  int grid;  // decode attention CTAs
+};
+
+// half = -1: every row; 0 / 1: the rows of that half of a split step.
+DecodeView decode_view(fmd_handle* h, int half) {
   const fmd_config& c = h->cfg;
-  const int R = h->max_slots, H = c.hidden_size, I = c.intermediate_size;
-  const int row_grid = std::min(R, 296);
-  const int* nrows = &h->plan.counts->n_rows;
-  const int* nsamp = &h->plan.counts->n_sample;
+  const int R = h->max_slots, H = c.hidden_size, I = c.intermediate_size, HqD = h->Hq() * kHeadDim;
+  DecodeView v;
+  v.plan = h->plan;
+  v.max_rows = R;
+  v.x = h->x;
+  v.qbuf = h->qbuf;
+  v.ctx = h->ctx;
+  v.hbuf = h->hbuf;
+  v.ssq = h->ssq;
+  v.pacc = h->pacc;
+  v.pml = h->pml;
+  v.counters = h->attn_counters;
+  v.grid = h->di_grid;
+  if (half < 0) return v;
+  const int S = R / 2, r0 = half * S;
+  v.plan.counts = h->half_counts + half;
+  v.plan.row_slot += r0;
+  v.plan.row_pos += r0;
+  v.plan.row_tok += r0;
+  v.plan.row_emb += r0;
+  v.max_rows = half ? R - S : S;
+  v.x = (uint16_t*)h->x + (size_t)r0 * H;
+  v.qbuf = (uint16_t*)h->qbuf + (size_t)r0 * HqD;
+  v.ctx = (uint16_t*)h->ctx + (size_t)r0 * HqD;
+  v.hbuf = (uint16_t*)h->hbuf + (size_t)r0 * I;
+  v.ssq = h->ssq + (size_t)r0 * (H / 64);
+  if (half) {
+    v.pacc = h->pacc2;
+    v.pml = h->pml2;
+  }
+  v.counters = h->attn_counters + (size_t)r0 * h->Hkv();
+  v.grid = h->n_sm;  // one attention CTA per SM leaves room for the other half's projections
+  return v;
+}
+
+// The layer loop of a decode-only pass over the rows of `v` on stream `s`.
+void decode_layers(fmd_handle* h, const DecodeView& v, cudaStream_t s, bool probe_attn) {
+  const fmd_config& c = h->cfg;
+  const int H = c.hidden_size, I = c.intermediate_size;
+  const int R = v.max_rows;
+  const int* nrows = &v.plan.counts->n_rows;
   const float eps = c.rms_norm_eps;
   const int ssq_tiles = H / 64;
   const int L = c.num_hidden_layers;
-  launch_embed_norm(h->at, h->plan, row_grid, h->embed, arena, h->x, h->layers[0].in_norm, h->xn, H, eps, h->ssq,
-                    ssq_tiles, s, h->chain_ok ? h->chain_sync : nullptr, h->chain_ok ? L * kChainSyncInts : 0);
-  trace(h, "embed_norm", -1);
   GemvEpi qkv;
-  qkv.ssq = h->ssq;
+  qkv.ssq = v.ssq;
   qkv.ssq_tiles = ssq_tiles;
   qkv.eps = eps;
-  qkv.plan = h->plan;
+  qkv.plan = v.plan;
   qkv.cos = h->rope_cos;
   qkv.sin = h->rope_sin;
-  qkv.q_out = h->qbuf;
+  qkv.q_out = v.qbuf;
   qkv.kv = h->kv;
   qkv.Hq = h->Hq();
   qkv.Hkv = h->Hkv();
   GemvEpi res;
-  res.x = h->x;
-  res.ssq_out = h->ssq;
+  res.x = v.x;
+  res.ssq_out = v.ssq;
   res.ssq_tiles = ssq_tiles;
   GemvEpi glu = qkv;
-  glu.h = h->hbuf;
+  glu.h = v.hbuf;
   glu.I = I;
   for (int l = 0; l < L; ++l) {
     const LayerDev& Ly = h->layers[l];
@@ -547,13 +601,13 @@ void run_forward_decode(fmd_handle* h, float* logits_dev, const void* arena) {
       qkv.qn_w = Ly.q_norm;
       qkv.kn_w = Ly.k_norm;
       qkv.layer = l;
-      if (!launch_gemv(h->at, kGemvQkv, true, Ly.qkv, h->x, H, nullptr, nrows, R, qkv, h->d_status, s)) h->launch_refused = true;
+      if (!launch_gemv(h->at, kGemvQkv, true, Ly.qkv, v.x, H, nullptr, nrows, R, qkv, h->d_status, s)) h->launch_refused = true;
       trace(h, "qkv", l);
     }
-    const bool probe = h->record_attn_events && l == h->attn_probe_layer();
+    const bool probe = probe_attn && h->record_attn_events && l == h->attn_probe_layer();
     if (probe) cudaEventRecordWithFlags(h->attn_events[0], s, cudaEventRecordExternal);
-    launch_attn_decode_tma(h->at, &h->kv_tmap, h->plan, h->di_grid, h->Hq(), h->Hkv(), h->qbuf, h->kv, l,
-                           h->attn_scale, h->pacc, h->pml, h->attn_counters, h->ctx, h->d_status, s);
+    launch_attn_decode_tma(h->at, &h->kv_tmap, v.plan, v.grid, h->Hq(), h->Hkv(), v.qbuf, h->kv, l,
+                           h->attn_scale, v.pacc, v.pml, v.counters, v.ctx, h->d_status, s);
     if (probe) cudaEventRecordWithFlags(h->attn_events[1], s, cudaEventRecordExternal);
     trace(h, "attn_decode", l);
     if (h->chain_ok) {
@@ -562,15 +616,50 @@ void run_forward_decode(fmd_handle* h, float* logits_dev, const void* arena) {
       trace(h, "layer_tail", l);
       continue;
     }
-    if (!launch_gemv(h->at, kGemvResid, false, Ly.o, h->ctx, h->Hq() * kHeadDim, nullptr, nrows, R, res, h->d_status, s)) h->launch_refused = true;
+    if (!launch_gemv(h->at, kGemvResid, false, Ly.o, v.ctx, h->Hq() * kHeadDim, nullptr, nrows, R, res, h->d_status, s)) h->launch_refused = true;
     trace(h, "o_proj", l);
     glu.norm_w = Ly.post_norm;
-    if (!launch_gemv(h->at, kGemvSwiglu, true, Ly.gate_up, h->x, H, nullptr, nrows, R, glu, h->d_status, s)) h->launch_refused = true;
+    if (!launch_gemv(h->at, kGemvSwiglu, true, Ly.gate_up, v.x, H, nullptr, nrows, R, glu, h->d_status, s)) h->launch_refused = true;
     trace(h, "gate_up", l);
-    if (!launch_gemv(h->at, kGemvResid, false, Ly.down, h->hbuf, I, nullptr, nrows, R, res, h->d_status, s)) h->launch_refused = true;
+    if (!launch_gemv(h->at, kGemvResid, false, Ly.down, v.hbuf, I, nullptr, nrows, R, res, h->d_status, s)) h->launch_refused = true;
     trace(h, "down", l);
   }
-  GemvEpi head = qkv;
+}
+
+// Decode-only forward pass (every row is a one-token decode row): per layer
+// QKV (input norm folded in, q/k norm + RoPE + KV write fused) -> attention
+// -> O (+ residual) -> gate/up (post-attention norm folded in, SwiGLU fused)
+// -> down (+ residual); the split-K of each projection is reduced inside a
+// thread-block cluster. A split step runs the layer loop of each half of the
+// rows on its own stream (rows are independent in every kernel of the loop,
+// so the results are those of one pass over all rows).
+void run_forward_decode(fmd_handle* h, float* logits_dev, const void* arena) {
+  cudaStream_t s = h->stream;
+  const fmd_config& c = h->cfg;
+  const int R = h->max_slots, H = c.hidden_size;
+  const int row_grid = std::min(R, 296);
+  const int* nsamp = &h->plan.counts->n_sample;
+  const float eps = c.rms_norm_eps;
+  const int ssq_tiles = H / 64;
+  const int L = c.num_hidden_layers;
+  launch_embed_norm(h->at, h->plan, row_grid, h->embed, arena, h->x, h->layers[0].in_norm, h->xn, H, eps, h->ssq,
+                    ssq_tiles, s, h->chain_ok ? h->chain_sync : nullptr, h->chain_ok ? L * kChainSyncInts : 0);
+  trace(h, "embed_norm", -1);
+  if (h->split_ok) {
+    launch_half_counts(h->plan.counts, h->half_counts, R / 2, s);
+    cudaEventRecord(h->fork_ev, s);
+    cudaStreamWaitEvent(h->stream2, h->fork_ev, 0);
+    decode_layers(h, decode_view(h, 0), s, true);
+    decode_layers(h, decode_view(h, 1), h->stream2, false);
+    cudaEventRecord(h->join_ev, h->stream2);
+    cudaStreamWaitEvent(s, h->join_ev, 0);
+  } else {
+    decode_layers(h, decode_view(h, -1), s, true);
+  }
+  GemvEpi head;
+  head.ssq = h->ssq;
+  head.ssq_tiles = ssq_tiles;
+  head.eps = eps;
   head.norm_w = h->final_norm;
   head.logits = logits_dev;
   head.best_val = h->best_val;
@@ -915,6 +1004,8 @@ int fmd_create(const fmd_config* cfg, int32_t precision, int32_t device, fmd_han
     h->lm_tc_allowed = !(lt != nullptr && lt[0] == '0');
     const char* pp = std::getenv("FMD_PREFILL_PP");
     h->pf_pp_allowed = !(pp != nullptr && pp[0] == '0');
+    const char* sp = std::getenv("FMD_DECODE_SPLIT");
+    h->split_allowed = sp != nullptr && sp[0] == '1';
   }
   if (cudaDeviceGetAttribute(&h->n_sm, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || h->n_sm < 1) {
     cudaGetLastError();
@@ -945,6 +1036,9 @@ int fmd_destroy(fmd_handle* h) {
     if (b->p) cudaFree(b->p);
   if (h->h_plan) cudaFreeHost(h->h_plan);
   if (h->h_ctr) cudaFreeHost(h->h_ctr);
+  if (h->fork_ev) cudaEventDestroy(h->fork_ev);
+  if (h->join_ev) cudaEventDestroy(h->join_ev);
+  if (h->stream2) cudaStreamDestroy(h->stream2);
   if (h->stream) cudaStreamDestroy(h->stream);
   delete h;
   return FMD_OK;
@@ -1121,6 +1215,19 @@ int fmd_kv_reserve(fmd_handle* h, int32_t max_slots, int64_t max_tokens_total, i
   if ((rc = A(attn_decode_partial_floats(h->di_grid) * 4, &p))) return rc;
   h->pacc = (float*)p;
   h->pml = h->pacc + (size_t)2 * h->di_grid * 2 * kHeadDim;
+  // a split decode step: the second half's attention partials, both halves' row counts
+  h->split_ok = h->split_allowed && !h->chain_ok && max_slots >= 16 && max_slots % 2 == 0;
+  if (h->split_ok) {
+    if ((rc = A(attn_decode_partial_floats(h->di_grid) * 4, &p))) return rc;
+    h->pacc2 = (float*)p;
+    h->pml2 = h->pacc2 + (size_t)2 * h->di_grid * 2 * kHeadDim;
+    if ((rc = A(2 * sizeof(PlanCounts), &p))) return rc;
+    CK(cudaMemset(p, 0, 2 * sizeof(PlanCounts)));
+    h->half_counts = (PlanCounts*)p;
+    if (!h->stream2) CK(cudaStreamCreateWithFlags(&h->stream2, cudaStreamNonBlocking));
+    if (!h->fork_ev) CK(cudaEventCreateWithFlags(&h->fork_ev, cudaEventDisableTiming));
+    if (!h->join_ev) CK(cudaEventCreateWithFlags(&h->join_ev, cudaEventDisableTiming));
+  }
   if ((rc = A((size_t)max_slots * V * 4, &p))) return rc;
   h->logits = (float*)p;
   if ((rc = A((size_t)max_slots * 4, &p))) return rc;
@@ -1455,6 +1562,7 @@ EngineDev make_engine_dev(fmd_handle* h, int max_batch, int chunk, int allow_pre
   e.max_batch = max_batch;
   e.prefill_chunk = chunk;
   e.max_rows = h->max_rows;
+  e.split_rows = h->split_ok ? h->max_slots / 2 : 0;
   e.max_pages_per_slot = h->max_pages_per_slot;
   e.eos = h->cfg.eos_token_id;
   e.vocab = h->cfg.vocab_size;
@@ -1615,6 +1723,7 @@ int fmd_engine_step(fmd_handle* h, int64_t max_steps, fmd_stats* stats) {
   e.consume_only = 1;
   CK(cudaEventRecord(h->win_end, h->stream));
   const long long kv_last = h->h_ctr->last_kv_tokens, rows_last = h->h_ctr->last_decode_rows;
+  const long long kv_lo_last = h->h_ctr->last_kv_tokens_lo, rows_lo_last = h->h_ctr->last_rows_lo;
   launch_schedule(e, h->stream);
   CK(cudaMemcpyAsync(h->h_ctr, h->eng_ctr, sizeof(EngineCounters), cudaMemcpyDeviceToHost, h->stream));
   if ((rc = sync_check(h))) return rc;
@@ -1644,8 +1753,9 @@ int fmd_engine_step(fmd_handle* h, int64_t max_steps, fmd_stats* stats) {
     stats->window_device_ms = win_ms;
     stats->attn_decode_ms = attn_ms;
     stats->lm_head_ms = lm_ms;
-    stats->attn_kv_tokens = kv_last;
-    stats->attn_rows = rows_last;
+    // a split step's probe times the first half's attention
+    stats->attn_kv_tokens = h->split_ok ? kv_lo_last : kv_last;
+    stats->attn_rows = h->split_ok ? rows_lo_last : rows_last;
     stats->window_mixed_steps = mixed_launched;
     stats->graph_kernels_mixed = h->graph_kernels_mixed;
     stats->graph_kernels_decode = h->graph_kernels_decode;
@@ -1748,7 +1858,7 @@ int fmd_debug_paths(const fmd_handle* h, int32_t* flags) {
   if (!h || !flags) return FMD_EINVAL;
   *flags = (h->chain_ok ? FMD_PATH_LAYER_TAIL : 0) | (h->tc_ready && h->proj_allowed ? FMD_PATH_PROJ_TC : 0) |
            (h->lm_tc_used ? FMD_PATH_LM_HEAD_TC : 0) |
-           (h->pf_pp_allowed ? FMD_PATH_PREFILL_PP : 0);
+           (h->pf_pp_allowed ? FMD_PATH_PREFILL_PP : 0) | (h->split_ok ? FMD_PATH_DECODE_SPLIT : 0);
   return FMD_OK;
 }
 

@@ -143,11 +143,12 @@ __global__ void __launch_bounds__(256) k_schedule(EngineDev e) {
 
     // ---- 3. lay out the next plan (segment descriptors) ----
     int rows = 0, items = 0, samples = 0, pblocks = 0;
-    long long kv_tokens = 0;
+    long long kv_tokens = 0, kv_lo = 0;
     for (int s = 0; s < nb; ++s) {
       s_seg_n[s] = 0;
       if (st_state[s] == kSlotDecode && rows < e.max_rows) {
         kv_tokens += st_len[s] + 1;
+        if (rows < e.split_rows) kv_lo += st_len[s] + 1;
         s_seg_row0[s] = rows;
         s_seg_n[s] = 1;
         s_seg_pos0[s] = st_len[s];
@@ -162,6 +163,8 @@ __global__ void __launch_bounds__(256) k_schedule(EngineDev e) {
     const int n_decode = rows;
     c->last_kv_tokens = kv_tokens;
     c->last_decode_rows = n_decode;
+    c->last_kv_tokens_lo = kv_lo;
+    c->last_rows_lo = n_decode < e.split_rows ? n_decode : e.split_rows;
     int budget_rows = e.allow_prefill ? e.prefill_chunk : 0;
     long long pending = 0;
     for (int s = 0; s < nb; ++s) {

@@ -31,6 +31,8 @@ struct EngineCounters {
   long long prefill_tokens;
   long long last_kv_tokens;    // sum of (pos + 1) over the decode rows of the latest plan
   long long last_decode_rows;
+  long long last_kv_tokens_lo; // the same over decode rows below EngineDev::split_rows
+  long long last_rows_lo;
   long long pending_prefill;   // prompt rows admitted but not yet planned
 };
 
@@ -42,6 +44,7 @@ struct EngineDev {
   int max_batch;       // slots in use (<= reserved slots)
   int prefill_chunk;   // prompt rows admitted per step
   int max_rows;        // plan capacity R
+  int split_rows;      // decode rows below this index run as the first half of a split step (0: no split)
   int max_pages_per_slot;
   int eos;
   int vocab;           // token ids outside [0, vocab) end their request with an error

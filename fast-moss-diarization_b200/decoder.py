@@ -243,11 +243,12 @@ class Qwen3Decoder:
         {"layer_tail": decode steps on the persistent layer tail,
         "proj_tc": mixed steps on the persistent projection GEMM,
         "lm_head_tc": the lm_head on the tensor cores,
-        "prefill_pp": prefill attention on persistent two-tile CTAs}."""
+        "prefill_pp": prefill attention on persistent two-tile CTAs,
+        "decode_split": decode-only steps run each half of their rows on its own stream}."""
         f = C.c_int32(0)
         self._check(self.lib.fmd_debug_paths(self._h, C.byref(f)))
         return {"layer_tail": bool(f.value & 1), "proj_tc": bool(f.value & 2), "lm_head_tc": bool(f.value & 4),
-                "prefill_pp": bool(f.value & 8)}
+                "prefill_pp": bool(f.value & 8), "decode_split": bool(f.value & 16)}
 
     def debug_kv(self, slot: int, layer: int, pos: int, n: int):
         shape = (n, self.cfg.num_key_value_heads, self.cfg.head_dim)

@@ -282,11 +282,14 @@ int fmd_debug_wait_timeout(fmd_handle* h, int32_t limit);
  * (or step-graph capture) ran on the tensor cores (Q8_0 lm_head, max_slots
  * <= 64; FMD_LM_HEAD_TC=0 turns it off),
  * bit 3 = prefill attention on persistent CTAs with two query tiles each
- * (FMD_PREFILL_PP=0 selects one CTA per prefill block and kv head). */
+ * (FMD_PREFILL_PP=0 selects one CTA per prefill block and kv head), bit 4 =
+ * decode-only steps run each half of their rows on its own stream
+ * (FMD_DECODE_SPLIT=1, even max_slots >= 16, layer tail off). */
 #define FMD_PATH_LAYER_TAIL 1
 #define FMD_PATH_PROJ_TC 2
 #define FMD_PATH_LM_HEAD_TC 4
 #define FMD_PATH_PREFILL_PP 8
+#define FMD_PATH_DECODE_SPLIT 16
 int fmd_debug_paths(const fmd_handle* h, int32_t* flags);
 
 /* ---- greedy pick without allocation -------------------------------------- */

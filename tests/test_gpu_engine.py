@@ -111,3 +111,41 @@ def test_engine_many_requests_page_recycling():
         assert out[i].finish_reason == "length"
         assert len(out[i].tokens) == max_new[i]
         assert all(0 <= t < cfg.vocab_size for t in out[i].tokens)
+
+
+@pytest.mark.parametrize("prec", ["int8_bf16", "bf16"])
+def test_split_decode_steps_are_bit_identical(prec, monkeypatch):
+    """Decode-only steps split over two streams (FMD_DECODE_SPLIT=1: rows
+    [0, 8) and [8, 16) of a 16-slot batch each run the layer loop on their
+    own stream, the lm_head over all rows after the join) give the same
+    tokens and logits as one pass over all rows: every kernel of the loop
+    treats rows independently. Requests outnumber slots, so the halves see
+    refills, uneven row counts and an empty second half at the queue's end."""
+    cfg = tiny_config()
+    w = syn.make_weights(cfg, seed=13, norm_jitter=0.2)
+    rng = np.random.default_rng(21)
+    n = 24
+    lens = [int(x) for x in rng.integers(1, 200, n)]
+    max_new = [int(x) for x in rng.integers(1, 40, n)]
+    forced = [-1] * n
+    prompts = [rng.standard_normal((k, cfg.hidden_size), dtype=np.float32) for k in lens]
+    arena = np.concatenate(prompts)
+    step_ids = [int(t) for t in rng.integers(0, 50, 13)]
+    got = {}
+    for split in ("1", "0"):
+        monkeypatch.setenv("FMD_DECODE_SPLIT", split)
+        with PKG.Qwen3Decoder(cfg, prec) as dec:
+            dec.load_weights(w)
+            dec.reserve(max_slots=16, max_tokens=16 * 256, max_rows=16 + 128)
+            assert dec.debug_paths()["decode_split"] == (split == "1")
+            eng = PKG.Engine(dec)
+            out, _ = eng.generate(lens, max_new, forced, arena, max_batch=16, prefill_chunk=128)
+            got[split] = [list(o.tokens) for o in out]
+            # the operator path too: one decode step over 13 rows (halves of 8 and 5)
+            for s in range(13):
+                dec.open_slot(s, lens[s] + 2)
+            dec.prefill(list(range(13)), prompts[:13], want_logits=False)
+            got[split + "op"] = dec.decode_step(list(range(13)), step_ids)
+    assert got["1"] == got["0"]
+    assert sum(len(t) for t in got["1"]) > n
+    assert np.array_equal(got["1op"][0], got["0op"][0]) and np.array_equal(got["1op"][1], got["0op"][1])
