@@ -651,7 +651,7 @@ def main():
                          "traffic": (tpk * kv_per_launch) if tpk else None, "peak_kind": peak_kind,
                          "alg_bytes_per_launch": alg_bytes, "ms_per_launch": ms_per_launch},
             "lm_head": {"kernel": "k_lm_head_tc (tcgen05, Q8_0)" if wl.precision.startswith("int8") and
-                        os.environ.get("FMD_LM_HEAD_TC", "1") != "0" and args.batch <= 64 else "k_lm_head (mma.sync)",
+                        os.environ.get("FMD_LM_HEAD_TC") == "1" and args.batch <= 64 else "k_lm_head (mma.sync)",
                         "ms_per_launch": lm_ms, "alg_bytes_per_launch": lm_bytes, "achieved_gbs": lm_gbs,
                         "frac": lm_gbs / peak if peak else None},
             "step_roofline": {"bytes_per_step": step_bytes, "ms_per_step": step_ms,

@@ -137,7 +137,7 @@ struct fmd_handle {
   // environment at fmd_create.
   int n_sm = 0;
   bool proj_allowed = true;  // mixed steps on k_proj_tc (fused epilogues); FMD_PROJ_TC=0 selects k_gemm_tc
-  bool lm_tc_allowed = true;  // Q8_0 lm_head on the tensor cores; FMD_LM_HEAD_TC=0 selects the mma.sync kernel
+  bool lm_tc_allowed = false;  // Q8_0 lm_head on the tensor cores (FMD_LM_HEAD_TC=1); else the mma.sync kernel
   bool lm_tc_used = false;     // the last lm_head launch (or graph capture) used the tensor-core kernel
   bool pf_pp_allowed = true;  // persistent two-tile prefill attention; FMD_PREFILL_PP=0 selects one CTA per block
   bool chain_allowed = false;
@@ -1001,7 +1001,7 @@ int fmd_create(const fmd_config* cfg, int32_t precision, int32_t device, fmd_han
     const char* p = std::getenv("FMD_PROJ_TC");
     h->proj_allowed = !(p != nullptr && p[0] == '0');
     const char* lt = std::getenv("FMD_LM_HEAD_TC");
-    h->lm_tc_allowed = !(lt != nullptr && lt[0] == '0');
+    h->lm_tc_allowed = lt != nullptr && lt[0] == '1';
     const char* pp = std::getenv("FMD_PREFILL_PP");
     h->pf_pp_allowed = !(pp != nullptr && pp[0] == '0');
     const char* sp = std::getenv("FMD_DECODE_SPLIT");

@@ -280,7 +280,7 @@ int fmd_debug_wait_timeout(fmd_handle* h, int32_t limit);
  * (FMD_LAYER_TAIL=1, Q8_0 weights, max_slots <= 32), bit 1 = mixed steps run
  * the persistent projection GEMM k_proj_tc, bit 2 = the last lm_head launch
  * (or step-graph capture) ran on the tensor cores (Q8_0 lm_head, max_slots
- * <= 64; FMD_LM_HEAD_TC=0 turns it off),
+ * <= 64; opt-in with FMD_LM_HEAD_TC=1),
  * bit 3 = prefill attention on persistent CTAs with two query tiles each
  * (FMD_PREFILL_PP=0 selects one CTA per prefill block and kv head), bit 4 =
  * decode-only steps run each half of their rows on its own stream
