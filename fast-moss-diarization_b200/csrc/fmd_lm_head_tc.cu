@@ -3,11 +3,16 @@
 // sampled rows.
 //
 // The reference dequantises each Q8_0 block (q * d, linear.rs:179-265) and
-// multiplies in f32. Here the int8 values themselves go through the MMA
-// (exact in f16 and bf16), every 32-wide block into its own f32 accumulator
-// in tensor memory, and the block's f16 scale is applied in f32 on the way
-// out: y = sum_b d_b * (sum_{k in b} q_k x_k), the reference's sum up to the
-// f32 summation order, as the mma.sync kernel (k_lm_head) computes it.
+// multiplies in f32. Here the int8 values themselves go through the MMA as
+// f16 (exact), every 32-wide block into its own f32 accumulator in tensor
+// memory, and the block's f16 scale is applied in f32 on the way out:
+// y = sum_b d_b * (sum_{k in b} q_k x_k), the reference's sum up to the f32
+// summation order, as the mma.sync kernel (k_lm_head) computes it. The
+// operands are f16 for both activation types (int8 -> f16 takes half the
+// instructions of int8 -> bf16): bf16 rows are scaled by a power of two that
+// puts their largest value in [2^14, 2^15), which leaves every value within
+// 2^28 of the row's largest exact in f16 (smaller ones weigh less than the
+// f32 rounding of the sum), and the logits are scaled back exactly.
 //
 // One CTA per SM walks 128-feature tiles (tile blockIdx.x + i * gridDim.x);
 // a tile's k-blocks of 64 are stages:
@@ -90,6 +95,8 @@ __global__ void __launch_bounds__(kLhThreads, 1)
       acc_empty[ACC], mma_done;
   __shared__ uint32_t tmem_base_s;
   __shared__ float rs_s[NR];
+  __shared__ uint32_t xmax_s[NR];  // largest |value| of each staged row (f32 bits)
+  __shared__ float inv_s[NR];      // 1 / the row's power-of-two operand scale
   __shared__ uint32_t sc_ring[kScaleAhead][kLhFeat];
   __shared__ int abort_s, stop_s;
 
@@ -165,7 +172,7 @@ __global__ void __launch_bounds__(kLhThreads, 1)
     tc_fence_after();
     const uint32_t tmem = tmem_base_s;
     if (lane == 0) {
-      constexpr uint32_t idesc = umma_idesc_f16(Act<T>::kIsBf16, kLhFeat, NR);
+      constexpr uint32_t idesc = umma_idesc_f16(false, kLhFeat, NR);  // f16 operands
       bool ok = true;
       for (int g = 0; ok && g < n_stages; ++g) {
         const int c = g % CONV, kb = g % nkb;
@@ -221,10 +228,10 @@ __global__ void __launch_bounds__(kLhThreads, 1)
         const int4 q = h ? qb : qa;
         const int r = u * 16 + gq + 8 * h;
         uint32_t o[8];
-        i8x4_to_act<T>((uint32_t)q.x, o[0], o[1]);
-        i8x4_to_act<T>((uint32_t)q.y, o[2], o[3]);
-        i8x4_to_act<T>((uint32_t)q.z, o[4], o[5]);
-        i8x4_to_act<T>((uint32_t)q.w, o[6], o[7]);
+        i8x4_to_act<__half>((uint32_t)q.x, o[0], o[1]);
+        i8x4_to_act<__half>((uint32_t)q.y, o[2], o[3]);
+        i8x4_to_act<__half>((uint32_t)q.z, o[4], o[5]);
+        i8x4_to_act<__half>((uint32_t)q.w, o[6], o[7]);
         const int4 c0 = make_int4(o[0], o[1], o[2], o[3]), c1 = make_int4(o[4], o[5], o[6], o[7]);
         uint8_t* rowp = tile + r * 128;
         const int j0 = t ^ (r & 7), j1 = (4 + t) ^ (r & 7);
@@ -249,6 +256,7 @@ __global__ void __launch_bounds__(kLhThreads, 1)
     griddep_launch();  // only after the wait: see griddep_launch
     const int rows = min(*n_rows_ptr, NR);
     const bool norm = ep.ssq != nullptr;  // else the rows are already normalised
+    for (int r = et; r < NR; r += NE) xmax_s[r] = 0u;
     if (norm) {
       for (int r = et; r < rows; r += NE) {
         const float* sp = ep.ssq + (size_t)(row_map ? row_map[r] : r) * ep.ssq_tiles;
@@ -262,8 +270,8 @@ __global__ void __launch_bounds__(kLhThreads, 1)
         }
         rs_s[r] = rsqrtf(ss / K + ep.eps);
       }
-      named_sync(1, NE);
     }
+    named_sync(1, NE);
     {
       // 16-byte chunk ch of row r: k-block ch / 8, chunk ch % 8 of the row,
       // stored swizzled (chunk j of row r at j ^ (r % 8))
@@ -294,10 +302,49 @@ __global__ void __launch_bounds__(kLhThreads, 1)
               uv[e] = Act<T>::pack2(f.x * rsr * gw.x, f.y * rsr * gw.y);
             }
           }
+          if constexpr (Act<T>::kIsBf16) {
+            const uint32_t* uv = reinterpret_cast<const uint32_t*>(&v[j]);
+            float m = 0.f;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 f = Act<T>::unpack2(uv[e]);
+              m = fmaxf(m, fmaxf(fabsf(f.x), fabsf(f.y)));
+            }
+            if (m > 0.f) atomicMax(&xmax_s[r], __float_as_uint(m));
+          }
           const int kb = ch >> 3, jj = ch & 7;
           *reinterpret_cast<int4*>(xs_p + (size_t)kb * NR * 128 + r * 128 + ((jj ^ (r & 7)) << 4)) = v[j];
         }
       }
+    }
+    named_sync(1, NE);
+    if constexpr (Act<T>::kIsBf16) {
+      // f16 operands: row r scaled by 2^(14 - e), e the exponent of its
+      // largest |value|; the rounded bf16 values scale and convert exactly
+      for (int r = et; r < NR; r += NE) {
+        const uint32_t mb = xmax_s[r];
+        const int e = (int)((mb >> 23) & 0xffu) - 127;
+        const int sh = mb == 0u || e > 127 ? 0 : max(-126, min(127, 14 - e));
+        inv_s[r] = __uint_as_float((uint32_t)(127 - sh) << 23);
+        rs_s[r] = __uint_as_float((uint32_t)(127 + sh) << 23);  // the staging's row scales are dead: reuse
+      }
+      named_sync(1, NE);
+      const int cpr = K >> 3;
+      for (int idx = et; idx < NR * cpr; idx += NE) {
+        const int r = idx / cpr, ch = idx - r * cpr, kb = ch >> 3, jj = ch & 7;
+        int4* pv = reinterpret_cast<int4*>(xs_p + (size_t)kb * NR * 128 + r * 128 + ((jj ^ (r & 7)) << 4));
+        int4 v = *pv;
+        uint32_t* uv = reinterpret_cast<uint32_t*>(&v);
+        const float sc = rs_s[r];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = Act<T>::unpack2(uv[e]);
+          uv[e] = Act<__half>::pack2(f.x * sc, f.y * sc);
+        }
+        *pv = v;
+      }
+    } else {
+      for (int r = et; r < NR; r += NE) inv_s[r] = 1.f;
     }
     asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // the rows, visible to tcgen05.mma
     named_sync(2, (1 + kLhEpiWarps) * 32);
@@ -371,7 +418,7 @@ __global__ void __launch_bounds__(kLhThreads, 1)
         named_sync(1, NE);  // the previous half's reads are done
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
-          const float v = rnd<T>(acc[h * 32 + j]);
+          const float v = rnd<T>(acc[h * 32 + j] * inv_s[h * 32 + j]);  // exact power-of-two unscale
           lg[j * kLhLgStride + fl] = v;
           if (ep.logits && h * 32 + j < rows) ep.logits[(size_t)(h * 32 + j) * W.N + f0 + fl] = v;
         }
