@@ -60,6 +60,39 @@ FMD_DEV uint64_t umma_desc_sw128_mn(uint32_t saddr, uint32_t mn_block_bytes) {
 
 FMD_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
 
+// Softmax arithmetic of one tile row (64 raw scores), shared by both prefill
+// kernels so that they compute the same values. Keys past the row's position
+// become -inf (only a tile that reaches it is checked); the maximum is taken
+// over the raw scores (the scale is positive, and rounding is monotonic, so
+// max(s) * scale = max(s * scale)) in 8 independent chains.
+FMD_DEV float pf_row_max(float (&s)[64], int key0, int qpos, float scale_log2) {
+  if (key0 + 63 > qpos) {
+#pragma unroll
+    for (int c = 0; c < 64; ++c) s[c] = key0 + c <= qpos ? s[c] : -INFINITY;
+  }
+  float m[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m[i] = s[i];
+#pragma unroll
+  for (int c = 8; c < 64; ++c) m[c & 7] = fmaxf(m[c & 7], s[c]);
+#pragma unroll
+  for (int i = 1; i < 8; ++i) m[0] = fmaxf(m[0], m[i]);
+  return m[0] * scale_log2;
+}
+// p = 2^(s * scale - m_ref) in place (one rounding of the argument); returns
+// the row sum of the tile, added in 8 independent chains.
+FMD_DEV float pf_row_exp(float (&s)[64], float scale_log2, float m_ref) {
+  float a[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) a[i] = 0.f;
+#pragma unroll
+  for (int c = 0; c < 64; ++c) {
+    s[c] = exp2f(fmaf(s[c], scale_log2, -m_ref));
+    a[c & 7] += s[c];
+  }
+  return ((a[0] + a[1]) + (a[2] + a[3])) + ((a[4] + a[5]) + (a[6] + a[7]));
+}
+
 template <typename T>
 __global__ void __launch_bounds__(192, 1)
     k_attn_prefill_tc(const __grid_constant__ CUtensorMap kvmap, const __grid_constant__ CUtensorMap qmap, Plan p,
@@ -255,13 +288,7 @@ __global__ void __launch_bounds__(192, 1)
       }
       tc_fence_before();
       mbar_arrive(&s_empty[sb]);
-      const int key0 = j * kPageTokens;
-      float mx = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        s[c] = key0 + c <= qpos ? s[c] * scale_log2 : -INFINITY;
-        mx = fmaxf(mx, s[c]);
-      }
+      const float mx = pf_row_max(s, j * kPageTokens, qpos, scale_log2);
       // a row moves its reference maximum when its new maximum exceeds it by
       // more than 2^8; its O (all PVs so far) and l then scale by
       // 2^(m_ref - mx). The rescale reads and writes O in tensor memory, a
@@ -294,13 +321,7 @@ __global__ void __launch_bounds__(192, 1)
           m_ref = mx;
         }
       }
-      float ps = 0.f;
-#pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        s[c] = exp2f(s[c] - m_ref);
-        ps += s[c];
-      }
-      l += ps;
+      l += pf_row_exp(s, scale_log2, m_ref);
       // P buffer j&1 was last read by PV_{j-2}
       if (j >= 2 && !wwait(&p_empty[sb], ((j - 2) >> 1) & 1)) {
         ok = false;
@@ -669,13 +690,7 @@ __global__ void __launch_bounds__(kPpThreads, 1)
         tc_fence_before();
         mbar_arrive(&s_empty[x][sb]);
         ++sn;
-        const int key0 = j * kPageTokens;
-        float mx = -INFINITY;
-#pragma unroll
-        for (int c2 = 0; c2 < 64; ++c2) {
-          s[c2] = key0 + c2 <= qpos ? s[c2] * scale_log2 : -INFINITY;
-          mx = fmaxf(mx, s[c2]);
-        }
+        const float mx = pf_row_max(s, j * kPageTokens, qpos, scale_log2);
         // lazy rescale (as k_attn_prefill_tc): the warp reads and writes O
         // when any of its rows moves its reference maximum; the previous PV
         // of this tile (the pn - 1-th) must have completed
@@ -706,13 +721,7 @@ __global__ void __launch_bounds__(kPpThreads, 1)
             m_ref = mx;
           }
         }
-        float ps = 0.f;
-#pragma unroll
-        for (int c2 = 0; c2 < 64; ++c2) {
-          s[c2] = exp2f(s[c2] - m_ref);
-          ps += s[c2];
-        }
-        l += ps;
+        l += pf_row_exp(s, scale_log2, m_ref);
         // the P buffer was last read by the previous PV of this tile role
         if (pn >= 1 && !wwait(&pv_done[x], (pn - 1) & 1)) {
           ok = false;
