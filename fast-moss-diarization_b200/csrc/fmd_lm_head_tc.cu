@@ -20,22 +20,26 @@
 //    of 16 features x 64 k, 8.5 KB, the k_lm_head layout) into a ring of RAW
 //    stages. Weights depend on no earlier kernel, so the ring fills before
 //    the dependency wait;
-//  * warps 2-9 (converters): warp w takes unit w of each stage, turns its
-//    int8 values into 16-bit operands and writes them as 16 rows of the
-//    stage's A tile (128 features x 64 k, K-major, 128-byte swizzle) in a
-//    ring of CONV slots, releasing the raw stage as soon as its fragments are
-//    in registers;
+//  * warps 2-5 (converters): warp w takes units w and w + 4 of each stage,
+//    turns their int8 values into f16 operands and writes them as 32 rows of
+//    the stage's A tile (128 features x 64 k, K-major, 128-byte swizzle) in
+//    a ring of CONV slots, releasing the raw stage as soon as its fragments
+//    are in registers;
 //  * warp 1 (one lane): tcgen05.mma M = 128 (features) x N = NR (rows) x
 //    K = 16, two per Q8_0 block, each block into the next of 256 / NR
 //    accumulators; tcgen05.commit releases the A slot and signals the block's
 //    accumulator;
-//  * warps 10-13 (epilogue): before the loop they stage the rows (final
-//    RMSNorm applied) as the B operand, resident for the whole launch. Per
-//    block, warp w reads tensor-memory lanes 32 (w % 4) .. (the thread's
-//    feature) x NR columns (the rows), frees the accumulator and adds
-//    d * value in f32. After a tile, the logits are rounded to the
-//    activation type (as the reference's lm_head output is) and reduced
-//    per row to the best (value, lowest index) through shared memory.
+//  * warps 6-13 (epilogue): before the loop they stage the rows (final
+//    RMSNorm applied) as the B operand, resident for the whole launch. Warp
+//    w reads tensor-memory lanes 32 (w % 4) .. (the thread's feature) x NR
+//    columns (the rows); warps 6-9 take the even stages of a tile, warps
+//    10-13 the odd ones, so two accumulator reads of a lane quarter are in
+//    flight at once. Per stage a warp loads both blocks' accumulators behind
+//    one wait, frees them and adds d0 x block 0, then d1 x block 1, in f32.
+//    After a tile, the even-stage sum plus the odd-stage sum is scaled back,
+//    rounded to the activation type (as the reference's lm_head output is)
+//    and reduced per row to the best (value, lowest index) through shared
+//    memory.
 // Each CTA writes one candidate per row; k_pick_reduce finishes the pick.
 // Every wait is bounded; a timeout sets the status word, each role stops,
 // and the CTA waits (bounded) for its copies and MMAs in flight before it
@@ -56,8 +60,8 @@ constexpr int kLhFeat = 128;                       // features of a tile = MMA M
 constexpr int kLhUnits = kLhFeat / 16;             // 16-feature units of a stage
 constexpr uint32_t kLhRaw = kLhUnits * kUnitQ8;    // packed stage: 8704 bytes
 constexpr uint32_t kLhConv = kLhFeat * 128;        // converted A tile: 128 rows x 64 k x 2 bytes
-constexpr int kLhConvWarps = kLhUnits;             // one unit per converter warp
-constexpr int kLhEpiWarps = 4;
+constexpr int kLhConvWarps = 4;                    // two units of each stage per converter warp
+constexpr int kLhEpiWarps = 8;                     // two per tensor-memory lane quarter: even / odd stages
 constexpr int kLhThreads = (2 + kLhConvWarps + kLhEpiWarps) * 32;  // 448
 constexpr int kLhTmemCols = 256;
 constexpr int kLhLgStride = 132;                   // row stride (floats) of the rounded-logit tile
@@ -69,7 +73,7 @@ constexpr int kScaleAhead = 8;                     // stages of block scales in 
 // memory goes to packed stages; two converted slots keep the MMAs fed.
 template <int NR>
 struct LhCfg {
-  static constexpr int RAW = NR == 32 ? 12 : 5;  // packed stages in flight
+  static constexpr int RAW = NR == 32 ? 12 : 4;  // packed stages in flight
   static constexpr int CONV = 2;                 // converted A slots
   static constexpr int ACC = kLhTmemCols / NR;   // block accumulators
 };
@@ -97,7 +101,7 @@ __global__ void __launch_bounds__(kLhThreads, 1)
   __shared__ float rs_s[NR];
   __shared__ uint32_t xmax_s[NR];  // largest |value| of each staged row (f32 bits)
   __shared__ float inv_s[NR];      // 1 / the row's power-of-two operand scale
-  __shared__ uint32_t sc_ring[kScaleAhead][kLhFeat];
+  __shared__ uint32_t sc_ring[2][kScaleAhead][kLhFeat];
   __shared__ int abort_s, stop_s;
 
   const int K = W.K, nkb = K / 64;
@@ -127,7 +131,7 @@ __global__ void __launch_bounds__(kLhThreads, 1)
     }
     for (int i = 0; i < ACC; ++i) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], kLhEpiWarps);
+      mbar_init(&acc_empty[i], kLhEpiWarps / 2);  // the four warps of the block's stage parity
     }
     mbar_init(&mma_done, 1);
     abort_s = 0;
@@ -201,8 +205,8 @@ __global__ void __launch_bounds__(kLhThreads, 1)
     }
     __syncwarp();
   } else if (warp < 2 + kLhConvWarps) {
-    // ---- converters: unit u of every stage -> rows 16u .. 16u + 15 of the A tile
-    const int u = warp - 2, gq = lane >> 2, t = lane & 3;
+    // ---- converters: units cw and cw + 4 of every stage -> rows 16u .. 16u + 15 of the A tile
+    const int cw = warp - 2, gq = lane >> 2, t = lane & 3;
     bool ok = true;
     for (int g = 0; ok && g < n_stages; ++g) {
       const int s = g % RAW, c = g % CONV;
@@ -214,9 +218,12 @@ __global__ void __launch_bounds__(kLhThreads, 1)
         ok = false;
         break;
       }
-      const uint8_t* un = rw_p + (size_t)s * kLhRaw + (size_t)u * kUnitQ8;
-      const int4 qa = *reinterpret_cast<const int4*>(un + lane * 16);        // feature gq
-      const int4 qb = *reinterpret_cast<const int4*>(un + 512 + lane * 16);  // feature gq + 8
+      int4 qv[4];  // (unit cw, cw + 4) x (feature gq, gq + 8)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint8_t* un = rw_p + (size_t)s * kLhRaw + (size_t)(cw + 4 * (k >> 1)) * kUnitQ8;
+        qv[k] = *reinterpret_cast<const int4*>(un + (k & 1) * 512 + lane * 16);
+      }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
       // lane (gq, t) holds k [8t, 8t + 8) of block 0 and [32 + 8t, +8) of
@@ -224,9 +231,9 @@ __global__ void __launch_bounds__(kLhThreads, 1)
       // block-1 chunk first, so each quarter-warp store covers all 32 banks.
       uint8_t* tile = cv_p + (size_t)c * kLhConv;
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int4 q = h ? qb : qa;
-        const int r = u * 16 + gq + 8 * h;
+      for (int k = 0; k < 4; ++k) {
+        const int4 q = qv[k];
+        const int r = (cw + 4 * (k >> 1)) * 16 + gq + 8 * (k & 1);
         uint32_t o[8];
         i8x4_to_act<__half>((uint32_t)q.x, o[0], o[1]);
         i8x4_to_act<__half>((uint32_t)q.y, o[2], o[3]);
@@ -351,90 +358,107 @@ __global__ void __launch_bounds__(kLhThreads, 1)
     tc_fence_after();
     const uint32_t tmem = tmem_base_s;
     const int q = warp & 3, fl = q * 32 + lane;  // this thread's feature of a tile
+    const int par = (et >> 7) & 1;               // warps 0-3 take the even stages, 4-7 the odd ones
     const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
-    // running best of rows j (+ 32) over this CTA's tiles: thread 4 j + fq
-    // scans features [32 fq, 32 fq + 32) of row j of each tile
-    const int jr = et >> 2, fq = et & 3;
+    // running best of rows j (+ 32) over this CTA's tiles: thread 8 j + fq
+    // scans features [16 fq, 16 fq + 16) of row j of each tile
+    const int jr = et >> 3, fq = et & 7;
     float rb_v[NR / 32];
     int rb_i[NR / 32];
 #pragma unroll
     for (int h = 0; h < NR / 32; ++h) rb_v[h] = -INFINITY, rb_i[h] = 0x7fffffff;
     bool ok = true;  // this warp's waits all passed
-    int g = 0;
-    // scale words (block 0 | block 1 f16) of this feature: each thread copies
-    // its own word of stage g + kScaleAhead into a private ring slot with
-    // cp.async (one group per stage), far enough ahead to hide the L2 latency
-    auto scale_fetch = [&](int gs) {
-      if (gs < n_stages) {
+    // scale words (block 0 | block 1 f16) of this feature for this warp's
+    // stages: each thread copies its own word of its stage n + kScaleAhead - 1
+    // (n counting the stages of its parity) into a private ring slot with
+    // cp.async, one group per stage, far enough ahead to hide the L2 latency
+    const int my_stages = (n_stages - par + 1) / 2;
+    auto scale_fetch = [&](int n) {
+      if (n < my_stages) {
+        const int gs = 2 * n + par;
         const int tile = blockIdx.x + (gs / nkb) * gridDim.x, kb = gs % nkb;
         const uint8_t* un = W.pk + ((size_t)tile * nkb + kb) * kLhRaw + (size_t)(fl >> 4) * kUnitQ8 + 1024;
-        cp_async4(&sc_ring[gs % kScaleAhead][fl], reinterpret_cast<const uint32_t*>(un) + (fl & 15));
+        cp_async4(&sc_ring[par][n % kScaleAhead][fl], reinterpret_cast<const uint32_t*>(un) + (fl & 15));
       }
       cp_async_commit();  // an empty group past the end keeps the group count per stage
     };
-    for (int gs = 0; gs < kScaleAhead - 1; ++gs) scale_fetch(gs);
-    // The four warps take every tile's named barriers together whatever
+    for (int n = 0; n < kScaleAhead - 1; ++n) scale_fetch(n);
+    // The eight warps take every tile's named barriers together whatever
     // their waits did: a warp whose wait gave up skips its tensor-memory
     // work, and all stop after the tile on a flag read between barriers.
+    int n = 0;  // this warp's stages so far
     for (int i = 0; i < my_tiles; ++i) {
       const int tile = blockIdx.x + i * gridDim.x;
       float acc[NR];
 #pragma unroll
       for (int j = 0; j < NR; ++j) acc[j] = 0.f;
-      for (int kb = 0; kb < nkb && ok; ++kb, ++g) {
-        scale_fetch(g + kScaleAhead - 1);
+      for (int kb = par; kb < nkb && ok; kb += 2, ++n) {
+        const int g = i * nkb + kb;
+        scale_fetch(n + kScaleAhead - 1);
         cp_async_wait<kScaleAhead - 1>();  // this stage's group has landed
-        const uint32_t sc = sc_ring[g % kScaleAhead][fl];
+        const uint32_t sc = sc_ring[par][n % kScaleAhead][fl];
         const float2 d = __half22float2(*reinterpret_cast<const __half2*>(&sc));
-        for (int b = 0; b < 2 && ok; ++b) {
-          const int B = 2 * g + b, a = B % ACC;
-          // the tensor-memory loads are warp-wide: the warp goes on only if
-          // the wait passed for all of its lanes
-          const bool got = !*abort_v && mbar_wait_bounded(&acc_full[a], (B / ACC) & 1, kLhWaitLimit);
-          if (!__all_sync(0xffffffffu, got)) {
-            ok = false;
-            *abort_v = 1;
-            break;
-          }
-          tc_fence_after();
-          const float db = b ? d.y : d.x;
+        const int a0 = (2 * g) % ACC, a1 = (2 * g + 1) % ACC;
+        // the tensor-memory loads are warp-wide: the warp goes on only if
+        // the waits passed for all of its lanes
+        const bool got = !*abort_v && mbar_wait_bounded(&acc_full[a0], ((2 * g) / ACC) & 1, kLhWaitLimit) &&
+                         mbar_wait_bounded(&acc_full[a1], ((2 * g + 1) / ACC) & 1, kLhWaitLimit);
+        if (!__all_sync(0xffffffffu, got)) {
+          ok = false;
+          *abort_v = 1;
+          break;
+        }
+        tc_fence_after();
 #pragma unroll
-          for (int c0 = 0; c0 < NR; c0 += 32) {
-            uint32_t r[32];
-            tmem_ld32(lane_base + (uint32_t)(a * NR + c0), r);
-            tmem_ld_wait();
+        for (int c0 = 0; c0 < NR; c0 += 32) {
+          // both blocks of the stage behind one wait; block 0 is added first
+          uint32_t r0[32], r1[32];
+          tmem_ld32(lane_base + (uint32_t)(a0 * NR + c0), r0);
+          tmem_ld32(lane_base + (uint32_t)(a1 * NR + c0), r1);
+          tmem_ld_wait();
 #pragma unroll
-            for (int j = 0; j < 32; ++j) acc[c0 + j] = fmaf(db, __uint_as_float(r[j]), acc[c0 + j]);
-          }
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&acc_empty[a]);
+          for (int j = 0; j < 32; ++j)
+            acc[c0 + j] = fmaf(d.y, __uint_as_float(r1[j]), fmaf(d.x, __uint_as_float(r0[j]), acc[c0 + j]));
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&acc_empty[a0]);
+          mbar_arrive(&acc_empty[a1]);
         }
       }
-      // rounded logits; per row the best (value, lowest index) of the tile
+      // the tile's logits: even-stage sum + odd-stage sum, scaled back and
+      // rounded; per row the best (value, lowest index) of the tile
       const int f0 = tile * kLhFeat;
 #pragma unroll
       for (int h = 0; h < NR / 32; ++h) {
         named_sync(1, NE);  // the previous half's reads are done
+        if (par == 1) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const float v = rnd<T>(acc[h * 32 + j] * inv_s[h * 32 + j]);  // exact power-of-two unscale
-          lg[j * kLhLgStride + fl] = v;
-          if (ep.logits && h * 32 + j < rows) ep.logits[(size_t)(h * 32 + j) * W.N + f0 + fl] = v;
+          for (int j = 0; j < 32; ++j) lg[j * kLhLgStride + fl] = acc[h * 32 + j];
+        }
+        named_sync(1, NE);
+        if (par == 0) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float v = rnd<T>((acc[h * 32 + j] + lg[j * kLhLgStride + fl]) * inv_s[h * 32 + j]);
+            lg[j * kLhLgStride + fl] = v;
+            if (ep.logits && h * 32 + j < rows) ep.logits[(size_t)(h * 32 + j) * W.N + f0 + fl] = v;
+          }
         }
         named_sync(1, NE);
         float bv = -INFINITY;
         int bi = 0x7fffffff;
-        const float* lr = lg + jr * kLhLgStride + fq * 32;
-#pragma unroll 8
-        for (int k = 0; k < 32; ++k) {
-          const int kk = (k + fq) & 31;  // lanes of a warp on 32 distinct banks
+        const float* lr = lg + jr * kLhLgStride + fq * 16;
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+          const int kk = (k + (fq >> 1)) & 15;  // the 32 lanes of a warp on 32 distinct banks
           const float v = lr[kk];
-          const int ix = f0 + fq * 32 + kk;
+          const int ix = f0 + fq * 16 + kk;
           if (v > bv || (v == bv && ix < bi)) bv = v, bi = ix;
         }
 #pragma unroll
-        for (int o = 1; o < 4; o <<= 1) {
+        for (int o = 1; o < 8; o <<= 1) {
           const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
           const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
           if (ov > bv || (ov == bv && oi < bi)) bv = ov, bi = oi;
@@ -446,6 +470,7 @@ __global__ void __launch_bounds__(kLhThreads, 1)
       named_sync(1, NE);
       if (stop_s) break;
     }
+    if (!ok) *abort_v = 1;
     cp_async_wait<0>();  // no scale copy may land after the CTA retires
     if (fq == 0) {
 #pragma unroll
@@ -507,7 +532,7 @@ int launch_t(const LinW& W, const void* x, int ldx, const int* row_map, const in
 int launch_lm_head_tc(ActType at, const LinW& W, const void* x, int ldx, const int* row_map, const int* n_rows_ptr,
                       int max_rows, const GemvEpi& ep, int* status, cudaStream_t s) {
   if (!W.q8 || W.pk == nullptr || max_rows > 64 || max_rows < 1 ||
-      W.N % kLhFeat != 0 || W.K % 64 != 0 || ep.best_val == nullptr || ep.best_idx == nullptr)
+      W.N % kLhFeat != 0 || W.K % 128 != 0 || ep.best_val == nullptr || ep.best_idx == nullptr)
     return 0;
   static int n_sm = 0;
   if (n_sm == 0) {
