@@ -73,8 +73,8 @@ constexpr int kScaleAhead = 8;                     // stages of block scales in 
 // memory goes to packed stages; two converted slots keep the MMAs fed.
 template <int NR>
 struct LhCfg {
-  static constexpr int RAW = NR == 32 ? 12 : 4;  // packed stages in flight
-  static constexpr int CONV = 2;                 // converted A slots
+  static constexpr int RAW = NR == 32 ? 8 : 4;   // packed stages in flight
+  static constexpr int CONV = NR == 32 ? 4 : 2;  // converted A slots
   static constexpr int ACC = kLhTmemCols / NR;   // block accumulators
 };
 
