@@ -212,12 +212,15 @@ WORKLOADS = {
 
 
 def build_model_and_queue(args, rank: int, world: int = 1):
-    """Model and this rank's request queue. Configs 2 and 3 hold
-    `args.requests` requests per GPU (weak scaling); config 5 is one queue
-    split over the GPUs (strong scaling). Every rank derives the same LPT
-    partition (fmd_b200.dp) from prompt lengths, budgets and the workload's
-    prior mean generation length, and builds prompt embeddings for its own
-    shard only."""
+    """Model and this rank's request queue. Configs 2 and 3 scale weakly:
+    every GPU serves the same `args.requests`-request queue as a one-GPU run
+    (the same lengths, budgets and stops; prompt rows seeded per rank), so a
+    GPU's work does not change with N and the timed windows of every rank see
+    the same mix of context lengths. Config 5 is one queue split over the
+    GPUs (strong scaling): every rank derives the same LPT partition
+    (fmd_b200.dp) from prompt lengths, budgets and the workload's prior mean
+    generation length, never the drawn stop steps, and builds prompt
+    embeddings for its own shard only."""
     pkg = __graft_entry__.load_package()
     import importlib
 
@@ -228,12 +231,14 @@ def build_model_and_queue(args, rank: int, world: int = 1):
     q8 = spec["precision"].startswith("int8")
     w = syn.make_weights(cfg, seed=args.seed, prequantized=q8)
     n_req = args.requests or spec["requests"]
-    n_total = n_req * world if spec["per_gpu"] else n_req
-    glob = syn.workload(int(args.workload), cfg, w["embed"], seed=args.seed, n_requests=n_total, with_arena=False)
+    glob = syn.workload(int(args.workload), cfg, w["embed"], seed=args.seed, n_requests=n_req, with_arena=False)
     glob.max_new = np.minimum(glob.max_new, args.max_new)
-    prior = np.full(len(glob.prompt_lens), spec["mean_new"])
-    part = dp.partition(glob.prompt_lens, glob.max_new, world, expected_new=prior)
-    wl = glob.subset(part.shard(rank))
+    if spec["per_gpu"]:
+        wl = glob
+    else:
+        prior = np.full(len(glob.prompt_lens), spec["mean_new"])
+        part = dp.partition(glob.prompt_lens, glob.max_new, world, expected_new=prior)
+        wl = glob.subset(part.shard(rank))
     wl.arena = syn.build_prompt_arena(cfg, w["embed"], wl.prompt_lens, args.seed + 7 * 3 + 1000 * rank,
                                       out_bf16=True)
     return pkg, cfg, w, wl
@@ -305,16 +310,20 @@ def cpu_sample(cfg, w, seconds: float = 15.0, steps: int | None = None, warmup: 
 def workload_config(args, cfg, n_requests: int, world: int) -> dict:
     """The `config` object both arms report."""
     spec = WORKLOADS[args.workload]
-    scale = (f"LPT request shards of a {n_requests * world}-request queue" if spec["per_gpu"] else
-             f"LPT request shards of one {spec['requests'] if not args.requests else args.requests}-request queue")
+    if spec["per_gpu"]:
+        scale = f"every GPU serves the one-GPU {n_requests}-request queue (prompt rows seeded per GPU)"
+        part = "none (weak scaling: the same queue per GPU)"
+    else:
+        scale = f"LPT request shards of one {spec['requests'] if not args.requests else args.requests}-request queue"
+        part = (f"greedy LPT on prompt length + budget + the workload's prior mean generation length "
+                f"({spec['mean_new']} tokens); drawn stop steps are not read")
     return {"workload": spec["desc"], "precision": spec["precision"],
             "requests_per_gpu": n_requests, "batch": args.batch, "prefill_chunk": args.chunk,
             "arrival": "seeded workload order for the timed windows; e2e through Engine.generate "
                        "(length-sorted queue, engine.rs:385)",
             "layers": cfg.num_hidden_layers, "step": f"{args.window} device steps",
             "l2": "working set >> L2 (no flush needed)",
-            "partition": f"greedy LPT on prompt length + budget + the workload's prior mean generation length "
-                         f"({spec['mean_new']} tokens); drawn stop steps are not read",
+            "partition": part,
             "parallelism": f"dp{world} ({scale}, no collective)"}
 
 
