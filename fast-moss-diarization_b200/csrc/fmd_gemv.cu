@@ -36,6 +36,8 @@
 //                optionally stored as f32, and the tile's (max, lowest index)
 //                per row.
 #include <cooperative_groups.h>
+#include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <float.h>
 #include <math.h>
@@ -867,12 +869,18 @@ cudaError_t init_gemv() {
 
 int gemv_tile_features(int epi) { return (epi == kGemvQkv || epi == kGemvLogits) ? 128 : 64; }
 
-// K split of one projection: the widest cluster (<= 8, portable) whose slices
-// are whole 64-wide k-blocks, but for lm_head only 2, since its activation
-// tile is re-read by each of the vocab/128 feature tiles. 0 if no split keeps
-// a slice within kMaxKb k-blocks.
+// K split of one projection: the widest cluster (<= 8, portable; a smaller
+// cap from FMD_GEMV_SPLIT in the environment, read once, for measurements)
+// whose slices are whole 64-wide k-blocks, but for lm_head only 2, since its
+// activation tile is re-read by each of the vocab/128 feature tiles. 0 if no
+// split keeps a slice within kMaxKb k-blocks.
 int gemv_split(int epi, int K) {
-  for (int s = epi == kGemvLogits ? 2 : 8; s >= 1; s >>= 1)
+  static const int cap = [] {
+    const char* v = std::getenv("FMD_GEMV_SPLIT");
+    const int c = v ? std::atoi(v) : 8;
+    return c == 1 || c == 2 || c == 4 ? c : 8;
+  }();
+  for (int s = epi == kGemvLogits ? std::min(2, cap) : cap; s >= 1; s >>= 1)
     if (K % (64 * s) == 0 && K / s <= 64 * kMaxKb) return s;
   return 0;
 }
