@@ -61,8 +61,8 @@ template <typename T>
 __global__ void __launch_bounds__(160, 2)
     k_attn_decode_tma(const __grid_constant__ CUtensorMap tmap, Plan p, int Hq, int Hkv, const T* __restrict__ q,
                       KvView kv, int layer, float scale_log2, float* __restrict__ part_acc,
-                      float* __restrict__ part_ml, int* __restrict__ counters, int* __restrict__ sched,
-                      T* __restrict__ ctx, int* __restrict__ status) {
+                      float* __restrict__ part_ml, int* __restrict__ counters, T* __restrict__ ctx,
+                      int* __restrict__ status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stages = smem;                                           // [kStages][K 16 KB | V 16 KB]
@@ -74,7 +74,6 @@ __global__ void __launch_bounds__(160, 2)
   uint64_t* full = reinterpret_cast<uint64_t*>(s_slot + kMaxRows + 1);  // 8-byte aligned (2 * 257 + 256 ints)
   uint64_t* empty = full + kStages;
   __shared__ int s_last;
-  __shared__ long long s_tilex[kStages];  // tile index of each stage (-1: end)
 
   // The plan, the page table and the KV rows of earlier steps come from
   // grids that completed before this one started (griddep_launch): the
@@ -124,18 +123,12 @@ __global__ void __launch_bounds__(160, 2)
   }
   __syncthreads();
   const long long Tt = (long long)Hkv * s_prefix[nd];
-  // Work: chunks of consecutive tiles. Static (sched == nullptr): CTA c of G
-  // owns chunk c = [c Tt / G, (c + 1) Tt / G) (with fewer tiles than CTAs
-  // only the first Tt take part, so every chunk holds a tile). Dynamic:
-  // chunks of C tiles, about four per CTA, handed out in order by a global
-  // counter, so the CTAs that stream faster take more of them.
-  const bool dyn = sched != nullptr;
-  const int G = dyn ? (int)gridDim.x : (int)min((long long)gridDim.x, Tt), c = blockIdx.x;
+  // with fewer tiles than CTAs only the first Tt take part, so that every
+  // participating CTA owns at least one tile (the merge counts on it)
+  const int G = (int)min((long long)gridDim.x, Tt), c = blockIdx.x;
   if (c >= G) return;
-  const long long C = dyn ? max(4LL, (Tt + 4LL * G - 1) / (4LL * G)) : 1;
-  const long long n_chunks = dyn ? (Tt + C - 1) / C : G;
-  auto chunk_lo = [&](long long k) -> long long { return dyn ? min(k * C, Tt) : k * Tt / G; };
-  auto chunk_of = [&](long long x) -> long long { return dyn ? x / C : (long long)cta_of(x, Tt, G); };
+  const long long x0 = (long long)c * Tt / G, x1 = (long long)(c + 1) * Tt / G;
+  const int ntl = (int)(x1 - x0);
   // (row, head, tile) of flattened tile x: the last row whose first tile is <= x
   auto locate = [&](long long x, int& r, int& h, int& j) {
     int lo = 0, hi = nd - 1;
@@ -153,15 +146,76 @@ __global__ void __launch_bounds__(160, 2)
 
   if (warp == 4) {
     // ---------------- producer warp: TMA tiles + query rows, runs ahead ----------------
-    // Each stage carries its tile's index (s_tilex) for the consumers; a
-    // stage with index -1 and no copies ends their loop.
     bool ok = true, waited = false;
-    int issued = 0;  // stages filled
+    int issued = 0;
     // copies held back until the dependency wait: stage s's query rows
     // (row, head) and its newest K/V page
     int held_q[kStages], held_kv[kStages], held_y[kStages];
-    auto issue_held = [&]() {
-      if (lane == 0)
+    for (int b0 = 0; b0 < ntl && ok; b0 += 32) {
+      // lane i looks up tile b0 + i: its row, head, tile index and page
+      int lr = 0, lh = 0, lj = 0, lpage = 0;
+      if (b0 + lane < ntl) {
+        locate(x0 + b0 + lane, lr, lh, lj);
+        lpage = kv.page_table[(size_t)s_slot[lr] * kv.max_pages_per_slot + lj];
+      }
+      const int cnt = min(32, ntl - b0);
+      for (int i = 0; i < cnt; ++i) {
+        const int r = __shfl_sync(0xffffffffu, lr, i), h = __shfl_sync(0xffffffffu, lh, i);
+        const int j = __shfl_sync(0xffffffffu, lj, i), page = __shfl_sync(0xffffffffu, lpage, i);
+        const int tt = b0 + i, s = tt % kStages;
+        if (!waited && tt >= kStages) {
+          // the ring is full: wait for the kernel before, then issue what was held back
+          griddep_wait();
+          griddep_launch();  // only after the wait: see griddep_launch
+          waited = true;
+          if (lane == 0)
+            for (int k = 0; k < kStages; ++k) {
+              uint8_t* dst = stages + k * kTileBytes;
+              if (held_kv[k]) {
+                tma_load_2d(dst, &tmap, 0, held_y[k], &full[k]);
+                tma_load_2d(dst + kBoxBytes, &tmap, 64, held_y[k], &full[k]);
+                tma_load_2d(dst + 2 * kBoxBytes, &tmap, 0, held_y[k] + Hkv * kPageTokens, &full[k]);
+                tma_load_2d(dst + 3 * kBoxBytes, &tmap, 64, held_y[k] + Hkv * kPageTokens, &full[k]);
+              }
+              if (held_q[k] >= 0) bulk_load(qbuf + k * kQBytes, q + (size_t)held_q[k], kQBytes, &full[k]);
+            }
+          __syncwarp();
+        }
+        if (tt >= kStages && !mbar_wait_bounded(&empty[s], ((tt / kStages) - 1) & 1, kWaitLimit)) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
+          const bool first = tt == 0 || j == 0;
+          const bool newest = j == ((s_len[r] + 63) >> 6) - 1;  // holds the row's own (new) position
+          const int yk = (int)(((((size_t)layer * kv.n_pages + page) * 2 + 0) * Hkv + h) * kPageTokens);
+          const int yv = yk + Hkv * kPageTokens;
+          uint8_t* dst = stages + s * kTileBytes;
+          const int qoff = r * Hq * kHeadDim + 2 * h * kHeadDim;
+          mbar_arrive_expect_tx(&full[s], kTileBytes + (first ? kQBytes : 0));
+          if (waited || !newest) {
+            tma_load_2d(dst, &tmap, 0, yk, &full[s]);
+            tma_load_2d(dst + kBoxBytes, &tmap, 64, yk, &full[s]);
+            tma_load_2d(dst + 2 * kBoxBytes, &tmap, 0, yv, &full[s]);
+            tma_load_2d(dst + 3 * kBoxBytes, &tmap, 64, yv, &full[s]);
+          }
+          if (first && waited) bulk_load(qbuf + s * kQBytes, q + (size_t)qoff, kQBytes, &full[s]);
+          if (!waited) {
+            held_kv[s] = newest;
+            held_y[s] = yk;
+            held_q[s] = first ? qoff : -1;
+          }
+        }
+        __syncwarp();
+        issued = tt + 1;
+      }
+    }
+    if (!waited) {
+      // fewer tiles than stages: everything held back goes out now
+      griddep_wait();
+      griddep_launch();  // only after the wait: see griddep_launch
+      waited = true;
+      if (lane == 0 && ok)
         for (int k = 0; k < kStages && k < issued; ++k) {
           uint8_t* dst = stages + k * kTileBytes;
           if (held_kv[k]) {
@@ -173,92 +227,6 @@ __global__ void __launch_bounds__(160, 2)
           if (held_q[k] >= 0) bulk_load(qbuf + k * kQBytes, q + (size_t)held_q[k], kQBytes, &full[k]);
         }
       __syncwarp();
-    };
-    for (long long k = dyn ? -1 : c; ok;) {
-      if (dyn) {
-        long long kk = 0;
-        if (lane == 0) kk = atomicAdd(&sched[0], 1);
-        k = __shfl_sync(0xffffffffu, kk, 0);
-      } else if (issued > 0) {
-        break;  // static: the CTA's one chunk is done
-      }
-      if (k >= n_chunks) break;
-      const long long xa = chunk_lo(k), xb = chunk_lo(k + 1);
-      const int ntl = (int)(xb - xa);
-      for (int b0 = 0; b0 < ntl && ok; b0 += 32) {
-        // lane i looks up tile b0 + i: its row, head, tile index and page
-        int lr = 0, lh = 0, lj = 0, lpage = 0;
-        if (b0 + lane < ntl) {
-          locate(xa + b0 + lane, lr, lh, lj);
-          lpage = kv.page_table[(size_t)s_slot[lr] * kv.max_pages_per_slot + lj];
-        }
-        const int cnt = min(32, ntl - b0);
-        for (int i = 0; i < cnt; ++i) {
-          const int r = __shfl_sync(0xffffffffu, lr, i), h = __shfl_sync(0xffffffffu, lh, i);
-          const int j = __shfl_sync(0xffffffffu, lj, i), page = __shfl_sync(0xffffffffu, lpage, i);
-          const int tt = issued, s = tt % kStages;
-          if (!waited && tt >= kStages) {
-            // the ring is full: wait for the kernel before, then issue what was held back
-            griddep_wait();
-            griddep_launch();  // only after the wait: see griddep_launch
-            waited = true;
-            issue_held();
-          }
-          if (tt >= kStages && !mbar_wait_bounded(&empty[s], ((tt / kStages) - 1) & 1, kWaitLimit)) {
-            ok = false;
-            break;
-          }
-          if (lane == 0) {
-            const bool first = b0 + i == 0 || j == 0;
-            const bool newest = j == ((s_len[r] + 63) >> 6) - 1;  // holds the row's own (new) position
-            const int yk = (int)(((((size_t)layer * kv.n_pages + page) * 2 + 0) * Hkv + h) * kPageTokens);
-            const int yv = yk + Hkv * kPageTokens;
-            uint8_t* dst = stages + s * kTileBytes;
-            const int qoff = r * Hq * kHeadDim + 2 * h * kHeadDim;
-            s_tilex[s] = xa + b0 + i;
-            mbar_arrive_expect_tx(&full[s], kTileBytes + (first ? kQBytes : 0));
-            if (waited || !newest) {
-              tma_load_2d(dst, &tmap, 0, yk, &full[s]);
-              tma_load_2d(dst + kBoxBytes, &tmap, 64, yk, &full[s]);
-              tma_load_2d(dst + 2 * kBoxBytes, &tmap, 0, yv, &full[s]);
-              tma_load_2d(dst + 3 * kBoxBytes, &tmap, 64, yv, &full[s]);
-            }
-            if (first && waited) bulk_load(qbuf + s * kQBytes, q + (size_t)qoff, kQBytes, &full[s]);
-            if (!waited) {
-              held_kv[s] = newest;
-              held_y[s] = yk;
-              held_q[s] = first ? qoff : -1;
-            }
-          }
-          __syncwarp();
-          issued = tt + 1;
-        }
-      }
-    }
-    if (!waited) {
-      // fewer tiles than stages: everything held back goes out now
-      griddep_wait();
-      griddep_launch();  // only after the wait: see griddep_launch
-      waited = true;
-      if (ok) issue_held();
-    }
-    if (ok) {
-      // the end mark
-      const int tt = issued, s = tt % kStages;
-      if (tt >= kStages && !mbar_wait_bounded(&empty[s], ((tt / kStages) - 1) & 1, kWaitLimit)) {
-        ok = false;
-      } else {
-        if (lane == 0) {
-          s_tilex[s] = -1;
-          mbar_arrive(&full[s]);
-        }
-        __syncwarp();
-      }
-    }
-    // the last CTA to stop taking chunks resets the counters for the next launch
-    if (dyn && lane == 0 && atomicAdd(&sched[1], 1) == G - 1) {
-      sched[0] = 0;
-      sched[1] = 0;
     }
     if (!ok && lane == 0) {
       report_timeout(status, kSiteAttnDecode);
@@ -275,26 +243,17 @@ __global__ void __launch_bounds__(160, 2)
   // before); the first tile's query rows arrive only after that anyway
   griddep_wait();
   bool aborted = false;
-  int cr = 0, ch = 0, cj = 0;  // the tile being consumed
-  int pj0 = 0;                 // first tile of the current piece
+  int cr, ch, cj;  // the tile being consumed, walked forward from x0
+  locate(x0, cr, ch, cj);
+  int ctr = s_prefix[cr + 1] - s_prefix[cr];
+  int pj0 = cj;    // first tile of the current piece
   uint32_t qf[8][2];
   float o[16][4];
   float m = -INFINITY, l = 0.f;
-  for (int tt = 0;; ++tt) {
+  for (int tt = 0; tt < ntl; ++tt) {
     const int s = tt % kStages;
-    // the four warps agree on every stage (bounded waits, one reduction
-    // barrier), so they leave the loop together and meet at every merge
-    const bool got = mbar_wait_bounded(&full[s], (tt / kStages) & 1, kWaitLimit);
-    if (named_sync_or(1, 128, !got)) {
-      aborted = true;
-      break;
-    }
-    const long long x = *reinterpret_cast<volatile long long*>(&s_tilex[s]);
-    if (x < 0) break;
-    locate(x, cr, ch, cj);
-    const int ctr = s_prefix[cr + 1] - s_prefix[cr];
-    const long long kc = chunk_of(x), xa = chunk_lo(kc), xb = chunk_lo(kc + 1);
-    const bool first = x == xa || cj == 0, last = x == xb - 1 || cj == ctr - 1;
+    if (!aborted && !mbar_wait_bounded(&full[s], (tt / kStages) & 1, kWaitLimit)) aborted = true;
+    const bool first = tt == 0 || cj == 0, last = tt == ntl - 1 || cj == ctr - 1;
     if (first) {
       pj0 = cj;
       m = -INFINITY;
@@ -309,65 +268,65 @@ __global__ void __launch_bounds__(160, 2)
         qf[ks][1] = g < 2 ? qrow[ks * 8 + 4 + t] : 0u;
       }
     }
-    const int nvalid = min(64, s_len[cr] - cj * 64);
-    if (warp * 16 < nvalid) {
-      const uint32_t kb = smem_u32(stages + s * kTileBytes);
-      const uint32_t vb = kb + 2 * kBoxBytes;
-      const int mi = lane >> 3;
-      float sc[2][4];
+      const int nvalid = min(64, s_len[cr] - cj * 64);
+      if (!aborted && warp * 16 < nvalid) {
+        const uint32_t kb = smem_u32(stages + s * kTileBytes);
+        const uint32_t vb = kb + 2 * kBoxBytes;
+        const int mi = lane >> 3;
+        float sc[2][4];
 #pragma unroll
-      for (int i = 0; i < 2; ++i) sc[i][0] = sc[i][1] = sc[i][2] = sc[i][3] = 0.f;
-      {
-        const int tok = warp * 16 + (mi >> 1) * 8 + (lane & 7);
+        for (int i = 0; i < 2; ++i) sc[i][0] = sc[i][1] = sc[i][2] = sc[i][3] = 0.f;
+        {
+          const int tok = warp * 16 + (mi >> 1) * 8 + (lane & 7);
 #pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {
+          for (int ks = 0; ks < 8; ++ks) {
+            uint32_t rr[4];
+            ldmatrix_x4(rr, kb + swz(tok, 2 * ks + (mi & 1)));
+            const uint32_t a[4] = {qf[ks][0], 0u, qf[ks][1], 0u};
+            mma16816<T>(sc[0], a, rr[0], rr[1]);
+            mma16816<T>(sc[1], a, rr[2], rr[3]);
+          }
+        }
+        float mx = -INFINITY;
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int tok = warp * 16 + nt * 8 + 2 * t + e;
+            sc[nt][e] = tok < nvalid ? sc[nt][e] * scale_log2 : -INFINITY;
+            mx = fmaxf(mx, sc[nt][e]);
+          }
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        const float mn = fmaxf(m, mx);  // finite: position warp*16 is valid
+        const float corr = exp2f(m - mn);
+        float ps = 0.f;
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            sc[nt][e] = exp2f(sc[nt][e] - mn);
+            ps += sc[nt][e];
+          }
+        l = l * corr + ps;
+        m = mn;
+#pragma unroll
+        for (int dn = 0; dn < 16; ++dn) {
+          o[dn][0] *= corr;
+          o[dn][1] *= corr;
+        }
+        const uint32_t pa[4] = {Act<T>::pack2(sc[0][0], sc[0][1]), 0u, Act<T>::pack2(sc[1][0], sc[1][1]), 0u};
+        const int tok = warp * 16 + (mi & 1) * 8 + (lane & 7);
+#pragma unroll
+        for (int dp = 0; dp < 8; ++dp) {
           uint32_t rr[4];
-          ldmatrix_x4(rr, kb + swz(tok, 2 * ks + (mi & 1)));
-          const uint32_t a[4] = {qf[ks][0], 0u, qf[ks][1], 0u};
-          mma16816<T>(sc[0], a, rr[0], rr[1]);
-          mma16816<T>(sc[1], a, rr[2], rr[3]);
+          ldmatrix_x4_trans(rr, vb + swz(tok, 2 * dp + (mi >> 1)));
+          mma16816<T>(o[2 * dp], pa, rr[0], rr[1]);
+          mma16816<T>(o[2 * dp + 1], pa, rr[2], rr[3]);
         }
       }
-      float mx = -INFINITY;
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int tok = warp * 16 + nt * 8 + 2 * t + e;
-          sc[nt][e] = tok < nvalid ? sc[nt][e] * scale_log2 : -INFINITY;
-          mx = fmaxf(mx, sc[nt][e]);
-        }
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-      const float mn = fmaxf(m, mx);  // finite: position warp*16 is valid
-      const float corr = exp2f(m - mn);
-      float ps = 0.f;
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          sc[nt][e] = exp2f(sc[nt][e] - mn);
-          ps += sc[nt][e];
-        }
-      l = l * corr + ps;
-      m = mn;
-#pragma unroll
-      for (int dn = 0; dn < 16; ++dn) {
-        o[dn][0] *= corr;
-        o[dn][1] *= corr;
-      }
-      const uint32_t pa[4] = {Act<T>::pack2(sc[0][0], sc[0][1]), 0u, Act<T>::pack2(sc[1][0], sc[1][1]), 0u};
-      const int tok = warp * 16 + (mi & 1) * 8 + (lane & 7);
-#pragma unroll
-      for (int dp = 0; dp < 8; ++dp) {
-        uint32_t rr[4];
-        ldmatrix_x4_trans(rr, vb + swz(tok, 2 * dp + (mi >> 1)));
-        mma16816<T>(o[2 * dp], pa, rr[0], rr[1]);
-        mma16816<T>(o[2 * dp + 1], pa, rr[2], rr[3]);
-      }
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);  // this warp is done with stage s
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);  // this warp is done with stage s
 
     if (last) {
       // ---- merge the 4 consumer warps over this piece ----
@@ -402,47 +361,55 @@ __global__ void __launch_bounds__(160, 2)
       }
       T* cdst = ctx + (size_t)cr * Hq * kHeadDim + (2 * ch + hd) * kHeadDim + d0;
       if (pj0 == 0 && cj == ctr - 1) {
-        // the whole segment lies in this chunk
-        *reinterpret_cast<uint32_t*>(cdst) = Act<T>::pack2(A0 / L, A1 / L);
+        // the whole segment lies in this CTA
+        if (!aborted) *reinterpret_cast<uint32_t*>(cdst) = Act<T>::pack2(A0 / L, A1 / L);
       } else {
         const long long seg0 = (long long)Hkv * s_prefix[cr] + (long long)ch * ctr;
-        // slot 2k holds a piece that began in an earlier chunk, 2k + 1 one that continues in a later one
-        const size_t slot = 2 * (size_t)kc + (seg0 < xa ? 0 : 1);
-        const size_t e = slot * 2 + hd;
+        // slot 2c holds a piece that began in an earlier CTA, 2c + 1 one that continues in a later one
+        const int slot = 2 * c + (seg0 < x0 ? 0 : 1);
+        const size_t e = (size_t)slot * 2 + hd;
         part_acc[e * kHeadDim + d0] = A0;
         part_acc[e * kHeadDim + d0 + 1] = A1;
         if (d0 == 0) {
           part_ml[e * 2] = M;
           part_ml[e * 2 + 1] = L;
         }
-        const long long cf = chunk_of(seg0), cl = chunk_of(seg0 + ctr - 1);
+        const int cf = cta_of(seg0, Tt, G), cl = cta_of(seg0 + ctr - 1, Tt, G);
         // the barrier orders every consumer's partial stores before thread
         // 0's fence (cumulative); the merging CTA's reads are ordered after its
         // fenced atomic the same way
         named_sync(1, 128);
         if (tid == 0) {
           __threadfence();
-          s_last = atomicAdd(&counters[cr * Hkv + ch], 1) == (int)(cl - cf);
+          s_last = atomicAdd(&counters[cr * Hkv + ch], 1) == cl - cf;
           if (s_last) __threadfence();
         }
         named_sync(1, 128);
         if (s_last) {
           float MM = -INFINITY;
-          for (long long cc = cf; cc <= cl; ++cc)
+          for (int cc = cf; cc <= cl; ++cc)
             MM = fmaxf(MM, __ldcg(&part_ml[((size_t)(2 * cc + (cc == cf ? 1 : 0)) * 2 + hd) * 2]));
           float LL = 0.f, B0 = 0.f, B1 = 0.f;
-          for (long long cc = cf; cc <= cl; ++cc) {
+          for (int cc = cf; cc <= cl; ++cc) {
             const size_t e2 = (size_t)(2 * cc + (cc == cf ? 1 : 0)) * 2 + hd;
             const float wgt = exp2f(__ldcg(&part_ml[e2 * 2]) - MM);
             LL = fmaf(__ldcg(&part_ml[e2 * 2 + 1]), wgt, LL);
             B0 = fmaf(__ldcg(&part_acc[e2 * kHeadDim + d0]), wgt, B0);
             B1 = fmaf(__ldcg(&part_acc[e2 * kHeadDim + d0 + 1]), wgt, B1);
           }
-          *reinterpret_cast<uint32_t*>(cdst) = Act<T>::pack2(B0 / LL, B1 / LL);
+          if (!aborted) *reinterpret_cast<uint32_t*>(cdst) = Act<T>::pack2(B0 / LL, B1 / LL);
           if (tid == 0) counters[cr * Hkv + ch] = 0;
         }
       }
       named_sync(1, 128);  // `red` is reused by the next piece
+    }
+    // advance to the next tile of the sequence
+    if (++cj == ctr) {
+      cj = 0;
+      if (++ch == Hkv) {
+        ch = 0;
+        if (++cr < nd) ctr = s_prefix[cr + 1] - s_prefix[cr];
+      }
     }
   }
   if (aborted && tid == 0) report_timeout(status, kSiteAttnDecode);
@@ -450,10 +417,7 @@ __global__ void __launch_bounds__(160, 2)
 
 }  // namespace
 
-// Split partials: two slots per chunk, at most 4 x grid chunks (dynamic
-// scheduling; the static split has one chunk per CTA).
-size_t attn_decode_partial_acc_floats(int grid) { return (size_t)2 * 4 * grid * 2 * kHeadDim; }
-size_t attn_decode_partial_floats(int grid) { return (size_t)2 * 4 * grid * 2 * (kHeadDim + 2); }
+size_t attn_decode_partial_floats(int grid) { return (size_t)2 * grid * 2 * (kHeadDim + 2); }
 
 size_t attn_decode_smem_bytes() {
   return 1024 + kStages * (kTileBytes + kQBytes) + 4 * 2 * kRedStride * 4 + (3 * kMaxRows + 2) * 4 +
@@ -470,17 +434,17 @@ cudaError_t init_attn_decode() {
 
 void launch_attn_decode_tma(ActType at, const void* tmap, const Plan& p, int grid, int Hq, int Hkv, const void* q,
                             const KvView& kv, int layer, float scale, float* part_acc, float* part_ml, int* counters,
-                            int* sched, void* ctx, int* status, cudaStream_t s) {
+                            void* ctx, int* status, cudaStream_t s) {
   const float scale_log2 = scale * 1.4426950408889634f;
   const CUtensorMap& m = *reinterpret_cast<const CUtensorMap*>(tmap);
   const size_t smem = attn_decode_smem_bytes();
   if (at == kBF16)
     launch_pdl(k_attn_decode_tma<__nv_bfloat16>, dim3(grid), dim3(160), smem, s, m, p, Hq, Hkv, (const __nv_bfloat16*)q, kv, layer,
-                                                             scale_log2, part_acc, part_ml, counters, sched,
+                                                             scale_log2, part_acc, part_ml, counters,
                                                              (__nv_bfloat16*)ctx, status);
   else
     launch_pdl(k_attn_decode_tma<__half>, dim3(grid), dim3(160), smem, s, m, p, Hq, Hkv, (const __half*)q, kv, layer, scale_log2,
-                                                      part_acc, part_ml, counters, sched, (__half*)ctx, status);
+                                                      part_acc, part_ml, counters, (__half*)ctx, status);
 }
 
 }  // namespace fmd

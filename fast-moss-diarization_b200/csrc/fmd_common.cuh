@@ -207,16 +207,6 @@ FMD_DEV void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar
 }
 // Named barrier over `nthreads` threads (a subset of the CTA).
 FMD_DEV void named_sync(int id, int nthreads) { asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(nthreads) : "memory"); }
-// The same barrier, returning whether `pred` held in any of the threads.
-FMD_DEV bool named_sync_or(int id, int nthreads, bool pred) {
-  uint32_t r;
-  asm volatile(
-      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, %2, %3, p;\n selp.u32 %0, 1, 0, q;\n}\n"
-      : "=r"(r)
-      : "r"((uint32_t)pred), "r"(id), "r"(nthreads)
-      : "memory");
-  return r != 0;
-}
 
 // ---- tcgen05 (5th-generation tensor cores, accumulators in tensor memory) ----------
 // Tensor memory: 512 columns x 128 lanes of 32 bits per SM. A warp may only

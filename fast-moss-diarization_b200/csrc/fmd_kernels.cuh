@@ -306,18 +306,12 @@ void launch_pick_reduce(const int* n_sample_ptr, int B, const float* best_val, c
 // [layers*pages*2*kv_heads*64 rows][128 dims], box 64x64, 128B swizzle.
 size_t attn_decode_smem_bytes();
 // floats of the split-segment partials of a decode-attention grid of `grid`
-// CTAs (two slots per chunk of tiles, up to 4 x grid chunks, both query
-// heads of a kv head): acc floats first (attn_decode_partial_acc_floats),
-// then m + l
-size_t attn_decode_partial_acc_floats(int grid);
+// CTAs (two slots per CTA, both query heads of a kv head, acc + m + l)
 size_t attn_decode_partial_floats(int grid);
 cudaError_t init_attn_decode();
-// `sched`: two zeroed ints (chunk counter, finished CTAs; reset by the
-// launch's last CTA) for dynamic chunk scheduling, or nullptr for the static
-// equal split over the CTAs.
 void launch_attn_decode_tma(ActType at, const void* tmap, const Plan& p, int grid, int Hq, int Hkv, const void* q,
                             const KvView& kv, int layer, float scale, float* part_acc, float* part_ml, int* counters,
-                            int* sched, void* ctx, int* status, cudaStream_t s);
+                            void* ctx, int* status, cudaStream_t s);
 
 // ---- tensor-core projections of mixed steps (fmd_gemm_tc.cu) ----
 // W [N][K] 16-bit behind a TMA map with box {64, bn} and the 128-byte

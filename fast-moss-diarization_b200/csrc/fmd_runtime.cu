@@ -162,10 +162,6 @@ struct fmd_handle {
   cudaEvent_t fork_ev = nullptr, join_ev = nullptr;
   PlanCounts* half_counts = nullptr;  // [2]
   float *pacc2 = nullptr, *pml2 = nullptr;
-  // decode attention: chunks of page tiles handed out by a counter
-  // (default; FMD_ATTN_DYNAMIC=0 selects the static equal split)
-  bool attn_dyn = true;
-  int* attn_sched = nullptr;  // [2 halves][chunk counter, finished CTAs]
   float* ssq = nullptr;       // [max_slots][hidden / 64] per-tile sums of squares of the residual stream
   float* best_val = nullptr;  // [max_slots][vocab / 64] greedy candidates of the decode path
   int* best_idx = nullptr;
@@ -530,8 +526,7 @@ struct DecodeView {
   void *x, *qbuf, *ctx, *hbuf;
   float *ssq, *pacc, *pml;
   int* counters;
-  int* sched;  // dynamic chunk counters of the decode attention, or nullptr
-  int grid;    // decode attention CTAs
+  int grid;  // decode attention CTAs
 };
 
 // half = -1: every row; 0 / 1: the rows of that half of a split step.
@@ -549,7 +544,6 @@ DecodeView decode_view(fmd_handle* h, int half) {
   v.pacc = h->pacc;
   v.pml = h->pml;
   v.counters = h->attn_counters;
-  v.sched = h->attn_dyn ? h->attn_sched : nullptr;
   v.grid = h->di_grid;
   if (half < 0) return v;
   const int S = R / 2, r0 = half * S;
@@ -569,7 +563,6 @@ DecodeView decode_view(fmd_handle* h, int half) {
     v.pml = h->pml2;
   }
   v.counters = h->attn_counters + (size_t)r0 * h->Hkv();
-  if (v.sched) v.sched += 2 * half;
   v.grid = h->n_sm;  // one attention CTA per SM leaves room for the other half's projections
   return v;
 }
@@ -614,7 +607,7 @@ void decode_layers(fmd_handle* h, const DecodeView& v, cudaStream_t s, bool prob
     const bool probe = probe_attn && h->record_attn_events && l == h->attn_probe_layer();
     if (probe) cudaEventRecordWithFlags(h->attn_events[0], s, cudaEventRecordExternal);
     launch_attn_decode_tma(h->at, &h->kv_tmap, v.plan, v.grid, h->Hq(), h->Hkv(), v.qbuf, h->kv, l,
-                           h->attn_scale, v.pacc, v.pml, v.counters, v.sched, v.ctx, h->d_status, s);
+                           h->attn_scale, v.pacc, v.pml, v.counters, v.ctx, h->d_status, s);
     if (probe) cudaEventRecordWithFlags(h->attn_events[1], s, cudaEventRecordExternal);
     trace(h, "attn_decode", l);
     if (h->chain_ok) {
@@ -747,8 +740,7 @@ void run_forward(fmd_handle* h, float* logits_dev, const void* arena, bool decod
     const bool probe = h->record_attn_events && l == h->attn_probe_layer();
     if (probe) cudaEventRecordWithFlags(h->attn_events[0], s, cudaEventRecordExternal);
     launch_attn_decode_tma(h->at, &h->kv_tmap, h->plan, h->di_grid, h->Hq(), h->Hkv(), h->qbuf, h->kv, l,
-                           h->attn_scale, h->pacc, h->pml, h->attn_counters, h->attn_dyn ? h->attn_sched : nullptr,
-                           h->ctx, h->d_status, s);
+                           h->attn_scale, h->pacc, h->pml, h->attn_counters, h->ctx, h->d_status, s);
     if (probe) cudaEventRecordWithFlags(h->attn_events[1], s, cudaEventRecordExternal);
     trace(h, "attn_decode", l);
     launch_attn_prefill_tc(h->at, &h->kv_tmap, &h->qmap, h->plan, h->pb_max, h->Hq(), h->Hkv(), h->kv, l,
@@ -885,9 +877,6 @@ int sync_check(fmd_handle* h) {
     if (e != cudaSuccess) return fail(h, FMD_EIO, std::string("status read: ") + cudaGetErrorString(e));
     if (st[0] != 0) {
       cudaMemset(h->d_status, 0, 2 * sizeof(int));
-      // a launch that gave up may have left its attention counters mid-count
-      if (h->attn_sched) cudaMemset(h->attn_sched, 0, 4 * sizeof(int));
-      if (h->attn_counters) cudaMemset(h->attn_counters, 0, (size_t)h->max_slots * h->Hkv() * sizeof(int));
       static const char* const kSites[] = {"?", "k_gemv", "k_lm_head", "k_attn_decode_tma", "k_attn_prefill_tc",
                                            "k_gemm_tc", "k_layer_tail", "k_wait_probe", "k_proj_tc"};
       constexpr int kNumSites = (int)(sizeof(kSites) / sizeof(kSites[0]));
@@ -1015,8 +1004,6 @@ int fmd_create(const fmd_config* cfg, int32_t precision, int32_t device, fmd_han
     h->lm_tc_allowed = lt != nullptr && lt[0] == '1';
     const char* pp = std::getenv("FMD_PREFILL_PP");
     h->pf_pp_allowed = !(pp != nullptr && pp[0] == '0');
-    const char* ad = std::getenv("FMD_ATTN_DYNAMIC");
-    h->attn_dyn = !(ad != nullptr && ad[0] == '0');
     const char* sp = std::getenv("FMD_DECODE_SPLIT");
     h->split_allowed = sp != nullptr && sp[0] == '1';
   }
@@ -1227,17 +1214,13 @@ int fmd_kv_reserve(fmd_handle* h, int32_t max_slots, int64_t max_tokens_total, i
   // decode attention split-segment partials: acc [2 * grid][2][128], then m/l [2 * grid][2][2]
   if ((rc = A(attn_decode_partial_floats(h->di_grid) * 4, &p))) return rc;
   h->pacc = (float*)p;
-  h->pml = h->pacc + attn_decode_partial_acc_floats(h->di_grid);
-  // dynamic chunk scheduling of decode attention: two counters per half of a split step
-  if ((rc = A(4 * sizeof(int), &p))) return rc;
-  CK(cudaMemset(p, 0, 4 * sizeof(int)));
-  h->attn_sched = (int*)p;
+  h->pml = h->pacc + (size_t)2 * h->di_grid * 2 * kHeadDim;
   // a split decode step: the second half's attention partials, both halves' row counts
   h->split_ok = h->split_allowed && !h->chain_ok && max_slots >= 16 && max_slots % 2 == 0;
   if (h->split_ok) {
     if ((rc = A(attn_decode_partial_floats(h->di_grid) * 4, &p))) return rc;
     h->pacc2 = (float*)p;
-    h->pml2 = h->pacc2 + attn_decode_partial_acc_floats(h->di_grid);
+    h->pml2 = h->pacc2 + (size_t)2 * h->di_grid * 2 * kHeadDim;
     if ((rc = A(2 * sizeof(PlanCounts), &p))) return rc;
     CK(cudaMemset(p, 0, 2 * sizeof(PlanCounts)));
     h->half_counts = (PlanCounts*)p;
