@@ -378,10 +378,11 @@ __global__ void __launch_bounds__(192, 1)
 
 // ---- persistent, two query tiles per CTA ------------------------------------
 // The same arithmetic as k_attn_prefill_tc, scheduled for the tensor cores:
-//  * a work item is a pair of consecutive 64-row blocks of one sequence (A, B)
-//    for one kv head: both tiles need the same key pages (B's history is A's
-//    plus at most one page), so each K/V page tile is read once for four
-//    query-head rows sets. A sequence's odd last block is an item of its own;
+//  * a work item is a pair of 64-row blocks of one sequence (A earlier, B
+//    later) for one kv head: both tiles read the same key pages up to A's
+//    history, so each such K/V page tile is read once for both. A sequence's
+//    run of n blocks pairs block i with block n - 1 - i, which evens out the
+//    items' key-tile counts; the middle block of an odd run is an item alone;
 //  * items are ranked by key tiles (longest first), work w = (item w / Hkv,
 //    head w % Hkv); CTA c of G takes works c, 2G - 1 - c, 2G + c, ... (snake
 //    order), so the long items are spread over the CTAs and the short ones
@@ -402,7 +403,7 @@ constexpr int kPpThreads = 320;
 constexpr int kPpTmemCols = 512;
 
 size_t attn_pp_smem_bytes() {
-  return 1024 + 2 * kPfQBytes + 2 * kPfPBytes + kPfStages * kPfKvBytes + (size_t)3 * kMaxPrefillBlocks * 4;
+  return 1024 + 2 * kPfQBytes + 2 * kPfPBytes + kPfStages * kPfKvBytes + (size_t)4 * kMaxPrefillBlocks * 4;
 }
 
 template <typename T>
@@ -426,26 +427,33 @@ __global__ void __launch_bounds__(kPpThreads, 1)
   int* s_slot = reinterpret_cast<int*>(base_p + 2 * kPfQBytes + 2 * kPfPBytes + kPfStages * kPfKvBytes);
   int* s_cost = s_slot + kMaxPrefillBlocks;
   int* s_order = s_cost + kMaxPrefillBlocks;
+  int* s_partner = s_order + kMaxPrefillBlocks;  // tile B of the item a block starts (-1: none)
 
   griddep_wait();  // q, the KV rows of this step and the plan come from earlier kernels
   griddep_launch();  // only after the wait: see griddep_launch
   const int n_blocks = min(p.counts->n_pblocks, kMaxPrefillBlocks);
   if (n_blocks == 0) return;  // whole CTA, before any barrier or tensor memory exists
   auto tiles_of = [&](int b) { return (p.row_pos[p.pb_row0[b]] + p.pb_n[b] + kPageTokens - 1) / kPageTokens; };
-  // ---- items: a block at an even position of its sequence's run starts one
+  // ---- items: the run of n blocks of one sequence pairs its block i with
+  // block n - 1 - i (the shortest history with the longest, so that every
+  // item needs about the same number of key tiles); the middle block of an
+  // odd run is an item of its own
   if (threadIdx.x == 0) n_items_s = 0;
   for (int b = threadIdx.x; b < n_blocks; b += kPpThreads) s_slot[b] = p.row_slot[p.pb_row0[b]];
   __syncthreads();
   for (int b = threadIdx.x; b < n_blocks; b += kPpThreads) {
-    int j = 0;
+    int j = 0, after = 0;
     while (b - j - 1 >= 0 && s_slot[b - j - 1] == s_slot[b]) ++j;
-    int cost = 0;
-    if ((j & 1) == 0) {
-      const bool pair = b + 1 < n_blocks && s_slot[b + 1] == s_slot[b];
-      cost = tiles_of(b) + (pair ? tiles_of(b + 1) : 0);
+    while (b + after + 1 < n_blocks && s_slot[b + after + 1] == s_slot[b]) ++after;
+    const int n = j + 1 + after;  // the run's length; b is its block j
+    int cost = 0, partner = -1;
+    if (2 * j + 1 <= n) {
+      partner = 2 * j + 1 < n ? b + (n - 1 - 2 * j) : -1;  // block n - 1 - j of the run
+      cost = tiles_of(b) + (partner >= 0 ? tiles_of(partner) : 0);
       atomicAdd(&n_items_s, 1);
     }
     s_cost[b] = cost;  // 0: not an item start (every item has >= 1 tile)
+    s_partner[b] = partner;
   }
   __syncthreads();
   for (int b = threadIdx.x; b < n_blocks; b += kPpThreads) {
@@ -504,7 +512,7 @@ __global__ void __launch_bounds__(kPpThreads, 1)
     if (wi >= n_works) return false;
     w.a = s_order[wi / Hkv];
     w.h = wi % Hkv;
-    w.b = w.a + 1 < n_blocks && s_slot[w.a + 1] == s_slot[w.a] ? w.a + 1 : -1;
+    w.b = s_partner[w.a];
     return true;
   };
 
