@@ -69,6 +69,7 @@ __global__ void __launch_bounds__(FW * KG * 32) k_gemv(const T* __restrict__ x, 
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t wbar[kMaxKb];
   __shared__ float rs_s[kRows];
+  __shared__ __align__(16) T nw_s[NORM ? kMaxKb * 64 : 8];  // the RMSNorm weights of this CTA's k-slice
 
   const int S = gridDim.y, rank = blockIdx.y;
   const int K = W.K;
@@ -93,6 +94,12 @@ __global__ void __launch_bounds__(FW * KG * 32) k_gemv(const T* __restrict__ x, 
       mbar_arrive_expect_tx(&wbar[kb], kb_bytes);
       bulk_load(wsm + kb * kb_bytes, src + (size_t)kb * kb_bytes, kb_bytes, &wbar[kb]);
     }
+  }
+  // RMSNorm weights of this CTA's k-slice (constant: fetched before the wait,
+  // off the path that starts when the activations arrive)
+  if constexpr (NORM) {
+    const int4* src = reinterpret_cast<const int4*>(reinterpret_cast<const T*>(ep.norm_w) + kbeg);
+    for (int i = threadIdx.x; i < (klen >> 3); i += NT) reinterpret_cast<int4*>(nw_s)[i] = src[i];
   }
   // q/k RMSNorm weights of this CTA's head (constant: fetched before the wait)
   float hnw[4] = {1.f, 1.f, 1.f, 1.f};
@@ -172,8 +179,8 @@ __global__ void __launch_bounds__(FW * KG * 32) k_gemv(const T* __restrict__ x, 
     if constexpr (NORM) rows_rsqrt(ep.ssq, ep.ssq_tiles, row_map, row0, rows, K, ep.eps, rs_s, NT);
     cp_async_wait<0>();
     if constexpr (NORM) {
-      __syncthreads();  // rs_s
-      const T* nw = reinterpret_cast<const T*>(ep.norm_w) + kbeg;
+      __syncthreads();  // rs_s, nw_s
+      const T* nw = nw_s;
       for (int c = threadIdx.x; c < rows * cpr; c += NT) {
         const int r = c / cpr, ch = c - r * cpr;
         int4* p = reinterpret_cast<int4*>(xs + (size_t)r * xstride + ch * 8);
