@@ -851,7 +851,7 @@ int launch_lm_head_t(const LinW& W, const void* x, int ldx, const int* row_map, 
 template <typename T, bool Q8>
 cudaError_t init_gemv_t() {
   cudaError_t e = cudaSuccess;
-  const int lim = 226 * 1024;  // opt-in limit less room for the static barrier and row scales
+  const int lim = 220 * 1024;  // opt-in limit less room for the static barriers, row scales and norm weights
   for (cudaError_t r : {
            cudaFuncSetAttribute(k_gemv<T, Q8, 8, kGemvQkv, true, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim),
            cudaFuncSetAttribute(k_gemv<T, Q8, 8, kGemvQkv, false, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim),
