@@ -264,27 +264,32 @@ __global__ void __launch_bounds__(FW * KG * 32) k_gemv(const T* __restrict__ x, 
   if (!ok) report_timeout(status, kSiteGemv);
   __syncthreads();  // the activation tile is dead: `part` reuses it
 
-  // ---- partial tile -> shared memory (the last k-block group writes, then
-  // groups KG-2 .. 0 add theirs in turn: a fixed order); the cluster sums the
-  // CTAs' tiles
+  // ---- partial tile -> shared memory (k-block group 1, then group 0 adds
+  // its own: a fixed order); the cluster sums the CTAs' tiles
   constexpr int PS = FT + 4;  // part row stride (floats)
-  static_assert(KG == 1 || KG == 2 || KG == 4, "one, two or four k-block groups");
+  static_assert(KG == 1 || KG == 2, "one or two k-block groups");
+  if (kgrp == KG - 1) {
 #pragma unroll
-  for (int gi = KG - 1; gi >= 0; --gi) {
-    if (gi < KG - 1) __syncthreads();
-    if (kgrp == gi) {
-      const bool add = gi < KG - 1;
+    for (int nt = 0; nt < 8; ++nt) {
+      if (nt < n_tiles) {
+        const int lr = nt * 8 + 2 * t;
+        part[lr * PS + fl] = acc[nt][0];
+        part[(lr + 1) * PS + fl] = acc[nt][1];
+        part[lr * PS + fl + 8] = acc[nt][2];
+        part[(lr + 1) * PS + fl + 8] = acc[nt][3];
+      }
+    }
+  }
+  if (KG == 2) __syncthreads();
+  if (KG == 2 && kgrp == 0) {
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
-        if (nt < n_tiles) {
-          const int lr = nt * 8 + 2 * t;
-          float* p0 = part + lr * PS + fl;
-          float* p1 = part + (lr + 1) * PS + fl;
-          p0[0] = add ? acc[nt][0] + p0[0] : acc[nt][0];
-          p1[0] = add ? acc[nt][1] + p1[0] : acc[nt][1];
-          p0[8] = add ? acc[nt][2] + p0[8] : acc[nt][2];
-          p1[8] = add ? acc[nt][3] + p1[8] : acc[nt][3];
-        }
+    for (int nt = 0; nt < 8; ++nt) {
+      if (nt < n_tiles) {
+        const int lr = nt * 8 + 2 * t;
+        part[lr * PS + fl] = acc[nt][0] + part[lr * PS + fl];
+        part[(lr + 1) * PS + fl] = acc[nt][1] + part[(lr + 1) * PS + fl];
+        part[lr * PS + fl + 8] = acc[nt][2] + part[lr * PS + fl + 8];
+        part[(lr + 1) * PS + fl + 8] = acc[nt][3] + part[(lr + 1) * PS + fl + 8];
       }
     }
   }
@@ -850,7 +855,7 @@ cudaError_t init_gemv_t() {
   for (cudaError_t r : {
            cudaFuncSetAttribute(k_gemv<T, Q8, 8, kGemvQkv, true, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim),
            cudaFuncSetAttribute(k_gemv<T, Q8, 8, kGemvQkv, false, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim),
-           cudaFuncSetAttribute(k_gemv<T, Q8, 4, kGemvResid, false, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim),
+           cudaFuncSetAttribute(k_gemv<T, Q8, 4, kGemvResid, false, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim),
            cudaFuncSetAttribute(k_gemv<T, Q8, 4, kGemvSwiglu, true, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim),
            cudaFuncSetAttribute(k_gemv<T, Q8, 8, kGemvLogits, true, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim),
            cudaFuncSetAttribute(k_lm_head<T, Q8, 4, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kHeadSmemBudget),
@@ -938,7 +943,7 @@ bool launch_gemv(ActType at, int epi, bool norm, const LinW& W, const void* x, i
       if (norm) launch_gemv_t<T, Q8, 8, kGemvQkv, true, 1>(W, S, x, ldx, row_map, n_rows_ptr, max_rows, ep, status, s);     \
       else launch_gemv_t<T, Q8, 8, kGemvQkv, false, 1>(W, S, x, ldx, row_map, n_rows_ptr, max_rows, ep, status, s);         \
       break;                                                                                                    \
-    case kGemvResid: launch_gemv_t<T, Q8, 4, kGemvResid, false, 4>(W, S, x, ldx, row_map, n_rows_ptr, max_rows, ep, status, s); break; \
+    case kGemvResid: launch_gemv_t<T, Q8, 4, kGemvResid, false, 2>(W, S, x, ldx, row_map, n_rows_ptr, max_rows, ep, status, s); break; \
     case kGemvSwiglu: launch_gemv_t<T, Q8, 4, kGemvSwiglu, true, 1>(W, S, x, ldx, row_map, n_rows_ptr, max_rows, ep, status, s); break; \
     default: launch_gemv_t<T, Q8, 8, kGemvLogits, true, 1>(W, S, x, ldx, row_map, n_rows_ptr, max_rows, ep, status, s); break; \
   }
