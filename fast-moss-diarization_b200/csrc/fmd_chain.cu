@@ -105,20 +105,14 @@ FMD_DEV void grid_barrier(cg::cluster_group& cluster, int* bar, int n_clusters, 
   cluster.sync();
   if (cluster.block_rank() == 0 && threadIdx.x == 0) {
     red_release(bar, 1);
-    uint64_t t0 = 0;  // the clock only on a long wait (see mbar_wait_bounded)
+    const uint64_t t0 = globaltimer_ns();
     bool ok = false;
     for (uint32_t i = 0; i < kSpinLimit; ++i) {
       if (ld_acquire(bar) >= n_clusters) {
         ok = true;
         break;
       }
-      if ((i & 255) == 255) {
-        const uint64_t now = globaltimer_ns();
-        if (t0 == 0)
-          t0 = now;
-        else if (now - t0 > kWaitNsCap)
-          break;
-      }
+      if ((i & 63) == 63 && globaltimer_ns() - t0 > kWaitNsCap) break;
       __nanosleep(32);
     }
     if (!ok) report_timeout(status, kSiteLayerTail);

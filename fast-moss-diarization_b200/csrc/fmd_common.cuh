@@ -159,20 +159,13 @@ FMD_DEV uint64_t globaltimer_ns() {
 // which can never complete surfaces as FMD_ETIMEDOUT within about a second.
 constexpr uint64_t kWaitNsCap = 500ull * 1000 * 1000;
 // Bounded wait: returns false if the phase did not complete within `limit`
-// polls or kWaitNsCap of wall time, whichever comes first. The clock is read
-// only every 256 polls (each poll may suspend the thread for a while), never
-// on the short waits of a running pipeline, whose hand-offs it would delay.
+// polls or kWaitNsCap of wall time, whichever comes first.
 FMD_DEV bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint32_t limit) {
-  uint64_t t0 = 0;
-  for (uint32_t i = 0; i < limit; ++i) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1; i < limit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255) == 255) {
-      const uint64_t now = globaltimer_ns();
-      if (t0 == 0)
-        t0 = now;
-      else if (now - t0 > kWaitNsCap)
-        return false;
-    }
+    if ((i & 63) == 0 && globaltimer_ns() - t0 > kWaitNsCap) return false;
   }
   return false;
 }
