@@ -94,9 +94,14 @@ __global__ void __launch_bounds__(kLhThreads, 1)
                  LinW W, GemvEpi ep, int* __restrict__ status) {
   using C = LhCfg<NR>;
   constexpr int RAW = C::RAW, CONV = C::CONV, ACC = C::ACC;
+  static_assert(ACC == 2 * CONV, "a stage's accumulators must follow its A slot");
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t full[RAW], empty[RAW], conv_full[CONV], conv_empty[CONV], acc_full[ACC],
-      acc_empty[ACC], mma_done;
+  // stage_done[c]: one tcgen05.commit per stage, after its four MMAs; it
+  // tells the epilogue that the stage's two accumulators hold their sums and
+  // the converters that A slot c is free again (accumulators 2c and 2c + 1
+  // belong to the stages that use slot c, because ACC == 2 * CONV)
+  __shared__ __align__(8) uint64_t full[RAW], empty[RAW], conv_full[CONV], stage_done[CONV], acc_empty[ACC],
+      mma_done;
   __shared__ uint32_t tmem_base_s;
   __shared__ float rs_s[NR];
   __shared__ uint32_t xmax_s[NR];  // largest |value| of each staged row (f32 bits)
@@ -127,12 +132,9 @@ __global__ void __launch_bounds__(kLhThreads, 1)
     }
     for (int i = 0; i < CONV; ++i) {
       mbar_init(&conv_full[i], kLhConvWarps);
-      mbar_init(&conv_empty[i], 1);  // tcgen05.commit after the stage's MMAs
+      mbar_init(&stage_done[i], 1);  // tcgen05.commit after the stage's MMAs
     }
-    for (int i = 0; i < ACC; ++i) {
-      mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], kLhEpiWarps / 2);  // the four warps of the block's stage parity
-    }
+    for (int i = 0; i < ACC; ++i) mbar_init(&acc_empty[i], kLhEpiWarps / 2);  // the four warps of the stage parity
     mbar_init(&mma_done, 1);
     abort_s = 0;
     stop_s = 0;
@@ -190,14 +192,16 @@ __global__ void __launch_bounds__(kLhThreads, 1)
             ok = false;
             break;
           }
-          tc_fence_after();
-          const uint32_t at = cv + (uint32_t)c * kLhConv + b * 64, bt = xs + (uint32_t)kb * NR * 128 + b * 64;
-          umma_f16(tmem + (uint32_t)(a * NR), umma_desc_sw128(at), umma_desc_sw128(bt), idesc, false);
-          umma_f16(tmem + (uint32_t)(a * NR), umma_desc_sw128(at + 32), umma_desc_sw128(bt + 32), idesc, true);
-          umma_commit(&acc_full[a]);
         }
         if (!ok) break;
-        umma_commit(&conv_empty[c]);  // the A slot is free once these MMAs have read it
+        tc_fence_after();
+        for (int b = 0; b < 2; ++b) {
+          const uint32_t acc = tmem + (uint32_t)(((2 * g + b) % ACC) * NR);
+          const uint32_t at = cv + (uint32_t)c * kLhConv + b * 64, bt = xs + (uint32_t)kb * NR * 128 + b * 64;
+          umma_f16(acc, umma_desc_sw128(at), umma_desc_sw128(bt), idesc, false);
+          umma_f16(acc, umma_desc_sw128(at + 32), umma_desc_sw128(bt + 32), idesc, true);
+        }
+        umma_commit(&stage_done[c]);  // sums ready and the A slot free once these MMAs complete
       }
       if (!ok) *abort_v = 1;
       umma_commit(&mma_done);  // every MMA issued so far has completed when this fires
@@ -210,7 +214,7 @@ __global__ void __launch_bounds__(kLhThreads, 1)
     bool ok = true;
     for (int g = 0; ok && g < n_stages; ++g) {
       const int s = g % RAW, c = g % CONV;
-      if (g >= CONV && (*abort_v || !mbar_wait_bounded(&conv_empty[c], ((g / CONV) + 1) & 1, kLhWaitLimit))) {
+      if (g >= CONV && (*abort_v || !mbar_wait_bounded(&stage_done[c], ((g / CONV) + 1) & 1, kLhWaitLimit))) {
         ok = false;
         break;
       }
@@ -401,8 +405,7 @@ __global__ void __launch_bounds__(kLhThreads, 1)
         const int a0 = (2 * g) % ACC, a1 = (2 * g + 1) % ACC;
         // the tensor-memory loads are warp-wide: the warp goes on only if
         // the waits passed for all of its lanes
-        const bool got = !*abort_v && mbar_wait_bounded(&acc_full[a0], ((2 * g) / ACC) & 1, kLhWaitLimit) &&
-                         mbar_wait_bounded(&acc_full[a1], ((2 * g + 1) / ACC) & 1, kLhWaitLimit);
+        const bool got = !*abort_v && mbar_wait_bounded(&stage_done[g % CONV], (g / CONV) & 1, kLhWaitLimit);
         if (!__all_sync(0xffffffffu, got)) {
           ok = false;
           *abort_v = 1;
