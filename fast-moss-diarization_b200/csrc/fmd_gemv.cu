@@ -37,6 +37,7 @@
 //                per row.
 #include <cooperative_groups.h>
 #include <algorithm>
+#include <type_traits>
 #include <cstdlib>
 #include <cstring>
 #include <float.h>
@@ -473,10 +474,21 @@ struct RingPos {
 
 // NTL: MMA n-tiles (8 rows each) of a row tile; G: consumer groups. Two
 // groups (17 warps) leave 96 registers per thread, enough for 4 n-tiles.
-template <typename T, bool Q8, int NTL, int G>
+// F16 (Q8_0 weights, bf16 rows): the MMAs take f16 operands. The exact int8
+// -> f16 conversion is 5 instructions per 4 weights against 11 for bf16, and
+// the register dequantisation is what bounds this kernel. Each staged row,
+// already rounded to bf16, is scaled by 2^(14 - e) (e the exponent of its
+// largest |value|) and converted to f16: exact for every value above 2^-17
+// after scaling (bf16 keeps 8 significant bits, f16 11, normal from 2^-14),
+// i.e. all but values 2^-31 below the row's largest, whose products sit
+// under the f32 sum's own rounding. The logits are scaled back by the exact
+// power of two before the rounding to bf16.
+template <typename T, bool Q8, int NTL, int G, bool F16>
 __global__ void __launch_bounds__((G * kHeadWarps + 1) * 32, 1)
     k_lm_head(const T* __restrict__ x, int ldx, const int* __restrict__ row_map, const int* __restrict__ n_rows_ptr,
               LinW W, GemvEpi ep, int xrows, int stages, int* __restrict__ status) {
+  static_assert(!F16 || (Q8 && Act<T>::kIsBf16), "f16 operands serve Q8_0 weights with bf16 rows");
+  using M = typename std::conditional<F16, __half, T>::type;  // MMA operand type
   constexpr int UNIT = Q8 ? kUnitQ8 : kUnitDense;
   constexpr uint32_t kStage = kHeadWarps * UNIT;
   constexpr int FT = kHeadWarps * 16;
@@ -485,6 +497,8 @@ __global__ void __launch_bounds__((G * kHeadWarps + 1) * 32, 1)
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t full[kHeadMaxStages], empty[kHeadMaxStages];
   __shared__ float rs_s[kRows];
+  __shared__ uint32_t xmax_s[F16 ? NTL * 8 : 1];  // F16: largest |value| of each staged row (f32 bits)
+  __shared__ float inv_s[F16 ? NTL * 8 : 1];      // F16: 1 / the row's operand scale
   __shared__ float cand_v[NCW][NTL * 8];
   __shared__ int cand_i[NCW][NTL * 8];
   __shared__ int abort_s;
@@ -566,28 +580,68 @@ __global__ void __launch_bounds__((G * kHeadWarps + 1) * 32, 1)
   cp_async_commit();
   const bool norm = ep.ssq != nullptr;  // else x is already normalised
   if (norm) rows_rsqrt(ep.ssq, ep.ssq_tiles, row_map, row0, rows, K, ep.eps, rs_s, NT);
+  if constexpr (F16)
+    for (int r = threadIdx.x; r < NTL * 8; r += NT) xmax_s[r] = 0u;
   cp_async_wait<0>();
   named_sync(1, NT);
-  if (norm) {
+  if (norm || F16) {
     const T* nw = reinterpret_cast<const T*>(ep.norm_w);
     for (int c = threadIdx.x; c < rows * cpr; c += NT) {
       const int r = c / cpr, ch = c - r * cpr;
       int4* p = reinterpret_cast<int4*>(xs + (size_t)r * xstride + ch * 8);
       int4 v = *p;
-      const int4 wv = *reinterpret_cast<const int4*>(nw + ch * 8);
       uint32_t* u = reinterpret_cast<uint32_t*>(&v);
-      const uint32_t* uw = reinterpret_cast<const uint32_t*>(&wv);
-      const float rsr = rs_s[r];
+      if (norm) {
+        const int4 wv = *reinterpret_cast<const int4*>(nw + ch * 8);
+        const uint32_t* uw = reinterpret_cast<const uint32_t*>(&wv);
+        const float rsr = rs_s[r];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float2 f = Act<T>::unpack2(u[j]);
-        const float2 gw = Act<T>::unpack2(uw[j]);
-        u[j] = Act<T>::pack2(f.x * rsr * gw.x, f.y * rsr * gw.y);
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = Act<T>::unpack2(u[j]);
+          const float2 gw = Act<T>::unpack2(uw[j]);
+          u[j] = Act<T>::pack2(f.x * rsr * gw.x, f.y * rsr * gw.y);
+        }
+        *p = v;
       }
-      *p = v;
+      if constexpr (F16) {
+        float m = 0.f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = Act<T>::unpack2(u[j]);
+          m = fmaxf(m, fmaxf(fabsf(f.x), fabsf(f.y)));
+        }
+        if (m > 0.f) atomicMax(&xmax_s[r], __float_as_uint(m));
+      }
     }
   }
   named_sync(1, NT);
+  if constexpr (F16) {
+    // the operand scale 2^sh of each row and its exact inverse; the padding
+    // rows (all zero) keep 1
+    for (int r = threadIdx.x; r < NTL * 8; r += NT) {
+      const uint32_t mb = xmax_s[r];
+      const int e = (int)((mb >> 23) & 0xffu) - 127;
+      const int sh = mb == 0u || e > 127 ? 0 : max(-126, min(126, 14 - e));
+      inv_s[r] = __uint_as_float((uint32_t)(127 - sh) << 23);
+      rs_s[r] = __uint_as_float((uint32_t)(127 + sh) << 23);  // the norm's row scales are dead: reuse
+    }
+    named_sync(1, NT);
+    for (int c = threadIdx.x; c < rows * cpr; c += NT) {
+      const int r = c / cpr, ch = c - r * cpr;
+      int4* p = reinterpret_cast<int4*>(xs + (size_t)r * xstride + ch * 8);
+      int4 v = *p;
+      uint32_t* u = reinterpret_cast<uint32_t*>(&v);
+      const float sc = rs_s[r];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = Act<T>::unpack2(u[j]);
+        u[j] = Act<__half>::pack2(f.x * sc, f.y * sc);
+      }
+      *p = v;
+    }
+    named_sync(1, NT);
+  }
+  const M* xm = reinterpret_cast<const M*>(xs);
 
   // running best of this thread's rows (nt * 8 + 2t + {0, 1}) over its features
   float bv[NTL][2];
@@ -636,13 +690,13 @@ __global__ void __launch_bounds__((G * kHeadWarps + 1) * 32, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[st]);  // this warp's fragments are in registers
       uint32_t af[4][4];
-      gemv_afrag<T, Q8>(w, af);
+      gemv_afrag<M, Q8>(w, af);
 #pragma unroll
       for (int nt = 0; nt < NTL; ++nt) {
         if (nt < n_nt) {
           uint32_t xw[8];
-          gemv_xfrag<T, Q8>(xs + (size_t)(nt * 8 + g) * xstride + kb * 64, t, xw);
-          gemv_kblock<T, Q8>(acc[nt], af, xw, w);
+          gemv_xfrag<M, Q8>(xm + (size_t)(nt * 8 + g) * xstride + kb * 64, t, xw);
+          gemv_kblock<M, Q8>(acc[nt], af, xw, w);
         }
       }
     }
@@ -656,7 +710,8 @@ __global__ void __launch_bounds__((G * kHeadWarps + 1) * 32, 1)
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           const int lr = nt * 8 + 2 * t + h;
-          const float va = rnd<T>(acc[nt][h]), vb = rnd<T>(acc[nt][2 + h]);
+          const float is = F16 ? inv_s[lr] : 1.f;
+          const float va = rnd<T>(acc[nt][h] * is), vb = rnd<T>(acc[nt][2 + h] * is);
           if (ep.logits && lr < rows) {
             float* lg = ep.logits + (size_t)(row0 + lr) * W.N;
             lg[f0] = va;
@@ -812,7 +867,7 @@ void launch_gemv_t(const LinW& W, int S, const void* x, int ldx, const int* row_
 }
 
 
-template <typename T, bool Q8, int NTL, int G>
+template <typename T, bool Q8, int NTL, int G, bool F16>
 int launch_lm_head_t(const LinW& W, const void* x, int ldx, const int* row_map, const int* n_rows_ptr,
                      int max_rows, const GemvEpi& ep, int* status, cudaStream_t s) {
   static int n_sm = 0;
@@ -843,7 +898,7 @@ int launch_lm_head_t(const LinW& W, const void* x, int ldx, const int* row_map, 
   cfg.stream = s;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaLaunchKernelEx(&cfg, k_lm_head<T, Q8, NTL, G>, (const T*)x, ldx, row_map, n_rows_ptr, W, ep, xrows, stages,
+  cudaLaunchKernelEx(&cfg, k_lm_head<T, Q8, NTL, G, F16>, (const T*)x, ldx, row_map, n_rows_ptr, W, ep, xrows, stages,
                      status);
   return grid;
 }
@@ -858,9 +913,17 @@ cudaError_t init_gemv_t() {
            cudaFuncSetAttribute(k_gemv<T, Q8, 4, kGemvResid, false, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim),
            cudaFuncSetAttribute(k_gemv<T, Q8, 4, kGemvSwiglu, true, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim),
            cudaFuncSetAttribute(k_gemv<T, Q8, 8, kGemvLogits, true, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim),
-           cudaFuncSetAttribute(k_lm_head<T, Q8, 4, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kHeadSmemBudget),
-           cudaFuncSetAttribute(k_lm_head<T, Q8, 8, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kHeadSmemBudget)})
+           cudaFuncSetAttribute(k_lm_head<T, Q8, 4, 2, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                kHeadSmemBudget),
+           cudaFuncSetAttribute(k_lm_head<T, Q8, 8, 1, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                kHeadSmemBudget)})
     if (r != cudaSuccess) e = r;
+  if constexpr (Q8 && Act<T>::kIsBf16)
+    for (cudaError_t r : {cudaFuncSetAttribute(k_lm_head<T, Q8, 4, 2, true>,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize, kHeadSmemBudget),
+                          cudaFuncSetAttribute(k_lm_head<T, Q8, 8, 1, true>,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize, kHeadSmemBudget)})
+      if (r != cudaSuccess) e = r;
   return e;
 }
 
@@ -957,7 +1020,8 @@ bool launch_gemv(ActType at, int epi, bool norm, const LinW& W, const void* x, i
 }
 
 int launch_lm_head(ActType at, const LinW& W, const void* x, int ldx, const int* row_map, const int* n_rows_ptr,
-                   int max_rows, const GemvEpi& ep, int* status, cudaStream_t s, bool tc, bool* used_tc) {
+                   int max_rows, const GemvEpi& ep, int* status, cudaStream_t s, bool tc, bool f16ops,
+                   bool* used_tc) {
   if (used_tc) *used_tc = false;
   if (W.pk == nullptr || W.N % (kHeadWarps * 16) != 0 || W.K % 64 != 0) return 0;
   int parts = tc ? launch_lm_head_tc(at, W, x, ldx, row_map, n_rows_ptr, max_rows, ep, status, s) : 0;
@@ -966,13 +1030,16 @@ int launch_lm_head(ActType at, const LinW& W, const void* x, int ldx, const int*
     return parts;
   }
   // row tiles of 32 rows (4 MMA n-tiles) up to a batch of 32, else 64
-#define FMD_HEAD(T, Q8)                                                                                        \
-  (max_rows <= 32 ? launch_lm_head_t<T, Q8, 4, 2>(W, x, ldx, row_map, n_rows_ptr, max_rows, ep, status, s)    \
-                  : launch_lm_head_t<T, Q8, 8, 1>(W, x, ldx, row_map, n_rows_ptr, max_rows, ep, status, s))
+  // (Q8_0 with bf16 rows: f16 operands unless f16ops is off)
+#define FMD_HEAD(T, Q8, F16)                                                                                      \
+  (max_rows <= 32 ? launch_lm_head_t<T, Q8, 4, 2, F16>(W, x, ldx, row_map, n_rows_ptr, max_rows, ep, status, s) \
+                  : launch_lm_head_t<T, Q8, 8, 1, F16>(W, x, ldx, row_map, n_rows_ptr, max_rows, ep, status, s))
   if (at == kBF16)
-    parts = W.q8 ? FMD_HEAD(__nv_bfloat16, true) : FMD_HEAD(__nv_bfloat16, false);
+    parts = !W.q8   ? FMD_HEAD(__nv_bfloat16, false, false)
+            : f16ops ? FMD_HEAD(__nv_bfloat16, true, true)
+                     : FMD_HEAD(__nv_bfloat16, true, false);
   else
-    parts = W.q8 ? FMD_HEAD(__half, true) : FMD_HEAD(__half, false);
+    parts = W.q8 ? FMD_HEAD(__half, true, false) : FMD_HEAD(__half, false, false);
 #undef FMD_HEAD
   if (parts > 0) return parts;
   // activation tile too large for the resident kernel: the cluster GEMV,

@@ -286,13 +286,13 @@ void gemv_pack(int epi, int N, int K, bool q8, const int8_t* qs, const uint16_t*
 bool launch_gemv(ActType at, int epi, bool norm, const LinW& W, const void* x, int ldx, const int* row_map,
                  const int* n_rows_ptr, int max_rows, const GemvEpi& ep, int* status, cudaStream_t s);
 // lm_head of the decode step: Q8_0 weights and up to 64 rows on the tensor
-// cores (k_lm_head_tc, when `tc`), else the persistent mma.sync kernel, else
-// the cluster GEMV when the activation tile does not fit. Returns the
-// candidates per row it writes into ep.best_val / best_idx (0: nothing
-// launched).
+// cores (k_lm_head_tc, when `tc`), else the persistent mma.sync kernel (f16
+// operands for Q8_0 with bf16 rows when `f16ops`), else the cluster GEMV when
+// the activation tile does not fit. Returns the candidates per row it writes
+// into ep.best_val / best_idx (0: nothing launched).
 int launch_lm_head(ActType at, const LinW& W, const void* x, int ldx, const int* row_map, const int* n_rows_ptr,
                    int max_rows, const GemvEpi& ep, int* status, cudaStream_t s, bool tc = true,
-                   bool* used_tc = nullptr);
+                   bool f16ops = true, bool* used_tc = nullptr);
 // fmd_lm_head_tc.cu: the tensor-core lm_head (0 when it cannot serve the shapes).
 int launch_lm_head_tc(ActType at, const LinW& W, const void* x, int ldx, const int* row_map, const int* n_rows_ptr,
                       int max_rows, const GemvEpi& ep, int* status, cudaStream_t s);

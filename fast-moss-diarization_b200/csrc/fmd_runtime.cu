@@ -138,6 +138,7 @@ struct fmd_handle {
   int n_sm = 0;
   bool proj_allowed = true;  // mixed steps on k_proj_tc (fused epilogues); FMD_PROJ_TC=0 selects k_gemm_tc
   bool lm_tc_allowed = false;  // Q8_0 lm_head on the tensor cores (FMD_LM_HEAD_TC=1); else the mma.sync kernel
+  bool lm_f16_allowed = true;  // mma.sync lm_head: f16 operands for Q8_0 with bf16 rows (FMD_LM_HEAD_F16=0: bf16)
   bool lm_tc_used = false;     // the last lm_head launch (or graph capture) used the tensor-core kernel
   bool pf_pp_allowed = true;  // persistent two-tile prefill attention; FMD_PREFILL_PP=0 selects one CTA per block
   bool chain_allowed = false;
@@ -666,7 +667,7 @@ void run_forward_decode(fmd_handle* h, float* logits_dev, const void* arena) {
   head.best_idx = h->best_idx;
   if (h->record_attn_events) cudaEventRecordWithFlags(h->attn_events[2], s, cudaEventRecordExternal);
   const int parts = launch_lm_head(h->at, h->lm_head, h->x, H, h->plan.sample_row, nsamp, h->max_slots, head,
-                                   h->d_status, s, h->lm_tc_allowed, &h->lm_tc_used);
+                                   h->d_status, s, h->lm_tc_allowed, h->lm_f16_allowed, &h->lm_tc_used);
   if (h->record_attn_events) cudaEventRecordWithFlags(h->attn_events[3], s, cudaEventRecordExternal);
   if (parts == 0) h->launch_refused = true;
   trace(h, "lm_head", -1);
@@ -778,7 +779,7 @@ void run_forward(fmd_handle* h, float* logits_dev, const void* arena, bool decod
   head.best_idx = h->best_idx;
   if (h->record_attn_events) cudaEventRecordWithFlags(h->attn_events[2], s, cudaEventRecordExternal);
   const int parts = launch_lm_head(h->at, h->lm_head, h->xn, H, h->plan.sample_row, nsamp, h->max_slots, head,
-                                   h->d_status, s, h->lm_tc_allowed, &h->lm_tc_used);
+                                   h->d_status, s, h->lm_tc_allowed, h->lm_f16_allowed, &h->lm_tc_used);
   if (h->record_attn_events) cudaEventRecordWithFlags(h->attn_events[3], s, cudaEventRecordExternal);
   trace(h, "lm_head", -1);
   if (parts > 0) {
@@ -1002,6 +1003,8 @@ int fmd_create(const fmd_config* cfg, int32_t precision, int32_t device, fmd_han
     h->proj_allowed = !(p != nullptr && p[0] == '0');
     const char* lt = std::getenv("FMD_LM_HEAD_TC");
     h->lm_tc_allowed = lt != nullptr && lt[0] == '1';
+    const char* lf = std::getenv("FMD_LM_HEAD_F16");
+    h->lm_f16_allowed = !(lf != nullptr && lf[0] == '0');
     const char* pp = std::getenv("FMD_PREFILL_PP");
     h->pf_pp_allowed = !(pp != nullptr && pp[0] == '0');
     const char* sp = std::getenv("FMD_DECODE_SPLIT");

@@ -347,6 +347,44 @@ def test_lm_head_on_the_tensor_cores(prec, n, monkeypatch):
     assert worst[0] <= 2.0 ** (-7 if prec == "int8_bf16" else -10), worst
 
 
+@pytest.mark.parametrize("n", [5, 32, 48])
+def test_lm_head_f16_operands_are_bit_identical(n, monkeypatch):
+    """The mma.sync lm_head for Q8_0 weights and bf16 rows takes f16 MMA
+    operands (fmd_gemv.cu k_lm_head, F16): each staged row, rounded to bf16,
+    is scaled by a power of two into f16 and the logits are scaled back. The
+    scaling is exact and the products are exact either way, so the logits
+    and picks equal those of the bf16-operand kernel (FMD_LM_HEAD_F16=0)
+    bit for bit, and match the oracle; 5 and 32 rows (one 32-row tile, two
+    consumer groups) and 48 rows (64-row tiles)."""
+    cfg = mid_config(num_hidden_layers=1)
+    w = syn.make_weights(cfg, seed=37)
+    m = oracle_model(cfg, w, "int8_bf16")
+    rng = np.random.default_rng(100 + n)
+    lens = rng.integers(1, 30, n)
+    prompts = [rng.standard_normal((int(k), cfg.hidden_size), dtype=np.float32) for k in lens]
+    toks = rng.integers(0, cfg.vocab_size, n)
+    got = {}
+    monkeypatch.setenv("FMD_LM_HEAD_TC", "0")
+    for f16 in ("1", "0"):
+        monkeypatch.setenv("FMD_LM_HEAD_F16", f16)
+        with make_decoder(cfg, w, "int8_bf16", slots=n, tokens=n * 64, rows=1024) as dec:
+            for s in range(n):
+                dec.open_slot(s, int(lens[s]) + 2)
+            dec.prefill(list(range(n)), prompts, want_logits=False)
+            got[f16] = dec.decode_step(list(range(n)), toks)
+            assert not dec.debug_paths()["lm_head_tc"]
+    (lg_a, ids_a), (lg_b, ids_b) = got["1"], got["0"]
+    diff = int(np.count_nonzero(lg_a != lg_b))
+    assert diff == 0, f"{diff} logits differ between f16 and bf16 operands"
+    assert np.array_equal(ids_a, ids_b)
+    for s in range(n):
+        cs = m.new_caches(1, int(lens[s]) + 2)
+        m.prefill(prompts[s][None], cs)
+        want = m.decode_step(int(toks[s]), cs).numpy()
+        assert rel_err(lg_a[s], want) < LOGIT_RTOL, s
+        check_pick(int(ids_a[s]), lg_a[s], want)
+
+
 @pytest.mark.parametrize("prec", ["bf16", "int8"])
 def test_prefill_attention_persistent_two_tile_is_bit_identical(prec, monkeypatch):
     """Prefill attention on persistent CTAs with two query tiles each
