@@ -15,7 +15,7 @@
 //  * warp 0 (one lane): TMA loads of the query tile (four 64x64 boxes,
 //    128-byte swizzle) and of each key page's K and V tiles (2 x 16 KB) into a
 //    3-stage full/empty mbarrier ring;
-//  * warp 1 (one lane): tcgen05.mma, f32 accumulators in tensor memory:
+//  * warp 1 (the whole warp, one elected lane issuing): tcgen05.mma, f32 accumulators in tensor memory:
 //    S_j = Q K_j^T (M 128, N 64 keys, K 128 dims; S double-buffered), then
 //    O += P_j V_j (M 128, N 128 dims, K 64 keys; V read MN-major straight from
 //    the page tile; O stays in tensor memory for the whole block);
@@ -204,54 +204,62 @@ __global__ void __launch_bounds__(192, 1)
         mbar_wait_bounded(&kv_full[j % kPfStages], (j / kPfStages) & 1, kPfWaitLimit);
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
-    if (lane == 0) {
+    // ---------------- MMA issuer: the whole warp runs the loop, the elected lane issues ----------------
+    {
       constexpr bool kBf = Act<T>::kIsBf16;
       constexpr uint32_t idesc_s = umma_idesc_f16(kBf, 128, 64);
       constexpr uint32_t idesc_o = umma_idesc_f16(kBf, 128, 128) | (1u << 16);  // B (V) MN-major
       const uint32_t o_tmem = tmem + 128;
       auto pv = [&](int i) -> bool {
         const int pb = i & 1;
-        if (*abort_v || !mbar_wait_bounded(&p_full[pb], (i >> 1) & 1, kPfWaitLimit)) return false;
+        if (*abort_v || !mbar_wait_warp(&p_full[pb], (i >> 1) & 1, kPfWaitLimit)) return false;
         tc_fence_after();
         const uint32_t v = kv_s + (i % kPfStages) * kPfKvBytes + 2 * kPfBox;
         const uint32_t pa = p_s + pb * kPfPBytes;
+        if (elect_one()) {
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          umma_f16(o_tmem, umma_desc_sw128(pa + kk * 32), umma_desc_sw128_mn(v + kk * 2048, kPfBox), idesc_o,
-                   (i | kk) != 0);
-        umma_commit(&o_full);
-        umma_commit(&p_empty[pb]);
-        umma_commit(&kv_empty[i % kPfStages]);
+          for (int kk = 0; kk < 4; ++kk)
+            umma_f16(o_tmem, umma_desc_sw128(pa + kk * 32), umma_desc_sw128_mn(v + kk * 2048, kPfBox), idesc_o,
+                     (i | kk) != 0);
+          umma_commit(&o_full);
+          umma_commit(&p_empty[pb]);
+          umma_commit(&kv_empty[i % kPfStages]);
+        }
+        __syncwarp();
         return true;
       };
-      bool ok = !*abort_v && mbar_wait_bounded(&q_full, 0, kPfWaitLimit);
+      bool ok = !*abort_v && mbar_wait_warp(&q_full, 0, kPfWaitLimit);
       for (int j = 0; ok && j < T_tiles; ++j) {
         const int st = j % kPfStages, sb = j & 1;
-        if (*abort_v || !mbar_wait_bounded(&kv_full[st], (j / kPfStages) & 1, kPfWaitLimit) ||
-            (j >= 2 && !mbar_wait_bounded(&s_empty[sb], ((j >> 1) - 1) & 1, kPfWaitLimit))) {
+        if (*abort_v || !mbar_wait_warp(&kv_full[st], (j / kPfStages) & 1, kPfWaitLimit) ||
+            (j >= 2 && !mbar_wait_warp(&s_empty[sb], ((j >> 1) - 1) & 1, kPfWaitLimit))) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t k = kv_s + st * kPfKvBytes;
+        if (elect_one()) {
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t a = q_s + (kk < 4 ? kk * 32 : 2 * kPfBox + (kk - 4) * 32);
-          const uint32_t bk = k + (kk < 4 ? kk * 32 : kPfBox + (kk - 4) * 32);
-          umma_f16(tmem + sb * 64, umma_desc_sw128(a), umma_desc_sw128(bk), idesc_s, kk != 0);
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint32_t a = q_s + (kk < 4 ? kk * 32 : 2 * kPfBox + (kk - 4) * 32);
+            const uint32_t bk = k + (kk < 4 ? kk * 32 : kPfBox + (kk - 4) * 32);
+            umma_f16(tmem + sb * 64, umma_desc_sw128(a), umma_desc_sw128(bk), idesc_s, kk != 0);
+          }
+          umma_commit(&s_full[sb]);
         }
-        umma_commit(&s_full[sb]);
+        __syncwarp();
         if (j >= 1 && !pv(j - 1)) {
           ok = false;
           break;
         }
       }
       if (ok) ok = pv(T_tiles - 1);
-      if (ok) umma_commit(&o_final);  // a phase of its own: the last o_full phase could alias
+      if (ok && elect_one()) umma_commit(&o_final);  // a phase of its own: the last o_full phase could alias
+      __syncwarp();
       if (!ok) *abort_v = 1;
-      umma_commit(&mma_done);  // every MMA issued so far has completed when this fires
-      mbar_wait_bounded(&mma_done, 0, kPfWaitLimit);
+      if (elect_one()) umma_commit(&mma_done);  // every MMA issued so far has completed when this fires
+      __syncwarp();
+      mbar_wait_warp(&mma_done, 0, kPfWaitLimit);
     }
   } else {
     // ---------------- softmax + output: one thread per tile row ----------------
@@ -569,8 +577,8 @@ __global__ void __launch_bounds__(kPpThreads, 1)
         mbar_wait_bounded(&kv_full[j % kPfStages], (j / kPfStages) & 1, kPfWaitLimit);
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
-    if (lane == 0) {
+    // ---------------- MMA issuer: the whole warp runs the loop, the elected lane issues ----------------
+    {
       constexpr bool kBf = Act<T>::kIsBf16;
       constexpr uint32_t idesc_s = umma_idesc_f16(kBf, 128, 64);
       constexpr uint32_t idesc_o = umma_idesc_f16(kBf, 128, 128) | (1u << 16);  // B (V) MN-major
@@ -580,18 +588,21 @@ __global__ void __launch_bounds__(kPpThreads, 1)
       // O_x += P_x V for key tile i of the item (first of the item: O_x = P_x V)
       auto pv = [&](int x, int i, int st) -> bool {
         if (i == 0 && wn[x] >= 1 &&
-            (*abort_v || !mbar_wait_bounded(&o_empty[x], (wn[x] - 1) & 1, kPfWaitLimit)))
+            (*abort_v || !mbar_wait_warp(&o_empty[x], (wn[x] - 1) & 1, kPfWaitLimit)))
           return false;
-        if (*abort_v || !mbar_wait_bounded(&p_full[x], pn[x] & 1, kPfWaitLimit)) return false;
+        if (*abort_v || !mbar_wait_warp(&p_full[x], pn[x] & 1, kPfWaitLimit)) return false;
         tc_fence_after();
         const uint32_t v = kv_s + st * kPfKvBytes + 2 * kPfBox;
         const uint32_t pa = p_s + x * kPfPBytes;
         const uint32_t o_tmem = tmem + x * 256 + 128;
+        if (elect_one()) {
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          umma_f16(o_tmem, umma_desc_sw128(pa + kk * 32), umma_desc_sw128_mn(v + kk * 2048, kPfBox), idesc_o,
-                   (i | kk) != 0);
-        umma_commit(&pv_done[x]);  // P_x is free and O_x holds this PV when it fires
+          for (int kk = 0; kk < 4; ++kk)
+            umma_f16(o_tmem, umma_desc_sw128(pa + kk * 32), umma_desc_sw128_mn(v + kk * 2048, kPfBox), idesc_o,
+                     (i | kk) != 0);
+          umma_commit(&pv_done[x]);  // P_x is free and O_x holds this PV when it fires
+        }
+        __syncwarp();
         ++pn[x];
         return true;
       };
@@ -599,7 +610,7 @@ __global__ void __launch_bounds__(kPpThreads, 1)
       for (int r = 0; ok && work(r, w); ++r, ++k) {
         const int Tx[2] = {tiles_of(w.a), w.b >= 0 ? tiles_of(w.b) : 0};
         const int T = w.b >= 0 ? Tx[1] : Tx[0];
-        if (*abort_v || !mbar_wait_bounded(&q_full, k & 1, kPfWaitLimit)) {
+        if (*abort_v || !mbar_wait_warp(&q_full, k & 1, kPfWaitLimit)) {
           ok = false;
           break;
         }
@@ -607,7 +618,7 @@ __global__ void __launch_bounds__(kPpThreads, 1)
         for (int j = 0; ok && j <= T; ++j) {
           if (j < T) {
             const int st = (g0 + j) % kPfStages;
-            if (*abort_v || !mbar_wait_bounded(&kv_full[st], ((g0 + j) / kPfStages) & 1, kPfWaitLimit)) {
+            if (*abort_v || !mbar_wait_warp(&kv_full[st], ((g0 + j) / kPfStages) & 1, kPfWaitLimit)) {
               ok = false;
               break;
             }
@@ -615,43 +626,50 @@ __global__ void __launch_bounds__(kPpThreads, 1)
             for (int x = 0; x < 2; ++x) {
               if (j >= Tx[x]) continue;
               const int n = sn[x], sb = n & 1;
-              if (n >= 2 && (*abort_v || !mbar_wait_bounded(&s_empty[x][sb], ((n >> 1) + 1) & 1, kPfWaitLimit))) {
+              if (n >= 2 && (*abort_v || !mbar_wait_warp(&s_empty[x][sb], ((n >> 1) + 1) & 1, kPfWaitLimit))) {
                 ok = false;
                 break;
               }
               tc_fence_after();
               const uint32_t qa = q_s + x * kPfQBytes;
+              if (elect_one()) {
 #pragma unroll
-              for (int kk = 0; kk < 8; ++kk) {
-                const uint32_t a = qa + (kk < 4 ? kk * 32 : 2 * kPfBox + (kk - 4) * 32);
-                const uint32_t bk = kt + (kk < 4 ? kk * 32 : kPfBox + (kk - 4) * 32);
-                umma_f16(tmem + x * 256 + sb * 64, umma_desc_sw128(a), umma_desc_sw128(bk), idesc_s, kk != 0);
+                for (int kk = 0; kk < 8; ++kk) {
+                  const uint32_t a = qa + (kk < 4 ? kk * 32 : 2 * kPfBox + (kk - 4) * 32);
+                  const uint32_t bk = kt + (kk < 4 ? kk * 32 : kPfBox + (kk - 4) * 32);
+                  umma_f16(tmem + x * 256 + sb * 64, umma_desc_sw128(a), umma_desc_sw128(bk), idesc_s, kk != 0);
+                }
+                umma_commit(&s_full[x][sb]);
               }
-              umma_commit(&s_full[x][sb]);
+              __syncwarp();
               ++sn[x];
             }
             if (!ok) break;
-            if (j == T - 1) umma_commit(&q_empty);  // the item's last score MMAs have read Q
+            if (j == T - 1 && elect_one()) umma_commit(&q_empty);  // the item's last score MMAs have read Q
+            __syncwarp();
           }
           if (j >= 1) {
             const int i = j - 1, st = (g0 + i) % kPfStages;
             for (int x = 0; x < 2 && ok; ++x)
               if (i < Tx[x]) ok = pv(x, i, st);
             if (!ok) break;
-            umma_commit(&kv_empty[st]);  // the page tile is free once its MMAs have read it
+            if (elect_one()) umma_commit(&kv_empty[st]);  // the page tile is free once its MMAs have read it
+            __syncwarp();
           }
         }
         if (!ok) break;
         g = g0 + T;
         for (int x = 0; x < 2; ++x)
           if (Tx[x] > 0) {
-            umma_commit(&o_final[x]);  // the item's O_x is complete when this fires
+            if (elect_one()) umma_commit(&o_final[x]);  // the item's O_x is complete when this fires
+            __syncwarp();
             ++wn[x];
           }
       }
       if (!ok) *abort_v = 1;
-      umma_commit(&mma_done);  // every MMA issued so far has completed when this fires
-      mbar_wait_bounded(&mma_done, 0, kPfWaitLimit);
+      if (elect_one()) umma_commit(&mma_done);  // every MMA issued so far has completed when this fires
+      __syncwarp();
+      mbar_wait_warp(&mma_done, 0, kPfWaitLimit);
     }
   } else {
     // ---------------- softmax + output of tile x: one thread per tile row ----------------

@@ -254,6 +254,21 @@ FMD_DEV void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"((uint32_t)accumulate)
       : "memory");
 }
+// True in exactly one lane of the calling (converged) warp. The MMA-issuing
+// warps run their whole issue loop as a warp (waits, descriptors, branches
+// uniform) and let the elected lane issue tcgen05.mma and tcgen05.commit:
+// measured on B200, an M 128 x K 16 MMA then takes 58 cycles (N 32, 64) to
+// 128 cycles (N 256, the tensor peak), against ~300 cycles for any N when
+// one thread of a diverged warp issues it.
+FMD_DEV bool elect_one() {
+  uint32_t pred;
+  asm volatile("{\n .reg .pred e;\n elect.sync _|e, 0xffffffff;\n selp.u32 %0, 1, 0, e;\n}\n" : "=r"(pred));
+  return pred != 0;
+}
+// Bounded wait of a whole warp, with one outcome for all its lanes.
+FMD_DEV bool mbar_wait_warp(uint64_t* bar, uint32_t parity, uint32_t limit) {
+  return __all_sync(0xffffffffu, mbar_wait_bounded(bar, parity, limit));
+}
 // Arrive once on `bar` when every MMA this thread issued so far has completed.
 FMD_DEV void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(smem_u32(bar))

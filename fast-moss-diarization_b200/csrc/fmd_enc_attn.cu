@@ -14,7 +14,7 @@
 //    past the chunk's last frame is zero-filled rather than reading the next
 //    chunk: the query tile (two boxes) and, per 64-key tile, K and V (8 KB
 //    each, 128-byte swizzle) into a 3-stage full/empty ring;
-//  * warp 1 (one lane): tcgen05.mma with f32 accumulators in tensor memory:
+//  * warp 1 (the whole warp, one elected lane issuing): tcgen05.mma with f32 accumulators in tensor memory:
 //    S_j = Q K_j^T (M 128, N 64 keys, K 64 dims; S double-buffered), then
 //    O += P_j V_j (M 128, N 64 dims, K 64 keys; V read MN-major from its tile);
 //  * warps 2-5 (one thread per query row = tensor-memory lane): online softmax
@@ -154,49 +154,58 @@ __global__ void __launch_bounds__(192, 2)
         mbar_wait_bounded(&kv_full[j % kEaStages], (j / kEaStages) & 1, kEaWaitLimit);
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    {
+      // the whole warp runs the loop; the elected lane issues (elect_one)
       constexpr bool kBf = Act<T>::kIsBf16;
       constexpr uint32_t idesc_s = umma_idesc_f16(kBf, 128, 64);
       constexpr uint32_t idesc_o = umma_idesc_f16(kBf, 128, 64) | (1u << 16);  // B (V) MN-major
       const uint32_t o_tmem = tmem + 128;
       auto pv = [&](int i) -> bool {
         const int pb = i & 1;
-        if (*abort_v || !mbar_wait_bounded(&p_full[pb], (i >> 1) & 1, kEaWaitLimit)) return false;
+        if (*abort_v || !mbar_wait_warp(&p_full[pb], (i >> 1) & 1, kEaWaitLimit)) return false;
         tc_fence_after();
         const uint32_t v = kv_s + (i % kEaStages) * kEaKvBytes + kEaBox;
         const uint32_t pa = p_s + pb * kEaPBytes;
+        if (elect_one()) {
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          umma_f16(o_tmem, umma_desc_sw128(pa + kk * 32), desc_sw128_mn(v + kk * 2048), idesc_o, (i | kk) != 0);
-        umma_commit(&o_full);
-        umma_commit(&p_empty[pb]);
-        umma_commit(&kv_empty[i % kEaStages]);
+          for (int kk = 0; kk < 4; ++kk)
+            umma_f16(o_tmem, umma_desc_sw128(pa + kk * 32), desc_sw128_mn(v + kk * 2048), idesc_o, (i | kk) != 0);
+          umma_commit(&o_full);
+          umma_commit(&p_empty[pb]);
+          umma_commit(&kv_empty[i % kEaStages]);
+        }
+        __syncwarp();
         return true;
       };
-      bool ok = !*abort_v && mbar_wait_bounded(&q_full, 0, kEaWaitLimit);
+      bool ok = !*abort_v && mbar_wait_warp(&q_full, 0, kEaWaitLimit);
       for (int j = 0; ok && j < n_tiles; ++j) {
         const int st = j % kEaStages, sb = j & 1;
-        if (*abort_v || !mbar_wait_bounded(&kv_full[st], (j / kEaStages) & 1, kEaWaitLimit) ||
-            (j >= 2 && !mbar_wait_bounded(&s_empty[sb], ((j >> 1) - 1) & 1, kEaWaitLimit))) {
+        if (*abort_v || !mbar_wait_warp(&kv_full[st], (j / kEaStages) & 1, kEaWaitLimit) ||
+            (j >= 2 && !mbar_wait_warp(&s_empty[sb], ((j >> 1) - 1) & 1, kEaWaitLimit))) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t k = kv_s + st * kEaKvBytes;
+        if (elect_one()) {
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          umma_f16(tmem + sb * 64, umma_desc_sw128(q_s + kk * 32), umma_desc_sw128(k + kk * 32), idesc_s, kk != 0);
-        umma_commit(&s_full[sb]);
+          for (int kk = 0; kk < 4; ++kk)
+            umma_f16(tmem + sb * 64, umma_desc_sw128(q_s + kk * 32), umma_desc_sw128(k + kk * 32), idesc_s, kk != 0);
+          umma_commit(&s_full[sb]);
+        }
+        __syncwarp();
         if (j >= 1 && !pv(j - 1)) {
           ok = false;
           break;
         }
       }
       if (ok) ok = pv(n_tiles - 1);
-      if (ok) umma_commit(&o_final);
+      if (ok && elect_one()) umma_commit(&o_final);
+      __syncwarp();
       if (!ok) *abort_v = 1;
-      umma_commit(&mma_done);
-      mbar_wait_bounded(&mma_done, 0, kEaWaitLimit);
+      if (elect_one()) umma_commit(&mma_done);
+      __syncwarp();
+      mbar_wait_warp(&mma_done, 0, kEaWaitLimit);
     }
   } else {
     const int q4 = warp & 3;

@@ -12,8 +12,8 @@
 //  * warp 0 (one lane) streams A (activations) and W (weights) k-blocks as
 //    16-bit K-major tiles by TMA with the 128-byte swizzle through a
 //    STAGES-deep full/empty mbarrier ring that runs on across tiles;
-//  * warp 1 allocates two BN-column f32 accumulators in tensor memory and one
-//    lane issues tcgen05.mma (M = 128, N = BN, K = 16; four per k-block) into
+//  * warp 1 allocates two BN-column f32 accumulators in tensor memory and,
+//    the whole warp running the loop, its elected lane issues tcgen05.mma (M = 128, N = BN, K = 16; four per k-block) into
 //    accumulator i % 2, releasing each stage with tcgen05.commit and handing
 //    the finished accumulator over with a commit to acc_full;
 //  * warps 2-9 are the epilogue: warp w reads tensor-memory lanes
@@ -190,13 +190,14 @@ __global__ void __launch_bounds__(kEgThreads, 1)
         mbar_wait_bounded(&full[j % STAGES], (j / STAGES) & 1, kEgWaitLimit);
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    {
+      // the whole warp runs the loop; the elected lane issues (elect_one)
       constexpr uint32_t idesc = umma_idesc_f16(Act<T>::kIsBf16, kEgBM, BN);
       int g = 0, i = 0;
       bool ok = true;
       for (int t = blockIdx.x; ok && t < n_tiles; t += gridDim.x, ++i) {
         const int buf = i & 1;
-        if (i >= 2 && (*abort_v || !mbar_wait_bounded(&acc_empty[buf], ((i >> 1) - 1) & 1, kEgWaitLimit))) {
+        if (i >= 2 && (*abort_v || !mbar_wait_warp(&acc_empty[buf], ((i >> 1) - 1) & 1, kEgWaitLimit))) {
           ok = false;
           break;
         }
@@ -204,22 +205,27 @@ __global__ void __launch_bounds__(kEgThreads, 1)
         const uint32_t acc = tmem + (uint32_t)(buf * BN);
         for (int kb = 0; kb < nk; ++kb, ++g) {
           const int st = g % STAGES;
-          if (*abort_v || !mbar_wait_bounded(&full[st], (g / STAGES) & 1, kEgWaitLimit)) {
+          if (*abort_v || !mbar_wait_warp(&full[st], (g / STAGES) & 1, kEgWaitLimit)) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint32_t a = tiles + st * STAGE_BYTES, b = a + A_BYTES;
+          if (elect_one()) {
 #pragma unroll
-          for (int j = 0; j < kEgBK / 16; ++j)
-            umma_f16(acc, umma_desc_sw128(a + j * 32), umma_desc_sw128(b + j * 32), idesc, (kb | j) != 0);
-          umma_commit(&empty[st]);  // the stage is free once these MMAs have read it
+            for (int j = 0; j < kEgBK / 16; ++j)
+              umma_f16(acc, umma_desc_sw128(a + j * 32), umma_desc_sw128(b + j * 32), idesc, (kb | j) != 0);
+            umma_commit(&empty[st]);  // the stage is free once these MMAs have read it
+          }
+          __syncwarp();
         }
-        if (ok) umma_commit(&acc_full[buf]);
+        if (ok && elect_one()) umma_commit(&acc_full[buf]);
+        __syncwarp();
       }
       if (!ok) *abort_v = 1;
-      umma_commit(&mma_done);  // every MMA issued so far has completed when this fires
-      mbar_wait_bounded(&mma_done, 0, kEgWaitLimit);
+      if (elect_one()) umma_commit(&mma_done);  // every MMA issued so far has completed when this fires
+      __syncwarp();
+      mbar_wait_warp(&mma_done, 0, kEgWaitLimit);
     }
   } else {
     const int q = warp & 3, half = (warp - 2) >> 2;

@@ -16,8 +16,8 @@
 //  * a CTA owns a 128-row x BN-feature tile (BN = 128 or 256) and a K range
 //    (split-K over gridDim.z when the feature count alone leaves SMs idle).
 //    Warp 0 (one lane) runs a STAGES-deep full/empty mbarrier ring of TMA
-//    loads, warp 1 allocates BN tensor-memory columns and one lane issues
-//    tcgen05.mma (M = 128, N = BN, K = 16; four per 64-wide k-block) and
+//    loads, warp 1 allocates BN tensor-memory columns and its elected lane
+//    (the whole warp running the loop) issues tcgen05.mma (M = 128, N = BN, K = 16; four per 64-wide k-block) and
 //    releases each stage with tcgen05.commit, warps 2-5 read the f32
 //    accumulator back with tcgen05.ld (warp w owns lanes 32 * (w % 4) ...)
 //    and store the rows;
@@ -121,23 +121,28 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    {
+      // the whole warp runs the loop; the elected lane issues (elect_one)
       constexpr uint32_t idesc = umma_idesc_f16(Act<T>::kIsBf16, kTcBM, BN);
       for (int kb = 0; kb < nk; ++kb) {
         const int st = kb % STAGES;
-        if (!mbar_wait_bounded(&full[st], (kb / STAGES) & 1, kTcWaitLimit) ||
-            (Q8 && !mbar_wait_bounded(&conv[st], (kb / STAGES) & 1, kTcWaitLimit))) {
+        if (!mbar_wait_warp(&full[st], (kb / STAGES) & 1, kTcWaitLimit) ||
+            (Q8 && !mbar_wait_warp(&conv[st], (kb / STAGES) & 1, kTcWaitLimit))) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t a = tiles + st * STAGE_BYTES, b = a + A_BYTES;
+        if (elect_one()) {
 #pragma unroll
-        for (int j = 0; j < kTcBK / 16; ++j)
-          umma_f16(tmem, umma_desc_sw128(a + j * 32), umma_desc_sw128(b + j * 32), idesc, (kb | j) != 0);
-        umma_commit(&empty[st]);  // the stage is free once these MMAs have read it
+          for (int j = 0; j < kTcBK / 16; ++j)
+            umma_f16(tmem, umma_desc_sw128(a + j * 32), umma_desc_sw128(b + j * 32), idesc, (kb | j) != 0);
+          umma_commit(&empty[st]);  // the stage is free once these MMAs have read it
+        }
+        __syncwarp();
       }
-      umma_commit(&done);  // also after an abort: the epilogue must not wait forever
+      if (elect_one()) umma_commit(&done);  // also after an abort: the epilogue must not wait forever
+      __syncwarp();
     }
   } else {
     if constexpr (Q8) {

@@ -25,7 +25,7 @@
 //    the stage's A tile (128 features x 64 k, K-major, 128-byte swizzle) in
 //    a ring of CONV slots, releasing the raw stage as soon as its fragments
 //    are in registers;
-//  * warp 1 (one lane): tcgen05.mma M = 128 (features) x N = NR (rows) x
+//  * warp 1 (the whole warp, one elected lane issuing): tcgen05.mma M = 128 (features) x N = NR (rows) x
 //    K = 16, two per Q8_0 block, each block into the next of 256 / NR
 //    accumulators; tcgen05.commit releases the A slot and signals the block's
 //    accumulator;
@@ -177,35 +177,40 @@ __global__ void __launch_bounds__(kLhThreads, 1)
     named_sync(2, (1 + kLhEpiWarps) * 32);  // with the epilogue: rows staged, columns allocated
     tc_fence_after();
     const uint32_t tmem = tmem_base_s;
-    if (lane == 0) {
+    {
+      // the whole warp runs the loop; the elected lane issues (elect_one)
       constexpr uint32_t idesc = umma_idesc_f16(false, kLhFeat, NR);  // f16 operands
       bool ok = true;
       for (int g = 0; ok && g < n_stages; ++g) {
         const int c = g % CONV, kb = g % nkb;
-        if (*abort_v || !mbar_wait_bounded(&conv_full[c], (g / CONV) & 1, kLhWaitLimit)) {
+        if (*abort_v || !mbar_wait_warp(&conv_full[c], (g / CONV) & 1, kLhWaitLimit)) {
           ok = false;
           break;
         }
         for (int b = 0; b < 2; ++b) {
           const int B = 2 * g + b, a = B % ACC;
-          if (B >= ACC && (*abort_v || !mbar_wait_bounded(&acc_empty[a], ((B / ACC) + 1) & 1, kLhWaitLimit))) {
+          if (B >= ACC && (*abort_v || !mbar_wait_warp(&acc_empty[a], ((B / ACC) + 1) & 1, kLhWaitLimit))) {
             ok = false;
             break;
           }
         }
         if (!ok) break;
         tc_fence_after();
-        for (int b = 0; b < 2; ++b) {
-          const uint32_t acc = tmem + (uint32_t)(((2 * g + b) % ACC) * NR);
-          const uint32_t at = cv + (uint32_t)c * kLhConv + b * 64, bt = xs + (uint32_t)kb * NR * 128 + b * 64;
-          umma_f16(acc, umma_desc_sw128(at), umma_desc_sw128(bt), idesc, false);
-          umma_f16(acc, umma_desc_sw128(at + 32), umma_desc_sw128(bt + 32), idesc, true);
+        if (elect_one()) {
+          for (int b = 0; b < 2; ++b) {
+            const uint32_t acc = tmem + (uint32_t)(((2 * g + b) % ACC) * NR);
+            const uint32_t at = cv + (uint32_t)c * kLhConv + b * 64, bt = xs + (uint32_t)kb * NR * 128 + b * 64;
+            umma_f16(acc, umma_desc_sw128(at), umma_desc_sw128(bt), idesc, false);
+            umma_f16(acc, umma_desc_sw128(at + 32), umma_desc_sw128(bt + 32), idesc, true);
+          }
+          umma_commit(&stage_done[c]);  // sums ready and the A slot free once these MMAs complete
         }
-        umma_commit(&stage_done[c]);  // sums ready and the A slot free once these MMAs complete
+        __syncwarp();
       }
-      if (!ok) *abort_v = 1;
-      umma_commit(&mma_done);  // every MMA issued so far has completed when this fires
-      mbar_wait_bounded(&mma_done, 0, kLhWaitLimit);
+      if (!ok && lane == 0) *abort_v = 1;
+      if (elect_one()) umma_commit(&mma_done);  // every MMA issued so far has completed when this fires
+      __syncwarp();
+      mbar_wait_warp(&mma_done, 0, kLhWaitLimit);
     }
     __syncwarp();
   } else if (warp < 2 + kLhConvWarps) {

@@ -20,8 +20,8 @@
 //    and their f16 block scales become q * d rounded to the activation type,
 //    written in the swizzled layout, then a proxy fence and an arrival on the
 //    stage's `conv` barrier;
-//  * warp 1 allocates two BN-column f32 accumulators in tensor memory and one
-//    lane issues tcgen05.mma (M = 128, N = BN, K = 16; four per k-block) into
+//  * warp 1 allocates two BN-column f32 accumulators in tensor memory and,
+//    the whole warp running the loop, its elected lane issues tcgen05.mma (M = 128, N = BN, K = 16; four per k-block) into
 //    accumulator i % 2, releasing each stage with tcgen05.commit;
 //  * warps 2-9: the epilogue. Warp w owns tensor-memory lanes 32 (w % 4) ...
 //    (32 rows of the tile) and half (w - 2) / 4 of its columns; with BN = 256
@@ -285,13 +285,14 @@ __global__ void __launch_bounds__(proj_threads<Q8>(), 1)
         mbar_wait_bounded(&full[j % STAGES], (j / STAGES) & 1, kPWaitLimit);
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    {
+      // the whole warp runs the loop; the elected lane issues (elect_one)
       constexpr uint32_t idesc = umma_idesc_f16(Act<T>::kIsBf16, kPBM, BN);
       int g = 0, i = 0;
       bool ok = true;
       for (int t = blockIdx.x; ok && t < n_tiles; t += gridDim.x, ++i) {
         const int buf = i & 1;
-        if (i >= 2 && (*abort_v || !mbar_wait_bounded(&acc_empty[buf], ((i >> 1) - 1) & 1, kPWaitLimit))) {
+        if (i >= 2 && (*abort_v || !mbar_wait_warp(&acc_empty[buf], ((i >> 1) - 1) & 1, kPWaitLimit))) {
           ok = false;
           break;
         }
@@ -299,23 +300,28 @@ __global__ void __launch_bounds__(proj_threads<Q8>(), 1)
         const uint32_t acc = tmem + (uint32_t)(buf * BN);
         for (int kb = 0; kb < nk; ++kb, ++g) {
           const int st = g % STAGES;
-          if (*abort_v || !mbar_wait_bounded(&full[st], (g / STAGES) & 1, kPWaitLimit) ||
-              (Q8 && !mbar_wait_bounded(&conv[st], (g / STAGES) & 1, kPWaitLimit))) {
+          if (*abort_v || !mbar_wait_warp(&full[st], (g / STAGES) & 1, kPWaitLimit) ||
+              (Q8 && !mbar_wait_warp(&conv[st], (g / STAGES) & 1, kPWaitLimit))) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint32_t a = tiles + st * STAGE_BYTES, b = a + A_BYTES;
+          if (elect_one()) {
 #pragma unroll
-          for (int j = 0; j < kPBK / 16; ++j)
-            umma_f16(acc, umma_desc_sw128(a + j * 32), umma_desc_sw128(b + j * 32), idesc, (kb | j) != 0);
-          umma_commit(&empty[st]);  // the stage is free once these MMAs have read it
+            for (int j = 0; j < kPBK / 16; ++j)
+              umma_f16(acc, umma_desc_sw128(a + j * 32), umma_desc_sw128(b + j * 32), idesc, (kb | j) != 0);
+            umma_commit(&empty[st]);  // the stage is free once these MMAs have read it
+          }
+          __syncwarp();
         }
-        if (ok) umma_commit(&acc_full[buf]);
+        if (ok && elect_one()) umma_commit(&acc_full[buf]);
+        __syncwarp();
       }
       if (!ok) *abort_v = 1;
-      umma_commit(&mma_done);  // every MMA issued so far has completed when this fires
-      mbar_wait_bounded(&mma_done, 0, kPWaitLimit);
+      if (elect_one()) umma_commit(&mma_done);  // every MMA issued so far has completed when this fires
+      __syncwarp();
+      mbar_wait_warp(&mma_done, 0, kPWaitLimit);
     }
   } else if (warp >= 10) {
     if constexpr (Q8) {
