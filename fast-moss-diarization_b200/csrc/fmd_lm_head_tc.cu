@@ -25,17 +25,19 @@
 //    the stage's A tile (128 features x 64 k, K-major, 128-byte swizzle) in
 //    a ring of CONV slots, releasing the raw stage as soon as its fragments
 //    are in registers;
-//  * warp 1 (the whole warp, one elected lane issuing): tcgen05.mma M = 128 (features) x N = NR (rows) x
-//    K = 16, two per Q8_0 block, each block into the next of 256 / NR
-//    accumulators; tcgen05.commit releases the A slot and signals the block's
-//    accumulator;
+//  * warp 1 (the whole warp, one elected lane issuing): tcgen05.mma M = 128
+//    (features) x N = NR (rows) x K = 16, two per Q8_0 block, each block into
+//    the next of 256 / NR accumulators; one tcgen05.commit per stage signals
+//    the stage's two accumulators to the epilogue, whose release of them
+//    also frees the stage's A slot for the converters;
 //  * warps 6-13 (epilogue): before the loop they stage the rows (final
 //    RMSNorm applied) as the B operand, resident for the whole launch. Warp
 //    w reads tensor-memory lanes 32 (w % 4) .. (the thread's feature) x NR
 //    columns (the rows); warps 6-9 take the even stages of a tile, warps
 //    10-13 the odd ones, so two accumulator reads of a lane quarter are in
 //    flight at once. Per stage a warp loads both blocks' accumulators behind
-//    one wait, frees them and adds d0 x block 0, then d1 x block 1, in f32.
+//    one wait, frees both with one arrival and adds d0 x block 0, then d1 x
+//    block 1, in f32.
 //    After a tile, the even-stage sum plus the odd-stage sum is scaled back,
 //    rounded to the activation type (as the reference's lm_head output is)
 //    and reduced per row to the best (value, lowest index) through shared
@@ -96,11 +98,15 @@ __global__ void __launch_bounds__(kLhThreads, 1)
   constexpr int RAW = C::RAW, CONV = C::CONV, ACC = C::ACC;
   static_assert(ACC == 2 * CONV, "a stage's accumulators must follow its A slot");
   extern __shared__ uint8_t smem_raw[];
-  // stage_done[c]: one tcgen05.commit per stage, after its four MMAs; it
-  // tells the epilogue that the stage's two accumulators hold their sums and
-  // the converters that A slot c is free again (accumulators 2c and 2c + 1
-  // belong to the stages that use slot c, because ACC == 2 * CONV)
-  __shared__ __align__(8) uint64_t full[RAW], empty[RAW], conv_full[CONV], stage_done[CONV], acc_empty[ACC],
+  // stage_done[c]: one tcgen05.commit per stage, after its four MMAs: the
+  // stage's two accumulators hold their sums (accumulators 2c and 2c + 1
+  // belong to the stages that use A slot c, because ACC == 2 * CONV).
+  // acc_empty[c]: the epilogue has read both accumulators of slot c's stage,
+  // so those MMAs are complete: A slot c and its accumulators are free. The
+  // converters wait on it before they refill slot c, so conv_full of a stage
+  // implies everything the MMA warp needs, and that warp waits once per
+  // stage (its barrier round trips, not the MMAs, bound the stage rate).
+  __shared__ __align__(8) uint64_t full[RAW], empty[RAW], conv_full[CONV], stage_done[CONV], acc_empty[CONV],
       mma_done;
   __shared__ uint32_t tmem_base_s;
   __shared__ float rs_s[NR];
@@ -134,7 +140,7 @@ __global__ void __launch_bounds__(kLhThreads, 1)
       mbar_init(&conv_full[i], kLhConvWarps);
       mbar_init(&stage_done[i], 1);  // tcgen05.commit after the stage's MMAs
     }
-    for (int i = 0; i < ACC; ++i) mbar_init(&acc_empty[i], kLhEpiWarps / 2);  // the four warps of the stage parity
+    for (int i = 0; i < CONV; ++i) mbar_init(&acc_empty[i], kLhEpiWarps / 2);  // the four warps of the stage parity
     mbar_init(&mma_done, 1);
     abort_s = 0;
     stop_s = 0;
@@ -183,18 +189,12 @@ __global__ void __launch_bounds__(kLhThreads, 1)
       bool ok = true;
       for (int g = 0; ok && g < n_stages; ++g) {
         const int c = g % CONV, kb = g % nkb;
+        // conv_full of stage g also means stage g - CONV's accumulators
+        // were read (the converters waited on acc_empty for the slot)
         if (*abort_v || !mbar_wait_warp(&conv_full[c], (g / CONV) & 1, kLhWaitLimit)) {
           ok = false;
           break;
         }
-        for (int b = 0; b < 2; ++b) {
-          const int B = 2 * g + b, a = B % ACC;
-          if (B >= ACC && (*abort_v || !mbar_wait_warp(&acc_empty[a], ((B / ACC) + 1) & 1, kLhWaitLimit))) {
-            ok = false;
-            break;
-          }
-        }
-        if (!ok) break;
         tc_fence_after();
         if (elect_one()) {
           for (int b = 0; b < 2; ++b) {
@@ -203,7 +203,7 @@ __global__ void __launch_bounds__(kLhThreads, 1)
             umma_f16(acc, umma_desc_sw128(at), umma_desc_sw128(bt), idesc, false);
             umma_f16(acc, umma_desc_sw128(at + 32), umma_desc_sw128(bt + 32), idesc, true);
           }
-          umma_commit(&stage_done[c]);  // sums ready and the A slot free once these MMAs complete
+          umma_commit(&stage_done[c]);  // the stage's sums are ready once these MMAs complete
         }
         __syncwarp();
       }
@@ -219,7 +219,8 @@ __global__ void __launch_bounds__(kLhThreads, 1)
     bool ok = true;
     for (int g = 0; ok && g < n_stages; ++g) {
       const int s = g % RAW, c = g % CONV;
-      if (g >= CONV && (*abort_v || !mbar_wait_bounded(&stage_done[c], ((g / CONV) + 1) & 1, kLhWaitLimit))) {
+      // slot c and its accumulators are free once stage g - CONV was read out
+      if (g >= CONV && (*abort_v || !mbar_wait_bounded(&acc_empty[c], ((g / CONV) + 1) & 1, kLhWaitLimit))) {
         ok = false;
         break;
       }
@@ -430,10 +431,7 @@ __global__ void __launch_bounds__(kLhThreads, 1)
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&acc_empty[a0]);
-          mbar_arrive(&acc_empty[a1]);
-        }
+        if (lane == 0) mbar_arrive(&acc_empty[g % CONV]);
       }
       // the tile's logits: even-stage sum + odd-stage sum, scaled back and
       // rounded; per row the best (value, lowest index) of the tile
