@@ -20,9 +20,9 @@
 //    of 16 features x 64 k, 8.5 KB, the k_lm_head layout) into a ring of RAW
 //    stages. Weights depend on no earlier kernel, so the ring fills before
 //    the dependency wait;
-//  * warps 2-5 (converters): warp w takes units w and w + 4 of each stage,
-//    turns their int8 values into f16 operands and writes them as 32 rows of
-//    the stage's A tile (128 features x 64 k, K-major, 128-byte swizzle) in
+//  * warps 2 .. 1 + CONVW (converters, 8 for 32 rows, 4 for 64): warp w takes
+//    units w - 2, w - 2 + CONVW, ... of each stage, turns their int8 values
+//    into f16 operands and writes them as 16 rows each of the stage's A tile (128 features x 64 k, K-major, 128-byte swizzle) in
 //    a ring of CONV slots, releasing the raw stage as soon as its fragments
 //    are in registers;
 //  * warp 1 (the whole warp, one elected lane issuing): tcgen05.mma M = 128
@@ -30,11 +30,11 @@
 //    the next of 256 / NR accumulators; one tcgen05.commit per stage signals
 //    the stage's two accumulators to the epilogue, whose release of them
 //    also frees the stage's A slot for the converters;
-//  * warps 6-13 (epilogue): before the loop they stage the rows (final
+//  * the last 8 warps (epilogue): before the loop they stage the rows (final
 //    RMSNorm applied) as the B operand, resident for the whole launch. Warp
 //    w reads tensor-memory lanes 32 (w % 4) .. (the thread's feature) x NR
-//    columns (the rows); warps 6-9 take the even stages of a tile, warps
-//    10-13 the odd ones, so two accumulator reads of a lane quarter are in
+//    columns (the rows); the first four take the even stages of a tile, the
+//    other four the odd ones, so two accumulator reads of a lane quarter are in
 //    flight at once. Per stage a warp loads both blocks' accumulators behind
 //    one wait, frees both with one arrival and adds d0 x block 0, then d1 x
 //    block 1, in f32.
@@ -62,9 +62,7 @@ constexpr int kLhFeat = 128;                       // features of a tile = MMA M
 constexpr int kLhUnits = kLhFeat / 16;             // 16-feature units of a stage
 constexpr uint32_t kLhRaw = kLhUnits * kUnitQ8;    // packed stage: 8704 bytes
 constexpr uint32_t kLhConv = kLhFeat * 128;        // converted A tile: 128 rows x 64 k x 2 bytes
-constexpr int kLhConvWarps = 4;                    // two units of each stage per converter warp
 constexpr int kLhEpiWarps = 8;                     // two per tensor-memory lane quarter: even / odd stages
-constexpr int kLhThreads = (2 + kLhConvWarps + kLhEpiWarps) * 32;  // 448
 constexpr int kLhTmemCols = 256;
 constexpr int kLhLgStride = 132;                   // row stride (floats) of the rounded-logit tile
 constexpr uint32_t kLhWaitLimit = 1u << 24;
@@ -73,11 +71,18 @@ constexpr int kScaleAhead = 8;                     // stages of block scales in 
 // The weight stream needs ~100 KB in flight per SM to run at the HBM rate
 // (bytes in flight = bandwidth x loaded latency), so most of the shared
 // memory goes to packed stages; two converted slots keep the MMAs fed.
+// Converter warps: with 32 rows, eight (one unit of a stage each; the
+// conversion is the longest step of a stage); with 64 rows the epilogue's
+// registers allow only four (two units each).
 template <int NR>
 struct LhCfg {
   static constexpr int RAW = NR == 32 ? 8 : 4;   // packed stages in flight
   static constexpr int CONV = NR == 32 ? 4 : 2;  // converted A slots
   static constexpr int ACC = kLhTmemCols / NR;   // block accumulators
+  static constexpr int CONVW = NR == 32 ? 8 : 4;  // converter warps
+  static constexpr int UPC = kLhUnits / CONVW;    // units of a stage per converter warp
+  static constexpr int THREADS = (2 + CONVW + kLhEpiWarps) * 32;
+  static_assert(kLhUnits % CONVW == 0, "whole units per converter warp");
 };
 
 // Dynamic shared memory: B (rows, K-major, swizzled) | CONV A slots | RAW
@@ -91,7 +96,7 @@ size_t lh_smem(int K) {
 }
 
 template <typename T, int NR>
-__global__ void __launch_bounds__(kLhThreads, 1)
+__global__ void __launch_bounds__(LhCfg<NR>::THREADS, 1)
     k_lm_head_tc(const T* __restrict__ x, int ldx, const int* __restrict__ row_map, const int* __restrict__ n_rows_ptr,
                  LinW W, GemvEpi ep, int* __restrict__ status) {
   using C = LhCfg<NR>;
@@ -111,6 +116,7 @@ __global__ void __launch_bounds__(kLhThreads, 1)
   __shared__ uint32_t tmem_base_s;
   __shared__ float rs_s[NR];
   __shared__ uint32_t xmax_s[NR];  // largest |value| of each staged row (f32 bits)
+  __shared__ int src_s[NR];        // source row of each staged row (-1: padding)
   __shared__ float inv_s[NR];      // 1 / the row's power-of-two operand scale
   __shared__ uint32_t sc_ring[2][kScaleAhead][kLhFeat];
   __shared__ int abort_s, stop_s;
@@ -134,10 +140,10 @@ __global__ void __launch_bounds__(kLhThreads, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < RAW; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], kLhConvWarps);
+      mbar_init(&empty[i], C::CONVW);
     }
     for (int i = 0; i < CONV; ++i) {
-      mbar_init(&conv_full[i], kLhConvWarps);
+      mbar_init(&conv_full[i], C::CONVW);
       mbar_init(&stage_done[i], 1);  // tcgen05.commit after the stage's MMAs
     }
     for (int i = 0; i < CONV; ++i) mbar_init(&acc_empty[i], kLhEpiWarps / 2);  // the four warps of the stage parity
@@ -213,8 +219,8 @@ __global__ void __launch_bounds__(kLhThreads, 1)
       mbar_wait_warp(&mma_done, 0, kLhWaitLimit);
     }
     __syncwarp();
-  } else if (warp < 2 + kLhConvWarps) {
-    // ---- converters: units cw and cw + 4 of every stage -> rows 16u .. 16u + 15 of the A tile
+  } else if (warp < 2 + C::CONVW) {
+    // ---- converters: units cw, cw + CONVW, ... of every stage -> rows 16u .. 16u + 15 of the A tile
     const int cw = warp - 2, gq = lane >> 2, t = lane & 3;
     bool ok = true;
     for (int g = 0; ok && g < n_stages; ++g) {
@@ -228,10 +234,10 @@ __global__ void __launch_bounds__(kLhThreads, 1)
         ok = false;
         break;
       }
-      int4 qv[4];  // (unit cw, cw + 4) x (feature gq, gq + 8)
+      int4 qv[2 * C::UPC];  // (unit cw + CONVW u) x (feature gq, gq + 8)
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const uint8_t* un = rw_p + (size_t)s * kLhRaw + (size_t)(cw + 4 * (k >> 1)) * kUnitQ8;
+      for (int k = 0; k < 2 * C::UPC; ++k) {
+        const uint8_t* un = rw_p + (size_t)s * kLhRaw + (size_t)(cw + C::CONVW * (k >> 1)) * kUnitQ8;
         qv[k] = *reinterpret_cast<const int4*>(un + (k & 1) * 512 + lane * 16);
       }
       __syncwarp();
@@ -241,9 +247,9 @@ __global__ void __launch_bounds__(kLhThreads, 1)
       // block-1 chunk first, so each quarter-warp store covers all 32 banks.
       uint8_t* tile = cv_p + (size_t)c * kLhConv;
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
+      for (int k = 0; k < 2 * C::UPC; ++k) {
         const int4 q = qv[k];
-        const int r = (cw + 4 * (k >> 1)) * 16 + gq + 8 * (k & 1);
+        const int r = (cw + C::CONVW * (k >> 1)) * 16 + gq + 8 * (k & 1);
         uint32_t o[8];
         i8x4_to_act<__half>((uint32_t)q.x, o[0], o[1]);
         i8x4_to_act<__half>((uint32_t)q.y, o[2], o[3]);
@@ -268,15 +274,30 @@ __global__ void __launch_bounds__(kLhThreads, 1)
   } else {
     // ---- epilogue warps: stage the rows, then the accumulators
     constexpr int NE = kLhEpiWarps * 32;
-    const int et = threadIdx.x - (2 + kLhConvWarps) * 32;
+    const int et = threadIdx.x - (2 + C::CONVW) * 32;
     griddep_wait();
     griddep_launch();  // only after the wait: see griddep_launch
     const int rows = min(*n_rows_ptr, NR);
     const bool norm = ep.ssq != nullptr;  // else the rows are already normalised
-    for (int r = et; r < NR; r += NE) xmax_s[r] = 0u;
-    if (norm) {
+    const int cpr = K >> 3;
+    // the source row of each staged row first: the copies below need it
+    for (int r = et; r < NR; r += NE) {
+      xmax_s[r] = 0u;
+      src_s[r] = r < rows ? (row_map ? row_map[r] : r) : -1;
+    }
+    named_sync(1, NE);
+    // every 16-byte chunk of the rows in one round of copies (zeros past the
+    // last row): chunk ch of row r is chunk ch % 8 of k-block ch / 8, stored
+    // swizzled (chunk j of row r at j ^ (r % 8))
+    for (int idx = et; idx < NR * cpr; idx += NE) {
+      const int r = idx / cpr, ch = idx - r * cpr, sr = src_s[r];
+      cp_async16(xs_p + (size_t)(ch >> 3) * NR * 128 + r * 128 + (((ch & 7) ^ (r & 7)) << 4),
+                 sr >= 0 ? (const void*)(x + (size_t)sr * ldx + ch * 8) : (const void*)x, sr >= 0 ? 16 : 0);
+    }
+    cp_async_commit();
+    if (norm) {  // the row norms, while the copies are in flight
       for (int r = et; r < rows; r += NE) {
-        const float* sp = ep.ssq + (size_t)(row_map ? row_map[r] : r) * ep.ssq_tiles;
+        const float* sp = ep.ssq + (size_t)src_s[r] * ep.ssq_tiles;
         float ss = 0.f;
         for (int i0 = 0; i0 < ep.ssq_tiles; i0 += 16) {
           float v[16];
@@ -288,49 +309,37 @@ __global__ void __launch_bounds__(kLhThreads, 1)
         rs_s[r] = rsqrtf(ss / K + ep.eps);
       }
     }
+    cp_async_wait<0>();
     named_sync(1, NE);
-    {
-      // 16-byte chunk ch of row r: k-block ch / 8, chunk ch % 8 of the row,
-      // stored swizzled (chunk j of row r at j ^ (r % 8))
-      const int cpr = K >> 3;
+    if (norm || Act<T>::kIsBf16) {
+      // RMSNorm in place (rounded to the activation type) and, for bf16 rows,
+      // each row's largest |value|
       const T* nw = reinterpret_cast<const T*>(ep.norm_w);
-      for (int i0 = et; i0 < NR * cpr; i0 += 4 * NE) {
-        int4 v[4];
+      for (int idx = et; idx < rows * cpr; idx += NE) {
+        const int r = idx / cpr, ch = idx - r * cpr;
+        int4* pv = reinterpret_cast<int4*>(xs_p + (size_t)(ch >> 3) * NR * 128 + r * 128 + (((ch & 7) ^ (r & 7)) << 4));
+        int4 v = *pv;
+        uint32_t* uv = reinterpret_cast<uint32_t*>(&v);
+        if (norm) {
+          const int4 wv = *reinterpret_cast<const int4*>(nw + ch * 8);
+          const uint32_t* uw = reinterpret_cast<const uint32_t*>(&wv);
+          const float rsr = rs_s[r];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int idx = i0 + j * NE, r = idx / cpr, ch = idx - r * cpr;
-          v[j] = make_int4(0, 0, 0, 0);
-          if (idx < NR * cpr && r < rows)
-            v[j] = *reinterpret_cast<const int4*>(x + (size_t)(row_map ? row_map[r] : r) * ldx + ch * 8);
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = Act<T>::unpack2(uv[e]);
+            const float2 gw = Act<T>::unpack2(uw[e]);
+            uv[e] = Act<T>::pack2(f.x * rsr * gw.x, f.y * rsr * gw.y);
+          }
+          *pv = v;
         }
+        if constexpr (Act<T>::kIsBf16) {
+          float m = 0.f;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int idx = i0 + j * NE, r = idx / cpr, ch = idx - r * cpr;
-          if (idx >= NR * cpr) continue;
-          if (norm && r < rows) {
-            const int4 wv = *reinterpret_cast<const int4*>(nw + ch * 8);
-            uint32_t* uv = reinterpret_cast<uint32_t*>(&v[j]);
-            const uint32_t* uw = reinterpret_cast<const uint32_t*>(&wv);
-            const float rsr = rs_s[r];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float2 f = Act<T>::unpack2(uv[e]);
-              const float2 gw = Act<T>::unpack2(uw[e]);
-              uv[e] = Act<T>::pack2(f.x * rsr * gw.x, f.y * rsr * gw.y);
-            }
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = Act<T>::unpack2(uv[e]);
+            m = fmaxf(m, fmaxf(fabsf(f.x), fabsf(f.y)));
           }
-          if constexpr (Act<T>::kIsBf16) {
-            const uint32_t* uv = reinterpret_cast<const uint32_t*>(&v[j]);
-            float m = 0.f;
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float2 f = Act<T>::unpack2(uv[e]);
-              m = fmaxf(m, fmaxf(fabsf(f.x), fabsf(f.y)));
-            }
-            if (m > 0.f) atomicMax(&xmax_s[r], __float_as_uint(m));
-          }
-          const int kb = ch >> 3, jj = ch & 7;
-          *reinterpret_cast<int4*>(xs_p + (size_t)kb * NR * 128 + r * 128 + ((jj ^ (r & 7)) << 4)) = v[j];
+          if (m > 0.f) atomicMax(&xmax_s[r], __float_as_uint(m));
         }
       }
     }
@@ -524,7 +533,7 @@ int launch_t(const LinW& W, const void* x, int ldx, const int* row_map, const in
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(kLhThreads);
+  cfg.blockDim = dim3(LhCfg<NR>::THREADS);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cfg.attrs = attr;
