@@ -20,9 +20,10 @@
 //    of 16 features x 64 k, 8.5 KB, the k_lm_head layout) into a ring of RAW
 //    stages. Weights depend on no earlier kernel, so the ring fills before
 //    the dependency wait;
-//  * warps 2 .. 1 + CONVW (converters, 8 for 32 rows, 4 for 64): warp w takes
-//    units w - 2, w - 2 + CONVW, ... of each stage, turns their int8 values
-//    into f16 operands and writes them as 16 rows each of the stage's A tile (128 features x 64 k, K-major, 128-byte swizzle) in
+//  * warps 2 .. 1 + CONVW (converters): one group of four warps, or two
+//    taking alternate stages (32 rows); warp w of a group takes units w and
+//    w + 4 of its stages, turns their int8 values into f16 operands and
+//    writes them as 16 rows each of the stage's A tile (128 features x 64 k, K-major, 128-byte swizzle) in
 //    a ring of CONV slots, releasing the raw stage as soon as its fragments
 //    are in registers;
 //  * warp 1 (the whole warp, one elected lane issuing): tcgen05.mma M = 128
@@ -71,18 +72,20 @@ constexpr int kScaleAhead = 8;                     // stages of block scales in 
 // The weight stream needs ~100 KB in flight per SM to run at the HBM rate
 // (bytes in flight = bandwidth x loaded latency), so most of the shared
 // memory goes to packed stages; two converted slots keep the MMAs fed.
-// Converter warps: with 32 rows, eight (one unit of a stage each; the
-// conversion is the longest step of a stage); with 64 rows the epilogue's
-// registers allow only four (two units each).
+// Converters: groups of four warps (two units of a stage each). A stage is
+// a chain of dependent steps for its group (slot and data waits, loads,
+// conversion, stores, proxy fence, arrival), longer than the MMAs of a stage,
+// so with 32 rows two groups take alternate stages; with 64 rows the
+// epilogue's registers leave room for one group.
 template <int NR>
 struct LhCfg {
   static constexpr int RAW = NR == 32 ? 8 : 4;   // packed stages in flight
   static constexpr int CONV = NR == 32 ? 4 : 2;  // converted A slots
   static constexpr int ACC = kLhTmemCols / NR;   // block accumulators
-  static constexpr int CONVW = NR == 32 ? 8 : 4;  // converter warps
-  static constexpr int UPC = kLhUnits / CONVW;    // units of a stage per converter warp
+  static constexpr int NG = NR == 32 ? 2 : 1;    // converter groups (stage g: group g % NG)
+  static constexpr int CONVW = 4 * NG;           // converter warps
   static constexpr int THREADS = (2 + CONVW + kLhEpiWarps) * 32;
-  static_assert(kLhUnits % CONVW == 0, "whole units per converter warp");
+  static_assert(RAW % NG == 0 && CONV % NG == 0, "a group's stages keep to its own ring slots");
 };
 
 // Dynamic shared memory: B (rows, K-major, swizzled) | CONV A slots | RAW
@@ -140,10 +143,10 @@ __global__ void __launch_bounds__(LhCfg<NR>::THREADS, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < RAW; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], C::CONVW);
+      mbar_init(&empty[i], 4);  // the four warps of the stage's converter group
     }
     for (int i = 0; i < CONV; ++i) {
-      mbar_init(&conv_full[i], C::CONVW);
+      mbar_init(&conv_full[i], 4);
       mbar_init(&stage_done[i], 1);  // tcgen05.commit after the stage's MMAs
     }
     for (int i = 0; i < CONV; ++i) mbar_init(&acc_empty[i], kLhEpiWarps / 2);  // the four warps of the stage parity
@@ -220,10 +223,11 @@ __global__ void __launch_bounds__(LhCfg<NR>::THREADS, 1)
     }
     __syncwarp();
   } else if (warp < 2 + C::CONVW) {
-    // ---- converters: units cw, cw + CONVW, ... of every stage -> rows 16u .. 16u + 15 of the A tile
-    const int cw = warp - 2, gq = lane >> 2, t = lane & 3;
+    // ---- converters: group grp takes stages grp, grp + NG, ...; its warp cw
+    // units cw and cw + 4 of each -> rows 16u .. 16u + 15 of the A tile
+    const int grp = (warp - 2) >> 2, cw = (warp - 2) & 3, gq = lane >> 2, t = lane & 3;
     bool ok = true;
-    for (int g = 0; ok && g < n_stages; ++g) {
+    for (int g = grp; ok && g < n_stages; g += C::NG) {
       const int s = g % RAW, c = g % CONV;
       // slot c and its accumulators are free once stage g - CONV was read out
       if (g >= CONV && (*abort_v || !mbar_wait_bounded(&acc_empty[c], ((g / CONV) + 1) & 1, kLhWaitLimit))) {
@@ -234,10 +238,10 @@ __global__ void __launch_bounds__(LhCfg<NR>::THREADS, 1)
         ok = false;
         break;
       }
-      int4 qv[2 * C::UPC];  // (unit cw + CONVW u) x (feature gq, gq + 8)
+      int4 qv[4];  // (unit cw, cw + 4) x (feature gq, gq + 8)
 #pragma unroll
-      for (int k = 0; k < 2 * C::UPC; ++k) {
-        const uint8_t* un = rw_p + (size_t)s * kLhRaw + (size_t)(cw + C::CONVW * (k >> 1)) * kUnitQ8;
+      for (int k = 0; k < 4; ++k) {
+        const uint8_t* un = rw_p + (size_t)s * kLhRaw + (size_t)(cw + 4 * (k >> 1)) * kUnitQ8;
         qv[k] = *reinterpret_cast<const int4*>(un + (k & 1) * 512 + lane * 16);
       }
       __syncwarp();
@@ -247,9 +251,9 @@ __global__ void __launch_bounds__(LhCfg<NR>::THREADS, 1)
       // block-1 chunk first, so each quarter-warp store covers all 32 banks.
       uint8_t* tile = cv_p + (size_t)c * kLhConv;
 #pragma unroll
-      for (int k = 0; k < 2 * C::UPC; ++k) {
+      for (int k = 0; k < 4; ++k) {
         const int4 q = qv[k];
-        const int r = (cw + C::CONVW * (k >> 1)) * 16 + gq + 8 * (k & 1);
+        const int r = (cw + 4 * (k >> 1)) * 16 + gq + 8 * (k & 1);
         uint32_t o[8];
         i8x4_to_act<__half>((uint32_t)q.x, o[0], o[1]);
         i8x4_to_act<__half>((uint32_t)q.y, o[2], o[3]);
