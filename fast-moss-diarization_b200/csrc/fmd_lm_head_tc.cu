@@ -196,23 +196,32 @@ __global__ void __launch_bounds__(LhCfg<NR>::THREADS, 1)
       // the whole warp runs the loop; the elected lane issues (elect_one)
       constexpr uint32_t idesc = umma_idesc_f16(false, kLhFeat, NR);  // f16 operands
       bool ok = true;
-      for (int g = 0; ok && g < n_stages; ++g) {
-        const int c = g % CONV, kb = g % nkb;
+      // two stages per pass (n_stages is even: K % 128 == 0), which halves
+      // this warp's loop and wait instructions per stage; it shares its
+      // scheduler with converter and epilogue warps, so its instruction
+      // count, not the MMAs, sets the pace
+      for (int g = 0; ok && g < n_stages; g += 2) {
         // conv_full of stage g also means stage g - CONV's accumulators
         // were read (the converters waited on acc_empty for the slot)
-        if (*abort_v || !mbar_wait_warp(&conv_full[c], (g / CONV) & 1, kLhWaitLimit)) {
+        if (*abort_v || !mbar_wait_warp(&conv_full[g % CONV], (g / CONV) & 1, kLhWaitLimit) ||
+            !mbar_wait_warp(&conv_full[(g + 1) % CONV], ((g + 1) / CONV) & 1, kLhWaitLimit)) {
           ok = false;
           break;
         }
         tc_fence_after();
         if (elect_one()) {
-          for (int b = 0; b < 2; ++b) {
-            const uint32_t acc = tmem + (uint32_t)(((2 * g + b) % ACC) * NR);
-            const uint32_t at = cv + (uint32_t)c * kLhConv + b * 64, bt = xs + (uint32_t)kb * NR * 128 + b * 64;
-            umma_f16(acc, umma_desc_sw128(at), umma_desc_sw128(bt), idesc, false);
-            umma_f16(acc, umma_desc_sw128(at + 32), umma_desc_sw128(bt + 32), idesc, true);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int gh = g + h, c = gh % CONV, kb = gh % nkb;
+#pragma unroll
+            for (int b = 0; b < 2; ++b) {
+              const uint32_t acc = tmem + (uint32_t)(((2 * gh + b) % ACC) * NR);
+              const uint32_t at = cv + (uint32_t)c * kLhConv + b * 64, bt = xs + (uint32_t)kb * NR * 128 + b * 64;
+              umma_f16(acc, umma_desc_sw128(at), umma_desc_sw128(bt), idesc, false);
+              umma_f16(acc, umma_desc_sw128(at + 32), umma_desc_sw128(bt + 32), idesc, true);
+            }
+            umma_commit(&stage_done[c]);  // the stage's sums are ready once these MMAs complete
           }
-          umma_commit(&stage_done[c]);  // the stage's sums are ready once these MMAs complete
         }
         __syncwarp();
       }
