@@ -23,14 +23,14 @@
 //  * warps 2 .. 1 + CONVW (converters): one group of four warps, or two
 //    taking alternate stages (32 rows); warp w of a group takes units w and
 //    w + 4 of its stages, turns their int8 values into f16 operands and
-//    writes them as 16 rows each of the stage's A tile (128 features x 64 k, K-major, 128-byte swizzle) in
-//    a ring of CONV slots, releasing the raw stage as soon as its fragments
-//    are in registers;
+//    writes them as 16 rows each of the stage's A tile (128 features x 64
+//    k, K-major, 128-byte swizzle) in a ring of CONV slots, releasing the raw
+//    stage as soon as its fragments are in registers;
 //  * warp 1 (the whole warp, one elected lane issuing): tcgen05.mma M = 128
 //    (features) x N = NR (rows) x K = 16, two per Q8_0 block, each block into
-//    the next of 256 / NR accumulators; one tcgen05.commit per stage signals
-//    the stage's two accumulators to the epilogue, whose release of them
-//    also frees the stage's A slot for the converters;
+//    the next of 512 / NR accumulators, two stages per pass; per pass one
+//    tcgen05.commit frees its A slots for the converters and one hands its
+//    accumulators to the epilogue;
 //  * the last 8 warps (epilogue): before the loop they stage the rows (final
 //    RMSNorm applied) as the B operand, resident for the whole launch. Warp
 //    w reads tensor-memory lanes 32 (w % 4) .. (the thread's feature) x NR
@@ -64,7 +64,7 @@ constexpr int kLhUnits = kLhFeat / 16;             // 16-feature units of a stag
 constexpr uint32_t kLhRaw = kLhUnits * kUnitQ8;    // packed stage: 8704 bytes
 constexpr uint32_t kLhConv = kLhFeat * 128;        // converted A tile: 128 rows x 64 k x 2 bytes
 constexpr int kLhEpiWarps = 8;                     // two per tensor-memory lane quarter: even / odd stages
-constexpr int kLhTmemCols = 256;
+constexpr int kLhTmemCols = 512;  // all of tensor memory: accumulator slack over a tile's end
 constexpr int kLhLgStride = 132;                   // row stride (floats) of the rounded-logit tile
 constexpr uint32_t kLhWaitLimit = 1u << 24;
 constexpr int kScaleAhead = 8;                     // stages of block scales in flight per epilogue thread
@@ -82,6 +82,8 @@ struct LhCfg {
   static constexpr int RAW = NR == 32 ? 8 : 4;   // packed stages in flight
   static constexpr int CONV = NR == 32 ? 4 : 2;  // converted A slots
   static constexpr int ACC = kLhTmemCols / NR;   // block accumulators
+  static constexpr int AP = ACC / 4;              // accumulator sets of a pass (two stages, four blocks)
+  static constexpr int CP = CONV / 2;             // A slot pairs (one pass each)
   static constexpr int NG = NR == 32 ? 2 : 1;    // converter groups (stage g: group g % NG)
   static constexpr int CONVW = 4 * NG;           // converter warps
   static constexpr int THREADS = (2 + CONVW + kLhEpiWarps) * 32;
@@ -103,19 +105,18 @@ __global__ void __launch_bounds__(LhCfg<NR>::THREADS, 1)
     k_lm_head_tc(const T* __restrict__ x, int ldx, const int* __restrict__ row_map, const int* __restrict__ n_rows_ptr,
                  LinW W, GemvEpi ep, int* __restrict__ status) {
   using C = LhCfg<NR>;
-  constexpr int RAW = C::RAW, CONV = C::CONV, ACC = C::ACC;
-  static_assert(ACC == 2 * CONV, "a stage's accumulators must follow its A slot");
+  constexpr int RAW = C::RAW, CONV = C::CONV, ACC = C::ACC, AP = C::AP, CP = C::CP;
   extern __shared__ uint8_t smem_raw[];
-  // stage_done[c]: one tcgen05.commit per stage, after its four MMAs: the
-  // stage's two accumulators hold their sums (accumulators 2c and 2c + 1
-  // belong to the stages that use A slot c, because ACC == 2 * CONV).
-  // acc_empty[c]: the epilogue has read both accumulators of slot c's stage,
-  // so those MMAs are complete: A slot c and its accumulators are free. The
-  // converters wait on it before they refill slot c, so conv_full of a stage
-  // implies everything the MMA warp needs, and that warp waits once per
-  // stage (its barrier round trips, not the MMAs, bound the stage rate).
-  __shared__ __align__(8) uint64_t full[RAW], empty[RAW], conv_full[CONV], stage_done[CONV], acc_empty[CONV],
-      mma_done;
+  // The MMA warp works in passes of two stages (p = g / 2; n_stages is even
+  // since K % 128 == 0), with one tcgen05.commit per pass on each of:
+  //  * conv_free[p % CP]: the pass's MMAs have read its two A slots;
+  //  * acc_full[p % AP]: its four block accumulators hold their sums;
+  // and the epilogue's eight warps release a pass's accumulators on
+  // acc_empty[p % AP]. With all 512 tensor-memory columns there are AP
+  // passes of accumulators, so the MMAs and the converters run on through
+  // the epilogue's end-of-tile work (logits, rounding, per-row best).
+  __shared__ __align__(8) uint64_t full[RAW], empty[RAW], conv_full[CONV], conv_free[CP], acc_full[AP],
+      acc_empty[AP], mma_done;
   __shared__ uint32_t tmem_base_s;
   __shared__ float rs_s[NR];
   __shared__ uint32_t xmax_s[NR];  // largest |value| of each staged row (f32 bits)
@@ -147,9 +148,12 @@ __global__ void __launch_bounds__(LhCfg<NR>::THREADS, 1)
     }
     for (int i = 0; i < CONV; ++i) {
       mbar_init(&conv_full[i], 4);
-      mbar_init(&stage_done[i], 1);  // tcgen05.commit after the stage's MMAs
     }
-    for (int i = 0; i < CONV; ++i) mbar_init(&acc_empty[i], kLhEpiWarps / 2);  // the four warps of the stage parity
+    for (int i = 0; i < CP; ++i) mbar_init(&conv_free[i], 1);  // tcgen05.commit after the pass's MMAs
+    for (int i = 0; i < AP; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], kLhEpiWarps);  // both stage parities' four warps
+    }
     mbar_init(&mma_done, 1);
     abort_s = 0;
     stop_s = 0;
@@ -196,15 +200,14 @@ __global__ void __launch_bounds__(LhCfg<NR>::THREADS, 1)
       // the whole warp runs the loop; the elected lane issues (elect_one)
       constexpr uint32_t idesc = umma_idesc_f16(false, kLhFeat, NR);  // f16 operands
       bool ok = true;
-      // two stages per pass (n_stages is even: K % 128 == 0), which halves
-      // this warp's loop and wait instructions per stage; it shares its
-      // scheduler with converter and epilogue warps, so its instruction
-      // count, not the MMAs, sets the pace
+      // two stages per pass, which halves this warp's loop and wait
+      // instructions per stage; it shares its scheduler with converter and
+      // epilogue warps, so its instruction count, not the MMAs, sets the pace
       for (int g = 0; ok && g < n_stages; g += 2) {
-        // conv_full of stage g also means stage g - CONV's accumulators
-        // were read (the converters waited on acc_empty for the slot)
+        const int p = g >> 1;
         if (*abort_v || !mbar_wait_warp(&conv_full[g % CONV], (g / CONV) & 1, kLhWaitLimit) ||
-            !mbar_wait_warp(&conv_full[(g + 1) % CONV], ((g + 1) / CONV) & 1, kLhWaitLimit)) {
+            !mbar_wait_warp(&conv_full[(g + 1) % CONV], ((g + 1) / CONV) & 1, kLhWaitLimit) ||
+            (p >= AP && !mbar_wait_warp(&acc_empty[p % AP], ((p / AP) + 1) & 1, kLhWaitLimit))) {
           ok = false;
           break;
         }
@@ -220,8 +223,9 @@ __global__ void __launch_bounds__(LhCfg<NR>::THREADS, 1)
               umma_f16(acc, umma_desc_sw128(at), umma_desc_sw128(bt), idesc, false);
               umma_f16(acc, umma_desc_sw128(at + 32), umma_desc_sw128(bt + 32), idesc, true);
             }
-            umma_commit(&stage_done[c]);  // the stage's sums are ready once these MMAs complete
           }
+          umma_commit(&conv_free[p % CP]);  // the pass's A slots are read once these MMAs complete
+          umma_commit(&acc_full[p % AP]);   // and its accumulators hold the sums
         }
         __syncwarp();
       }
@@ -238,8 +242,9 @@ __global__ void __launch_bounds__(LhCfg<NR>::THREADS, 1)
     bool ok = true;
     for (int g = grp; ok && g < n_stages; g += C::NG) {
       const int s = g % RAW, c = g % CONV;
-      // slot c and its accumulators are free once stage g - CONV was read out
-      if (g >= CONV && (*abort_v || !mbar_wait_bounded(&acc_empty[c], ((g / CONV) + 1) & 1, kLhWaitLimit))) {
+      // slot c is free once the MMAs of pass g / 2 - CP have completed
+      const int p = g >> 1;
+      if (p >= CP && (*abort_v || !mbar_wait_bounded(&conv_free[p % CP], ((p / CP) + 1) & 1, kLhWaitLimit))) {
         ok = false;
         break;
       }
@@ -433,7 +438,7 @@ __global__ void __launch_bounds__(LhCfg<NR>::THREADS, 1)
         const int a0 = (2 * g) % ACC, a1 = (2 * g + 1) % ACC;
         // the tensor-memory loads are warp-wide: the warp goes on only if
         // the waits passed for all of its lanes
-        const bool got = !*abort_v && mbar_wait_bounded(&stage_done[g % CONV], (g / CONV) & 1, kLhWaitLimit);
+        const bool got = !*abort_v && mbar_wait_bounded(&acc_full[(g >> 1) % AP], ((g >> 1) / AP) & 1, kLhWaitLimit);
         if (!__all_sync(0xffffffffu, got)) {
           ok = false;
           *abort_v = 1;
@@ -453,7 +458,7 @@ __global__ void __launch_bounds__(LhCfg<NR>::THREADS, 1)
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&acc_empty[g % CONV]);
+        if (lane == 0) mbar_arrive(&acc_empty[(g >> 1) % AP]);
       }
       // the tile's logits: even-stage sum + odd-stage sum, scaled back and
       // rounded; per row the best (value, lowest index) of the tile
