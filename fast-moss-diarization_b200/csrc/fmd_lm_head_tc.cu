@@ -466,18 +466,24 @@ __global__ void __launch_bounds__(LhCfg<NR>::THREADS, 1)
 #pragma unroll
       for (int h = 0; h < NR / 32; ++h) {
         named_sync(1, NE);  // the previous half's reads are done
-        if (par == 1) {
+        // each parity hands the other its partial sums of half the rows
+        // (odd: rows 0-15, even: rows 16-31), then completes the other half:
+        // even sum + odd sum, scaled back, rounded
+        // (register indices stay compile-time: the parity selects values)
+        const int mine = par == 0 ? 0 : 16, theirs = 16 - mine;
 #pragma unroll
-          for (int j = 0; j < 32; ++j) lg[j * kLhLgStride + fl] = acc[h * 32 + j];
-        }
+        for (int j = 0; j < 16; ++j)
+          lg[(theirs + j) * kLhLgStride + fl] = par == 0 ? acc[h * 32 + 16 + j] : acc[h * 32 + j];
         named_sync(1, NE);
-        if (par == 0) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float v = rnd<T>((acc[h * 32 + j] + lg[j * kLhLgStride + fl]) * inv_s[h * 32 + j]);
-            lg[j * kLhLgStride + fl] = v;
-            if (ep.logits && h * 32 + j < rows) ep.logits[(size_t)(h * 32 + j) * W.N + f0 + fl] = v;
-          }
+        for (int j = 0; j < 16; ++j) {
+          const int r = mine + j;
+          const float o = lg[r * kLhLgStride + fl];
+          const float a = par == 0 ? acc[h * 32 + j] : acc[h * 32 + 16 + j];
+          // the even stages' sum first, as a fixed order for both halves
+          const float v = rnd<T>((par == 0 ? a + o : o + a) * inv_s[h * 32 + r]);
+          lg[r * kLhLgStride + fl] = v;
+          if (ep.logits && h * 32 + r < rows) ep.logits[(size_t)(h * 32 + r) * W.N + f0 + fl] = v;
         }
         named_sync(1, NE);
         float bv = -INFINITY;
