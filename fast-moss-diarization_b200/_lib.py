@@ -40,7 +40,7 @@ EXPORTS = [
     "fmd_slot_len", "fmd_prefill", "fmd_decode_step", "fmd_engine_load", "fmd_engine_start", "fmd_engine_step",
     "fmd_engine_run", "fmd_engine_fetch",
     "fmd_generate", "fmd_debug_weight", "fmd_debug_kv", "fmd_q8_0_quantize", "fmd_q8_0_quantize_device", "fmd_greedy_pick_noalloc",
-    "fmd_debug_wait_timeout", "fmd_debug_paths",
+    "fmd_debug_wait_timeout", "fmd_debug_paths", "fmd_debug_mma_issue",
     # include/fmd_audio.h
     "fmd_audio_create", "fmd_audio_destroy", "fmd_audio_last_error", "fmd_audio_memory_bytes", "fmd_audio_encode",
     "fmd_audio_encode_audio", "fmd_audio_token_offsets", "fmd_audio_last_timing", "fmd_mel_create", "fmd_mel_destroy", "fmd_mel_last_error",
@@ -169,6 +169,7 @@ def load() -> C.CDLL:
         "fmd_greedy_pick_noalloc": (C.c_int, [P, I32, I32, P, P]),
         "fmd_debug_wait_timeout": (C.c_int, [P, I32]),
         "fmd_debug_paths": (C.c_int, [P, C.POINTER(I32)]),
+        "fmd_debug_mma_issue": (C.c_int, [P, I32, I32, I32, C.POINTER(C.c_double)]),
         "fmd_audio_create": (C.c_int, [C.POINTER(AudioConfig), C.POINTER(AudioWeights), I32, I32, I32,
                                        C.POINTER(P)]),
         "fmd_audio_destroy": (C.c_int, [P]),

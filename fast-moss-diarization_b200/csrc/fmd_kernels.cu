@@ -572,6 +572,86 @@ __global__ void k_wait_probe(uint32_t limit, int* __restrict__ status) {
 
 void launch_wait_probe(uint32_t limit, int* status, cudaStream_t s) { k_wait_probe<<<1, 32, 0, s>>>(limit, status); }
 
+// Issue cost of tcgen05.mma (M 128 x N x K 16, kind::f16, zero operands in
+// shared memory) in the two forms a kernel can take: form 0, one thread of a
+// diverged warp runs the loop (`if (threadIdx.x == 0)`); form 1, the whole
+// warp runs the loop and its elected lane issues, the form every tensor-core
+// kernel of this library uses. cycles[0] = SM cycles per MMA from the first
+// issue to the completion of the last (clock64, one CTA), or -1 if the final
+// wait gave up.
+__global__ void __launch_bounds__(128, 1) k_mma_issue_probe(int form, int n, int iters, long long* cycles,
+                                                            int* status) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t done;
+  __shared__ uint32_t tmem_base_s;
+  const uint32_t raw_u = smem_u32(smem_raw);
+  const uint32_t base = (raw_u + 1023u) & ~1023u;  // A: 128 x 128 B, B: up to 256 x 128 B, swizzle atoms aligned
+  uint8_t* base_p = smem_raw + (base - raw_u);
+  for (int i = threadIdx.x; i < (48 * 1024) / 16; i += blockDim.x)
+    reinterpret_cast<int4*>(base_p)[i] = make_int4(0, 0, 0, 0);
+  if (threadIdx.x == 0) {
+    mbar_init(&done, 1);
+    fence_barrier_init();
+  }
+  asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+  if (threadIdx.x < 32) {
+    tmem_alloc(&tmem_base_s, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base_s, a = base, b = base + 16 * 1024;
+  const uint32_t idesc = umma_idesc_f16(false, 128, n);
+  if (threadIdx.x < 32) {
+    long long t0 = 0, t1 = 0;
+    bool ok = true;
+    if (form == 0) {
+      if (threadIdx.x == 0) {
+        t0 = clock64();
+        for (int i = 0; i < iters; ++i) {
+          const uint32_t ko = (uint32_t)(i & 3) * 32u;
+          umma_f16(tmem + (uint32_t)(((i >> 2) & 1) * n), umma_desc_sw128(a + ko), umma_desc_sw128(b + ko), idesc,
+                   (i & 3) != 0);
+        }
+        umma_commit(&done);
+        ok = mbar_wait_bounded(&done, 0, 1u << 24);
+        t1 = clock64();
+      }
+      __syncwarp();
+    } else {
+      t0 = clock64();
+      for (int i = 0; i < iters; ++i) {
+        const uint32_t ko = (uint32_t)(i & 3) * 32u;
+        if (elect_one())
+          umma_f16(tmem + (uint32_t)(((i >> 2) & 1) * n), umma_desc_sw128(a + ko), umma_desc_sw128(b + ko), idesc,
+                   (i & 3) != 0);
+        __syncwarp();
+      }
+      if (elect_one()) umma_commit(&done);
+      __syncwarp();
+      ok = mbar_wait_warp(&done, 0, 1u << 24);
+      t1 = clock64();
+    }
+    if (threadIdx.x == 0) {
+      if (!ok) report_timeout(status, kSiteWaitProbe);
+      cycles[0] = ok ? (t1 - t0) : -1;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (threadIdx.x < 32) tmem_dealloc(tmem, 512);
+}
+
+cudaError_t launch_mma_issue_probe(int form, int n, int iters, long long* cycles, int* status, cudaStream_t s) {
+  constexpr int kSmem = 48 * 1024 + 1024;
+  cudaError_t e = cudaFuncSetAttribute(k_mma_issue_probe, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+  if (e != cudaSuccess) return e;
+  k_mma_issue_probe<<<1, 128, kSmem, s>>>(form, n, iters, cycles, status);
+  return cudaGetLastError();
+}
+
 cudaError_t init_kernels() { return cudaSuccess; }
 
 void launch_dequant(ActType at, const LinW& W, float* out, cudaStream_t s) {

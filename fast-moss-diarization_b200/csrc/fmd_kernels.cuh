@@ -267,6 +267,10 @@ void launch_half_counts(const PlanCounts* full, PlanCounts* halves, int split, c
 // One bounded wait that runs out after `limit` tries and sets *status to
 // FMD_ETIMEDOUT (the failure path of every ring kernel's waits).
 void launch_wait_probe(uint32_t limit, int* status, cudaStream_t s);
+// tcgen05.mma issue cost probe (fmd_debug_mma_issue): one CTA, `iters` MMAs
+// of M 128 x N n x K 16 issued in `form` 0 (lone thread of a diverged warp)
+// or 1 (converged warp, elected lane); cycles[0] = SM cycles for all of them.
+cudaError_t launch_mma_issue_probe(int form, int n, int iters, long long* cycles, int* status, cudaStream_t s);
 // fmd_splice.cu: prompt rows from vocabulary ids (src >= 0) or audio rows
 // (src = -row - 1), H a multiple of 8, every pointer 16-byte aligned.
 void launch_splice(ActType at, const int* src, long long n, const void* table, const void* audio, bool audio_f32,

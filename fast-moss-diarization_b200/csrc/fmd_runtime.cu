@@ -1857,6 +1857,25 @@ int fmd_debug_wait_timeout(fmd_handle* h, int32_t limit) {
   return sync_check(h);
 }
 
+int fmd_debug_mma_issue(fmd_handle* h, int32_t form, int32_t n, int32_t iters, double* cycles_per_mma) {
+  int rc = check_ready(h);
+  if (rc) return rc;
+  if (!cycles_per_mma || (form != 0 && form != 1) || n < 16 || n > 256 || n % 16 || iters < 8 || iters > (1 << 20) ||
+      iters % 8)
+    return fail(h, FMD_EINVAL, "form must be 0 or 1, n a multiple of 16 in [16, 256], iters a multiple of 8 in [8, 2^20]");
+  CK(cudaSetDevice(h->device));
+  long long* d = nullptr;
+  CK(cudaMalloc((void**)&d, sizeof(long long)));
+  long long c = -1;
+  cudaError_t e = launch_mma_issue_probe(form, n, iters, d, h->d_status, h->stream);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(&c, d, sizeof(c), cudaMemcpyDeviceToHost, h->stream);
+  rc = e != cudaSuccess ? fail(h, FMD_EIO, cudaGetErrorString(e)) : sync_check(h);
+  cudaFree(d);
+  if (rc) return rc;
+  *cycles_per_mma = c < 0 ? -1.0 : (double)c / iters;
+  return FMD_OK;
+}
+
 int fmd_debug_paths(const fmd_handle* h, int32_t* flags) {
   if (!h || !flags) return FMD_EINVAL;
   *flags = (h->chain_ok ? FMD_PATH_LAYER_TAIL : 0) | (h->tc_ready && h->proj_allowed ? FMD_PATH_PROJ_TC : 0) |

@@ -238,6 +238,14 @@ class Qwen3Decoder:
         raises FmdError with FMD_ETIMEDOUT, after which the handle stays usable."""
         self._check(self.lib.fmd_debug_wait_timeout(self._h, int(limit)))
 
+    def debug_mma_issue(self, form: int, n: int, iters: int = 4096) -> float:
+        """SM cycles per tcgen05.mma (M 128 x N n x K 16) issued by one thread
+        of a diverged warp (form 0) or the elected lane of a converged warp
+        (form 1, the library's kernels) (`fmd_debug_mma_issue`)."""
+        c = C.c_double(0.0)
+        self._check(self.lib.fmd_debug_mma_issue(self._h, int(form), int(n), int(iters), C.byref(c)))
+        return float(c.value)
+
     def debug_paths(self) -> dict:
         """Which kernels serve this handle's steps (`fmd_debug_paths`):
         {"layer_tail": decode steps on the persistent layer tail,
