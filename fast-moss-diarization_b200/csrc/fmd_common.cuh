@@ -256,10 +256,12 @@ FMD_DEV void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_
 }
 // True in exactly one lane of the calling (converged) warp. The MMA-issuing
 // warps run their whole issue loop as a warp (waits, descriptors, branches
-// uniform) and let the elected lane issue tcgen05.mma and tcgen05.commit:
-// measured on B200, an M 128 x K 16 MMA then takes 58 cycles (N 32, 64) to
-// 128 cycles (N 256, the tensor peak), against ~300 cycles for any N when
-// one thread of a diverged warp issues it.
+// uniform) and let the elected lane issue tcgen05.mma and tcgen05.commit.
+// In this library's kernels that form was faster than a lone thread of a
+// diverged warp running the loop (prefill attention 161 -> 143 us per
+// captured launch, the tensor-core lm_head 119 -> 107 us); the cost of an
+// issue depends on the code around it (fmd_debug_mma_issue measures both
+// forms on a bare loop).
 FMD_DEV bool elect_one() {
   uint32_t pred;
   asm volatile("{\n .reg .pred e;\n elect.sync _|e, 0xffffffff;\n selp.u32 %0, 1, 0, e;\n}\n" : "=r"(pred));

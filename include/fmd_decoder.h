@@ -277,11 +277,13 @@ int fmd_debug_wait_timeout(fmd_handle* h, int32_t limit);
 
 /* Issue cost of a tcgen05.mma (no reference counterpart; a hardware check
  * behind the kernels' design): one CTA issues `iters` MMAs of M 128 x N `n`
- * x K 16 (f16, operands in shared memory) either from one thread of a
- * diverged warp (`form` 0) or from the elected lane of a warp that runs the
- * issue loop converged (`form` 1, the form the library's tensor-core kernels
- * use), and *cycles_per_mma receives the SM cycles per MMA from the first
- * issue to the completion of the last. n: a multiple of 16 in [16, 256];
+ * x K 16 (f16, operands in shared memory) in a bare loop, either from one
+ * thread of a diverged warp (`form` 0) or from the elected lane of a warp
+ * that runs the loop converged (`form` 1, the form the library's tensor-core
+ * kernels use), and *cycles_per_mma receives the SM cycles per MMA from the
+ * first issue to the completion of the last: the per-instruction floor that
+ * small-N MMAs (the lm_head's 32 rows, attention's 64 keys) run into, and the
+ * tensor peak at N 256 (128 cycles). n: a multiple of 16 in [16, 256];
  * iters: a multiple of 8 in [8, 2^20]; the handle must have weights loaded and
  * a KV pool reserved, as for the other debug calls. */
 int fmd_debug_mma_issue(fmd_handle* h, int32_t form, int32_t n, int32_t iters, double* cycles_per_mma);

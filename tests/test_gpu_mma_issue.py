@@ -1,11 +1,14 @@
-"""The issue form of tcgen05.mma that every tensor-core kernel of the library
-uses (fmd_common.cuh elect_one: the MMA warp runs its issue loop converged and
-one elected lane issues) against one thread of a diverged warp issuing alone
-(`if (threadIdx.x == 0)`), through fmd_debug_mma_issue: one CTA, 4,096 MMAs of
-M 128 x N x K 16. On B200 the converged form runs small MMAs several times
-faster and reaches the tensor peak at N = 256 (128 cycles per MMA of 524,288
-multiply-adds = 4,096 per cycle per SM); the diverged form costs about 300
-cycles per MMA whatever N."""
+"""tcgen05.mma issue cost through fmd_debug_mma_issue: one CTA issues 4,096
+MMAs of M 128 x N x K 16 in a bare loop, from a lone thread of a diverged warp
+(form 0) or from the elected lane of a converged warp (form 1, the form of
+every tensor-core kernel in the library, fmd_common.cuh elect_one). Whatever
+the form, an MMA costs a fixed number of cycles up to N 128 (the floor the
+lm_head's 32-row and attention's 64-key MMAs run into), and at N 256 the
+converged form reaches the tensor peak: 128 cycles per MMA of 524,288
+multiply-adds, 4,096 per cycle per SM. Which form is cheaper on a bare loop
+depends on the code the compiler makes of it; inside the library's kernels
+the converged form measured faster (prefill attention 161 -> 143 us per
+captured launch, the tensor-core lm_head 119 -> 107 us)."""
 
 from __future__ import annotations
 
@@ -19,7 +22,7 @@ syn = importlib.import_module("fmd_b200.synthetic")
 pytestmark = pytest.mark.gpu
 
 
-def test_converged_issue_is_faster_and_reaches_the_tensor_peak():
+def test_small_mmas_cost_a_fixed_issue_time_and_n256_reaches_the_tensor_peak():
     cfg = tiny_config()
     with PKG.Qwen3Decoder(cfg, "bf16") as dec:
         dec.load_weights(syn.make_weights(cfg, seed=3))
@@ -31,11 +34,10 @@ def test_converged_issue_is_faster_and_reaches_the_tensor_peak():
             assert converged > 0 and diverged > 0
         print("\nN, cycles per MMA (diverged thread, converged warp + elected lane):",
               [(n, round(a, 1), round(b, 1)) for n, a, b in rows])
-        for n, diverged, converged in rows:
-            # small MMAs: the converged form at least twice as fast
-            if n <= 64:
-                assert converged * 2 <= diverged, (n, diverged, converged)
-        # N = 256: within 25 % of the tensor peak (128 cycles per MMA)
+        # up to N 128 a fixed cost per MMA: N 32 costs as much as N 128
+        for form in (1, 2):
+            assert abs(rows[0][form] - rows[2][form]) <= 0.1 * rows[2][form], rows
+        # N 256, converged: within 25 % of the tensor peak (128 cycles per MMA)
         assert rows[-1][2] < 160.0, rows[-1]
         with pytest.raises(PKG.FmdError) as e:
             dec.debug_mma_issue(2, 64)
