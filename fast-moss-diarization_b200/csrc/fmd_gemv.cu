@@ -111,29 +111,19 @@ __global__ void __launch_bounds__(FW * KG * 32) k_gemv(const T* __restrict__ x, 
       for (int i = 0; i < 4; ++i) hnw[i] = Act<T>::to_f(nw[i]);
     }
   }
-  griddep_wait();
-  griddep_launch();  // only after the wait: see griddep_launch
-
+  // The row count, the plan's positions / slots / pages and the residual
+  // rows come from kernels at least two launches back (the scheduler, the
+  // embedding, an earlier projection), which are complete when this kernel
+  // starts: every kernel signals its dependents only after its own
+  // dependency wait. So they are read before the wait, off the path that
+  // starts when the previous kernel's activations land.
   const int n_rows = *n_rows_ptr;
   const int row0 = blockIdx.z * kRows;
   const int cpr = klen >> 3;  // 16-byte chunks per activation row
-  // Without a row map every row this tile can hold exists in x (the pass has
-  // at most `max_rows` rows), so its copies are issued before the row count
-  // arrives; rows past the count are never stored.
-  const bool eager = row_map == nullptr;
-  if (eager) {
-    const int avail = min(min(kRows, xrows), max_rows - row0);
-    for (int c = threadIdx.x; c < avail * cpr; c += NT) {
-      const int r = c / cpr, ch = c - r * cpr;
-      cp_async16(xs + (size_t)r * xstride + ch * 8, x + (size_t)(row0 + r) * ldx + kbeg + ch * 8, 16);
-    }
-    cp_async_commit();
-  }
   const int rows = max(0, min(min(kRows, xrows), n_rows - row0));
   const int n_tiles = (rows + 7) >> 3;
 
-  // epilogue operands written by earlier kernels, fetched now so that their
-  // latency hides behind the k-loop: the first kPre rows this warp will own
+  // epilogue operands, in flight during the k-loop: the first kPre rows this warp will own
   // after the cluster reduction (lr = rank + warp * S + i * NW * S)
   constexpr int FPL = FT / 32;  // features per lane in the epilogue (2 or 4)
   constexpr int kPre = 2;
@@ -160,7 +150,32 @@ __global__ void __launch_bounds__(FW * KG * 32) k_gemv(const T* __restrict__ x, 
     }
   }
 
-  if (rows > 0 && !eager) {
+  // RoPE factors of those rows (constant tables), in flight during the k-loop
+  float rcs[kPre][4], rsn[kPre][4];
+#pragma unroll
+  for (int i = 0; i < kPre; ++i)
+#pragma unroll
+    for (int f = 0; f < 4; ++f) rcs[i][f] = rsn[i][f] = 0.f;
+  if constexpr (EPI == kGemvQkv) {
+    if ((int)blockIdx.x < ep.Hq + ep.Hkv) {
+      const int dd = (lane & 15) * 4;
+#pragma unroll
+      for (int i = 0; i < kPre; ++i)
+        if (rank + warp * S + i * NW * S < rows) {
+          const T* ct = reinterpret_cast<const T*>(ep.cos) + (size_t)ppos[i] * (kHeadDim / 2) + dd;
+          const T* st = reinterpret_cast<const T*>(ep.sin) + (size_t)ppos[i] * (kHeadDim / 2) + dd;
+#pragma unroll
+          for (int f = 0; f < 4; ++f) {
+            rcs[i][f] = Act<T>::to_f(ct[f]);
+            rsn[i][f] = Act<T>::to_f(st[f]);
+          }
+        }
+    }
+  }
+  griddep_wait();
+  griddep_launch();  // only after the wait: see griddep_launch
+
+  if (rows > 0) {
     // activation tile rows x klen through the row map (rows of a partial
     // n-tile zero-filled)
     for (int c = threadIdx.x; c < n_tiles * 8 * cpr; c += NT) {
@@ -198,29 +213,6 @@ __global__ void __launch_bounds__(FW * KG * 32) k_gemv(const T* __restrict__ x, 
         }
         *p = v;
       }
-    }
-  }
-  // RoPE factors of the prefetched rows (their positions have landed by now);
-  // in flight during the k-loop
-  float rcs[kPre][4], rsn[kPre][4];
-#pragma unroll
-  for (int i = 0; i < kPre; ++i)
-#pragma unroll
-    for (int f = 0; f < 4; ++f) rcs[i][f] = rsn[i][f] = 0.f;
-  if constexpr (EPI == kGemvQkv) {
-    if ((int)blockIdx.x < ep.Hq + ep.Hkv) {
-      const int dd = (lane & 15) * 4;
-#pragma unroll
-      for (int i = 0; i < kPre; ++i)
-        if (rank + warp * S + i * NW * S < rows) {
-          const T* ct = reinterpret_cast<const T*>(ep.cos) + (size_t)ppos[i] * (kHeadDim / 2) + dd;
-          const T* st = reinterpret_cast<const T*>(ep.sin) + (size_t)ppos[i] * (kHeadDim / 2) + dd;
-#pragma unroll
-          for (int f = 0; f < 4; ++f) {
-            rcs[i][f] = Act<T>::to_f(ct[f]);
-            rsn[i][f] = Act<T>::to_f(st[f]);
-          }
-        }
     }
   }
   __syncthreads();  // barrier inits (and rs_s) visible to all threads

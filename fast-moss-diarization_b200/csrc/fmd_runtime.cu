@@ -643,11 +643,14 @@ void run_forward_decode(fmd_handle* h, float* logits_dev, const void* arena) {
   const float eps = c.rms_norm_eps;
   const int ssq_tiles = H / 64;
   const int L = c.num_hidden_layers;
+  // the halves' row counts before the embedding: the projections read their
+  // row count ahead of their dependency wait, so it must come from a kernel
+  // at least two launches back
+  if (h->split_ok) launch_half_counts(h->plan.counts, h->half_counts, R / 2, s);
   launch_embed_norm(h->at, h->plan, row_grid, h->embed, arena, h->x, h->layers[0].in_norm, h->xn, H, eps, h->ssq,
                     ssq_tiles, s, h->chain_ok ? h->chain_sync : nullptr, h->chain_ok ? L * kChainSyncInts : 0);
   trace(h, "embed_norm", -1);
   if (h->split_ok) {
-    launch_half_counts(h->plan.counts, h->half_counts, R / 2, s);
     cudaEventRecord(h->fork_ev, s);
     cudaStreamWaitEvent(h->stream2, h->fork_ev, 0);
     decode_layers(h, decode_view(h, 0), s, true);
