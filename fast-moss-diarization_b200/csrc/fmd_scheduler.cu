@@ -37,6 +37,11 @@ __global__ void __launch_bounds__(256) k_schedule(EngineDev e) {
   __shared__ int smp_slot[kMaxSlots], smp_tok[kMaxSlots];
   __shared__ EngineCounters s_ctr;
   __shared__ int s_prev;
+  // page moves recorded by the serial bookkeeping and done by all threads:
+  // the pages of finished slots onto the free stack (frees) and off it into
+  // admitted slots' page tables (allocations), in the stack's LIFO order
+  __shared__ int s_nf, fin_slot[kMaxSlots], fin_np[kMaxSlots], fin_base[kMaxSlots];
+  __shared__ int s_na, adm_slot[kMaxSlots], adm_need[kMaxSlots], adm_top[kMaxSlots];
   PlanCounts* cnt = e.plan.counts;
   const int nb = e.max_batch;
 
@@ -67,6 +72,7 @@ __global__ void __launch_bounds__(256) k_schedule(EngineDev e) {
     // ---- 1. consume the previous step's samples ----
     const int prev = s_prev;
     long long emitted = 0;
+    int nf = 0;
     for (int i = 0; i < prev; ++i) {
       const int slot = smp_slot[i];
       const int tok = smp_tok[i];
@@ -95,24 +101,36 @@ __global__ void __launch_bounds__(256) k_schedule(EngineDev e) {
       if (finish >= 0) {
         e.results[req].n_tokens = st_ngen[slot];
         e.results[req].finish_reason = finish;
-        const int np = st_npages[slot];
-        const int* pt = e.page_table + (size_t)slot * e.max_pages_per_slot;
-        for (int k = 0; k < np; ++k) e.free_stack[c->free_top++] = pt[k];
+        // its pages go onto the free stack at free_top .. free_top + np - 1
+        fin_slot[nf] = slot;
+        fin_np[nf] = st_npages[slot];
+        fin_base[nf] = c->free_top;
+        c->free_top += st_npages[slot];
+        ++nf;
         st_npages[slot] = 0;
         st_state[slot] = kSlotFree;
         c->done += 1;
       }
     }
     c->gen_tokens += emitted;
+    s_nf = nf;
+    s_na = 0;
     if (e.consume_only) {
       cnt->n_rows = cnt->n_decode = cnt->n_sample = cnt->n_pblocks = cnt->n_ditems = 0;
       cnt->finished = c->done >= e.n_reqs ? 1 : 0;
     }
   }
+  __syncthreads();
+  for (int f = 0; f < s_nf; ++f) {
+    const int* pt = e.page_table + (size_t)fin_slot[f] * e.max_pages_per_slot;
+    for (int k = threadIdx.x; k < fin_np[f]; k += blockDim.x) e.free_stack[fin_base[f] + k] = pt[k];
+  }
+  __syncthreads();  // the freed pages are on the stack before admission pops them
   if (!e.consume_only && threadIdx.x == 0) {
     EngineCounters* c = &s_ctr;
 
     // ---- 2. admit queued requests into free slots ----
+    int na = 0;
     for (int s = 0; s < nb && c->next_req < e.n_reqs; ++s) {
       if (st_state[s] != kSlotFree) continue;
       const DevRequest rq = e.reqs[c->next_req];
@@ -129,8 +147,12 @@ __global__ void __launch_bounds__(256) k_schedule(EngineDev e) {
         continue;
       }
       if (need > c->free_top) break;  // wait for pages to come back (FIFO)
-      int* pt = e.page_table + (size_t)s * e.max_pages_per_slot;
-      for (int k = 0; k < need; ++k) pt[k] = e.free_stack[--c->free_top];
+      // page k of the slot is stack entry free_top - 1 - k
+      adm_slot[na] = s;
+      adm_need[na] = need;
+      adm_top[na] = c->free_top;
+      c->free_top -= need;
+      ++na;
       st_npages[s] = need;
       st_state[s] = kSlotPrefill;
       st_req[s] = c->next_req;
@@ -140,6 +162,7 @@ __global__ void __launch_bounds__(256) k_schedule(EngineDev e) {
       st_ngen[s] = 0;
       c->next_req += 1;
     }
+    s_na = na;
 
     // ---- 3. lay out the next plan (segment descriptors) ----
     int rows = 0, items = 0, samples = 0, pblocks = 0;
@@ -199,6 +222,10 @@ __global__ void __launch_bounds__(256) k_schedule(EngineDev e) {
     if (rows > 0) c->steps += 1;
   }
   __syncthreads();
+  for (int a = 0; a < s_na; ++a) {
+    int* pt = e.page_table + (size_t)adm_slot[a] * e.max_pages_per_slot;
+    for (int k = threadIdx.x; k < adm_need[a]; k += blockDim.x) pt[k] = e.free_stack[adm_top[a] - 1 - k];
+  }
   // ---- write the slot state and counters back ----
   for (int s = threadIdx.x; s < nb; s += blockDim.x) {
     e.slot_state[s] = st_state[s];
