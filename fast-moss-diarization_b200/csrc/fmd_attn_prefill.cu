@@ -81,13 +81,22 @@ FMD_DEV float pf_row_max(float (&s)[64], int key0, int qpos, float scale_log2) {
 }
 // p = 2^(s * scale - m_ref) in place (one rounding of the argument); returns
 // the row sum of the tile, added in 8 independent chains.
+// 2^x by the hardware approximation (PTX ex2.approx.ftz.f32: relative error
+// about 2^-22, results below 2^-126 flushed to zero). The probabilities are
+// rounded to the 16-bit operand type right after, so its error is far below
+// what reaches the PV product.
+FMD_DEV float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 FMD_DEV float pf_row_exp(float (&s)[64], float scale_log2, float m_ref) {
   float a[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) a[i] = 0.f;
 #pragma unroll
   for (int c = 0; c < 64; ++c) {
-    s[c] = exp2f(fmaf(s[c], scale_log2, -m_ref));
+    s[c] = ex2_approx(fmaf(s[c], scale_log2, -m_ref));
     a[c & 7] += s[c];
   }
   return ((a[0] + a[1]) + (a[2] + a[3])) + ((a[4] + a[5]) + (a[6] + a[7]));
