@@ -90,16 +90,41 @@ FMD_DEV float ex2_approx(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+// Two f32 lanes at once (PTX fma.rn.f32x2 / add.rn.f32x2, sm_100): each lane
+// rounds exactly as the scalar instruction, so the results are those of two
+// scalar FMAs or adds, in half the instructions.
+FMD_DEV float2 ffma2(float2 a, float2 b, float2 c) {
+  unsigned long long d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;"
+      : "=l"(d)
+      : "l"(*reinterpret_cast<unsigned long long*>(&a)), "l"(*reinterpret_cast<unsigned long long*>(&b)),
+        "l"(*reinterpret_cast<unsigned long long*>(&c)));
+  return *reinterpret_cast<float2*>(&d);
+}
+FMD_DEV float2 fadd2(float2 a, float2 b) {
+  unsigned long long d;
+  asm("add.rn.f32x2 %0, %1, %2;"
+      : "=l"(d)
+      : "l"(*reinterpret_cast<unsigned long long*>(&a)), "l"(*reinterpret_cast<unsigned long long*>(&b)));
+  return *reinterpret_cast<float2*>(&d);
+}
+// p = 2^(s * scale - m_ref) in place, and the row sum: eight partial sums
+// (key c into sum c % 8, two per packed lane pair), added in a fixed tree.
 FMD_DEV float pf_row_exp(float (&s)[64], float scale_log2, float m_ref) {
-  float a[8];
+  float2 a[4];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) a[i] = 0.f;
+  for (int i = 0; i < 4; ++i) a[i] = make_float2(0.f, 0.f);
+  const float2 sc = make_float2(scale_log2, scale_log2), nm = make_float2(-m_ref, -m_ref);
 #pragma unroll
-  for (int c = 0; c < 64; ++c) {
-    s[c] = ex2_approx(fmaf(s[c], scale_log2, -m_ref));
-    a[c & 7] += s[c];
+  for (int c = 0; c < 64; c += 2) {
+    float2 v = ffma2(make_float2(s[c], s[c + 1]), sc, nm);
+    v.x = ex2_approx(v.x);
+    v.y = ex2_approx(v.y);
+    s[c] = v.x;
+    s[c + 1] = v.y;
+    a[(c >> 1) & 3] = fadd2(a[(c >> 1) & 3], v);
   }
-  return ((a[0] + a[1]) + (a[2] + a[3])) + ((a[4] + a[5]) + (a[6] + a[7]));
+  return ((a[0].x + a[0].y) + (a[1].x + a[1].y)) + ((a[2].x + a[2].y) + (a[3].x + a[3].y));
 }
 
 template <typename T>
