@@ -1,8 +1,9 @@
-"""CPU simulation of the mbarrier protocols of the audio-tower kernels.
+"""CPU simulation of the mbarrier protocols of the ring-based kernels.
 
 A discrete-event model of `k_enc_gemm` (fmd_enc_gemm.cu), `k_enc_attn`
-(fmd_enc_attn.cu) and the decoder's persistent `k_lm_head` ring with G
-consumer groups (fmd_gemv.cu): every role (TMA producer, MMA issuer, epilogue / softmax
+(fmd_enc_attn.cu), the decoder's persistent `k_lm_head` ring with G
+consumer groups (fmd_gemv.cu) and the tensor-core lm_head `k_lm_head_tc`
+(fmd_lm_head_tc.cu: converter groups, passes of two stages): every role (TMA producer, MMA issuer, epilogue / softmax
 warps) runs as a coroutine, asynchronous work (TMA copies landing, MMA groups
 completing and their tcgen05.commit arrivals) completes at random later
 times, and the scheduler interleaves everything in random order. The model
@@ -472,3 +473,144 @@ def test_an_odd_stage_count_with_a_shared_ring_is_a_hazard():
         except AssertionError:
             hits += 1
     assert hits > 0
+
+
+# ---- k_lm_head_tc ---------------------------------------------------------------------------
+def lm_head_tc_protocol(sim, NR, my_tiles, nkb, bug=None):
+    """`k_lm_head_tc` (fmd_lm_head_tc.cu) on one CTA: a producer streams the
+    packed stages into RAW ring slots; NG groups of 4 converter warps take
+    stages g = grp, grp + NG, ... into CONV A slots; the MMA warp works in
+    passes of two stages (p = g / 2), waiting for both stages' conv_full and,
+    from the AP-th pass on, for acc_empty of pass p - AP, then one commit
+    frees the pass's A slots (conv_free[p % CP]) and one hands over its
+    accumulators (acc_full[p % AP]); 8 epilogue warps, four per stage
+    parity, read a stage's accumulators and release the pass on
+    acc_empty[p % AP] (count 8). Converters refill slot c of pass p only
+    after conv_free of pass p - CP. `bug` plants a mistake: "conv_free_early"
+    (a converter waits one release too early) or "acc_early" (the MMA warp
+    waits one accumulator release too early)."""
+    RAW, CONV, NG = (8, 4, 2) if NR == 32 else (4, 2, 1)
+    ACC = 512 // NR
+    AP, CP = ACC // 4, CONV // 2
+    n_stages = my_tiles * nkb
+    assert n_stages % 2 == 0 and nkb % 2 == 0
+    full = [Bar(f"full{s}", 1) for s in range(RAW)]
+    empty = [Bar(f"empty{s}", 4) for s in range(RAW)]
+    conv_full = [Bar(f"conv_full{c}", 4) for c in range(CONV)]
+    conv_free = [Bar(f"conv_free{q}", 1) for q in range(CP)]
+    acc_full = [Bar(f"acc_full{r}", 1) for r in range(AP)]
+    acc_empty = [Bar(f"acc_empty{r}", 8) for r in range(AP)]
+    raw = [Buf(f"raw{s}") for s in range(RAW)]
+    conv = [Buf(f"conv{c}") for c in range(CONV)]
+    acc = [Buf(f"acc{r}") for r in range(AP)]
+
+    def producer():
+        for g in range(n_stages):
+            s = g % RAW
+            if g >= RAW:
+                yield lambda b=empty[s], p=g // RAW - 1: b.try_wait(p)
+            full[s].arrive(expect_tx=1)
+
+            def land(s=s, g=g):
+                raw[s].write(g)
+                full[s].complete_tx(1)
+            sim.later(land, tag=g)
+
+    def converter(grp, w):
+        for g in range(grp, n_stages, NG):
+            s, c, p = g % RAW, g % CONV, g // 2
+            if p >= CP:
+                ph = p // CP - 1 - (1 if bug == "conv_free_early" else 0)
+                if ph >= 0:
+                    yield lambda b=conv_free[p % CP], q=ph: b.try_wait(q)
+            yield lambda b=full[s], q=g // RAW: b.try_wait(q)
+            raw[s].check(g)
+            raw[s].readers += 1
+            yield None  # fragments to registers
+            raw[s].readers -= 1
+            empty[s].arrive()
+            conv[c].write(g)  # this warp's rows of the A tile
+            yield None
+            conv_full[c].arrive()
+
+    pending = []
+
+    def drain_one():
+        pending.pop(0)()
+
+    def mma():
+        for g in range(0, n_stages, 2):
+            p = g // 2
+            yield lambda b=conv_full[g % CONV], q=g // CONV: b.try_wait(q)
+            yield lambda b=conv_full[(g + 1) % CONV], q=(g + 1) // CONV: b.try_wait(q)
+            if p >= AP:
+                ph = p // AP - 1 - (1 if bug == "acc_early" else 0)
+                if ph >= 0:
+                    yield lambda b=acc_empty[p % AP], q=ph: b.try_wait(q)
+            conv[g % CONV].check(g)
+            conv[(g + 1) % CONV].check(g + 1)
+            conv[g % CONV].readers += 1
+            conv[(g + 1) % CONV].readers += 1
+            acc[p % AP].write(p)
+
+            def done(g=g, p=p):
+                conv[g % CONV].readers -= 1
+                conv[(g + 1) % CONV].readers -= 1
+                conv_free[p % CP].arrive()
+                acc_full[p % AP].arrive()
+            pending.append(done)
+            sim.later(drain_one)
+
+    def epilogue(par, w):
+        for i in range(my_tiles):
+            for kb in range(par, nkb, 2):
+                g = i * nkb + kb
+                p = g // 2
+                yield lambda b=acc_full[p % AP], q=p // AP: b.try_wait(q)
+                acc[p % AP].check(p)
+                acc[p % AP].readers += 1
+                yield None  # tcgen05.ld of the stage's two accumulators
+                acc[p % AP].readers -= 1
+                acc_empty[p % AP].arrive()
+            yield None  # the tile's logits and per-row best (named barriers)
+
+    sim.spawn(producer())
+    for grp in range(NG):
+        for w in range(4):
+            sim.spawn(converter(grp, w))
+    sim.spawn(mma())
+    for par in range(2):
+        for w in range(4):
+            sim.spawn(epilogue(par, w))
+
+
+@pytest.mark.parametrize("seed", range(25))
+@pytest.mark.parametrize("NR,my_tiles,nkb", [(32, 9, 16), (32, 8, 16), (32, 1, 2), (64, 9, 16), (64, 2, 4)])
+def test_lm_head_tc_protocol(seed, NR, my_tiles, nkb):
+    sim = Sim(seed * 131 + NR + my_tiles * 7 + nkb)
+    lm_head_tc_protocol(sim, NR, my_tiles, nkb)
+    sim.run()
+
+
+@pytest.mark.parametrize("seed", range(10))
+def test_lm_head_tc_protocol_survives_a_late_copy(seed):
+    """One copy held back until nothing else can run (the converter group of
+    its stage stalls, the other group and the MMA passes run ahead as far as
+    the slots allow): no alias, no overwrite, no deadlock."""
+    sim = Sim(seed, hold=[37])
+    lm_head_tc_protocol(sim, 32, 4, 16)
+    sim.run()
+
+
+@pytest.mark.parametrize("bug", ["conv_free_early", "acc_early"])
+def test_the_lm_head_tc_model_catches_a_planted_mistake(bug):
+    failures = 0
+    for seed in range(20):
+        sim = Sim(seed)
+        lm_head_tc_protocol(sim, 32, 3, 16, bug=bug)
+        try:
+            sim.run()
+        except AssertionError as e:
+            assert any(k in str(e) for k in ("alias", "overwritten", "read", "behind")), e
+            failures += 1
+    assert failures == 20
