@@ -13,7 +13,8 @@
 //    16-bit K-major tiles by TMA with the 128-byte swizzle through a
 //    STAGES-deep full/empty mbarrier ring that runs on across tiles;
 //  * warp 1 allocates two BN-column f32 accumulators in tensor memory and,
-//    the whole warp running the loop, its elected lane issues tcgen05.mma (M = 128, N = BN, K = 16; four per k-block) into
+//    the whole warp running the loop, its elected lane issues tcgen05.mma
+//    (M = 128, N = BN, K = 16; four per k-block) into
 //    accumulator i % 2, releasing each stage with tcgen05.commit and handing
 //    the finished accumulator over with a commit to acc_full;
 //  * warps 2-9 are the epilogue: warp w reads tensor-memory lanes

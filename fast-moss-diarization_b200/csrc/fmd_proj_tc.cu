@@ -16,12 +16,13 @@
 //    full/empty mbarrier ring that runs on across tiles. Dense weights arrive
 //    as the swizzled 16-bit tile the MMA reads; Q8_0 weights as their int8
 //    tile (64-byte rows);
-//  * Q8_0 only, warps 10-13: converters. Each k-block's BN x 64 int8 values
+//  * Q8_0 only, warps 10-17: converters. Each k-block's BN x 64 int8 values
 //    and their f16 block scales become q * d rounded to the activation type,
 //    written in the swizzled layout, then a proxy fence and an arrival on the
 //    stage's `conv` barrier;
 //  * warp 1 allocates two BN-column f32 accumulators in tensor memory and,
-//    the whole warp running the loop, its elected lane issues tcgen05.mma (M = 128, N = BN, K = 16; four per k-block) into
+//    the whole warp running the loop, its elected lane issues tcgen05.mma
+//    (M = 128, N = BN, K = 16; four per k-block) into
 //    accumulator i % 2, releasing each stage with tcgen05.commit;
 //  * warps 2-9: the epilogue. Warp w owns tensor-memory lanes 32 (w % 4) ...
 //    (32 rows of the tile) and half (w - 2) / 4 of its columns; with BN = 256
@@ -53,9 +54,13 @@ template <int BN, bool Q8>
 constexpr size_t proj_smem() {
   return (size_t)proj_stages<BN, Q8>() * (kPBM * kPBK * 2 + BN * kPBK * 2 + (Q8 ? BN * kPBK : 0)) + 1024;
 }
+// Q8_0: 8 converter warps (warps 10-17); the dequantisation of a stage's
+// int8 tile, not the MMAs, paces the Q8_0 k-loop, so it is split over as many
+// warps as the registers allow (112 per thread at 576 threads)
+constexpr int kPConvWarps = 8;
 template <bool Q8>
 constexpr int proj_threads() {
-  return Q8 ? 448 : 320;
+  return Q8 ? (10 + kPConvWarps) * 32 : 320;
 }
 
 // 16 int8 weights (one lane's 16 bytes) times their block scale, rounded to
@@ -225,7 +230,7 @@ __global__ void __launch_bounds__(proj_threads<Q8>(), 1)
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
-      mbar_init(&conv[s], 4);  // Q8_0: one arrival per converter warp
+      mbar_init(&conv[s], kPConvWarps);  // Q8_0: one arrival per converter warp
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
@@ -325,12 +330,13 @@ __global__ void __launch_bounds__(proj_threads<Q8>(), 1)
     }
   } else if (warp >= 10) {
     if constexpr (Q8) {
-      // converters: warp cw turns rows cw*8 + 32*i + (lane >> 2) of each
-      // stage's int8 tile into the swizzled 16-bit B tile; lane & 3 picks 16
-      // consecutive k (half a Q8_0 block), so a lane needs one scale. The
-      // stage's previous B tile is free: the new copy landed only after the
-      // MMAs that read the old one completed (the producer waited on empty).
-      const int cw = warp - 10, c = lane & 3;
+      // converters: warp cw turns rows (cw % 4)*8 + 32*i + (lane >> 2), for the
+      // 32-row bands i of parity cw / 4, of each stage's int8 tile into the
+      // swizzled 16-bit B tile; lane & 3 picks 16 consecutive k (half a Q8_0
+      // block), so a lane needs one scale. The stage's previous B tile is
+      // free: the new copy landed only after the MMAs that read the old one
+      // completed (the producer waited on empty).
+      const int cw = (warp - 10) & 3, band = (warp - 10) >> 2, c = lane & 3;
       const int KB = K / 32;
       int g = 0;
       bool ok = true;
@@ -338,11 +344,11 @@ __global__ void __launch_bounds__(proj_threads<Q8>(), 1)
         const int n0 = (t / m_tiles) * BN;
         for (int kb = 0; kb < nk; ++kb, ++g) {
           const int st = g % STAGES;
-          float dsc[BN / 32];  // the scales first: their latency overlaps the copy's
+          float dsc[BN / 64];  // the scales first: their latency overlaps the copy's
 #pragma unroll
-          for (int i = 0; i < BN / 32; ++i) {
-            const int r = cw * 8 + 32 * i + (lane >> 2);
-            dsc[i] = h2f_bits(__ldg(wd + (size_t)(n0 + r) * KB + kb * 2 + (c >> 1)));
+          for (int ii = 0; ii < BN / 64; ++ii) {
+            const int r = cw * 8 + 32 * (2 * ii + band) + (lane >> 2);
+            dsc[ii] = h2f_bits(__ldg(wd + (size_t)(n0 + r) * KB + kb * 2 + (c >> 1)));
           }
           if (*abort_v || !mbar_wait_bounded(&full[st], (g / STAGES) & 1, kPWaitLimit)) {
             ok = false;
@@ -350,12 +356,12 @@ __global__ void __launch_bounds__(proj_threads<Q8>(), 1)
           }
           const uint8_t* qt = tiles_p + st * STAGE_BYTES + A_BYTES + B_BYTES;
           uint8_t* bt = tiles_p + st * STAGE_BYTES + A_BYTES;
-#pragma unroll 4
-          for (int i = 0; i < BN / 32; ++i) {
-            const int r = cw * 8 + 32 * i + (lane >> 2);
+#pragma unroll
+          for (int ii = 0; ii < BN / 64; ++ii) {
+            const int r = cw * 8 + 32 * (2 * ii + band) + (lane >> 2);
             const int4 qv = *reinterpret_cast<const int4*>(qt + r * kPBK + c * 16);
             uint32_t o[8];
-            dequant16<T>(qv, dsc[i], o);
+            dequant16<T>(qv, dsc[ii], o);
             // 16-byte chunk j of row r sits at chunk j ^ (r % 8) (128-byte swizzle)
             uint8_t* rowp = bt + r * 128;
             *reinterpret_cast<int4*>(rowp + (((2 * c) ^ (r & 7)) << 4)) = make_int4(o[0], o[1], o[2], o[3]);
