@@ -2,8 +2,10 @@
 
 A discrete-event model of `k_enc_gemm` (fmd_enc_gemm.cu), `k_enc_attn`
 (fmd_enc_attn.cu), the decoder's persistent `k_lm_head` ring with G
-consumer groups (fmd_gemv.cu) and the tensor-core lm_head `k_lm_head_tc`
-(fmd_lm_head_tc.cu: converter groups, passes of two stages): every role (TMA producer, MMA issuer, epilogue / softmax
+consumer groups (fmd_gemv.cu), the tensor-core lm_head `k_lm_head_tc`
+(fmd_lm_head_tc.cu: converter groups, passes of two stages) and the Q8_0
+converter hand-off of the projection GEMM `k_proj_tc` (fmd_proj_tc.cu):
+every role (TMA producer, MMA issuer, epilogue / softmax
 warps) runs as a coroutine, asynchronous work (TMA copies landing, MMA groups
 completing and their tcgen05.commit arrivals) completes at random later
 times, and the scheduler interleaves everything in random order. The model
@@ -612,5 +614,124 @@ def test_the_lm_head_tc_model_catches_a_planted_mistake(bug):
             sim.run()
         except AssertionError as e:
             assert any(k in str(e) for k in ("alias", "overwritten", "read", "behind")), e
+            failures += 1
+    assert failures == 20
+
+
+# ---- k_proj_tc with Q8_0 weights ------------------------------------------------------------
+def proj_tc_q8_protocol(sim, stages, n_tiles, nk, conv_warps=8, epi_warps=8, bug=None):
+    """`k_proj_tc` (fmd_proj_tc.cu) with Q8_0 weights: the producer's copy of
+    a stage brings the activation tile and the int8 weight tile (full[st]);
+    `conv_warps` converter warps each write their rows of the stage's 16-bit
+    B tile and arrive on conv[st]; the MMA warp waits on both full[st] and
+    conv[st], and its commit frees the stage (empty[st]) for the producer,
+    whose next copy into that stage is what lets the converters overwrite
+    its B tile; two accumulators hand tiles to the epilogue. `bug`:
+    "conv_skip" (the MMA warp does not wait for the converters)."""
+    full = [Bar(f"full{s}", 1) for s in range(stages)]
+    empty = [Bar(f"empty{s}", 1) for s in range(stages)]
+    conv = [Bar(f"conv{s}", conv_warps) for s in range(stages)]
+    acc_full = [Bar(f"acc_full{b}", 1) for b in range(2)]
+    acc_empty = [Bar(f"acc_empty{b}", epi_warps) for b in range(2)]
+    ring = [Buf(f"stage{s}") for s in range(stages)]
+    btile = [[Buf(f"b{s}.{w}") for w in range(conv_warps)] for s in range(stages)]
+    acc = [Buf(f"acc{b}") for b in range(2)]
+
+    def producer():
+        g = 0
+        for t in range(n_tiles):
+            for kb in range(nk):
+                st = g % stages
+                if g >= stages:
+                    yield lambda b=empty[st], p=g // stages - 1: b.try_wait(p)
+                full[st].arrive(expect_tx=1)
+
+                def land(st=st, tag=(t, kb)):
+                    ring[st].write(tag)
+                    full[st].complete_tx(1)
+                sim.later(land)
+                g += 1
+
+    def converter(w):
+        g = 0
+        for t in range(n_tiles):
+            for kb in range(nk):
+                st = g % stages
+                yield lambda b=full[st], p=g // stages: b.try_wait(p)
+                ring[st].check((t, kb))
+                btile[st][w].write((t, kb))  # this warp's rows of the 16-bit B tile
+                yield None
+                conv[st].arrive()
+                g += 1
+
+    pending = []
+
+    def drain_one():
+        pending.pop(0)()
+
+    def mma():
+        g = 0
+        for i in range(n_tiles):
+            buf = i & 1
+            if i >= 2:
+                yield lambda b=acc_empty[buf], p=(i >> 1) - 1: b.try_wait(p)
+            acc[buf].write(("acc", i))
+            for kb in range(nk):
+                st = g % stages
+                yield lambda b=full[st], p=g // stages: b.try_wait(p)
+                if bug != "conv_skip":
+                    yield lambda b=conv[st], p=g // stages: b.try_wait(p)
+                ring[st].check((i, kb))
+                for w in range(conv_warps):
+                    btile[st][w].check((i, kb))
+                    btile[st][w].readers += 1
+                ring[st].readers += 1
+
+                def done(st=st):
+                    ring[st].readers -= 1
+                    for w in range(conv_warps):
+                        btile[st][w].readers -= 1
+                    empty[st].arrive()
+                pending.append(done)
+                sim.later(drain_one)
+                g += 1
+            pending.append(lambda buf=buf: acc_full[buf].arrive())
+            sim.later(drain_one)
+
+    def epilogue(w):
+        for i in range(n_tiles):
+            buf = i & 1
+            yield lambda b=acc_full[buf], p=i >> 1: b.try_wait(p)
+            acc[buf].check(("acc", i))
+            acc[buf].readers += 1
+            yield None
+            acc[buf].readers -= 1
+            acc_empty[buf].arrive()
+
+    sim.spawn(producer())
+    for w in range(conv_warps):
+        sim.spawn(converter(w))
+    sim.spawn(mma())
+    for w in range(epi_warps):
+        sim.spawn(epilogue(w))
+
+
+@pytest.mark.parametrize("seed", range(25))
+@pytest.mark.parametrize("stages,n_tiles,nk", [(3, 4, 16), (5, 3, 16), (3, 1, 2), (5, 6, 4)])
+def test_proj_tc_q8_protocol(seed, stages, n_tiles, nk):
+    sim = Sim(seed * 17 + stages * 5 + n_tiles * 3 + nk)
+    proj_tc_q8_protocol(sim, stages, n_tiles, nk)
+    sim.run()
+
+
+def test_the_proj_tc_model_catches_a_skipped_converter_wait():
+    failures = 0
+    for seed in range(20):
+        sim = Sim(seed)
+        proj_tc_q8_protocol(sim, 3, 3, 16, bug="conv_skip")
+        try:
+            sim.run()
+        except AssertionError as e:
+            assert "read" in str(e) or "overwritten" in str(e), e
             failures += 1
     assert failures == 20
