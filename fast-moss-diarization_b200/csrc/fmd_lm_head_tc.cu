@@ -368,7 +368,7 @@ __global__ void __launch_bounds__(LhCfg<NR>::THREADS, 1)
       for (int r = et; r < NR; r += NE) {
         const uint32_t mb = xmax_s[r];
         const int e = (int)((mb >> 23) & 0xffu) - 127;
-        const int sh = mb == 0u || e > 127 ? 0 : max(-126, min(127, 14 - e));
+        const int sh = mb == 0u || e > 127 ? 0 : max(-126, min(126, 14 - e));  // 2^-sh stays a normal f32
         inv_s[r] = __uint_as_float((uint32_t)(127 - sh) << 23);
         rs_s[r] = __uint_as_float((uint32_t)(127 + sh) << 23);  // the staging's row scales are dead: reuse
       }
